@@ -1,0 +1,87 @@
+"""ctypes binding of libhyq.so (the C ABI declared in include/hyq.h).
+
+The library is the only compute path: if it is missing or fails to load,
+importing this module raises.  There is no CPU fallback.
+"""
+import ctypes as C
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "lib", "libhyq.so")
+
+HYQ_OK = 0
+ERRORS = {
+    -1: "HYQ_E_INVALID",
+    -2: "HYQ_E_SHAPE",
+    -3: "HYQ_E_ALIGN",
+    -4: "HYQ_E_CUDA",
+    -5: "HYQ_E_DEVICE",
+    -6: "HYQ_E_UNSUPPORTED",
+    -7: "HYQ_E_NOMEM",
+}
+
+
+class HyqError(RuntimeError):
+    """A libhyq call returned a negative status."""
+
+    def __init__(self, code, message):
+        super().__init__(f"{ERRORS.get(code, code)}: {message}")
+        self.code = code
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"libhyq.so not built ({LIB_PATH}); run `python -m hy_mt_rs_b200.build`")
+    return C.CDLL(LIB_PATH)
+
+
+lib = _load()
+
+_vp = C.c_void_p
+_i64 = C.c_int64
+_i64p = C.POINTER(C.c_int64)
+_wp = C.c_void_p  # hyq_weight*
+
+_SIGS = {
+    "hyq_last_error": ([], C.c_char_p),
+    "hyq_block_len": ([C.c_int], C.c_int),
+    "hyq_block_bytes": ([C.c_int], C.c_int),
+    "hyq_dtype_from_id": ([C.c_uint32, C.c_int, C.POINTER(C.c_int)], C.c_int),
+    "hyq_upload": ([_vp, C.c_size_t, C.c_int, C.c_int, _i64p, C.POINTER(_wp)], C.c_int),
+    "hyq_weight_wrap": ([_vp, C.c_size_t, C.c_int, C.c_int, _i64p, C.POINTER(_wp)], C.c_int),
+    "hyq_weight_expert": ([_wp, _i64, C.POINTER(_wp)], C.c_int),
+    "hyq_weight_info": ([_wp, C.POINTER(C.c_int), C.POINTER(C.c_int), _i64p, C.POINTER(C.c_size_t),
+                         C.POINTER(_vp)], C.c_int),
+    "hyq_free": ([_wp], None),
+    "hyq_decode": ([C.c_int, _vp, C.c_size_t, _vp, C.c_size_t, _vp], C.c_int),
+    "hyq_weight_row_into": ([_wp, _i64, _vp, _i64, _vp], C.c_int),
+    "hyq_dot": ([_vp, _vp, C.c_size_t, _vp, _vp], C.c_int),
+    "hyq_matmul": ([_wp, _vp, _i64, _vp, _vp], C.c_int),
+    "hyq_gemv_qkv": ([_wp, _wp, _wp, _vp, _vp, _vp, _vp, _vp], C.c_int),
+    "hyq_matmul_gate_up_silu": ([_wp, _wp, _vp, _vp, _vp], C.c_int),
+    "hyq_q8_quantize": ([_vp, _i64, _vp, _vp, _vp, _vp], C.c_int),
+    "hyq_gemv_q8": ([_wp, _vp, _vp, _vp, _vp, _vp], C.c_int),
+    "hyq_gemv_qkv_q8": ([_wp, _wp, _wp, _vp, _vp, _vp, _vp, _vp, _vp, _vp], C.c_int),
+    "hyq_matmul_gate_up_silu_q8": ([_wp, _wp, _vp, _vp, _vp, _vp, _vp], C.c_int),
+    "hyq_device_status": ([_vp, C.POINTER(C.c_uint32)], C.c_int),
+}
+
+for _name, (_args, _res) in _SIGS.items():
+    _f = getattr(lib, _name)
+    _f.argtypes = _args
+    _f.restype = _res
+
+
+def exported_symbols():
+    """Names this binding requires from the library."""
+    return sorted(_SIGS)
+
+
+def last_error():
+    return lib.hyq_last_error().decode(errors="replace")
+
+
+def check(rc):
+    if rc != HYQ_OK:
+        raise HyqError(rc, last_error())
+    return rc

@@ -1,0 +1,405 @@
+// C ABI of libhyq (include/hyq.h): argument validation mirroring the
+// reference's ensure! checks, weight handles, status reporting, and dispatch
+// to the kernel translation units.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/hyq.h"
+#include "hyq_common.cuh"
+#include "hyq_kernels.h"
+
+struct hyq_weight {
+  int dtype;
+  int ndim;
+  int64_t dims[3];
+  size_t byte_len;
+  const uint8_t* data;  // device
+  bool owns;
+};
+
+namespace {
+
+thread_local std::string t_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  t_err = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(HYQ_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool valid_dtype(int t) { return t >= HYQ_F32 && t <= HYQ_STQ1_0; }
+
+int64_t row_bytes(int dtype, int64_t K) { return K / hyq::block_len(dtype) * hyq::block_bytes(dtype); }
+
+// Per-device status word: a module-scope device variable (no allocation).
+__device__ unsigned g_status;
+
+constexpr int kMaxDevices = 64;
+unsigned* g_status_ptr[kMaxDevices] = {};
+std::mutex g_status_mu;
+
+int status_ptr(unsigned** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(HYQ_E_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_status_mu);
+  if (!g_status_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_status);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(status)");
+    g_status_ptr[dev] = static_cast<unsigned*>(p);
+  }
+  *out = g_status_ptr[dev];
+  return HYQ_OK;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int check_matrix(const hyq_weight* w, const char* name) {
+  if (!w) return fail(HYQ_E_INVALID, "%s: null weight", name);
+  if (w->ndim != 2) return fail(HYQ_E_SHAPE, "%s is not a matrix", name);
+  return HYQ_OK;
+}
+
+int launch_status(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return HYQ_OK;
+}
+
+int make_weight(const void* data, size_t byte_len, int dtype, int ndim, const int64_t* dims, bool device,
+                hyq_weight** out) {
+  if (!out) return fail(HYQ_E_INVALID, "weight: null output handle");
+  *out = nullptr;
+  if (!valid_dtype(dtype)) return fail(HYQ_E_INVALID, "unsupported tensor type %d", dtype);
+  if (!data || !dims) return fail(HYQ_E_INVALID, "weight: null data or dims");
+  if (ndim < 1 || ndim > 3) return fail(HYQ_E_SHAPE, "weight: rank %d not supported", ndim);
+  int64_t d[3] = {1, 1, 1};
+  for (int i = 0; i < ndim; ++i) {
+    if (dims[i] <= 0) return fail(HYQ_E_SHAPE, "weight: non-positive dimension");
+    d[i] = dims[i];
+  }
+  if (d[0] % hyq::block_len(dtype) != 0) return fail(HYQ_E_SHAPE, "weight: K=%lld is not a multiple of %d",
+                                                     (long long)d[0], hyq::block_len(dtype));
+  const int64_t expect = row_bytes(dtype, d[0]) * d[1] * d[2];
+  if ((int64_t)byte_len != expect)
+    return fail(HYQ_E_SHAPE, "weight: byte_len %zu does not match shape (expected %lld)", byte_len,
+                (long long)expect);
+  hyq_weight* w = new hyq_weight{};
+  w->dtype = dtype;
+  w->ndim = ndim;
+  for (int i = 0; i < 3; ++i) w->dims[i] = i < ndim ? d[i] : 0;
+  w->byte_len = byte_len;
+  if (device) {
+    w->data = static_cast<const uint8_t*>(data);
+    w->owns = false;
+  } else {
+    void* p = nullptr;
+    // Pad to a 16-byte multiple so bulk copies of the last rows stay inside.
+    cudaError_t e = cudaMalloc(&p, (byte_len + 15) / 16 * 16 + 16);
+    if (e != cudaSuccess) {
+      delete w;
+      return fail(HYQ_E_NOMEM, "cudaMalloc(%zu): %s", byte_len, cudaGetErrorString(e));
+    }
+    e = cudaMemcpy(p, data, byte_len, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      cudaFree(p);
+      delete w;
+      return cuda_fail(e, "cudaMemcpy(upload)");
+    }
+    w->data = static_cast<const uint8_t*>(p);
+    w->owns = true;
+  }
+  *out = w;
+  return HYQ_OK;
+}
+
+// Activations given either as f32 or as Q8 (values, scales).
+struct Act {
+  const float* x = nullptr;
+  const int8_t* xq = nullptr;
+  const float* xs = nullptr;
+};
+
+int run_gemv(int n_mat, const hyq_weight* const* ws, float* const* ys, const hyq_weight* up, const Act& a,
+             cudaStream_t st, const char* name) {
+  unsigned* status = nullptr;
+  int rc = status_ptr(&status);
+  if (rc) return rc;
+  hyq::GemvJob j;
+  j.dtype = ws[0]->dtype;
+  j.n_mat = n_mat;
+  for (int m = 0; m < n_mat; ++m) {
+    j.w[m] = ws[m]->data;
+    j.y[m] = ys[m];
+    j.rows[m] = ws[m]->dims[1];
+  }
+  j.up = up ? up->data : nullptr;
+  j.K = ws[0]->dims[0];
+  j.x = a.x;
+  j.xq = a.xq;
+  j.xs = a.xs;
+  j.status = status;
+  return launch_status(hyq::launch_gemv(j, st), name);
+}
+
+int check_act(const Act& a, const char* name) {
+  if (a.x) {
+    if (!aligned(a.x, 4)) return fail(HYQ_E_ALIGN, "%s: input not 4-byte aligned", name);
+    return HYQ_OK;
+  }
+  if (!a.xq || !a.xs) return fail(HYQ_E_INVALID, "%s: null activations", name);
+  if (!aligned(a.xs, 4)) return fail(HYQ_E_ALIGN, "%s: scales not 4-byte aligned", name);
+  return HYQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* hyq_last_error(void) { return t_err.c_str(); }
+
+int hyq_block_len(int dtype) { return valid_dtype(dtype) ? hyq::block_len(dtype) : 0; }
+
+int hyq_block_bytes(int dtype) { return valid_dtype(dtype) ? hyq::block_bytes(dtype) : 0; }
+
+int hyq_dtype_from_id(uint32_t id, int profile, int* dtype_out) {
+  if (!dtype_out) return fail(HYQ_E_INVALID, "dtype_from_id: null output");
+  int t = -1;
+  switch (id) {
+    case 0: t = HYQ_F32; break;
+    case 1: t = HYQ_F16; break;
+    case 8: t = HYQ_Q8_0; break;
+    case 12: t = HYQ_Q4_K; break;
+    case 14: t = HYQ_Q6_K; break;
+    case 40: t = profile == HYQ_PROFILE_TENCENT_Q2_0C ? HYQ_Q2_0C : -1; break;
+    case 42: t = profile == HYQ_PROFILE_TENCENT_STQ1 ? HYQ_STQ1_0 : -1; break;
+    default: break;
+  }
+  if (t < 0) return fail(HYQ_E_INVALID, "unsupported GGUF tensor type %u for profile %d", id, profile);
+  *dtype_out = t;
+  return HYQ_OK;
+}
+
+int hyq_upload(const void* packed_host, size_t byte_len, int dtype, int ndim, const int64_t* dims,
+               hyq_weight** out) {
+  return make_weight(packed_host, byte_len, dtype, ndim, dims, false, out);
+}
+
+int hyq_weight_wrap(const void* packed_device, size_t byte_len, int dtype, int ndim, const int64_t* dims,
+                    hyq_weight** out) {
+  return make_weight(packed_device, byte_len, dtype, ndim, dims, true, out);
+}
+
+int hyq_weight_expert(const hyq_weight* w, int64_t index, hyq_weight** out) {
+  if (!w || !out) return fail(HYQ_E_INVALID, "expert: null argument");
+  *out = nullptr;
+  if (w->ndim != 3 || index < 0 || index >= w->dims[2])
+    return fail(HYQ_E_SHAPE, "invalid expert %lld", (long long)index);
+  hyq_weight* e = new hyq_weight{};
+  e->dtype = w->dtype;
+  e->ndim = 2;
+  e->dims[0] = w->dims[0];
+  e->dims[1] = w->dims[1];
+  e->byte_len = w->byte_len / (size_t)w->dims[2];
+  e->data = w->data + (size_t)index * e->byte_len;
+  e->owns = false;
+  *out = e;
+  return HYQ_OK;
+}
+
+int hyq_weight_info(const hyq_weight* w, int* dtype, int* ndim, int64_t* dims, size_t* byte_len,
+                    const void** device_ptr) {
+  if (!w) return fail(HYQ_E_INVALID, "info: null weight");
+  if (dtype) *dtype = w->dtype;
+  if (ndim) *ndim = w->ndim;
+  if (dims)
+    for (int i = 0; i < 3; ++i) dims[i] = w->dims[i];
+  if (byte_len) *byte_len = w->byte_len;
+  if (device_ptr) *device_ptr = w->data;
+  return HYQ_OK;
+}
+
+void hyq_free(hyq_weight* w) {
+  if (!w) return;
+  if (w->owns) cudaFree(const_cast<uint8_t*>(w->data));
+  delete w;
+}
+
+int hyq_decode(int dtype, const void* bytes, size_t byte_len, float* out, size_t out_len, void* stream) {
+  if (!valid_dtype(dtype)) return fail(HYQ_E_INVALID, "unsupported tensor type %d", dtype);
+  const size_t bl = (size_t)hyq::block_len(dtype), bb = (size_t)hyq::block_bytes(dtype);
+  if (out_len % bl) return fail(HYQ_E_SHAPE, "partial output block");
+  if (byte_len != out_len / bl * bb) return fail(HYQ_E_SHAPE, "wrong byte count");
+  if (out_len == 0) return HYQ_OK;
+  if (!bytes || !out) return fail(HYQ_E_INVALID, "decode: null pointer");
+  if (!aligned(out, 4)) return fail(HYQ_E_ALIGN, "decode: output not 4-byte aligned");
+  return launch_status(hyq::launch_decode(dtype, bytes, out, (int64_t)out_len, (cudaStream_t)stream), "decode");
+}
+
+int hyq_weight_row_into(const hyq_weight* w, int64_t row, float* out, int64_t out_len, void* stream) {
+  if (!w || !out) return fail(HYQ_E_INVALID, "row_into: null argument");
+  const int64_t n = w->dims[0];
+  if (out_len != n) return fail(HYQ_E_SHAPE, "out buffer length mismatch");
+  const int64_t rb = row_bytes(w->dtype, n);
+  if (row < 0 || row >= (int64_t)w->byte_len / rb) return fail(HYQ_E_SHAPE, "row %lld out of range", (long long)row);
+  if (!aligned(out, 4)) return fail(HYQ_E_ALIGN, "row_into: output not 4-byte aligned");
+  return launch_status(hyq::launch_decode(w->dtype, w->data + row * rb, out, n, (cudaStream_t)stream), "row_into");
+}
+
+int hyq_dot(const float* a, const float* b, size_t n, float* out, void* stream) {
+  if (!a || !b || !out) return fail(HYQ_E_INVALID, "dot: null pointer");
+  return launch_status(hyq::launch_dot(a, b, (int64_t)n, out, (cudaStream_t)stream), "dot");
+}
+
+int hyq_matmul(const hyq_weight* w, const float* input, int64_t batch, float* out, void* stream) {
+  int rc = check_matrix(w, "matmul");
+  if (rc) return rc;
+  if (batch <= 0) return fail(HYQ_E_SHAPE, "invalid activation shape");
+  if (!input || !out) return fail(HYQ_E_INVALID, "matmul: null pointer");
+  Act a;
+  a.x = input;
+  if ((rc = check_act(a, "matmul"))) return rc;
+  const int64_t K = w->dims[0], N = w->dims[1];
+  for (int64_t b = 0; b < batch; ++b) {
+    Act ab;
+    ab.x = input + b * K;
+    float* y = out + b * N;
+    rc = run_gemv(1, &w, &y, nullptr, ab, (cudaStream_t)stream, "matmul");
+    if (rc) return rc;
+  }
+  return HYQ_OK;
+}
+
+static int qkv_checks(const hyq_weight* q, const hyq_weight* k, const hyq_weight* v) {
+  if (!q || !k || !v) return fail(HYQ_E_INVALID, "qkv: null weight");
+  if (q->ndim != 2 || k->ndim != 2 || v->ndim != 2 || k->dims[0] != q->dims[0] || v->dims[0] != q->dims[0])
+    return fail(HYQ_E_SHAPE, "query, key and value must be matrices that share an input width");
+  return HYQ_OK;
+}
+
+static int qkv_run(const hyq_weight* q, const hyq_weight* k, const hyq_weight* v, const Act& a, float* qo,
+                   float* ko, float* vo, cudaStream_t st) {
+  if (!qo || !ko || !vo) return fail(HYQ_E_INVALID, "qkv: null output");
+  const hyq_weight* ws[3] = {q, k, v};
+  float* ys[3] = {qo, ko, vo};
+  if (q->dtype == k->dtype && q->dtype == v->dtype) return run_gemv(3, ws, ys, nullptr, a, st, "qkv");
+  for (int m = 0; m < 3; ++m) {
+    int rc = run_gemv(1, &ws[m], &ys[m], nullptr, a, st, "qkv");
+    if (rc) return rc;
+  }
+  return HYQ_OK;
+}
+
+int hyq_gemv_qkv(const hyq_weight* q, const hyq_weight* k, const hyq_weight* v, const float* input, float* q_out,
+                 float* k_out, float* v_out, void* stream) {
+  int rc = qkv_checks(q, k, v);
+  if (rc) return rc;
+  Act a;
+  a.x = input;
+  if (!input) return fail(HYQ_E_INVALID, "qkv: null input");
+  if ((rc = check_act(a, "qkv"))) return rc;
+  return qkv_run(q, k, v, a, q_out, k_out, v_out, (cudaStream_t)stream);
+}
+
+static int gate_up_checks(const hyq_weight* gate, const hyq_weight* up) {
+  int rc = check_matrix(gate, "gate");
+  if (rc) return rc;
+  if ((rc = check_matrix(up, "up"))) return rc;
+  if (up->dims[0] != gate->dims[0] || up->dims[1] != gate->dims[1]) return fail(HYQ_E_SHAPE, "gate and up shape mismatch");
+  if (up->dtype != gate->dtype) return fail(HYQ_E_UNSUPPORTED, "gate and up must share a tensor type");
+  return HYQ_OK;
+}
+
+int hyq_matmul_gate_up_silu(const hyq_weight* gate, const hyq_weight* up, const float* input, float* out,
+                            void* stream) {
+  int rc = gate_up_checks(gate, up);
+  if (rc) return rc;
+  if (!input || !out) return fail(HYQ_E_INVALID, "gate_up_silu: null pointer");
+  Act a;
+  a.x = input;
+  if ((rc = check_act(a, "gate_up_silu"))) return rc;
+  return run_gemv(1, &gate, &out, up, a, (cudaStream_t)stream, "gate_up_silu");
+}
+
+int hyq_q8_quantize(const float* input, int64_t len, int8_t* values, float* scales, int8_t* values_q2c,
+                    void* stream) {
+  if (len < 0) return fail(HYQ_E_SHAPE, "q8: negative length");
+  if (len == 0) return HYQ_OK;
+  if (!input || !values || !scales) return fail(HYQ_E_INVALID, "q8: null pointer");
+  if (!aligned(input, 4) || !aligned(scales, 4)) return fail(HYQ_E_ALIGN, "q8: f32 buffers must be 4-byte aligned");
+  return launch_status(hyq::launch_q8_quantize(input, len, values, scales, values_q2c, (cudaStream_t)stream), "q8");
+}
+
+int hyq_gemv_q8(const hyq_weight* w, const int8_t* values, const float* scales, const int8_t* values_q2c,
+                float* out, void* stream) {
+  (void)values_q2c;  // the kernels permute the natural-order values themselves
+  int rc = check_matrix(w, "gemv_q8");
+  if (rc) return rc;
+  if (!out) return fail(HYQ_E_INVALID, "gemv_q8: null output");
+  Act a;
+  a.xq = values;
+  a.xs = scales;
+  if ((rc = check_act(a, "gemv_q8"))) return rc;
+  return run_gemv(1, &w, &out, nullptr, a, (cudaStream_t)stream, "gemv_q8");
+}
+
+int hyq_gemv_qkv_q8(const hyq_weight* q, const hyq_weight* k, const hyq_weight* v, const int8_t* values,
+                    const float* scales, const int8_t* values_q2c, float* q_out, float* k_out, float* v_out,
+                    void* stream) {
+  (void)values_q2c;
+  int rc = qkv_checks(q, k, v);
+  if (rc) return rc;
+  Act a;
+  a.xq = values;
+  a.xs = scales;
+  if ((rc = check_act(a, "qkv_q8"))) return rc;
+  return qkv_run(q, k, v, a, q_out, k_out, v_out, (cudaStream_t)stream);
+}
+
+int hyq_matmul_gate_up_silu_q8(const hyq_weight* gate, const hyq_weight* up, const int8_t* values,
+                               const float* scales, const int8_t* values_q2c, float* out, void* stream) {
+  (void)values_q2c;
+  int rc = gate_up_checks(gate, up);
+  if (rc) return rc;
+  if (!out) return fail(HYQ_E_INVALID, "gate_up_silu_q8: null output");
+  Act a;
+  a.xq = values;
+  a.xs = scales;
+  if ((rc = check_act(a, "gate_up_silu_q8"))) return rc;
+  return run_gemv(1, &gate, &out, up, a, (cudaStream_t)stream, "gate_up_silu_q8");
+}
+
+int hyq_device_status(void* stream, uint32_t* status_out) {
+  if (!status_out) return fail(HYQ_E_INVALID, "device_status: null output");
+  unsigned* sp = nullptr;
+  int rc = status_ptr(&sp);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  unsigned v = 0;
+  e = cudaMemcpy(&v, sp, sizeof v, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "read status");
+  const unsigned zero = 0;
+  e = cudaMemcpy(sp, &zero, sizeof zero, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return cuda_fail(e, "clear status");
+  *status_out = v;
+  if (v) return fail(HYQ_E_DEVICE, "device status 0x%x (bounded wait expired)", v);
+  return HYQ_OK;
+}
+
+}  // extern "C"

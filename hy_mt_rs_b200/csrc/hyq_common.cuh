@@ -1,0 +1,202 @@
+// Shared device helpers for the hyq kernels (sm_100a).
+//
+// Block geometry follows hy-mt-rs src/quant.rs:17-63 (DType, block_len,
+// block_bytes).  Synchronisation uses mbarriers and bulk-async copies
+// (cp.async.bulk, the TMA 1-D engine); every wait is bounded in time so that a
+// lost completion turns into a status word the host can read instead of a hung
+// GPU.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace hyq {
+
+// DType order of quant.rs:19-27; the C ABI uses the same values.
+enum DType : int { F32 = 0, F16 = 1, Q4_K = 2, Q6_K = 3, Q8_0 = 4, Q2_0C = 5, STQ1_0 = 6 };
+
+__host__ __device__ constexpr int block_len(int t) {
+  return (t == F32 || t == F16) ? 1 : (t == Q8_0 ? 32 : (t == Q2_0C ? 512 : 256));
+}
+
+__host__ __device__ constexpr int block_bytes(int t) {
+  return t == F32 ? 4
+       : t == F16 ? 2
+       : t == Q4_K ? 144
+       : t == Q6_K ? 210
+       : t == Q8_0 ? 34
+       : t == Q2_0C ? 130
+       : t == STQ1_0 ? 42 : 0;
+}
+
+// Device status bits (OR-ed into a status word owned by the library).
+enum : unsigned {
+  DEV_TIMEOUT_FULL = 1u,   // consumer gave up waiting for a stage to land
+  DEV_TIMEOUT_EMPTY = 2u,  // producer gave up waiting for a stage to drain
+  DEV_TIMEOUT_DRAIN = 4u,  // exit path gave up waiting for copies in flight
+  DEV_BAD_ARGS = 8u,       // kernel saw arguments the host should have rejected
+};
+
+// Bound on any single wait (nanoseconds of %globaltimer).
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for phase `parity` of an mbarrier, giving up after kWaitLimitNs or as
+// soon as another thread of the CTA raised `*abort` (abort may be null: then
+// only the time bound applies).  Returns false on give-up (the caller then
+// records a status bit and leaves its loop).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (abort && *abort) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    }
+  }
+}
+
+// Make prior generic-proxy accesses of shared memory ordered before later
+// async-proxy (bulk copy) writes to it.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Bulk-async copy global -> shared (16-byte aligned addresses, size a multiple
+// of 16), completing `bytes` of transaction count on `bar`.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// Exact IEEE binary16 -> f32 of the `half` crate (finite values are exact,
+// NaNs are quieted with their payload).  Used where decode output bits matter.
+__device__ __forceinline__ float half_bits_to_f32(uint32_t h) {
+  const uint32_t sign = (h & 0x8000u) << 16;
+  const uint32_t e = (h >> 10) & 0x1fu;
+  uint32_t m = h & 0x3ffu;
+  if ((h & 0x7fffu) == 0) return __uint_as_float(sign);
+  if (e == 0x1f) return __uint_as_float(m ? (sign | 0x7fc00000u | (m << 13)) : (sign | 0x7f800000u));
+  if (e == 0) {
+    const int lz = __clz(m) - 21;  // shifts that bring bit 10 up
+    m = (m << lz) & 0x3ffu;
+    return __uint_as_float(sign | ((uint32_t)(113 - lz) << 23) | (m << 13));
+  }
+  return __uint_as_float(sign | ((e + 112u) << 23) | (m << 13));
+}
+
+// Fast f16 -> f32 for scales inside dot products (hardware conversion; exact
+// for every finite value).
+__device__ __forceinline__ float half_to_f32(uint32_t h) {
+  float f;
+  asm("{ .reg .b16 t; mov.b16 t, %1; cvt.f32.f16 %0, t; }" : "=f"(f) : "h"((unsigned short)h));
+  return f;
+}
+
+// Little-endian loads of 16/32 bits from shared memory at a 2-byte aligned
+// address.
+__device__ __forceinline__ uint32_t lds_u16(const uint8_t* p) {
+  return *reinterpret_cast<const uint16_t*>(p);
+}
+
+__device__ __forceinline__ uint32_t lds_u32_a2(const uint8_t* p) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+  const uint32_t sh = (uint32_t)(a & 2u) * 8u;
+  return __funnelshift_r(w[0], w[1], sh);
+}
+
+// N consecutive 32-bit words starting at a 2-byte aligned shared address.
+template <int N>
+__device__ __forceinline__ void lds_words_a2(const uint8_t* p, uint32_t (&out)[N]) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+  const uint32_t sh = (uint32_t)(a & 2u) * 8u;
+  uint32_t t[N + 1];
+#pragma unroll
+  for (int i = 0; i <= N; ++i) t[i] = w[i];
+#pragma unroll
+  for (int i = 0; i < N; ++i) out[i] = __funnelshift_r(t[i], t[i + 1], sh);
+}
+
+__device__ __forceinline__ int dp4a_uu(uint32_t a, uint32_t b, int c) {
+  return __dp4a(a, b, (unsigned)c);
+}
+
+// unsigned bytes of a times signed bytes of b
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
+  return __dp4a((int)a, (int)b, c);
+}
+
+// All-reduce of a flag over the threads of named barrier `id` (`count`
+// threads, a multiple of 32): true only if every participant passed true.
+__device__ __forceinline__ bool bar_red_and(int id, int count, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.and.pred po, %2, %3, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ void bar_sync_named(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+}  // namespace hyq

@@ -1,0 +1,39 @@
+// Internal host-side launch interface between the C ABI layer (hyq_api.cu)
+// and the kernel translation units.  Not part of the public ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace hyq {
+
+cudaError_t launch_decode(int dtype, const void* src, float* dst, int64_t n_out, cudaStream_t st);
+cudaError_t launch_dot(const float* a, const float* b, int64_t n, float* out, cudaStream_t st);
+cudaError_t launch_q8_quantize(const float* x, int64_t len, int8_t* values, float* scales, int8_t* values_q2c,
+                               cudaStream_t st);
+
+// One fused matrix-vector launch over up to three matrices that share the
+// input width K and the packed type (QKV), or over a gate/up pair whose rows
+// are combined as silu(gate) * up.
+struct GemvJob {
+  int dtype = 0;
+  int n_mat = 1;                  // 1..3
+  const uint8_t* w[3] = {};       // packed rows, device
+  float* y[3] = {};               // outputs, device
+  int64_t rows[3] = {};
+  const uint8_t* up = nullptr;    // gate/up mode: up rows (same shape as w[0])
+  int64_t K = 0;
+  // Activations: exactly one of (x) or (xq, xs) is set.
+  const float* x = nullptr;       // f32 [K]
+  const int8_t* xq = nullptr;     // int8 [K] (natural order, as Q8::values)
+  const float* xs = nullptr;      // f32 [ceil(K/256)] (Q8::scales)
+  unsigned* status = nullptr;     // device status word (bounded-wait failures)
+};
+
+cudaError_t launch_gemv(const GemvJob& job, cudaStream_t st);
+
+// Which engine launch_gemv picks for a job (for tests and the bench):
+// 0 = streaming bulk-copy kernel, 1 = per-element fallback.
+int gemv_engine(const GemvJob& job);
+
+}  // namespace hyq

@@ -1,0 +1,147 @@
+/*
+ * hyq.h -- C ABI of the B200 block-quantized GEMV/GEMM library (libhyq.so).
+ *
+ * Drop-in boundary for the quantized linear-algebra path of hy-mt-rs
+ * (src/quant.rs).  Every entry point names the reference routine it replaces.
+ * Conventions:
+ *   - plain pointers and sizes; device pointers unless a name says host;
+ *   - weights are packed GGUF blocks, uploaded unchanged; dims follow GGUF
+ *     order: dims[0] = K (contiguous input width), dims[1] = N (output rows),
+ *     dims[2] = number of experts (optional);
+ *   - outputs of batched products are [batch, N] row-major (quant.rs:337-343);
+ *   - every call is ordered on `stream` (a cudaStream_t, NULL = legacy default
+ *     stream) and returns HYQ_OK or a negative HYQ_E_* code; nothing aborts;
+ *     hyq_last_error() describes the last failure of the calling thread;
+ *   - calls on different streams may run concurrently; a weight handle may be
+ *     shared by any number of threads (it is immutable after creation).
+ */
+#ifndef HYQ_H_
+#define HYQ_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Packed tensor types, in the order of DType (quant.rs:19-27). */
+typedef enum hyq_dtype {
+  HYQ_F32 = 0,
+  HYQ_F16 = 1,
+  HYQ_Q4_K = 2,
+  HYQ_Q6_K = 3,
+  HYQ_Q8_0 = 4,
+  HYQ_Q2_0C = 5,  /* Tencent Q2_0C: 512 weights per 130-byte block */
+  HYQ_STQ1_0 = 6  /* Tencent STQ1 stride-16 sparse ternary: 256 weights per 42 bytes */
+} hyq_dtype;
+
+/* GGUF type-id profiles (gguf.rs:17-27, Profile; Auto is resolved by the caller). */
+typedef enum hyq_profile {
+  HYQ_PROFILE_STANDARD = 1,
+  HYQ_PROFILE_TENCENT_Q2_0C = 2,
+  HYQ_PROFILE_TENCENT_STQ1 = 3
+} hyq_profile;
+
+#define HYQ_OK 0
+#define HYQ_E_INVALID (-1)     /* null pointer, unknown dtype/profile, bad argument */
+#define HYQ_E_SHAPE (-2)       /* shape or byte count mismatch (the reference's ensure! checks) */
+#define HYQ_E_ALIGN (-3)       /* a device pointer is not aligned to its element size */
+#define HYQ_E_CUDA (-4)        /* CUDA runtime error; see hyq_last_error() */
+#define HYQ_E_DEVICE (-5)      /* a kernel's bounded wait expired (see hyq_device_status) */
+#define HYQ_E_UNSUPPORTED (-6) /* combination the library does not implement */
+#define HYQ_E_NOMEM (-7)       /* device allocation failed */
+
+/* Device status bits returned by hyq_device_status. */
+#define HYQ_DEV_TIMEOUT_FULL 1u  /* a consumer gave up waiting for a tile copy */
+#define HYQ_DEV_TIMEOUT_EMPTY 2u /* a producer gave up waiting for a free stage */
+#define HYQ_DEV_TIMEOUT_DRAIN 4u /* exit path gave up waiting for copies in flight */
+
+typedef struct hyq_weight hyq_weight;
+
+/* Message for the last failing call on this thread ("" if none). */
+const char* hyq_last_error(void);
+
+/* DType::block_len / block_bytes (quant.rs:43-62).  0 for an unknown dtype. */
+int hyq_block_len(int dtype);
+int hyq_block_bytes(int dtype);
+
+/* DType::from_id (quant.rs:30-41): GGUF tensor type id -> dtype under a
+ * profile.  IDs 40/42 are only valid under their Tencent profile. */
+int hyq_dtype_from_id(uint32_t type_id, int profile, int* dtype_out);
+
+/* Weight (quant.rs:65-97): copy `byte_len` packed bytes from host memory
+ * (e.g. a memory-mapped GGUF tensor) to a new device buffer, unchanged.
+ * byte_len must equal dims[1] * (dims[2] or 1) * dims[0] / block_len * block_bytes. */
+int hyq_upload(const void* packed_host, size_t byte_len, int dtype, int ndim, const int64_t* dims,
+               hyq_weight** out);
+
+/* As hyq_upload, but borrow packed bytes that already live in device memory
+ * (the caller keeps them alive while the handle is used). */
+int hyq_weight_wrap(const void* packed_device, size_t byte_len, int dtype, int ndim, const int64_t* dims,
+                    hyq_weight** out);
+
+/* Weight::expert (quant.rs:144-154): view of expert `index` of a rank-3
+ * weight [K, N, E] as a [K, N] matrix (byte offset index * byte_len / E). */
+int hyq_weight_expert(const hyq_weight* w, int64_t index, hyq_weight** out);
+
+/* Shape/type/buffer of a handle (any output pointer may be NULL; dims needs 3). */
+int hyq_weight_info(const hyq_weight* w, int* dtype, int* ndim, int64_t* dims, size_t* byte_len,
+                    const void** device_ptr);
+
+/* Release a handle (frees the device buffer only if hyq_upload made it). */
+void hyq_free(hyq_weight* w);
+
+/* decode (quant.rs:1066-1079): `byte_len` packed bytes -> `out_len` f32, bit
+ * for bit as decode_unchecked (quant.rs:2405-2486). */
+int hyq_decode(int dtype, const void* bytes, size_t byte_len, float* out, size_t out_len, void* stream);
+
+/* Weight::row_into (quant.rs:123-142): decode one row (embedding lookup). */
+int hyq_weight_row_into(const hyq_weight* w, int64_t row, float* out, int64_t out_len, void* stream);
+
+/* dot (quant.rs:2500): *out = sum a[i]*b[i] (f32; summation order differs). */
+int hyq_dot(const float* a, const float* b, size_t n, float* out, void* stream);
+
+/* Weight::matmul (quant.rs:159-344): out[batch, N] = input[batch, K] . W^T
+ * with f32 activations. */
+int hyq_matmul(const hyq_weight* w, const float* input, int64_t batch, float* out, void* stream);
+
+/* Weight::gemv_qkv (quant.rs:658-721): three batch-1 projections of one
+ * input in one launch. */
+int hyq_gemv_qkv(const hyq_weight* q, const hyq_weight* k, const hyq_weight* v, const float* input,
+                 float* q_out, float* k_out, float* v_out, void* stream);
+
+/* Weight::matmul_gate_up_silu (quant.rs:724-841): out = silu(gate.x) * up.x. */
+int hyq_matmul_gate_up_silu(const hyq_weight* gate, const hyq_weight* up, const float* input, float* out,
+                            void* stream);
+
+/* Q8::quantize_into (quant.rs:904-922): int8 activations, one f32 scale per
+ * 256 values, and the Q2_0C de-interleaved copy (values_q2c may be NULL).
+ * Bit-exact with the reference.  scales has ceil(len/256) entries. */
+int hyq_q8_quantize(const float* input, int64_t len, int8_t* values, float* scales, int8_t* values_q2c,
+                    void* stream);
+
+/* gemv_q8_fast (quant.rs:353-357): batch-1 product on pre-quantized
+ * activations (values/scales from hyq_q8_quantize; values_q2c may be NULL). */
+int hyq_gemv_q8(const hyq_weight* w, const int8_t* values, const float* scales, const int8_t* values_q2c,
+                float* out, void* stream);
+
+/* gemv_qkv_fast (quant.rs:441-538). */
+int hyq_gemv_qkv_q8(const hyq_weight* q, const hyq_weight* k, const hyq_weight* v, const int8_t* values,
+                    const float* scales, const int8_t* values_q2c, float* q_out, float* k_out, float* v_out,
+                    void* stream);
+
+/* matmul_gate_up_silu_fast (quant.rs:540-651). */
+int hyq_matmul_gate_up_silu_q8(const hyq_weight* gate, const hyq_weight* up, const int8_t* values,
+                               const float* scales, const int8_t* values_q2c, float* out, void* stream);
+
+/* Synchronize `stream`, then return (and clear) the device status word of
+ * the current device: 0, or HYQ_DEV_* bits from kernels whose bounded waits
+ * expired. */
+int hyq_device_status(void* stream, uint32_t* status_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HYQ_H_ */
