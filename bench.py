@@ -1,0 +1,480 @@
+#!/usr/bin/env python
+"""Benchmark of the block-quantized decode GEMV path (hy-mt-rs config 2).
+
+Workload ("1.8B decoder-layer projections + lm_head, batch 1"): the
+projections one Hy-MT2-1.8B decode step runs per layer (model.rs:403-538),
+repeated for each low-bit format -- Q2_0C and STQ1_0 layers with
+q 2048x2048, k/v 512x2048, o 2048x2048, gate/up 6144x2048 (fused SiLU),
+down 2048x6144 -- followed by the Q6_K lm_head 120832x2048.  Weights are
+seeded N(0, 0.02) packed by hy_mt_rs_b200.synth; activations N(0, 1).
+
+A step is one pass of that chain.  The metric is quantized-GEMV HBM
+throughput: algorithmic bytes (packed weights + f32 activations read + f32
+outputs written) per second, whole job.  Every step reads the 203 MB lm_head,
+which is larger than the 126 MB L2, and the layers rotate over `--copies`
+distinct weight copies, so no step starts with its weights in L2.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--path f32|q8]
+    python bench.py --impl reference ...   # the reference's CPU path
+
+--path f32 (default) takes f32 activations like the reference's x86 path;
+--path q8 quantizes activations per 256 values first, like the reference's
+aarch64 decode loop (model.rs:404-533).
+"""
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+HIDDEN, FFN, KV, VOCAB = 2048, 6144, 512, 120832
+# (name, rows N, input width K) of one decoder layer, in call order
+LAYER = [("attn_q", HIDDEN, HIDDEN), ("attn_k", KV, HIDDEN), ("attn_v", KV, HIDDEN),
+         ("attn_output", HIDDEN, HIDDEN), ("ffn_gate", FFN, HIDDEN), ("ffn_up", FFN, HIDDEN),
+         ("ffn_down", HIDDEN, FFN)]
+N_LAYERS_MODEL = 32
+
+
+def args_parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["hyq", "reference"], default="hyq")
+    ap.add_argument("--path", choices=["f32", "q8"], default="f32")
+    ap.add_argument("--copies", type=int, default=4)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    return ap.parse_args()
+
+
+def row_bytes(dtype, K):
+    bl = {0: 1, 1: 1, 2: 256, 3: 256, 4: 32, 5: 512, 6: 256}[int(dtype)]
+    bb = {0: 4, 1: 2, 2: 144, 3: 210, 4: 34, 5: 130, 6: 42}[int(dtype)]
+    return K // bl * bb
+
+
+def gemv_bytes(dtype, N, K):
+    """Algorithmic bytes of one batch-1 product: packed W + f32 x + f32 y."""
+    return N * row_bytes(dtype, K) + 4 * K + 4 * N
+
+
+def layer_bytes(dtype):
+    b = 0
+    for name, N, K in LAYER:
+        b += N * row_bytes(dtype, K)
+    # activations: qkv reads x once, writes q,k,v; o; gate/up reads x once, writes N; down
+    b += 4 * (HIDDEN + HIDDEN + 2 * KV) + 4 * (HIDDEN + HIDDEN) + 4 * (HIDDEN + FFN) + 4 * (FFN + HIDDEN)
+    return b
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profile_traffic(kernel_key):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu
+    summary (profiles/ncu_traffic.json), or None."""
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return d.get(kernel_key, {}).get("dram_bytes_per_launch")
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    """Samples SM clock and throttle reasons of one GPU through NVML (read-only)."""
+
+    REASONS = [
+        ("gpu_idle", 0x1), ("applications_clocks_setting", 0x2), ("sw_power_cap", 0x4),
+        ("hw_slowdown", 0x8), ("sync_boost", 0x10), ("sw_thermal_slowdown", 0x20),
+        ("hw_thermal_slowdown", 0x40), ("hw_power_brake_slowdown", 0x80), ("display_clock_setting", 0x100),
+    ]
+
+    def __init__(self, uuid, period=0.005):
+        self.samples = []
+        self.reasons = 0
+        self.period = period
+        self._stop = threading.Event()
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.max_mhz = None
+
+    def _sample(self):
+        try:
+            self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+            self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        except Exception:
+            pass
+
+    def _run(self):
+        while not self._stop.is_set():
+            self._sample()
+            time.sleep(self.period)
+
+    def start(self):
+        if self.ok:
+            self._sample()
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+
+    def stop(self):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+            self._sample()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml_unavailable"], "samples": 0}
+        reasons = [n for n, bit in self.REASONS if self.reasons & bit and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline / reference arm: the oracle port of the reference's x86 path
+# ---------------------------------------------------------------------------
+def cpu_workload(seed=0, lm_rows=None):
+    import numpy as np
+
+    from hy_mt_rs_b200 import synth
+
+    layers = {}
+    for fmt in (5, 6):
+        layers[fmt] = [(name, N, K, synth.random_packed(fmt, N, K, seed=seed + 100 * fmt + i).numpy())
+                       for i, (name, N, K) in enumerate(LAYER)]
+    lm_rows = lm_rows or VOCAB
+    lm = synth.random_packed(3, lm_rows, HIDDEN, seed=seed + 7).numpy()
+    x = np.random.default_rng(seed).standard_normal(HIDDEN).astype(np.float32)
+    return layers, lm, lm_rows, x
+
+
+def cpu_step(layers, lm, lm_rows, x, threads=0):
+    """One pass of the chain through the oracle (x86 f32 order)."""
+    from oracle import oracle as O
+
+    h = x
+    for fmt in (5, 6):
+        L = {name: (N, K, p) for name, N, K, p in layers[fmt]}
+        q = O.matmul(fmt, L["attn_q"][2], HIDDEN, HIDDEN, h, 1, threads)[0]
+        O.matmul(fmt, L["attn_k"][2], HIDDEN, KV, h, 1, threads)
+        O.matmul(fmt, L["attn_v"][2], HIDDEN, KV, h, 1, threads)
+        o = O.matmul(fmt, L["attn_output"][2], HIDDEN, HIDDEN, q, 1, threads)[0]
+        g = O.gate_up_silu(fmt, L["ffn_gate"][2], L["ffn_up"][2], HIDDEN, FFN, o, threads)
+        h = O.matmul(fmt, L["ffn_down"][2], FFN, HIDDEN, g, 1, threads)[0]
+    return O.matmul(3, lm, HIDDEN, lm_rows, h, 1, threads)[0]
+
+
+def cpu_step_bytes(lm_rows):
+    return layer_bytes(5) + layer_bytes(6) + gemv_bytes(3, lm_rows, HIDDEN)
+
+
+def run_cpu(seconds, lm_rows):
+    from oracle import oracle as O
+
+    layers, lm, lm_rows, x = cpu_workload(lm_rows=lm_rows)
+    cpu_step(layers, lm, lm_rows, x)  # warm
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        cpu_step(layers, lm, lm_rows, x)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    gbs = n * cpu_step_bytes(lm_rows) / el / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": O.max_threads(), "kind": "port",
+            "sample": f"{n} passes of the full chain with the lm_head cut to {lm_rows} of {VOCAB} rows "
+                      f"({el:.1f} s); oracle/hyq_oracle.c x86 f32 order, OpenMP"}
+
+
+def reference_arm(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from oracle import oracle as O
+
+    lm_rows = VOCAB // 16
+    layers, lm, lm_rows, x = cpu_workload(lm_rows=lm_rows)
+    for _ in range(a.warmup):
+        cpu_step(layers, lm, lm_rows, x)
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        cpu_step(layers, lm, lm_rows, x)
+    el = time.perf_counter() - t0
+    gbs = a.steps * cpu_step_bytes(lm_rows) / el / 1e9
+    sample = (f"each step: both layers in full + lm_head rows 0..{lm_rows} of {VOCAB} "
+              f"(CPU port of the reference's x86 f32 path, oracle/hyq_oracle.c)")
+    line = {
+        "metric": "quantized GEMV HBM GB/s (1.8B layer projections Q2_0C+STQ1_0 + Q6_K lm_head, batch 1)",
+        "value": round(gbs, 3), "unit": "GB/s", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": round(el / a.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "hy-mt-rs config 2: 1.8B decoder-layer projections (Q2_0C, STQ1_0) + Q6_K lm_head "
+                               "120832x2048, batch 1", "path": "f32"},
+        "impl": "reference",
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": O.max_threads(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def build_weights(dev, copies, seed=0):
+    from hy_mt_rs_b200 import quant, synth
+
+    layers = {5: [], 6: []}
+    for fmt in (5, 6):
+        for c in range(copies):
+            L = {}
+            for i, (name, N, K) in enumerate(LAYER):
+                packed = synth.random_packed(fmt, N, K, seed=seed + 1000 * c + 100 * fmt + i, device=dev)
+                L[name] = quant.Weight(packed, fmt, [K, N], name=name)
+            layers[fmt].append(L)
+    lm = quant.Weight(synth.random_packed(3, VOCAB, HIDDEN, seed=seed + 7, device=dev), 3, [HIDDEN, VOCAB],
+                      name="output")
+    return layers, lm
+
+
+def layer_chain(L, h, path, q8h=None, q8f=None):
+    """Projections of one decoder layer (model.rs:403-538 order)."""
+    from hy_mt_rs_b200.quant import Weight
+
+    if path == "f32":
+        q, k, v = Weight.gemv_qkv(L["attn_q"], L["attn_k"], L["attn_v"], h)
+        o = L["attn_output"].matmul(q, 1)[0]  # attention output stands in as q (same width)
+        g = L["ffn_gate"].matmul_gate_up_silu(L["ffn_up"], o)
+        return L["ffn_down"].matmul(g, 1)[0]
+    q8h.quantize_into(h)
+    q, k, v = Weight.gemv_qkv_fast(L["attn_q"], L["attn_k"], L["attn_v"], q8h)
+    q8h.quantize_into(q)
+    o = L["attn_output"].gemv_q8_fast(q8h)
+    q8h.quantize_into(o)
+    g = L["ffn_gate"].matmul_gate_up_silu_fast(L["ffn_up"], q8h)
+    q8f.quantize_into(g)
+    return L["ffn_down"].gemv_q8_fast(q8f)
+
+
+def lm_head(lm, h, path, q8h=None):
+    if path == "f32":
+        return lm.matmul(h, 1)[0]
+    q8h.quantize_into(h)
+    return lm.gemv_q8_fast(q8h)
+
+
+def gpu_arm(a):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(dev)
+
+    import hy_mt_rs_b200  # noqa: F401
+    from hy_mt_rs_b200 import quant
+
+    copies = max(1, a.copies)
+    layers, lm = build_weights(dev, copies)
+    path = a.path
+    x_static = torch.randn(HIDDEN, generator=torch.Generator().manual_seed(0)).to(dev)
+    q8h = quant.Q8(HIDDEN, dev)
+    q8f = quant.Q8(FFN, dev)
+
+    # One graph per (format, copy) for the layer chain, one for the lm_head.
+    stream = torch.cuda.Stream(dev)
+    h_mid = {}
+    graphs = {}
+    with torch.cuda.stream(stream):
+        for _ in range(2):  # warm every path (plans, smem attributes, status word)
+            h = x_static
+            for fmt in (5, 6):
+                for c in range(copies):
+                    hh = layer_chain(layers[fmt][c], h, path, q8h, q8f)
+                h = hh
+            lm_head(lm, h, path, q8h)
+        stream.synchronize()
+        for c in range(copies):
+            h = x_static
+            for fmt in (5, 6):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    out = layer_chain(layers[fmt][c], h, path, q8h, q8f)
+                graphs[(fmt, c)] = g
+                h_mid[(fmt, c)] = out
+                h = out
+        # all copies end in the same buffer role; the lm_head reads copy 0's output
+        h_last = h_mid[(6, 0)]
+        g_lm = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_lm, stream=stream):
+            logits = lm_head(lm, h_last, path, q8h)
+    launches_per_step = (4 if path == "f32" else 8) * 2 + (1 if path == "f32" else 2)
+
+    def step(i, evs=None):
+        c = i % copies
+        if evs is not None:
+            evs[0].record(stream)
+        graphs[(5, c)].replay()
+        if evs is not None:
+            evs[1].record(stream)
+        graphs[(6, c)].replay()
+        if evs is not None:
+            evs[2].record(stream)
+        g_lm.replay()
+        if evs is not None:
+            evs[3].record(stream)
+
+    with torch.cuda.stream(stream):
+        for i in range(a.warmup):
+            step(i)
+    stream.synchronize()
+
+    sampler = ClockSampler("GPU-" + str(torch.cuda.get_device_properties(dev).uuid))
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(a.steps)]
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    sampler.start()
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for i in range(a.steps):
+            step(i, evs[i])
+        end.record(stream)
+    stream.synchronize()
+    torch.cuda.synchronize(dev)
+    sampler.stop()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    t_q2 = statistics.fmean(e[0].elapsed_time(e[1]) for e in evs)
+    t_stq = statistics.fmean(e[1].elapsed_time(e[2]) for e in evs)
+    t_lm = statistics.fmean(e[2].elapsed_time(e[3]) for e in evs)
+    assert quant.device_status(dev) == 0
+
+    # ---- e2e: host buffers through the public API, copies inside the region
+    x_host = torch.randn(HIDDEN, generator=torch.Generator().manual_seed(1)).pin_memory()
+    logits_host = torch.empty(VOCAB, dtype=torch.float32).pin_memory()
+    e2e_steps = a.steps
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            x_static.copy_(x_host, non_blocking=True)
+            step(i)
+            logits_host.copy_(logits, non_blocking=True)
+        stream.synchronize()
+        e0.record(stream)
+        for i in range(e2e_steps):
+            x_static.copy_(x_host, non_blocking=True)
+            step(i)
+            logits_host.copy_(logits, non_blocking=True)
+            stream.synchronize()  # a decode loop needs the logits on the host every token
+        e1.record(stream)
+    stream.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+
+    step_bytes = layer_bytes(5) + layer_bytes(6) + gemv_bytes(3, VOCAB, HIDDEN)
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0]), float(t[1])
+        clocks_all = [None] * world
+        dist.all_gather_object(clocks_all, sampler.summary())
+    else:
+        clocks_all = [sampler.summary()]
+
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        lm_bytes = gemv_bytes(3, VOCAB, HIDDEN)
+        achieved = lm_bytes / (t_lm * 1e-3) / 1e9
+        value = step_bytes * a.steps * world / (ms * 1e-3) / 1e9
+        e2e_value = step_bytes * e2e_steps * world / (e2e_ms * 1e-3) / 1e9
+        sm = [c["sm_mhz"] for c in clocks_all if c.get("sm_mhz")]
+        reasons = sorted({r for c in clocks_all for r in c.get("reasons", [])})
+        kernel_key = f"lm_head_{path}"
+        line = {
+            "metric": "quantized GEMV HBM GB/s (1.8B layer projections Q2_0C+STQ1_0 + Q6_K lm_head, batch 1)",
+            "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": round(ms / a.steps, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32 activations x packed int weights (exact int32 dp4a, f32 accumulate)" if path == "f32"
+                     else "int8 activations (Q8, per-256 scale) x packed int weights",
+            "data": "synthetic (seeded N(0,0.02) weights packed by hy_mt_rs_b200.synth; N(0,1) activations)",
+            "config": {"workload": "hy-mt-rs config 2: 1.8B decoder-layer projections (Q2_0C, STQ1_0) + "
+                                   "Q6_K lm_head 120832x2048, batch 1",
+                       "path": path, "layer_copies": copies, "step_bytes": step_bytes,
+                       "l2": "inputs larger than L2: every step streams the 203 MB lm_head; layers rotate copies",
+                       "parallelism": f"replicas x{world} (rows are independent; no collective)"},
+            "roofline": {"bound": "hbm", "kernel": f"lm_head Q6_K {path} GEMV", "achieved": round(achieved, 1),
+                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": profile_traffic(kernel_key),
+                         "algorithmic_bytes_per_launch": lm_bytes, "avg_launch_ms": round(t_lm, 5)},
+            "per_stage_ms": {"q2_0c_layer": round(t_q2, 5), "stq1_0_layer": round(t_stq, 5),
+                             "q6k_lm_head": round(t_lm, 5)},
+            "decode_tok_s_projection_only": {
+                "q2_0c": round(1e3 / (N_LAYERS_MODEL * t_q2 + t_lm), 1),
+                "stq1_0": round(1e3 / (N_LAYERS_MODEL * t_stq + t_lm), 1)},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * HIDDEN,
+                    "d2h_bytes_per_step": 4 * VOCAB, "ms_per_step": round(e2e_ms / e2e_steps, 5),
+                    "how": "pinned host x -> device, graph-replayed public-API chain, logits -> pinned host, "
+                           "stream sync per step"},
+            "gpu_launches": launches_per_step * a.steps,
+            "clocks": {"sm_mhz": statistics.median(sm) if sm else None,
+                       "sm_max_mhz": clocks_all[0].get("sm_max_mhz"), "reasons": reasons,
+                       "samples": sum(c.get("samples", 0) for c in clocks_all)},
+        }
+        if world == 1:
+            line["cpu_baseline"] = run_cpu(a.cpu_seconds, VOCAB // 16)
+        print(json.dumps(line), flush=True)
+    for g in list(graphs.values()) + [g_lm]:
+        del g
+    graphs.clear()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    a = args_parse()
+    if a.impl == "reference":
+        return reference_arm(a)
+    return gpu_arm(a)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

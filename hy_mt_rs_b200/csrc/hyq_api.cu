@@ -261,7 +261,7 @@ int hyq_weight_row_into(const hyq_weight* w, int64_t row, float* out, int64_t ou
 }
 
 int hyq_dot(const float* a, const float* b, size_t n, float* out, void* stream) {
-  if (!a || !b || !out) return fail(HYQ_E_INVALID, "dot: null pointer");
+  if (!out || (n && (!a || !b))) return fail(HYQ_E_INVALID, "dot: null pointer");
   return launch_status(hyq::launch_dot(a, b, (int64_t)n, out, (cudaStream_t)stream), "dot");
 }
 

@@ -1,0 +1,41 @@
+"""Run one batch-1 product shape a few times, for profiler captures.
+
+    python -m hy_mt_rs_b200.profile_gemv --dtype Q6_K --rows 120832 --cols 2048 \
+        --path f32 --iters 3
+
+Every iteration is one launch of the product kernel (plus one Q8 launch
+with --path q8).  Weights are seeded synthetic (hy_mt_rs_b200.synth).
+"""
+import argparse
+
+import torch
+
+from . import quant, synth
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--dtype", default="Q6_K", choices=[d.name for d in quant.DType])
+    ap.add_argument("--rows", type=int, default=120832)
+    ap.add_argument("--cols", type=int, default=2048)
+    ap.add_argument("--path", choices=["f32", "q8"], default="f32")
+    ap.add_argument("--iters", type=int, default=3)
+    a = ap.parse_args()
+    dev = torch.device("cuda", 0)
+    t = quant.DType[a.dtype]
+    w = quant.Weight(synth.random_packed(t, a.rows, a.cols, seed=1, device=dev), t, [a.cols, a.rows])
+    x = torch.randn(a.cols, generator=torch.Generator().manual_seed(0)).to(dev)
+    q8 = quant.Q8(a.cols, dev)
+    for _ in range(a.iters):
+        if a.path == "f32":
+            w.matmul(x, 1)
+        else:
+            q8.quantize_into(x)
+            w.gemv_q8_fast(q8)
+    torch.cuda.synchronize()
+    assert quant.device_status() == 0
+    print("ok")
+
+
+if __name__ == "__main__":
+    main()

@@ -59,7 +59,12 @@ def test_decode_matches_oracle_bits(cuda, t):
     out = torch.empty(n, dtype=torch.float32, device=cuda)
     quant.decode(t, to_dev(blob, cuda), out)
     got = out.cpu().numpy()
-    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+    # Bit-exact for every non-NaN value.  NaN payloads are platform-defined
+    # (the reference itself yields different NaN bits on x86 and aarch64;
+    # GPU arithmetic returns the canonical NaN), so NaNs compare by position.
+    nan = np.isnan(ref)
+    assert np.array_equal(np.isnan(got), nan)
+    assert np.array_equal(got.view(np.uint32)[~nan], ref.view(np.uint32)[~nan])
 
 
 def test_decode_shape_errors(cuda):
