@@ -273,21 +273,18 @@ def layer_chain(L, h, path, q8h=None, q8f=None):
         o = L["attn_output"].matmul(q, 1)[0]  # attention output stands in as q (same width)
         g = L["ffn_gate"].matmul_gate_up_silu(L["ffn_up"], o)
         return L["ffn_down"].matmul(g, 1)[0]
-    q8h.quantize_into(h)
-    q, k, v = Weight.gemv_qkv_fast(L["attn_q"], L["attn_k"], L["attn_v"], q8h)
-    q8h.quantize_into(q)
-    o = L["attn_output"].gemv_q8_fast(q8h)
-    q8h.quantize_into(o)
-    g = L["ffn_gate"].matmul_gate_up_silu_fast(L["ffn_up"], q8h)
-    q8f.quantize_into(g)
-    return L["ffn_down"].gemv_q8_fast(q8f)
+    # int8 activations quantized inside each product kernel (one launch per
+    # projection group, as the reference quantizes once per group)
+    q, k, v = Weight.gemv_qkv_int8(L["attn_q"], L["attn_k"], L["attn_v"], h)
+    o = L["attn_output"].gemv_int8(q)
+    g = L["ffn_gate"].matmul_gate_up_silu_int8(L["ffn_up"], o)
+    return L["ffn_down"].gemv_int8(g)
 
 
 def lm_head(lm, h, path, q8h=None):
     if path == "f32":
         return lm.matmul(h, 1)[0]
-    q8h.quantize_into(h)
-    return lm.gemv_q8_fast(q8h)
+    return lm.gemv_int8(h)
 
 
 def gpu_arm(a):
@@ -341,7 +338,7 @@ def gpu_arm(a):
         g_lm = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g_lm, stream=stream):
             logits = lm_head(lm, h_last, path, q8h)
-    launches_per_step = (4 if path == "f32" else 8) * 2 + (1 if path == "f32" else 2)
+    launches_per_step = 4 * 2 + 1
 
     def step(i, evs=None):
         c = i % copies

@@ -1,6 +1,8 @@
 """Build libhyq.so (the C-ABI CUDA library) in-tree for sm_100a.
 
-    python -m hy_mt_rs_b200.build [--force] [-v]
+    python hy_mt_rs_b200/build.py [--force] [-v]
+
+(run it by path: importing the package loads the library it builds)
 
 Each csrc/*.cu is compiled with nvcc for sm_100a only and linked into
 hy_mt_rs_b200/lib/libhyq.so.  Objects go to hy_mt_rs_b200/_build/.

@@ -132,6 +132,7 @@ struct Act {
   const float* x = nullptr;
   const int8_t* xq = nullptr;
   const float* xs = nullptr;
+  bool quantize = false;  // x is quantized to Q8 inside the kernel
 };
 
 int run_gemv(int n_mat, const hyq_weight* const* ws, float* const* ys, const hyq_weight* up, const Act& a,
@@ -152,8 +153,12 @@ int run_gemv(int n_mat, const hyq_weight* const* ws, float* const* ys, const hyq
   j.x = a.x;
   j.xq = a.xq;
   j.xs = a.xs;
+  j.quantize_q8 = a.quantize;
   j.status = status;
-  return launch_status(hyq::launch_gemv(j, st), name);
+  const cudaError_t e = hyq::launch_gemv(j, st);
+  if (e == cudaErrorNotSupported)
+    return fail(HYQ_E_UNSUPPORTED, "%s: in-kernel Q8 needs K to be a multiple of 256 for this buffer layout", name);
+  return launch_status(e, name);
 }
 
 int check_act(const Act& a, const char* name) {
@@ -381,6 +386,41 @@ int hyq_matmul_gate_up_silu_q8(const hyq_weight* gate, const hyq_weight* up, con
   a.xs = scales;
   if ((rc = check_act(a, "gate_up_silu_q8"))) return rc;
   return run_gemv(1, &gate, &out, up, a, (cudaStream_t)stream, "gate_up_silu_q8");
+}
+
+int hyq_gemv_int8(const hyq_weight* w, const float* input, float* out, void* stream) {
+  int rc = check_matrix(w, "gemv_int8");
+  if (rc) return rc;
+  if (!input || !out) return fail(HYQ_E_INVALID, "gemv_int8: null pointer");
+  Act a;
+  a.x = input;
+  a.quantize = true;
+  if ((rc = check_act(a, "gemv_int8"))) return rc;
+  return run_gemv(1, &w, &out, nullptr, a, (cudaStream_t)stream, "gemv_int8");
+}
+
+int hyq_gemv_qkv_int8(const hyq_weight* q, const hyq_weight* k, const hyq_weight* v, const float* input,
+                      float* q_out, float* k_out, float* v_out, void* stream) {
+  int rc = qkv_checks(q, k, v);
+  if (rc) return rc;
+  if (!input) return fail(HYQ_E_INVALID, "qkv_int8: null input");
+  Act a;
+  a.x = input;
+  a.quantize = true;
+  if ((rc = check_act(a, "qkv_int8"))) return rc;
+  return qkv_run(q, k, v, a, q_out, k_out, v_out, (cudaStream_t)stream);
+}
+
+int hyq_matmul_gate_up_silu_int8(const hyq_weight* gate, const hyq_weight* up, const float* input, float* out,
+                                 void* stream) {
+  int rc = gate_up_checks(gate, up);
+  if (rc) return rc;
+  if (!input || !out) return fail(HYQ_E_INVALID, "gate_up_silu_int8: null pointer");
+  Act a;
+  a.x = input;
+  a.quantize = true;
+  if ((rc = check_act(a, "gate_up_silu_int8"))) return rc;
+  return run_gemv(1, &gate, &out, up, a, (cudaStream_t)stream, "gate_up_silu_int8");
 }
 
 int hyq_device_status(void* stream, uint32_t* status_out) {

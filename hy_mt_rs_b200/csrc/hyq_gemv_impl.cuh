@@ -1,0 +1,765 @@
+// Batch-1 matrix-vector products over packed GGUF rows (sm_100a): kernels.
+// Included by one translation unit per packed format (hyq_gemv_<fmt>.cu).
+//
+// Reference behaviour (hy-mt-rs src/quant.rs):
+//   Weight::matmul batch 1          :159-270   (f32 activations)
+//   gemv_q8 (quantize + SDOT rows)  :346-380   (int8 activations)
+//   gemv_q8_fast / compute_chunk_q8 :353-439
+//   gemv_qkv(_fast)                 :441-538, :653-721
+//   matmul_gate_up_silu(_fast)      :540-651, :723-841
+//
+// Engine.  Rows are streamed, never re-read: a persistent CTA per SM owns a
+// ring of shared-memory stages; one producer thread fills each stage with a
+// tile of consecutive packed rows using cp.async.bulk (one contiguous copy of
+// the packed bytes, unchanged) and an mbarrier transaction count; 12 consumer
+// warps decode the codes out of shared memory and reduce them against the
+// activations.  The activations are prepared once per CTA into shared memory
+// in the order the codes come out of each format's decoder, then every lane
+// keeps the 64-column "units" it owns in registers for the CTA's lifetime.  A
+// row is split over KS warps when K is too wide for one warp's registers or
+// when splitting gives the grid enough row tiles.
+//
+// Arithmetic.  Codes are multiplied in the integer domain with dp4a:
+//   XQ8 / XQ8F (NP=1): the reference's Q8 activations, given (gemv_q8_fast)
+//     or computed in the CTA prologue from f32 input exactly as
+//     Q8::quantize_into does (gemv_q8); per 256-column group the exact
+//     integer sum is scaled by (weight scale * activation scale), as the SDOT
+//     kernels do (quant.rs:1511-1557, 1891-1955, 2257-2332).
+//   XF32 (NP=3): each f32 activation is written as a 24-bit integer X times
+//     a power-of-two group scale 2^(e-22) (e = exponent of the 256-column
+//     group's max |x|) and split exactly into three signed bytes.  Products
+//     and sums are exact integers; the only roundings are |dX| <= 1/2 per
+//     activation (2^(e-23) absolute) and the final f32 accumulation: f32-level
+//     accuracy.
+#pragma once
+
+#include "hyq_common.cuh"
+#include "hyq_formats.cuh"
+#include "hyq_kernels.h"
+
+namespace hyq {
+namespace gemv {
+
+constexpr int kCW = 12;                    // consumer warps (13 warps: <= 128 registers)
+constexpr int kThreads = (kCW + 1) * 32;   // + one producer warp
+constexpr int kMaxStages = 32;
+constexpr int kRedOffset = 528;            // partial sums: 2 copies x 12 warps x 4 rows x (gate, up)
+constexpr int kHeaderBytes = 2048;         // barriers [0,512), abort flag, partial sums [528,1296)
+constexpr int kConsumerBarrier = 15;       // named barrier of the 12 consumer warps
+
+// Activation modes.
+enum XMode : int { XF32 = 0, XQ8 = 1, XQ8F = 2 };
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t ld_s32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t ld_s16(uint32_t a) {
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+  return v;
+}
+
+__device__ __forceinline__ uint4 ld_s128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+
+// N consecutive 32-bit words at a 2-byte aligned shared address (reads one
+// word past the span when the address is 4-byte aligned).
+template <int N>
+__device__ __forceinline__ void ld_s_words(uint32_t a, uint32_t (&out)[N]) {
+  const uint32_t base = a & ~3u;
+  const uint32_t sh = (a & 2u) * 8u;
+  uint32_t t[N + 1];
+#pragma unroll
+  for (int i = 0; i <= N; ++i) t[i] = ld_s32(base + 4 * i);
+#pragma unroll
+  for (int i = 0; i < N; ++i) out[i] = __funnelshift_r(t[i], t[i + 1], sh);
+}
+
+struct MatDev {
+  const uint8_t* w;
+  float* y;
+  int64_t rows;
+  int64_t batch_begin;
+};
+
+struct Params {
+  MatDev mat[3];
+  const uint8_t* up;
+  int n_mat;
+  int64_t total_batches;
+  int K, U, row_bytes;
+  int ks, rg, slice;   // K-split, row groups (rg*ks == kCW), units per slice
+  int stages;
+  int half_bytes;      // bytes of one row-tile buffer
+  int stage_bytes;
+  int x_off;           // shared-memory offset of the prepared activations
+  int stage_off;       // shared-memory offset of stage 0
+  int xmode;
+  const float* x;      // XF32 / XQ8F
+  const int8_t* xq;    // XQ8
+  const float* xs;     // XQ8
+  unsigned* status;
+};
+
+// ---------------------------------------------------------------------------
+// Unit geometry.  A unit is 64 columns that one lane owns; its columns are
+// listed in "unit order" (two runs of 32), and code word j byte b of the
+// decoded unit multiplies column rel(j, b) of that list.
+// ---------------------------------------------------------------------------
+template <int FMT>
+__device__ __forceinline__ void unit_runs(int u, int& c0, int& c1) {
+  if (FMT == Q6_K) {
+    const int B = u >> 2, c = (u >> 1) & 1, pp = u & 1;
+    c0 = B * 256 + c * 128 + pp * 32;  // plane pp of chunk c, then plane pp+2
+    c1 = c0 + 64;
+  } else {
+    c0 = u * 64;
+    c1 = c0 + 32;
+  }
+}
+
+template <int FMT>
+__host__ __device__ constexpr int rel(int j, int b) {
+  return FMT == Q2_0C ? 16 * (j >> 2) + 4 * b + (j & 3)
+       : FMT == STQ1_0 ? 16 * (j & 3) + 4 * (j >> 2) + b
+       : 4 * j + b;
+}
+
+template <int FMT>
+__device__ __forceinline__ int unit_col(int u, int r) {
+  int c0, c1;
+  unit_runs<FMT>(u, c0, c1);
+  return r < 32 ? c0 + r : c1 + (r - 32);
+}
+
+template <int FMT>
+__host__ __device__ constexpr int nseg() {
+  return FMT == Q6_K ? 4 : ((FMT == Q4_K || FMT == Q8_0) ? 2 : 1);
+}
+
+template <int NP>
+struct XUnit {
+  uint32_t w[NP][16];
+  int xsum[4];
+  float sg;
+};
+
+struct WUnit {
+  uint32_t c[16];
+  float s[4];
+  float m[2];
+};
+
+// ---------------------------------------------------------------------------
+// Activation prologue: all consumer threads write the activations of every
+// unit into shared memory as words[piece][j][u] (u fastest), plus one scale
+// per 256-column group; each lane then loads its own units into registers.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void consumers_sync() {
+  asm volatile("bar.sync %0, %1;" ::"r"(kConsumerBarrier), "r"(kCW * 32) : "memory");
+}
+
+template <int FMT, int NP>
+__device__ void prepare_x(const Params& p, uint8_t* smem) {
+  uint32_t* words = reinterpret_cast<uint32_t*>(smem + p.x_off);
+  const int U = p.U, G = U >> 2;
+  float* sg = reinterpret_cast<float*>(words + NP * 16 * U);
+  float* gaux = sg + G;  // XF32: 2^(22-e); XQ8F: 127/max
+  const int ctid = threadIdx.x, warp = ctid >> 5, lane = ctid & 31;
+  if (p.xmode == XQ8) {
+    for (int g = ctid; g < G; g += kCW * 32) sg[g] = p.xs[g];
+  } else {
+    // Group maxima: one warp per 256-column group.
+    for (int g = warp; g < G; g += kCW) {
+      const float4* src = reinterpret_cast<const float4*>(p.x + 256 * g);
+      const float4 a = src[lane], b = src[32 + lane];
+      const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      float m = 0.f;
+      int bad = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float av = fabsf(v[i]);
+        bad |= isnan(av) ? 1 : 0;
+        bad |= (NP == 3 && isinf(av)) ? 1 : 0;
+        m = fmaxf(m, av);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+      }
+      if (lane == 0) {
+        if (NP == 3) {
+          // |x| <= m < 2^e: x * 2^(22-e) is an exact scaling below 2^22.
+          int e = 0;
+          frexpf(m, &e);
+          if (bad) {
+            sg[g] = __int_as_float(0x7fc00000);
+            gaux[g] = 0.f;
+          } else if (22 - e <= 127 && e - 22 >= -126) {
+            sg[g] = __int_as_float((127 + e - 22) << 23);
+            gaux[g] = __int_as_float((127 + 22 - e) << 23);
+          } else {
+            sg[g] = ldexpf(1.f, e - 22);
+            gaux[g] = ldexpf(1.f, 22 - e);
+          }
+        } else {
+          // Q8::quantize_into (quant.rs:904-922): a NaN in the group makes the
+          // max NaN (NEON fmax), and then scale = inverse = 0.
+          const float mm = bad ? __int_as_float(0x7fc00000) : m;
+          float scale = 0.f, inverse = 0.f;
+          if (mm > 0.f) {
+            scale = __fdiv_rn(mm, 127.f);
+            inverse = __fdiv_rn(127.f, mm);
+          }
+          sg[g] = scale;
+          gaux[g] = inverse;
+        }
+      }
+    }
+    consumers_sync();
+  }
+  for (int idx = ctid; idx < 16 * U; idx += kCW * 32) {
+    const int u = idx % U, j = idx / U;
+    uint32_t w0 = 0, w1 = 0, w2 = 0;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int col = unit_col<FMT>(u, rel<FMT>(j, b));
+      if (p.xmode == XQ8) {
+        w0 |= ((uint32_t)(uint8_t)p.xq[col]) << (8 * b);
+      } else if (p.xmode == XQ8F) {
+        // vcvtnq_s32_f32 + saturating narrows: nearest-even, NaN -> 0.
+        const float s = __fmul_rn(p.x[col], gaux[u >> 2]);
+        const int q = isnan(s) ? 0 : max(-128, min(127, __float2int_rn(s)));
+        w0 |= ((uint32_t)q & 0xffu) << (8 * b);
+      } else {
+        const float sc = gaux[u >> 2];
+        const int X = sc == 0.f ? 0 : __float2int_rn(p.x[col] * sc);
+        const int p0 = (int)(int8_t)(X & 0xff);
+        const int t = (X - p0) >> 8;
+        const int p1 = (int)(int8_t)(t & 0xff);
+        const int p2 = (t - p1) >> 8;
+        w0 |= ((uint32_t)p0 & 0xffu) << (8 * b);
+        w1 |= ((uint32_t)p1 & 0xffu) << (8 * b);
+        w2 |= ((uint32_t)p2 & 0xffu) << (8 * b);
+      }
+    }
+    words[j * U + u] = w0;
+    if (NP == 3) {
+      words[(16 + j) * U + u] = w1;
+      words[(32 + j) * U + u] = w2;
+    }
+  }
+  consumers_sync();
+}
+
+template <int FMT, int NP>
+__device__ __forceinline__ void load_x(const Params& p, const uint8_t* smem, int u, bool valid, XUnit<NP>& xu) {
+  const uint32_t* words = reinterpret_cast<const uint32_t*>(smem + p.x_off);
+  const float* sg = reinterpret_cast<const float*>(words + NP * 16 * p.U);
+  constexpr int NS = nseg<FMT>(), WPS = 16 / NS;
+#pragma unroll
+  for (int pc = 0; pc < NP; ++pc)
+#pragma unroll
+    for (int j = 0; j < 16; ++j) xu.w[pc][j] = valid ? words[(pc * 16 + j) * p.U + u] : 0u;
+  xu.sg = valid ? sg[u >> 2] : 0.f;
+#pragma unroll
+  for (int s = 0; s < 4; ++s) xu.xsum[s] = 0;
+#pragma unroll
+  for (int s = 0; s < NS; ++s) {
+    int a0 = 0, a1 = 0, a2 = 0;
+#pragma unroll
+    for (int j = s * WPS; j < (s + 1) * WPS; ++j) {
+      a0 = __dp4a((int)xu.w[0][j], 0x01010101, a0);
+      if (NP == 3) {
+        a1 = __dp4a((int)xu.w[NP > 1 ? 1 : 0][j], 0x01010101, a1);
+        a2 = __dp4a((int)xu.w[NP > 2 ? 2 : 0][j], 0x01010101, a2);
+      }
+    }
+    xu.xsum[s] = NP == 3 ? a0 + (a1 << 8) + (a2 << 16) : a0;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Weight unit decode from shared memory.  `row` is the shared address of the
+// row (2-byte aligned; Q4_K rows are 16-byte aligned).
+// ---------------------------------------------------------------------------
+template <int FMT>
+__device__ __forceinline__ void decode_unit(uint32_t row, int u, WUnit& wu) {
+  if (FMT == Q2_0C) {
+    // quant.rs:2419-2432: 2-bit code c -> (2c - 3) * d, four codes per byte.
+    const uint32_t blk = row + (u >> 3) * 130;
+    wu.s[0] = half_to_f32(ld_s16(blk));
+    uint32_t q[4];
+    ld_s_words<4>(blk + 2 + 16 * (u & 7), q);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) wu.c[4 * i + k] = (q[i] >> (2 * k)) & 0x03030303u;
+  } else if (FMT == STQ1_0) {
+    // quant.rs:1103-1123: group g of chunk c: codebook[(sign << 4) | nibble],
+    // lane p -> column 16p + (g % 16).  Four groups at a time: PRMT looks the
+    // codebook up in registers, byte masks pick the half by nibble bit 3 and
+    // by the sign bit.
+    const uint32_t blk = row + (u >> 2) * 42;
+    const int c = u & 3;
+    wu.s[0] = half_to_f32(ld_s16(blk + 40));
+    uint32_t nb[2];
+    ld_s_words<2>(blk + 8 * c, nb);
+    const uint32_t sbits = ld_s16(blk + 32 + 2 * c);
+    const uint32_t T0 = 0x092989a9u, T1 = 0x062686a6u, T2 = 0x121a929au, T3 = 0x424a626au;
+    const uint32_t T4 = 0xa1812101u, T5 = 0xa4842404u, T6 = 0x98901810u, T7 = 0x68604840u;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t hw = (i & 1) ? (nb[i >> 1] >> 16) : (nb[i >> 1] & 0xffffu);
+      const uint32_t sel = hw & 0x7777u;
+      const uint32_t p0 = prmt(T0, T1, sel), p1 = prmt(T2, T3, sel);
+      const uint32_t p2 = prmt(T4, T5, sel), p3 = prmt(T6, T7, sel);
+      const uint32_t m3 = prmt(hw << 4, hw, 0xD9C8u);
+      const uint32_t s4 = (sbits >> (4 * i)) & 15u;
+      const uint32_t sm = prmt(s4 * 0x10204080u, 0u, 0xBA98u);
+      const uint32_t lo = (p0 & ~m3) | (p1 & m3);
+      const uint32_t hi = (p2 & ~m3) | (p3 & m3);
+      const uint32_t cb = (lo & ~sm) | (hi & sm);
+#pragma unroll
+      for (int pl = 0; pl < 4; ++pl) wu.c[4 * i + pl] = (cb >> (2 * pl)) & 0x03030303u;
+    }
+  } else if (FMT == Q4_K) {
+    // quant.rs:2437-2461.
+    const uint32_t blk = row + (u >> 2) * 144;
+    const int g = u & 3;
+    const uint4 h = ld_s128(blk);
+    const float d = half_to_f32(h.x & 0xffffu), dmin = half_to_f32(h.x >> 16);
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int j = 2 * g + hh;
+      uint32_t s, m;
+      if (j < 4) {
+        s = (h.y >> (8 * j)) & 63u;
+        m = (h.z >> (8 * j)) & 63u;
+      } else {
+        const int k = j - 4;
+        const uint32_t hi = (h.w >> (8 * k)) & 0xffu;
+        s = (hi & 15u) | ((((h.y >> (8 * k)) & 0xffu) >> 6) << 4);
+        m = (hi >> 4) | ((((h.z >> (8 * k)) & 0xffu) >> 6) << 4);
+      }
+      wu.s[hh] = d * (float)s;
+      wu.m[hh] = dmin * (float)m;
+    }
+    const uint4 q0 = ld_s128(blk + 16 + 32 * g);
+    const uint4 q1 = ld_s128(blk + 32 + 32 * g);
+    const uint32_t q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      wu.c[i] = q[i] & 0x0f0f0f0fu;
+      wu.c[8 + i] = (q[i] >> 4) & 0x0f0f0f0fu;
+    }
+  } else if (FMT == Q6_K) {
+    // quant.rs:2462-2483; this unit holds planes pp and pp+2 of chunk c.
+    const uint32_t blk = row + (u >> 2) * 210;
+    const int c = (u >> 1) & 1, pp = u & 1;
+    uint32_t ql[8], qh[8];
+    ld_s_words<8>(blk + 64 * c + 32 * pp, ql);
+    ld_s_words<8>(blk + 128 + 32 * c, qh);
+    const uint32_t s01 = ld_s16(blk + 192 + 8 * c + 2 * pp);
+    const uint32_t s45 = ld_s16(blk + 196 + 8 * c + 2 * pp);
+    wu.m[0] = half_to_f32(ld_s16(blk + 208));
+    wu.s[0] = (float)(int8_t)(s01 & 0xffu);
+    wu.s[1] = (float)(int8_t)(s01 >> 8);
+    wu.s[2] = (float)(int8_t)(s45 & 0xffu);
+    wu.s[3] = (float)(int8_t)(s45 >> 8);
+    // code = low nibble | (2 high bits << 4): the high bits of plane pp sit
+    // at bits 2pp..2pp+1 of each qh byte, those of plane pp+2 four bits up.
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t h0 = pp ? (qh[i] << 2) : (qh[i] << 4);
+      const uint32_t h1 = pp ? (qh[i] >> 2) : qh[i];
+      wu.c[i] = (ql[i] & 0x0f0f0f0fu) | (h0 & 0x30303030u);
+      wu.c[8 + i] = ((ql[i] >> 4) & 0x0f0f0f0fu) | (h1 & 0x30303030u);
+    }
+  } else {  // Q8_0, quant.rs:2413-2418
+    const uint32_t blk = row + u * 68;
+    wu.s[0] = half_to_f32(ld_s16(blk));
+    wu.s[1] = half_to_f32(ld_s16(blk + 34));
+    uint32_t q0[8], q1[8];
+    ld_s_words<8>(blk + 2, q0);
+    ld_s_words<8>(blk + 36, q1);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      wu.c[i] = q0[i];
+      wu.c[8 + i] = q1[i];
+    }
+  }
+}
+
+template <int FMT>
+__device__ __forceinline__ int dp4(uint32_t code, uint32_t x, int acc) {
+  return FMT == Q8_0 ? dp4a_ss(code, x, acc) : dp4a_us(code, x, acc);
+}
+
+// Integer sum of codes x activations over words [j0, j1) of a unit: exact
+// in 32 bits for one activation byte plane; the three planes of the f32 path
+// are combined in 64 bits.
+template <int FMT, int NP>
+__device__ __forceinline__ long long seg_dot(const WUnit& wu, const XUnit<NP>& xu, int j0, int j1) {
+  if (NP == 1) {
+    int a = 0;
+#pragma unroll
+    for (int j = j0; j < j1; ++j) a = dp4<FMT>(wu.c[j], xu.w[0][j], a);
+    return a;
+  } else {
+    int a0 = 0, a1 = 0, a2 = 0;
+#pragma unroll
+    for (int j = j0; j < j1; ++j) {
+      a0 = dp4<FMT>(wu.c[j], xu.w[0][j], a0);
+      a1 = dp4<FMT>(wu.c[j], xu.w[NP > 1 ? 1 : 0][j], a1);
+      a2 = dp4<FMT>(wu.c[j], xu.w[NP > 2 ? 2 : 0][j], a2);
+    }
+    return (long long)a0 + ((long long)a1 << 8) + ((long long)a2 << 16);
+  }
+}
+
+// int -> float for the NP=1 (32-bit) and NP=3 (64-bit) sums.
+template <int NP>
+__device__ __forceinline__ float to_f(long long v) {
+  return NP == 1 ? (float)(int)v : __ll2float_rn(v);
+}
+
+template <int FMT, int NP>
+__device__ __forceinline__ float combine(const WUnit& wu, const XUnit<NP>& xu, float acc) {
+  if (FMT == Q2_0C) {
+    // sum (2c - 3) x = 2 sum c x - 3 sum x
+    const long long a = 2 * seg_dot<FMT, NP>(wu, xu, 0, 16) - 3ll * xu.xsum[0];
+    return fmaf(to_f<NP>(a), wu.s[0] * xu.sg, acc);
+  } else if (FMT == STQ1_0) {
+    // digit = code - 1
+    const long long a = seg_dot<FMT, NP>(wu, xu, 0, 16) - (long long)xu.xsum[0];
+    return fmaf(to_f<NP>(a), wu.s[0] * xu.sg, acc);
+  } else if (FMT == Q4_K) {
+    // sum (d1 q - m1) x = d1 sum q x - m1 sum x, per 32-column sub-block
+    const float a0 = to_f<NP>(seg_dot<FMT, NP>(wu, xu, 0, 8));
+    const float a1 = to_f<NP>(seg_dot<FMT, NP>(wu, xu, 8, 16));
+    float t = wu.s[0] * a0 - wu.m[0] * (float)xu.xsum[0];
+    t += wu.s[1] * a1 - wu.m[1] * (float)xu.xsum[1];
+    return fmaf(t, xu.sg, acc);
+  } else if (FMT == Q6_K) {
+    // per 16-weight plane: (q - 32) x, scaled by (d * s_x) * sc
+    const float ds = wu.m[0] * xu.sg;
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      const long long a = seg_dot<FMT, NP>(wu, xu, 4 * s, 4 * s + 4) - 32ll * xu.xsum[s];
+      acc = fmaf(to_f<NP>(a), ds * wu.s[s], acc);
+    }
+    return acc;
+  } else {  // Q8_0
+    acc = fmaf(to_f<NP>(seg_dot<FMT, NP>(wu, xu, 0, 8)), wu.s[0] * xu.sg, acc);
+    return fmaf(to_f<NP>(seg_dot<FMT, NP>(wu, xu, 8, 16)), wu.s[1] * xu.sg, acc);
+  }
+}
+
+__device__ __forceinline__ void batch_of(const Params& p, int64_t bt, int R, int& m, int64_t& row0, int& nrows) {
+  m = 0;
+  if (p.n_mat > 1 && bt >= p.mat[1].batch_begin) m = 1;
+  if (p.n_mat > 2 && bt >= p.mat[2].batch_begin) m = 2;
+  row0 = (bt - p.mat[m].batch_begin) * R;
+  const int64_t left = p.mat[m].rows - row0;
+  nrows = (int)(left < R ? left : R);
+}
+
+// Row tiles land in shared memory as the 16-byte aligned window around them:
+// [floor16(src), floor16(src + bytes)) by one bulk copy, and the last
+// (src + bytes) % 16 bytes by plain loads, so row data starts at
+// dst + (src & 15).  stage_tail must run before the arrive that releases the
+// stage; stage_bulk after it.
+__device__ __forceinline__ uint32_t stage_tail(uint8_t* dst, const uint8_t* src, int64_t bytes) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(src);
+  const uintptr_t a0 = a & ~uintptr_t(15);
+  const uintptr_t a1 = a + (uintptr_t)bytes;
+  const uintptr_t b1 = (a1 & ~uintptr_t(15)) > a0 ? (a1 & ~uintptr_t(15)) : a0;
+  const uint8_t* t = reinterpret_cast<const uint8_t*>(b1);
+  uint8_t* d = dst + (b1 - a0);
+  for (uintptr_t k = 0; k < a1 - b1; ++k) d[k] = t[k];
+  return (uint32_t)(b1 - a0);
+}
+
+__device__ __forceinline__ void stage_bulk(uint8_t* dst, const uint8_t* src, uint32_t bulk, uint32_t bar) {
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(src) & ~uintptr_t(15);
+  if (bulk) bulk_g2s(smem_addr(dst), reinterpret_cast<const void*>(a0), bulk, bar);
+}
+
+// Reduce V = 2^k per-lane values over the warp with a transposed butterfly:
+// each level keeps half of the values and exchanges the other half, so V rows
+// cost (V-1) + (5-k) shuffles instead of 5V.  Afterwards lane l holds the
+// total of value index reduce_index<V>(l) in v[0].
+template <int V>
+__device__ __forceinline__ void warp_reduce_multi(float (&v)[V], int lane) {
+  int n = V;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    if (n > 1) {
+      const bool upper = (lane & o) != 0;
+#pragma unroll
+      for (int j = 0; j < V / 2; ++j) {
+        if (j < n / 2) {
+          const float send = upper ? v[j] : v[j + n / 2];
+          const float keep = upper ? v[j + n / 2] : v[j];
+          v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+      }
+      n /= 2;
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+    }
+  }
+}
+
+template <int V>
+__device__ __forceinline__ int reduce_index(int lane) {
+  int idx = 0, n = V;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    if (n > 1) {
+      if (lane & o) idx += n / 2;
+      n /= 2;
+    }
+  }
+  return idx;
+}
+
+// The lowest lane of each group that holds one reduced index.
+template <int V>
+__device__ __forceinline__ bool reduce_writer(int lane) {
+  constexpr int k = V == 1 ? 0 : (V == 2 ? 1 : (V == 4 ? 2 : 3));
+  return (lane & ((32 >> k) - 1)) == 0;
+}
+
+template <int FMT, int NP, int UPL, int RW, bool PAIR>
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ Params p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + kMaxStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 16 * kMaxStages);
+  float* red = reinterpret_cast<float*>(smem + kRedOffset);
+  uint8_t* stages = smem + p.stage_off;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = p.stages;
+  const int R = p.rg * RW;  // rows per tile: RW per row group
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(smem_addr(&full[s]), 1);
+      mbar_init(smem_addr(&empty[s]), kCW);
+    }
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  if (warp == kCW) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0) {
+      int64_t issued = 0;
+      for (int64_t bt = blockIdx.x; bt < p.total_batches; bt += gridDim.x, ++issued) {
+        const int s = (int)(issued % S);
+        if (issued >= S) {
+          const uint32_t par = (uint32_t)(((issued / S) - 1) & 1);
+          if (!mbar_wait(smem_addr(&empty[s]), par, abort_flag)) {
+            atomicOr(p.status, DEV_TIMEOUT_EMPTY);
+            *abort_flag = 1;
+            break;
+          }
+        }
+        fence_proxy_async_smem();
+        int m, nrows;
+        int64_t row0;
+        batch_of(p, bt, R, m, row0, nrows);
+        uint8_t* dst = stages + (size_t)s * p.stage_bytes;
+        const int64_t bytes = (int64_t)nrows * p.row_bytes;
+        const uint8_t* src = p.mat[m].w + row0 * p.row_bytes;
+        const uint32_t bar = smem_addr(&full[s]);
+        const uint8_t* srcu = PAIR ? p.up + row0 * p.row_bytes : nullptr;
+        const uint32_t b0 = stage_tail(dst, src, bytes);
+        const uint32_t b1 = PAIR ? stage_tail(dst + p.half_bytes, srcu, bytes) : 0u;
+        mbar_arrive_expect_tx(bar, b0 + b1);
+        stage_bulk(dst, src, b0, bar);
+        if (PAIR) stage_bulk(dst + p.half_bytes, srcu, b1, bar);
+      }
+      // Do not leave while copies into this CTA's shared memory are in flight.
+      const int64_t last = issued;
+      for (int64_t k = (last > S ? last - S : 0); k < last; ++k) {
+        const int s = (int)(k % S);
+        const uint32_t par = (uint32_t)((k / S) & 1);
+        if (!mbar_wait(smem_addr(&full[s]), par, nullptr)) atomicOr(p.status, DEV_TIMEOUT_DRAIN);
+      }
+    }
+    return;
+  }
+
+  // ------------------------------ consumers -------------------------------
+  prepare_x<FMT, NP>(p, smem);
+  const int ksi = warp % p.ks, rgi = warp / p.ks;
+  XUnit<NP> xu[UPL];
+  int uu[UPL];
+  bool uv[UPL];
+#pragma unroll
+  for (int i = 0; i < UPL; ++i) {
+    const int local = lane + 32 * i;
+    uu[i] = ksi * p.slice + local;
+    uv[i] = local < p.slice && uu[i] < p.U;
+    load_x<FMT, NP>(p, smem, uu[i], uv[i], xu[i]);
+  }
+  const int ridx = reduce_index<RW>(lane);
+  const bool writer = reduce_writer<RW>(lane);
+  const uint32_t stages_s = smem_addr(stages);
+
+  int64_t it = 0;
+  for (int64_t bt = blockIdx.x; bt < p.total_batches; bt += gridDim.x, ++it) {
+    const int s = (int)(it % S);
+    const uint32_t par = (uint32_t)((it / S) & 1);
+    bool ok = mbar_wait(smem_addr(&full[s]), par, abort_flag);
+    // The warps that share a row leave together, or the named barrier below
+    // would wait for a warp that is gone.
+    if (p.ks > 1) ok = bar_red_and(1 + rgi, p.ks * 32, ok);
+    if (!ok) {
+      if (lane == 0) atomicOr(p.status, DEV_TIMEOUT_FULL);
+      *abort_flag = 1;
+      break;
+    }
+    int m, nrows;
+    int64_t row0;
+    batch_of(p, bt, R, m, row0, nrows);
+    const uint32_t tile = stages_s + (uint32_t)s * (uint32_t)p.stage_bytes;
+    const uint32_t base = tile + (uint32_t)(reinterpret_cast<uintptr_t>(p.mat[m].w + row0 * p.row_bytes) & 15);
+    const uint32_t baseu =
+        tile + (uint32_t)p.half_bytes +
+        (PAIR ? (uint32_t)(reinterpret_cast<uintptr_t>(p.up + row0 * p.row_bytes) & 15) : 0u);
+    float g[RW], u[RW];
+#pragma unroll
+    for (int rr = 0; rr < RW; ++rr) g[rr] = u[rr] = 0.f;
+#pragma unroll
+    for (int i = 0; i < UPL; ++i) {
+      if (uv[i]) {
+#pragma unroll
+        for (int rr = 0; rr < RW; ++rr) {
+          const int r = rgi + p.rg * rr;
+          if (r < nrows) {
+            WUnit wu;
+            decode_unit<FMT>(base + (uint32_t)(r * p.row_bytes), uu[i], wu);
+            g[rr] = combine<FMT, NP>(wu, xu[i], g[rr]);
+            if (PAIR) {
+              WUnit wv;
+              decode_unit<FMT>(baseu + (uint32_t)(r * p.row_bytes), uu[i], wv);
+              u[rr] = combine<FMT, NP>(wv, xu[i], u[rr]);
+            }
+          }
+        }
+      }
+    }
+    warp_reduce_multi<RW>(g, lane);
+    if (PAIR) warp_reduce_multi<RW>(u, lane);
+    const int r = rgi + p.rg * ridx;  // the row this lane now holds
+    if (p.ks == 1) {
+      if (writer && r < nrows) {
+        float out = g[0];
+        if (PAIR) out = (g[0] / (1.0f + expf(-g[0]))) * u[0];  // quant.rs:573-574
+        p.mat[m].y[row0 + r] = out;
+      }
+    } else {
+      // Partial sums of the ks warps of each row, double-buffered by tile
+      // parity: a writer two tiles ahead has passed this group's barrier of
+      // the next tile, which the reader reaches only after reading.
+      float* rb = red + (it & 1) * (2 * kCW * 4);
+      if (writer) {
+        rb[((rgi * RW + ridx) * p.ks + ksi) * 2] = g[0];
+        rb[((rgi * RW + ridx) * p.ks + ksi) * 2 + 1] = PAIR ? u[0] : 0.f;
+      }
+      bar_sync_named(1 + rgi, p.ks * 32);
+      if (ksi == 0 && writer && r < nrows) {
+        float gs = 0.f, us = 0.f;
+        for (int k = 0; k < p.ks; ++k) {
+          gs += rb[((rgi * RW + ridx) * p.ks + k) * 2];
+          us += rb[((rgi * RW + ridx) * p.ks + k) * 2 + 1];
+        }
+        float out = gs;
+        if (PAIR) out = (gs / (1.0f + expf(-gs))) * us;
+        p.mat[m].y[row0 + r] = out;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_addr(&empty[s]));
+  }
+}
+
+// Launch geometry chosen by the host (hyq_gemv.cu, make_plan).
+struct Plan {
+  bool streaming = false;
+  int ks = 1, slice = 0, upl = 1, rw = 1, stages = 0, half_bytes = 0, stage_bytes = 0;
+  int x_bytes = 0;
+  int64_t total_batches = 0;
+  int64_t batch_begin[3] = {};
+  size_t smem = 0;
+  int smem_cap = 0;
+  int grid = 0;
+};
+
+template <int FMT, int NP, int UPL, int RW, bool PAIR>
+cudaError_t run_stream(const Params& p, const Plan& pl, cudaStream_t st) {
+  auto k = gemv_kernel<FMT, NP, UPL, RW, PAIR>;
+  // Raise the dynamic shared-memory limit once per device and instantiation.
+  static int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem_cap);
+    if (e != cudaSuccess) return e;
+    configured_dev = dev;
+  }
+  k<<<pl.grid, kThreads, pl.smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+template <int FMT, int NP, int UPL, bool PAIR>
+cudaError_t dispatch_rw(const Params& p, const Plan& pl, cudaStream_t st) {
+  switch (pl.rw) {
+    case 1: return run_stream<FMT, NP, UPL, 1, PAIR>(p, pl, st);
+    case 2: return run_stream<FMT, NP, UPL, 2, PAIR>(p, pl, st);
+    default: return run_stream<FMT, NP, UPL, 4, PAIR>(p, pl, st);
+  }
+}
+
+template <int FMT, int NP, bool PAIR>
+cudaError_t dispatch_upl(const Params& p, const Plan& pl, cudaStream_t st) {
+  if constexpr (NP == 3) {
+    return dispatch_rw<FMT, NP, 1, PAIR>(p, pl, st);
+  } else {
+    switch (pl.upl) {
+      case 1: return dispatch_rw<FMT, NP, 1, PAIR>(p, pl, st);
+      case 2: return dispatch_rw<FMT, NP, 2, PAIR>(p, pl, st);
+      case 3: return dispatch_rw<FMT, NP, 3, PAIR>(p, pl, st);
+      default: return dispatch_rw<FMT, NP, 4, PAIR>(p, pl, st);
+    }
+  }
+}
+
+// Entry of one format's translation unit.
+template <int FMT>
+cudaError_t dispatch_fmt(const Params& p, const Plan& pl, bool pair, cudaStream_t st) {
+  if (p.xmode == XF32)
+    return pair ? dispatch_upl<FMT, 3, true>(p, pl, st) : dispatch_upl<FMT, 3, false>(p, pl, st);
+  return pair ? dispatch_upl<FMT, 1, true>(p, pl, st) : dispatch_upl<FMT, 1, false>(p, pl, st);
+}
+
+}  // namespace gemv
+}  // namespace hyq

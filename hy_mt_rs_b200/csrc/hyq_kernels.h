@@ -27,6 +27,9 @@ struct GemvJob {
   const float* x = nullptr;       // f32 [K]
   const int8_t* xq = nullptr;     // int8 [K] (natural order, as Q8::values)
   const float* xs = nullptr;      // f32 [ceil(K/256)] (Q8::scales)
+  // With x set: quantize it to Q8 inside the kernel (gemv_q8, quant.rs:348)
+  // instead of multiplying the f32 values.
+  bool quantize_q8 = false;
   unsigned* status = nullptr;     // device status word (bounded-wait failures)
 };
 

@@ -220,6 +220,41 @@ class Weight:
         return out
 
     # ------------------------------------------------------ int8 products
+    def gemv_int8(self, input, out=None):
+        """Batch-1 product through Q8 activations quantized in the kernel: the
+        aarch64 path of Weight::matmul (quant.rs:169-178, gemv_q8 :346-351)."""
+        _need_cuda(input, "gemv_int8 input", torch.float32)
+        if input.numel() != self._shape[0]:
+            raise HyqError(-2, f"{self.name}: invalid activation shape")
+        if out is None:
+            out = torch.empty(self._shape[1], dtype=torch.float32, device=input.device)
+        check(lib.hyq_gemv_int8(self._h, _ptr(input), _ptr(out), _stream(input.device)))
+        return out
+
+    @staticmethod
+    def gemv_qkv_int8(q, k, v, input):
+        """Weight::gemv_qkv through int8 activations (quant.rs:673-714)."""
+        _need_cuda(input, "qkv input", torch.float32)
+        if input.numel() != q._shape[0]:
+            raise HyqError(-2, "invalid activation shape for qkv")
+        dev = input.device
+        qo = torch.empty(q._shape[1], dtype=torch.float32, device=dev)
+        ko = torch.empty(k._shape[1], dtype=torch.float32, device=dev)
+        vo = torch.empty(v._shape[1], dtype=torch.float32, device=dev)
+        check(lib.hyq_gemv_qkv_int8(q._h, k._h, v._h, _ptr(input), _ptr(qo), _ptr(ko), _ptr(vo), _stream(dev)))
+        return qo, ko, vo
+
+    def matmul_gate_up_silu_int8(self, up, input):
+        """Weight::matmul_gate_up_silu through int8 activations (quant.rs:735-766)."""
+        if up._shape != self._shape:
+            raise HyqError(-2, "gate and up shape mismatch")
+        _need_cuda(input, "gate_up_silu input", torch.float32)
+        if input.numel() != self._shape[0]:
+            raise HyqError(-2, "invalid activation shape for gate_up_silu")
+        out = torch.empty(self._shape[1], dtype=torch.float32, device=input.device)
+        check(lib.hyq_matmul_gate_up_silu_int8(self._h, up._h, _ptr(input), _ptr(out), _stream(input.device)))
+        return out
+
     def gemv_q8_fast(self, q8, out=None):
         """gemv_q8_fast (quant.rs:353-357)."""
         if out is None:

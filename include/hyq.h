@@ -135,6 +135,21 @@ int hyq_gemv_qkv_q8(const hyq_weight* q, const hyq_weight* k, const hyq_weight* 
 int hyq_matmul_gate_up_silu_q8(const hyq_weight* gate, const hyq_weight* up, const int8_t* values,
                                const float* scales, const int8_t* values_q2c, float* out, void* stream);
 
+/* Batch-1 product through int8 activations, quantized inside the kernel
+ * exactly as Q8::quantize would (the aarch64 path of Weight::matmul:
+ * quant.rs:169-178 -> gemv_q8 :346-351).  Same result as hyq_q8_quantize
+ * followed by hyq_gemv_q8, in one launch and without the Q8 buffers.
+ * K must be a multiple of 256 unless the buffers are 16-byte aligned. */
+int hyq_gemv_int8(const hyq_weight* w, const float* input, float* out, void* stream);
+
+/* Weight::gemv_qkv through int8 activations (quant.rs:673-714). */
+int hyq_gemv_qkv_int8(const hyq_weight* q, const hyq_weight* k, const hyq_weight* v, const float* input,
+                      float* q_out, float* k_out, float* v_out, void* stream);
+
+/* Weight::matmul_gate_up_silu through int8 activations (quant.rs:735-766). */
+int hyq_matmul_gate_up_silu_int8(const hyq_weight* gate, const hyq_weight* up, const float* input, float* out,
+                                 void* stream);
+
 /* Synchronize `stream`, then return (and clear) the device status word of
  * the current device: 0, or HYQ_DEV_* bits from kernels whose bounded waits
  * expired. */

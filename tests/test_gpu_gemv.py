@@ -197,3 +197,47 @@ def test_full_size_lm_head_properties(cuda):
     mag8 = np.abs(wd) @ np.abs(vals.astype(np.float64) * scales[np.arange(K) // 256])
     check_close(y8[rows], ref8.astype(np.float64), mag8, what="lm_head q8 rows")
     assert quant.device_status() == 0
+
+
+@pytest.mark.parametrize("t", PACKED)
+@pytest.mark.parametrize("N,K", [(16, 2048), (40, 6144), (9, 14336), (100, 4096), (7, 256)])
+def test_int8_in_kernel_matches_two_step(cuda, t, N, K):
+    """hyq_gemv_int8 (Q8 inside the kernel) == hyq_q8_quantize + hyq_gemv_q8,
+    bit for bit, including a NaN group and an all-zero group."""
+    import torch
+    from hy_mt_rs_b200 import quant
+
+    packed, w = make(t, N, K, 3 * N + K, cuda)
+    x = (np.random.default_rng(K + N).standard_normal(K) * 2).astype(np.float32)
+    if K >= 1024:
+        x[256:512] = 0.0
+        x[700] = np.nan
+    xd = to_dev(x, cuda)
+    y1 = w.gemv_int8(xd)
+    y2 = w.gemv_q8_fast(quant.Q8.quantize(xd))
+    assert torch.equal(torch.nan_to_num(y1, nan=123.0), torch.nan_to_num(y2, nan=123.0))
+    vals, scales, q2c = O.q8_quantize(x)
+    ref = O.gemv_q8(t, packed, K, N, vals, scales, q2c)
+    wd = O.decode(t, packed, N * K).reshape(N, K).astype(np.float64)
+    mag = np.abs(wd) @ np.abs(vals.astype(np.float64) * scales[np.arange(K) // 256])
+    check_close(y1.cpu().numpy(), ref.astype(np.float64), mag, what=f"int8 {NAMES[t]} {N}x{K}")
+
+
+@pytest.mark.parametrize("t", [Q2_0C, STQ1_0, Q6_K])
+def test_fused_int8_entry_points(cuda, t):
+    """gemv_qkv / matmul_gate_up_silu through in-kernel Q8 == their two-step forms."""
+    import torch
+    from hy_mt_rs_b200 import quant
+
+    K = 2048
+    _, q = make(t, 2048, K, 21, cuda)
+    _, k = make(t, 512, K, 22, cuda)
+    _, v = make(t, 512, K, 23, cuda)
+    _, g = make(t, 6144, K, 24, cuda)
+    _, u = make(t, 6144, K, 25, cuda)
+    xd = to_dev(np.random.default_rng(9).standard_normal(K).astype(np.float32), cuda)
+    q8 = quant.Q8.quantize(xd)
+    for a, b in zip(quant.Weight.gemv_qkv_int8(q, k, v, xd), quant.Weight.gemv_qkv_fast(q, k, v, q8)):
+        assert torch.equal(a, b)
+    assert torch.equal(g.matmul_gate_up_silu_int8(u, xd), g.matmul_gate_up_silu_fast(u, q8))
+    assert quant.device_status() == 0
