@@ -69,6 +69,10 @@ int status_ptr(unsigned** out) {
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Batches from this size up go to the tensor-core GEMM when the format and
+// shape allow it; smaller batches run batch-1 products.
+constexpr int64_t kGemmMinBatch = 16;
+
 int check_matrix(const hyq_weight* w, const char* name) {
   if (!w) return fail(HYQ_E_INVALID, "%s: null weight", name);
   if (w->ndim != 2) return fail(HYQ_E_SHAPE, "%s is not a matrix", name);
@@ -279,6 +283,19 @@ int hyq_matmul(const hyq_weight* w, const float* input, int64_t batch, float* ou
   a.x = input;
   if ((rc = check_act(a, "matmul"))) return rc;
   const int64_t K = w->dims[0], N = w->dims[1];
+  if (batch >= kGemmMinBatch && hyq::gemm_supported(w->dtype, K, N, batch, w->data) && aligned(input, 16)) {
+    unsigned* status = nullptr;
+    if ((rc = status_ptr(&status))) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    void* ws = nullptr;
+    cudaError_t e = cudaMallocAsync(&ws, hyq::gemm_workspace_bytes(K, batch), st);
+    if (e != cudaSuccess) return fail(HYQ_E_NOMEM, "matmul workspace: %s", cudaGetErrorString(e));
+    e = hyq::launch_gemm(w->dtype, w->data, K, N, input, batch, out, ws, status, st);
+    cudaError_t e2 = cudaFreeAsync(ws, st);
+    if (e != cudaSuccess) return cuda_fail(e, "matmul (tensor-core GEMM)");
+    if (e2 != cudaSuccess) return cuda_fail(e2, "matmul workspace free");
+    return HYQ_OK;
+  }
   for (int64_t b = 0; b < batch; ++b) {
     Act ab;
     ab.x = input + b * K;

@@ -39,4 +39,12 @@ cudaError_t launch_gemv(const GemvJob& job, cudaStream_t st);
 // 0 = streaming bulk-copy kernel, 1 = per-element fallback.
 int gemv_engine(const GemvJob& job);
 
+// Batched products (Weight::matmul, batch >= 2) on tcgen05 tensor cores.
+// The activations are first rounded to fp16 into `workspace`
+// (gemm_workspace_bytes(K, M) bytes, 16-byte aligned).
+bool gemm_supported(int dtype, int64_t K, int64_t N, int64_t M, const void* w);
+size_t gemm_workspace_bytes(int64_t K, int64_t M);
+cudaError_t launch_gemm(int dtype, const uint8_t* w, int64_t K, int64_t N, const float* x, int64_t M, float* y,
+                        void* workspace, unsigned* status, cudaStream_t st);
+
 }  // namespace hyq
