@@ -50,6 +50,9 @@ def args_parse():
     ap.add_argument("--path", choices=["f32", "q8"], default="f32")
     ap.add_argument("--copies", type=int, default=4)
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
+                    help="decode: config 2 (default line); prefill: config 3 (7B layer GEMMs)")
+    ap.add_argument("--tokens", type=int, default=512, help="prefill: tokens M")
     return ap.parse_args()
 
 
@@ -466,10 +469,90 @@ def gpu_arm(a):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# Prefill (config 3): one 7B decoder layer's projections at M tokens
+# ---------------------------------------------------------------------------
+LAYER_7B = [("attn_q", 4096, 4096, 2), ("attn_k", 1024, 4096, 2), ("attn_v", 1024, 4096, 2),
+            ("attn_output", 4096, 4096, 2), ("ffn_gate", 14336, 4096, 2), ("ffn_up", 14336, 4096, 2),
+            ("ffn_down", 4096, 14336, 3)]  # (name, N, K, dtype): Q4_K_M-style, Q6_K down
+
+
+def prefill_arm(a):
+    import torch
+
+    import hy_mt_rs_b200  # noqa: F401
+    from hy_mt_rs_b200 import quant, synth
+
+    dev = torch.device("cuda", 0)
+    M = a.tokens
+    ws = []
+    for i, (name, N, K, t) in enumerate(LAYER_7B):
+        ws.append(quant.Weight(synth.random_packed(t, N, K, seed=50 + i, device=dev), t, [K, N], name=name))
+    xs = {K: torch.randn(M, K, generator=torch.Generator().manual_seed(K)).to(dev) for K in (4096, 14336)}
+    flops = sum(2 * M * N * K for _, N, K, _ in LAYER_7B)
+    wbytes = sum(N * row_bytes(t, K) for _, N, K, t in LAYER_7B)
+    stream = torch.cuda.Stream(dev)
+    outs = {}
+
+    def step():
+        for w, (_, N, K, _) in zip(ws, LAYER_7B):
+            outs[w.name] = w.matmul(xs[K], M)
+
+    with torch.cuda.stream(stream):
+        for _ in range(a.warmup):
+            step()
+        stream.synchronize()
+        per = {w.name: [] for w in ws}
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(a.steps):
+            for w, (_, N, K, _) in zip(ws, LAYER_7B):
+                b = torch.cuda.Event(enable_timing=True)
+                c = torch.cuda.Event(enable_timing=True)
+                b.record(stream)
+                w.matmul(xs[K], M)
+                c.record(stream)
+                per[w.name].append((b, c))
+        e1.record(stream)
+    stream.synchronize()
+    assert quant.device_status(dev) == 0
+    ms = e0.elapsed_time(e1) / a.steps
+    per_ms = {k: statistics.fmean(b.elapsed_time(c) for b, c in v) for k, v in per.items()}
+    gate = per_ms["ffn_gate"]
+    gate_flops = 2 * M * 14336 * 4096
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:
+        pass
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    line = {
+        "metric": "prefill GEMM TFLOP/s (7B layer projections, Q4_K + Q6_K down, fp16 tensor cores)",
+        "value": round(flops / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": 1, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp16 operands (decoded weights, activations), f32 accumulate",
+        "data": "synthetic", "config": {"workload": f"hy-mt-rs config 3: 7B layer projections, M={M}",
+                                        "tokens": M, "flops_per_step": flops, "weight_bytes": wbytes},
+        "roofline": {"bound": "tensor", "kernel": "ffn_gate Q4_K 14336x4096 GEMM",
+                     "achieved": round(gate_flops / (gate * 1e-3) / 1e12, 2), "peak": peak,
+                     "peak_kind": "measured" if peaks else "fallback", "unit": "TFLOP/s",
+                     "frac": round(gate_flops / (gate * 1e-3) / 1e12 / peak, 4), "traffic": None,
+                     "avg_launch_ms": round(gate, 5)},
+        "per_projection_ms": {k: round(v, 5) for k, v in per_ms.items()},
+        "prefill_tok_s_layer": round(M / (ms * 1e-3), 1),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     a = args_parse()
     if a.impl == "reference":
         return reference_arm(a)
+    if a.workload == "prefill":
+        return prefill_arm(a)
     return gpu_arm(a)
 
 
