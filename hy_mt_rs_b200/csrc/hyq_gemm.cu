@@ -5,8 +5,11 @@
 // src/quant.rs:272-343): Y[batch, N] = X[batch, K] . W^T, where the reference
 // decodes 64-row tiles to f32 and multiplies them with Candle's CPU GEMM.
 //
-// Tile: 128 weight rows (the MMA's M) x 128 tokens (the MMA's N) x K, with
-// D = W_tile . X_tile^T accumulated in f32 in tensor memory.  Roles:
+// Tile: 128 weight rows (the MMA's M) x BN tokens (the MMA's N, 128 or 256)
+// x K, with D = W_tile . X_tile^T accumulated in f32 in tensor memory.
+// Within every 64-column K step the activations are stored in the order the
+// dequantizer produces weight pairs (see k_perm), so both operands agree on
+// the K order without shuffles.  Roles:
 //   warp 0  : TMA producer -- packed weight block columns (2-D tensor map over
 //             the raw GGUF bytes: 128 rows x one block column, taken as the
 //             16-byte aligned window around it) and fp16 activation tiles
@@ -18,8 +21,11 @@
 //             the reference's operation order, then rounded to fp16), then
 //             fence the writes into the async proxy; warps 2-5 also run the
 //             epilogue (tcgen05.ld -> coalesced f32 stores of Y).
-// Operands are fp16 (both), accumulation f32: relative error ~4e-4 of the
-// f32 reference, inside the 1e-3 relative-L2 bound.
+// Operands are fp16 (both), accumulation f32.  Weights are decoded with fp16
+// arithmetic from exact integer codes: 1024 + q is built in the fp16 bit
+// pattern, 1024 (and the Q6_K offset 32) is subtracted exactly, and one fused
+// multiply-add with the fp16 sub-block scale and min rounds the result.  The
+// product stays inside the 1e-3 relative-L2 bound.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
@@ -33,14 +39,15 @@ namespace hyq {
 namespace gemm {
 
 constexpr int BM = 128;          // weight rows per tile (MMA M)
-constexpr int BN = 128;          // tokens per tile (MMA N)
 constexpr int BK = 64;           // K per stage: one 128-byte swizzle row of fp16
-constexpr int S = 4;             // activation / decoded-weight stages
 constexpr int WS = 2;            // packed weight block-column stages
 constexpr int kDequantWarps = 8;
 constexpr int kThreads = (2 + kDequantWarps) * 32;
 constexpr int kDequantThreads = kDequantWarps * 32;
-constexpr int kTileBytes = 128 * 128;  // one 128-row x 64-fp16 tile
+constexpr int kTileBytes = 128 * 128;  // one 128-row x 64-fp16 tile (A); B tiles are BN rows
+
+// Activation / decoded-weight stages for a BN-token tile.
+__host__ __device__ constexpr int stages_for(int bn) { return bn == 256 ? 3 : 4; }
 
 struct Params {
   int K, N, M;
@@ -52,10 +59,13 @@ struct Params {
   unsigned* status;
 };
 
+template <int BN>
 struct Smem {
+  static constexpr int S = stages_for(BN);
+  static constexpr int x_tile = BN * 128;
   // offsets from the 1024-aligned base
   static constexpr int x = 0;
-  static constexpr int a = x + S * kTileBytes;
+  static constexpr int a = x + S * x_tile;
   static constexpr int w = a + S * kTileBytes;
   static constexpr int w_stage = 128 * 256;  // max box bytes per row (256) x 128 rows
   static constexpr int bars = w + WS * w_stage;
@@ -142,81 +152,132 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Decode 32 consecutive weights of one row (K offset `kc` inside the
-// block-column tile, a multiple of 32) into 16 fp16x2 words, using the
-// reference's f32 operation order (quant.rs:2437-2483) before rounding.
+// K order inside one 64-column step.  Slot pair P = 16h + 4t + j (h: which
+// thread of the row, t: 32-bit word, j: pair inside the word) holds columns
+// c + T[j][0], c + T[j][1] with c = 16h + 4t; T is the order in which pairs of
+// codes fall out of a 32-bit word with (w >> 4k) & 0x000F000F.
+__host__ __device__ constexpr int k_perm(int fmt, int slot) {
+  const int P = slot >> 1, e = slot & 1;
+  const int h = P >> 4, t = (P >> 2) & 3, j = P & 3;
+  const int c = 16 * h + 4 * t;
+  // Q4_K: low nibbles (cols c..), high nibbles (cols c+32..)
+  // Q6_K: plane p0 (cols c..), plane p0+1 (cols c+32..)
+  const int q4[4][2] = {{0, 2}, {32, 34}, {1, 3}, {33, 35}};
+  const int q6[4][2] = {{0, 2}, {1, 3}, {32, 34}, {33, 35}};
+  return c + (fmt == Q4_K ? q4[j][e] : q6[j][e]);
+}
+
+__device__ __forceinline__ uint32_t hsub2_u(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t hmul2_u(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t h2_splat(float f) {
+  __half h = __float2half_rn(f);
+  const uint32_t u = *reinterpret_cast<unsigned short*>(&h);
+  return u | (u << 16);
+}
+
+// Decode this thread's 32 weights of one row for K step `j4` of the block
+// column (the row's bytes start at `row`): 16 fp16x2 words in k_perm order.
 template <int FMT>
-__device__ __forceinline__ void decode32(uint32_t row, int kc, uint32_t (&o)[16]) {
+__device__ __forceinline__ void decode32(uint32_t row, int j4, int h, uint32_t (&o)[16]) {
+  constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024 in both halves
   if (FMT == Q4_K) {
-    const int g = kc >> 6, hh = (kc >> 5) & 1;  // group of 64, low/high nibbles
-    const uint4 h = ld_s128(row);
-    const float d = half_to_f32(h.x & 0xffffu), dmin = half_to_f32(h.x >> 16);
-    const int j = 2 * g + hh;
-    uint32_t s, m;
-    if (j < 4) {
-      s = (h.y >> (8 * j)) & 63u;
-      m = (h.z >> (8 * j)) & 63u;
-    } else {
-      const int k = j - 4;
-      const uint32_t hi = (h.w >> (8 * k)) & 0xffu;
-      s = (hi & 15u) | ((((h.y >> (8 * k)) & 0xffu) >> 6) << 4);
-      m = (hi >> 4) | ((((h.z >> (8 * k)) & 0xffu) >> 6) << 4);
+    const int g = j4;  // 64-column group of the 256-column block
+    const uint4 hd = ld_s128(row);
+    const float d = half_to_f32(hd.x & 0xffffu), dmin = half_to_f32(hd.x >> 16);
+    uint32_t sm[2], mm[2];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int j = 2 * g + hh;
+      uint32_t sc, mn;
+      if (j < 4) {
+        sc = (hd.y >> (8 * j)) & 63u;
+        mn = (hd.z >> (8 * j)) & 63u;
+      } else {
+        const int k = j - 4;
+        const uint32_t hi = (hd.w >> (8 * k)) & 0xffu;
+        sc = (hi & 15u) | ((((hd.y >> (8 * k)) & 0xffu) >> 6) << 4);
+        mn = (hi >> 4) | ((((hd.z >> (8 * k)) & 0xffu) >> 6) << 4);
+      }
+      sm[hh] = h2_splat(d * (float)sc);
+      mm[hh] = h2_splat(-(dmin * (float)mn));
     }
-    const float d1 = d * (float)s, m1 = dmin * (float)m;
-    const uint4 q0 = ld_s128(row + 16 + 32 * g), q1 = ld_s128(row + 32 + 32 * g);
-    const uint32_t q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    // this thread's 16 quant bytes: both nibbles -> columns c.. and c+32..
+    const uint4 q = ld_s128(row + 16 + 32 * g + 16 * h);
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t nib = hh ? (q[i] >> 4) & 0x0f0f0f0fu : q[i] & 0x0f0f0f0fu;
-      float v[4];
+    for (int t = 0; t < 4; ++t) {
 #pragma unroll
-      for (int b = 0; b < 4; ++b) v[b] = __fsub_rn(__fmul_rn(d1, (float)((nib >> (8 * b)) & 0xffu)), m1);
-      o[2 * i] = pack_h2(v[0], v[1]);
-      o[2 * i + 1] = pack_h2(v[2], v[3]);
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t v = ((w[t] >> (4 * j)) & 0x000f000fu) | kMagic;  // 1024 + q, exact
+        const int hi = j & 1;                                          // high nibble: sub-block 2g+1
+        o[4 * t + j] = hfma2_u(hsub2_u(v, kMagic), sm[hi], mm[hi]);
+      }
     }
   } else {  // Q6_K
-    const int chunk = kc >> 7, p = (kc >> 5) & 3;
-    uint32_t ql[8], qh[8];
-    ld_s_words<8>(row + chunk * 64 + (p & 1) * 32, ql);
-    ld_s_words<8>(row + 128 + chunk * 32, qh);
-    const uint32_t sc = ld_s16(row + 192 + chunk * 8 + 2 * p);
+    const int chunk = j4 >> 1, p0 = 2 * (j4 & 1);
+    const int nsh = (p0 >> 1) * 4;
+    uint32_t A[4], B[4], H[4];
+    ld_s_words<4>(row + chunk * 64 + 16 * h, A);       // plane p0 low/high nibbles
+    ld_s_words<4>(row + chunk * 64 + 32 + 16 * h, B);  // plane p0+1
+    ld_s_words<4>(row + 128 + chunk * 32 + 16 * h, H);
     const float d = half_to_f32(ld_s16(row + 208));
-    const float s0 = __fmul_rn(d, (float)(int8_t)(sc & 0xffu));
-    const float s1 = __fmul_rn(d, (float)(int8_t)(sc >> 8));
-    const int nsh = (p >> 1) * 4, hsh = 2 * p;
+    const uint32_t sc0 = ld_s16(row + 192 + chunk * 8 + 2 * p0) >> (8 * h);
+    const uint32_t sc1 = ld_s16(row + 192 + chunk * 8 + 2 * p0 + 2) >> (8 * h);
+    const uint32_t s0 = h2_splat(d * (float)(int8_t)(sc0 & 0xffu));
+    const uint32_t s1 = h2_splat(d * (float)(int8_t)(sc1 & 0xffu));
+    const uint32_t k1056 = 0x64206420u;  // fp16 1056 = 1024 + 32
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float s = i < 4 ? s0 : s1;  // columns 0..15 use half 0, 16..31 half 1
-      float v[4];
+    for (int t = 0; t < 4; ++t) {
 #pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const int q = (int)(((ql[i] >> (8 * b + nsh)) & 15u) | (((qh[i] >> (8 * b + hsh)) & 3u) << 4));
-        v[b] = __fmul_rn(s, (float)(q - 32));
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t src = j < 2 ? A[t] : B[t];
+        const int bsh = 8 * (j & 1);                 // bytes (0,2) or (1,3)
+        const int hsh = 2 * (p0 + (j >> 1));         // qh bits of this plane
+        const uint32_t lo = ((src >> (nsh + bsh)) & 0x000f000fu) | kMagic;
+        const uint32_t hb = (H[t] >> (hsh + bsh)) & 0x00030003u;
+        const uint32_t v = lo | (hb << 4);         // 1024 + q6, exact
+        o[4 * t + j] = hmul2_u(hsub2_u(v, k1056), j < 2 ? s0 : s1);
       }
-      o[2 * i] = pack_h2(v[0], v[1]);
-      o[2 * i + 1] = pack_h2(v[2], v[3]);
     }
   }
 }
 
-template <int FMT>
+template <int FMT, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                 const __grid_constant__ Params p) {
+  using L = Smem<BN>;
+  constexpr int S = L::S;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled tiles
   const uint32_t raw_s = smem_addr(smem_raw);
   const uint32_t base = (raw_s + 1023u) & ~1023u;
   uint8_t* base_g = smem_raw + (base - raw_s);
-  const uint32_t bars = base + Smem::bars;
+  const uint32_t bars = base + L::bars;
   auto xfull = [&](int s) { return bars + 8 * s; };
   auto afull = [&](int s) { return bars + 8 * (S + s); };
   auto empty = [&](int s) { return bars + 8 * (2 * S + s); };
   auto wfull = [&](int s) { return bars + 8 * (3 * S + s); };
   auto wempty = [&](int s) { return bars + 8 * (3 * S + WS + s); };
   const uint32_t accfull = bars + 8 * (3 * S + 2 * WS);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base_g + Smem::misc);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(base_g + Smem::misc + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base_g + L::misc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(base_g + L::misc + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = blockIdx.x * BM, tok0 = blockIdx.y * BN;
@@ -262,7 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const int x0 = (wb * p.wbytes) & ~15;
           mbar_arrive_expect_tx(wfull(ws), (uint32_t)(BM * p.wbox));
-          tma_load_2d(base + Smem::w + ws * Smem::w_stage, &tmap_w, x0, row0, wfull(ws));
+          tma_load_2d(base + L::w + ws * L::w_stage, &tmap_w, x0, row0, wfull(ws));
           ++issued_w;
         }
         const int s = ks % S;
@@ -270,8 +331,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(xfull(s), (uint32_t)kTileBytes);
-        tma_load_2d(base + Smem::x + s * kTileBytes, &tmap_x, ks * BK, tok0, xfull(s));
+        mbar_arrive_expect_tx(xfull(s), (uint32_t)L::x_tile);
+        tma_load_2d(base + L::x + s * L::x_tile, &tmap_x, ks * BK, tok0, xfull(s));
         ++issued_x;
       }
       if (!ok) {
@@ -299,8 +360,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       if (lane == 0) {
-        const uint32_t a0 = base + Smem::a + s * kTileBytes;
-        const uint32_t b0 = base + Smem::x + s * kTileBytes;
+        const uint32_t a0 = base + L::a + s * kTileBytes;
+        const uint32_t b0 = base + L::x + s * L::x_tile;
 #pragma unroll
         for (int k = 0; k < BK / 16; ++k)
           umma_f16(tmem, sw128_desc(a0 + 32 * k), sw128_desc(b0 + 32 * k), idesc, (ks > 0 || k > 0) ? 1u : 0u);
@@ -328,11 +389,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       const int skew = (wb * p.wbytes) & 15;
-      const uint32_t rowp = base + Smem::w + ws * Smem::w_stage + r * p.wbox + skew;
-      const int kc = (ks % steps_per_w) * BK + 32 * h;
+      const uint32_t rowp = base + L::w + ws * L::w_stage + r * p.wbox + skew;
       uint32_t o[16];
-      decode32<FMT>(rowp, kc, o);
-      const uint32_t dst = base + Smem::a + s * kTileBytes + r * 128;
+      decode32<FMT>(rowp, ks % steps_per_w, h, o);
+      const uint32_t dst = base + L::a + s * kTileBytes + r * 128;
 #pragma unroll
       for (int c = 0; c < 4; ++c)
         st_s128(dst + ((((uint32_t)(4 * h + c)) ^ swz) << 4), make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]));
@@ -379,18 +439,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// fp16 copy of the activations for the TMA-fed operand.
-__global__ void __launch_bounds__(256) to_half_kernel(const float* __restrict__ x, __half* __restrict__ h,
-                                                       int64_t n) {
-  const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
-  if (i + 3 < n) {
-    const float4 v = *reinterpret_cast<const float4*>(x + i);
-    __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
-    *reinterpret_cast<__half2*>(h + i) = a;
-    *reinterpret_cast<__half2*>(h + i + 2) = b;
-  } else {
-    for (int64_t k = i; k < n; ++k) h[k] = __float2half_rn(x[k]);
-  }
+// fp16 copy of the activations for the TMA-fed operand, with every 64-column
+// step stored in k_perm order.  One thread per 2 output slots.
+template <int FMT>
+__global__ void __launch_bounds__(256) to_half_kernel(const float* __restrict__ x, __half2* __restrict__ h,
+                                                       int64_t K, int64_t total_pairs) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total_pairs) return;
+  const int64_t e = 2 * i;  // element index of the first slot
+  const int64_t tok = e / K;
+  const int64_t kk = e - tok * K;
+  const int64_t step0 = kk & ~int64_t(63);
+  const int slot = (int)(kk & 63);
+  const float* row = x + tok * K + step0;
+  h[i] = __floats2half2_rn(row[k_perm(FMT, slot)], row[k_perm(FMT, slot + 1)]);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -420,13 +482,13 @@ bool geometry(int dtype, int64_t K, int64_t row_bytes, Geometry& g) {
   return K % g.wcol == 0;
 }
 
-template <int FMT>
+template <int FMT, int BN>
 cudaError_t run(const CUtensorMap& tw, const CUtensorMap& tx, const Params& p, cudaStream_t st) {
-  auto k = gemm_kernel<FMT>;
+  auto k = gemm_kernel<FMT, BN>;
   static int configured_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
-  const int smem = Smem::total + 1024;
+  const int smem = Smem<BN>::total + 1024;
   if (configured_dev != dev) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
@@ -460,12 +522,16 @@ cudaError_t launch_gemm(int dtype, const uint8_t* w, int64_t K, int64_t N, const
   if (!enc) return cudaErrorNotSupported;
   __half* xh = static_cast<__half*>(workspace);
   {
-    const int64_t n = K * M;
-    const int64_t threads = (n + 3) / 4;
-    to_half_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(x, xh, n);
+    const int64_t pairs = K * M / 2;
+    const unsigned blocks = (unsigned)((pairs + 255) / 256);
+    if (dtype == Q4_K)
+      to_half_kernel<Q4_K><<<blocks, 256, 0, st>>>(x, reinterpret_cast<__half2*>(xh), K, pairs);
+    else
+      to_half_kernel<Q6_K><<<blocks, 256, 0, st>>>(x, reinterpret_cast<__half2*>(xh), K, pairs);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
+  const int bn = M >= 256 ? 256 : 128;
   CUtensorMap tw, tx;
   {
     const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)N};
@@ -480,7 +546,7 @@ cudaError_t launch_gemm(int dtype, const uint8_t* w, int64_t K, int64_t N, const
   {
     const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
     const cuuint64_t strides[1] = {(cuuint64_t)(K * 2)};
-    const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)BN};
+    const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)bn};
     const cuuint32_t es[2] = {1, 1};
     if (enc(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xh, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
@@ -498,8 +564,8 @@ cudaError_t launch_gemm(int dtype, const uint8_t* w, int64_t K, int64_t N, const
   p.y = y;
   p.status = status;
   switch (dtype) {
-    case Q4_K: return run<Q4_K>(tw, tx, p, st);
-    case Q6_K: return run<Q6_K>(tw, tx, p, st);
+    case Q4_K: return bn == 256 ? run<Q4_K, 256>(tw, tx, p, st) : run<Q4_K, 128>(tw, tx, p, st);
+    case Q6_K: return bn == 256 ? run<Q6_K, 256>(tw, tx, p, st) : run<Q6_K, 128>(tw, tx, p, st);
     default: return cudaErrorNotSupported;
   }
 }
