@@ -160,11 +160,10 @@ __host__ __device__ constexpr int k_perm(int fmt, int slot) {
   const int P = slot >> 1, e = slot & 1;
   const int h = P >> 4, t = (P >> 2) & 3, j = P & 3;
   const int c = 16 * h + 4 * t;
-  // Q4_K: low nibbles (cols c..), high nibbles (cols c+32..)
-  // Q6_K: plane p0 (cols c..), plane p0+1 (cols c+32..)
-  const int q4[4][2] = {{0, 2}, {32, 34}, {1, 3}, {33, 35}};
-  const int q6[4][2] = {{0, 2}, {1, 3}, {32, 34}, {33, 35}};
-  return c + (fmt == Q4_K ? q4[j][e] : q6[j][e]);
+  // Q4_K, j = 0..3: (0,2) (32,34) (1,3) (33,35)  [low / high nibbles]
+  // Q6_K, j = 0..3: (0,2) (1,3) (32,34) (33,35)  [plane p0 / plane p0+1]
+  const int off = fmt == Q4_K ? (j & 1) * 32 + (j >> 1) : (j >> 1) * 32 + (j & 1);
+  return c + off + 2 * e;
 }
 
 __device__ __forceinline__ uint32_t hsub2_u(uint32_t a, uint32_t b) {
