@@ -69,6 +69,20 @@ int status_ptr(unsigned** out) {
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Keep stream-ordered workspace memory cached in the device's default pool
+// between calls instead of returning it to the driver at every sync.
+void ensure_pool() {
+  static bool done[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices || done[dev]) return;
+  cudaMemPool_t pool;
+  if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+    uint64_t keep = UINT64_MAX;
+    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+  }
+  done[dev] = true;
+}
+
 // Batches from this size up go to the tensor-core GEMM when the format and
 // shape allow it; smaller batches run batch-1 products.
 constexpr int64_t kGemmMinBatch = 16;
@@ -288,7 +302,8 @@ int hyq_matmul(const hyq_weight* w, const float* input, int64_t batch, float* ou
     if ((rc = status_ptr(&status))) return rc;
     cudaStream_t st = (cudaStream_t)stream;
     void* ws = nullptr;
-    cudaError_t e = cudaMallocAsync(&ws, hyq::gemm_workspace_bytes(K, batch), st);
+    ensure_pool();
+    cudaError_t e = cudaMallocAsync(&ws, hyq::gemm_workspace_bytes(w->dtype, K, N, batch), st);
     if (e != cudaSuccess) return fail(HYQ_E_NOMEM, "matmul workspace: %s", cudaGetErrorString(e));
     e = hyq::launch_gemm(w->dtype, w->data, K, N, input, batch, out, ws, status, st);
     cudaError_t e2 = cudaFreeAsync(ws, st);

@@ -41,7 +41,7 @@ namespace gemm {
 constexpr int BM = 128;          // weight rows per tile (MMA M)
 constexpr int BK = 64;           // K per stage: one 128-byte swizzle row of fp16
 constexpr int WS = 2;            // packed weight block-column stages
-constexpr int kDequantWarps = 8;
+constexpr int kDequantWarps = 16;  // 4 threads per weight row, 16 weights each
 constexpr int kThreads = (2 + kDequantWarps) * 32;
 constexpr int kDequantThreads = kDequantWarps * 32;
 constexpr int kTileBytes = 128 * 128;  // one 128-row x 64-fp16 tile (A); B tiles are BN rows
@@ -51,11 +51,12 @@ __host__ __device__ constexpr int stages_for(int bn) { return bn == 256 ? 3 : 4;
 
 struct Params {
   int K, N, M;
+  int steps_per_split;  // K steps of one split-K slice (a whole number of block columns)
   int row_bytes;
   int wcol;             // K columns per packed block-column tile
   int wbox;             // bytes per row of that tile (TMA box inner size)
   int wbytes;           // packed bytes of one row per block column
-  float* y;             // [M, N]
+  float* y;             // [M, N], or split-K partials [splits, M, N]
   unsigned* status;
 };
 
@@ -190,10 +191,17 @@ __device__ __forceinline__ uint32_t h2_splat(float f) {
   return u | (u << 16);
 }
 
-// Decode this thread's 32 weights of one row for K step `j4` of the block
-// column (the row's bytes start at `row`): 16 fp16x2 words in k_perm order.
+__device__ __forceinline__ uint2 ld_s64(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+
+// Decode 8 weights per code word t = t0 .. t0+1 of half `h` of one row for K
+// step `j4` of the block column (the row's bytes start at `row`): 8 fp16x2
+// words in k_perm order (pairs 16h + 4t + j).
 template <int FMT>
-__device__ __forceinline__ void decode32(uint32_t row, int j4, int h, uint32_t (&o)[16]) {
+__device__ __forceinline__ void decode16(uint32_t row, int j4, int h, int t0, uint32_t (&o)[8]) {
   constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024 in both halves
   if (FMT == Q4_K) {
     const int g = j4;  // 64-column group of the 256-column block
@@ -216,11 +224,11 @@ __device__ __forceinline__ void decode32(uint32_t row, int j4, int h, uint32_t (
       sm[hh] = h2_splat(d * (float)sc);
       mm[hh] = h2_splat(-(dmin * (float)mn));
     }
-    // this thread's 16 quant bytes: both nibbles -> columns c.. and c+32..
-    const uint4 q = ld_s128(row + 16 + 32 * g + 16 * h);
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    // this thread's 8 quant bytes: both nibbles -> columns c.. and c+32..
+    const uint2 q = ld_s64(row + 16 + 32 * g + 16 * h + 4 * t0);
+    const uint32_t w[2] = {q.x, q.y};
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
+    for (int t = 0; t < 2; ++t) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const uint32_t v = ((w[t] >> (4 * j)) & 0x000f000fu) | kMagic;  // 1024 + q, exact
@@ -231,10 +239,10 @@ __device__ __forceinline__ void decode32(uint32_t row, int j4, int h, uint32_t (
   } else {  // Q6_K
     const int chunk = j4 >> 1, p0 = 2 * (j4 & 1);
     const int nsh = (p0 >> 1) * 4;
-    uint32_t A[4], B[4], H[4];
-    ld_s_words<4>(row + chunk * 64 + 16 * h, A);       // plane p0 low/high nibbles
-    ld_s_words<4>(row + chunk * 64 + 32 + 16 * h, B);  // plane p0+1
-    ld_s_words<4>(row + 128 + chunk * 32 + 16 * h, H);
+    uint32_t A[2], B[2], H[2];
+    ld_s_words<2>(row + chunk * 64 + 16 * h + 4 * t0, A);       // plane p0 low/high nibbles
+    ld_s_words<2>(row + chunk * 64 + 32 + 16 * h + 4 * t0, B);  // plane p0+1
+    ld_s_words<2>(row + 128 + chunk * 32 + 16 * h + 4 * t0, H);
     const float d = half_to_f32(ld_s16(row + 208));
     const uint32_t sc0 = ld_s16(row + 192 + chunk * 8 + 2 * p0) >> (8 * h);
     const uint32_t sc1 = ld_s16(row + 192 + chunk * 8 + 2 * p0 + 2) >> (8 * h);
@@ -242,7 +250,7 @@ __device__ __forceinline__ void decode32(uint32_t row, int j4, int h, uint32_t (
     const uint32_t s1 = h2_splat(d * (float)(int8_t)(sc1 & 0xffu));
     const uint32_t k1056 = 0x64206420u;  // fp16 1056 = 1024 + 32
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
+    for (int t = 0; t < 2; ++t) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const uint32_t src = j < 2 ? A[t] : B[t];
@@ -280,18 +288,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = blockIdx.x * BM, tok0 = blockIdx.y * BN;
-  const int nk = p.K / BK;
   const int steps_per_w = p.wcol / BK;
+  // split-K slice of this CTA: K steps [kbeg, kbeg + nk)
+  const int kbeg = blockIdx.z * p.steps_per_split;
+  const int nk_all = p.K / BK;
+  const int nk = min(p.steps_per_split, nk_all - kbeg);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(xfull(s), 1);
-      mbar_init(afull(s), kDequantThreads);
+      mbar_init(afull(s), kDequantWarps);
       mbar_init(empty(s), 1);
     }
     for (int s = 0; s < WS; ++s) {
       mbar_init(wfull(s), 1);
-      mbar_init(wempty(s), kDequantThreads);
+      mbar_init(wempty(s), kDequantWarps);
     }
     mbar_init(accfull, 1);
     *abort_flag = 0;
@@ -320,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          const int x0 = (wb * p.wbytes) & ~15;
+          const int x0 = (((kbeg + ks) / steps_per_w) * p.wbytes) & ~15;
           mbar_arrive_expect_tx(wfull(ws), (uint32_t)(BM * p.wbox));
           tma_load_2d(base + L::w + ws * L::w_stage, &tmap_w, x0, row0, wfull(ws));
           ++issued_w;
@@ -331,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         mbar_arrive_expect_tx(xfull(s), (uint32_t)L::x_tile);
-        tma_load_2d(base + L::x + s * L::x_tile, &tmap_x, ks * BK, tok0, xfull(s));
+        tma_load_2d(base + L::x + s * L::x_tile, &tmap_x, (kbeg + ks) * BK, tok0, xfull(s));
         ++issued_x;
       }
       if (!ok) {
@@ -374,7 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // --------------------------- dequant + epilogue ---------------------------
     const int dt = threadIdx.x - 64;
-    const int r = dt >> 1, h = dt & 1;
+    const int r = dt >> 2, h = (dt >> 1) & 1, t0 = 2 * (dt & 1);
     const uint32_t swz = (uint32_t)(r & 7);
     for (int ks = 0; ks < nk; ++ks) {
       const int wb = ks / steps_per_w, ws = wb % WS;
@@ -387,17 +398,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_flag = 1;
         break;
       }
-      const int skew = (wb * p.wbytes) & 15;
+      const int skew = (((kbeg + ks) / steps_per_w) * p.wbytes) & 15;
       const uint32_t rowp = base + L::w + ws * L::w_stage + r * p.wbox + skew;
-      uint32_t o[16];
-      decode32<FMT>(rowp, ks % steps_per_w, h, o);
+      uint32_t o[8];
+      decode16<FMT>(rowp, (kbeg + ks) % steps_per_w, h, t0, o);
       const uint32_t dst = base + L::a + s * kTileBytes + r * 128;
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-        st_s128(dst + ((((uint32_t)(4 * h + c)) ^ swz) << 4), make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]));
+      for (int c = 0; c < 2; ++c)
+        st_s128(dst + ((((uint32_t)(4 * h + t0 + c)) ^ swz) << 4),
+                make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]));
+      // Every writer makes its stores visible to the tensor core (async
+      // proxy); the warp then signals the stage once.
       fence_proxy_async_smem();
-      mbar_arrive(afull(s));
-      if (ks % steps_per_w == steps_per_w - 1) mbar_arrive(wempty(ws));
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(afull(s));
+        if (ks % steps_per_w == steps_per_w - 1 || ks == nk - 1) mbar_arrive(wempty(ws));
+      }
     }
     // Epilogue: warps 2..5 own TMEM lanes 32*(warp%4) .. +31.
     if (warp < 6) {
@@ -418,10 +435,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               : "r"(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0));
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
           if (row < p.N) {
+            float* yz = p.y + (size_t)blockIdx.z * p.M * p.N;
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const int tok = tok0 + c0 + i;
-              if (tok < p.M) p.y[(size_t)tok * p.N + row] = __uint_as_float(v[i]);
+              if (tok < p.M) yz[(size_t)tok * p.N + row] = __uint_as_float(v[i]);
             }
           }
         }
@@ -493,9 +511,42 @@ cudaError_t run(const CUtensorMap& tw, const CUtensorMap& tx, const Params& p, c
     if (e != cudaSuccess) return e;
     configured_dev = dev;
   }
-  dim3 grid((unsigned)((p.N + BM - 1) / BM), (unsigned)((p.M + BN - 1) / BN));
+  const int splits = (p.K / BK + p.steps_per_split - 1) / p.steps_per_split;
+  dim3 grid((unsigned)((p.N + BM - 1) / BM), (unsigned)((p.M + BN - 1) / BN), (unsigned)splits);
   k<<<grid, kThreads, smem, st>>>(tw, tx, p);
   return cudaGetLastError();
+}
+
+// y = sum over split-K slices of the partials, in slice order.
+__global__ void __launch_bounds__(256) reduce_splits_kernel(const float* __restrict__ part, float* __restrict__ y,
+                                                             int64_t n, int splits) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float s = part[i];
+  for (int z = 1; z < splits; ++z) s += part[(int64_t)z * n + i];
+  y[i] = s;
+}
+
+int device_sms() {
+  static int sms[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  return sms[dev] > 0 ? sms[dev] : 148;
+}
+
+// Split-K slices (in block columns) so that small grids still fill the GPU.
+int choose_splits(int64_t K, int64_t N, int64_t M, int wcol) {
+  const int64_t bn = M >= 256 ? 256 : 128;
+  const int64_t tiles = ((N + BM - 1) / BM) * ((M + bn - 1) / bn);
+  const int64_t nwb = K / wcol;
+  const int64_t sms = device_sms();
+  if (tiles >= sms) return 1;
+  int64_t z = (sms + tiles - 1) / tiles;
+  if (z > nwb) z = nwb;
+  if (z > 16) z = 16;
+  return (int)(z < 1 ? 1 : z);
 }
 
 }  // namespace gemm
@@ -509,7 +560,14 @@ bool gemm_supported(int dtype, int64_t K, int64_t N, int64_t M, const void* w) {
   return gemm::encode_fn() != nullptr;
 }
 
-size_t gemm_workspace_bytes(int64_t K, int64_t M) { return (size_t)(K * M) * sizeof(__half) + 16; }
+size_t gemm_workspace_bytes(int dtype, int64_t K, int64_t N, int64_t M) {
+  gemm::Geometry g;
+  const int64_t row_bytes = K / block_len(dtype) * block_bytes(dtype);
+  if (!gemm::geometry(dtype, K, row_bytes, g)) return 0;
+  const int z = gemm::choose_splits(K, N, M, g.wcol);
+  const size_t xb = ((size_t)(K * M) * sizeof(__half) + 255) / 256 * 256;
+  return xb + (z > 1 ? (size_t)z * M * N * sizeof(float) : 0) + 16;
+}
 
 cudaError_t launch_gemm(int dtype, const uint8_t* w, int64_t K, int64_t N, const float* x, int64_t M, float* y,
                         void* workspace, unsigned* status, cudaStream_t st) {
@@ -552,21 +610,34 @@ cudaError_t launch_gemm(int dtype, const uint8_t* w, int64_t K, int64_t N, const
         CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
+  const int splits = choose_splits(K, N, M, g.wcol);
+  const int nwb = (int)(K / g.wcol);
+  const int wb_per_split = (nwb + splits - 1) / splits;
+  float* partials = nullptr;
+  if (splits > 1)
+    partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
+                                        ((size_t)(K * M) * sizeof(__half) + 255) / 256 * 256);
   Params p;
   p.K = (int)K;
   p.N = (int)N;
   p.M = (int)M;
+  p.steps_per_split = wb_per_split * (g.wcol / BK);
   p.row_bytes = (int)row_bytes;
   p.wcol = g.wcol;
   p.wbox = g.wbox;
   p.wbytes = g.wbytes;
-  p.y = y;
+  p.y = splits > 1 ? partials : y;
   p.status = status;
+  cudaError_t e;
   switch (dtype) {
-    case Q4_K: return bn == 256 ? run<Q4_K, 256>(tw, tx, p, st) : run<Q4_K, 128>(tw, tx, p, st);
-    case Q6_K: return bn == 256 ? run<Q6_K, 256>(tw, tx, p, st) : run<Q6_K, 128>(tw, tx, p, st);
+    case Q4_K: e = bn == 256 ? run<Q4_K, 256>(tw, tx, p, st) : run<Q4_K, 128>(tw, tx, p, st); break;
+    case Q6_K: e = bn == 256 ? run<Q6_K, 256>(tw, tx, p, st) : run<Q6_K, 128>(tw, tx, p, st); break;
     default: return cudaErrorNotSupported;
   }
+  if (e != cudaSuccess || splits == 1) return e;
+  const int64_t n = M * N;
+  reduce_splits_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(partials, y, n, splits);
+  return cudaGetLastError();
 }
 
 }  // namespace hyq

@@ -41,9 +41,10 @@ int gemv_engine(const GemvJob& job);
 
 // Batched products (Weight::matmul, batch >= 2) on tcgen05 tensor cores.
 // The activations are first rounded to fp16 into `workspace`
-// (gemm_workspace_bytes(K, M) bytes, 16-byte aligned).
+// (gemm_workspace_bytes bytes, 256-byte aligned), which also holds split-K
+// partial sums when the grid is small.
 bool gemm_supported(int dtype, int64_t K, int64_t N, int64_t M, const void* w);
-size_t gemm_workspace_bytes(int64_t K, int64_t M);
+size_t gemm_workspace_bytes(int dtype, int64_t K, int64_t N, int64_t M);
 cudaError_t launch_gemm(int dtype, const uint8_t* w, int64_t K, int64_t N, const float* x, int64_t M, float* y,
                         void* workspace, unsigned* status, cudaStream_t st);
 
