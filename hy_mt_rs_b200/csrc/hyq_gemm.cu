@@ -610,9 +610,10 @@ cudaError_t launch_gemm(int dtype, const uint8_t* w, int64_t K, int64_t N, const
         CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
-  const int splits = choose_splits(K, N, M, g.wcol);
   const int nwb = (int)(K / g.wcol);
-  const int wb_per_split = (nwb + splits - 1) / splits;
+  const int wb_per_split = (nwb + choose_splits(K, N, M, g.wcol) - 1) / choose_splits(K, N, M, g.wcol);
+  // slices actually launched (rounding to whole block columns can drop some)
+  const int splits = (nwb + wb_per_split - 1) / wb_per_split;
   float* partials = nullptr;
   if (splits > 1)
     partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
