@@ -41,7 +41,7 @@ namespace gemm {
 constexpr int BM = 128;          // weight rows per tile (MMA M)
 constexpr int BK = 64;           // K per stage: one 128-byte swizzle row of fp16
 constexpr int WS = 2;            // packed weight block-column stages
-constexpr int kDequantWarps = 16;  // 4 threads per weight row, 16 weights each
+constexpr int kDequantWarps = 8;   // 2 threads per weight row, 32 weights each
 constexpr int kThreads = (2 + kDequantWarps) * 32;
 constexpr int kDequantThreads = kDequantWarps * 32;
 constexpr int kTileBytes = 128 * 128;  // one 128-row x 64-fp16 tile (A); B tiles are BN rows
@@ -197,11 +197,11 @@ __device__ __forceinline__ uint2 ld_s64(uint32_t a) {
   return v;
 }
 
-// Decode 8 weights per code word t = t0 .. t0+1 of half `h` of one row for K
-// step `j4` of the block column (the row's bytes start at `row`): 8 fp16x2
-// words in k_perm order (pairs 16h + 4t + j).
+// Decode 8 weights per code word t = 0..3 of half `h` of one row for K step
+// `j4` of the block column (the row's bytes start at `row`): 16 fp16x2 words
+// in k_perm order (pairs 16h + 4t + j).
 template <int FMT>
-__device__ __forceinline__ void decode16(uint32_t row, int j4, int h, int t0, uint32_t (&o)[8]) {
+__device__ __forceinline__ void decode32(uint32_t row, int j4, int h, uint32_t (&o)[16]) {
   constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024 in both halves
   if (FMT == Q4_K) {
     const int g = j4;  // 64-column group of the 256-column block
@@ -224,11 +224,11 @@ __device__ __forceinline__ void decode16(uint32_t row, int j4, int h, int t0, ui
       sm[hh] = h2_splat(d * (float)sc);
       mm[hh] = h2_splat(-(dmin * (float)mn));
     }
-    // this thread's 8 quant bytes: both nibbles -> columns c.. and c+32..
-    const uint2 q = ld_s64(row + 16 + 32 * g + 16 * h + 4 * t0);
-    const uint32_t w[2] = {q.x, q.y};
+    // this thread's 16 quant bytes: both nibbles -> columns c.. and c+32..
+    const uint4 q = ld_s128(row + 16 + 32 * g + 16 * h);
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-    for (int t = 0; t < 2; ++t) {
+    for (int t = 0; t < 4; ++t) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const uint32_t v = ((w[t] >> (4 * j)) & 0x000f000fu) | kMagic;  // 1024 + q, exact
@@ -239,10 +239,10 @@ __device__ __forceinline__ void decode16(uint32_t row, int j4, int h, int t0, ui
   } else {  // Q6_K
     const int chunk = j4 >> 1, p0 = 2 * (j4 & 1);
     const int nsh = (p0 >> 1) * 4;
-    uint32_t A[2], B[2], H[2];
-    ld_s_words<2>(row + chunk * 64 + 16 * h + 4 * t0, A);       // plane p0 low/high nibbles
-    ld_s_words<2>(row + chunk * 64 + 32 + 16 * h + 4 * t0, B);  // plane p0+1
-    ld_s_words<2>(row + 128 + chunk * 32 + 16 * h + 4 * t0, H);
+    uint32_t A[4], B[4], H[4];
+    ld_s_words<4>(row + chunk * 64 + 16 * h, A);       // plane p0 low/high nibbles
+    ld_s_words<4>(row + chunk * 64 + 32 + 16 * h, B);  // plane p0+1
+    ld_s_words<4>(row + 128 + chunk * 32 + 16 * h, H);
     const float d = half_to_f32(ld_s16(row + 208));
     const uint32_t sc0 = ld_s16(row + 192 + chunk * 8 + 2 * p0) >> (8 * h);
     const uint32_t sc1 = ld_s16(row + 192 + chunk * 8 + 2 * p0 + 2) >> (8 * h);
@@ -250,7 +250,7 @@ __device__ __forceinline__ void decode16(uint32_t row, int j4, int h, int t0, ui
     const uint32_t s1 = h2_splat(d * (float)(int8_t)(sc1 & 0xffu));
     const uint32_t k1056 = 0x64206420u;  // fp16 1056 = 1024 + 32
 #pragma unroll
-    for (int t = 0; t < 2; ++t) {
+    for (int t = 0; t < 4; ++t) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const uint32_t src = j < 2 ? A[t] : B[t];
@@ -385,7 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // --------------------------- dequant + epilogue ---------------------------
     const int dt = threadIdx.x - 64;
-    const int r = dt >> 2, h = (dt >> 1) & 1, t0 = 2 * (dt & 1);
+    const int r = dt >> 1, h = dt & 1;
     const uint32_t swz = (uint32_t)(r & 7);
     for (int ks = 0; ks < nk; ++ks) {
       const int wb = ks / steps_per_w, ws = wb % WS;
@@ -400,12 +400,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int skew = (((kbeg + ks) / steps_per_w) * p.wbytes) & 15;
       const uint32_t rowp = base + L::w + ws * L::w_stage + r * p.wbox + skew;
-      uint32_t o[8];
-      decode16<FMT>(rowp, (kbeg + ks) % steps_per_w, h, t0, o);
+      uint32_t o[16];
+      decode32<FMT>(rowp, (kbeg + ks) % steps_per_w, h, o);
       const uint32_t dst = base + L::a + s * kTileBytes + r * 128;
 #pragma unroll
-      for (int c = 0; c < 2; ++c)
-        st_s128(dst + ((((uint32_t)(4 * h + t0 + c)) ^ swz) << 4),
+      for (int c = 0; c < 4; ++c)
+        st_s128(dst + ((((uint32_t)(4 * h + c)) ^ swz) << 4),
                 make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]));
       // Every writer makes its stores visible to the tensor core (async
       // proxy); the warp then signals the stage once.

@@ -1,4 +1,4 @@
-"""Run one batch-1 product shape a few times, for profiler captures.
+"""Run one product shape a few times, for profiler captures.
 
     python -m hy_mt_rs_b200.profile_gemv --dtype Q6_K --rows 120832 --cols 2048 \
         --path f32 --iters 3
@@ -20,14 +20,17 @@ def main():
     ap.add_argument("--cols", type=int, default=2048)
     ap.add_argument("--path", choices=["f32", "q8"], default="f32")
     ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--batch", type=int, default=1, help="> 1: batched product (tensor-core GEMM)")
     a = ap.parse_args()
     dev = torch.device("cuda", 0)
     t = quant.DType[a.dtype]
     w = quant.Weight(synth.random_packed(t, a.rows, a.cols, seed=1, device=dev), t, [a.cols, a.rows])
-    x = torch.randn(a.cols, generator=torch.Generator().manual_seed(0)).to(dev)
+    x = torch.randn(a.batch * a.cols, generator=torch.Generator().manual_seed(0)).to(dev)
     q8 = quant.Q8(a.cols, dev)
     for _ in range(a.iters):
-        if a.path == "f32":
+        if a.batch > 1:
+            w.matmul(x, a.batch)
+        elif a.path == "f32":
             w.matmul(x, 1)
         else:
             q8.quantize_into(x)
