@@ -41,7 +41,8 @@ namespace gemm {
 constexpr int BM = 128;          // weight rows per tile (MMA M)
 constexpr int BK = 64;           // K per stage: one 128-byte swizzle row of fp16
 constexpr int WS = 2;            // packed weight block-column stages
-constexpr int kDequantWarps = 8;   // 2 threads per weight row, 32 weights each
+constexpr int kDequantWarps = 8;   // two groups of 4 warps; each group takes every other K step
+constexpr int kGroupWarps = 4;     // one thread per weight row, 64 weights per step
 constexpr int kThreads = (2 + kDequantWarps) * 32;
 constexpr int kDequantThreads = kDequantWarps * 32;
 constexpr int kTileBytes = 128 * 128;  // one 128-row x 64-fp16 tile (A); B tiles are BN rows
@@ -197,11 +198,11 @@ __device__ __forceinline__ uint2 ld_s64(uint32_t a) {
   return v;
 }
 
-// Decode 8 weights per code word t = 0..3 of half `h` of one row for K step
-// `j4` of the block column (the row's bytes start at `row`): 16 fp16x2 words
-// in k_perm order (pairs 16h + 4t + j).
+// Decode one row's 64 weights of K step `j4` of the block column (the row's
+// bytes start at `row`) into 32 fp16x2 words in k_perm order: word 4c + j is
+// pair P = 4c + j, i.e. 16-byte chunk c of the 128-byte tile row.
 template <int FMT>
-__device__ __forceinline__ void decode32(uint32_t row, int j4, int h, uint32_t (&o)[16]) {
+__device__ __forceinline__ void decode64(uint32_t row, int j4, uint32_t (&o)[32]) {
   constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024 in both halves
   if (FMT == Q4_K) {
     const int g = j4;  // 64-column group of the 256-column block
@@ -224,42 +225,47 @@ __device__ __forceinline__ void decode32(uint32_t row, int j4, int h, uint32_t (
       sm[hh] = h2_splat(d * (float)sc);
       mm[hh] = h2_splat(-(dmin * (float)mn));
     }
-    // this thread's 16 quant bytes: both nibbles -> columns c.. and c+32..
-    const uint4 q = ld_s128(row + 16 + 32 * g + 16 * h);
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    // 32 quant bytes: low nibbles -> columns 0..31, high nibbles -> 32..63
+    const uint4 q0 = ld_s128(row + 16 + 32 * g), q1 = ld_s128(row + 32 + 32 * g);
+    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
+    for (int c = 0; c < 8; ++c) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const uint32_t v = ((w[t] >> (4 * j)) & 0x000f000fu) | kMagic;  // 1024 + q, exact
+        const uint32_t v = ((w[c] >> (4 * j)) & 0x000f000fu) | kMagic;  // 1024 + q, exact
         const int hi = j & 1;                                          // high nibble: sub-block 2g+1
-        o[4 * t + j] = hfma2_u(hsub2_u(v, kMagic), sm[hi], mm[hi]);
+        o[4 * c + j] = hfma2_u(hsub2_u(v, kMagic), sm[hi], mm[hi]);
       }
     }
   } else {  // Q6_K
     const int chunk = j4 >> 1, p0 = 2 * (j4 & 1);
     const int nsh = (p0 >> 1) * 4;
-    uint32_t A[4], B[4], H[4];
-    ld_s_words<4>(row + chunk * 64 + 16 * h, A);       // plane p0 low/high nibbles
-    ld_s_words<4>(row + chunk * 64 + 32 + 16 * h, B);  // plane p0+1
-    ld_s_words<4>(row + 128 + chunk * 32 + 16 * h, H);
+    uint32_t A[8], B[8], H[8];
+    ld_s_words<8>(row + chunk * 64, A);       // plane p0 (low or high nibbles)
+    ld_s_words<8>(row + chunk * 64 + 32, B);  // plane p0+1
+    ld_s_words<8>(row + 128 + chunk * 32, H);
     const float d = half_to_f32(ld_s16(row + 208));
-    const uint32_t sc0 = ld_s16(row + 192 + chunk * 8 + 2 * p0) >> (8 * h);
-    const uint32_t sc1 = ld_s16(row + 192 + chunk * 8 + 2 * p0 + 2) >> (8 * h);
-    const uint32_t s0 = h2_splat(d * (float)(int8_t)(sc0 & 0xffu));
-    const uint32_t s1 = h2_splat(d * (float)(int8_t)(sc1 & 0xffu));
+    const uint32_t sc0 = ld_s16(row + 192 + chunk * 8 + 2 * p0);      // plane p0, halves 0/1
+    const uint32_t sc1 = ld_s16(row + 192 + chunk * 8 + 2 * p0 + 2);  // plane p0+1
+    uint32_t sv[2][2];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      sv[0][hh] = h2_splat(d * (float)(int8_t)((sc0 >> (8 * hh)) & 0xffu));
+      sv[1][hh] = h2_splat(d * (float)(int8_t)((sc1 >> (8 * hh)) & 0xffu));
+    }
     const uint32_t k1056 = 0x64206420u;  // fp16 1056 = 1024 + 32
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
+    for (int c = 0; c < 8; ++c) {
+      const int hh = c >> 2;  // columns 0..15 use half 0, 16..31 half 1
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const uint32_t src = j < 2 ? A[t] : B[t];
-        const int bsh = 8 * (j & 1);                 // bytes (0,2) or (1,3)
-        const int hsh = 2 * (p0 + (j >> 1));         // qh bits of this plane
+        const uint32_t src = j < 2 ? A[c] : B[c];
+        const int bsh = 8 * (j & 1);          // bytes (0,2) or (1,3)
+        const int hsh = 2 * (p0 + (j >> 1));  // qh bits of this plane
         const uint32_t lo = ((src >> (nsh + bsh)) & 0x000f000fu) | kMagic;
-        const uint32_t hb = (H[t] >> (hsh + bsh)) & 0x00030003u;
-        const uint32_t v = lo | (hb << 4);         // 1024 + q6, exact
-        o[4 * t + j] = hmul2_u(hsub2_u(v, k1056), j < 2 ? s0 : s1);
+        const uint32_t hb = (H[c] >> (hsh + bsh)) & 0x00030003u;
+        const uint32_t v = lo | (hb << 4);  // 1024 + q6, exact
+        o[4 * c + j] = hmul2_u(hsub2_u(v, k1056), sv[j >> 1][hh]);
       }
     }
   }
@@ -297,7 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(xfull(s), 1);
-      mbar_init(afull(s), kDequantWarps);
+      mbar_init(afull(s), kGroupWarps);
       mbar_init(empty(s), 1);
     }
     for (int s = 0; s < WS; ++s) {
@@ -384,13 +390,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // --------------------------- dequant + epilogue ---------------------------
-    const int dt = threadIdx.x - 64;
-    const int r = dt >> 1, h = dt & 1;
+    const int grp = (warp - 2) / kGroupWarps;           // 0: even K steps, 1: odd
+    const int r = ((warp - 2) % kGroupWarps) * 32 + lane;  // weight row of the tile
     const uint32_t swz = (uint32_t)(r & 7);
-    for (int ks = 0; ks < nk; ++ks) {
+    for (int ks = grp; ks < nk; ks += 2) {
       const int wb = ks / steps_per_w, ws = wb % WS;
       bool ok = true;
-      if (ks % steps_per_w == 0) ok = mbar_wait(wfull(ws), (wb / WS) & 1, abort_flag);
+      // first step of this block column that this group handles
+      if (ks % steps_per_w == grp) ok = mbar_wait(wfull(ws), (wb / WS) & 1, abort_flag);
       const int s = ks % S;
       if (ok && ks >= S) ok = mbar_wait(empty(s), ((ks / S) - 1) & 1, abort_flag);
       if (!ok) {
@@ -400,20 +407,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int skew = (((kbeg + ks) / steps_per_w) * p.wbytes) & 15;
       const uint32_t rowp = base + L::w + ws * L::w_stage + r * p.wbox + skew;
-      uint32_t o[16];
-      decode32<FMT>(rowp, (kbeg + ks) % steps_per_w, h, o);
       const uint32_t dst = base + L::a + s * kTileBytes + r * 128;
+      uint32_t o[32];
+      decode64<FMT>(rowp, (kbeg + ks) % steps_per_w, o);
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-        st_s128(dst + ((((uint32_t)(4 * h + c)) ^ swz) << 4),
-                make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]));
+      for (int c = 0; c < 8; ++c)
+        st_s128(dst + ((((uint32_t)c) ^ swz) << 4), make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]));
       // Every writer makes its stores visible to the tensor core (async
       // proxy); the warp then signals the stage once.
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(afull(s));
-        if (ks % steps_per_w == steps_per_w - 1 || ks == nk - 1) mbar_arrive(wempty(ws));
+        // last step of this block column that this group handles
+        if (ks % steps_per_w >= steps_per_w - 2 || ks + 2 >= nk) mbar_arrive(wempty(ws));
       }
     }
     // Epilogue: warps 2..5 own TMEM lanes 32*(warp%4) .. +31.
