@@ -66,6 +66,7 @@ _SIGS = {
     "hyq_gemv_int8": ([_wp, _vp, _vp, _vp], C.c_int),
     "hyq_gemv_qkv_int8": ([_wp, _wp, _wp, _vp, _vp, _vp, _vp, _vp], C.c_int),
     "hyq_matmul_gate_up_silu_int8": ([_wp, _wp, _vp, _vp, _vp], C.c_int),
+    "hyq_matmul_noalloc": ([_wp, _vp, _i64, _vp, _vp], C.c_int),
     "hyq_device_status": ([_vp, C.POINTER(C.c_uint32)], C.c_int),
 }
 

@@ -191,6 +191,24 @@ int check_act(const Act& a, const char* name) {
 
 }  // namespace
 
+namespace hyq {
+
+// Error and status plumbing shared with C-ABI entry points defined in other
+// translation units.
+int api_fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  t_err = buf;
+  return code;
+}
+
+int api_status_word(unsigned** out) { return status_ptr(out); }
+
+}  // namespace hyq
+
 extern "C" {
 
 const char* hyq_last_error(void) { return t_err.c_str(); }

@@ -48,4 +48,9 @@ size_t gemm_workspace_bytes(int dtype, int64_t K, int64_t N, int64_t M);
 cudaError_t launch_gemm(int dtype, const uint8_t* w, int64_t K, int64_t N, const float* x, int64_t M, float* y,
                         void* workspace, unsigned* status, cudaStream_t st);
 
+// C-ABI plumbing (hyq_api.cu): set the calling thread's hyq_last_error text
+// and return `code`; the current device's status word.
+int api_fail(int code, const char* fmt, ...);
+int api_status_word(unsigned** out);
+
 }  // namespace hyq

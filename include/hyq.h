@@ -150,6 +150,30 @@ int hyq_gemv_qkv_int8(const hyq_weight* q, const hyq_weight* k, const hyq_weight
 int hyq_matmul_gate_up_silu_int8(const hyq_weight* gate, const hyq_weight* up, const float* input, float* out,
                                  void* stream);
 
+/* Bytes of the fixed device scratch behind hyq_matmul_noalloc (64 MiB). */
+#define HYQ_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)
+
+/* hyq_matmul with no device allocation: same arguments, checks and result
+ * (the same kernels run), but the tensor-core path keeps its fp16 activation
+ * copy and split-K partial sums in a device array of
+ * HYQ_NOALLOC_SCRATCH_BYTES that belongs to the library's module image (every
+ * GPU that loads the library holds it until the process exits), instead of a
+ * stream-ordered allocation.  No counterpart in the reference, whose matmul
+ * works in host memory.  It serves callers that may not allocate device
+ * memory per call: a server that hands all free HBM to its own cache at
+ * start-up (where a per-call allocation could fail mid request), and hosts
+ * that own the device's default memory pool (hyq_matmul raises that pool's
+ * release threshold to keep its workspace cached).
+ * Limits:
+ *   - a batch whose scratch would exceed HYQ_NOALLOC_SCRATCH_BYTES
+ *     (K * batch * 2 bytes plus split-K partials) fails with HYQ_E_SHAPE;
+ *   - the first call on each device looks up the array's device address with
+ *     that device current; make that first call before any stream capture;
+ *   - every call on a device shares the one array, so calls that overlap on
+ *     the GPU (different streams, no ordering between them) race: keep them
+ *     on one stream or order them with events. */
+int hyq_matmul_noalloc(const hyq_weight* w, const float* input, int64_t batch, float* out, void* stream);
+
 /* Synchronize `stream`, then return (and clear) the device status word of
  * the current device: 0, or HYQ_DEV_* bits from kernels whose bounded waits
  * expired. */
