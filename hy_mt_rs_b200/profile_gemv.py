@@ -4,7 +4,8 @@
         --path f32 --iters 3
 
 Every iteration is one launch of the product kernel (plus one Q8 launch
-with --path q8).  Weights are seeded synthetic (hy_mt_rs_b200.synth).
+with --path q8; --path int8 quantizes inside the product kernel, as the
+bench's q8 decode chain does).  Weights are seeded synthetic (hy_mt_rs_b200.synth).
 """
 import argparse
 
@@ -18,7 +19,7 @@ def main():
     ap.add_argument("--dtype", default="Q6_K", choices=[d.name for d in quant.DType])
     ap.add_argument("--rows", type=int, default=120832)
     ap.add_argument("--cols", type=int, default=2048)
-    ap.add_argument("--path", choices=["f32", "q8"], default="f32")
+    ap.add_argument("--path", choices=["f32", "q8", "int8"], default="f32")
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--batch", type=int, default=1, help="> 1: batched product (tensor-core GEMM)")
     a = ap.parse_args()
@@ -32,6 +33,8 @@ def main():
             w.matmul(x, a.batch)
         elif a.path == "f32":
             w.matmul(x, 1)
+        elif a.path == "int8":
+            w.gemv_int8(x)
         else:
             q8.quantize_into(x)
             w.gemv_q8_fast(q8)
