@@ -7,6 +7,11 @@
 //
 // Tile: 128 weight rows (the MMA's M) x BN tokens (the MMA's N, 128 or 256)
 // x K, with D = W_tile . X_tile^T accumulated in f32 in tensor memory.
+// The decoded weights (operand A) never touch shared memory: each dequant
+// thread owns one weight row = one TMEM lane and stores its fp16 pairs with
+// tcgen05.st, and the MMA reads A from tensor memory.  Shared memory carries
+// only the activation tiles (TMA in, MMA out) and the packed weight bytes,
+// which keeps it below its bandwidth at full tensor-core rate.
 // Within every 64-column K step the activations are stored in the order the
 // dequantizer produces weight pairs (see k_perm), so both operands agree on
 // the K order without shuffles.  Roles:
@@ -16,11 +21,13 @@
 //             (SWIZZLE_128B);
 //   warp 1  : allocates TMEM and issues tcgen05.mma (one elected thread),
 //             releasing each stage with tcgen05.commit;
-//   warps 2-9: dequantize the packed block column into the fp16 K-major
-//             SWIZZLE_128B tile the MMA reads (weights decoded in f32 with
-//             the reference's operation order, then rounded to fp16), then
-//             fence the writes into the async proxy; warps 2-5 also run the
-//             epilogue (tcgen05.ld -> coalesced f32 stores of Y).
+//   warps 2-9: two groups of 4 warps taking alternate K steps; warp w serves
+//             TMEM lanes 32*(w%4).. (its rows), decodes the packed block
+//             column into the fp16 A stage in tensor memory, waits for the
+//             stores and signals the stage; warps 2-5 also run the epilogue
+//             (tcgen05.ld -> f32 stores of Y).
+// Tensor memory (512 columns): accumulator in columns [0, BN), A stage s in
+// columns [BN + 32 s, BN + 32 s + 32) (128 lanes x 64 fp16).
 // Operands are fp16 (both), accumulation f32.  Weights are decoded with fp16
 // arithmetic from exact integer codes: 1024 + q is built in the fp16 bit
 // pattern, 1024 (and the Q6_K offset 32) is subtracted exactly, and one fused
@@ -44,11 +51,14 @@ constexpr int WS = 2;            // packed weight block-column stages
 constexpr int kDequantWarps = 8;   // two groups of 4 warps; each group takes every other K step
 constexpr int kGroupWarps = 4;     // one thread per weight row, 64 weights per step
 constexpr int kThreads = (2 + kDequantWarps) * 32;
-constexpr int kDequantThreads = kDequantWarps * 32;
-constexpr int kTileBytes = 128 * 128;  // one 128-row x 64-fp16 tile (A); B tiles are BN rows
+constexpr int kTmemCols = 512;
 
-// Activation / decoded-weight stages for a BN-token tile.
-__host__ __device__ constexpr int stages_for(int bn) { return bn == 256 ? 3 : 4; }
+// Activation / decoded-weight stages for a BN-token tile (shared memory
+// holds S activation tiles and two packed block columns).
+__host__ __device__ constexpr int stages_for(int bn) { return bn == 256 ? 5 : 8; }
+
+// Bytes per row of the packed block-column tile (TMA box inner size).
+__host__ __device__ constexpr int wbox_for(int fmt) { return fmt == Q4_K ? 144 : 224; }
 
 struct Params {
   int K, N, M;
@@ -61,15 +71,14 @@ struct Params {
   unsigned* status;
 };
 
-template <int BN>
+template <int FMT, int BN>
 struct Smem {
   static constexpr int S = stages_for(BN);
   static constexpr int x_tile = BN * 128;
   // offsets from the 1024-aligned base
   static constexpr int x = 0;
-  static constexpr int a = x + S * x_tile;
-  static constexpr int w = a + S * kTileBytes;
-  static constexpr int w_stage = 128 * 256;  // max box bytes per row (256) x 128 rows
+  static constexpr int w = x + S * x_tile;
+  static constexpr int w_stage = (BM * wbox_for(FMT) + 1023) / 1024 * 1024;
   static constexpr int bars = w + WS * w_stage;
   // barriers: xfull[S], afull[S], empty[S], wfull[WS], wempty[WS], accfull
   static constexpr int n_bars = 3 * S + 2 * WS + 1;
@@ -99,6 +108,29 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D (TMEM) += A (TMEM, 128 lanes x 16 fp16) . B (shared memory descriptor)^T
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 consecutive 32-bit TMEM columns of this thread's lane <- o[0..31].
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&o)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(o[0]), "r"(o[1]), "r"(o[2]), "r"(o[3]), "r"(o[4]), "r"(o[5]), "r"(o[6]), "r"(o[7]), "r"(o[8]), "r"(o[9]),
+      "r"(o[10]), "r"(o[11]), "r"(o[12]), "r"(o[13]), "r"(o[14]), "r"(o[15]), "r"(o[16]), "r"(o[17]), "r"(o[18]),
+      "r"(o[19]), "r"(o[20]), "r"(o[21]), "r"(o[22]), "r"(o[23]), "r"(o[24]), "r"(o[25]), "r"(o[26]), "r"(o[27]),
+      "r"(o[28]), "r"(o[29]), "r"(o[30]), "r"(o[31])
       : "memory");
 }
 
@@ -199,8 +231,8 @@ __device__ __forceinline__ uint2 ld_s64(uint32_t a) {
 }
 
 // Decode one row's 64 weights of K step `j4` of the block column (the row's
-// bytes start at `row`) into 32 fp16x2 words in k_perm order: word 4c + j is
-// pair P = 4c + j, i.e. 16-byte chunk c of the 128-byte tile row.
+// bytes start at `row`) into 32 fp16x2 words in k_perm order: word P holds
+// slot pair P, i.e. TMEM column P of the row's A stage.
 template <int FMT>
 __device__ __forceinline__ void decode64(uint32_t row, int j4, uint32_t (&o)[32]) {
   constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024 in both halves
@@ -275,8 +307,9 @@ template <int FMT, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                 const __grid_constant__ Params p) {
-  using L = Smem<BN>;
+  using L = Smem<FMT, BN>;
   constexpr int S = L::S;
+  static_assert(BN + 32 * S <= kTmemCols, "accumulator and A stages exceed tensor memory");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled tiles
   const uint32_t raw_s = smem_addr(smem_raw);
@@ -315,9 +348,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_fence_init();
   }
   if (warp == 1) {
-    // TMEM accumulator: 128 lanes x BN f32 columns.
+    // TMEM: accumulator (BN columns) and the A stages.  One CTA per SM (the
+    // shared-memory footprint allows no second one), so all 512 columns.
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
-                 "r"(BN));
+                 "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
@@ -376,11 +410,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       if (lane == 0) {
-        const uint32_t a0 = base + L::a + s * kTileBytes;
+        const uint32_t a0 = tmem + (uint32_t)(BN + 32 * s);
         const uint32_t b0 = base + L::x + s * L::x_tile;
 #pragma unroll
         for (int k = 0; k < BK / 16; ++k)
-          umma_f16(tmem, sw128_desc(a0 + 32 * k), sw128_desc(b0 + 32 * k), idesc, (ks > 0 || k > 0) ? 1u : 0u);
+          umma_f16_ts(tmem, a0 + 8 * k, sw128_desc(b0 + 32 * k), idesc, (ks > 0 || k > 0) ? 1u : 0u);
         umma_commit(empty(s));
       }
       __syncwarp();
@@ -391,8 +425,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // --------------------------- dequant + epilogue ---------------------------
     const int grp = (warp - 2) / kGroupWarps;           // 0: even K steps, 1: odd
-    const int r = ((warp - 2) % kGroupWarps) * 32 + lane;  // weight row of the tile
-    const uint32_t swz = (uint32_t)(r & 7);
+    // A warp reaches only TMEM lanes 32*(warp%4)..+31: those are its rows.
+    const int r = (warp & 3) * 32 + lane;  // weight row of the tile = TMEM lane
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
     for (int ks = grp; ks < nk; ks += 2) {
       const int wb = ks / steps_per_w, ws = wb % WS;
       bool ok = true;
@@ -405,17 +440,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_flag = 1;
         break;
       }
+      tc_fence_after();  // the MMAs that read this A stage are complete
       const int skew = (((kbeg + ks) / steps_per_w) * p.wbytes) & 15;
       const uint32_t rowp = base + L::w + ws * L::w_stage + r * p.wbox + skew;
-      const uint32_t dst = base + L::a + s * kTileBytes + r * 128;
       uint32_t o[32];
       decode64<FMT>(rowp, (kbeg + ks) % steps_per_w, o);
-#pragma unroll
-      for (int c = 0; c < 8; ++c)
-        st_s128(dst + ((((uint32_t)c) ^ swz) << 4), make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]));
-      // Every writer makes its stores visible to the tensor core (async
-      // proxy); the warp then signals the stage once.
-      fence_proxy_async_smem();
+      tmem_st32(tmem + lane_base + (uint32_t)(BN + 32 * s), o);
+      // Every writer waits for its tensor-memory stores and orders them
+      // before the barrier; the warp then signals the stage once.
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(afull(s));
@@ -459,7 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
   }
 }
 
@@ -499,8 +533,8 @@ struct Geometry {
 bool geometry(int dtype, int64_t K, int64_t row_bytes, Geometry& g) {
   if (K % BK != 0 || row_bytes % 16 != 0) return false;
   switch (dtype) {
-    case Q4_K: g.wcol = 256; g.wbytes = 144; g.wbox = 144; break;
-    case Q6_K: g.wcol = 256; g.wbytes = 210; g.wbox = 224; break;
+    case Q4_K: g.wcol = 256; g.wbytes = 144; g.wbox = wbox_for(Q4_K); break;
+    case Q6_K: g.wcol = 256; g.wbytes = 210; g.wbox = wbox_for(Q6_K); break;
     default: return false;
   }
   return K % g.wcol == 0;
@@ -512,7 +546,7 @@ cudaError_t run(const CUtensorMap& tw, const CUtensorMap& tx, const Params& p, c
   static int configured_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
-  const int smem = Smem<BN>::total + 1024;
+  const int smem = Smem<FMT, BN>::total + 1024;
   if (configured_dev != dev) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
