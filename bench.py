@@ -477,6 +477,21 @@ LAYER_7B = [("attn_q", 4096, 4096, 2), ("attn_k", 1024, 4096, 2), ("attn_v", 102
             ("ffn_down", 4096, 14336, 3)]  # (name, N, K, dtype): Q4_K_M-style, Q6_K down
 
 
+def gemm_launches(N, K, M, sms):
+    """Kernel launches of one batched product in libhyq (hyq_gemm.cu): the
+    fp16 activation copy, the GEMM, and the split-K reduction when the grid
+    of 128-row x (256|128)-token tiles is smaller than the SM count."""
+    bn = 256 if M >= 256 else 128
+    tiles = -(-N // 128) * -(-M // bn)
+    nwb = K // 256
+    z = 1
+    if tiles < sms:
+        z = max(1, min(-(-sms // tiles), nwb, 16))
+    per = -(-nwb // z)
+    splits = -(-nwb // per)
+    return 2 + (1 if splits > 1 else 0)
+
+
 def prefill_arm(a):
     import torch
 
@@ -498,10 +513,12 @@ def prefill_arm(a):
         for w, (_, N, K, _) in zip(ws, LAYER_7B):
             outs[w.name] = w.matmul(xs[K], M)
 
+    sampler = ClockSampler("GPU-" + str(torch.cuda.get_device_properties(dev).uuid))
     with torch.cuda.stream(stream):
         for _ in range(a.warmup):
             step()
         stream.synchronize()
+        sampler.start()
         per = {w.name: [] for w in ws}
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
@@ -516,8 +533,12 @@ def prefill_arm(a):
                 per[w.name].append((b, c))
         e1.record(stream)
     stream.synchronize()
+    sampler.stop()
+    clocks = sampler.summary()
     assert quant.device_status(dev) == 0
     ms = e0.elapsed_time(e1) / a.steps
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    launches = sum(gemm_launches(N, K, M, sms) for _, N, K, _ in LAYER_7B) * a.steps
     per_ms = {k: statistics.fmean(b.elapsed_time(c) for b, c in v) for k, v in per.items()}
     gate = per_ms["ffn_gate"]
     gate_flops = 2 * M * 14336 * 4096
@@ -538,10 +559,13 @@ def prefill_arm(a):
         "roofline": {"bound": "tensor", "kernel": "ffn_gate Q4_K 14336x4096 GEMM",
                      "achieved": round(gate_flops / (gate * 1e-3) / 1e12, 2), "peak": peak,
                      "peak_kind": "measured" if peaks else "fallback", "unit": "TFLOP/s",
-                     "frac": round(gate_flops / (gate * 1e-3) / 1e12 / peak, 4), "traffic": None,
-                     "avg_launch_ms": round(gate, 5)},
+                     "frac": round(gate_flops / (gate * 1e-3) / 1e12 / peak, 4),
+                     "traffic": profile_traffic(f"gemm_gate_m{M}"), "avg_launch_ms": round(gate, 5)},
         "per_projection_ms": {k: round(v, 5) for k, v in per_ms.items()},
         "prefill_tok_s_layer": round(M / (ms * 1e-3), 1),
+        "gpu_launches": launches,
+        "clocks": {"sm_mhz": clocks.get("sm_mhz"), "sm_max_mhz": clocks.get("sm_max_mhz"),
+                   "reasons": clocks.get("reasons", []), "samples": clocks.get("samples", 0)},
     }
     print(json.dumps(line), flush=True)
     return 0
