@@ -196,21 +196,29 @@ def cpu_step_bytes(lm_rows):
     return layer_bytes(5) + layer_bytes(6) + gemv_bytes(3, lm_rows, HIDDEN)
 
 
-def run_cpu(seconds, lm_rows):
-    from oracle import oracle as O
+def host_threads():
+    """Every host core this process may run on.  Set explicitly on each
+    oracle call, because torchrun exports OMP_NUM_THREADS=1 to its ranks."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
+
+def run_cpu(seconds, lm_rows):
     layers, lm, lm_rows, x = cpu_workload(lm_rows=lm_rows)
-    cpu_step(layers, lm, lm_rows, x)  # warm
+    threads = host_threads()
+    cpu_step(layers, lm, lm_rows, x, threads)  # warm
     n = 0
     t0 = time.perf_counter()
     while True:
-        cpu_step(layers, lm, lm_rows, x)
+        cpu_step(layers, lm, lm_rows, x, threads)
         n += 1
         el = time.perf_counter() - t0
         if el >= seconds:
             break
     gbs = n * cpu_step_bytes(lm_rows) / el / 1e9
-    return {"value": round(gbs, 3), "unit": "GB/s", "cores": O.max_threads(), "kind": "port",
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
             "sample": f"{n} passes of the full chain with the lm_head cut to {lm_rows} of {VOCAB} rows "
                       f"({el:.1f} s); oracle/hyq_oracle.c x86 f32 order, OpenMP"}
 
@@ -219,15 +227,14 @@ def reference_arm(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    from oracle import oracle as O
-
     lm_rows = VOCAB // 16
     layers, lm, lm_rows, x = cpu_workload(lm_rows=lm_rows)
+    threads = host_threads()
     for _ in range(a.warmup):
-        cpu_step(layers, lm, lm_rows, x)
+        cpu_step(layers, lm, lm_rows, x, threads)
     t0 = time.perf_counter()
     for _ in range(a.steps):
-        cpu_step(layers, lm, lm_rows, x)
+        cpu_step(layers, lm, lm_rows, x, threads)
     el = time.perf_counter() - t0
     gbs = a.steps * cpu_step_bytes(lm_rows) / el / 1e9
     sample = (f"each step: both layers in full + lm_head rows 0..{lm_rows} of {VOCAB} "
@@ -240,7 +247,7 @@ def reference_arm(a):
         "config": {"workload": "hy-mt-rs config 2: 1.8B decoder-layer projections (Q2_0C, STQ1_0) + Q6_K lm_head "
                                "120832x2048, batch 1", "path": "f32"},
         "impl": "reference",
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": O.max_threads(), "kind": "port",
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -290,7 +297,41 @@ def lm_head(lm, h, path, q8h=None):
     return lm.gemv_int8(h)
 
 
-def gpu_arm(a):
+def reduce_over_ranks(times_ms, clocks, device):
+    """Timing across replicas: every rank's device-timed durations reduced
+    with MAX (the job ends when its slowest rank does) and every rank's clock
+    summary gathered.  Same collectives, same order, on every rank."""
+    import torch
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return [float(t) for t in times_ms], [clocks]
+    t = torch.tensor([float(x) for x in times_ms], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    clocks_all = [None] * dist.get_world_size()
+    dist.all_gather_object(clocks_all, clocks)
+    return [float(x) for x in t.tolist()], clocks_all
+
+
+def device_failed(quant, dev):
+    """1.0 when a kernel on this device reported an expired bounded wait (the
+    status word), else 0.0; reduced with the timings so every rank raises
+    together instead of leaving the others inside a collective."""
+    try:
+        return 0.0 if quant.device_status(dev) == 0 else 1.0
+    except quant.HyqError:
+        return 1.0
+
+
+def job_rate(unit_per_step, steps, world, ms):
+    """Whole-job throughput: the units all replicas processed over the
+    max-over-ranks time, in units per second."""
+    return unit_per_step * steps * world / (ms * 1e-3)
+
+
+def init_ranks():
+    """One process per GPU (torchrun's RANK / LOCAL_RANK / WORLD_SIZE); NCCL
+    only for the barriers and the max-over-ranks timing."""
     import torch
     import torch.distributed as dist
 
@@ -303,6 +344,14 @@ def gpu_arm(a):
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local if world > 1 else 0)
     torch.cuda.set_device(dev)
+    return world, rank, dev
+
+
+def gpu_arm(a):
+    import torch
+    import torch.distributed as dist
+
+    world, rank, dev = init_ranks()
 
     import hy_mt_rs_b200  # noqa: F401
     from hy_mt_rs_b200 import quant
@@ -384,7 +433,7 @@ def gpu_arm(a):
     t_q2 = statistics.fmean(e[0].elapsed_time(e[1]) for e in evs)
     t_stq = statistics.fmean(e[1].elapsed_time(e[2]) for e in evs)
     t_lm = statistics.fmean(e[2].elapsed_time(e[3]) for e in evs)
-    assert quant.device_status(dev) == 0
+    failed = device_failed(quant, dev)
 
     # ---- e2e: host buffers through the public API, copies inside the region
     x_host = torch.randn(HIDDEN, generator=torch.Generator().manual_seed(1)).pin_memory()
@@ -409,21 +458,17 @@ def gpu_arm(a):
     e2e_ms = e0.elapsed_time(e1)
 
     step_bytes = layer_bytes(5) + layer_bytes(6) + gemv_bytes(3, VOCAB, HIDDEN)
-    if world > 1:
-        t = torch.tensor([ms, e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms = float(t[0]), float(t[1])
-        clocks_all = [None] * world
-        dist.all_gather_object(clocks_all, sampler.summary())
-    else:
-        clocks_all = [sampler.summary()]
+    (ms, e2e_ms, failed), clocks_all = reduce_over_ranks([ms, e2e_ms, failed + device_failed(quant, dev)],
+                                                         sampler.summary(), dev)
+    if failed:
+        raise RuntimeError("a kernel reported an expired bounded wait (device status word) on some rank")
 
     if rank == 0:
         peak, peak_kind = measured_peaks()
         lm_bytes = gemv_bytes(3, VOCAB, HIDDEN)
         achieved = lm_bytes / (t_lm * 1e-3) / 1e9
-        value = step_bytes * a.steps * world / (ms * 1e-3) / 1e9
-        e2e_value = step_bytes * e2e_steps * world / (e2e_ms * 1e-3) / 1e9
+        value = job_rate(step_bytes, a.steps, world, ms) / 1e9
+        e2e_value = job_rate(step_bytes, e2e_steps, world, e2e_ms) / 1e9
         sm = [c["sm_mhz"] for c in clocks_all if c.get("sm_mhz")]
         reasons = sorted({r for c in clocks_all for r in c.get("reasons", [])})
         kernel_key = f"lm_head_{path}"
@@ -494,11 +539,12 @@ def gemm_launches(N, K, M, sms):
 
 def prefill_arm(a):
     import torch
+    import torch.distributed as dist
 
+    world, rank, dev = init_ranks()
     import hy_mt_rs_b200  # noqa: F401
     from hy_mt_rs_b200 import quant, synth
 
-    dev = torch.device("cuda", 0)
     M = a.tokens
     ws = []
     for i, (name, N, K, t) in enumerate(LAYER_7B):
@@ -518,6 +564,9 @@ def prefill_arm(a):
         for _ in range(a.warmup):
             step()
         stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
         sampler.start()
         per = {w.name: [] for w in ws}
         e0 = torch.cuda.Event(enable_timing=True)
@@ -533,10 +582,23 @@ def prefill_arm(a):
                 per[w.name].append((b, c))
         e1.record(stream)
     stream.synchronize()
+    torch.cuda.synchronize(dev)
     sampler.stop()
-    clocks = sampler.summary()
-    assert quant.device_status(dev) == 0
-    ms = e0.elapsed_time(e1) / a.steps
+    if world > 1:
+        dist.barrier()
+    (ms_total, failed), clocks_all = reduce_over_ranks([e0.elapsed_time(e1), device_failed(quant, dev)],
+                                                       sampler.summary(), dev)
+    if failed:
+        raise RuntimeError("a kernel reported an expired bounded wait (device status word) on some rank")
+    ms = ms_total / a.steps
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    sm = [c["sm_mhz"] for c in clocks_all if c.get("sm_mhz")]
+    clocks = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": clocks_all[0].get("sm_max_mhz"),
+              "reasons": sorted({r for c in clocks_all for r in c.get("reasons", [])}),
+              "samples": sum(c.get("samples", 0) for c in clocks_all)}
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     launches = sum(gemm_launches(N, K, M, sms) for _, N, K, _ in LAYER_7B) * a.steps
     per_ms = {k: statistics.fmean(b.elapsed_time(c) for b, c in v) for k, v in per.items()}
@@ -551,21 +613,22 @@ def prefill_arm(a):
     peak = float(peaks.get("bf16_tflops", 1590.0))
     line = {
         "metric": "prefill GEMM TFLOP/s (7B layer projections, Q4_K + Q6_K down, fp16 tensor cores)",
-        "value": round(flops / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": 1, "steps": a.steps,
+        "value": round(job_rate(flops, 1, world, ms) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "fp16 operands (decoded weights, activations), f32 accumulate",
         "data": "synthetic", "config": {"workload": f"hy-mt-rs config 3: 7B layer projections, M={M}",
-                                        "tokens": M, "flops_per_step": flops, "weight_bytes": wbytes},
+                                        "tokens": M, "flops_per_step": flops, "weight_bytes": wbytes,
+                                        "parallelism": f"replicas x{world} (independent token batches)"},
         "roofline": {"bound": "tensor", "kernel": "ffn_gate Q4_K 14336x4096 GEMM",
                      "achieved": round(gate_flops / (gate * 1e-3) / 1e12, 2), "peak": peak,
                      "peak_kind": "measured" if peaks else "fallback", "unit": "TFLOP/s",
                      "frac": round(gate_flops / (gate * 1e-3) / 1e12 / peak, 4),
                      "traffic": profile_traffic(f"gemm_gate_m{M}"), "avg_launch_ms": round(gate, 5)},
         "per_projection_ms": {k: round(v, 5) for k, v in per_ms.items()},
-        "prefill_tok_s_layer": round(M / (ms * 1e-3), 1),
+        "prefill_tok_s_layer": round(job_rate(M, 1, world, ms), 1),
         "gpu_launches": launches,
-        "clocks": {"sm_mhz": clocks.get("sm_mhz"), "sm_max_mhz": clocks.get("sm_max_mhz"),
-                   "reasons": clocks.get("reasons", []), "samples": clocks.get("samples", 0)},
+        "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
     return 0

@@ -1,0 +1,88 @@
+"""Host-side logic of bench.py's N-GPU runs, on CPU with two gloo ranks:
+device-timed durations are reduced with MAX over ranks (the job ends with
+its slowest replica), clock summaries are gathered from every rank, a
+device-status failure on one rank reaches all of them through the same
+collective, and the whole-job value counts the units of every replica."""
+import os
+import socket
+import subprocess
+import sys
+from datetime import timedelta
+
+import pytest
+
+from conftest import ROOT
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, q):
+    sys.path.insert(0, ROOT)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import torch
+    import torch.distributed as dist
+
+    import bench
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        # rank r took 2 + r ms for the timed steps and 5 - r ms end to end;
+        # only rank 1 saw a failed status word
+        times, clocks = bench.reduce_over_ranks([2.0 + rank, 5.0 - rank, float(rank == 1)],
+                                                {"sm_mhz": 1900 + rank, "reasons": [f"r{rank}"], "samples": 3},
+                                                torch.device("cpu"))
+        q.put((rank, times, clocks))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_reduce_over_ranks_two_gloo_ranks():
+    import torch.multiprocessing as mp
+
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in range(world):
+        rank, times, clocks = q.get(timeout=120)
+        results[rank] = (times, clocks)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank in range(world):
+        times, clocks = results[rank]
+        assert times == [3.0, 5.0, 1.0]  # max over ranks, same on every rank
+        assert [c["sm_mhz"] for c in clocks] == [1900, 1901]
+
+
+def test_single_process_needs_no_process_group():
+    import torch
+
+    import bench
+
+    times, clocks = bench.reduce_over_ranks([1.5, 2.5], {"sm_mhz": 1965}, torch.device("cpu"))
+    assert times == [1.5, 2.5] and clocks == [{"sm_mhz": 1965}]
+
+
+def test_job_rate_counts_every_replica():
+    import bench
+
+    # 100 units per step, 10 steps, 4 replicas, slowest rank 2 ms -> 2e6 units/s
+    assert bench.job_rate(100, 10, 4, 2.0) == pytest.approx(2e6)
+    assert bench.job_rate(100, 10, 1, 2.0) == pytest.approx(5e5)
+
+
+def test_reference_arm_other_ranks_exit_without_work():
+    env = dict(os.environ, RANK="1", WORLD_SIZE="2", LOCAL_RANK="1")
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--gpus", "2",
+                        "--steps", "1", "--warmup", "0"], env=env, capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0
+    assert r.stdout.strip() == ""
