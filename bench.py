@@ -49,9 +49,14 @@ def args_parse():
     ap.add_argument("--impl", choices=["hyq", "reference"], default="hyq")
     ap.add_argument("--path", choices=["f32", "q8"], default="f32")
     ap.add_argument("--copies", type=int, default=4)
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="decode: plain stream order instead of overlapped launches (hyq_set_launch_overlap)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
-    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
-                    help="decode: config 2 (default line); prefill: config 3 (7B layer GEMMs)")
+    ap.add_argument("--workload", choices=["decode", "prefill", "gemv"], default="decode",
+                    help="decode: config 2 (default line); prefill: config 3 (7B layer GEMMs); "
+                         "gemv: config 1 (one 6144x2048 product, L2 defeated by rotating copies)")
+    ap.add_argument("--sweep", action="store_true",
+                    help="gemv: also measure every packed format at 6144x2048 and 120832x2048, both paths")
     ap.add_argument("--tokens", type=int, default=512, help="prefill: tokens M")
     return ap.parse_args()
 
@@ -359,6 +364,10 @@ def gpu_arm(a):
     copies = max(1, a.copies)
     layers, lm = build_weights(dev, copies)
     path = a.path
+    # The weights are final before any product is issued, which is what
+    # overlapped launches require of the caller.
+    torch.cuda.synchronize(dev)
+    quant.set_launch_overlap(not a.no_overlap)
     x_static = torch.randn(HIDDEN, generator=torch.Generator().manual_seed(0)).to(dev)
     q8h = quant.Q8(HIDDEN, dev)
     q8f = quant.Q8(FFN, dev)
@@ -483,6 +492,7 @@ def gpu_arm(a):
             "config": {"workload": "hy-mt-rs config 2: 1.8B decoder-layer projections (Q2_0C, STQ1_0) + "
                                    "Q6_K lm_head 120832x2048, batch 1",
                        "path": path, "layer_copies": copies, "step_bytes": step_bytes,
+                       "launch_overlap": not a.no_overlap,
                        "l2": "inputs larger than L2: every step streams the 203 MB lm_head; layers rotate copies",
                        "parallelism": f"replicas x{world} (rows are independent; no collective)"},
             "roofline": {"bound": "hbm", "kernel": f"lm_head Q6_K {path} GEMV", "achieved": round(achieved, 1),
@@ -634,12 +644,119 @@ def prefill_arm(a):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# Single products (config 1, and every format at two sizes with --sweep)
+# ---------------------------------------------------------------------------
+FMT_NAMES = {2: "Q4_K", 3: "Q6_K", 4: "Q8_0", 5: "Q2_0C", 6: "STQ1_0"}
+
+
+def time_products(dtype, N, K, path, dev, min_bytes=256 << 20, reps=1000, seed=0):
+    """Batch-1 products over enough distinct weight copies that their bytes
+    exceed L2 twice over, replayed from one CUDA graph (one launch per copy)
+    until `reps` products ran.  Returns (bytes per product, mean ms per
+    product, copies)."""
+    import torch
+    from hy_mt_rs_b200 import quant, synth
+
+    one = gemv_bytes(dtype, N, K)
+    copies = max(2, -(-min_bytes // (N * row_bytes(dtype, K))))
+    ws = [quant.Weight(synth.random_packed(dtype, N, K, seed=seed + c, device=dev), dtype, [K, N])
+          for c in range(copies)]
+    x = torch.randn(K, generator=torch.Generator().manual_seed(seed)).to(dev)
+    ys = [torch.empty(N, device=dev) for _ in range(copies)]
+    torch.cuda.synchronize(dev)
+    quant.set_launch_overlap(True)
+    stream = torch.cuda.Stream(dev)
+
+    def run():
+        for w, y in zip(ws, ys):
+            if path == "f32":
+                quant.check(quant.lib.hyq_matmul(w.handle, quant._ptr(x), 1, quant._ptr(y), quant._stream(dev)))
+            else:
+                w.gemv_int8(x, out=y)
+
+    with torch.cuda.stream(stream):
+        run()
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            run()
+        rounds = max(1, -(-reps // copies))
+        for _ in range(3):
+            g.replay()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(rounds):
+            g.replay()
+        e1.record(stream)
+        stream.synchronize()
+    ms = e0.elapsed_time(e1) / (rounds * copies)
+    if quant.device_status(dev) != 0:
+        raise RuntimeError("device status word set")
+    del g
+    return one, ms, copies
+
+
+def gemv_arm(a):
+    import torch
+
+    world, rank, dev = init_ranks()
+    import hy_mt_rs_b200  # noqa: F401
+
+    peak, peak_kind = measured_peaks()
+    sampler = ClockSampler("GPU-" + str(torch.cuda.get_device_properties(dev).uuid))
+    sampler.start()
+    res = {}
+    for path in ("f32", "int8"):
+        b, ms, copies = time_products(2, 6144, 2048, path, dev)
+        res[path] = {"gb_s": round(b / (ms * 1e-3) / 1e9, 1), "us_per_product": round(ms * 1e3, 3),
+                     "frac_of_hbm": round(b / (ms * 1e-3) / 1e9 / peak, 4), "copies": copies}
+    sweep = {}
+    if a.sweep:
+        for t in (2, 3, 4, 5, 6):
+            for N in (6144, 120832):
+                for path in ("f32", "int8"):
+                    b, ms, copies = time_products(t, N, 2048, path, dev, seed=10 * t)
+                    sweep[f"{FMT_NAMES[t]} {N}x2048 {path}"] = {
+                        "gb_s": round(b / (ms * 1e-3) / 1e9, 1), "us": round(ms * 1e3, 2),
+                        "frac_of_hbm": round(b / (ms * 1e-3) / 1e9 / peak, 4)}
+    sampler.stop()
+    clocks = sampler.summary()
+    f32 = res["f32"]
+    b = gemv_bytes(2, 6144, 2048)
+    line = {
+        "metric": "quantized GEMV HBM GB/s (config 1: Q4_K 6144x2048, batch 1)",
+        "value": f32["gb_s"], "unit": "GB/s", "n_gpus": 1, "steps": 1000, "warmup": 3,
+        "ms_per_step": round(f32["us_per_product"] / 1e3, 6), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 activations x packed int weights (exact int32 dp4a)",
+        "data": "synthetic (seeded N(0,0.02) weights packed by hy_mt_rs_b200.synth; N(0,1) activations)",
+        "config": {"workload": "hy-mt-rs config 1: Q4_K 6144x2048 batch-1 product, 1000 products",
+                   "l2": f"{f32['copies']} distinct weight copies rotate (> 2 x L2), one CUDA graph",
+                   "launch_overlap": True},
+        "paths": res,
+        "roofline": {"bound": "hbm", "kernel": "Q4_K 6144x2048 f32 GEMV", "achieved": f32["gb_s"], "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": f32["frac_of_hbm"], "traffic": None,
+                     "algorithmic_bytes_per_launch": b, "avg_launch_ms": round(f32["us_per_product"] / 1e3, 6)},
+        "gpu_launches": 1000,
+        "clocks": {"sm_mhz": clocks.get("sm_mhz"), "sm_max_mhz": clocks.get("sm_max_mhz"),
+                   "reasons": clocks.get("reasons", []), "samples": clocks.get("samples", 0)},
+    }
+    if sweep:
+        line["sweep"] = sweep
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     a = args_parse()
     if a.impl == "reference":
         return reference_arm(a)
     if a.workload == "prefill":
         return prefill_arm(a)
+    if a.workload == "gemv":
+        return gemv_arm(a)
     return gpu_arm(a)
 
 

@@ -67,6 +67,7 @@ _SIGS = {
     "hyq_gemv_qkv_int8": ([_wp, _wp, _wp, _vp, _vp, _vp, _vp, _vp], C.c_int),
     "hyq_matmul_gate_up_silu_int8": ([_wp, _wp, _vp, _vp, _vp], C.c_int),
     "hyq_matmul_noalloc": ([_wp, _vp, _i64, _vp, _vp], C.c_int),
+    "hyq_set_launch_overlap": ([C.c_int], C.c_int),
     "hyq_device_status": ([_vp, C.POINTER(C.c_uint32)], C.c_int),
 }
 

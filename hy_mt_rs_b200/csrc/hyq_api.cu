@@ -3,6 +3,7 @@
 // to the kernel translation units.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -82,6 +83,10 @@ void ensure_pool() {
   }
   done[dev] = true;
 }
+
+// hyq_set_launch_overlap: batch-1 products launch as programmatic dependents
+// of the preceding grid in their stream.
+std::atomic<int> g_launch_overlap{0};
 
 // Batches from this size up go to the tensor-core GEMM when the format and
 // shape allow it; smaller batches run batch-1 products.
@@ -173,6 +178,7 @@ int run_gemv(int n_mat, const hyq_weight* const* ws, float* const* ys, const hyq
   j.xs = a.xs;
   j.quantize_q8 = a.quantize;
   j.status = status;
+  j.overlap = g_launch_overlap.load(std::memory_order_relaxed) != 0;
   const cudaError_t e = hyq::launch_gemv(j, st);
   if (e == cudaErrorNotSupported)
     return fail(HYQ_E_UNSUPPORTED, "%s: in-kernel Q8 needs K to be a multiple of 256 for this buffer layout", name);
@@ -471,6 +477,11 @@ int hyq_matmul_gate_up_silu_int8(const hyq_weight* gate, const hyq_weight* up, c
   a.quantize = true;
   if ((rc = check_act(a, "gate_up_silu_int8"))) return rc;
   return run_gemv(1, &gate, &out, up, a, (cudaStream_t)stream, "gate_up_silu_int8");
+}
+
+int hyq_set_launch_overlap(int enable) {
+  g_launch_overlap.store(enable ? 1 : 0, std::memory_order_relaxed);
+  return HYQ_OK;
 }
 
 int hyq_device_status(void* stream, uint32_t* status_out) {

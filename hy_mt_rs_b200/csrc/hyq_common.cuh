@@ -109,6 +109,25 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       : "memory");
 }
 
+// L2 policy for data read once per call (streamed weights): such lines go
+// first when L2 needs room, so the weights do not push kernel code,
+// parameters and activations out of L2.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// bulk_g2s with an L2 cache policy.
+__device__ __forceinline__ void bulk_g2s_hint(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                              uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+      : "memory");
+}
+
 // Exact IEEE binary16 -> f32 of the `half` crate (finite values are exact,
 // NaNs are quieted with their payload).  Used where decode output bits matter.
 __device__ __forceinline__ float half_bits_to_f32(uint32_t h) {
@@ -187,6 +206,16 @@ __device__ __forceinline__ bool bar_red_and(int id, int count, bool v) {
       : "r"((uint32_t)v), "r"(id), "r"(count)
       : "memory");
   return r != 0;
+}
+
+// Programmatic dependent launch.  `grid_dependency_wait` returns once every
+// grid this one depends on has completed and its memory is visible (at once
+// when the launch carried no programmatic dependency);
+// `allow_dependents_launch` lets the next grid in the stream be scheduled
+// before this one completes.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_dependents_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 __device__ __forceinline__ void bar_sync_named(int id, int count) {

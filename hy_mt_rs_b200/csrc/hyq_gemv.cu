@@ -116,7 +116,10 @@ Plan make_plan(const GemvJob& j) {
   const int np = (j.x && !j.quantize_q8) ? 3 : 1;
   // prepared activations: np byte planes of 16 words per unit, 2 floats per group
   pl.x_bytes = (np * 16 * U + 2 * (U / 4)) * 4;
-  const int stage_off = (kHeaderBytes + pl.x_bytes + 127) / 128 * 128;
+  // f32 activations staged by one bulk copy when they are small
+  pl.x_raw_bytes = (j.x && j.K * 4 <= kXStageMax) ? (int)(j.K * 4) : 0;
+  pl.x_raw_off = pl.x_raw_bytes ? (kHeaderBytes + pl.x_bytes + 15) / 16 * 16 : 0;
+  const int stage_off = (kHeaderBytes + pl.x_bytes + (pl.x_raw_bytes ? 16 + pl.x_raw_bytes : 0) + 127) / 128 * 128;
   const int upl_max = np == 1 ? 4 : 1;
   const int64_t row_bytes = j.K / block_len(t) * block_bytes(t);
   int64_t total_rows = 0;
@@ -162,6 +165,13 @@ Plan make_plan(const GemvJob& j) {
   }
   int stages = (int)((smem_cap - stage_off) / pl.stage_bytes);
   if (stages > kMaxStages) stages = kMaxStages;
+  // No more stages than a CTA has tiles (plus one): small products then
+  // initialise fewer barriers and claim less shared memory.
+  {
+    const int64_t grid = pl.total_batches < g_num_sms ? pl.total_batches : g_num_sms;
+    const int64_t per_cta = grid > 0 ? (pl.total_batches + grid - 1) / grid : 1;
+    if (per_cta + 1 < stages) stages = (int)(per_cta + 1 > 2 ? per_cta + 1 : 2);
+  }
   if (stages < 2) return pl;
   pl.stages = stages;
   pl.smem = (size_t)stage_off + (size_t)stages * pl.stage_bytes;
@@ -213,7 +223,8 @@ cudaError_t launch_gemv(const GemvJob& j, cudaStream_t st) {
   p.xmode = j.x ? (j.quantize_q8 ? XQ8F : XF32) : XQ8;
   p.status = j.status;
   const bool pair = j.up != nullptr;
-  const Plan pl = make_plan(j);
+  Plan pl = make_plan(j);
+  pl.overlap = j.overlap;
   if (!pl.streaming) {
     if (p.xmode == XQ8F && j.K % 256 != 0) return cudaErrorNotSupported;
     switch (j.dtype) {
@@ -236,6 +247,7 @@ cudaError_t launch_gemv(const GemvJob& j, cudaStream_t st) {
   p.half_bytes = pl.half_bytes;
   p.stage_bytes = pl.stage_bytes;
   p.x_off = kHeaderBytes;
+  p.x_raw_off = pl.x_raw_off;
   p.stage_off = (int)(pl.smem - (size_t)pl.stages * pl.stage_bytes);
   switch (j.dtype) {
     case Q4_K: return dispatch_fmt<Q4_K>(p, pl, pair, st);

@@ -44,7 +44,9 @@ constexpr int kCW = 12;                    // consumer warps (13 warps: <= 128 r
 constexpr int kThreads = (kCW + 1) * 32;   // + one producer warp
 constexpr int kMaxStages = 32;
 constexpr int kRedOffset = 528;            // partial sums: 2 copies x 12 warps x 4 rows x (gate, up)
-constexpr int kHeaderBytes = 2048;         // barriers [0,512), abort flag, partial sums [528,1296)
+constexpr int kHeaderBytes = 2048;         // barriers [0,512), abort flag, partial sums [528,1296), x barrier
+constexpr int kXBarOffset = 1296;          // mbarrier of the activation copy
+constexpr int kXStageMax = 32768;          // f32 activations up to this many bytes arrive by one bulk copy
 constexpr int kConsumerBarrier = 15;       // named barrier of the 12 consumer warps
 
 // Activation modes.
@@ -105,6 +107,7 @@ struct Params {
   int half_bytes;      // bytes of one row-tile buffer
   int stage_bytes;
   int x_off;           // shared-memory offset of the prepared activations
+  int x_raw_off;       // shared-memory offset of the f32 activation copy (0: read x from global memory)
   int stage_off;       // shared-memory offset of stage 0
   int xmode;
   const float* x;      // XF32 / XQ8F
@@ -178,12 +181,34 @@ __device__ void prepare_x(const Params& p, uint8_t* smem) {
   float* sg = reinterpret_cast<float*>(words + NP * 16 * U);
   float* gaux = sg + G;  // XF32: 2^(22-e); XQ8F: 127/max
   const int ctid = threadIdx.x, warp = ctid >> 5, lane = ctid & 31;
+  // f32 activations come into shared memory with one bulk copy (after the
+  // preceding grid has completed); the maxima and the words read them there.
+  const float* xsrc = p.x;
+  if (p.x_raw_off) {
+    const uint32_t xbar = smem_addr(smem + kXBarOffset);
+    float* raw = reinterpret_cast<float*>(smem + p.x_raw_off);
+    const uint32_t bytes = (uint32_t)p.K * 4u;
+    if (ctid == 0) {
+      mbar_arrive_expect_tx(xbar, bytes);
+      bulk_g2s(smem_addr(raw), p.x, bytes, xbar);
+    }
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 16 * kMaxStages);
+    if (!mbar_wait(xbar, 0, abort_flag)) {
+      if (ctid == 0) {
+        atomicOr(p.status, DEV_TIMEOUT_FULL);
+        *abort_flag = 1;
+        // no copy may land after the CTA is gone
+        if (!mbar_wait(xbar, 0, nullptr)) atomicOr(p.status, DEV_TIMEOUT_DRAIN);
+      }
+    }
+    xsrc = raw;
+  }
   if (p.xmode == XQ8) {
     for (int g = ctid; g < G; g += kCW * 32) sg[g] = p.xs[g];
   } else {
     // Group maxima: one warp per 256-column group.
     for (int g = warp; g < G; g += kCW) {
-      const float4* src = reinterpret_cast<const float4*>(p.x + 256 * g);
+      const float4* src = reinterpret_cast<const float4*>(xsrc + 256 * g);
       const float4 a = src[lane], b = src[32 + lane];
       const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
       float m = 0.f;
@@ -241,12 +266,12 @@ __device__ void prepare_x(const Params& p, uint8_t* smem) {
         w0 |= ((uint32_t)(uint8_t)p.xq[col]) << (8 * b);
       } else if (p.xmode == XQ8F) {
         // vcvtnq_s32_f32 + saturating narrows: nearest-even, NaN -> 0.
-        const float s = __fmul_rn(p.x[col], gaux[u >> 2]);
+        const float s = __fmul_rn(xsrc[col], gaux[u >> 2]);
         const int q = isnan(s) ? 0 : max(-128, min(127, __float2int_rn(s)));
         w0 |= ((uint32_t)q & 0xffu) << (8 * b);
       } else {
         const float sc = gaux[u >> 2];
-        const int X = sc == 0.f ? 0 : __float2int_rn(p.x[col] * sc);
+        const int X = sc == 0.f ? 0 : __float2int_rn(xsrc[col] * sc);
         const int p0 = (int)(int8_t)(X & 0xff);
         const int t = (X - p0) >> 8;
         const int p1 = (int)(int8_t)(t & 0xff);
@@ -494,9 +519,10 @@ __device__ __forceinline__ uint32_t stage_tail(uint8_t* dst, const uint8_t* src,
   return (uint32_t)(b1 - a0);
 }
 
-__device__ __forceinline__ void stage_bulk(uint8_t* dst, const uint8_t* src, uint32_t bulk, uint32_t bar) {
+__device__ __forceinline__ void stage_bulk(uint8_t* dst, const uint8_t* src, uint32_t bulk, uint32_t bar,
+                                           uint64_t policy) {
   const uintptr_t a0 = reinterpret_cast<uintptr_t>(src) & ~uintptr_t(15);
-  if (bulk) bulk_g2s(smem_addr(dst), reinterpret_cast<const void*>(a0), bulk, bar);
+  if (bulk) bulk_g2s_hint(smem_addr(dst), reinterpret_cast<const void*>(a0), bulk, bar, policy);
 }
 
 // Reduce V = 2^k per-lane values over the warp with a transposed butterfly:
@@ -562,17 +588,27 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
       mbar_init(smem_addr(&full[s]), 1);
       mbar_init(smem_addr(&empty[s]), kCW);
     }
+    mbar_init(smem_addr(smem + kXBarOffset), 1);
     *abort_flag = 0;
     mbar_fence_init();
+    // With an overlapped launch the next product may start streaming its
+    // weights now; everything it reads from this grid waits for completion.
+    allow_dependents_launch();
   }
   __syncthreads();
 
   if (warp == kCW) {
     // ------------------------------ producer ------------------------------
+    // The packed weights are read-only for the whole call sequence, so the
+    // first ring of tiles is fetched before the preceding grid completes
+    // (overlapped launches only); the bounded waits start after it has.
     if (lane == 0) {
+      // Each packed weight byte is used once per call.
+      const uint64_t policy = l2_evict_first_policy();
       int64_t issued = 0;
       for (int64_t bt = blockIdx.x; bt < p.total_batches; bt += gridDim.x, ++issued) {
         const int s = (int)(issued % S);
+        if (issued == S) grid_dependency_wait();
         if (issued >= S) {
           const uint32_t par = (uint32_t)(((issued / S) - 1) & 1);
           if (!mbar_wait(smem_addr(&empty[s]), par, abort_flag)) {
@@ -593,8 +629,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         const uint32_t b0 = stage_tail(dst, src, bytes);
         const uint32_t b1 = PAIR ? stage_tail(dst + p.half_bytes, srcu, bytes) : 0u;
         mbar_arrive_expect_tx(bar, b0 + b1);
-        stage_bulk(dst, src, b0, bar);
-        if (PAIR) stage_bulk(dst + p.half_bytes, srcu, b1, bar);
+        stage_bulk(dst, src, b0, bar, policy);
+        if (PAIR) stage_bulk(dst + p.half_bytes, srcu, b1, bar, policy);
       }
       // Do not leave while copies into this CTA's shared memory are in flight.
       const int64_t last = issued;
@@ -608,6 +644,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
   }
 
   // ------------------------------ consumers -------------------------------
+  grid_dependency_wait();  // x is the preceding grid's output; y may be its input
   prepare_x<FMT, NP>(p, smem);
   const int ksi = warp % p.ks, rgi = warp / p.ks;
   XUnit<NP> xu[UPL];
@@ -707,11 +744,15 @@ struct Plan {
   bool streaming = false;
   int ks = 1, slice = 0, upl = 1, rw = 1, stages = 0, half_bytes = 0, stage_bytes = 0;
   int x_bytes = 0;
+  int x_raw_bytes = 0, x_raw_off = 0;  // staged f32 activations (0: none)
   int64_t total_batches = 0;
   int64_t batch_begin[3] = {};
   size_t smem = 0;
   int smem_cap = 0;
   int grid = 0;
+  // Launch as a programmatic dependent of the preceding grid in the stream
+  // (the caller guarantees no kernel still in flight writes the weights).
+  bool overlap = false;
 };
 
 template <int FMT, int NP, int UPL, int RW, bool PAIR>
@@ -725,6 +766,19 @@ cudaError_t run_stream(const Params& p, const Plan& pl, cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem_cap);
     if (e != cudaSuccess) return e;
     configured_dev = dev;
+  }
+  if (pl.overlap) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)pl.grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = pl.smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k, p);
   }
   k<<<pl.grid, kThreads, pl.smem, st>>>(p);
   return cudaGetLastError();

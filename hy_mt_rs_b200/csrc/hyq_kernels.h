@@ -31,6 +31,9 @@ struct GemvJob {
   // instead of multiplying the f32 values.
   bool quantize_q8 = false;
   unsigned* status = nullptr;     // device status word (bounded-wait failures)
+  // Launch as a programmatic dependent of the preceding grid in the stream
+  // (hyq_set_launch_overlap); weights must not be written by work in flight.
+  bool overlap = false;
 };
 
 cudaError_t launch_gemv(const GemvJob& job, cudaStream_t st);

@@ -27,7 +27,8 @@ import torch
 from . import _native
 from ._native import HyqError, check, lib
 
-__all__ = ["DType", "Profile", "Weight", "Q8", "decode", "dot", "device_status", "HyqError"]
+__all__ = ["DType", "Profile", "Weight", "Q8", "decode", "dot", "device_status", "set_launch_overlap",
+           "HyqError"]
 
 
 class Profile(enum.IntEnum):
@@ -334,6 +335,14 @@ def dot(a, b):
     out = torch.empty((), dtype=torch.float32, device=a.device)
     check(lib.hyq_dot(_ptr(a), _ptr(b), a.numel(), _ptr(out), _stream(a.device)))
     return out
+
+
+def set_launch_overlap(enable):
+    """hyq_set_launch_overlap: let batch-1 products start streaming their
+    weights while the preceding kernel in the stream still runs (launch-latency
+    hiding in decode chains).  Only for weights that no kernel in flight
+    writes: build or upload them, synchronize, then enable."""
+    check(lib.hyq_set_launch_overlap(1 if enable else 0))
 
 
 def device_status(device=None):

@@ -150,6 +150,19 @@ int hyq_gemv_qkv_int8(const hyq_weight* q, const hyq_weight* k, const hyq_weight
 int hyq_matmul_gate_up_silu_int8(const hyq_weight* gate, const hyq_weight* up, const float* input, float* out,
                                  void* stream);
 
+/* Overlapped launches (no counterpart in the reference, which runs on the
+ * host).  With `enable` != 0, every later batch-1 product (hyq_matmul with
+ * batch 1..15, hyq_gemv_*, hyq_matmul_gate_up_silu*) launches as a
+ * programmatic dependent of the preceding grid in its stream: it is scheduled
+ * while that grid is still running and starts streaming its packed weights,
+ * and waits for that grid to complete before it reads activations or writes
+ * outputs.  This hides launch latency and the first weight fetch in chains of
+ * products (a decode step).  Contract: no kernel still in flight on the stream
+ * when a product is issued may write that product's weights (upload or wrap
+ * the weights, then order them before use, e.g. by a stream synchronization).
+ * Process-wide; default 0 (plain stream order). */
+int hyq_set_launch_overlap(int enable);
+
 /* Bytes of the fixed device scratch behind hyq_matmul_noalloc (64 MiB). */
 #define HYQ_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)
 
