@@ -52,9 +52,11 @@ def args_parse():
     ap.add_argument("--no-overlap", action="store_true",
                     help="decode: plain stream order instead of overlapped launches (hyq_set_launch_overlap)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
-    ap.add_argument("--workload", choices=["decode", "prefill", "gemv"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "gemv", "tp"], default="decode",
                     help="decode: config 2 (default line); prefill: config 3 (7B layer GEMMs); "
                          "gemv: config 1 (one 6144x2048 product, L2 defeated by rotating copies)")
+    ap.add_argument("--tp-mode", choices=["decode", "prefill"], default="decode",
+                    help="tp: batch-1 layer chain (decode) or the layer's GEMMs at --tokens (prefill)")
     ap.add_argument("--sweep", action="store_true",
                     help="gemv: also measure every packed format at 6144x2048 and 120832x2048, both paths")
     ap.add_argument("--tokens", type=int, default=512, help="prefill: tokens M")
@@ -749,6 +751,116 @@ def gemv_arm(a):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# Tensor parallelism over the 7B layer (config 3 shapes), one process per GPU
+# ---------------------------------------------------------------------------
+TP_COL = ("attn_q", "attn_k", "attn_v", "ffn_gate", "ffn_up")  # split output rows
+TP_ROW = ("attn_output", "ffn_down")                               # split input columns + all-reduce
+
+
+def tp_arm(a):
+    """Dense tensor parallelism of one 7B decoder layer's projections: QKV and
+    gate/up column-parallel, O and down row-parallel with an all-reduce of the
+    partial outputs (NCCL).  Every rank builds the full layer from the same
+    seeds and keeps its shards, so the job equals the one-GPU layer."""
+    import torch
+    import torch.distributed as dist
+
+    world, rank, dev = init_ranks()
+    import hy_mt_rs_b200  # noqa: F401
+    from hy_mt_rs_b200 import quant, synth
+
+    full = {}
+    for i, (name, N, K, t) in enumerate(LAYER_7B):
+        full[name] = quant.Weight(synth.random_packed(t, N, K, seed=50 + i, device=dev), t, [K, N], name=name)
+    sh = {n: (w.shard(0, rank, world) if n in TP_COL else w.shard(1, rank, world)) for n, w in full.items()}
+    for n in TP_ROW:
+        del full[n]  # row shards are copies
+    torch.cuda.synchronize(dev)
+    quant.set_launch_overlap(a.tp_mode == "decode")
+    H, F = 4096, 14336
+    stream = torch.cuda.Stream(dev)
+    if a.tp_mode == "decode":
+        M = 1
+        x = torch.randn(H, generator=torch.Generator().manual_seed(1)).to(dev)
+
+        def step():
+            q, k, v = quant.Weight.gemv_qkv(sh["attn_q"], sh["attn_k"], sh["attn_v"], x)
+            o = sh["attn_output"].matmul(q, 1)[0]  # attention output stands in as q (same shard width)
+            if world > 1:
+                dist.all_reduce(o)
+            g = sh["ffn_gate"].matmul_gate_up_silu(sh["ffn_up"], o)
+            h = sh["ffn_down"].matmul(g, 1)[0]
+            if world > 1:
+                dist.all_reduce(h)
+            return h
+        flops = 2 * sum(N * K for _, N, K, _ in LAYER_7B)
+    else:
+        M = a.tokens
+        xs = {H: torch.randn(M, H, generator=torch.Generator().manual_seed(H)).to(dev),
+              F // world: torch.randn(M, F // world, generator=torch.Generator().manual_seed(F)).to(dev),
+              H // world: torch.randn(M, H // world, generator=torch.Generator().manual_seed(7)).to(dev)}
+
+        def step():
+            for n in ("attn_q", "attn_k", "attn_v", "ffn_gate", "ffn_up"):
+                sh[n].matmul(xs[H], M)
+            o = sh["attn_output"].matmul(xs[H // world], M)
+            d = sh["ffn_down"].matmul(xs[F // world], M)
+            if world > 1:
+                dist.all_reduce(o)
+                dist.all_reduce(d)
+            return d
+        flops = 2 * M * sum(N * K for _, N, K, _ in LAYER_7B)
+    wbytes = sum(N * row_bytes(t, K) for _, N, K, t in LAYER_7B)
+    with torch.cuda.stream(stream):
+        for _ in range(a.warmup):
+            step()
+        stream.synchronize()
+        graph = None
+        if a.tp_mode == "decode":
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                step()
+            for _ in range(3):
+                graph.replay()
+            stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(a.steps):
+            graph.replay() if graph is not None else step()
+        e1.record(stream)
+        stream.synchronize()
+    failed = device_failed(quant, dev)
+    (ms_total, failed), _ = reduce_over_ranks([e0.elapsed_time(e1), failed], {}, dev)
+    if failed:
+        raise RuntimeError("a kernel reported an expired bounded wait (device status word) on some rank")
+    ms = ms_total / a.steps
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    if a.tp_mode == "decode":
+        line = {"metric": "7B layer projections, batch-1 decode, tensor-parallel: weight GB/s",
+                "value": round(wbytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "layer_us": round(ms * 1e3, 3), "dtype": "f32 activations x packed int weights"}
+    else:
+        line = {"metric": f"7B layer GEMMs at M={M}, tensor-parallel: TFLOP/s",
+                "value": round(flops / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                "layer_us": round(ms * 1e3, 3), "dtype": "fp16 operands, f32 accumulate"}
+    line.update({"n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms, 5),
+                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "data": "synthetic",
+                 "config": {"workload": f"hy-mt-rs config 3 shapes, TP={world} ({a.tp_mode})", "tokens": M,
+                            "parallelism": f"tp{world}: QKV, gate/up column-parallel; O, down row-parallel "
+                                           "+ NCCL all-reduce", "weight_bytes": wbytes}})
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     a = args_parse()
     if a.impl == "reference":
@@ -757,6 +869,8 @@ def main():
         return prefill_arm(a)
     if a.workload == "gemv":
         return gemv_arm(a)
+    if a.workload == "tp":
+        return tp_arm(a)
     return gpu_arm(a)
 
 

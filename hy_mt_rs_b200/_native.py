@@ -50,6 +50,7 @@ _SIGS = {
     "hyq_upload": ([_vp, C.c_size_t, C.c_int, C.c_int, _i64p, C.POINTER(_wp)], C.c_int),
     "hyq_weight_wrap": ([_vp, C.c_size_t, C.c_int, C.c_int, _i64p, C.POINTER(_wp)], C.c_int),
     "hyq_weight_expert": ([_wp, _i64, C.POINTER(_wp)], C.c_int),
+    "hyq_weight_shard": ([_wp, C.c_int, _i64, _i64, _vp, C.POINTER(_wp)], C.c_int),
     "hyq_weight_info": ([_wp, C.POINTER(C.c_int), C.POINTER(C.c_int), _i64p, C.POINTER(C.c_size_t),
                          C.POINTER(_vp)], C.c_int),
     "hyq_free": ([_wp], None),

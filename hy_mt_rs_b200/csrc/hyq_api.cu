@@ -268,6 +268,60 @@ int hyq_weight_expert(const hyq_weight* w, int64_t index, hyq_weight** out) {
   return HYQ_OK;
 }
 
+int hyq_weight_shard(const hyq_weight* w, int axis, int64_t part, int64_t parts, void* stream, hyq_weight** out) {
+  if (!w || !out) return fail(HYQ_E_INVALID, "shard: null argument");
+  *out = nullptr;
+  if (w->ndim != 2) return fail(HYQ_E_SHAPE, "shard: weight is not a matrix");
+  if (parts < 1 || part < 0 || part >= parts) return fail(HYQ_E_INVALID, "shard: part %lld of %lld", (long long)part,
+                                                          (long long)parts);
+  const int64_t K = w->dims[0], N = w->dims[1];
+  const int64_t rb = row_bytes(w->dtype, K);
+  if (axis == 0) {
+    // Column-parallel: a contiguous range of output rows, viewed in place.
+    if (N % parts != 0) return fail(HYQ_E_SHAPE, "shard: %lld rows do not split into %lld parts", (long long)N,
+                                    (long long)parts);
+    const int64_t n = N / parts;
+    hyq_weight* s = new hyq_weight{};
+    s->dtype = w->dtype;
+    s->ndim = 2;
+    s->dims[0] = K;
+    s->dims[1] = n;
+    s->byte_len = (size_t)(n * rb);
+    s->data = w->data + part * n * rb;
+    s->owns = false;
+    *out = s;
+    return HYQ_OK;
+  }
+  if (axis != 1) return fail(HYQ_E_INVALID, "shard: axis %d (0 = rows, 1 = input columns)", axis);
+  // Row-parallel: the same K range of every row, on block boundaries, gathered
+  // into a new [K / parts, N] buffer (packed bytes unchanged).
+  const int bl = hyq::block_len(w->dtype);
+  if (K % parts != 0 || (K / parts) % bl != 0)
+    return fail(HYQ_E_SHAPE, "shard: K=%lld does not split into %lld parts of whole %d-weight blocks", (long long)K,
+                (long long)parts, bl);
+  const int64_t k = K / parts;
+  const int64_t srb = row_bytes(w->dtype, k);
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, (size_t)((N * srb + 15) / 16 * 16 + 16));
+  if (e != cudaSuccess) return fail(HYQ_E_NOMEM, "shard: cudaMalloc: %s", cudaGetErrorString(e));
+  e = cudaMemcpy2DAsync(p, (size_t)srb, w->data + part * srb, (size_t)rb, (size_t)srb, (size_t)N,
+                        cudaMemcpyDeviceToDevice, (cudaStream_t)stream);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "shard: copy");
+  }
+  hyq_weight* s = new hyq_weight{};
+  s->dtype = w->dtype;
+  s->ndim = 2;
+  s->dims[0] = k;
+  s->dims[1] = N;
+  s->byte_len = (size_t)(N * srb);
+  s->data = static_cast<const uint8_t*>(p);
+  s->owns = true;
+  *out = s;
+  return HYQ_OK;
+}
+
 int hyq_weight_info(const hyq_weight* w, int* dtype, int* ndim, int64_t* dims, size_t* byte_len,
                     const void** device_ptr) {
   if (!w) return fail(HYQ_E_INVALID, "info: null weight");

@@ -67,6 +67,7 @@ struct Params {
   int wcol;             // K columns per packed block-column tile
   int wbox;             // bytes per row of that tile (TMA box inner size)
   int wbytes;           // packed bytes of one row per block column
+  int g;                // rows per 16-byte-aligned pitch of the weight tensor map (1, 2, 4 or 8)
   float* y;             // [M, N], or split-K partials [splits, M, N]
   unsigned* status;
 };
@@ -371,9 +372,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          const int x0 = (((kbeg + ks) / steps_per_w) * p.wbytes) & ~15;
+          // The tensor map sees g rows as one pitch (a multiple of 16 bytes):
+          // one load per row class j fetches rows row0 + j, + j + g, ...
+          const int64_t kb = (kbeg + ks) / steps_per_w;
           mbar_arrive_expect_tx(wfull(ws), (uint32_t)(BM * p.wbox));
-          tma_load_2d(base + L::w + ws * L::w_stage, &tmap_w, x0, row0, wfull(ws));
+          for (int j = 0; j < p.g; ++j) {
+            const int x0 = (int)(((int64_t)j * p.row_bytes + kb * p.wbytes) & ~int64_t(15));
+            tma_load_2d(base + L::w + ws * L::w_stage + j * (BM / p.g) * p.wbox, &tmap_w, x0, row0 / p.g,
+                        wfull(ws));
+          }
           ++issued_w;
         }
         const int s = ks % S;
@@ -441,8 +448,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();  // the MMAs that read this A stage are complete
-      const int skew = (((kbeg + ks) / steps_per_w) * p.wbytes) & 15;
-      const uint32_t rowp = base + L::w + ws * L::w_stage + r * p.wbox + skew;
+      // row r is row r / g of row class r % g; its bytes start `skew` into
+      // the 16-byte aligned window of that class
+      const int64_t kb = (kbeg + ks) / steps_per_w;
+      const int jc = r % p.g;
+      const int skew = (int)(((int64_t)jc * p.row_bytes + kb * p.wbytes) & 15);
+      const uint32_t rowp = base + L::w + ws * L::w_stage + (jc * (BM / p.g) + r / p.g) * p.wbox + skew;
       uint32_t o[32];
       decode64<FMT>(rowp, (kbeg + ks) % steps_per_w, o);
       tmem_st32(tmem + lane_base + (uint32_t)(BN + 32 * s), o);
@@ -528,10 +539,17 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 struct Geometry {
   int wcol, wbytes, wbox;
+  int rows;  // rows per 16-byte-aligned pitch: 16 / gcd(row_bytes, 16)
 };
 
-bool geometry(int dtype, int64_t K, int64_t row_bytes, Geometry& g) {
-  if (K % BK != 0 || row_bytes % 16 != 0) return false;
+// The weight tensor map needs a pitch that is a multiple of 16 bytes, so it
+// treats `rows` consecutive rows as one pitch (Q6_K rows of 28 blocks are
+// 5880 bytes: two rows per pitch).  N must be a multiple of it.
+bool geometry(int dtype, int64_t K, int64_t N, int64_t row_bytes, Geometry& g) {
+  if (K % BK != 0 || (row_bytes & 1)) return false;
+  const int r = (int)(row_bytes & 15);
+  g.rows = r == 0 ? 1 : (r % 8 == 0 ? 2 : (r % 4 == 0 ? 4 : 8));
+  if (N % g.rows != 0) return false;
   switch (dtype) {
     case Q4_K: g.wcol = 256; g.wbytes = 144; g.wbox = wbox_for(Q4_K); break;
     case Q6_K: g.wcol = 256; g.wbytes = 210; g.wbox = wbox_for(Q6_K); break;
@@ -595,7 +613,7 @@ int choose_splits(int64_t K, int64_t N, int64_t M, int wcol) {
 bool gemm_supported(int dtype, int64_t K, int64_t N, int64_t M, const void* w) {
   gemm::Geometry g;
   const int64_t row_bytes = K / block_len(dtype) * block_bytes(dtype);
-  if (!gemm::geometry(dtype, K, row_bytes, g)) return false;
+  if (!gemm::geometry(dtype, K, N, row_bytes, g)) return false;
   if ((reinterpret_cast<uintptr_t>(w) & 15) != 0) return false;
   if (N > INT32_MAX / 2 || M > INT32_MAX / 2) return false;
   return gemm::encode_fn() != nullptr;
@@ -604,7 +622,7 @@ bool gemm_supported(int dtype, int64_t K, int64_t N, int64_t M, const void* w) {
 size_t gemm_workspace_bytes(int dtype, int64_t K, int64_t N, int64_t M) {
   gemm::Geometry g;
   const int64_t row_bytes = K / block_len(dtype) * block_bytes(dtype);
-  if (!gemm::geometry(dtype, K, row_bytes, g)) return 0;
+  if (!gemm::geometry(dtype, K, N, row_bytes, g)) return 0;
   const int z = gemm::choose_splits(K, N, M, g.wcol);
   const size_t xb = ((size_t)(K * M) * sizeof(__half) + 255) / 256 * 256;
   return xb + (z > 1 ? (size_t)z * M * N * sizeof(float) : 0) + 16;
@@ -615,7 +633,7 @@ cudaError_t launch_gemm(int dtype, const uint8_t* w, int64_t K, int64_t N, const
   using namespace gemm;
   Geometry g;
   const int64_t row_bytes = K / block_len(dtype) * block_bytes(dtype);
-  if (!geometry(dtype, K, row_bytes, g)) return cudaErrorNotSupported;
+  if (!geometry(dtype, K, N, row_bytes, g)) return cudaErrorNotSupported;
   auto enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
   __half* xh = static_cast<__half*>(workspace);
@@ -632,9 +650,9 @@ cudaError_t launch_gemm(int dtype, const uint8_t* w, int64_t K, int64_t N, const
   const int bn = M >= 256 ? 256 : 128;
   CUtensorMap tw, tx;
   {
-    const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)N};
-    const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
-    const cuuint32_t box[2] = {(cuuint32_t)g.wbox, (cuuint32_t)BM};
+    const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes * g.rows), (cuuint64_t)(N / g.rows)};
+    const cuuint64_t strides[1] = {(cuuint64_t)(row_bytes * g.rows)};
+    const cuuint32_t box[2] = {(cuuint32_t)g.wbox, (cuuint32_t)(BM / g.rows)};
     const cuuint32_t es[2] = {1, 1};
     if (enc(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w), dims, strides, box, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -668,6 +686,7 @@ cudaError_t launch_gemm(int dtype, const uint8_t* w, int64_t K, int64_t N, const
   p.wcol = g.wcol;
   p.wbox = g.wbox;
   p.wbytes = g.wbytes;
+  p.g = g.rows;
   p.y = splits > 1 ? partials : y;
   p.status = status;
   cudaError_t e;

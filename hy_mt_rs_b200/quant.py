@@ -163,6 +163,17 @@ class Weight:
         check(lib.hyq_weight_expert(self._h, int(index), C.byref(h)))
         return Weight(self.packed, self.dtype, self._shape[:2], f"{self.name}[{index}]", _handle=h, _owner=self)
 
+    def shard(self, axis, part, parts):
+        """Tensor-parallel shard (hyq_weight_shard): axis 0 = output rows
+        (column-parallel, a view), axis 1 = input columns on block
+        boundaries (row-parallel, a gathered copy)."""
+        h = C.c_void_p()
+        check(lib.hyq_weight_shard(self._h, int(axis), int(part), int(parts), _stream(self.device()), C.byref(h)))
+        shape = ((self._shape[0], self._shape[1] // parts) if axis == 0 else
+                 (self._shape[0] // parts, self._shape[1]))
+        return Weight(self.packed if axis == 0 else None, self.dtype, shape,
+                      f"{self.name}[{axis}:{part}/{parts}]", _handle=h, _owner=self if axis == 0 else None)
+
     def row(self, row):
         """Weight::row (quant.rs:106-121)."""
         out = torch.empty(self._shape[0], dtype=torch.float32, device=self.device())

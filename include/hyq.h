@@ -85,6 +85,18 @@ int hyq_weight_wrap(const void* packed_device, size_t byte_len, int dtype, int n
  * weight [K, N, E] as a [K, N] matrix (byte offset index * byte_len / E). */
 int hyq_weight_expert(const hyq_weight* w, int64_t index, hyq_weight** out);
 
+/* Tensor-parallel shard of a [K, N] matrix (no counterpart in the CPU
+ * reference; the split SURVEY's dense TP plan uses for 7B layers).
+ *   axis 0 (column-parallel: QKV, gate/up, lm_head): output rows
+ *     [part*N/parts, (part+1)*N/parts), a view of the parent's bytes (the
+ *     parent must outlive it); N % parts == 0.
+ *   axis 1 (row-parallel: O, down): input columns [part*K/parts, ...) of every
+ *     row, on whole blocks, gathered into a new device buffer by one strided
+ *     copy ordered on `stream`; the partial products of all parts sum to the
+ *     full product.  K/parts must be a multiple of the block length
+ *     (HYQ_E_SHAPE otherwise, e.g. Q2_0C K=6144 at parts=8). */
+int hyq_weight_shard(const hyq_weight* w, int axis, int64_t part, int64_t parts, void* stream, hyq_weight** out);
+
 /* Shape/type/buffer of a handle (any output pointer may be NULL; dims needs 3). */
 int hyq_weight_info(const hyq_weight* w, int* dtype, int* ndim, int64_t* dims, size_t* byte_len,
                     const void** device_ptr);

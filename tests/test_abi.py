@@ -77,8 +77,39 @@ def test_weight_handle_validation():
     assert L.hyq_weight_info(e, None, C.byref(nd), dims, C.byref(nb), C.byref(ptr)) == 0
     assert nd.value == 2 and nb.value == 1024 * 1152 and ptr.value == 0x10000 + 5 * 1024 * 1152
     assert L.hyq_weight_expert(h3, 64, C.byref(e)) == -2
-    assert L.hyq_weight_expert(h, 0, C.byref(e)) in (-1, -2)
+    rc, h2 = _wrap(2, [2048, 6144], 6144 * 1152)
+    assert L.hyq_weight_expert(h2, 0, C.byref(e)) == -2  # a matrix has no experts
+    L.hyq_free(e)
+    L.hyq_free(h2)
     L.hyq_free(h3)
+
+
+def test_weight_shard_validation():
+    """hyq_weight_shard: row shards are views at the right byte offset; the
+    K split must fall on block boundaries (checked before any allocation)."""
+    from hy_mt_rs_b200 import _native
+
+    L = _native.lib
+    rc, h = _wrap(2, [4096, 14336], 14336 * 2304)  # Q4_K 14336x4096 (7B gate)
+    assert rc == 0
+    s = C.c_void_p()
+    dims = (C.c_int64 * 3)()
+    nb = C.c_size_t()
+    ptr = C.c_void_p()
+    assert L.hyq_weight_shard(h, 0, 3, 8, None, C.byref(s)) == 0
+    assert L.hyq_weight_info(s, None, None, dims, C.byref(nb), C.byref(ptr)) == 0
+    assert list(dims)[:2] == [4096, 1792] and nb.value == 1792 * 2304
+    assert ptr.value == 0x10000 + 3 * 1792 * 2304
+    L.hyq_free(s)
+    assert L.hyq_weight_shard(h, 0, 8, 8, None, C.byref(s)) == -1       # part out of range
+    assert L.hyq_weight_shard(h, 2, 0, 2, None, C.byref(s)) == -1       # no such axis
+    assert L.hyq_weight_shard(h, 0, 0, 5, None, C.byref(s)) == -2       # 14336 rows / 5
+    assert L.hyq_weight_shard(h, 1, 0, 32, None, C.byref(s)) == -2      # 4096/32 = 128 < one block
+    L.hyq_free(h)
+    rc, h = _wrap(5, [6144, 2048], 2048 * 12 * 130)  # Q2_0C down, K = 12 blocks of 512
+    assert L.hyq_weight_shard(h, 1, 0, 8, None, C.byref(s)) == -2       # 768 is not whole blocks
+    assert "whole 512-weight blocks" in _native.last_error()
+    L.hyq_free(h)
 
 
 def test_entry_points_reject_bad_shapes_before_launch():
