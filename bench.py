@@ -57,6 +57,8 @@ def args_parse():
                          "gemv: config 1 (one 6144x2048 product, L2 defeated by rotating copies)")
     ap.add_argument("--tp-mode", choices=["decode", "prefill"], default="decode",
                     help="tp: batch-1 layer chain (decode) or the layer's GEMMs at --tokens (prefill)")
+    ap.add_argument("--tp-allreduce", choices=["peer", "nccl"], default="peer",
+                    help="tp decode: all-reduce by hyq_peer_allreduce (NVLink peer memory) or NCCL")
     ap.add_argument("--sweep", action="store_true",
                     help="gemv: also measure every packed format at 6144x2048 and 120832x2048, both paths")
     ap.add_argument("--tokens", type=int, default=512, help="prefill: tokens M")
@@ -780,19 +782,36 @@ def tp_arm(a):
     quant.set_launch_overlap(a.tp_mode == "decode")
     H, F = 4096, 14336
     stream = torch.cuda.Stream(dev)
+    ar = None
     if a.tp_mode == "decode":
         M = 1
         x = torch.randn(H, generator=torch.Generator().manual_seed(1)).to(dev)
+        o = torch.empty(H, device=dev)
+        h = torch.empty(H, device=dev)
+        use_peer = world > 1 and a.tp_allreduce == "peer"
+        if use_peer:
+            from hy_mt_rs_b200.peer import PeerAllReduce
+            ar = PeerAllReduce(H, device=dev)
 
         def step():
             q, k, v = quant.Weight.gemv_qkv(sh["attn_q"], sh["attn_k"], sh["attn_v"], x)
-            o = sh["attn_output"].matmul(q, 1)[0]  # attention output stands in as q (same shard width)
-            if world > 1:
-                dist.all_reduce(o)
+            # attention output stands in as q (same shard width); the
+            # row-parallel partials go straight into the all-reduce buffer
+            if use_peer:
+                sh["attn_output"].matmul(q, 1, out=ar.partial)
+                ar.allreduce(o)
+            else:
+                sh["attn_output"].matmul(q, 1, out=o)
+                if world > 1:
+                    dist.all_reduce(o)
             g = sh["ffn_gate"].matmul_gate_up_silu(sh["ffn_up"], o)
-            h = sh["ffn_down"].matmul(g, 1)[0]
-            if world > 1:
-                dist.all_reduce(h)
+            if use_peer:
+                sh["ffn_down"].matmul(g, 1, out=ar.partial)
+                ar.allreduce(h)
+            else:
+                sh["ffn_down"].matmul(g, 1, out=h)
+                if world > 1:
+                    dist.all_reduce(h)
             return h
         flops = 2 * sum(N * K for _, N, K, _ in LAYER_7B)
     else:
@@ -839,6 +858,8 @@ def tp_arm(a):
         raise RuntimeError("a kernel reported an expired bounded wait (device status word) on some rank")
     ms = ms_total / a.steps
     del graph
+    if ar is not None:
+        ar.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -856,7 +877,8 @@ def tp_arm(a):
                  "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "data": "synthetic",
                  "config": {"workload": f"hy-mt-rs config 3 shapes, TP={world} ({a.tp_mode})", "tokens": M,
                             "parallelism": f"tp{world}: QKV, gate/up column-parallel; O, down row-parallel "
-                                           "+ NCCL all-reduce", "weight_bytes": wbytes}})
+                                           f"+ all-reduce ({'NCCL' if (a.tp_mode == 'prefill' or a.tp_allreduce == 'nccl') else 'hyq_peer_allreduce over NVLink peer memory'})",
+                            "weight_bytes": wbytes}})
     print(json.dumps(line), flush=True)
     return 0
 

@@ -69,6 +69,11 @@ _SIGS = {
     "hyq_matmul_gate_up_silu_int8": ([_wp, _wp, _vp, _vp, _vp], C.c_int),
     "hyq_matmul_noalloc": ([_wp, _vp, _i64, _vp, _vp], C.c_int),
     "hyq_set_launch_overlap": ([C.c_int], C.c_int),
+    "hyq_peer_alloc": ([C.c_size_t, C.POINTER(_vp), _vp], C.c_int),
+    "hyq_peer_open": ([_vp, C.POINTER(_vp)], C.c_int),
+    "hyq_peer_close": ([_vp], C.c_int),
+    "hyq_peer_free": ([_vp], C.c_int),
+    "hyq_peer_allreduce": ([C.POINTER(C.c_uint64), C.c_int, C.c_int, _i64, _vp, _vp], C.c_int),
     "hyq_device_status": ([_vp, C.POINTER(C.c_uint32)], C.c_int),
 }
 

@@ -35,6 +35,7 @@ enum : unsigned {
   DEV_TIMEOUT_EMPTY = 2u,  // producer gave up waiting for a stage to drain
   DEV_TIMEOUT_DRAIN = 4u,  // exit path gave up waiting for copies in flight
   DEV_BAD_ARGS = 8u,       // kernel saw arguments the host should have rejected
+  DEV_TIMEOUT_PEER = 16u,  // a peer all-reduce gave up waiting for another rank's flag
 };
 
 // Bound on any single wait (nanoseconds of %globaltimer).

@@ -193,14 +193,18 @@ class Weight:
         return out
 
     # ------------------------------------------------------- f32 products
-    def matmul(self, input, batch):
-        """Weight::matmul (quant.rs:159-344): [batch, K] x W^T -> [batch, N]."""
+    def matmul(self, input, batch, out=None):
+        """Weight::matmul (quant.rs:159-344): [batch, K] x W^T -> [batch, N]
+        (into `out`, batch * N float32 values, when given)."""
         if len(self._shape) != 2:
             raise HyqError(-2, f"{self.name} is not a matrix")
         _need_cuda(input, "matmul input", torch.float32)
         if batch <= 0 or input.numel() != batch * self._shape[0]:
             raise HyqError(-2, f"{self.name}: invalid activation shape")
-        out = torch.empty((batch, self._shape[1]), dtype=torch.float32, device=input.device)
+        if out is None:
+            out = torch.empty((batch, self._shape[1]), dtype=torch.float32, device=input.device)
+        elif out.numel() != batch * self._shape[1] or out.dtype != torch.float32:
+            raise HyqError(-2, f"{self.name}: invalid output buffer")
         check(lib.hyq_matmul(self._h, _ptr(input), int(batch), _ptr(out), _stream(input.device)))
         return out
 

@@ -56,6 +56,8 @@ typedef enum hyq_profile {
 #define HYQ_DEV_TIMEOUT_FULL 1u  /* a consumer gave up waiting for a tile copy */
 #define HYQ_DEV_TIMEOUT_EMPTY 2u /* a producer gave up waiting for a free stage */
 #define HYQ_DEV_TIMEOUT_DRAIN 4u /* exit path gave up waiting for copies in flight */
+#define HYQ_DEV_BAD_ARGS 8u      /* a kernel saw arguments the host should have rejected */
+#define HYQ_DEV_TIMEOUT_PEER 16u /* hyq_peer_allreduce gave up waiting for another rank */
 
 typedef struct hyq_weight hyq_weight;
 
@@ -198,6 +200,28 @@ int hyq_set_launch_overlap(int enable);
  *     the GPU (different streams, no ordering between them) race: keep them
  *     on one stream or order them with events. */
 int hyq_matmul_noalloc(const hyq_weight* w, const float* input, int64_t batch, float* out, void* stream);
+
+/* --- Tensor-parallel all-reduce over NVLink peer memory ------------------
+ * No counterpart in the reference (CPU only).  Sums the row-parallel partial
+ * products (O, down) of a tensor-parallel layer across the ranks of one node
+ * with plain peer loads and stores, no multicast.  Each rank owns a peer
+ * region: HYQ_PEER_DATA_OFFSET bytes of flags, then its partial product.
+ * hyq_peer_alloc: cudaMalloc a zeroed region for `data_bytes` of partials and
+ *   return its CUDA IPC handle (64 bytes) for the other ranks;
+ * hyq_peer_open / hyq_peer_close: map / unmap another rank's region;
+ * hyq_peer_allreduce: regions[q] = rank q's region as mapped in this process
+ *   (regions[rank] = the own one); out[0..n) = sum of the n partials at
+ *   region + HYQ_PEER_DATA_OFFSET over all ranks, in rank order (identical on
+ *   every rank).  Every rank makes the same sequence of calls; a call waits
+ *   (bounded, 5 s -> HYQ_DEV_TIMEOUT_PEER) for the other ranks' flags, so the
+ *   ranks' streams must all reach it.  At most 8 ranks; the partial may be
+ *   rewritten once the call has completed on the stream.  */
+#define HYQ_PEER_DATA_OFFSET 1024
+int hyq_peer_alloc(size_t data_bytes, void** region, void* ipc_handle);
+int hyq_peer_open(const void* ipc_handle, void** region);
+int hyq_peer_close(void* region);
+int hyq_peer_free(void* region);
+int hyq_peer_allreduce(const uint64_t* regions, int rank, int world, int64_t n, float* out, void* stream);
 
 /* Synchronize `stream`, then return (and clear) the device status word of
  * the current device: 0, or HYQ_DEV_* bits from kernels whose bounded waits
