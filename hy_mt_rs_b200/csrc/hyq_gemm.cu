@@ -37,6 +37,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "hyq_common.cuh"
@@ -508,6 +509,315 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// 2-SM variant: a cluster of two CTAs computes a 256-row x 256-token tile
+// with tcgen05.mma.cta_group::2 (M = 256, N = 256).  CTA rank r holds weight
+// rows [128 r, 128 r + 128) -- its own packed block columns, dequant warps
+// and TMEM lanes (A operand and accumulator) -- and tokens [128 r, 128 r +
+// 128) of the activation tile in its shared memory (half of the MMA's B).
+// Each SM therefore streams half the activation bytes of the 1-SM tile per
+// flop.  Rank 0 issues the MMAs; its barriers collect both CTAs' readiness:
+//   xfull[s]: armed by rank 0 for both halves; each CTA's TMA load completes
+//             its bytes on rank 0's barrier (cta_group::2 form, no multicast);
+//   afull[s]: 4 dequant warps of each CTA arrive (rank 1 remotely);
+//   empty[s], accfull: tcgen05.commit with a CTA mask arrives in both CTAs.
+// ---------------------------------------------------------------------------
+constexpr int kPairStages = 8;
+constexpr int kPairHalf = 128;  // tokens per CTA (half of the MMA's N)
+
+template <int FMT>
+struct Smem2 {
+  static constexpr int S = kPairStages;
+  static constexpr int x_tile = kPairHalf * 128;  // 128 tokens x 64 fp16
+  static constexpr int x = 0;
+  static constexpr int w = x + S * x_tile;
+  static constexpr int w_stage = (BM * wbox_for(FMT) + 1023) / 1024 * 1024;
+  static constexpr int bars = w + WS * w_stage;
+  static constexpr int n_bars = 3 * S + 2 * WS + 1;
+  static constexpr int misc = bars + 8 * n_bars;
+  static constexpr int total = misc + 16;
+};
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t local_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrive on the barrier at the same offset in CTA `rank` of the cluster.
+// The data it publishes (tensor-memory stores) is ordered by tcgen05.wait::st
+// and the tcgen05 thread-sync fences, so the arrive keeps the default
+// CTA-scope release and needs no cluster-wide fence.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t local_bar, uint32_t rank) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(map_to_rank(local_bar, rank)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// mbar_wait for barriers that receive arrivals from the other CTA.
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, const volatile int* abort) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (abort && *abort) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    }
+  }
+}
+
+// TMA load into this CTA's shared memory whose bytes complete on the barrier
+// of rank 0 (cluster address `bar0`).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar0) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar0)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_f16_ts_pair(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on the barrier at this offset in both CTAs once the issued MMAs end.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"((unsigned short)3)
+      : "memory");
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm2_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                 const __grid_constant__ Params p) {
+  using L = Smem2<FMT>;
+  constexpr int S = L::S;
+  constexpr int NACC = 2 * kPairHalf;  // accumulator columns (the pair's tokens)
+  static_assert(NACC + 32 * S <= kTmemCols, "accumulator and A stages exceed tensor memory");
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t raw_s = smem_addr(smem_raw);
+  const uint32_t base = (raw_s + 1023u) & ~1023u;
+  uint8_t* base_g = smem_raw + (base - raw_s);
+  const uint32_t bars = base + L::bars;
+  auto xfull = [&](int s) { return bars + 8 * s; };
+  auto afull = [&](int s) { return bars + 8 * (S + s); };
+  auto empty = [&](int s) { return bars + 8 * (2 * S + s); };
+  auto wfull = [&](int s) { return bars + 8 * (3 * S + s); };
+  auto wempty = [&](int s) { return bars + 8 * (3 * S + WS + s); };
+  const uint32_t accfull = bars + 8 * (3 * S + 2 * WS);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base_g + L::misc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(base_g + L::misc + 4);
+
+  const uint32_t crank = cluster_ctarank();
+  const bool leader = crank == 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = blockIdx.x * BM;  // this CTA's 128 rows (the pair covers 2 x 128)
+  const int tokp = blockIdx.y * NACC;  // the pair's first token
+  const int steps_per_w = p.wcol / BK;
+  const int kbeg = blockIdx.z * p.steps_per_split;
+  const int nk = min(p.steps_per_split, p.K / BK - kbeg);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(xfull(s), 1);
+      mbar_init(afull(s), 2 * kGroupWarps);
+      mbar_init(empty(s), 1);
+    }
+    for (int s = 0; s < WS; ++s) {
+      mbar_init(wfull(s), 1);
+      mbar_init(wempty(s), kDequantWarps);
+    }
+    mbar_init(accfull, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    // Both CTAs allocate, from the same warp, the same 512 columns.
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  tc_fence_before();
+  // barriers of both CTAs exist before any cross-CTA arrive or copy
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ----------------------------
+    if (lane == 0) {
+      int issued_x = 0, issued_w = 0;
+      bool ok = true;
+      for (int ks = 0; ks < nk && ok; ++ks) {
+        if (ks % steps_per_w == 0) {
+          const int wb = ks / steps_per_w, ws = wb % WS;
+          if (wb >= WS && !mbar_wait(wempty(ws), ((wb / WS) - 1) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const int64_t kb = (kbeg + ks) / steps_per_w;
+          mbar_arrive_expect_tx(wfull(ws), (uint32_t)(BM * p.wbox));
+          for (int j = 0; j < p.g; ++j) {
+            const int x0 = (int)(((int64_t)j * p.row_bytes + kb * p.wbytes) & ~int64_t(15));
+            tma_load_2d(base + L::w + ws * L::w_stage + j * (BM / p.g) * p.wbox, &tmap_w, x0, row0 / p.g,
+                        wfull(ws));
+          }
+          ++issued_w;
+        }
+        const int s = ks % S;
+        if (ks >= S && !mbar_wait(empty(s), ((ks / S) - 1) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        // rank 0 expects both halves; each CTA's copy completes there
+        if (leader) mbar_arrive_expect_tx(xfull(s), (uint32_t)(2 * L::x_tile));
+        tma_load_2d_pair(base + L::x + s * L::x_tile, &tmap_x, (kbeg + ks) * BK, tokp + kPairHalf * (int)crank,
+                         map_to_rank(xfull(s), 0));
+        ++issued_x;
+      }
+      if (!ok) {
+        atomicOr(p.status, DEV_TIMEOUT_EMPTY);
+        *abort_flag = 1;
+      }
+      // Drain.  Both CTAs' activation copies complete on rank 0's barriers,
+      // so rank 0 waits for them (the final cluster barrier keeps rank 1
+      // resident until then); each CTA waits for its own weight copies.
+      if (leader)
+        for (int k = (issued_x > S ? issued_x - S : 0); k < issued_x; ++k)
+          if (!mbar_wait_cluster(xfull(k % S), (k / S) & 1, nullptr)) atomicOr(p.status, DEV_TIMEOUT_DRAIN);
+      for (int k = (issued_w > WS ? issued_w - WS : 0); k < issued_w; ++k)
+        if (!mbar_wait(wfull(k % WS), (k / WS) & 1, nullptr)) atomicOr(p.status, DEV_TIMEOUT_DRAIN);
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer (rank 0) ---------------------
+    if (leader) {
+      // idesc: f32 accumulate, fp16 A and B, K-major, N = 256, M = 256.
+      const uint32_t idesc = (1u << 4) | ((uint32_t)(NACC >> 3) << 17) | ((uint32_t)((2 * BM) >> 4) << 24);
+      for (int ks = 0; ks < nk; ++ks) {
+        const int s = ks % S;
+        const uint32_t par = (ks / S) & 1;
+        if (!mbar_wait_cluster(afull(s), par, abort_flag) || !mbar_wait_cluster(xfull(s), par, abort_flag)) {
+          if (lane == 0) atomicOr(p.status, DEV_TIMEOUT_FULL);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a0 = tmem + (uint32_t)(NACC + 32 * s);
+          const uint32_t b0 = base + L::x + s * L::x_tile;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_f16_ts_pair(tmem, a0 + 8 * k, sw128_desc(b0 + 32 * k), idesc, (ks > 0 || k > 0) ? 1u : 0u);
+          umma_commit_pair(empty(s));
+        }
+        __syncwarp();
+      }
+      if (lane == 0) umma_commit_pair(accfull);
+      __syncwarp();
+    }
+  } else {
+    // --------------------------- dequant + epilogue ---------------------------
+    const int grp = (warp - 2) / kGroupWarps;
+    const int r = (warp & 3) * 32 + lane;  // weight row of this CTA's half = TMEM lane
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+    for (int ks = grp; ks < nk; ks += 2) {
+      const int wb = ks / steps_per_w, ws = wb % WS;
+      bool ok = true;
+      if (ks % steps_per_w == grp) ok = mbar_wait(wfull(ws), (wb / WS) & 1, abort_flag);
+      const int s = ks % S;
+      if (ok && ks >= S) ok = mbar_wait(empty(s), ((ks / S) - 1) & 1, abort_flag);
+      if (!ok) {
+        atomicOr(p.status, DEV_TIMEOUT_FULL);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int64_t kb = (kbeg + ks) / steps_per_w;
+      const int jc = r % p.g;
+      const int skew = (int)(((int64_t)jc * p.row_bytes + kb * p.wbytes) & 15);
+      const uint32_t rowp = base + L::w + ws * L::w_stage + (jc * (BM / p.g) + r / p.g) * p.wbox + skew;
+      uint32_t o[32];
+      decode64<FMT>(rowp, (kbeg + ks) % steps_per_w, o);
+      tmem_st32(tmem + lane_base + (uint32_t)(NACC + 32 * s), o);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive_cluster(afull(s), 0);
+        if (ks % steps_per_w >= steps_per_w - 2 || ks + 2 >= nk) mbar_arrive(wempty(ws));
+      }
+    }
+    if (warp < 6) {
+      const bool ok = mbar_wait(accfull, 0, nullptr);
+      tc_fence_after();
+      if (ok && !*abort_flag) {
+        const int q = warp & 3;
+        const int row = row0 + 32 * q + lane;
+        float* yz = p.y + (size_t)blockIdx.z * p.M * p.N;
+#pragma unroll 1
+        for (int c0 = 0; c0 < NACC; c0 += 16) {
+          uint32_t v[16];
+          asm volatile(
+              "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+              "%14, %15}, [%16];"
+              : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+                "=r"(v[15])
+              : "r"(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0));
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          if (row < p.N) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int tok = tokp + c0 + i;
+              if (tok < p.M) yz[(size_t)tok * p.N + row] = __uint_as_float(v[i]);
+            }
+          }
+        }
+      } else if (!ok) {
+        atomicOr(p.status, DEV_TIMEOUT_FULL);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  // Neither CTA leaves (or frees tensor memory) while the pair's MMAs may
+  // still read its shared memory or tensor memory.
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
 // fp16 copy of the activations for the TMA-fed operand, with every 64-column
 // step stored in k_perm order.  One thread per 2 output slots.
 template <int FMT>
@@ -556,6 +866,45 @@ bool geometry(int dtype, int64_t K, int64_t N, int64_t row_bytes, Geometry& g) {
     default: return false;
   }
   return K % g.wcol == 0;
+}
+
+template <int FMT>
+cudaError_t run_pair(const CUtensorMap& tw, const CUtensorMap& tx, const Params& p, int splits, cudaStream_t st) {
+  auto k = gemm2_kernel<FMT>;
+  static int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int smem = Smem2<FMT>::total + 1024;
+  if (configured_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    configured_dev = dev;
+  }
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(p.N / BM), (unsigned)((p.M + 2 * kPairHalf - 1) / (2 * kPairHalf)), (unsigned)splits);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, tw, tx, p);
+}
+
+// The 2-SM kernel serves tiles of 256 tokens when the rows pair up and the
+// process opted in (HYQ_GEMM_PAIR=1): measured on B200 it ties the 1-SM
+// kernel at 2048 tokens (gate 311 vs 309 us, down 376 vs 383 us) and trails
+// it at 512-1024 tokens, so the 1-SM kernel stays the default.
+bool use_pair(int64_t N, int64_t M) {
+  static const int enabled = [] {
+    const char* e = getenv("HYQ_GEMM_PAIR");
+    return (e && e[0] == '1') ? 1 : 0;
+  }();
+  return enabled && M >= 256 && N % (2 * BM) == 0;
 }
 
 template <int FMT, int BN>
@@ -662,7 +1011,7 @@ cudaError_t launch_gemm(int dtype, const uint8_t* w, int64_t K, int64_t N, const
   {
     const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
     const cuuint64_t strides[1] = {(cuuint64_t)(K * 2)};
-    const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)bn};
+    const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)(use_pair(N, M) ? kPairHalf : bn)};
     const cuuint32_t es[2] = {1, 1};
     if (enc(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xh, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
@@ -690,10 +1039,14 @@ cudaError_t launch_gemm(int dtype, const uint8_t* w, int64_t K, int64_t N, const
   p.y = splits > 1 ? partials : y;
   p.status = status;
   cudaError_t e;
-  switch (dtype) {
-    case Q4_K: e = bn == 256 ? run<Q4_K, 256>(tw, tx, p, st) : run<Q4_K, 128>(tw, tx, p, st); break;
-    case Q6_K: e = bn == 256 ? run<Q6_K, 256>(tw, tx, p, st) : run<Q6_K, 128>(tw, tx, p, st); break;
-    default: return cudaErrorNotSupported;
+  if (use_pair(N, M)) {
+    e = dtype == Q4_K ? run_pair<Q4_K>(tw, tx, p, splits, st) : run_pair<Q6_K>(tw, tx, p, splits, st);
+  } else {
+    switch (dtype) {
+      case Q4_K: e = bn == 256 ? run<Q4_K, 256>(tw, tx, p, st) : run<Q4_K, 128>(tw, tx, p, st); break;
+      case Q6_K: e = bn == 256 ? run<Q6_K, 256>(tw, tx, p, st) : run<Q6_K, 128>(tw, tx, p, st); break;
+      default: return cudaErrorNotSupported;
+    }
   }
   if (e != cudaSuccess || splits == 1) return e;
   const int64_t n = M * N;

@@ -47,6 +47,31 @@ def test_gemm_7b_shapes(cuda, t, N, K, M):
     run_case(cuda, t, N, K, M, seed=7)
 
 
+# 2-SM tiles (256 rows x 256 tokens per CTA pair): N a multiple of 256 and at
+# least 256 tokens; a partial last token tile, a 2-row pitch (Q6_K, 4 blocks)
+# and split-K slices of pairs.
+PAIR_CASES = [(Q4_K, 512, 1024, 256), (Q6_K, 768, 1024, 300), (Q6_K, 2048, 7168, 512), (Q4_K, 1024, 4096, 1000)]
+
+
+def test_gemm_pair_tiles(cuda):
+    """The opt-in 2-SM kernel (HYQ_GEMM_PAIR=1 is read once per process, so
+    the cases run in a child process)."""
+    import os
+    import subprocess
+    import sys
+
+    from conftest import ROOT
+
+    code = ("import sys; sys.path.insert(0, %r); sys.path.insert(0, %r)\n"
+            "import test_gpu_gemm as T, torch\n"
+            "dev = torch.device('cuda', 0)\n"
+            "for c in T.PAIR_CASES: T.run_case(dev, *c, seed=c[1] + c[3])\n"
+            "print('ok')\n") % (ROOT, os.path.join(ROOT, "tests"))
+    env = dict(os.environ, HYQ_GEMM_PAIR="1")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-3000:]
+
+
 def test_gemm_matches_gemv_path(cuda):
     """Batch 16 (tensor cores) and batch-1 rows agree to fp16-operand accuracy."""
     import torch
