@@ -60,6 +60,8 @@ _SIGS = {
     "hyq_matmul": ([_wp, _vp, _i64, _vp, _vp], C.c_int),
     "hyq_gemv_qkv": ([_wp, _wp, _wp, _vp, _vp, _vp, _vp, _vp], C.c_int),
     "hyq_matmul_gate_up_silu": ([_wp, _wp, _vp, _vp, _vp], C.c_int),
+    "hyq_matmul_qkv": ([_wp, _wp, _wp, _vp, _i64, _vp, _vp, _vp, _vp], C.c_int),
+    "hyq_matmul_gate_up_silu_batch": ([_wp, _wp, _vp, _i64, _vp, _vp], C.c_int),
     "hyq_q8_quantize": ([_vp, _i64, _vp, _vp, _vp, _vp], C.c_int),
     "hyq_gemv_q8": ([_wp, _vp, _vp, _vp, _vp, _vp], C.c_int),
     "hyq_gemv_qkv_q8": ([_wp, _wp, _wp, _vp, _vp, _vp, _vp, _vp, _vp, _vp], C.c_int),

@@ -450,6 +450,93 @@ int hyq_matmul_gate_up_silu(const hyq_weight* gate, const hyq_weight* up, const 
   return run_gemv(1, &gate, &out, up, a, (cudaStream_t)stream, "gate_up_silu");
 }
 
+// A grouped tensor-core product with a stream-ordered workspace.
+static int run_gemm_job(const hyq::GemmJob& j, cudaStream_t st, const char* name) {
+  unsigned* status = nullptr;
+  int rc = status_ptr(&status);
+  if (rc) return rc;
+  hyq::GemmJob jj = j;
+  jj.status = status;
+  void* ws = nullptr;
+  ensure_pool();
+  cudaError_t e = cudaMallocAsync(&ws, hyq::gemm_job_workspace_bytes(jj), st);
+  if (e != cudaSuccess) return fail(HYQ_E_NOMEM, "%s workspace: %s", name, cudaGetErrorString(e));
+  e = hyq::launch_gemm_job(jj, ws, st);
+  const cudaError_t e2 = cudaFreeAsync(ws, st);
+  if (e != cudaSuccess) return cuda_fail(e, name);
+  if (e2 != cudaSuccess) return cuda_fail(e2, name);
+  return HYQ_OK;
+}
+
+int hyq_matmul_qkv(const hyq_weight* q, const hyq_weight* k, const hyq_weight* v, const float* input, int64_t batch,
+                   float* q_out, float* k_out, float* v_out, void* stream) {
+  int rc = qkv_checks(q, k, v);
+  if (rc) return rc;
+  if (batch <= 0) return fail(HYQ_E_SHAPE, "invalid activation shape");
+  if (!input || !q_out || !k_out || !v_out) return fail(HYQ_E_INVALID, "matmul_qkv: null pointer");
+  Act a;
+  a.x = input;
+  if ((rc = check_act(a, "matmul_qkv"))) return rc;
+  const int64_t K = q->dims[0];
+  cudaStream_t st = (cudaStream_t)stream;
+  hyq::GemmJob j;
+  j.dtype = q->dtype;
+  j.n_mat = 3;
+  const hyq_weight* ws[3] = {q, k, v};
+  float* ys[3] = {q_out, k_out, v_out};
+  for (int m = 0; m < 3; ++m) {
+    j.w[m] = ws[m]->data;
+    j.rows[m] = ws[m]->dims[1];
+    j.y[m] = ys[m];
+  }
+  j.K = K;
+  j.M = batch;
+  j.x = input;
+  if (batch >= kGemmMinBatch && k->dtype == q->dtype && v->dtype == q->dtype && aligned(input, 16) &&
+      hyq::gemm_job_supported(j))
+    return run_gemm_job(j, st, "matmul_qkv (tensor-core GEMM)");
+  for (int64_t b = 0; b < batch; ++b) {
+    Act ab;
+    ab.x = input + b * K;
+    if ((rc = qkv_run(q, k, v, ab, q_out + b * q->dims[1], k_out + b * k->dims[1], v_out + b * v->dims[1], st)))
+      return rc;
+  }
+  return HYQ_OK;
+}
+
+int hyq_matmul_gate_up_silu_batch(const hyq_weight* gate, const hyq_weight* up, const float* input, int64_t batch,
+                                  float* out, void* stream) {
+  int rc = gate_up_checks(gate, up);
+  if (rc) return rc;
+  if (batch <= 0) return fail(HYQ_E_SHAPE, "invalid activation shape");
+  if (!input || !out) return fail(HYQ_E_INVALID, "gate_up_silu_batch: null pointer");
+  Act a;
+  a.x = input;
+  if ((rc = check_act(a, "gate_up_silu_batch"))) return rc;
+  const int64_t K = gate->dims[0], N = gate->dims[1];
+  cudaStream_t st = (cudaStream_t)stream;
+  hyq::GemmJob j;
+  j.dtype = gate->dtype;
+  j.n_mat = 2;
+  j.gate_up = true;
+  j.w[0] = gate->data;
+  j.w[1] = up->data;
+  j.rows[0] = j.rows[1] = N;
+  j.y[0] = out;
+  j.K = K;
+  j.M = batch;
+  j.x = input;
+  if (batch >= kGemmMinBatch && aligned(input, 16) && hyq::gemm_job_supported(j))
+    return run_gemm_job(j, st, "gate_up_silu_batch (tensor-core GEMM)");
+  for (int64_t b = 0; b < batch; ++b) {
+    Act ab;
+    ab.x = input + b * K;
+    float* y = out + b * N;
+    if ((rc = run_gemv(1, &gate, &y, up, ab, st, "gate_up_silu_batch"))) return rc;
+  }
+  return HYQ_OK;
+}
+
 int hyq_q8_quantize(const float* input, int64_t len, int8_t* values, float* scales, int8_t* values_q2c,
                     void* stream) {
   if (len < 0) return fail(HYQ_E_SHAPE, "q8: negative length");

@@ -69,8 +69,21 @@ struct Params {
   int wbox;             // bytes per row of that tile (TMA box inner size)
   int wbytes;           // packed bytes of one row per block column
   int g;                // rows per 16-byte-aligned pitch of the weight tensor map (1, 2, 4 or 8)
-  float* y;             // [M, N], or split-K partials [splits, M, N]
+  float* y;             // split-K partials [splits, M, N] (N = all matrices' columns), or unused
   unsigned* status;
+  // Matrices sharing the activations (QKV): row tile t belongs to matrix m
+  // for seg_tile0[m] <= t < seg_tile0[m + 1]; its output is ys[m] [M,
+  // seg_rows[m]], or columns seg_col0[m].. of the split-K partials.
+  int n_seg;
+  int seg_tile0[4];
+  int seg_rows[3];
+  int seg_col0[3];
+  float* ys[3];
+  // Gate/up pair (matmul_gate_up_silu): a 128-row tile holds 64 gate and the
+  // same 64 up rows, interleaved by 16 in each 32-lane TMEM quarter; the
+  // output is silu(gate x) * (up x) in ys[0] [M, seg_rows[0]] (split-K:
+  // gate partials in columns 0.., up partials in columns seg_rows[0]..).
+  int gate_up;
 };
 
 template <int FMT, int BN>
@@ -307,7 +320,8 @@ __device__ __forceinline__ void decode64(uint32_t row, int j4, uint32_t (&o)[32]
 
 template <int FMT, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+    gemm_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_constant__ CUtensorMap tmap_w1,
+                const __grid_constant__ CUtensorMap tmap_w2, const __grid_constant__ CUtensorMap tmap_x,
                 const __grid_constant__ Params p) {
   using L = Smem<FMT, BN>;
   constexpr int S = L::S;
@@ -328,7 +342,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base_g + L::misc + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row0 = blockIdx.x * BM, tok0 = blockIdx.y * BN;
+  const int tok0 = blockIdx.y * BN;
+  // row tile -> matrix and its first row (a gate/up tile covers 64 rows of each)
+  int seg = 0;
+  while (seg + 1 < p.n_seg && (int)blockIdx.x >= p.seg_tile0[seg + 1]) ++seg;
+  const int tile_rows = p.gate_up ? BM / 2 : BM;
+  const int row0 = ((int)blockIdx.x - p.seg_tile0[seg]) * tile_rows;
   const int steps_per_w = p.wcol / BK;
   // split-K slice of this CTA: K steps [kbeg, kbeg + nk)
   const int kbeg = blockIdx.z * p.steps_per_split;
@@ -374,13 +393,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           // The tensor map sees g rows as one pitch (a multiple of 16 bytes):
-          // one load per row class j fetches rows row0 + j, + j + g, ...
+          // one load per row class j fetches rows row0 + j, + j + g, ...;
+          // a gate/up tile loads 64 rows of each matrix.
           const int64_t kb = (kbeg + ks) / steps_per_w;
+          const CUtensorMap* maps[3] = {&tmap_w0, &tmap_w1, &tmap_w2};
           mbar_arrive_expect_tx(wfull(ws), (uint32_t)(BM * p.wbox));
-          for (int j = 0; j < p.g; ++j) {
-            const int x0 = (int)(((int64_t)j * p.row_bytes + kb * p.wbytes) & ~int64_t(15));
-            tma_load_2d(base + L::w + ws * L::w_stage + j * (BM / p.g) * p.wbox, &tmap_w, x0, row0 / p.g,
-                        wfull(ws));
+          for (int mt = 0; mt < (p.gate_up ? 2 : 1); ++mt) {
+            const CUtensorMap* map = maps[p.gate_up ? mt : seg];
+            for (int j = 0; j < p.g; ++j) {
+              const int x0 = (int)(((int64_t)j * p.row_bytes + kb * p.wbytes) & ~int64_t(15));
+              tma_load_2d(base + L::w + ws * L::w_stage + (mt * tile_rows + j * (tile_rows / p.g)) * p.wbox, map,
+                          x0, row0 / p.g, wfull(ws));
+            }
           }
           ++issued_w;
         }
@@ -449,12 +473,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();  // the MMAs that read this A stage are complete
-      // row r is row r / g of row class r % g; its bytes start `skew` into
-      // the 16-byte aligned window of that class
+      // TMEM lane r holds row rl of matrix mt (gate/up: lanes 16..31 of each
+      // quarter are the up rows); that row is row rl / g of row class rl % g
+      // in shared memory, its bytes `skew` into the class's aligned window.
       const int64_t kb = (kbeg + ks) / steps_per_w;
-      const int jc = r % p.g;
+      const int mt = p.gate_up ? ((r & 31) >> 4) : 0;
+      const int rl = p.gate_up ? 16 * (r >> 5) + (r & 15) : r;
+      const int jc = rl % p.g;
       const int skew = (int)(((int64_t)jc * p.row_bytes + kb * p.wbytes) & 15);
-      const uint32_t rowp = base + L::w + ws * L::w_stage + (jc * (BM / p.g) + r / p.g) * p.wbox + skew;
+      const uint32_t rowp =
+          base + L::w + ws * L::w_stage + (mt * tile_rows + jc * (tile_rows / p.g) + rl / p.g) * p.wbox + skew;
       uint32_t o[32];
       decode64<FMT>(rowp, (kbeg + ks) % steps_per_w, o);
       tmem_st32(tmem + lane_base + (uint32_t)(BN + 32 * s), o);
@@ -469,15 +497,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ks % steps_per_w >= steps_per_w - 2 || ks + 2 >= nk) mbar_arrive(wempty(ws));
       }
     }
-    // Epilogue: warps 2..5 own TMEM lanes 32*(warp%4) .. +31.
-    if (warp < 6) {
+    // Epilogue: all 8 dequant warps; warp w reads TMEM lanes 32*(w%4) ..
+    // +31, warps 2-5 the first half of the accumulator columns, warps 6-9
+    // the second.
+    {
       const bool ok = mbar_wait(accfull, 0, nullptr);
       tc_fence_after();
       if (ok && !*abort_flag) {
         const int q = warp & 3;
-        const int row = row0 + 32 * q + lane;
+        const int cbeg = (warp < 6) ? 0 : BN / 2;
+        const bool split = p.y != nullptr;
+        const int rows_m = p.seg_rows[seg];
+        float* yz = split ? p.y + (size_t)blockIdx.z * p.M * p.N : nullptr;
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 16) {
+        for (int c0 = cbeg; c0 < cbeg + BN / 2; c0 += 16) {
           uint32_t v[16];
           asm volatile(
               "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
@@ -487,12 +520,38 @@ __global__ void __launch_bounds__(kThreads, 1)
                 "=r"(v[15])
               : "r"(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0));
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-          if (row < p.N) {
-            float* yz = p.y + (size_t)blockIdx.z * p.M * p.N;
+          if (!p.gate_up) {
+            const int row = row0 + 32 * q + lane;
+            if (row < rows_m) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int tok = tok0 + c0 + i;
-              if (tok < p.M) yz[(size_t)tok * p.N + row] = __uint_as_float(v[i]);
+              for (int i = 0; i < 16; ++i) {
+                const int tok = tok0 + c0 + i;
+                if (tok >= p.M) continue;
+                if (split) yz[(size_t)tok * p.N + p.seg_col0[seg] + row] = __uint_as_float(v[i]);
+                else p.ys[seg][(size_t)tok * rows_m + row] = __uint_as_float(v[i]);
+              }
+            }
+          } else {
+            // lanes 0..15: gate rows, lanes 16..31: the same up rows
+            const int hi = lane >> 4;
+            const int row = row0 + 16 * q + (lane & 15);
+            float u[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) u[i] = __shfl_down_sync(0xffffffffu, __uint_as_float(v[i]), 16);
+            if (row < rows_m) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const int tok = tok0 + c0 + i;
+                if (tok >= p.M) continue;
+                if (split) {
+                  yz[(size_t)tok * p.N + hi * rows_m + row] = __uint_as_float(v[i]);
+                } else if (!hi) {
+                  // silu(g) * u = g / (1 + e^-g) * u (quant.rs:573-574), with
+                  // the fast exponential and division: the operands are fp16
+                  const float g = __uint_as_float(v[i]);
+                  p.ys[0][(size_t)tok * rows_m + row] = __fdividef(g, 1.0f + __expf(-g)) * u[i];
+                }
+              }
             }
           }
         }
@@ -908,7 +967,8 @@ bool use_pair(int64_t N, int64_t M) {
 }
 
 template <int FMT, int BN>
-cudaError_t run(const CUtensorMap& tw, const CUtensorMap& tx, const Params& p, cudaStream_t st) {
+cudaError_t run(const CUtensorMap* tw, const CUtensorMap& tx, const Params& p, int tiles, int splits,
+                cudaStream_t st) {
   auto k = gemm_kernel<FMT, BN>;
   static int configured_dev = -1;
   int dev = 0;
@@ -919,20 +979,45 @@ cudaError_t run(const CUtensorMap& tw, const CUtensorMap& tx, const Params& p, c
     if (e != cudaSuccess) return e;
     configured_dev = dev;
   }
-  const int splits = (p.K / BK + p.steps_per_split - 1) / p.steps_per_split;
-  dim3 grid((unsigned)((p.N + BM - 1) / BM), (unsigned)((p.M + BN - 1) / BN), (unsigned)splits);
-  k<<<grid, kThreads, smem, st>>>(tw, tx, p);
+  dim3 grid((unsigned)tiles, (unsigned)((p.M + BN - 1) / BN), (unsigned)splits);
+  k<<<grid, kThreads, smem, st>>>(tw[0], tw[1], tw[2], tx, p);
   return cudaGetLastError();
 }
 
-// y = sum over split-K slices of the partials, in slice order.
-__global__ void __launch_bounds__(256) reduce_splits_kernel(const float* __restrict__ part, float* __restrict__ y,
-                                                             int64_t n, int splits) {
+// Sum of the split-K partials in slice order, written to the matrices'
+// outputs (gate/up: silu(sum gate) * sum up).
+struct ReduceArgs {
+  const float* part;
+  int64_t M;
+  int N;  // partial columns
+  int splits;
+  int gate_up;
+  int n_seg;
+  int seg_col0[3];
+  int seg_rows[3];
+  float* ys[3];
+};
+
+__global__ void __launch_bounds__(256) reduce_splits_kernel(const __grid_constant__ ReduceArgs a) {
+  const int cols = a.gate_up ? a.seg_rows[0] : a.N;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  float s = part[i];
-  for (int z = 1; z < splits; ++z) s += part[(int64_t)z * n + i];
-  y[i] = s;
+  if (i >= a.M * cols) return;
+  const int64_t tok = i / cols;
+  const int c = (int)(i - tok * cols);
+  const int64_t n = a.M * a.N;
+  const float* src = a.part + tok * a.N + c;
+  float s = src[0];
+  for (int z = 1; z < a.splits; ++z) s += src[(int64_t)z * n];
+  if (a.gate_up) {
+    const float* su = src + a.seg_rows[0];
+    float u = su[0];
+    for (int z = 1; z < a.splits; ++z) u += su[(int64_t)z * n];
+    a.ys[0][tok * a.seg_rows[0] + c] = __fdividef(s, 1.0f + __expf(-s)) * u;  // as in the GEMM epilogue
+    return;
+  }
+  int m = 0;
+  while (m + 1 < a.n_seg && c >= a.seg_col0[m + 1]) ++m;
+  a.ys[m][tok * a.seg_rows[m] + (c - a.seg_col0[m])] = s;
 }
 
 int device_sms() {
@@ -945,9 +1030,9 @@ int device_sms() {
 }
 
 // Split-K slices (in block columns) so that small grids still fill the GPU.
-int choose_splits(int64_t K, int64_t N, int64_t M, int wcol) {
+int choose_splits(int64_t K, int64_t row_tiles, int64_t M, int wcol) {
   const int64_t bn = M >= 256 ? 256 : 128;
-  const int64_t tiles = ((N + BM - 1) / BM) * ((M + bn - 1) / bn);
+  const int64_t tiles = row_tiles * ((M + bn - 1) / bn);
   const int64_t nwb = K / wcol;
   const int64_t sms = device_sms();
   if (tiles >= sms) return 1;
@@ -957,53 +1042,96 @@ int choose_splits(int64_t K, int64_t N, int64_t M, int wcol) {
   return (int)(z < 1 ? 1 : z);
 }
 
+// Row tiles of a job and the columns of its split-K partials.
+struct Layout {
+  int tiles = 0;
+  int tile0[4] = {};
+  int col0[3] = {};
+  int ncols = 0;
+};
+
+Layout layout_of(const GemmJob& j) {
+  Layout L;
+  if (j.gate_up) {
+    L.tiles = (int)((j.rows[0] + BM / 2 - 1) / (BM / 2));
+    L.tile0[1] = L.tiles;
+    L.ncols = (int)(2 * j.rows[0]);
+    return L;
+  }
+  for (int m = 0; m < j.n_mat; ++m) {
+    L.tile0[m] = L.tiles;
+    L.col0[m] = L.ncols;
+    L.tiles += (int)((j.rows[m] + BM - 1) / BM);
+    L.ncols += (int)j.rows[m];
+  }
+  L.tile0[j.n_mat] = L.tiles;
+  return L;
+}
+
+// The shared tile geometry of a job's matrices, or false when the tensor-core
+// path does not take it.
+bool job_geometry(const GemmJob& j, Geometry& g) {
+  if (j.gate_up ? j.n_mat != 2 : (j.n_mat < 1 || j.n_mat > 3)) return false;
+  if (j.gate_up && j.rows[0] != j.rows[1]) return false;
+  const int64_t row_bytes = j.K / block_len(j.dtype) * block_bytes(j.dtype);
+  for (int m = 0; m < j.n_mat; ++m) {
+    if (!geometry(j.dtype, j.K, j.rows[m], row_bytes, g)) return false;
+    if (j.rows[m] > INT32_MAX / 4) return false;
+  }
+  return j.M <= INT32_MAX / 2;
+}
+
+size_t x_bytes(int64_t K, int64_t M) { return ((size_t)(K * M) * sizeof(__half) + 255) / 256 * 256; }
+
 }  // namespace gemm
 
-bool gemm_supported(int dtype, int64_t K, int64_t N, int64_t M, const void* w) {
+bool gemm_job_supported(const GemmJob& j) {
   gemm::Geometry g;
-  const int64_t row_bytes = K / block_len(dtype) * block_bytes(dtype);
-  if (!gemm::geometry(dtype, K, N, row_bytes, g)) return false;
-  if ((reinterpret_cast<uintptr_t>(w) & 15) != 0) return false;
-  if (N > INT32_MAX / 2 || M > INT32_MAX / 2) return false;
+  if (!gemm::job_geometry(j, g)) return false;
+  for (int m = 0; m < j.n_mat; ++m)
+    if (!j.w[m] || (reinterpret_cast<uintptr_t>(j.w[m]) & 15) != 0) return false;
   return gemm::encode_fn() != nullptr;
 }
 
-size_t gemm_workspace_bytes(int dtype, int64_t K, int64_t N, int64_t M) {
+size_t gemm_job_workspace_bytes(const GemmJob& j) {
   gemm::Geometry g;
-  const int64_t row_bytes = K / block_len(dtype) * block_bytes(dtype);
-  if (!gemm::geometry(dtype, K, N, row_bytes, g)) return 0;
-  const int z = gemm::choose_splits(K, N, M, g.wcol);
-  const size_t xb = ((size_t)(K * M) * sizeof(__half) + 255) / 256 * 256;
-  return xb + (z > 1 ? (size_t)z * M * N * sizeof(float) : 0) + 16;
+  if (!gemm::job_geometry(j, g)) return 0;
+  const gemm::Layout L = gemm::layout_of(j);
+  const int z = gemm::choose_splits(j.K, L.tiles, j.M, g.wcol);
+  return gemm::x_bytes(j.K, j.M) + (z > 1 ? (size_t)z * j.M * L.ncols * sizeof(float) : 0) + 16;
 }
 
-cudaError_t launch_gemm(int dtype, const uint8_t* w, int64_t K, int64_t N, const float* x, int64_t M, float* y,
-                        void* workspace, unsigned* status, cudaStream_t st) {
+cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) {
   using namespace gemm;
   Geometry g;
-  const int64_t row_bytes = K / block_len(dtype) * block_bytes(dtype);
-  if (!geometry(dtype, K, N, row_bytes, g)) return cudaErrorNotSupported;
+  if (!job_geometry(j, g)) return cudaErrorNotSupported;
   auto enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
+  const int64_t K = j.K, M = j.M;
+  const int64_t row_bytes = K / block_len(j.dtype) * block_bytes(j.dtype);
+  const Layout lay = layout_of(j);
+  const bool pair = !j.gate_up && j.n_mat == 1 && use_pair(j.rows[0], M);
   __half* xh = static_cast<__half*>(workspace);
   {
     const int64_t pairs = K * M / 2;
     const unsigned blocks = (unsigned)((pairs + 255) / 256);
-    if (dtype == Q4_K)
-      to_half_kernel<Q4_K><<<blocks, 256, 0, st>>>(x, reinterpret_cast<__half2*>(xh), K, pairs);
+    if (j.dtype == Q4_K)
+      to_half_kernel<Q4_K><<<blocks, 256, 0, st>>>(j.x, reinterpret_cast<__half2*>(xh), K, pairs);
     else
-      to_half_kernel<Q6_K><<<blocks, 256, 0, st>>>(x, reinterpret_cast<__half2*>(xh), K, pairs);
+      to_half_kernel<Q6_K><<<blocks, 256, 0, st>>>(j.x, reinterpret_cast<__half2*>(xh), K, pairs);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
   const int bn = M >= 256 ? 256 : 128;
-  CUtensorMap tw, tx;
-  {
-    const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes * g.rows), (cuuint64_t)(N / g.rows)};
+  const int tile_rows = j.gate_up ? BM / 2 : BM;
+  CUtensorMap tw[3], tx;
+  for (int m = 0; m < 3; ++m) {
+    const int mm = m < j.n_mat ? m : 0;  // unused maps repeat the first
+    const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes * g.rows), (cuuint64_t)(j.rows[mm] / g.rows)};
     const cuuint64_t strides[1] = {(cuuint64_t)(row_bytes * g.rows)};
-    const cuuint32_t box[2] = {(cuuint32_t)g.wbox, (cuuint32_t)(BM / g.rows)};
+    const cuuint32_t box[2] = {(cuuint32_t)g.wbox, (cuuint32_t)(tile_rows / g.rows)};
     const cuuint32_t es[2] = {1, 1};
-    if (enc(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w), dims, strides, box, es,
+    if (enc(&tw[m], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(j.w[mm]), dims, strides, box, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
@@ -1011,7 +1139,7 @@ cudaError_t launch_gemm(int dtype, const uint8_t* w, int64_t K, int64_t N, const
   {
     const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
     const cuuint64_t strides[1] = {(cuuint64_t)(K * 2)};
-    const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)(use_pair(N, M) ? kPairHalf : bn)};
+    const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)(pair ? kPairHalf : bn)};
     const cuuint32_t es[2] = {1, 1};
     if (enc(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xh, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
@@ -1019,16 +1147,15 @@ cudaError_t launch_gemm(int dtype, const uint8_t* w, int64_t K, int64_t N, const
       return cudaErrorInvalidValue;
   }
   const int nwb = (int)(K / g.wcol);
-  const int wb_per_split = (nwb + choose_splits(K, N, M, g.wcol) - 1) / choose_splits(K, N, M, g.wcol);
+  const int z = choose_splits(K, lay.tiles, M, g.wcol);
+  const int wb_per_split = (nwb + z - 1) / z;
   // slices actually launched (rounding to whole block columns can drop some)
   const int splits = (nwb + wb_per_split - 1) / wb_per_split;
-  float* partials = nullptr;
-  if (splits > 1)
-    partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
-                                        ((size_t)(K * M) * sizeof(__half) + 255) / 256 * 256);
-  Params p;
+  float* partials =
+      splits > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + x_bytes(K, M)) : nullptr;
+  Params p{};
   p.K = (int)K;
-  p.N = (int)N;
+  p.N = lay.ncols;
   p.M = (int)M;
   p.steps_per_split = wb_per_split * (g.wcol / BK);
   p.row_bytes = (int)row_bytes;
@@ -1036,22 +1163,73 @@ cudaError_t launch_gemm(int dtype, const uint8_t* w, int64_t K, int64_t N, const
   p.wbox = g.wbox;
   p.wbytes = g.wbytes;
   p.g = g.rows;
-  p.y = splits > 1 ? partials : y;
-  p.status = status;
+  p.y = partials;
+  p.status = j.status;
+  p.n_seg = j.gate_up ? 1 : j.n_mat;
+  for (int m = 0; m < 4; ++m) p.seg_tile0[m] = lay.tile0[m];
+  for (int m = 0; m < 3; ++m) {
+    p.seg_rows[m] = m < j.n_mat ? (int)j.rows[m] : 0;
+    p.seg_col0[m] = lay.col0[m];
+    p.ys[m] = m < j.n_mat ? j.y[m] : nullptr;
+  }
+  p.gate_up = j.gate_up ? 1 : 0;
   cudaError_t e;
-  if (use_pair(N, M)) {
-    e = dtype == Q4_K ? run_pair<Q4_K>(tw, tx, p, splits, st) : run_pair<Q6_K>(tw, tx, p, splits, st);
+  if (pair) {
+    p.N = (int)j.rows[0];
+    p.y = splits > 1 ? partials : j.y[0];
+    e = j.dtype == Q4_K ? run_pair<Q4_K>(tw[0], tx, p, splits, st) : run_pair<Q6_K>(tw[0], tx, p, splits, st);
+  } else if (j.dtype == Q4_K) {
+    e = bn == 256 ? run<Q4_K, 256>(tw, tx, p, lay.tiles, splits, st)
+                  : run<Q4_K, 128>(tw, tx, p, lay.tiles, splits, st);
   } else {
-    switch (dtype) {
-      case Q4_K: e = bn == 256 ? run<Q4_K, 256>(tw, tx, p, st) : run<Q4_K, 128>(tw, tx, p, st); break;
-      case Q6_K: e = bn == 256 ? run<Q6_K, 256>(tw, tx, p, st) : run<Q6_K, 128>(tw, tx, p, st); break;
-      default: return cudaErrorNotSupported;
-    }
+    e = bn == 256 ? run<Q6_K, 256>(tw, tx, p, lay.tiles, splits, st)
+                  : run<Q6_K, 128>(tw, tx, p, lay.tiles, splits, st);
   }
   if (e != cudaSuccess || splits == 1) return e;
-  const int64_t n = M * N;
-  reduce_splits_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(partials, y, n, splits);
+  ReduceArgs r{};
+  r.part = partials;
+  r.M = M;
+  r.N = lay.ncols;
+  r.splits = splits;
+  r.gate_up = p.gate_up;
+  r.n_seg = p.n_seg;
+  for (int m = 0; m < 3; ++m) {
+    r.seg_col0[m] = p.seg_col0[m];
+    r.seg_rows[m] = p.seg_rows[m];
+    r.ys[m] = p.ys[m];
+  }
+  const int64_t n = M * (j.gate_up ? j.rows[0] : lay.ncols);
+  reduce_splits_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(r);
   return cudaGetLastError();
+}
+
+// Single-matrix forms used by hyq_matmul and hyq_matmul_noalloc.
+static GemmJob single_job(int dtype, const uint8_t* w, int64_t K, int64_t N, const float* x, int64_t M, float* y,
+                          unsigned* status) {
+  GemmJob j;
+  j.dtype = dtype;
+  j.n_mat = 1;
+  j.w[0] = w;
+  j.rows[0] = N;
+  j.y[0] = y;
+  j.K = K;
+  j.M = M;
+  j.x = x;
+  j.status = status;
+  return j;
+}
+
+bool gemm_supported(int dtype, int64_t K, int64_t N, int64_t M, const void* w) {
+  return gemm_job_supported(single_job(dtype, static_cast<const uint8_t*>(w), K, N, nullptr, M, nullptr, nullptr));
+}
+
+size_t gemm_workspace_bytes(int dtype, int64_t K, int64_t N, int64_t M) {
+  return gemm_job_workspace_bytes(single_job(dtype, nullptr, K, N, nullptr, M, nullptr, nullptr));
+}
+
+cudaError_t launch_gemm(int dtype, const uint8_t* w, int64_t K, int64_t N, const float* x, int64_t M, float* y,
+                        void* workspace, unsigned* status, cudaStream_t st) {
+  return launch_gemm_job(single_job(dtype, w, K, N, x, M, y, status), workspace, st);
 }
 
 }  // namespace hyq

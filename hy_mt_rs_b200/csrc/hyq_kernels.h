@@ -46,6 +46,23 @@ int gemv_engine(const GemvJob& job);
 // The activations are first rounded to fp16 into `workspace`
 // (gemm_workspace_bytes bytes, 256-byte aligned), which also holds split-K
 // partial sums when the grid is small.
+// Several matrices of one type sharing K and the activations (QKV: their
+// outputs are separate), or a gate/up pair with out = silu(gate x) * (up x).
+struct GemmJob {
+  int dtype = 0;
+  int n_mat = 1;                // 1..3, or 2 with gate_up
+  bool gate_up = false;
+  const uint8_t* w[3] = {};     // packed rows, 16-byte aligned
+  int64_t rows[3] = {};
+  float* y[3] = {};             // [M, rows[m]]; gate_up: y[0] only
+  int64_t K = 0, M = 0;
+  const float* x = nullptr;     // f32 [M, K]
+  unsigned* status = nullptr;
+};
+bool gemm_job_supported(const GemmJob& job);
+size_t gemm_job_workspace_bytes(const GemmJob& job);
+cudaError_t launch_gemm_job(const GemmJob& job, void* workspace, cudaStream_t st);
+
 bool gemm_supported(int dtype, int64_t K, int64_t N, int64_t M, const void* w);
 size_t gemm_workspace_bytes(int dtype, int64_t K, int64_t N, int64_t M);
 cudaError_t launch_gemm(int dtype, const uint8_t* w, int64_t K, int64_t N, const float* x, int64_t M, float* y,

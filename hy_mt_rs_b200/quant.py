@@ -224,6 +224,29 @@ class Weight:
         check(lib.hyq_gemv_qkv(q._h, k._h, v._h, _ptr(input), _ptr(qo), _ptr(ko), _ptr(vo), _stream(dev)))
         return qo, ko, vo
 
+    @staticmethod
+    def matmul_qkv(q, k, v, input, batch):
+        """Batched gemv_qkv (hyq_matmul_qkv): three [batch, N] outputs from
+        one [batch, K] input, one tensor-core launch from 16 tokens up."""
+        _need_cuda(input, "matmul_qkv input", torch.float32)
+        if batch <= 0 or input.numel() != batch * q._shape[0]:
+            raise HyqError(-2, "matmul_qkv: invalid activation shape")
+        outs = [torch.empty((batch, w._shape[1]), dtype=torch.float32, device=input.device) for w in (q, k, v)]
+        check(lib.hyq_matmul_qkv(q._h, k._h, v._h, _ptr(input), int(batch), *(_ptr(o) for o in outs),
+                                 _stream(input.device)))
+        return tuple(outs)
+
+    def matmul_gate_up_silu_batch(self, up, input, batch):
+        """Batched matmul_gate_up_silu (hyq_matmul_gate_up_silu_batch):
+        silu(x gate^T) * (x up^T) for [batch, K] inputs."""
+        _need_cuda(input, "gate_up_silu_batch input", torch.float32)
+        if batch <= 0 or input.numel() != batch * self._shape[0]:
+            raise HyqError(-2, "gate_up_silu_batch: invalid activation shape")
+        out = torch.empty((batch, self._shape[1]), dtype=torch.float32, device=input.device)
+        check(lib.hyq_matmul_gate_up_silu_batch(self._h, up._h, _ptr(input), int(batch), _ptr(out),
+                                                _stream(input.device)))
+        return out
+
     def matmul_gate_up_silu(self, up, input):
         """Weight::matmul_gate_up_silu (quant.rs:724-841): silu(gate x) * (up x)."""
         if up._shape != self._shape:

@@ -129,6 +129,23 @@ int hyq_gemv_qkv(const hyq_weight* q, const hyq_weight* k, const hyq_weight* v, 
 int hyq_matmul_gate_up_silu(const hyq_weight* gate, const hyq_weight* up, const float* input, float* out,
                             void* stream);
 
+/* Batched Weight::gemv_qkv: q/k/v_out[batch, N_q|N_k|N_v] = input[batch, K] .
+ * {Q,K,V}^T.  The reference runs gemv_qkv per token (quant.rs:658-721) and
+ * three Weight::matmul calls for prefill (model.rs:559-565); here one
+ * tensor-core launch covers all three matrices (the activations are
+ * converted once) from 16 tokens up, batch-1 products below. */
+int hyq_matmul_qkv(const hyq_weight* q, const hyq_weight* k, const hyq_weight* v, const float* input, int64_t batch,
+                   float* q_out, float* k_out, float* v_out, void* stream);
+
+/* Batched matmul_gate_up_silu (quant.rs:724-841 per token; for batches
+ * DenseFfn::forward runs gate and up through Weight::matmul and combines
+ * them elementwise, model.rs:678-682):
+ * out[batch, N] = silu(input . gate^T) * (input . up^T), silu(g) = g/(1+e^-g).
+ * From 16 tokens up one tensor-core launch computes matching gate and up rows
+ * in the same tile and writes only the combined output. */
+int hyq_matmul_gate_up_silu_batch(const hyq_weight* gate, const hyq_weight* up, const float* input, int64_t batch,
+                                  float* out, void* stream);
+
 /* Q8::quantize_into (quant.rs:904-922): int8 activations, one f32 scale per
  * 256 values, and the Q2_0C de-interleaved copy (values_q2c may be NULL).
  * Bit-exact with the reference.  scales has ceil(len/256) entries. */

@@ -84,3 +84,47 @@ def test_gemm_matches_gemv_path(cuda):
     y = w.matmul(x, M)
     rows = torch.stack([w.matmul(x[i].contiguous(), 1)[0] for i in range(M)])
     assert (torch.linalg.norm(y - rows) / torch.linalg.norm(rows)).item() < 1e-3
+
+
+def _w(cuda, t, N, K, seed):
+    from hy_mt_rs_b200 import quant, synth
+    return quant.Weight(synth.random_packed(t, N, K, seed=seed, device=cuda), t, [K, N])
+
+
+def _rel(a, b):
+    import torch
+    return (torch.linalg.norm(a - b) / torch.linalg.norm(b)).item()
+
+
+@pytest.mark.parametrize("t,K,Nq,Nkv,M", [(Q4_K, 4096, 4096, 1024, 512), (Q4_K, 2048, 1024, 256, 37),
+                                          (Q6_K, 1024, 512, 128, 300), (Q4_K, 1024, 256, 128, 7)])
+def test_matmul_qkv_matches_separate_products(cuda, t, K, Nq, Nkv, M):
+    """One grouped launch (QKV share the input) equals three products; M=7
+    takes the batch-1 path."""
+    import torch
+    from hy_mt_rs_b200 import quant
+
+    q, k, v = _w(cuda, t, Nq, K, 1), _w(cuda, t, Nkv, K, 2), _w(cuda, t, Nkv, K, 3)
+    x = torch.randn(M, K, generator=torch.Generator().manual_seed(4)).to(cuda)
+    got = quant.Weight.matmul_qkv(q, k, v, x, M)
+    for w, y in zip((q, k, v), got):
+        ref = w.matmul(x, M)
+        assert _rel(y, ref) < 1e-5, _rel(y, ref)
+    assert quant.device_status() == 0
+
+
+@pytest.mark.parametrize("t,N,K,M", [(Q4_K, 14336, 4096, 512), (Q4_K, 1024, 2048, 64), (Q6_K, 768, 1024, 200),
+                                     (Q4_K, 512, 1024, 9)])
+def test_gate_up_silu_batch_matches_separate_products(cuda, t, N, K, M):
+    """silu(gate) * up from one fused launch equals the reference's batched
+    DenseFfn (two products, then the elementwise combination)."""
+    import torch
+    from hy_mt_rs_b200 import quant
+
+    gate, up = _w(cuda, t, N, K, 5), _w(cuda, t, N, K, 6)
+    x = torch.randn(M, K, generator=torch.Generator().manual_seed(7)).to(cuda)
+    got = gate.matmul_gate_up_silu_batch(up, x, M)
+    g, u = gate.matmul(x, M), up.matmul(x, M)
+    ref = (g / (1.0 + torch.exp(-g))) * u
+    assert _rel(got, ref) < 1e-5, _rel(got, ref)
+    assert quant.device_status() == 0
