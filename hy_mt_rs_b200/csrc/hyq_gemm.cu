@@ -41,6 +41,7 @@
 #include <mutex>
 
 #include "hyq_common.cuh"
+#include "hyq_formats.cuh"
 #include "hyq_kernels.h"
 
 namespace hyq {
@@ -59,7 +60,10 @@ constexpr int kTmemCols = 512;
 __host__ __device__ constexpr int stages_for(int bn) { return bn == 256 ? 5 : 8; }
 
 // Bytes per row of the packed block-column tile (TMA box inner size).
-__host__ __device__ constexpr int wbox_for(int fmt) { return fmt == Q4_K ? 144 : 224; }
+// (the 16-byte aligned window around one block column: packed bytes + skew)
+__host__ __device__ constexpr int wbox_for(int fmt) {
+  return fmt == Q4_K ? 144 : fmt == Q6_K ? 224 : fmt == Q8_0 ? 160 : fmt == Q2_0C ? 144 : 64;
+}
 
 struct Params {
   int K, N, M;
@@ -205,8 +209,17 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
 // thread of the row, t: 32-bit word, j: pair inside the word) holds columns
 // c + T[j][0], c + T[j][1] with c = 16h + 4t; T is the order in which pairs of
 // codes fall out of a 32-bit word with (w >> 4k) & 0x000F000F.
+//
+// Q8_0 keeps the natural order.  Q2_0C: word t of the step's 16 code bytes,
+// code k of its bytes (0, 2) or (1, 3) (ab = 0 / 1): pair P = 8t + 2k + ab
+// holds columns 16t + 4ab + k and + 8.  STQ1_0: lane p of the patterns of
+// groups 4i + (0, 2) or (1, 3): pair P = 8i + 2p + ab holds columns
+// 4i + ab + 16p and + 2.
 __host__ __device__ constexpr int k_perm(int fmt, int slot) {
   const int P = slot >> 1, e = slot & 1;
+  if (fmt == Q8_0) return slot;
+  if (fmt == Q2_0C) return 16 * (P >> 3) + 4 * (P & 1) + ((P >> 1) & 3) + 8 * e;
+  if (fmt == STQ1_0) return 4 * (P >> 3) + (P & 1) + 2 * e + 16 * ((P >> 1) & 3);
   const int h = P >> 4, t = (P >> 2) & 3, j = P & 3;
   const int c = 16 * h + 4 * t;
   // Q4_K, j = 0..3: (0,2) (32,34) (1,3) (33,35)  [low / high nibbles]
@@ -251,7 +264,68 @@ __device__ __forceinline__ uint2 ld_s64(uint32_t a) {
 template <int FMT>
 __device__ __forceinline__ void decode64(uint32_t row, int j4, uint32_t (&o)[32]) {
   constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024 in both halves
-  if (FMT == Q4_K) {
+  if constexpr (FMT == Q8_0) {
+    // Step j4 of a 4-block column: blocks 2 j4, 2 j4 + 1 (quant.rs:2413-2418,
+    // d * q).  Flipping the sign bit gives q + 128 in 0..255; PRMT places two
+    // such bytes under fp16 1024's exponent; subtracting 1152 leaves q.
+    const uint32_t k1152 = 0x64806480u;
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      const uint32_t blk = row + (2 * j4 + b) * 34;
+      const uint32_t d = ld_s16(blk);
+      const uint32_t d2 = d | (d << 16);
+      uint32_t w[8];
+      ld_s_words<8>(blk + 2, w);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const uint32_t u = w[t] ^ 0x80808080u;
+        o[16 * b + 2 * t] = hmul2_u(hsub2_u(prmt_b32(u, 0x64646464u, 0x4140u), k1152), d2);
+        o[16 * b + 2 * t + 1] = hmul2_u(hsub2_u(prmt_b32(u, 0x64646464u, 0x4342u), k1152), d2);
+      }
+    }
+  } else if constexpr (FMT == Q2_0C) {
+    // One 512-weight block per block column (quant.rs:2419-2432: (2c - 3) d,
+    // four codes per byte); step j4 = code bytes 16 j4 .. + 15.
+    const uint32_t d = ld_s16(row);
+    const uint32_t d2 = d | (d << 16);
+    uint32_t w[4];
+    ld_s_words<4>(row + 2 + 16 * j4, w);
+    const uint32_t k2 = 0x40004000u, km3 = 0xC200C200u;  // fp16 2, -3
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+#pragma unroll
+        for (int ab = 0; ab < 2; ++ab) {
+          const uint32_t v = ((w[t] >> (2 * k + 8 * ab)) & 0x00030003u) | kMagic;  // 1024 + c
+          const uint32_t c = hsub2_u(v, kMagic);
+          o[8 * t + 2 * k + ab] = hmul2_u(hfma2_u(c, k2, km3), d2);  // (2c - 3) d, rounded once
+        }
+      }
+    }
+  } else if constexpr (FMT == STQ1_0) {
+    // One 256-weight block per block column; step j4 = chunk j4 (16 groups,
+    // columns 64 j4 + g % 16 + 16 p): (digit - 1) d (quant.rs:1103-1123).
+    const uint32_t d = ld_s16(row + 40);
+    const uint32_t d2 = d | (d << 16);
+    uint32_t nb[2];
+    ld_s_words<2>(row + 8 * j4, nb);
+    const uint32_t sbits = ld_s16(row + 32 + 2 * j4);
+    const uint32_t k1025 = 0x64016401u;  // fp16 1025
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t hw = (i & 1) ? (nb[i >> 1] >> 16) : (nb[i >> 1] & 0xffffu);
+      const uint32_t cb = stq_patterns4(hw, (sbits >> (4 * i)) & 15u);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+#pragma unroll
+        for (int ab = 0; ab < 2; ++ab) {
+          const uint32_t v = ((cb >> (2 * p + 8 * ab)) & 0x00030003u) | kMagic;  // 1024 + digit
+          o[8 * i + 2 * p + ab] = hmul2_u(hsub2_u(v, k1025), d2);
+        }
+      }
+    }
+  } else if constexpr (FMT == Q4_K) {
     const int g = j4;  // 64-column group of the 256-column block
     const uint4 hd = ld_s128(row);
     const float d = half_to_f32(hd.x & 0xffffu), dmin = half_to_f32(hd.x >> 16);
@@ -285,6 +359,7 @@ __device__ __forceinline__ void decode64(uint32_t row, int j4, uint32_t (&o)[32]
       }
     }
   } else {  // Q6_K
+    static_assert(FMT == Q6_K, "format without a GEMM decoder");
     const int chunk = j4 >> 1, p0 = 2 * (j4 & 1);
     const int nsh = (p0 >> 1) * 4;
     uint32_t A[8], B[8], H[8];
@@ -396,10 +471,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           // one load per row class j fetches rows row0 + j, + j + g, ...;
           // a gate/up tile loads 64 rows of each matrix.
           const int64_t kb = (kbeg + ks) / steps_per_w;
-          const CUtensorMap* maps[3] = {&tmap_w0, &tmap_w1, &tmap_w2};
           mbar_arrive_expect_tx(wfull(ws), (uint32_t)(BM * p.wbox));
           for (int mt = 0; mt < (p.gate_up ? 2 : 1); ++mt) {
-            const CUtensorMap* map = maps[p.gate_up ? mt : seg];
+            const int mi = p.gate_up ? mt : seg;
+            const CUtensorMap* map = mi == 0 ? &tmap_w0 : (mi == 1 ? &tmap_w1 : &tmap_w2);
             for (int j = 0; j < p.g; ++j) {
               const int x0 = (int)(((int64_t)j * p.row_bytes + kb * p.wbytes) & ~int64_t(15));
               tma_load_2d(base + L::w + ws * L::w_stage + (mt * tile_rows + j * (tile_rows / p.g)) * p.wbox, map,
@@ -922,6 +997,9 @@ bool geometry(int dtype, int64_t K, int64_t N, int64_t row_bytes, Geometry& g) {
   switch (dtype) {
     case Q4_K: g.wcol = 256; g.wbytes = 144; g.wbox = wbox_for(Q4_K); break;
     case Q6_K: g.wcol = 256; g.wbytes = 210; g.wbox = wbox_for(Q6_K); break;
+    case Q8_0: g.wcol = 128; g.wbytes = 136; g.wbox = wbox_for(Q8_0); break;   // 4 blocks
+    case Q2_0C: g.wcol = 512; g.wbytes = 130; g.wbox = wbox_for(Q2_0C); break;
+    case STQ1_0: g.wcol = 256; g.wbytes = 42; g.wbox = wbox_for(STQ1_0); break;
     default: return false;
   }
   return K % g.wcol == 0;
@@ -1110,15 +1188,19 @@ cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) 
   const int64_t K = j.K, M = j.M;
   const int64_t row_bytes = K / block_len(j.dtype) * block_bytes(j.dtype);
   const Layout lay = layout_of(j);
-  const bool pair = !j.gate_up && j.n_mat == 1 && use_pair(j.rows[0], M);
+  const bool pair = !j.gate_up && j.n_mat == 1 && (j.dtype == Q4_K || j.dtype == Q6_K) && use_pair(j.rows[0], M);
   __half* xh = static_cast<__half*>(workspace);
   {
     const int64_t pairs = K * M / 2;
     const unsigned blocks = (unsigned)((pairs + 255) / 256);
-    if (j.dtype == Q4_K)
-      to_half_kernel<Q4_K><<<blocks, 256, 0, st>>>(j.x, reinterpret_cast<__half2*>(xh), K, pairs);
-    else
-      to_half_kernel<Q6_K><<<blocks, 256, 0, st>>>(j.x, reinterpret_cast<__half2*>(xh), K, pairs);
+    __half2* xh2 = reinterpret_cast<__half2*>(xh);
+    switch (j.dtype) {
+      case Q4_K: to_half_kernel<Q4_K><<<blocks, 256, 0, st>>>(j.x, xh2, K, pairs); break;
+      case Q6_K: to_half_kernel<Q6_K><<<blocks, 256, 0, st>>>(j.x, xh2, K, pairs); break;
+      case Q8_0: to_half_kernel<Q8_0><<<blocks, 256, 0, st>>>(j.x, xh2, K, pairs); break;
+      case Q2_0C: to_half_kernel<Q2_0C><<<blocks, 256, 0, st>>>(j.x, xh2, K, pairs); break;
+      default: to_half_kernel<STQ1_0><<<blocks, 256, 0, st>>>(j.x, xh2, K, pairs); break;
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
@@ -1178,12 +1260,20 @@ cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) 
     p.N = (int)j.rows[0];
     p.y = splits > 1 ? partials : j.y[0];
     e = j.dtype == Q4_K ? run_pair<Q4_K>(tw[0], tx, p, splits, st) : run_pair<Q6_K>(tw[0], tx, p, splits, st);
-  } else if (j.dtype == Q4_K) {
-    e = bn == 256 ? run<Q4_K, 256>(tw, tx, p, lay.tiles, splits, st)
-                  : run<Q4_K, 128>(tw, tx, p, lay.tiles, splits, st);
   } else {
-    e = bn == 256 ? run<Q6_K, 256>(tw, tx, p, lay.tiles, splits, st)
-                  : run<Q6_K, 128>(tw, tx, p, lay.tiles, splits, st);
+    switch (j.dtype) {
+#define HYQ_RUN(F) \
+  case F:          \
+    e = bn == 256 ? run<F, 256>(tw, tx, p, lay.tiles, splits, st) : run<F, 128>(tw, tx, p, lay.tiles, splits, st); \
+    break;
+      HYQ_RUN(Q4_K)
+      HYQ_RUN(Q6_K)
+      HYQ_RUN(Q8_0)
+      HYQ_RUN(Q2_0C)
+      HYQ_RUN(STQ1_0)
+#undef HYQ_RUN
+      default: return cudaErrorNotSupported;
+    }
   }
   if (e != cudaSuccess || splits == 1) return e;
   ReduceArgs r{};

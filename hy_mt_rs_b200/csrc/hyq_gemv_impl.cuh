@@ -344,20 +344,10 @@ __device__ __forceinline__ void decode_unit(uint32_t row, int u, WUnit& wu) {
     uint32_t nb[2];
     ld_s_words<2>(blk + 8 * c, nb);
     const uint32_t sbits = ld_s16(blk + 32 + 2 * c);
-    const uint32_t T0 = 0x092989a9u, T1 = 0x062686a6u, T2 = 0x121a929au, T3 = 0x424a626au;
-    const uint32_t T4 = 0xa1812101u, T5 = 0xa4842404u, T6 = 0x98901810u, T7 = 0x68604840u;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const uint32_t hw = (i & 1) ? (nb[i >> 1] >> 16) : (nb[i >> 1] & 0xffffu);
-      const uint32_t sel = hw & 0x7777u;
-      const uint32_t p0 = prmt(T0, T1, sel), p1 = prmt(T2, T3, sel);
-      const uint32_t p2 = prmt(T4, T5, sel), p3 = prmt(T6, T7, sel);
-      const uint32_t m3 = prmt(hw << 4, hw, 0xD9C8u);
-      const uint32_t s4 = (sbits >> (4 * i)) & 15u;
-      const uint32_t sm = prmt(s4 * 0x10204080u, 0u, 0xBA98u);
-      const uint32_t lo = (p0 & ~m3) | (p1 & m3);
-      const uint32_t hi = (p2 & ~m3) | (p3 & m3);
-      const uint32_t cb = (lo & ~sm) | (hi & sm);
+      const uint32_t cb = stq_patterns4(hw, (sbits >> (4 * i)) & 15u);
 #pragma unroll
       for (int pl = 0; pl < 4; ++pl) wu.c[4 * i + pl] = (cb >> (2 * pl)) & 0x03030303u;
     }

@@ -11,7 +11,7 @@ from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
 
-Q4_K, Q6_K = 2, 3
+Q4_K, Q6_K, Q8_0, Q2_0C, STQ1_0 = 2, 3, 4, 5, 6
 
 
 def to_dev(a, cuda):
@@ -127,4 +127,31 @@ def test_gate_up_silu_batch_matches_separate_products(cuda, t, N, K, M):
     g, u = gate.matmul(x, M), up.matmul(x, M)
     ref = (g / (1.0 + torch.exp(-g))) * u
     assert _rel(got, ref) < 1e-5, _rel(got, ref)
+    assert quant.device_status() == 0
+
+
+# The other packed formats (Q8_0 in 4-block columns, Q2_0C in 512-weight
+# blocks, STQ1_0 ternary through the codebook), at small and 1.8B shapes.
+@pytest.mark.parametrize("t,N,K,M", [(Q8_0, 128, 256, 16), (Q8_0, 300, 1024, 37), (Q8_0, 2048, 2048, 512),
+                                     (Q2_0C, 128, 512, 16), (Q2_0C, 300, 2048, 200), (Q2_0C, 2048, 6144, 512),
+                                     (STQ1_0, 128, 256, 16), (STQ1_0, 257, 2048, 130), (STQ1_0, 6144, 2048, 256)])
+def test_gemm_other_formats(cuda, t, N, K, M):
+    run_case(cuda, t, N, K, M, seed=N + K + M + t)
+
+
+@pytest.mark.parametrize("t", [Q2_0C, STQ1_0])
+def test_gemm_1p8b_layer_calls(cuda, t):
+    """Grouped QKV and fused gate/up-SiLU on the 1.8B layer shapes."""
+    import torch
+    from hy_mt_rs_b200 import quant
+
+    M = 256
+    q, k, v = _w(cuda, t, 2048, 2048, 1), _w(cuda, t, 512, 2048, 2), _w(cuda, t, 512, 2048, 3)
+    x = torch.randn(M, 2048, generator=torch.Generator().manual_seed(8)).to(cuda)
+    for w, y in zip((q, k, v), quant.Weight.matmul_qkv(q, k, v, x, M)):
+        assert _rel(y, w.matmul(x, M)) < 1e-5
+    gate, up = _w(cuda, t, 6144, 2048, 4), _w(cuda, t, 6144, 2048, 5)
+    got = gate.matmul_gate_up_silu_batch(up, x, M)
+    g, u = gate.matmul(x, M), up.matmul(x, M)
+    assert _rel(got, (g / (1.0 + torch.exp(-g))) * u) < 1e-5
     assert quant.device_status() == 0
