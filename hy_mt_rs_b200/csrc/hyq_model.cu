@@ -1,0 +1,402 @@
+// Decoder-step kernels around the quantized products: the rest of one
+// single-token step of the Dense architecture (Hy-MT2, model.rs:374-547):
+// embedding row, RMSNorm, RoPE with the per-head q/k norm, KV-cache append,
+// attention over the cache, residual add and greedy argmax.  Every kernel
+// that depends on the token position reads it from device memory, so a whole
+// step is one CUDA graph replayed for every token.
+//
+// Numerics follow the reference's x86 branches: the dot products of the
+// norms and of the attention scores are summed in the order of dot_avx2
+// (quant.rs:2562-2596: two 8-lane FMA accumulators over 16-wide chunks, an
+// 8-wide tail, a sequential lane sum from -0, the scalar tail); elementwise
+// products are rounded separately as Rust does (no contraction).  Only the
+// softmax exponential differs from the reference's libm expf.
+#include <cuda_runtime.h>
+
+#include <cmath>
+
+#include "../../include/hyq.h"
+#include "hyq_common.cuh"
+#include "hyq_formats.cuh"
+#include "hyq_kernels.h"
+
+namespace hyq {
+namespace model {
+
+// dot_avx2 order over n floats, by the 16 lanes [b, b + 16) of a warp (b =
+// lane & 16), one per AVX2 accumulator lane.  Every lane of the group returns
+// the result.  `mask` covers the calling lanes.
+__device__ __forceinline__ float dot_x86(const float* a, const float* b, int n, unsigned mask) {
+  const int lane = threadIdx.x & 31;
+  const int l = lane & 15, base = lane & 16;
+  const int chunks = n / 16;
+  float acc = 0.f;
+  for (int c = 0; c < chunks; ++c) acc = fmaf(a[16 * c + l], b[16 * c + l], acc);
+  // sum[l] = s0[l] + s1[l] for l < 8
+  float sum = __fadd_rn(acc, __shfl_sync(mask, acc, base + ((l + 8) & 15)));
+  const int simd_end = chunks * 16, vec_end = n / 8 * 8;
+  if (vec_end > simd_end && l < 8) sum = fmaf(a[simd_end + l], b[simd_end + l], sum);
+  float h = -0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) h = __fadd_rn(h, __shfl_sync(mask, sum, base + k));
+  float t = -0.0f;
+  for (int i = vec_end; i < n; ++i) t = __fadd_rn(t, __fmul_rn(a[i], b[i]));
+  return __fadd_rn(h, t);
+}
+
+// RMSNorm of `rows` rows of n floats (rms_norm_into, model.rs:785-830; per
+// head, model.rs:832-872): variance = dot(x, x) / n, scale = 1 / sqrt(var +
+// eps), out = (x * scale) * w.  One CTA per row.
+__global__ void __launch_bounds__(256) rms_norm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                        int n, float eps, float* __restrict__ out) {
+  const float* xr = x + (size_t)blockIdx.x * n;
+  float* orow = out + (size_t)blockIdx.x * n;
+  __shared__ float scale_s;
+  if (threadIdx.x < 16) {
+    const float d = dot_x86(xr, xr, n, 0xffffu);
+    if (threadIdx.x == 0) {
+      const float variance = __fdiv_rn(d, (float)n);
+      scale_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(variance, eps)));
+    }
+  }
+  __syncthreads();
+  const float scale = scale_s;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) orow[i] = __fmul_rn(__fmul_rn(xr[i], scale), w[i]);
+}
+
+// Embedding row (Weight::row_into, quant.rs:123-142) of the token held in
+// device memory, decoded bit for bit.
+template <int T>
+__global__ void __launch_bounds__(256) embed_kernel(const uint8_t* __restrict__ w, int64_t row_bytes, int64_t n,
+                                                     int64_t rows, const int32_t* __restrict__ token,
+                                                     float* __restrict__ out, unsigned* status) {
+  const int64_t tok = *token;
+  if (tok < 0 || tok >= rows) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(status, DEV_BAD_ARGS);
+    return;
+  }
+  const uint8_t* row = w + tok * row_bytes;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = i / block_len(T);
+    out[i] = decode_elem<T>(row + b * block_bytes(T), (int)(i - b * block_len(T)));
+  }
+}
+
+// RoPE (rope_with_cache, model.rs:874-913) of q and k with the table row of
+// the current position, then (Dense, model.rs:443-446) the per-head RMSNorm
+// with q_norm / k_norm; `norm_first` runs the norm before the rotation
+// (HyV3, model.rs:425-428).  Also appends k and v to the KV cache at the
+// position (KvCache::append, model.rs:650-667).  One warp per head; grid =
+// heads + kv_heads.
+struct RopeArgs {
+  float* q;
+  float* k;
+  const float* v;
+  int heads, kv_heads, dim;
+  const float* cos_tab;  // [positions, dim / 2]
+  const float* sin_tab;
+  int positions;
+  const int32_t* pos;
+  const float* q_norm;   // [dim] or null
+  const float* k_norm;
+  float eps;
+  int norm_first;
+  float* k_cache;        // [positions, kv_heads * dim]
+  float* v_cache;
+  unsigned* status;
+};
+
+__device__ void head_norm(float* hd, const float* w, int dim, float eps) {
+  const int lane = threadIdx.x & 31;
+  float scale = 0.f;
+  const float d = dot_x86(hd, hd, dim, 0xffffffffu);  // both half-warps compute it
+  scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(d, (float)dim), eps)));
+  __syncwarp();
+  for (int i = lane; i < dim; i += 32) hd[i] = __fmul_rn(__fmul_rn(hd[i], scale), w[i]);
+  __syncwarp();
+}
+
+__device__ void head_rope(float* hd, const float* c, const float* s, int dim) {
+  const int half = dim / 2;
+  for (int j = threadIdx.x & 31; j < half; j += 32) {
+    const float a = hd[j], b = hd[j + half];
+    hd[j] = __fsub_rn(__fmul_rn(a, c[j]), __fmul_rn(b, s[j]));
+    hd[j + half] = __fadd_rn(__fmul_rn(a, s[j]), __fmul_rn(b, c[j]));
+  }
+  __syncwarp();
+}
+
+__global__ void __launch_bounds__(32) rope_qk_kernel(const __grid_constant__ RopeArgs a) {
+  const int pos = *a.pos;
+  if (pos < 0 || pos >= a.positions) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(a.status, DEV_BAD_ARGS);
+    return;
+  }
+  const int h = blockIdx.x;
+  const bool is_q = h < a.heads;
+  float* hd = is_q ? a.q + (size_t)h * a.dim : a.k + (size_t)(h - a.heads) * a.dim;
+  const float* nw = is_q ? a.q_norm : a.k_norm;
+  const float* c = a.cos_tab + (size_t)pos * (a.dim / 2);
+  const float* s = a.sin_tab + (size_t)pos * (a.dim / 2);
+  if (a.norm_first && nw) head_norm(hd, nw, a.dim, a.eps);
+  head_rope(hd, c, s, a.dim);
+  if (!a.norm_first && nw) head_norm(hd, nw, a.dim, a.eps);
+  if (!is_q) {
+    const int kh = h - a.heads;
+    const size_t width = (size_t)a.kv_heads * a.dim;
+    float* kc = a.k_cache + (size_t)pos * width + (size_t)kh * a.dim;
+    float* vc = a.v_cache + (size_t)pos * width + (size_t)kh * a.dim;
+    const float* vv = a.v + (size_t)kh * a.dim;
+    for (int i = threadIdx.x; i < a.dim; i += 32) {
+      kc[i] = hd[i];
+      vc[i] = vv[i];
+    }
+  }
+}
+
+// attention_into for one query token (model.rs:949-1021): per head, scores
+// over the positions 0..pos (dot in the x86 order, times 1/sqrt(dim)),
+// softmax, and the probability-weighted sum of the values in position order.
+// One CTA of 256 threads per head; scores in shared memory.
+constexpr int kMaxPositions = 16384;
+
+__global__ void __launch_bounds__(256) attention_kernel(const float* __restrict__ q,
+                                                         const float* __restrict__ k_cache,
+                                                         const float* __restrict__ v_cache, int heads, int kv_heads,
+                                                         int dim, const int32_t* __restrict__ pos_dev,
+                                                         int positions, float* __restrict__ out, unsigned* status) {
+  extern __shared__ float scores[];
+  __shared__ float red[32];
+  const int pos = *pos_dev;
+  if (pos < 0 || pos >= positions || pos >= kMaxPositions) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(status, DEV_BAD_ARGS);
+    return;
+  }
+  const int visible = pos + 1;
+  const int h = blockIdx.x;
+  const int kvh = h / (heads / kv_heads);
+  const size_t width = (size_t)kv_heads * dim;
+  const float* query = q + (size_t)h * dim;
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)dim));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // scores: a warp takes the pair of positions 2 pp, 2 pp + 1, one per
+  // half-warp (whole-warp shuffles; a position past the end reads position 0
+  // and is discarded)
+  const int nwarps = blockDim.x >> 5;
+  for (int pp = warp; 2 * pp < visible; pp += nwarps) {
+    const int p = 2 * pp + (lane >> 4);
+    const bool valid = p < visible;
+    const int pr = valid ? p : 0;
+    const float d = dot_x86(query, k_cache + (size_t)pr * width + (size_t)kvh * dim, dim, 0xffffffffu);
+    if (valid && (lane & 15) == 0) scores[p] = __fmul_rn(d, scale);
+  }
+  __syncthreads();
+  // max
+  float m = -INFINITY;
+  for (int p = threadIdx.x; p < visible; p += blockDim.x) m = fmaxf(m, scores[p]);
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float mm = red[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) mm = fmaxf(mm, red[w]);
+    red[31] = mm;
+  }
+  __syncthreads();
+  m = red[31];
+  __syncthreads();
+  // exponentials and their sum (in position order, by one warp per 32
+  // positions, then a fixed-order sum of the warp totals)
+  for (int p = threadIdx.x; p < visible; p += blockDim.x) scores[p] = expf(__fsub_rn(scores[p], m));
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float sum = 0.f;
+    for (int p = 0; p < visible; ++p) sum = __fadd_rn(sum, scores[p]);
+    red[30] = __fdiv_rn(1.0f, sum);
+  }
+  __syncthreads();
+  const float inv_sum = red[30];
+  for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+    float o = 0.f;
+    for (int p = 0; p < visible; ++p)
+      o = __fadd_rn(o, __fmul_rn(__fmul_rn(scores[p], inv_sum), v_cache[(size_t)p * width + (size_t)kvh * dim + d]));
+    out[(size_t)h * dim + d] = o;
+  }
+}
+
+__global__ void __launch_bounds__(256) add_kernel(float* __restrict__ dst, const float* __restrict__ src, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) dst[i] = __fadd_rn(dst[i], src[i]);
+}
+
+// Greedy token (generation.rs:281-290): the first index of the largest value.
+// One CTA; optionally advances the position counter.
+__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ x, int64_t n, int32_t* token,
+                                                       int32_t* pos) {
+  float best = -INFINITY;
+  int64_t idx = n;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = x[i];
+    if (v > best || (v == best && i < idx)) {
+      best = v;
+      idx = i;
+    }
+  }
+  __shared__ float bv[32];
+  __shared__ int64_t bi[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ov > best || (ov == best && oi < idx)) {
+      best = ov;
+      idx = oi;
+    }
+  }
+  if (lane == 0) {
+    bv[warp] = best;
+    bi[warp] = idx;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+      if (bv[w] > best || (bv[w] == best && bi[w] < idx)) {
+        best = bv[w];
+        idx = bi[w];
+      }
+    *token = (int32_t)(idx < n ? idx : 0);
+    if (pos) *pos += 1;
+  }
+}
+
+}  // namespace model
+}  // namespace hyq
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+extern "C" {
+
+int hyq_rope_table(int64_t positions, int head_dim, float rope_base, float* cos_out, float* sin_out) {
+  if (positions < 0 || head_dim <= 0 || (head_dim & 1) || !cos_out || !sin_out)
+    return hyq::api_fail(HYQ_E_INVALID, "rope_table: bad arguments");
+  const int half = head_dim / 2;
+  for (int j = 0; j < half; ++j) {
+    // model.rs:266-272 and 378-391: f32 powf, then (pos * freq).sin_cos()
+    const float freq = powf(rope_base, -2.0f * (float)j / (float)head_dim);
+    for (int64_t p = 0; p < positions; ++p) {
+      const float a = (float)p * freq;
+      sin_out[p * half + j] = sinf(a);
+      cos_out[p * half + j] = cosf(a);
+    }
+  }
+  return HYQ_OK;
+}
+
+int hyq_rms_norm(const float* x, const float* w, int64_t n, int64_t rows, float eps, float* out, void* stream) {
+  if (!x || !w || !out) return hyq::api_fail(HYQ_E_INVALID, "rms_norm: null pointer");
+  if (n <= 0 || rows <= 0 || n > INT32_MAX || rows > INT32_MAX) return hyq::api_fail(HYQ_E_SHAPE, "rms_norm: shape");
+  hyq::model::rms_norm_kernel<<<(unsigned)rows, 256, 0, (cudaStream_t)stream>>>(x, w, (int)n, eps, out);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "rms_norm: %s", cudaGetErrorString(e));
+}
+
+int hyq_embed(const hyq_weight* w, const int32_t* token, float* out, void* stream) {
+  int dtype = 0, ndim = 0;
+  int64_t dims[3] = {};
+  const void* data = nullptr;
+  if (!w || !token || !out) return hyq::api_fail(HYQ_E_INVALID, "embed: null pointer");
+  int rc = hyq_weight_info(w, &dtype, &ndim, dims, nullptr, &data);
+  if (rc) return rc;
+  if (ndim != 2) return hyq::api_fail(HYQ_E_SHAPE, "embed: weight is not a matrix");
+  unsigned* status = nullptr;
+  if ((rc = hyq::api_status_word(&status))) return rc;
+  const int64_t n = dims[0], rows = dims[1];
+  const int64_t rb = n / hyq::block_len(dtype) * hyq::block_bytes(dtype);
+  const unsigned blocks = (unsigned)((n + 255) / 256);
+  cudaStream_t st = (cudaStream_t)stream;
+  const uint8_t* wd = static_cast<const uint8_t*>(data);
+  switch (dtype) {
+    case hyq::F32: hyq::model::embed_kernel<hyq::F32><<<blocks, 256, 0, st>>>(wd, rb, n, rows, token, out, status); break;
+    case hyq::F16: hyq::model::embed_kernel<hyq::F16><<<blocks, 256, 0, st>>>(wd, rb, n, rows, token, out, status); break;
+    case hyq::Q4_K: hyq::model::embed_kernel<hyq::Q4_K><<<blocks, 256, 0, st>>>(wd, rb, n, rows, token, out, status); break;
+    case hyq::Q6_K: hyq::model::embed_kernel<hyq::Q6_K><<<blocks, 256, 0, st>>>(wd, rb, n, rows, token, out, status); break;
+    case hyq::Q8_0: hyq::model::embed_kernel<hyq::Q8_0><<<blocks, 256, 0, st>>>(wd, rb, n, rows, token, out, status); break;
+    case hyq::Q2_0C: hyq::model::embed_kernel<hyq::Q2_0C><<<blocks, 256, 0, st>>>(wd, rb, n, rows, token, out, status); break;
+    default: hyq::model::embed_kernel<hyq::STQ1_0><<<blocks, 256, 0, st>>>(wd, rb, n, rows, token, out, status); break;
+  }
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "embed: %s", cudaGetErrorString(e));
+}
+
+int hyq_rope_qk(float* q, float* k, const float* v, int heads, int kv_heads, int head_dim, const float* cos_tab,
+                const float* sin_tab, int64_t positions, const int32_t* pos, const float* q_norm,
+                const float* k_norm, float eps, int norm_first, float* k_cache, float* v_cache, void* stream) {
+  if (!q || !k || !v || !cos_tab || !sin_tab || !pos || !k_cache || !v_cache)
+    return hyq::api_fail(HYQ_E_INVALID, "rope_qk: null pointer");
+  if (heads <= 0 || kv_heads <= 0 || heads % kv_heads || head_dim <= 0 || (head_dim & 1) || positions <= 0 ||
+      positions > INT32_MAX)
+    return hyq::api_fail(HYQ_E_SHAPE, "rope_qk: shape");
+  hyq::model::RopeArgs a{};
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.heads = heads;
+  a.kv_heads = kv_heads;
+  a.dim = head_dim;
+  a.cos_tab = cos_tab;
+  a.sin_tab = sin_tab;
+  a.positions = (int)positions;
+  a.pos = pos;
+  a.q_norm = q_norm;
+  a.k_norm = k_norm;
+  a.eps = eps;
+  a.norm_first = norm_first;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  int rc = hyq::api_status_word(&a.status);
+  if (rc) return rc;
+  hyq::model::rope_qk_kernel<<<(unsigned)(heads + kv_heads), 32, 0, (cudaStream_t)stream>>>(a);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "rope_qk: %s", cudaGetErrorString(e));
+}
+
+int hyq_attention(const float* q, const float* k_cache, const float* v_cache, int heads, int kv_heads,
+                  int head_dim, int64_t positions, const int32_t* pos, float* out, void* stream) {
+  if (!q || !k_cache || !v_cache || !pos || !out) return hyq::api_fail(HYQ_E_INVALID, "attention: null pointer");
+  if (heads <= 0 || kv_heads <= 0 || heads % kv_heads || head_dim <= 0 || positions <= 0 ||
+      positions > hyq::model::kMaxPositions)
+    return hyq::api_fail(HYQ_E_SHAPE, "attention: shape (at most %d positions)", hyq::model::kMaxPositions);
+  unsigned* status = nullptr;
+  int rc = hyq::api_status_word(&status);
+  if (rc) return rc;
+  const size_t smem = (size_t)positions * sizeof(float);
+  static int configured = 0;
+  if (!configured) {
+    cudaFuncSetAttribute(hyq::model::attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         hyq::model::kMaxPositions * (int)sizeof(float));
+    configured = 1;
+  }
+  hyq::model::attention_kernel<<<(unsigned)heads, 256, smem, (cudaStream_t)stream>>>(
+      q, k_cache, v_cache, heads, kv_heads, head_dim, pos, (int)positions, out, status);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "attention: %s", cudaGetErrorString(e));
+}
+
+int hyq_add(float* dst, const float* src, int64_t n, void* stream) {
+  if (!dst || !src) return hyq::api_fail(HYQ_E_INVALID, "add: null pointer");
+  if (n <= 0) return n == 0 ? HYQ_OK : hyq::api_fail(HYQ_E_SHAPE, "add: negative length");
+  hyq::model::add_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(dst, src, n);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "add: %s", cudaGetErrorString(e));
+}
+
+int hyq_argmax(const float* x, int64_t n, int32_t* token, int32_t* pos, void* stream) {
+  if (!x || !token) return hyq::api_fail(HYQ_E_INVALID, "argmax: null pointer");
+  if (n <= 0 || n > INT32_MAX) return hyq::api_fail(HYQ_E_SHAPE, "argmax: length");
+  hyq::model::argmax_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(x, n, token, pos);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "argmax: %s", cudaGetErrorString(e));
+}
+
+}  // extern "C"

@@ -1,0 +1,167 @@
+"""Single-token decode of the Dense architecture (Hy-MT2: model.rs:374-547)
+on the device, through libhyq only: embedding row, per layer RMSNorm -> QKV
+-> RoPE + q/k norm + KV append -> attention -> O + residual -> RMSNorm ->
+gate/up-SiLU -> down + residual, then the output norm, the lm_head product
+and the greedy argmax.  The position and the token live in device memory,
+so one captured CUDA graph replays a whole token step.
+
+Weights are packed GGUF bytes (any hyq_dtype for the linears; the embedding
+is tied to the lm_head as in the 1.8B model); norms are f32.  The KV cache is
+f32, as in the reference (model.rs:116-120).
+"""
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import quant
+from ._native import check, lib
+
+
+@dataclass
+class DenseConfig:
+    layers: int = 32
+    hidden: int = 2048
+    heads: int = 16
+    kv_heads: int = 4
+    head_dim: int = 128
+    ffn: int = 6144
+    vocab: int = 120832
+    rope_base: float = 10000.0
+    eps: float = 1e-5
+    positions: int = 512        # KV-cache capacity (prompt + generated tokens)
+    linear_dtype: int = 5       # Q2_0C
+    embed_dtype: int = 3        # Q6_K
+
+
+def random_weights(cfg, device, seed=0):
+    """Seeded random-init weights of the architecture: N(0, 0.02) linears
+    packed by hy_mt_rs_b200.synth, norms 1 + N(0, 0.02)."""
+    from . import synth
+
+    H, A, KV, F = cfg.hidden, cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim, cfg.ffn
+    g = torch.Generator().manual_seed(seed)
+
+    def norm(n):
+        return (1.0 + 0.02 * torch.randn(n, generator=g)).to(device)
+
+    shapes = {"q": (A, H), "k": (KV, H), "v": (KV, H), "o": (H, A), "gate": (F, H), "up": (F, H), "down": (H, F)}
+    layers = []
+    for i in range(cfg.layers):
+        L = {n: synth.random_packed(cfg.linear_dtype, N, K, seed=seed + 1000 * i + j, device=device)
+             for j, (n, (N, K)) in enumerate(shapes.items())}
+        L.update(input_norm=norm(H), ffn_norm=norm(H), q_norm=norm(cfg.head_dim), k_norm=norm(cfg.head_dim))
+        layers.append(L)
+    embed = synth.random_packed(cfg.embed_dtype, cfg.vocab, H, seed=seed + 7, device=device)
+    return {"layers": layers, "embed": embed, "output_norm": norm(H), "shapes": shapes}
+
+
+def _p(t):
+    return C.c_void_p(t.data_ptr())
+
+
+class DenseModel:
+    def __init__(self, cfg, weights, device):
+        self.cfg = cfg
+        self.device = device
+        H, A, KV, F = cfg.hidden, cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim, cfg.ffn
+        sh = weights["shapes"]
+        self.layers = []
+        for L in weights["layers"]:
+            W = {n: quant.Weight(L[n], cfg.linear_dtype, [sh[n][1], sh[n][0]], name=n) for n in sh}
+            W.update({n: L[n] for n in ("input_norm", "ffn_norm", "q_norm", "k_norm")})
+            W["k_cache"] = torch.zeros(cfg.positions, KV, device=device)
+            W["v_cache"] = torch.zeros(cfg.positions, KV, device=device)
+            self.layers.append(W)
+        self.embed = quant.Weight(weights["embed"], cfg.embed_dtype, [H, cfg.vocab], name="token_embd")
+        self.output_norm = weights["output_norm"]
+        z = lambda n: torch.zeros(n, device=device)  # noqa: E731
+        self.hidden, self.normalized, self.attended = z(H), z(H), z(A)
+        self.projected, self.ff, self.gate = z(H), z(H), z(F)
+        self.q, self.k, self.v, self.logits = z(A), z(KV), z(KV), z(cfg.vocab)
+        self.token = torch.zeros(1, dtype=torch.int32, device=device)
+        self.pos = torch.zeros(1, dtype=torch.int32, device=device)
+        half = cfg.head_dim // 2
+        cos = np.empty(cfg.positions * half, dtype=np.float32)
+        sin = np.empty_like(cos)
+        check(lib.hyq_rope_table(cfg.positions, cfg.head_dim, cfg.rope_base, cos.ctypes.data_as(C.c_void_p),
+                                 sin.ctypes.data_as(C.c_void_p)))
+        self.cos = torch.from_numpy(cos).to(device)
+        self.sin = torch.from_numpy(sin).to(device)
+        self.graph = None
+
+    # ----------------------------------------------------------------- step
+    def _stream(self):
+        return C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+
+    def enqueue_step(self):
+        """One token: reads self.token / self.pos, leaves the logits, the next
+        greedy token in self.token, and pos + 1."""
+        cfg, st = self.cfg, self._stream()
+        H, A, KV = cfg.hidden, cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
+        check(lib.hyq_embed(self.embed.handle, _p(self.token), _p(self.hidden), st))
+        for W in self.layers:
+            check(lib.hyq_rms_norm(_p(self.hidden), _p(W["input_norm"]), H, 1, cfg.eps, _p(self.normalized), st))
+            check(lib.hyq_gemv_qkv(W["q"].handle, W["k"].handle, W["v"].handle, _p(self.normalized), _p(self.q),
+                                   _p(self.k), _p(self.v), st))
+            check(lib.hyq_rope_qk(_p(self.q), _p(self.k), _p(self.v), cfg.heads, cfg.kv_heads, cfg.head_dim,
+                                  _p(self.cos), _p(self.sin), cfg.positions, _p(self.pos), _p(W["q_norm"]),
+                                  _p(W["k_norm"]), cfg.eps, 0, _p(W["k_cache"]), _p(W["v_cache"]), st))
+            check(lib.hyq_attention(_p(self.q), _p(W["k_cache"]), _p(W["v_cache"]), cfg.heads, cfg.kv_heads,
+                                    cfg.head_dim, cfg.positions, _p(self.pos), _p(self.attended), st))
+            check(lib.hyq_matmul(W["o"].handle, _p(self.attended), 1, _p(self.projected), st))
+            check(lib.hyq_add(_p(self.hidden), _p(self.projected), H, st))
+            check(lib.hyq_rms_norm(_p(self.hidden), _p(W["ffn_norm"]), H, 1, cfg.eps, _p(self.normalized), st))
+            check(lib.hyq_matmul_gate_up_silu(W["gate"].handle, W["up"].handle, _p(self.normalized), _p(self.gate),
+                                              st))
+            check(lib.hyq_matmul(W["down"].handle, _p(self.gate), 1, _p(self.ff), st))
+            check(lib.hyq_add(_p(self.hidden), _p(self.ff), H, st))
+        check(lib.hyq_rms_norm(_p(self.hidden), _p(self.output_norm), H, 1, cfg.eps, _p(self.normalized), st))
+        check(lib.hyq_matmul(self.embed.handle, _p(self.normalized), 1, _p(self.logits), st))
+        check(lib.hyq_argmax(_p(self.logits), cfg.vocab, _p(self.token), _p(self.pos), st))
+
+    def capture(self, stream):
+        """Capture enqueue_step as one CUDA graph on `stream`."""
+        quant.set_launch_overlap(True)  # the weights are final; see hyq_set_launch_overlap
+        with torch.cuda.stream(stream):
+            self.pos.zero_()
+            self.enqueue_step()  # warm every path outside the capture
+            stream.synchronize()
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph, stream=stream):
+                self.enqueue_step()
+            self.reset()
+        return self.graph
+
+    def reset(self):
+        self.pos.zero_()
+        for W in self.layers:
+            W["k_cache"].zero_()
+            W["v_cache"].zero_()
+
+    def generate(self, prompt, n_new, stream, logits_out=None):
+        """Greedy decode: feed `prompt` token by token, then `n_new` tokens.
+        Returns the generated ids (and fills logits_out[i] with the logits
+        that chose token i when given)."""
+        if self.graph is None:
+            self.capture(stream)
+        if len(prompt) + n_new > self.cfg.positions:
+            raise ValueError("prompt + generated tokens exceed the KV-cache capacity")
+        out = torch.empty(n_new, dtype=torch.int32, device=self.device)
+        ids = torch.tensor(prompt, dtype=torch.int32).to(self.device)
+        with torch.cuda.stream(stream):
+            self.reset()
+            # after the step of the last prompt token, self.token holds
+            # generated token 0 and self.logits the logits that chose it
+            for i in range(len(prompt)):
+                self.token.copy_(ids[i:i + 1])
+                self.graph.replay()
+            for i in range(n_new):
+                out[i:i + 1].copy_(self.token)
+                if logits_out is not None:
+                    logits_out[i].copy_(self.logits)
+                if i < n_new - 1:
+                    self.graph.replay()
+        stream.synchronize()
+        return out.cpu().tolist()

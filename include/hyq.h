@@ -218,6 +218,48 @@ int hyq_set_launch_overlap(int enable);
  *     on one stream or order them with events. */
 int hyq_matmul_noalloc(const hyq_weight* w, const float* input, int64_t batch, float* out, void* stream);
 
+/* --- Single-token decoder step around the products ----------------------
+ * The rest of Model::forward_into for one token (Dense architecture,
+ * model.rs:374-547), so that a whole step runs on the device and replays as
+ * one CUDA graph: kernels that depend on the position read it from `pos`
+ * (device int32), the embedding reads the token from `token` (device int32),
+ * and hyq_argmax writes the next token there and advances `pos`.  Norms and
+ * attention scores sum in the reference's x86 dot order; the softmax uses the
+ * device exponential. */
+
+/* Rotary tables on the host (model.rs:266-272, 378-391): cos/sin[p * hd/2 + j]
+ * = (p * base^(-2j/hd)).sin_cos() in f32, for p < positions. */
+int hyq_rope_table(int64_t positions, int head_dim, float rope_base, float* cos_out, float* sin_out);
+
+/* rms_norm_into (model.rs:785-830) of `rows` rows of n floats (rows > 1: the
+ * per-head q/k norm, model.rs:832-872): out = x * (1/sqrt(mean(x^2)+eps)) * w. */
+int hyq_rms_norm(const float* x, const float* w, int64_t n, int64_t rows, float eps, float* out, void* stream);
+
+/* Weight::row_into (quant.rs:123-142) of the row *token (device int32). */
+int hyq_embed(const hyq_weight* w, const int32_t* token, float* out, void* stream);
+
+/* RoPE of q [heads, hd] and k [kv_heads, hd] at position *pos (tables from
+ * hyq_rope_table, on the device), the per-head RMSNorm with q_norm/k_norm
+ * after it (Dense, model.rs:435-446) or before it (norm_first: HyV3,
+ * model.rs:425-434; NULL norms skip it), then KvCache::append of k and v
+ * (model.rs:650-667) into row *pos of k_cache/v_cache [positions, kv_heads*hd]. */
+int hyq_rope_qk(float* q, float* k, const float* v, int heads, int kv_heads, int head_dim, const float* cos_tab,
+                const float* sin_tab, int64_t positions, const int32_t* pos, const float* q_norm,
+                const float* k_norm, float eps, int norm_first, float* k_cache, float* v_cache, void* stream);
+
+/* attention_into for one token (model.rs:949-1021) over cache rows 0..*pos
+ * (grouped-query: head h reads kv head h / (heads / kv_heads)).  positions
+ * is the cache capacity (at most 16384). */
+int hyq_attention(const float* q, const float* k_cache, const float* v_cache, int heads, int kv_heads,
+                  int head_dim, int64_t positions, const int32_t* pos, float* out, void* stream);
+
+/* add (model.rs:1043-1071): dst += src. */
+int hyq_add(float* dst, const float* src, int64_t n, void* stream);
+
+/* Greedy token (generation.rs:281-290: first index of the largest value)
+ * into *token; when pos is not NULL, *pos += 1. */
+int hyq_argmax(const float* x, int64_t n, int32_t* token, int32_t* pos, void* stream);
+
 /* --- Tensor-parallel all-reduce over NVLink peer memory ------------------
  * No counterpart in the reference (CPU only).  Sums the row-parallel partial
  * products (O, down) of a tensor-parallel layer across the ranks of one node

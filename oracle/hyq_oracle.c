@@ -573,3 +573,81 @@ int hyo_max_threads(void) {
   return 1;
 #endif
 }
+
+/* ---------------------------------------------------------------------------
+ * Dense decoder step primitives (x86 branches of src/model.rs), for the
+ * full-model decode parity test.  No golden vectors exist for these (the
+ * reference's logits fixtures need its real GGUF files): parity unpinned.
+ * ------------------------------------------------------------------------ */
+
+/* rms_norm_into (model.rs:785-830, x86 loop :827-829):
+ * variance = dot(x, x) / n; scale = recip(sqrt(variance + eps));
+ * out = (x * scale) * w. */
+void hyo_rms_norm(const float* x, const float* w, int64_t n, float eps, float* out) {
+  const float variance = hyo_dot(x, x, (size_t)n) / (float)n;
+  const float scale = 1.0f / sqrtf(variance + eps);
+  for (int64_t i = 0; i < n; ++i) out[i] = x[i] * scale * w[i];
+}
+
+/* rms_norm over rows of width `dim` in place (model.rs:832-872): the
+ * per-head q/k norm of the Dense architecture (model.rs:443-446). */
+void hyo_rms_norm_rows(float* v, int64_t rows, const float* w, int64_t dim, float eps) {
+  for (int64_t r = 0; r < rows; ++r) hyo_rms_norm(v + r * dim, w, dim, eps, v + r * dim);
+}
+
+/* Rotary table for one position (model.rs:378-391): (pos * freq).sin_cos()
+ * with freq_j = rope_base.powf(-2 j / head_dim) (model.rs:266-272). */
+void hyo_rope_table(int64_t pos, int head_dim, float rope_base, float* cos_out, float* sin_out) {
+  for (int j = 0; j < head_dim / 2; ++j) {
+    const float freq = powf(rope_base, -2.0f * (float)j / (float)head_dim);
+    const float a = (float)pos * freq;
+    sin_out[j] = sinf(a);
+    cos_out[j] = cosf(a);
+  }
+}
+
+/* rope_with_cache (model.rs:874-913, x86 loop :907-912), per head of `dim`. */
+void hyo_rope(float* v, int64_t heads, int64_t dim, const float* cos_s, const float* sin_s) {
+  const int64_t half = dim / 2;
+  for (int64_t h = 0; h < heads; ++h) {
+    float* head = v + h * dim;
+    for (int64_t j = 0; j < half; ++j) {
+      const float a = head[j], b = head[j + half];
+      head[j] = a * cos_s[j] - b * sin_s[j];
+      head[j + half] = a * sin_s[j] + b * cos_s[j];
+    }
+  }
+}
+
+/* attention_into for one query token (model.rs:949-1021, x86 branch):
+ * keys/values hold `past + 1` positions of kv_heads * dim floats. */
+void hyo_attention(const float* q, const float* keys, const float* values, int heads, int kv_heads, int dim,
+                   int64_t past, float* out) {
+  const int64_t kv_width = (int64_t)kv_heads * dim;
+  const int repeats = heads / kv_heads;
+  const float scale = 1.0f / sqrtf((float)dim);
+  const int64_t visible = past + 1;
+  float* scores = (float*)malloc(sizeof(float) * (size_t)visible);
+  for (int h = 0; h < heads; ++h) {
+    const int kvh = h / repeats;
+    const float* query = q + (int64_t)h * dim;
+    float* o = out + (int64_t)h * dim;
+    for (int d = 0; d < dim; ++d) o[d] = 0.0f;
+    for (int64_t pos = 0; pos < visible; ++pos)
+      scores[pos] = hyo_dot(query, keys + pos * kv_width + (int64_t)kvh * dim, (size_t)dim) * scale;
+    float max = -INFINITY;
+    for (int64_t pos = 0; pos < visible; ++pos) max = fmaxf(max, scores[pos]);
+    float sum = 0.0f;
+    for (int64_t pos = 0; pos < visible; ++pos) {
+      scores[pos] = expf(scores[pos] - max);
+      sum += scores[pos];
+    }
+    const float inv_sum = 1.0f / sum;
+    for (int64_t pos = 0; pos < visible; ++pos) {
+      const float p = scores[pos] * inv_sum;
+      const float* val = values + pos * kv_width + (int64_t)kvh * dim;
+      for (int d = 0; d < dim; ++d) o[d] += p * val[d];
+    }
+  }
+  free(scores);
+}

@@ -44,6 +44,16 @@ def lib():
         L.hyo_row_dot_q8.argtypes = [C.c_int, _u8p, C.c_int64, _i8p, _f32p, _i8p]
         L.hyo_row_dot_q8.restype = C.c_float
         L.hyo_gemv_q8.argtypes = [C.c_int, _u8p, C.c_int64, C.c_int64, _i8p, _f32p, _i8p, _f32p, C.c_int]
+        L.hyo_rms_norm.argtypes = [_f32p, _f32p, C.c_int64, C.c_float, _f32p]
+        L.hyo_rms_norm.restype = None
+        L.hyo_rms_norm_rows.argtypes = [_f32p, C.c_int64, _f32p, C.c_int64, C.c_float]
+        L.hyo_rms_norm_rows.restype = None
+        L.hyo_rope_table.argtypes = [C.c_int64, C.c_int, C.c_float, _f32p, _f32p]
+        L.hyo_rope_table.restype = None
+        L.hyo_rope.argtypes = [_f32p, C.c_int64, C.c_int64, _f32p, _f32p]
+        L.hyo_rope.restype = None
+        L.hyo_attention.argtypes = [_f32p, _f32p, _f32p, C.c_int, C.c_int, C.c_int, C.c_int64, _f32p]
+        L.hyo_attention.restype = None
         L.hyo_gemv_q8.restype = None
         L.hyo_gate_up_silu_q8.argtypes = [C.c_int, _u8p, _u8p, C.c_int64, C.c_int64, _i8p, _f32p, _i8p,
                                           _f32p, C.c_int]
@@ -171,3 +181,46 @@ def max_threads():
 
 def host_cores():
     return os.cpu_count() or 1
+
+
+# ---------------------------------------------------------------- model step
+def rms_norm(x, w, eps):
+    """rms_norm_into (model.rs:785-830)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty_like(x)
+    lib().hyo_rms_norm(_p(x, _f32p), _p(np.ascontiguousarray(w, dtype=np.float32), _f32p), x.size, eps,
+                       _p(out, _f32p))
+    return out
+
+
+def rms_norm_rows(v, w, eps):
+    """rms_norm per row of len(w) (model.rs:832-872); returns a new array."""
+    v = np.array(v, dtype=np.float32, copy=True)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    lib().hyo_rms_norm_rows(_p(v, _f32p), v.size // w.size, _p(w, _f32p), w.size, eps)
+    return v
+
+
+def rope_table(pos, head_dim, base):
+    """cos, sin for one position (model.rs:266-272, 378-391)."""
+    c = np.empty(head_dim // 2, dtype=np.float32)
+    s = np.empty(head_dim // 2, dtype=np.float32)
+    lib().hyo_rope_table(pos, head_dim, base, _p(c, _f32p), _p(s, _f32p))
+    return c, s
+
+
+def rope(v, heads, dim, cos, sin):
+    """rope_with_cache (model.rs:874-913); returns a new array."""
+    v = np.array(v, dtype=np.float32, copy=True)
+    lib().hyo_rope(_p(v, _f32p), heads, dim, _p(cos, _f32p), _p(sin, _f32p))
+    return v
+
+
+def attention(q, keys, values, heads, kv_heads, dim, past):
+    """attention_into for one token (model.rs:949-1021)."""
+    out = np.empty(heads * dim, dtype=np.float32)
+    lib().hyo_attention(_p(np.ascontiguousarray(q, dtype=np.float32), _f32p),
+                        _p(np.ascontiguousarray(keys, dtype=np.float32), _f32p),
+                        _p(np.ascontiguousarray(values, dtype=np.float32), _f32p), heads, kv_heads, dim, past,
+                        _p(out, _f32p))
+    return out
