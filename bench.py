@@ -52,7 +52,7 @@ def args_parse():
     ap.add_argument("--no-overlap", action="store_true",
                     help="decode: plain stream order instead of overlapped launches (hyq_set_launch_overlap)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
-    ap.add_argument("--workload", choices=["decode", "prefill", "gemv", "tp"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "gemv", "tp", "model"], default="decode",
                     help="decode: config 2 (default line); prefill: config 3 (7B layer GEMMs); "
                          "gemv: config 1 (one 6144x2048 product, L2 defeated by rotating copies)")
     ap.add_argument("--tp-mode", choices=["decode", "prefill"], default="decode",
@@ -895,6 +895,127 @@ def tp_arm(a):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# Full-model greedy decode (config 4): random-init 1.8B architecture
+# ---------------------------------------------------------------------------
+def model_arm(a):
+    import numpy as np
+    import torch
+
+    world, rank, dev = init_ranks()
+    import hy_mt_rs_b200  # noqa: F401
+    from hy_mt_rs_b200 import quant
+    from hy_mt_rs_b200.model import DenseConfig, DenseModel, random_weights
+
+    n_prompt, n_new = 256, 256
+    cfg = DenseConfig(layers=N_LAYERS_MODEL, positions=n_prompt + n_new)
+    weights = random_weights(cfg, dev, seed=1)
+    torch.cuda.synchronize(dev)
+    model = DenseModel(cfg, weights, dev)
+    stream = torch.cuda.Stream(dev)
+    model.capture(stream)
+    prompt = np.random.default_rng(0).integers(0, cfg.vocab, n_prompt).tolist()
+    ids = torch.tensor(prompt, dtype=torch.int32).to(dev)
+    sampler = ClockSampler("GPU-" + str(torch.cuda.get_device_properties(dev).uuid))
+    e0, e1, e1b, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(4))
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, a.warmup)):
+            model.graph.replay()
+        model.reset()
+        e0.record(stream)
+        for i in range(n_prompt):  # the prompt, one step per token
+            model.token.copy_(ids[i:i + 1])
+            model.graph.replay()
+        e1.record(stream)
+        stream.synchronize()
+        sampler.start()
+        e1b.record(stream)
+        for _ in range(n_new - 1):
+            model.graph.replay()
+        e2.record(stream)
+        stream.synchronize()
+        sampler.stop()
+        # e2e: the serving loop reads every new token back to the host
+        model.reset()
+        for i in range(n_prompt):
+            model.token.copy_(ids[i:i + 1])
+            model.graph.replay()
+        # one step of lookahead: step i+1 is enqueued before the host waits
+        # for token i, as a streaming server does (it stops on a token it
+        # has read, one step late)
+        tok_host = torch.empty(n_new, dtype=torch.int32).pin_memory()
+        done = [torch.cuda.Event() for _ in range(n_new)]
+        got = []
+        stream.synchronize()  # the prompt steps are not part of the decode rate
+        t0 = time.perf_counter()
+        for i in range(n_new - 1):
+            model.graph.replay()
+            tok_host[i:i + 1].copy_(model.token, non_blocking=True)
+            done[i].record(stream)
+            if i:
+                done[i - 1].synchronize()
+                got.append(int(tok_host[i - 1]))
+        done[n_new - 2].synchronize()
+        got.append(int(tok_host[n_new - 2]))
+        e2e_s = time.perf_counter() - t0
+    failed = device_failed(quant, dev)
+    (ms_decode, ms_prompt, failed), clocks_all = reduce_over_ranks(
+        [e1b.elapsed_time(e2), e0.elapsed_time(e1), failed + 0.0], sampler.summary(), dev)
+    if failed:
+        raise RuntimeError("a kernel reported an expired bounded wait (device status word) on some rank")
+    model_launches = model.launches()
+    model.graph = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    steps = n_new - 1
+    tok_s = steps / (ms_decode * 1e-3) * world
+    token_bytes = N_LAYERS_MODEL * sum(N * row_bytes(5, K) for _, N, K in LAYER) + VOCAB * row_bytes(3, HIDDEN)
+    peak, peak_kind = measured_peaks()
+    # CPU baseline: the oracle's x86 step on all host cores, a bounded sample
+    from oracle.model import DenseOracle
+    ocfg = DenseConfig(layers=N_LAYERS_MODEL, positions=8)
+    oracle = DenseOracle(ocfg, weights, threads=host_threads())
+    t0 = time.perf_counter()
+    n_cpu = 0
+    while n_cpu < 8 and (n_cpu == 0 or time.perf_counter() - t0 < 20.0):
+        oracle.step(prompt[n_cpu], n_cpu)
+        n_cpu += 1
+    cpu_s = (time.perf_counter() - t0) / n_cpu
+    sm = [c["sm_mhz"] for c in clocks_all if c.get("sm_mhz")]
+    line = {
+        "metric": "decode tokens/s (random-init Hy-MT2-1.8B architecture, Q2_0C linears, Q6_K tied embedding, "
+                  "batch 1, greedy)",
+        "value": round(tok_s, 1), "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": max(3, a.warmup),
+        "ms_per_step": round(ms_decode / steps, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 activations x packed int weights; f32 KV cache",
+        "data": "synthetic (seeded random-init weights, 256 seeded random prompt ids)",
+        "config": {"workload": "hy-mt-rs config 4: 32 layers, hidden 2048, 16/4 heads x 128, SwiGLU 6144, "
+                               "vocab 120832, RoPE 10000; 256-token prompt (one step per token), 256 generated",
+                   "concurrency": 1, "positions": cfg.positions, "launch_overlap": True,
+                   "parallelism": f"replicas x{world}"},
+        "prompt_ms": round(ms_prompt, 2),
+        "weight_gb_s": round(token_bytes / (ms_decode / steps * 1e-3) / 1e9, 1),
+        "roofline": {"bound": "hbm", "kernel": "whole decode step (weights per token)", "unit": "GB/s",
+                     "achieved": round(token_bytes / (ms_decode / steps * 1e-3) / 1e9, 1), "peak": peak,
+                     "peak_kind": peak_kind, "frac": round(token_bytes / (ms_decode / steps * 1e-3) / 1e9 / peak, 4),
+                     "traffic": None, "algorithmic_bytes_per_launch": token_bytes},
+        "e2e": {"value": round(steps / e2e_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 4, "how": "graph replay per token, each token read back to the host one step late"},
+        "gpu_launches": steps * model_launches,
+        "clocks": {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": clocks_all[0].get("sm_max_mhz"),
+                   "reasons": sorted({r for c in clocks_all for r in c.get("reasons", [])}),
+                   "samples": sum(c.get("samples", 0) for c in clocks_all)},
+        "cpu_baseline": {"value": round(1.0 / cpu_s, 3), "unit": "tokens/s", "cores": host_threads(), "kind": "port",
+                         "sample": f"{n_cpu} decode steps of the same model through oracle/model.py (x86 f32 "
+                                   "order, OpenMP)"},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     a = args_parse()
     if a.impl == "reference":
@@ -905,6 +1026,8 @@ def main():
         return gemv_arm(a)
     if a.workload == "tp":
         return tp_arm(a)
+    if a.workload == "model":
+        return model_arm(a)
     return gpu_arm(a)
 
 

@@ -213,6 +213,8 @@ int api_fail(int code, const char* fmt, ...) {
 
 int api_status_word(unsigned** out) { return status_ptr(out); }
 
+bool launch_overlap() { return g_launch_overlap.load(std::memory_order_relaxed) != 0; }
+
 }  // namespace hyq
 
 extern "C" {

@@ -72,5 +72,7 @@ cudaError_t launch_gemm(int dtype, const uint8_t* w, int64_t K, int64_t N, const
 // and return `code`; the current device's status word.
 int api_fail(int code, const char* fmt, ...);
 int api_status_word(unsigned** out);
+// hyq_set_launch_overlap's switch, read at launch time.
+bool launch_overlap();
 
 }  // namespace hyq

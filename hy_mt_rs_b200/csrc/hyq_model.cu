@@ -23,6 +23,24 @@
 namespace hyq {
 namespace model {
 
+// Launch with the programmatic-dependent attribute when hyq_set_launch_overlap
+// is on: every kernel here waits for its predecessor grid before touching
+// memory (griddepcontrol.wait) and lets its own dependents launch at once.
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = launch_overlap() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+}
+
 // dot_avx2 order over n floats, by the 16 lanes [b, b + 16) of a warp (b =
 // lane & 16), one per AVX2 accumulator lane.  Every lane of the group returns
 // the result.  `mask` covers the calling lanes.
@@ -49,6 +67,8 @@ __device__ __forceinline__ float dot_x86(const float* a, const float* b, int n, 
 // eps), out = (x * scale) * w.  One CTA per row.
 __global__ void __launch_bounds__(256) rms_norm_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                         int n, float eps, float* __restrict__ out) {
+  grid_dependency_wait();
+  allow_dependents_launch();
   const float* xr = x + (size_t)blockIdx.x * n;
   float* orow = out + (size_t)blockIdx.x * n;
   __shared__ float scale_s;
@@ -70,6 +90,8 @@ template <int T>
 __global__ void __launch_bounds__(256) embed_kernel(const uint8_t* __restrict__ w, int64_t row_bytes, int64_t n,
                                                      int64_t rows, const int32_t* __restrict__ token,
                                                      float* __restrict__ out, unsigned* status) {
+  grid_dependency_wait();
+  allow_dependents_launch();
   const int64_t tok = *token;
   if (tok < 0 || tok >= rows) {
     if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(status, DEV_BAD_ARGS);
@@ -127,6 +149,8 @@ __device__ void head_rope(float* hd, const float* c, const float* s, int dim) {
 }
 
 __global__ void __launch_bounds__(32) rope_qk_kernel(const __grid_constant__ RopeArgs a) {
+  grid_dependency_wait();
+  allow_dependents_launch();
   const int pos = *a.pos;
   if (pos < 0 || pos >= a.positions) {
     if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(a.status, DEV_BAD_ARGS);
@@ -154,85 +178,170 @@ __global__ void __launch_bounds__(32) rope_qk_kernel(const __grid_constant__ Rop
   }
 }
 
-// attention_into for one query token (model.rs:949-1021): per head, scores
-// over the positions 0..pos (dot in the x86 order, times 1/sqrt(dim)),
-// softmax, and the probability-weighted sum of the values in position order.
-// One CTA of 256 threads per head; scores in shared memory.
+// attention_into for one query token (model.rs:949-1021), split over the
+// cached positions as in flash decoding: CTA (split, head) takes positions
+// [64 split, 64 split + 64) of 0..pos, writes its local max m, exponential
+// sum l and unnormalised output to the workspace, and the last CTA of a head
+// to finish combines them: out = sum_i o_i e^(m_i - M) / sum_i l_i e^(m_i - M).
+// Scores are dot(q, k) * (1 / sqrt(dim)) in the reference's x86 dot order;
+// the exponentials come from the device expf and the sums follow the split
+// tree, so outputs match the reference to rounding, not bit for bit.
 constexpr int kMaxPositions = 16384;
+constexpr int kAttnChunk = 64;
+constexpr int kAttnThreads = 128;
+constexpr int kAttnMaxDim = 256;
 
-__global__ void __launch_bounds__(256) attention_kernel(const float* __restrict__ q,
-                                                         const float* __restrict__ k_cache,
-                                                         const float* __restrict__ v_cache, int heads, int kv_heads,
-                                                         int dim, const int32_t* __restrict__ pos_dev,
-                                                         int positions, float* __restrict__ out, unsigned* status) {
-  extern __shared__ float scores[];
-  __shared__ float red[32];
-  const int pos = *pos_dev;
-  if (pos < 0 || pos >= positions || pos >= kMaxPositions) {
-    if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(status, DEV_BAD_ARGS);
+// Per-head counters at the head of the workspace, padded to 256 bytes.
+inline size_t attn_counter_bytes(int heads) { return ((size_t)heads * sizeof(unsigned) + 255) / 256 * 256; }
+
+struct AttnArgs {
+  const float* q;
+  const float* k_cache;
+  const float* v_cache;
+  int heads, kv_heads, dim;
+  const int32_t* pos;
+  int positions;
+  float* out;
+  float* ws;           // [heads][splits][2 + dim]
+  unsigned* counters;  // [heads], zero between calls
+  unsigned* status;
+};
+
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_constant__ AttnArgs a) {
+  grid_dependency_wait();
+  allow_dependents_launch();
+  __shared__ float q_s[kAttnMaxDim];
+  __shared__ float e_s[kAttnChunk];
+  __shared__ float cw_s[kMaxPositions / kAttnChunk];
+  __shared__ float bc[2];
+  __shared__ int last_s;
+  const int pos = *a.pos;
+  if (pos < 0 || pos >= a.positions) {
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) atomicOr(a.status, DEV_BAD_ARGS);
     return;
   }
   const int visible = pos + 1;
-  const int h = blockIdx.x;
-  const int kvh = h / (heads / kv_heads);
-  const size_t width = (size_t)kv_heads * dim;
-  const float* query = q + (size_t)h * dim;
+  const int used = (visible + kAttnChunk - 1) / kAttnChunk;  // splits with positions
+  const int split = blockIdx.x, h = blockIdx.y;
+  if (split >= used) return;
+  const int dim = a.dim;
+  const int kvh = h / (a.heads / a.kv_heads);
+  const size_t width = (size_t)a.kv_heads * dim;
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)dim));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // scores: a warp takes the pair of positions 2 pp, 2 pp + 1, one per
-  // half-warp (whole-warp shuffles; a position past the end reads position 0
-  // and is discarded)
-  const int nwarps = blockDim.x >> 5;
-  for (int pp = warp; 2 * pp < visible; pp += nwarps) {
-    const int p = 2 * pp + (lane >> 4);
-    const bool valid = p < visible;
-    const int pr = valid ? p : 0;
-    const float d = dot_x86(query, k_cache + (size_t)pr * width + (size_t)kvh * dim, dim, 0xffffffffu);
-    if (valid && (lane & 15) == 0) scores[p] = __fmul_rn(d, scale);
+  for (int d = threadIdx.x; d < dim; d += kAttnThreads) q_s[d] = a.q[(size_t)h * dim + d];
+  __syncthreads();
+  const int p0 = split * kAttnChunk;
+  const int n = min(kAttnChunk, visible - p0);
+  // scores of this chunk in the x86 dot order: a half-warp per position
+  for (int base = 2 * warp; base < n; base += kAttnThreads / 16) {
+    const int i = base + (lane >> 4);
+    const bool valid = i < n;
+    const float* kr = a.k_cache + (size_t)(p0 + (valid ? i : 0)) * width + (size_t)kvh * dim;
+    const float d = dot_x86(q_s, kr, dim, 0xffffffffu);
+    if (valid && (lane & 15) == 0) e_s[i] = __fmul_rn(d, scale);
   }
   __syncthreads();
-  // max
-  float m = -INFINITY;
-  for (int p = threadIdx.x; p < visible; p += blockDim.x) m = fmaxf(m, scores[p]);
-  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if (lane == 0) red[warp] = m;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float mm = red[0];
-    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) mm = fmaxf(mm, red[w]);
-    red[31] = mm;
+  // local max and exponentials
+  if (warp == 0) {
+    float m = -INFINITY;
+    for (int i = lane; i < n; i += 32) m = fmaxf(m, e_s[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float l = 0.f;
+    for (int i = lane; i < n; i += 32) {
+      const float e = expf(__fsub_rn(e_s[i], m));
+      e_s[i] = e;
+      l += e;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    if (lane == 0) {
+      bc[0] = m;
+      bc[1] = l;
+    }
   }
   __syncthreads();
-  m = red[31];
-  __syncthreads();
-  // exponentials and their sum (in position order, by one warp per 32
-  // positions, then a fixed-order sum of the warp totals)
-  for (int p = threadIdx.x; p < visible; p += blockDim.x) scores[p] = expf(__fsub_rn(scores[p], m));
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float sum = 0.f;
-    for (int p = 0; p < visible; ++p) sum = __fadd_rn(sum, scores[p]);
-    red[30] = __fdiv_rn(1.0f, sum);
-  }
-  __syncthreads();
-  const float inv_sum = red[30];
-  for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+  const int nsplit = (a.positions + kAttnChunk - 1) / kAttnChunk;
+  float* w = a.ws + ((size_t)h * nsplit + split) * (2 + dim);
+  for (int d = threadIdx.x; d < dim; d += kAttnThreads) {
+    const float* vr = a.v_cache + (size_t)p0 * width + (size_t)kvh * dim + d;
     float o = 0.f;
-    for (int p = 0; p < visible; ++p)
-      o = __fadd_rn(o, __fmul_rn(__fmul_rn(scores[p], inv_sum), v_cache[(size_t)p * width + (size_t)kvh * dim + d]));
-    out[(size_t)h * dim + d] = o;
+    for (int i = 0; i < n; ++i) o = fmaf(e_s[i], vr[(size_t)i * width], o);
+    w[2 + d] = o;
   }
+  if (threadIdx.x == 0) {
+    w[0] = bc[0];
+    w[1] = bc[1];
+  }
+  // the last CTA of this head combines the splits
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last_s = atomicAdd(&a.counters[h], 1u) == (unsigned)(used - 1);
+  __syncthreads();
+  if (!last_s) return;
+  __threadfence();
+  // partials of other CTAs are read past L1 (__ldcg)
+  const float* wh = a.ws + (size_t)h * nsplit * (2 + dim);
+  const size_t stride = 2 + (size_t)dim;
+  if (warp == 0) {
+    float m = -INFINITY;
+    for (int i = lane; i < used; i += 32) m = fmaxf(m, __ldcg(wh + i * stride));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float l = 0.f;
+    for (int i = lane; i < used; i += 32) {
+      const float c = expf(__ldcg(wh + i * stride) - m);
+      cw_s[i] = c;
+      l = fmaf(__ldcg(wh + i * stride + 1), c, l);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    if (lane == 0) bc[1] = 1.0f / l;
+  }
+  __syncthreads();
+  const float inv = bc[1];
+  for (int d = threadIdx.x; d < dim; d += kAttnThreads) {
+    float o = 0.f;
+    for (int i = 0; i < used; ++i) o = fmaf(__ldcg(wh + i * stride + 2 + d), cw_s[i], o);
+    a.out[(size_t)h * dim + d] = o * inv;
+  }
+  if (threadIdx.x == 0) a.counters[h] = 0;  // ready for the next call
 }
 
 __global__ void __launch_bounds__(256) add_kernel(float* __restrict__ dst, const float* __restrict__ src, int64_t n) {
+  grid_dependency_wait();
+  allow_dependents_launch();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) dst[i] = __fadd_rn(dst[i], src[i]);
+}
+
+// add (model.rs:1043-1071) followed by rms_norm_into (model.rs:785-830) of
+// the sum: hidden += delta; out = (hidden * scale) * w.  One CTA.
+__global__ void __launch_bounds__(256) add_rms_norm_kernel(float* __restrict__ hidden,
+                                                            const float* __restrict__ delta,
+                                                            const float* __restrict__ w, int n, float eps,
+                                                            float* __restrict__ out) {
+  grid_dependency_wait();
+  allow_dependents_launch();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) hidden[i] = __fadd_rn(hidden[i], delta[i]);
+  __syncthreads();
+  __shared__ float scale_s;
+  if (threadIdx.x < 16) {
+    const float d = dot_x86(hidden, hidden, n, 0xffffu);
+    if (threadIdx.x == 0) scale_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(d, (float)n), eps)));
+  }
+  __syncthreads();
+  const float scale = scale_s;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(hidden[i], scale), w[i]);
 }
 
 // Greedy token (generation.rs:281-290): the first index of the largest value.
 // One CTA; optionally advances the position counter.
 __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ x, int64_t n, int32_t* token,
                                                        int32_t* pos) {
+  grid_dependency_wait();
+  allow_dependents_launch();
   float best = -INFINITY;
   int64_t idx = n;
   for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
@@ -296,8 +405,9 @@ int hyq_rope_table(int64_t positions, int head_dim, float rope_base, float* cos_
 int hyq_rms_norm(const float* x, const float* w, int64_t n, int64_t rows, float eps, float* out, void* stream) {
   if (!x || !w || !out) return hyq::api_fail(HYQ_E_INVALID, "rms_norm: null pointer");
   if (n <= 0 || rows <= 0 || n > INT32_MAX || rows > INT32_MAX) return hyq::api_fail(HYQ_E_SHAPE, "rms_norm: shape");
-  hyq::model::rms_norm_kernel<<<(unsigned)rows, 256, 0, (cudaStream_t)stream>>>(x, w, (int)n, eps, out);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e =
+      hyq::model::launch(hyq::model::rms_norm_kernel, dim3((unsigned)rows), dim3(256), 0, (cudaStream_t)stream, x, w,
+                         (int)n, eps, out);
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "rms_norm: %s", cudaGetErrorString(e));
 }
 
@@ -316,16 +426,16 @@ int hyq_embed(const hyq_weight* w, const int32_t* token, float* out, void* strea
   const unsigned blocks = (unsigned)((n + 255) / 256);
   cudaStream_t st = (cudaStream_t)stream;
   const uint8_t* wd = static_cast<const uint8_t*>(data);
+  cudaError_t e = cudaSuccess;
   switch (dtype) {
-    case hyq::F32: hyq::model::embed_kernel<hyq::F32><<<blocks, 256, 0, st>>>(wd, rb, n, rows, token, out, status); break;
-    case hyq::F16: hyq::model::embed_kernel<hyq::F16><<<blocks, 256, 0, st>>>(wd, rb, n, rows, token, out, status); break;
-    case hyq::Q4_K: hyq::model::embed_kernel<hyq::Q4_K><<<blocks, 256, 0, st>>>(wd, rb, n, rows, token, out, status); break;
-    case hyq::Q6_K: hyq::model::embed_kernel<hyq::Q6_K><<<blocks, 256, 0, st>>>(wd, rb, n, rows, token, out, status); break;
-    case hyq::Q8_0: hyq::model::embed_kernel<hyq::Q8_0><<<blocks, 256, 0, st>>>(wd, rb, n, rows, token, out, status); break;
-    case hyq::Q2_0C: hyq::model::embed_kernel<hyq::Q2_0C><<<blocks, 256, 0, st>>>(wd, rb, n, rows, token, out, status); break;
-    default: hyq::model::embed_kernel<hyq::STQ1_0><<<blocks, 256, 0, st>>>(wd, rb, n, rows, token, out, status); break;
+    case hyq::F32: e = hyq::model::launch(hyq::model::embed_kernel<hyq::F32>, dim3(blocks), dim3(256), 0, st, wd, rb, n, rows, token, out, status); break;
+    case hyq::F16: e = hyq::model::launch(hyq::model::embed_kernel<hyq::F16>, dim3(blocks), dim3(256), 0, st, wd, rb, n, rows, token, out, status); break;
+    case hyq::Q4_K: e = hyq::model::launch(hyq::model::embed_kernel<hyq::Q4_K>, dim3(blocks), dim3(256), 0, st, wd, rb, n, rows, token, out, status); break;
+    case hyq::Q6_K: e = hyq::model::launch(hyq::model::embed_kernel<hyq::Q6_K>, dim3(blocks), dim3(256), 0, st, wd, rb, n, rows, token, out, status); break;
+    case hyq::Q8_0: e = hyq::model::launch(hyq::model::embed_kernel<hyq::Q8_0>, dim3(blocks), dim3(256), 0, st, wd, rb, n, rows, token, out, status); break;
+    case hyq::Q2_0C: e = hyq::model::launch(hyq::model::embed_kernel<hyq::Q2_0C>, dim3(blocks), dim3(256), 0, st, wd, rb, n, rows, token, out, status); break;
+    default: e = hyq::model::launch(hyq::model::embed_kernel<hyq::STQ1_0>, dim3(blocks), dim3(256), 0, st, wd, rb, n, rows, token, out, status); break;
   }
-  const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "embed: %s", cudaGetErrorString(e));
 }
 
@@ -356,46 +466,72 @@ int hyq_rope_qk(float* q, float* k, const float* v, int heads, int kv_heads, int
   a.v_cache = v_cache;
   int rc = hyq::api_status_word(&a.status);
   if (rc) return rc;
-  hyq::model::rope_qk_kernel<<<(unsigned)(heads + kv_heads), 32, 0, (cudaStream_t)stream>>>(a);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e = hyq::model::launch(hyq::model::rope_qk_kernel, dim3((unsigned)(heads + kv_heads)), dim3(32), 0,
+                                           (cudaStream_t)stream, a);
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "rope_qk: %s", cudaGetErrorString(e));
 }
 
+int hyq_attention_workspace_bytes(int heads, int head_dim, int64_t positions, size_t* bytes) {
+  if (!bytes) return hyq::api_fail(HYQ_E_INVALID, "attention_workspace_bytes: null pointer");
+  if (heads <= 0 || head_dim <= 0 || positions <= 0)
+    return hyq::api_fail(HYQ_E_SHAPE, "attention_workspace_bytes: shape");
+  const int64_t splits = (positions + hyq::model::kAttnChunk - 1) / hyq::model::kAttnChunk;
+  *bytes = hyq::model::attn_counter_bytes(heads) + (size_t)heads * splits * (2 + head_dim) * sizeof(float);
+  return HYQ_OK;
+}
+
 int hyq_attention(const float* q, const float* k_cache, const float* v_cache, int heads, int kv_heads,
-                  int head_dim, int64_t positions, const int32_t* pos, float* out, void* stream) {
-  if (!q || !k_cache || !v_cache || !pos || !out) return hyq::api_fail(HYQ_E_INVALID, "attention: null pointer");
-  if (heads <= 0 || kv_heads <= 0 || heads % kv_heads || head_dim <= 0 || positions <= 0 ||
-      positions > hyq::model::kMaxPositions)
-    return hyq::api_fail(HYQ_E_SHAPE, "attention: shape (at most %d positions)", hyq::model::kMaxPositions);
-  unsigned* status = nullptr;
-  int rc = hyq::api_status_word(&status);
+                  int head_dim, int64_t positions, const int32_t* pos, float* out, void* workspace,
+                  void* stream) {
+  if (!q || !k_cache || !v_cache || !pos || !out || !workspace)
+    return hyq::api_fail(HYQ_E_INVALID, "attention: null pointer");
+  if (heads <= 0 || kv_heads <= 0 || heads % kv_heads || head_dim <= 0 || head_dim > hyq::model::kAttnMaxDim ||
+      positions <= 0 || positions > hyq::model::kMaxPositions)
+    return hyq::api_fail(HYQ_E_SHAPE, "attention: shape (head_dim at most %d, at most %d positions)",
+                         hyq::model::kAttnMaxDim, hyq::model::kMaxPositions);
+  if (reinterpret_cast<uintptr_t>(workspace) % 16) return hyq::api_fail(HYQ_E_INVALID, "attention: workspace alignment");
+  hyq::model::AttnArgs a{};
+  a.q = q;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.heads = heads;
+  a.kv_heads = kv_heads;
+  a.dim = head_dim;
+  a.pos = pos;
+  a.positions = (int)positions;
+  a.out = out;
+  a.counters = static_cast<unsigned*>(workspace);
+  a.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + hyq::model::attn_counter_bytes(heads));
+  int rc = hyq::api_status_word(&a.status);
   if (rc) return rc;
-  const size_t smem = (size_t)positions * sizeof(float);
-  static int configured = 0;
-  if (!configured) {
-    cudaFuncSetAttribute(hyq::model::attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         hyq::model::kMaxPositions * (int)sizeof(float));
-    configured = 1;
-  }
-  hyq::model::attention_kernel<<<(unsigned)heads, 256, smem, (cudaStream_t)stream>>>(
-      q, k_cache, v_cache, heads, kv_heads, head_dim, pos, (int)positions, out, status);
-  const cudaError_t e = cudaGetLastError();
+  const unsigned splits = (unsigned)((positions + hyq::model::kAttnChunk - 1) / hyq::model::kAttnChunk);
+  const cudaError_t e = hyq::model::launch(hyq::model::attention_kernel, dim3(splits, (unsigned)heads),
+                                           dim3(hyq::model::kAttnThreads), 0, (cudaStream_t)stream, a);
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "attention: %s", cudaGetErrorString(e));
 }
 
 int hyq_add(float* dst, const float* src, int64_t n, void* stream) {
   if (!dst || !src) return hyq::api_fail(HYQ_E_INVALID, "add: null pointer");
   if (n <= 0) return n == 0 ? HYQ_OK : hyq::api_fail(HYQ_E_SHAPE, "add: negative length");
-  hyq::model::add_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(dst, src, n);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e = hyq::model::launch(hyq::model::add_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0,
+                                           (cudaStream_t)stream, dst, src, n);
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "add: %s", cudaGetErrorString(e));
+}
+
+int hyq_add_rms_norm(float* hidden, const float* delta, const float* w, int64_t n, float eps, float* out,
+                     void* stream) {
+  if (!hidden || !delta || !w || !out) return hyq::api_fail(HYQ_E_INVALID, "add_rms_norm: null pointer");
+  if (n <= 0 || n > INT32_MAX) return hyq::api_fail(HYQ_E_SHAPE, "add_rms_norm: length");
+  const cudaError_t e = hyq::model::launch(hyq::model::add_rms_norm_kernel, dim3(1), dim3(256), 0,
+                                           (cudaStream_t)stream, hidden, delta, w, (int)n, eps, out);
+  return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "add_rms_norm: %s", cudaGetErrorString(e));
 }
 
 int hyq_argmax(const float* x, int64_t n, int32_t* token, int32_t* pos, void* stream) {
   if (!x || !token) return hyq::api_fail(HYQ_E_INVALID, "argmax: null pointer");
   if (n <= 0 || n > INT32_MAX) return hyq::api_fail(HYQ_E_SHAPE, "argmax: length");
-  hyq::model::argmax_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(x, n, token, pos);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e =
+      hyq::model::launch(hyq::model::argmax_kernel, dim3(1), dim3(1024), 0, (cudaStream_t)stream, x, n, token, pos);
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "argmax: %s", cudaGetErrorString(e));
 }
 

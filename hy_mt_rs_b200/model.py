@@ -89,6 +89,10 @@ class DenseModel:
                                  sin.ctypes.data_as(C.c_void_p)))
         self.cos = torch.from_numpy(cos).to(device)
         self.sin = torch.from_numpy(sin).to(device)
+        ws = C.c_size_t()
+        check(lib.hyq_attention_workspace_bytes(cfg.heads, cfg.head_dim, cfg.positions, C.byref(ws)))
+        # split partials + per-head counters; zero once, every call leaves it zero
+        self.attn_ws = torch.zeros(ws.value, dtype=torch.uint8, device=device)
         self.graph = None
 
     # ----------------------------------------------------------------- step
@@ -101,25 +105,32 @@ class DenseModel:
         cfg, st = self.cfg, self._stream()
         H, A, KV = cfg.hidden, cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
         check(lib.hyq_embed(self.embed.handle, _p(self.token), _p(self.hidden), st))
-        for W in self.layers:
-            check(lib.hyq_rms_norm(_p(self.hidden), _p(W["input_norm"]), H, 1, cfg.eps, _p(self.normalized), st))
+        check(lib.hyq_rms_norm(_p(self.hidden), _p(self.layers[0]["input_norm"]), H, 1, cfg.eps, _p(self.normalized),
+                               st))
+        for i, W in enumerate(self.layers):
             check(lib.hyq_gemv_qkv(W["q"].handle, W["k"].handle, W["v"].handle, _p(self.normalized), _p(self.q),
                                    _p(self.k), _p(self.v), st))
             check(lib.hyq_rope_qk(_p(self.q), _p(self.k), _p(self.v), cfg.heads, cfg.kv_heads, cfg.head_dim,
                                   _p(self.cos), _p(self.sin), cfg.positions, _p(self.pos), _p(W["q_norm"]),
                                   _p(W["k_norm"]), cfg.eps, 0, _p(W["k_cache"]), _p(W["v_cache"]), st))
             check(lib.hyq_attention(_p(self.q), _p(W["k_cache"]), _p(W["v_cache"]), cfg.heads, cfg.kv_heads,
-                                    cfg.head_dim, cfg.positions, _p(self.pos), _p(self.attended), st))
+                                    cfg.head_dim, cfg.positions, _p(self.pos), _p(self.attended), _p(self.attn_ws),
+                                    st))
             check(lib.hyq_matmul(W["o"].handle, _p(self.attended), 1, _p(self.projected), st))
-            check(lib.hyq_add(_p(self.hidden), _p(self.projected), H, st))
-            check(lib.hyq_rms_norm(_p(self.hidden), _p(W["ffn_norm"]), H, 1, cfg.eps, _p(self.normalized), st))
+            # residual add fused with the norm that follows it
+            check(lib.hyq_add_rms_norm(_p(self.hidden), _p(self.projected), _p(W["ffn_norm"]), H, cfg.eps,
+                                       _p(self.normalized), st))
             check(lib.hyq_matmul_gate_up_silu(W["gate"].handle, W["up"].handle, _p(self.normalized), _p(self.gate),
                                               st))
             check(lib.hyq_matmul(W["down"].handle, _p(self.gate), 1, _p(self.ff), st))
-            check(lib.hyq_add(_p(self.hidden), _p(self.ff), H, st))
-        check(lib.hyq_rms_norm(_p(self.hidden), _p(self.output_norm), H, 1, cfg.eps, _p(self.normalized), st))
+            nxt = self.layers[i + 1]["input_norm"] if i + 1 < len(self.layers) else self.output_norm
+            check(lib.hyq_add_rms_norm(_p(self.hidden), _p(self.ff), _p(nxt), H, cfg.eps, _p(self.normalized), st))
         check(lib.hyq_matmul(self.embed.handle, _p(self.normalized), 1, _p(self.logits), st))
         check(lib.hyq_argmax(_p(self.logits), cfg.vocab, _p(self.token), _p(self.pos), st))
+
+    # kernel launches of one enqueue_step
+    def launches(self):
+        return 2 + 8 * self.cfg.layers + 2
 
     def capture(self, stream):
         """Capture enqueue_step as one CUDA graph on `stream`."""

@@ -249,12 +249,25 @@ int hyq_rope_qk(float* q, float* k, const float* v, int heads, int kv_heads, int
 
 /* attention_into for one token (model.rs:949-1021) over cache rows 0..*pos
  * (grouped-query: head h reads kv head h / (heads / kv_heads)).  positions
- * is the cache capacity (at most 16384). */
+ * is the cache capacity (at most 16384), head_dim at most 256.  The cached
+ * positions are split into chunks of 64 whose partial softmax sums are
+ * combined on the device; `workspace` holds those partials and one counter
+ * per head: hyq_attention_workspace_bytes bytes, zero before the first call
+ * (every call leaves it zero again).  Calls that share a workspace must not
+ * overlap in time. */
+int hyq_attention_workspace_bytes(int heads, int head_dim, int64_t positions, size_t* bytes);
 int hyq_attention(const float* q, const float* k_cache, const float* v_cache, int heads, int kv_heads,
-                  int head_dim, int64_t positions, const int32_t* pos, float* out, void* stream);
+                  int head_dim, int64_t positions, const int32_t* pos, float* out, void* workspace,
+                  void* stream);
 
 /* add (model.rs:1043-1071): dst += src. */
 int hyq_add(float* dst, const float* src, int64_t n, void* stream);
+
+/* The residual add followed by the next rms_norm_into (model.rs:1043-1071,
+ * 785-830) in one launch: hidden += delta; out = hidden * scale * w, with
+ * scale from the updated hidden. */
+int hyq_add_rms_norm(float* hidden, const float* delta, const float* w, int64_t n, float eps, float* out,
+                     void* stream);
 
 /* Greedy token (generation.rs:281-290: first index of the largest value)
  * into *token; when pos is not NULL, *pos += 1. */

@@ -46,3 +46,60 @@ def test_dense_decode_matches_oracle(cuda):
     # the same stream again from the same graph (KV caches and position reset)
     again = model.generate(prompt, n_new, stream)
     assert again == ids
+
+
+@pytest.mark.parametrize("pos", [0, 63, 64, 777, 4095])
+def test_attention_splits_match_oracle(cuda, pos):
+    """hyq_attention over 64-position splits (one to 64 of them) against the
+    oracle's single-pass softmax (model.rs:949-1021); two calls in a row on
+    the same workspace, so the per-head counters are seen to reset."""
+    import ctypes as C
+    import torch
+    from hy_mt_rs_b200._native import check, lib
+    from oracle import oracle as O
+
+    heads, kv_heads, dim, positions = 16, 4, 128, 4096
+    g = torch.Generator().manual_seed(pos)
+    q = torch.randn(heads * dim, generator=g)
+    kc = torch.randn(positions, kv_heads * dim, generator=g)
+    vc = torch.randn(positions, kv_heads * dim, generator=g)
+    ws = C.c_size_t()
+    check(lib.hyq_attention_workspace_bytes(heads, dim, positions, C.byref(ws)))
+    work = torch.zeros(ws.value, dtype=torch.uint8, device=cuda)
+    d = [t.to(cuda) for t in (q, kc, vc)]
+    p = torch.tensor([pos], dtype=torch.int32, device=cuda)
+    outs = []
+    for _ in range(2):
+        out = torch.full((heads * dim,), float("nan"), device=cuda)
+        check(lib.hyq_attention(*(C.c_void_p(t.data_ptr()) for t in d), heads, kv_heads, dim, positions,
+                                C.c_void_p(p.data_ptr()), C.c_void_p(out.data_ptr()), C.c_void_p(work.data_ptr()),
+                                C.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)))
+        outs.append(out.cpu().numpy())
+    torch.cuda.synchronize()
+    ref = O.attention(q.numpy(), kc[:pos + 1].numpy(), vc[:pos + 1].numpy(), heads, kv_heads, dim, pos)
+    np.testing.assert_allclose(outs[0], ref, rtol=2e-5, atol=2e-6)
+    np.testing.assert_array_equal(outs[0], outs[1])
+    counters = work[:heads * 4].cpu().numpy()
+    assert not counters.any()
+
+
+def test_add_rms_norm_bit_exact(cuda):
+    """hyq_add_rms_norm = the residual add then rms_norm_into (model.rs:
+    1043-1071, 785-830), bit for bit against the oracle's x86 order."""
+    import ctypes as C
+    import torch
+    from hy_mt_rs_b200._native import check, lib
+    from oracle import oracle as O
+
+    n = 2048
+    g = torch.Generator().manual_seed(5)
+    h, dlt, w = (torch.randn(n, generator=g) for _ in range(3))
+    hd, dd, wd = (t.to(cuda) for t in (h, dlt, w))
+    out = torch.empty(n, device=cuda)
+    check(lib.hyq_add_rms_norm(C.c_void_p(hd.data_ptr()), C.c_void_p(dd.data_ptr()), C.c_void_p(wd.data_ptr()), n,
+                               1e-5, C.c_void_p(out.data_ptr()),
+                               C.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)))
+    torch.cuda.synchronize()
+    s = (h.numpy() + dlt.numpy()).astype(np.float32)
+    np.testing.assert_array_equal(hd.cpu().numpy(), s)
+    np.testing.assert_array_equal(out.cpu().numpy(), O.rms_norm(s, w.numpy(), 1e-5))
