@@ -66,8 +66,10 @@ __device__ __forceinline__ float decode_elem(const uint8_t* __restrict__ x, int 
 // STQ1_0 codebook (quant.rs:1081-1123) looked up for four groups at once:
 // `hw` holds their four 4-bit nibble codes, `s4` their four sign bits; byte
 // b of the result is the 4-digit pattern (2 bits per lane p, digit - 1 =
-// weight / d) of group b.  PRMT reads the 32-entry codebook from eight
-// register tables; byte masks choose by nibble bit 3 and by the sign bit.
+// weight / d) of group b.  The sign-1 half of the table is the digit-wise
+// negation of the sign-0 half (entry 16 + n = 0xaa - entry n), so PRMT reads
+// the 16 sign-0 entries from four register tables, a byte mask picks the half
+// by nibble bit 3, and the sign swaps each digit d for 2 - d.
 __device__ __forceinline__ uint32_t prmt_b32(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t d;
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
@@ -76,15 +78,12 @@ __device__ __forceinline__ uint32_t prmt_b32(uint32_t a, uint32_t b, uint32_t se
 
 __device__ __forceinline__ uint32_t stq_patterns4(uint32_t hw, uint32_t s4) {
   const uint32_t T0 = 0x092989a9u, T1 = 0x062686a6u, T2 = 0x121a929au, T3 = 0x424a626au;
-  const uint32_t T4 = 0xa1812101u, T5 = 0xa4842404u, T6 = 0x98901810u, T7 = 0x68604840u;
   const uint32_t sel = hw & 0x7777u;
   const uint32_t p0 = prmt_b32(T0, T1, sel), p1 = prmt_b32(T2, T3, sel);
-  const uint32_t p2 = prmt_b32(T4, T5, sel), p3 = prmt_b32(T6, T7, sel);
-  const uint32_t m3 = prmt_b32(hw << 4, hw, 0xD9C8u);
-  const uint32_t sm = prmt_b32(s4 * 0x10204080u, 0u, 0xBA98u);
-  const uint32_t lo = (p0 & ~m3) | (p1 & m3);
-  const uint32_t hi = (p2 & ~m3) | (p3 & m3);
-  return (lo & ~sm) | (hi & sm);
+  const uint32_t m3 = prmt_b32(hw << 4, hw, 0xD9C8u);           // 0xff where nibble bit 3 is set
+  const uint32_t sm = prmt_b32(s4 * 0x10204080u, 0u, 0xBA98u);  // 0xff where the sign bit is set
+  const uint32_t cb = (p0 & ~m3) | (p1 & m3);
+  return cb ^ (sm & (cb ^ (0xaaaaaaaau - cb)));
 }
 
 }  // namespace hyq

@@ -9,6 +9,8 @@
 // make_plan chooses the streaming kernel's geometry (hyq_gemv_impl.cuh) or
 // the per-element fallback for shapes and pointers the streaming kernel does
 // not take.
+#include <cstdlib>
+
 #include "hyq_gemv_impl.cuh"
 
 namespace hyq {
@@ -87,16 +89,31 @@ __global__ void __launch_bounds__(256) gemv_fallback_kernel(const __grid_constan
 
 int g_num_sms = 0;
 int g_smem_optin = 0;
+int g_smem_dual = 0;  // dynamic shared memory per CTA with two CTAs per SM
 
 void device_limits() {
   int dev = 0;
   cudaGetDevice(&dev);
   static int cached_dev = -1;
   if (cached_dev != dev) {
+    int per_sm = 0, reserved = 0;
     cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
     cudaDeviceGetAttribute(&g_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+    g_smem_dual = (per_sm / 2 - reserved) / 1024 * 1024;
+    if (g_smem_dual > g_smem_optin) g_smem_dual = g_smem_optin;
     cached_dev = dev;
   }
+}
+
+// HYQ_GEMV_DUAL=0 keeps one CTA per SM for every variant (for comparisons).
+bool dual_enabled() {
+  static const int on = [] {
+    const char* e = getenv("HYQ_GEMV_DUAL");
+    return (e && e[0] == '0') ? 0 : 1;
+  }();
+  return on != 0;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -136,14 +153,25 @@ Plan make_plan(const GemvJob& j) {
     const int upl = (slice + 31) / 32;
     if (upl > upl_max) continue;
     const int rg = kCW / ks;
+    // Two CTAs share an SM for the variants built for it (dual_variant) when
+    // every CTA still gets at least two tiles; small products keep one CTA
+    // per SM.
+    int per_sm = 1;
+    if (dual_enabled() && dual_variant(t, np, upl, pair)) {
+      int64_t tiles = 0;
+      for (int m = 0; m < j.n_mat; ++m) tiles += (j.rows[m] + rg - 1) / rg;  // at rw = 1
+      per_sm = tiles >= (int64_t)4 * 4 * g_num_sms ? 2 : 1;  // >= 2 tiles per CTA at rw = 4
+    }
+    const int cap = per_sm == 2 ? g_smem_dual : smem_cap;
     for (int rw : kRows) {
       const int R = rg * rw;
       const int64_t half = ((int64_t)R * row_bytes + 32 + 15) / 16 * 16;
       const int64_t stage = half * (pair ? 2 : 1);
-      if (stage_off + 2 * stage > smem_cap) continue;
+      if (stage_off + 2 * stage > cap) continue;
       int64_t batches = 0;
       for (int m = 0; m < j.n_mat; ++m) batches += (j.rows[m] + R - 1) / R;
-      const int64_t waves = (batches + g_num_sms - 1) / g_num_sms;
+      const int64_t ctas = (int64_t)g_num_sms * per_sm;
+      const int64_t waves = (batches + ctas - 1) / ctas;
       const int64_t cost = waves * (rw * upl * (pair ? 2 : 1) + 1);
       if (best < 0 || cost < best) {
         best = cost;
@@ -153,6 +181,7 @@ Plan make_plan(const GemvJob& j) {
         pl.rw = rw;
         pl.half_bytes = (int)half;
         pl.stage_bytes = (int)stage;
+        pl.ctas_per_sm = per_sm;
       }
     }
   }
@@ -163,20 +192,22 @@ Plan make_plan(const GemvJob& j) {
     pl.batch_begin[m] = pl.total_batches;
     pl.total_batches += (j.rows[m] + R - 1) / R;
   }
-  int stages = (int)((smem_cap - stage_off) / pl.stage_bytes);
+  const int cap = pl.ctas_per_sm == 2 ? g_smem_dual : smem_cap;
+  const int64_t max_grid = (int64_t)g_num_sms * pl.ctas_per_sm;
+  int stages = (int)((cap - stage_off) / pl.stage_bytes);
   if (stages > kMaxStages) stages = kMaxStages;
   // No more stages than a CTA has tiles (plus one): small products then
   // initialise fewer barriers and claim less shared memory.
   {
-    const int64_t grid = pl.total_batches < g_num_sms ? pl.total_batches : g_num_sms;
+    const int64_t grid = pl.total_batches < max_grid ? pl.total_batches : max_grid;
     const int64_t per_cta = grid > 0 ? (pl.total_batches + grid - 1) / grid : 1;
     if (per_cta + 1 < stages) stages = (int)(per_cta + 1 > 2 ? per_cta + 1 : 2);
   }
   if (stages < 2) return pl;
   pl.stages = stages;
   pl.smem = (size_t)stage_off + (size_t)stages * pl.stage_bytes;
-  pl.smem_cap = smem_cap;
-  pl.grid = (int)(pl.total_batches < g_num_sms ? pl.total_batches : g_num_sms);
+  pl.smem_cap = cap;
+  pl.grid = (int)(pl.total_batches < max_grid ? pl.total_batches : max_grid);
   pl.streaming = pl.grid > 0;
   (void)total_rows;
   return pl;

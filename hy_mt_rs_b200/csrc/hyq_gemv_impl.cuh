@@ -315,6 +315,11 @@ __device__ __forceinline__ void load_x(const Params& p, const uint8_t* smem, int
     }
     xu.xsum[s] = NP == 3 ? a0 + (a1 << 8) + (a2 << 16) : a0;
   }
+  // constants of combine() for the 2-bit and ternary formats
+  if (FMT == Q2_0C || FMT == STQ1_0) {
+    if (NP == 1) xu.xsum[0] *= FMT == Q2_0C ? 96 : 64;
+    xu.sg *= FMT == Q2_0C ? (1.0f / 32.0f) : (1.0f / 64.0f);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -329,10 +334,11 @@ __device__ __forceinline__ void decode_unit(uint32_t row, int u, WUnit& wu) {
     wu.s[0] = half_to_f32(ld_s16(blk));
     uint32_t q[4];
     ld_s_words<4>(blk + 2 + 16 * (u & 7), q);
+    // Plane k keeps its codes in place (c << 2k): seg_dot divides by 4^k.
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int k = 0; k < 4; ++k) wu.c[4 * i + k] = (q[i] >> (2 * k)) & 0x03030303u;
+      for (int k = 0; k < 4; ++k) wu.c[4 * i + k] = q[i] & (0x03030303u << (2 * k));
   } else if (FMT == STQ1_0) {
     // quant.rs:1103-1123: group g of chunk c: codebook[(sign << 4) | nibble],
     // lane p -> column 16p + (g % 16).  Four groups at a time: PRMT looks the
@@ -349,7 +355,7 @@ __device__ __forceinline__ void decode_unit(uint32_t row, int u, WUnit& wu) {
       const uint32_t hw = (i & 1) ? (nb[i >> 1] >> 16) : (nb[i >> 1] & 0xffffu);
       const uint32_t cb = stq_patterns4(hw, (sbits >> (4 * i)) & 15u);
 #pragma unroll
-      for (int pl = 0; pl < 4; ++pl) wu.c[4 * i + pl] = (cb >> (2 * pl)) & 0x03030303u;
+      for (int pl = 0; pl < 4; ++pl) wu.c[4 * i + pl] = cb & (0x03030303u << (2 * pl));
     }
   } else if (FMT == Q4_K) {
     // quant.rs:2437-2461.
@@ -427,6 +433,29 @@ __device__ __forceinline__ int dp4(uint32_t code, uint32_t x, int acc) {
 // Integer sum of codes x activations over words [j0, j1) of a unit: exact
 // in 32 bits for one activation byte plane; the three planes of the f32 path
 // are combined in 64 bits.
+// Q2_0C and STQ1_0 words: word j holds plane k = j & 3 of its codes in
+// place, i.e. code << 2k, so plane k sums carry a factor 4^k; one accumulator
+// per plane keeps the four dp4a chains independent.  Returns
+// 64 a0 + 16 a1 + 4 a2 + a3 = 64 x the exact code-activation sum.
+template <int FMT>
+__device__ __forceinline__ int plane_dot64(const WUnit& wu, const uint32_t (&x)[16]) {
+  int a[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int j = 0; j < 16; ++j) a[j & 3] = dp4<FMT>(wu.c[j], x[j], a[j & 3]);
+  return a[3] + 4 * (a[2] + 4 * (a[1] + 4 * a[0]));
+}
+
+// 64 x sum(code * activation) over a unit, one plane (NP=1) or the three
+// exact planes of the f32 path (NP=3, 64-bit).
+template <int FMT, int NP>
+__device__ __forceinline__ long long plane_dot64_np(const WUnit& wu, const XUnit<NP>& xu) {
+  const int a0 = plane_dot64<FMT>(wu, xu.w[0]);
+  if (NP == 1) return a0;
+  const int a1 = plane_dot64<FMT>(wu, xu.w[NP > 1 ? 1 : 0]);
+  const int a2 = plane_dot64<FMT>(wu, xu.w[NP > 2 ? 2 : 0]);
+  return (long long)a0 + ((long long)a1 << 8) + ((long long)a2 << 16);
+}
+
 template <int FMT, int NP>
 __device__ __forceinline__ long long seg_dot(const WUnit& wu, const XUnit<NP>& xu, int j0, int j1) {
   if (NP == 1) {
@@ -454,14 +483,16 @@ __device__ __forceinline__ float to_f(long long v) {
 
 template <int FMT, int NP>
 __device__ __forceinline__ float combine(const WUnit& wu, const XUnit<NP>& xu, float acc) {
-  if (FMT == Q2_0C) {
-    // sum (2c - 3) x = 2 sum c x - 3 sum x
-    const long long a = 2 * seg_dot<FMT, NP>(wu, xu, 0, 16) - 3ll * xu.xsum[0];
-    return fmaf(to_f<NP>(a), wu.s[0] * xu.sg, acc);
-  } else if (FMT == STQ1_0) {
-    // digit = code - 1
-    const long long a = seg_dot<FMT, NP>(wu, xu, 0, 16) - (long long)xu.xsum[0];
-    return fmaf(to_f<NP>(a), wu.s[0] * xu.sg, acc);
+  if (FMT == Q2_0C || FMT == STQ1_0) {
+    // Q2_0C: sum (2c - 3) x = 2 sum c x - 3 sum x; STQ1_0: digit = code - 1.
+    // With V = 64 sum c x - C sum x (C = 96 / 64) the sum is V / D (D = 32
+    // / 64); load_x pre-multiplies xsum by C (NP=1) and pre-divides the
+    // activation scale by D, an exact power of two, so the product equals
+    // sum * (weight scale * activation scale) rounded once, as before.
+    constexpr int C = FMT == Q2_0C ? 96 : 64;
+    if (NP == 1) return fmaf((float)((int)plane_dot64_np<FMT, NP>(wu, xu) - xu.xsum[0]), wu.s[0] * xu.sg, acc);
+    const long long v = plane_dot64_np<FMT, NP>(wu, xu) - (long long)C * xu.xsum[0];
+    return fmaf(__ll2float_rn(v), wu.s[0] * xu.sg, acc);
   } else if (FMT == Q4_K) {
     // sum (d1 q - m1) x = d1 sum q x - m1 sum x, per 32-column sub-block
     const float a0 = to_f<NP>(seg_dot<FMT, NP>(wu, xu, 0, 8));
@@ -561,8 +592,45 @@ __device__ __forceinline__ bool reduce_writer(int lane) {
   return (lane & ((32 >> k) - 1)) == 0;
 }
 
-template <int FMT, int NP, int UPL, int RW, bool PAIR>
-__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ Params p) {
+// The RW rows x UPL units of one warp in one tile, as straight-line code so
+// that their loads and dp4a chains interleave.  CHECK (the last tile of a
+// matrix, or lanes without a unit): rows past the tile's end re-read row 0
+// and are never written; a lane without a unit decodes unit 0 and keeps its
+// sums unchanged.
+template <int FMT, int NP, int UPL, int RW, bool PAIR, bool CHECK>
+__device__ __forceinline__ void tile_rows(uint32_t base, uint32_t baseu, int row_bytes, int rg, int rgi, int nrows,
+                                          const int (&ui)[UPL], const bool (&uv)[UPL], const XUnit<NP> (&xu)[UPL],
+                                          float (&g)[RW], float (&u)[RW]) {
+#pragma unroll
+  for (int i = 0; i < UPL; ++i) {
+#pragma unroll
+    for (int rr = 0; rr < RW; ++rr) {
+      const int r = rgi + rg * rr;
+      const uint32_t off = (uint32_t)(((CHECK && r >= nrows) ? 0 : r) * row_bytes);
+      WUnit wu;
+      decode_unit<FMT>(base + off, ui[i], wu);
+      const float gv = combine<FMT, NP>(wu, xu[i], g[rr]);
+      g[rr] = (!CHECK || uv[i]) ? gv : g[rr];
+      if (PAIR) {
+        WUnit wv;
+        decode_unit<FMT>(baseu + off, ui[i], wv);
+        const float uvv = combine<FMT, NP>(wv, xu[i], u[rr]);
+        u[rr] = (!CHECK || uv[i]) ? uvv : u[rr];
+      }
+    }
+  }
+}
+
+// Variants that also come in a two-CTAs-per-SM build (DUAL: <= 72 registers,
+// 26 warps per SM): the int8 path of the 2-bit and ternary formats with one
+// unit per lane, whose dp4a and shared-load chains need more warps to hide
+// their latency.  The others take the whole SM.
+__host__ __device__ constexpr bool dual_variant(int fmt, int np, int upl, bool pair) {
+  return (fmt == Q2_0C || fmt == STQ1_0) && np == 1 && upl == 1 && !pair;
+}
+
+template <int FMT, int NP, int UPL, int RW, bool PAIR, bool DUAL>
+__global__ void __launch_bounds__(kThreads, DUAL ? 2 : 1) gemv_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kMaxStages;
@@ -596,11 +664,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
       // Each packed weight byte is used once per call.
       const uint64_t policy = l2_evict_first_policy();
       int64_t issued = 0;
+      int s = 0;
+      uint32_t par = 1;  // phase of the empty barrier being waited for, from the second lap
       for (int64_t bt = blockIdx.x; bt < p.total_batches; bt += gridDim.x, ++issued) {
-        const int s = (int)(issued % S);
         if (issued == S) grid_dependency_wait();
         if (issued >= S) {
-          const uint32_t par = (uint32_t)(((issued / S) - 1) & 1);
           if (!mbar_wait(smem_addr(&empty[s]), par, abort_flag)) {
             atomicOr(p.status, DEV_TIMEOUT_EMPTY);
             *abort_flag = 1;
@@ -621,6 +689,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         mbar_arrive_expect_tx(bar, b0 + b1);
         stage_bulk(dst, src, b0, bar, policy);
         if (PAIR) stage_bulk(dst + p.half_bytes, srcu, b1, bar, policy);
+        if (++s == S) {
+          s = 0;
+          par ^= 1u;
+        }
       }
       // Do not leave while copies into this CTA's shared memory are in flight.
       const int64_t last = issued;
@@ -650,11 +722,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
   const int ridx = reduce_index<RW>(lane);
   const bool writer = reduce_writer<RW>(lane);
   const uint32_t stages_s = smem_addr(stages);
+  int ui[UPL];
+  bool lanes_ok = true;
+#pragma unroll
+  for (int i = 0; i < UPL; ++i) {
+    ui[i] = uv[i] ? uu[i] : 0;
+    lanes_ok = lanes_ok && uv[i];
+  }
+  const bool all_units = __all_sync(0xffffffffu, lanes_ok);
+  const int row_bytes = p.row_bytes, rg = p.rg;
 
+  // Ring slot and phase advance by increments (no division per tile).
+  int s = 0;
+  uint32_t par = 0;
   int64_t it = 0;
   for (int64_t bt = blockIdx.x; bt < p.total_batches; bt += gridDim.x, ++it) {
-    const int s = (int)(it % S);
-    const uint32_t par = (uint32_t)((it / S) & 1);
     bool ok = mbar_wait(smem_addr(&full[s]), par, abort_flag);
     // The warps that share a row leave together, or the named barrier below
     // would wait for a warp that is gone.
@@ -668,32 +750,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     int64_t row0;
     batch_of(p, bt, R, m, row0, nrows);
     const uint32_t tile = stages_s + (uint32_t)s * (uint32_t)p.stage_bytes;
-    const uint32_t base = tile + (uint32_t)(reinterpret_cast<uintptr_t>(p.mat[m].w + row0 * p.row_bytes) & 15);
+    const uint32_t base = tile + (uint32_t)(reinterpret_cast<uintptr_t>(p.mat[m].w + row0 * row_bytes) & 15);
     const uint32_t baseu =
         tile + (uint32_t)p.half_bytes +
-        (PAIR ? (uint32_t)(reinterpret_cast<uintptr_t>(p.up + row0 * p.row_bytes) & 15) : 0u);
+        (PAIR ? (uint32_t)(reinterpret_cast<uintptr_t>(p.up + row0 * row_bytes) & 15) : 0u);
     float g[RW], u[RW];
 #pragma unroll
     for (int rr = 0; rr < RW; ++rr) g[rr] = u[rr] = 0.f;
-#pragma unroll
-    for (int i = 0; i < UPL; ++i) {
-      if (uv[i]) {
-#pragma unroll
-        for (int rr = 0; rr < RW; ++rr) {
-          const int r = rgi + p.rg * rr;
-          if (r < nrows) {
-            WUnit wu;
-            decode_unit<FMT>(base + (uint32_t)(r * p.row_bytes), uu[i], wu);
-            g[rr] = combine<FMT, NP>(wu, xu[i], g[rr]);
-            if (PAIR) {
-              WUnit wv;
-              decode_unit<FMT>(baseu + (uint32_t)(r * p.row_bytes), uu[i], wv);
-              u[rr] = combine<FMT, NP>(wv, xu[i], u[rr]);
-            }
-          }
-        }
-      }
-    }
+    // (UPL 4 keeps one copy: two do not fit in 128 registers.)
+    if (UPL <= 3 && all_units && nrows == R)
+      tile_rows<FMT, NP, UPL, RW, PAIR, (UPL > 3)>(base, baseu, row_bytes, rg, rgi, nrows, ui, uv, xu, g, u);
+    else
+      tile_rows<FMT, NP, UPL, RW, PAIR, true>(base, baseu, row_bytes, rg, rgi, nrows, ui, uv, xu, g, u);
     warp_reduce_multi<RW>(g, lane);
     if (PAIR) warp_reduce_multi<RW>(u, lane);
     const int r = rgi + p.rg * ridx;  // the row this lane now holds
@@ -726,6 +794,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_addr(&empty[s]));
+    if (++s == S) {
+      s = 0;
+      par ^= 1u;
+    }
   }
 }
 
@@ -740,14 +812,15 @@ struct Plan {
   size_t smem = 0;
   int smem_cap = 0;
   int grid = 0;
+  int ctas_per_sm = 1;
   // Launch as a programmatic dependent of the preceding grid in the stream
   // (the caller guarantees no kernel still in flight writes the weights).
   bool overlap = false;
 };
 
-template <int FMT, int NP, int UPL, int RW, bool PAIR>
+template <int FMT, int NP, int UPL, int RW, bool PAIR, bool DUAL>
 cudaError_t run_stream(const Params& p, const Plan& pl, cudaStream_t st) {
-  auto k = gemv_kernel<FMT, NP, UPL, RW, PAIR>;
+  auto k = gemv_kernel<FMT, NP, UPL, RW, PAIR, DUAL>;
   // Raise the dynamic shared-memory limit once per device and instantiation.
   static int configured_dev = -1;
   int dev = 0;
@@ -776,10 +849,19 @@ cudaError_t run_stream(const Params& p, const Plan& pl, cudaStream_t st) {
 
 template <int FMT, int NP, int UPL, bool PAIR>
 cudaError_t dispatch_rw(const Params& p, const Plan& pl, cudaStream_t st) {
+  if constexpr (dual_variant(FMT, NP, UPL, PAIR)) {
+    if (pl.ctas_per_sm == 2) {
+      switch (pl.rw) {
+        case 1: return run_stream<FMT, NP, UPL, 1, PAIR, true>(p, pl, st);
+        case 2: return run_stream<FMT, NP, UPL, 2, PAIR, true>(p, pl, st);
+        default: return run_stream<FMT, NP, UPL, 4, PAIR, true>(p, pl, st);
+      }
+    }
+  }
   switch (pl.rw) {
-    case 1: return run_stream<FMT, NP, UPL, 1, PAIR>(p, pl, st);
-    case 2: return run_stream<FMT, NP, UPL, 2, PAIR>(p, pl, st);
-    default: return run_stream<FMT, NP, UPL, 4, PAIR>(p, pl, st);
+    case 1: return run_stream<FMT, NP, UPL, 1, PAIR, false>(p, pl, st);
+    case 2: return run_stream<FMT, NP, UPL, 2, PAIR, false>(p, pl, st);
+    default: return run_stream<FMT, NP, UPL, 4, PAIR, false>(p, pl, st);
   }
 }
 
