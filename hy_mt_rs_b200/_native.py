@@ -80,7 +80,7 @@ _SIGS = {
     "hyq_attention": ([_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _i64, _vp, _vp, _vp, _vp], C.c_int),
     "hyq_add": ([_vp, _vp, _i64, _vp], C.c_int),
     "hyq_add_rms_norm": ([_vp, _vp, _vp, _i64, C.c_float, _vp, _vp], C.c_int),
-    "hyq_argmax": ([_vp, _i64, _vp, _vp, _vp], C.c_int),
+    "hyq_argmax": ([_vp, _i64, _vp, _vp, _vp, _vp], C.c_int),
     "hyq_peer_alloc": ([C.c_size_t, C.POINTER(_vp), _vp], C.c_int),
     "hyq_peer_open": ([_vp, C.POINTER(_vp)], C.c_int),
     "hyq_peer_close": ([_vp], C.c_int),

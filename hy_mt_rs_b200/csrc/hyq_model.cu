@@ -41,6 +41,19 @@ cudaError_t launch(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cuda
   return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
 }
 
+// Dynamic shared memory of the norm kernels: up to kNormMaxN floats (set once
+// per device and kernel).
+template <typename K>
+void norm_smem_limit(K k) {
+  static int done_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (done_dev != dev) {
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 16384 * (int)sizeof(float));
+    done_dev = dev;
+  }
+}
+
 // dot_avx2 order over n floats, by the 16 lanes [b, b + 16) of a warp (b =
 // lane & 16), one per AVX2 accumulator lane.  Every lane of the group returns
 // the result.  `mask` covers the calling lanes.
@@ -64,24 +77,31 @@ __device__ __forceinline__ float dot_x86(const float* a, const float* b, int n, 
 
 // RMSNorm of `rows` rows of n floats (rms_norm_into, model.rs:785-830; per
 // head, model.rs:832-872): variance = dot(x, x) / n, scale = 1 / sqrt(var +
-// eps), out = (x * scale) * w.  One CTA per row.
+// eps), out = (x * scale) * w.  One CTA per row; the row is staged in shared
+// memory (n <= kNormMaxN) so that the 16-lane x86-order sum runs from there.
+constexpr int kNormMaxN = 16384;
+
+__device__ __forceinline__ float staged_rms_scale(const float* xs, int n, float eps) {
+  __shared__ float scale_s;
+  if (threadIdx.x < 16) {
+    const float d = dot_x86(xs, xs, n, 0xffffu);
+    if (threadIdx.x == 0) scale_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(d, (float)n), eps)));
+  }
+  __syncthreads();
+  return scale_s;
+}
+
 __global__ void __launch_bounds__(256) rms_norm_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                         int n, float eps, float* __restrict__ out) {
   grid_dependency_wait();
   allow_dependents_launch();
+  extern __shared__ float xs[];
   const float* xr = x + (size_t)blockIdx.x * n;
   float* orow = out + (size_t)blockIdx.x * n;
-  __shared__ float scale_s;
-  if (threadIdx.x < 16) {
-    const float d = dot_x86(xr, xr, n, 0xffffu);
-    if (threadIdx.x == 0) {
-      const float variance = __fdiv_rn(d, (float)n);
-      scale_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(variance, eps)));
-    }
-  }
+  for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = xr[i];
   __syncthreads();
-  const float scale = scale_s;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) orow[i] = __fmul_rn(__fmul_rn(xr[i], scale), w[i]);
+  const float scale = staged_rms_scale(xs, n, eps);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) orow[i] = __fmul_rn(__fmul_rn(xs[i], scale), w[i]);
 }
 
 // Embedding row (Weight::row_into, quant.rs:123-142) of the token held in
@@ -110,6 +130,8 @@ __global__ void __launch_bounds__(256) embed_kernel(const uint8_t* __restrict__ 
 // (HyV3, model.rs:425-428).  Also appends k and v to the KV cache at the
 // position (KvCache::append, model.rs:650-667).  One warp per head; grid =
 // heads + kv_heads.
+constexpr int kRopeMaxDim = 256;
+
 struct RopeArgs {
   float* q;
   float* k;
@@ -162,9 +184,13 @@ __global__ void __launch_bounds__(32) rope_qk_kernel(const __grid_constant__ Rop
   const float* nw = is_q ? a.q_norm : a.k_norm;
   const float* c = a.cos_tab + (size_t)pos * (a.dim / 2);
   const float* s = a.sin_tab + (size_t)pos * (a.dim / 2);
-  if (a.norm_first && nw) head_norm(hd, nw, a.dim, a.eps);
-  head_rope(hd, c, s, a.dim);
-  if (!a.norm_first && nw) head_norm(hd, nw, a.dim, a.eps);
+  __shared__ float hs[kRopeMaxDim];  // the head, worked on in shared memory
+  for (int i = threadIdx.x; i < a.dim; i += 32) hs[i] = hd[i];
+  __syncwarp();
+  if (a.norm_first && nw) head_norm(hs, nw, a.dim, a.eps);
+  head_rope(hs, c, s, a.dim);
+  if (!a.norm_first && nw) head_norm(hs, nw, a.dim, a.eps);
+  for (int i = threadIdx.x; i < a.dim; i += 32) hd[i] = hs[i];
   if (!is_q) {
     const int kh = h - a.heads;
     const size_t width = (size_t)a.kv_heads * a.dim;
@@ -172,7 +198,7 @@ __global__ void __launch_bounds__(32) rope_qk_kernel(const __grid_constant__ Rop
     float* vc = a.v_cache + (size_t)pos * width + (size_t)kh * a.dim;
     const float* vv = a.v + (size_t)kh * a.dim;
     for (int i = threadIdx.x; i < a.dim; i += 32) {
-      kc[i] = hd[i];
+      kc[i] = hs[i];
       vc[i] = vv[i];
     }
   }
@@ -317,64 +343,71 @@ __global__ void __launch_bounds__(256) add_kernel(float* __restrict__ dst, const
 }
 
 // add (model.rs:1043-1071) followed by rms_norm_into (model.rs:785-830) of
-// the sum: hidden += delta; out = (hidden * scale) * w.  One CTA.
+// the sum: hidden += delta; out = (hidden * scale) * w.  One CTA; the sum is
+// staged in shared memory for the norm.
 __global__ void __launch_bounds__(256) add_rms_norm_kernel(float* __restrict__ hidden,
                                                             const float* __restrict__ delta,
                                                             const float* __restrict__ w, int n, float eps,
                                                             float* __restrict__ out) {
   grid_dependency_wait();
   allow_dependents_launch();
-  for (int i = threadIdx.x; i < n; i += blockDim.x) hidden[i] = __fadd_rn(hidden[i], delta[i]);
-  __syncthreads();
-  __shared__ float scale_s;
-  if (threadIdx.x < 16) {
-    const float d = dot_x86(hidden, hidden, n, 0xffffu);
-    if (threadIdx.x == 0) scale_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(d, (float)n), eps)));
+  extern __shared__ float xs[];
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = __fadd_rn(hidden[i], delta[i]);
+    hidden[i] = v;
+    xs[i] = v;
   }
   __syncthreads();
-  const float scale = scale_s;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(hidden[i], scale), w[i]);
+  const float scale = staged_rms_scale(xs, n, eps);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(xs[i], scale), w[i]);
 }
 
-// Greedy token (generation.rs:281-290): the first index of the largest value.
-// One CTA; optionally advances the position counter.
-__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ x, int64_t n, int32_t* token,
-                                                       int32_t* pos) {
+// Greedy token (generation.rs:281-290): the first index of the largest value
+// (NaN never wins; all-NaN gives 0).  Many CTAs: each reduces its share to a
+// 64-bit key (order-preserving value bits, then ~index so that the lowest
+// index wins a tie; -0 counts as +0) and folds it into workspace[0] with
+// atomicMax; the last CTA to finish (counter in workspace[1]) writes the
+// token, advances the position and leaves the workspace zero.
+constexpr int kArgmaxThreads = 512;
+
+__device__ __forceinline__ unsigned long long argmax_key(float v, unsigned i) {
+  if (isnan(v)) return 0ull;
+  unsigned b = __float_as_uint(v == 0.0f ? 0.0f : v);
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((unsigned long long)b << 32) | (0xffffffffu - i);
+}
+
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __restrict__ x, int n, int32_t* token,
+                                                                int32_t* pos, unsigned long long* ws) {
   grid_dependency_wait();
   allow_dependents_launch();
-  float best = -INFINITY;
-  int64_t idx = n;
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = x[i];
-    if (v > best || (v == best && i < idx)) {
-      best = v;
-      idx = i;
-    }
+  unsigned long long best = 0ull;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const unsigned long long k = argmax_key(x[i], (unsigned)i);
+    best = k > best ? k : best;
   }
-  __shared__ float bv[32];
-  __shared__ int64_t bi[32];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-    const int64_t oi = __shfl_xor_sync(0xffffffffu, idx, o);
-    if (ov > best || (ov == best && oi < idx)) {
-      best = ov;
-      idx = oi;
-    }
+    const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
+    best = k > best ? k : best;
   }
-  if (lane == 0) {
-    bv[warp] = best;
-    bi[warp] = idx;
-  }
+  __shared__ unsigned long long wb[kArgmaxThreads / 32];
+  __shared__ int last_s;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) wb[warp] = best;
   __syncthreads();
   if (threadIdx.x == 0) {
-    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
-      if (bv[w] > best || (bv[w] == best && bi[w] < idx)) {
-        best = bv[w];
-        idx = bi[w];
-      }
-    *token = (int32_t)(idx < n ? idx : 0);
-    if (pos) *pos += 1;
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = wb[w] > best ? wb[w] : best;
+    atomicMax(&ws[0], best);
+    __threadfence();
+    last_s = atomicAdd(reinterpret_cast<unsigned*>(&ws[1]), 1u) == gridDim.x - 1;
+    if (last_s) {
+      __threadfence();
+      const unsigned long long k = atomicExch(&ws[0], 0ull);
+      atomicExch(reinterpret_cast<unsigned*>(&ws[1]), 0u);
+      *token = k ? (int32_t)(0xffffffffu - (unsigned)(k & 0xffffffffull)) : 0;
+      if (pos) *pos += 1;
+    }
   }
 }
 
@@ -405,9 +438,11 @@ int hyq_rope_table(int64_t positions, int head_dim, float rope_base, float* cos_
 int hyq_rms_norm(const float* x, const float* w, int64_t n, int64_t rows, float eps, float* out, void* stream) {
   if (!x || !w || !out) return hyq::api_fail(HYQ_E_INVALID, "rms_norm: null pointer");
   if (n <= 0 || rows <= 0 || n > INT32_MAX || rows > INT32_MAX) return hyq::api_fail(HYQ_E_SHAPE, "rms_norm: shape");
+  if (n > hyq::model::kNormMaxN) return hyq::api_fail(HYQ_E_SHAPE, "rms_norm: at most %d columns", hyq::model::kNormMaxN);
+  hyq::model::norm_smem_limit(hyq::model::rms_norm_kernel);
   const cudaError_t e =
-      hyq::model::launch(hyq::model::rms_norm_kernel, dim3((unsigned)rows), dim3(256), 0, (cudaStream_t)stream, x, w,
-                         (int)n, eps, out);
+      hyq::model::launch(hyq::model::rms_norm_kernel, dim3((unsigned)rows), dim3(256), (size_t)n * sizeof(float),
+                         (cudaStream_t)stream, x, w, (int)n, eps, out);
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "rms_norm: %s", cudaGetErrorString(e));
 }
 
@@ -521,17 +556,28 @@ int hyq_add(float* dst, const float* src, int64_t n, void* stream) {
 int hyq_add_rms_norm(float* hidden, const float* delta, const float* w, int64_t n, float eps, float* out,
                      void* stream) {
   if (!hidden || !delta || !w || !out) return hyq::api_fail(HYQ_E_INVALID, "add_rms_norm: null pointer");
-  if (n <= 0 || n > INT32_MAX) return hyq::api_fail(HYQ_E_SHAPE, "add_rms_norm: length");
-  const cudaError_t e = hyq::model::launch(hyq::model::add_rms_norm_kernel, dim3(1), dim3(256), 0,
-                                           (cudaStream_t)stream, hidden, delta, w, (int)n, eps, out);
+  if (n <= 0 || n > hyq::model::kNormMaxN)
+    return hyq::api_fail(HYQ_E_SHAPE, "add_rms_norm: 1 to %d columns", hyq::model::kNormMaxN);
+  hyq::model::norm_smem_limit(hyq::model::add_rms_norm_kernel);
+  const cudaError_t e = hyq::model::launch(hyq::model::add_rms_norm_kernel, dim3(1), dim3(256),
+                                           (size_t)n * sizeof(float), (cudaStream_t)stream, hidden, delta, w, (int)n,
+                                           eps, out);
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "add_rms_norm: %s", cudaGetErrorString(e));
 }
 
-int hyq_argmax(const float* x, int64_t n, int32_t* token, int32_t* pos, void* stream) {
-  if (!x || !token) return hyq::api_fail(HYQ_E_INVALID, "argmax: null pointer");
+int hyq_argmax(const float* x, int64_t n, int32_t* token, int32_t* pos, void* workspace, void* stream) {
+  if (!x || !token || !workspace) return hyq::api_fail(HYQ_E_INVALID, "argmax: null pointer");
   if (n <= 0 || n > INT32_MAX) return hyq::api_fail(HYQ_E_SHAPE, "argmax: length");
-  const cudaError_t e =
-      hyq::model::launch(hyq::model::argmax_kernel, dim3(1), dim3(1024), 0, (cudaStream_t)stream, x, n, token, pos);
+  if (reinterpret_cast<uintptr_t>(workspace) % 8) return hyq::api_fail(HYQ_E_INVALID, "argmax: workspace alignment");
+  // about 2048 values per CTA, at most one CTA per SM
+  int sms = 148;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int64_t blocks = (n + 4 * hyq::model::kArgmaxThreads - 1) / (4 * hyq::model::kArgmaxThreads);
+  if (blocks > sms) blocks = sms;
+  const cudaError_t e = hyq::model::launch(hyq::model::argmax_kernel, dim3((unsigned)blocks),
+                                           dim3(hyq::model::kArgmaxThreads), 0, (cudaStream_t)stream, x, (int)n,
+                                           token, pos, static_cast<unsigned long long*>(workspace));
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "argmax: %s", cudaGetErrorString(e));
 }
 

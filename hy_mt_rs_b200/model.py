@@ -93,6 +93,7 @@ class DenseModel:
         check(lib.hyq_attention_workspace_bytes(cfg.heads, cfg.head_dim, cfg.positions, C.byref(ws)))
         # split partials + per-head counters; zero once, every call leaves it zero
         self.attn_ws = torch.zeros(ws.value, dtype=torch.uint8, device=device)
+        self.argmax_ws = torch.zeros(2, dtype=torch.int64, device=device)  # HYQ_ARGMAX_WORKSPACE_BYTES, zero
         self.graph = None
 
     # ----------------------------------------------------------------- step
@@ -126,7 +127,7 @@ class DenseModel:
             nxt = self.layers[i + 1]["input_norm"] if i + 1 < len(self.layers) else self.output_norm
             check(lib.hyq_add_rms_norm(_p(self.hidden), _p(self.ff), _p(nxt), H, cfg.eps, _p(self.normalized), st))
         check(lib.hyq_matmul(self.embed.handle, _p(self.normalized), 1, _p(self.logits), st))
-        check(lib.hyq_argmax(_p(self.logits), cfg.vocab, _p(self.token), _p(self.pos), st))
+        check(lib.hyq_argmax(_p(self.logits), cfg.vocab, _p(self.token), _p(self.pos), _p(self.argmax_ws), st))
 
     # kernel launches of one enqueue_step
     def launches(self):

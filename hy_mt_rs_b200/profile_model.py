@@ -1,0 +1,35 @@
+"""Run token steps of the Dense decoder (hy_mt_rs_b200.model), for profiler
+captures.
+
+    python -m hy_mt_rs_b200.profile_model --layers 32 --prompt 8 --steps 3
+
+Builds the seeded random-init model with the 1.8B shapes (Q2_0C linears,
+tied Q6_K embedding), captures one token step as a CUDA graph, feeds
+`--prompt` tokens and then `--steps` greedy steps, one graph replay each.
+Every replay launches the same kernels in the same order (a launch list of
+one replay is one token step).
+"""
+import argparse
+
+import torch
+
+from .model import DenseConfig, DenseModel, random_weights
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--prompt", type=int, default=8)
+    ap.add_argument("--steps", type=int, default=3)
+    a = ap.parse_args()
+    dev = torch.device("cuda", 0)
+    cfg = DenseConfig(layers=a.layers, positions=a.prompt + a.steps + 1)
+    model = DenseModel(cfg, random_weights(cfg, dev, seed=1), dev)
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(dev)
+    ids = model.generate(list(range(1, a.prompt + 1)), a.steps, stream)
+    print("tokens", ids)
+
+
+if __name__ == "__main__":
+    main()

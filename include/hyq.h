@@ -232,7 +232,8 @@ int hyq_matmul_noalloc(const hyq_weight* w, const float* input, int64_t batch, f
 int hyq_rope_table(int64_t positions, int head_dim, float rope_base, float* cos_out, float* sin_out);
 
 /* rms_norm_into (model.rs:785-830) of `rows` rows of n floats (rows > 1: the
- * per-head q/k norm, model.rs:832-872): out = x * (1/sqrt(mean(x^2)+eps)) * w. */
+ * per-head q/k norm, model.rs:832-872): out = x * (1/sqrt(mean(x^2)+eps)) * w.
+ * n is at most 16384 (the row is staged in shared memory). */
 int hyq_rms_norm(const float* x, const float* w, int64_t n, int64_t rows, float eps, float* out, void* stream);
 
 /* Weight::row_into (quant.rs:123-142) of the row *token (device int32). */
@@ -270,8 +271,11 @@ int hyq_add_rms_norm(float* hidden, const float* delta, const float* w, int64_t 
                      void* stream);
 
 /* Greedy token (generation.rs:281-290: first index of the largest value)
- * into *token; when pos is not NULL, *pos += 1. */
-int hyq_argmax(const float* x, int64_t n, int32_t* token, int32_t* pos, void* stream);
+ * into *token; when pos is not NULL, *pos += 1.  `workspace`: 16 bytes,
+ * 8-byte aligned, zero before the first call (every call leaves it zero);
+ * calls that share one must not overlap in time. */
+#define HYQ_ARGMAX_WORKSPACE_BYTES 16
+int hyq_argmax(const float* x, int64_t n, int32_t* token, int32_t* pos, void* workspace, void* stream);
 
 /* --- Tensor-parallel all-reduce over NVLink peer memory ------------------
  * No counterpart in the reference (CPU only).  Sums the row-parallel partial

@@ -103,3 +103,40 @@ def test_add_rms_norm_bit_exact(cuda):
     s = (h.numpy() + dlt.numpy()).astype(np.float32)
     np.testing.assert_array_equal(hd.cpu().numpy(), s)
     np.testing.assert_array_equal(out.cpu().numpy(), O.rms_norm(s, w.numpy(), 1e-5))
+
+
+def test_argmax_ties_nan_and_workspace(cuda):
+    """hyq_argmax (generation.rs:281-290): the first index of the largest
+    value across CTAs, NaN never wins, all-NaN gives 0, -0 ties +0; the
+    workspace is left zero after every call and pos advances."""
+    import ctypes as C
+    import torch
+    from hy_mt_rs_b200._native import check, lib
+
+    def run(x):
+        xd = torch.from_numpy(x).to(cuda)
+        tok = torch.full((1,), -1, dtype=torch.int32, device=cuda)
+        pos = torch.zeros(1, dtype=torch.int32, device=cuda)
+        ws = torch.zeros(2, dtype=torch.int64, device=cuda)
+        for _ in range(2):
+            check(lib.hyq_argmax(C.c_void_p(xd.data_ptr()), x.size, C.c_void_p(tok.data_ptr()),
+                                 C.c_void_p(pos.data_ptr()), C.c_void_p(ws.data_ptr()),
+                                 C.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)))
+        torch.cuda.synchronize()
+        assert int(pos) == 2 and not ws.any()
+        return int(tok)
+
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal(120832).astype(np.float32)
+    assert run(x) == int(np.argmax(x))
+    x[[5, 70000, 120831]] = x.max() + 1.0   # a three-way tie across CTAs
+    assert run(x) == 5
+    x[3] = np.nan
+    assert run(x) == 5
+    y = np.full(4096, -np.inf, dtype=np.float32)
+    y[100] = -0.0
+    y[50] = 0.0
+    y[10] = np.nan
+    assert run(y) == 50
+    assert run(np.full(1000, np.nan, dtype=np.float32)) == 0
+    assert run(np.full(3000, -np.inf, dtype=np.float32)) == 0
