@@ -52,7 +52,7 @@ def args_parse():
     ap.add_argument("--no-overlap", action="store_true",
                     help="decode: plain stream order instead of overlapped launches (hyq_set_launch_overlap)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
-    ap.add_argument("--workload", choices=["decode", "prefill", "gemv", "tp", "model"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "gemv", "tp", "model", "moe"], default="decode",
                     help="decode: config 2 (default line); prefill: config 3 (7B layer GEMMs); "
                          "gemv: config 1 (one 6144x2048 product, L2 defeated by rotating copies)")
     ap.add_argument("--tp-mode", choices=["decode", "prefill"], default="decode",
@@ -1016,6 +1016,126 @@ def model_arm(a):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# Mixture-of-experts FFN (config 5): decode batch 64, prefill M = 1024
+# ---------------------------------------------------------------------------
+MOE_DECODE_TOKENS, MOE_PREFILL_TOKENS = 64, 1024
+
+
+def moe_arm(a):
+    import numpy as np
+    import torch
+
+    world, rank, dev = init_ranks()
+    import hy_mt_rs_b200  # noqa: F401
+    from hy_mt_rs_b200 import quant
+    from hy_mt_rs_b200.moe import MoeConfig, MoeLayer, random_moe_weights
+
+    cfg = MoeConfig()
+    weights = random_moe_weights(cfg, dev, seed=3)
+    layer = MoeLayer(cfg, weights)
+    H, E, M, S, U = cfg.hidden, cfg.experts, cfg.mid, cfg.shared_mid, cfg.used
+    expert_bytes = 3 * M * row_bytes(cfg.dtype, H)  # gate + up + down of one expert (same byte count)
+    shared_bytes = 3 * S * row_bytes(cfg.dtype, H)
+    stream = torch.cuda.Stream(dev)
+    sampler = ClockSampler("GPU-" + str(torch.cuda.get_device_properties(dev).uuid))
+    res = {}
+    for T in (MOE_DECODE_TOKENS, MOE_PREFILL_TOKENS):
+        x = torch.randn(T, H, generator=torch.Generator().manual_seed(T)).to(dev)
+        out = torch.empty(T, H, device=dev)
+        with torch.cuda.stream(stream):
+            for _ in range(max(3, a.warmup)):
+                layer.forward(x, T, out)
+            stream.synchronize()
+            if T == MOE_DECODE_TOKENS:
+                sampler.start()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(a.steps):
+                layer.forward(x, T, out)
+            e1.record(stream)
+            stream.synchronize()
+            if T == MOE_DECODE_TOKENS:
+                sampler.stop()
+            off = layer._buffers(T, dev)["off"].cpu().numpy()
+            # e2e: host activations in (pinned), the layer, host result out, every step
+            xh = x.cpu().pin_memory()
+            oh = torch.empty(T, H).pin_memory()
+            xd = torch.empty_like(x)
+            torch.cuda.synchronize(dev)
+            t0 = time.perf_counter()
+            for _ in range(a.steps):
+                xd.copy_(xh, non_blocking=True)
+                layer.forward(xd, T, out)
+                oh.copy_(out, non_blocking=True)
+                stream.synchronize()
+            e2e_s = (time.perf_counter() - t0) / a.steps
+        hit = int((np.diff(off) > 0).sum())
+        res[T] = {"ms": e0.elapsed_time(e1) / a.steps, "e2e_s": e2e_s, "experts_hit": hit,
+                  "bytes": hit * expert_bytes + shared_bytes + E * H * 4,
+                  "flops": 2 * T * (U * 3 * M * H + 3 * S * H + E * H)}
+    failed = device_failed(quant, dev)
+    (ms_dec, ms_pre, failed), clocks_all = reduce_over_ranks(
+        [res[MOE_DECODE_TOKENS]["ms"], res[MOE_PREFILL_TOKENS]["ms"], failed + 0.0], sampler.summary(), dev)
+    if failed:
+        raise RuntimeError("a kernel reported an expired bounded wait (device status word) on some rank")
+    launches = layer.launches(MOE_DECODE_TOKENS) * a.steps
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    dec, pre = res[MOE_DECODE_TOKENS], res[MOE_PREFILL_TOKENS]
+    peak, peak_kind = measured_peaks()
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:
+        pass
+    tpeak = float(peaks.get("bf16_tflops", 1590.0))
+    gbs = dec["bytes"] / (ms_dec * 1e-3) / 1e9
+    # CPU baseline: the oracle port of the reference's Moe::forward on a sample
+    from oracle.moe import moe_forward_port
+    wn = {k: v.cpu().numpy() for k, v in weights.items()}
+    xs = np.random.default_rng(0).standard_normal((8, H)).astype(np.float32)
+    t0 = time.perf_counter()
+    moe_forward_port(cfg, wn, xs, host_threads())
+    cpu_tok_s = xs.shape[0] / (time.perf_counter() - t0)
+    sm = [c["sm_mhz"] for c in clocks_all if c.get("sm_mhz")]
+    line = {
+        "metric": "MoE FFN decode tokens/s (config 5: 64 experts top-8, 2048->1024->2048 Q4_K, batch 64)",
+        "value": round(MOE_DECODE_TOKENS / (ms_dec * 1e-3) * world, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": a.steps, "warmup": max(3, a.warmup), "ms_per_step": round(ms_dec, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp16 tensor-core operands, f32 accumulate; f32 router and routing",
+        "data": "synthetic (seeded N(0,1) F32 router, N(0,0.1) bias, N(0,0.02) Q4_K experts; N(0,1) activations)",
+        "config": {"workload": "hy-mt-rs config 5: one MoE FFN (router, sigmoid top-8 routing, 64 experts "
+                               "2048->1024->2048 SwiGLU Q4_K, shared expert 2048->1024->2048), batch 64",
+                   "experts": E, "used": U, "parallelism": f"replicas x{world}",
+                   "l2": "expert weights 226 MB per layer > L2"},
+        "prefill": {"tokens": MOE_PREFILL_TOKENS, "ms_per_step": round(ms_pre, 4),
+                    "tokens_per_s": round(MOE_PREFILL_TOKENS / (ms_pre * 1e-3) * world, 1),
+                    "tflops": round(pre["flops"] / (ms_pre * 1e-3) / 1e12, 2),
+                    "frac_of_bf16": round(pre["flops"] / (ms_pre * 1e-3) / 1e12 / tpeak, 4)},
+        "roofline": {"bound": "hbm", "kernel": "whole decode step (router + experts hit + shared expert bytes)",
+                     "unit": "GB/s", "achieved": round(gbs, 1), "peak": peak, "peak_kind": peak_kind,
+                     "frac": round(gbs / peak, 4), "traffic": None,
+                     "algorithmic_bytes_per_launch": dec["bytes"], "experts_hit": dec["experts_hit"]},
+        "e2e": {"value": round(MOE_DECODE_TOKENS / dec["e2e_s"], 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": MOE_DECODE_TOKENS * H * 4, "d2h_bytes_per_step": MOE_DECODE_TOKENS * H * 4},
+        "gpu_launches": launches,
+        "clocks": {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": clocks_all[0].get("sm_max_mhz"),
+                   "reasons": sorted({r for c in clocks_all for r in c.get("reasons", [])}),
+                   "samples": sum(c.get("samples", 0) for c in clocks_all)},
+        "cpu_baseline": {"value": round(cpu_tok_s, 3), "unit": "tokens/s", "cores": host_threads(), "kind": "port",
+                         "sample": "8 tokens through oracle/moe.py moe_forward_port (the reference's expert loop, "
+                                   "x86 f32 order; f64 accumulation in the batch >= 8 products)"},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     a = args_parse()
     if a.impl == "reference":
@@ -1028,6 +1148,8 @@ def main():
         return tp_arm(a)
     if a.workload == "model":
         return model_arm(a)
+    if a.workload == "moe":
+        return moe_arm(a)
     return gpu_arm(a)
 
 

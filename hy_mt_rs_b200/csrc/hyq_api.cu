@@ -506,6 +506,54 @@ int hyq_matmul_qkv(const hyq_weight* q, const hyq_weight* k, const hyq_weight* v
   return HYQ_OK;
 }
 
+// Grouped expert products (expert mode of the tensor-core GEMM).
+static int experts_job(const hyq_weight* w, const hyq_weight* up, const float* input, const int32_t* input_rows,
+                       int64_t rows, const int32_t* expert_off, int64_t max_rows, float* out, hyq::GemmJob& j,
+                       const char* name) {
+  if (!w || !input || !expert_off || !out) return fail(HYQ_E_INVALID, "%s: null pointer", name);
+  if (w->ndim != 3 || (up && (up->ndim != 3 || up->dtype != w->dtype || up->dims[0] != w->dims[0] ||
+                              up->dims[1] != w->dims[1] || up->dims[2] != w->dims[2])))
+    return fail(HYQ_E_SHAPE, "%s: weights must be [K, N, experts] tensors of one shape", name);
+  if (rows <= 0 || max_rows <= 0) return fail(HYQ_E_SHAPE, "%s: invalid activation shape", name);
+  if (!aligned(input, 16)) return fail(HYQ_E_ALIGN, "%s: input must be 16-byte aligned", name);
+  j.dtype = w->dtype;
+  j.n_mat = up ? 2 : 1;
+  j.gate_up = up != nullptr;
+  j.w[0] = w->data;
+  if (up) j.w[1] = up->data;
+  j.rows[0] = j.rows[1] = w->dims[1];
+  j.y[0] = out;
+  j.K = w->dims[0];
+  j.M = rows;
+  j.x = input;
+  j.experts = (int)w->dims[2];
+  j.expert_off = expert_off;
+  j.expert_max_rows = max_rows;
+  j.x_rows = input_rows;
+  if (!hyq::gemm_job_supported(j))
+    return fail(HYQ_E_UNSUPPORTED, "%s: the tensor-core path does not take this expert format or shape", name);
+  return HYQ_OK;
+}
+
+int hyq_matmul_experts(const hyq_weight* w, const float* input, const int32_t* input_rows, int64_t rows,
+                       const int32_t* expert_off, int64_t max_rows, float* out, void* stream) {
+  hyq::GemmJob j;
+  int rc = experts_job(w, nullptr, input, input_rows, rows, expert_off, max_rows, out, j, "matmul_experts");
+  if (rc) return rc;
+  return run_gemm_job(j, (cudaStream_t)stream, "matmul_experts (tensor-core GEMM)");
+}
+
+int hyq_matmul_experts_gate_up_silu(const hyq_weight* gate, const hyq_weight* up, const float* input,
+                                    const int32_t* input_rows, int64_t rows, const int32_t* expert_off,
+                                    int64_t max_rows, float* out, void* stream) {
+  if (!up) return fail(HYQ_E_INVALID, "matmul_experts_gate_up_silu: null pointer");
+  hyq::GemmJob j;
+  int rc = experts_job(gate, up, input, input_rows, rows, expert_off, max_rows, out, j,
+                       "matmul_experts_gate_up_silu");
+  if (rc) return rc;
+  return run_gemm_job(j, (cudaStream_t)stream, "matmul_experts_gate_up_silu (tensor-core GEMM)");
+}
+
 int hyq_matmul_gate_up_silu_batch(const hyq_weight* gate, const hyq_weight* up, const float* input, int64_t batch,
                                   float* out, void* stream) {
   int rc = gate_up_checks(gate, up);

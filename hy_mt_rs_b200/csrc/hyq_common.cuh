@@ -235,4 +235,26 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// dot_avx2 order (quant.rs:2562-2596: two 8-lane FMA accumulators per 16
+// floats, their lane sums, a scalar tail) over n floats, by the 16 lanes
+// [b, b + 16) of a warp (b = lane & 16), one per AVX2 accumulator lane.  Every lane of the group returns
+// the result.  `mask` covers the calling lanes.
+__device__ __forceinline__ float dot_x86(const float* a, const float* b, int n, unsigned mask) {
+  const int lane = threadIdx.x & 31;
+  const int l = lane & 15, base = lane & 16;
+  const int chunks = n / 16;
+  float acc = 0.f;
+  for (int c = 0; c < chunks; ++c) acc = fmaf(a[16 * c + l], b[16 * c + l], acc);
+  // sum[l] = s0[l] + s1[l] for l < 8
+  float sum = __fadd_rn(acc, __shfl_sync(mask, acc, base + ((l + 8) & 15)));
+  const int simd_end = chunks * 16, vec_end = n / 8 * 8;
+  if (vec_end > simd_end && l < 8) sum = fmaf(a[simd_end + l], b[simd_end + l], sum);
+  float h = -0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) h = __fadd_rn(h, __shfl_sync(mask, sum, base + k));
+  float t = -0.0f;
+  for (int i = vec_end; i < n; ++i) t = __fadd_rn(t, __fmul_rn(a[i], b[i]));
+  return __fadd_rn(h, t);
+}
+
 }  // namespace hyq

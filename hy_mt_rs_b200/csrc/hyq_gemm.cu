@@ -88,6 +88,12 @@ struct Params {
   // output is silu(gate x) * (up x) in ys[0] [M, seg_rows[0]] (split-K:
   // gate partials in columns 0.., up partials in columns seg_rows[0]..).
   int gate_up;
+  // Expert mode: CTA x serves expert x / expert_tiles, whose weight rows
+  // start at e * expert_rows and whose activation rows are expert_off[e] ..
+  // expert_off[e + 1]; a CTA whose token tile holds none of them returns.
+  const int32_t* expert_off;
+  int expert_tiles;
+  int expert_rows;
 };
 
 template <int FMT, int BN>
@@ -417,12 +423,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base_g + L::misc + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tok0 = blockIdx.y * BN;
+  int tok0 = blockIdx.y * BN;
+  int tok_end = p.M;  // activation rows of this tile end here
   // row tile -> matrix and its first row (a gate/up tile covers 64 rows of each)
   int seg = 0;
   while (seg + 1 < p.n_seg && (int)blockIdx.x >= p.seg_tile0[seg + 1]) ++seg;
   const int tile_rows = p.gate_up ? BM / 2 : BM;
-  const int row0 = ((int)blockIdx.x - p.seg_tile0[seg]) * tile_rows;
+  int row0 = ((int)blockIdx.x - p.seg_tile0[seg]) * tile_rows;
+  int wrow0 = row0;  // first row in the weight tensor map
+  if (p.expert_off) {
+    const int e = (int)blockIdx.x / p.expert_tiles;
+    const int t_end = p.expert_off[e + 1];
+    tok0 = p.expert_off[e] + (int)blockIdx.y * BN;
+    if (tok0 >= t_end) return;  // nothing allocated or armed yet
+    tok_end = t_end;
+    row0 = ((int)blockIdx.x % p.expert_tiles) * tile_rows;
+    wrow0 = e * p.expert_rows + row0;
+  }
   const int steps_per_w = p.wcol / BK;
   // split-K slice of this CTA: K steps [kbeg, kbeg + nk)
   const int kbeg = blockIdx.z * p.steps_per_split;
@@ -478,7 +495,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < p.g; ++j) {
               const int x0 = (int)(((int64_t)j * p.row_bytes + kb * p.wbytes) & ~int64_t(15));
               tma_load_2d(base + L::w + ws * L::w_stage + (mt * tile_rows + j * (tile_rows / p.g)) * p.wbox, map,
-                          x0, row0 / p.g, wfull(ws));
+                          x0, wrow0 / p.g, wfull(ws));
             }
           }
           ++issued_w;
@@ -601,7 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int i = 0; i < 16; ++i) {
                 const int tok = tok0 + c0 + i;
-                if (tok >= p.M) continue;
+                if (tok >= tok_end) continue;
                 if (split) yz[(size_t)tok * p.N + p.seg_col0[seg] + row] = __uint_as_float(v[i]);
                 else p.ys[seg][(size_t)tok * rows_m + row] = __uint_as_float(v[i]);
               }
@@ -617,7 +634,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int i = 0; i < 16; ++i) {
                 const int tok = tok0 + c0 + i;
-                if (tok >= p.M) continue;
+                if (tok >= tok_end) continue;
                 if (split) {
                   yz[(size_t)tok * p.N + hi * rows_m + row] = __uint_as_float(v[i]);
                 } else if (!hi) {
@@ -956,7 +973,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // step stored in k_perm order.  One thread per 2 output slots.
 template <int FMT>
 __global__ void __launch_bounds__(256) to_half_kernel(const float* __restrict__ x, __half2* __restrict__ h,
-                                                       int64_t K, int64_t total_pairs) {
+                                                       int64_t K, int64_t total_pairs,
+                                                       const int32_t* __restrict__ rows) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= total_pairs) return;
   const int64_t e = 2 * i;  // element index of the first slot
@@ -964,7 +982,7 @@ __global__ void __launch_bounds__(256) to_half_kernel(const float* __restrict__ 
   const int64_t kk = e - tok * K;
   const int64_t step0 = kk & ~int64_t(63);
   const int slot = (int)(kk & 63);
-  const float* row = x + tok * K + step0;
+  const float* row = x + (rows ? (int64_t)rows[tok] : tok) * K + step0;  // expert mode: gathered rows
   h[i] = __floats2half2_rn(row[k_perm(FMT, slot)], row[k_perm(FMT, slot + 1)]);
 }
 
@@ -1046,7 +1064,7 @@ bool use_pair(int64_t N, int64_t M) {
 
 template <int FMT, int BN>
 cudaError_t run(const CUtensorMap* tw, const CUtensorMap& tx, const Params& p, int tiles, int splits,
-                cudaStream_t st) {
+                int64_t max_rows, cudaStream_t st) {
   auto k = gemm_kernel<FMT, BN>;
   static int configured_dev = -1;
   int dev = 0;
@@ -1057,7 +1075,8 @@ cudaError_t run(const CUtensorMap* tw, const CUtensorMap& tx, const Params& p, i
     if (e != cudaSuccess) return e;
     configured_dev = dev;
   }
-  dim3 grid((unsigned)tiles, (unsigned)((p.M + BN - 1) / BN), (unsigned)splits);
+  // token tiles: of all M rows, or (expert mode) of the most rows one expert can have
+  dim3 grid((unsigned)tiles, (unsigned)((max_rows + BN - 1) / BN), (unsigned)splits);
   k<<<grid, kThreads, smem, st>>>(tw[0], tw[1], tw[2], tx, p);
   return cudaGetLastError();
 }
@@ -1130,6 +1149,14 @@ struct Layout {
 
 Layout layout_of(const GemmJob& j) {
   Layout L;
+  if (j.experts > 0) {
+    // expert e owns row tiles [e * per, (e + 1) * per)
+    const int per = (int)((j.rows[0] + (j.gate_up ? BM / 2 : BM) - 1) / (j.gate_up ? BM / 2 : BM));
+    L.tiles = j.experts * per;
+    L.tile0[1] = L.tiles;
+    L.ncols = (int)(j.gate_up ? 2 * j.rows[0] : j.rows[0]);
+    return L;
+  }
   if (j.gate_up) {
     L.tiles = (int)((j.rows[0] + BM / 2 - 1) / (BM / 2));
     L.tile0[1] = L.tiles;
@@ -1150,6 +1177,10 @@ Layout layout_of(const GemmJob& j) {
 // path does not take it.
 bool job_geometry(const GemmJob& j, Geometry& g) {
   if (j.gate_up ? j.n_mat != 2 : (j.n_mat < 1 || j.n_mat > 3)) return false;
+  if (j.experts > 0) {
+    if (!j.expert_off || j.n_mat != (j.gate_up ? 2 : 1) || j.expert_max_rows <= 0) return false;
+    if ((int64_t)j.experts * j.rows[0] > INT32_MAX / 4) return false;
+  }
   if (j.gate_up && j.rows[0] != j.rows[1]) return false;
   const int64_t row_bytes = j.K / block_len(j.dtype) * block_bytes(j.dtype);
   for (int m = 0; m < j.n_mat; ++m) {
@@ -1175,7 +1206,7 @@ size_t gemm_job_workspace_bytes(const GemmJob& j) {
   gemm::Geometry g;
   if (!gemm::job_geometry(j, g)) return 0;
   const gemm::Layout L = gemm::layout_of(j);
-  const int z = gemm::choose_splits(j.K, L.tiles, j.M, g.wcol);
+  const int z = j.experts > 0 ? 1 : gemm::choose_splits(j.K, L.tiles, j.M, g.wcol);
   return gemm::x_bytes(j.K, j.M) + (z > 1 ? (size_t)z * j.M * L.ncols * sizeof(float) : 0) + 16;
 }
 
@@ -1188,28 +1219,31 @@ cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) 
   const int64_t K = j.K, M = j.M;
   const int64_t row_bytes = K / block_len(j.dtype) * block_bytes(j.dtype);
   const Layout lay = layout_of(j);
-  const bool pair = !j.gate_up && j.n_mat == 1 && (j.dtype == Q4_K || j.dtype == Q6_K) && use_pair(j.rows[0], M);
+  const bool pair = j.experts == 0 && !j.gate_up && j.n_mat == 1 && (j.dtype == Q4_K || j.dtype == Q6_K) &&
+                    use_pair(j.rows[0], M);
   __half* xh = static_cast<__half*>(workspace);
   {
     const int64_t pairs = K * M / 2;
     const unsigned blocks = (unsigned)((pairs + 255) / 256);
     __half2* xh2 = reinterpret_cast<__half2*>(xh);
     switch (j.dtype) {
-      case Q4_K: to_half_kernel<Q4_K><<<blocks, 256, 0, st>>>(j.x, xh2, K, pairs); break;
-      case Q6_K: to_half_kernel<Q6_K><<<blocks, 256, 0, st>>>(j.x, xh2, K, pairs); break;
-      case Q8_0: to_half_kernel<Q8_0><<<blocks, 256, 0, st>>>(j.x, xh2, K, pairs); break;
-      case Q2_0C: to_half_kernel<Q2_0C><<<blocks, 256, 0, st>>>(j.x, xh2, K, pairs); break;
-      default: to_half_kernel<STQ1_0><<<blocks, 256, 0, st>>>(j.x, xh2, K, pairs); break;
+      case Q4_K: to_half_kernel<Q4_K><<<blocks, 256, 0, st>>>(j.x, xh2, K, pairs, j.x_rows); break;
+      case Q6_K: to_half_kernel<Q6_K><<<blocks, 256, 0, st>>>(j.x, xh2, K, pairs, j.x_rows); break;
+      case Q8_0: to_half_kernel<Q8_0><<<blocks, 256, 0, st>>>(j.x, xh2, K, pairs, j.x_rows); break;
+      case Q2_0C: to_half_kernel<Q2_0C><<<blocks, 256, 0, st>>>(j.x, xh2, K, pairs, j.x_rows); break;
+      default: to_half_kernel<STQ1_0><<<blocks, 256, 0, st>>>(j.x, xh2, K, pairs, j.x_rows); break;
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
-  const int bn = M >= 256 ? 256 : 128;
+  // expert mode: the typical rows per expert pick the token tile
+  const int bn = (j.experts > 0 ? M / j.experts : M) >= 256 ? 256 : 128;
   const int tile_rows = j.gate_up ? BM / 2 : BM;
+  const int64_t map_mats = j.experts > 0 ? j.experts : 1;  // expert mode: the maps cover every expert
   CUtensorMap tw[3], tx;
   for (int m = 0; m < 3; ++m) {
     const int mm = m < j.n_mat ? m : 0;  // unused maps repeat the first
-    const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes * g.rows), (cuuint64_t)(j.rows[mm] / g.rows)};
+    const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes * g.rows), (cuuint64_t)(map_mats * j.rows[mm] / g.rows)};
     const cuuint64_t strides[1] = {(cuuint64_t)(row_bytes * g.rows)};
     const cuuint32_t box[2] = {(cuuint32_t)g.wbox, (cuuint32_t)(tile_rows / g.rows)};
     const cuuint32_t es[2] = {1, 1};
@@ -1229,7 +1263,7 @@ cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) 
       return cudaErrorInvalidValue;
   }
   const int nwb = (int)(K / g.wcol);
-  const int z = choose_splits(K, lay.tiles, M, g.wcol);
+  const int z = j.experts > 0 ? 1 : choose_splits(K, lay.tiles, M, g.wcol);
   const int wb_per_split = (nwb + z - 1) / z;
   // slices actually launched (rounding to whole block columns can drop some)
   const int splits = (nwb + wb_per_split - 1) / wb_per_split;
@@ -1255,6 +1289,12 @@ cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) 
     p.ys[m] = m < j.n_mat ? j.y[m] : nullptr;
   }
   p.gate_up = j.gate_up ? 1 : 0;
+  if (j.experts > 0) {
+    p.expert_off = j.expert_off;
+    p.expert_tiles = lay.tiles / j.experts;
+    p.expert_rows = (int)j.rows[0];
+  }
+  const int64_t max_rows = j.experts > 0 ? (j.expert_max_rows < M ? j.expert_max_rows : M) : M;
   cudaError_t e;
   if (pair) {
     p.N = (int)j.rows[0];
@@ -1264,7 +1304,8 @@ cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) 
     switch (j.dtype) {
 #define HYQ_RUN(F) \
   case F:          \
-    e = bn == 256 ? run<F, 256>(tw, tx, p, lay.tiles, splits, st) : run<F, 128>(tw, tx, p, lay.tiles, splits, st); \
+    e = bn == 256 ? run<F, 256>(tw, tx, p, lay.tiles, splits, max_rows, st)                                        \
+                  : run<F, 128>(tw, tx, p, lay.tiles, splits, max_rows, st);                                       \
     break;
       HYQ_RUN(Q4_K)
       HYQ_RUN(Q6_K)

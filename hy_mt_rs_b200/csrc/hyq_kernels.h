@@ -58,6 +58,16 @@ struct GemmJob {
   int64_t K = 0, M = 0;
   const float* x = nullptr;     // f32 [M, K]
   unsigned* status = nullptr;
+  // Expert mode (Moe::forward, model.rs:688-726): w[m] hold `experts`
+  // matrices of rows[m] rows each, back to back (a GGUF [K, rows, experts]
+  // tensor), and the M activation rows are grouped by expert: those of expert
+  // e are rows expert_off[e] .. expert_off[e + 1] (device memory, written by
+  // an earlier kernel in the stream; at most expert_max_rows per expert).
+  // Row i of the activations is row x_rows[i] of x (x_rows null: row i).
+  int experts = 0;
+  const int32_t* expert_off = nullptr;
+  int64_t expert_max_rows = 0;
+  const int32_t* x_rows = nullptr;
 };
 bool gemm_job_supported(const GemmJob& job);
 size_t gemm_job_workspace_bytes(const GemmJob& job);

@@ -1,0 +1,282 @@
+// Mixture-of-experts layer on the device (Moe::forward, hy-mt-rs
+// src/model.rs:688-767): router logits, sigmoid top-k routing, expert
+// assignment lists, the grouped expert products on the tensor cores
+// (hyq_gemm.cu, expert mode) and the weighted combine.
+//
+// The reference loops over experts on the host with one small matmul each;
+// here every step is one launch over all tokens and experts, and the expert
+// token lists stay in device memory (the expert products read them), so a
+// MoE layer needs no host round trip.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+
+#include "../../include/hyq.h"
+#include "hyq_common.cuh"
+#include "hyq_kernels.h"
+
+namespace hyq {
+namespace moe {
+
+// Router logits [tokens, experts] of an F32 router (the reference requires
+// F32 for the sigmoid router, model.rs:223-227): each logit is the
+// reference's batch-1 F32 row product, dot(row, x) in the x86 order
+// (quant.rs:225-238).  One CTA per token, the token row staged in shared
+// memory, a half-warp per expert.
+constexpr int kRouterMaxK = 16384;
+
+__global__ void __launch_bounds__(256) router_kernel(const float* __restrict__ w, const float* __restrict__ x, int K,
+                                                     int experts, float* __restrict__ logits) {
+  extern __shared__ float xs[];
+  const float* xr = x + (size_t)blockIdx.x * K;
+  for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = xr[i];
+  __syncthreads();
+  const int hw = threadIdx.x >> 4, lane = threadIdx.x & 31;
+  const unsigned mask = (lane & 16) ? 0xffff0000u : 0x0000ffffu;
+  for (int e = hw; e < experts; e += blockDim.x / 16) {
+    const float d = dot_x86(w + (size_t)e * K, xs, K, mask);
+    if ((lane & 15) == 0) logits[(size_t)blockIdx.x * experts + e] = d;
+  }
+}
+
+// route (model.rs:728-767) for one token per warp: sigmoid with the
+// reference's two branches, order by sigmoid + bias descending under
+// f32::total_cmp with ties to the lower index, keep `used`, then weights
+// sigmoid / max(sum of the kept sigmoids in that order, f16 MIN_POSITIVE)
+// * scale (normalize) or sigmoid * scale.
+constexpr int kRouteMaxExperts = 1024;
+constexpr float kF16MinPositive = 6.103515625e-05f;
+
+__device__ __forceinline__ int total_order_key(float v) {
+  const int b = __float_as_int(v);
+  return b ^ ((b >> 31) & 0x7fffffff);
+}
+
+__global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ logits, int tokens, int experts,
+                                                    const float* __restrict__ bias, int used, int normalize,
+                                                    float scale, int32_t* __restrict__ topk_idx,
+                                                    float* __restrict__ topk_w) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (t >= tokens) return;
+  const float* lg = logits + (size_t)t * experts;
+  constexpr int kPer = kRouteMaxExperts / 32;
+  float sig[kPer];
+  int key[kPer];  // total order of sigmoid + bias
+  const int per = (experts + 31) / 32;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    sig[j] = 0.f;
+    key[j] = INT_MIN;
+    if (j < per) {
+      const int e = lane + 32 * j;
+      if (e < experts) {
+        const float xv = lg[e];
+        float s;
+        if (xv >= 0.f) {
+          s = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-xv)));
+        } else {
+          const float ev = expf(xv);
+          s = __fdiv_rn(ev, __fadd_rn(1.0f, ev));
+        }
+        sig[j] = s;
+        key[j] = total_order_key(__fadd_rn(s, bias[e]));
+      }
+    }
+  }
+  float sum = 0.f;
+  uint32_t taken = 0u;  // bit j: expert lane + 32 j is already chosen
+  int my_e = 0;
+  float my_s = 0.f;
+  for (int k = 0; k < used; ++k) {
+    // the largest key, then the lowest expert index, among those not taken
+    int bk = INT_MIN, be = INT_MAX;
+    float bs = 0.f;
+    bool have = false;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      if (j < per) {
+        const int e = lane + 32 * j;
+        if (e < experts && !((taken >> j) & 1u) && (!have || key[j] > bk || (key[j] == bk && e < be))) {
+          bk = key[j];
+          be = e;
+          bs = sig[j];
+          have = true;
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const int ok = __shfl_xor_sync(0xffffffffu, bk, o);
+      const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+      const float os = __shfl_xor_sync(0xffffffffu, bs, o);
+      const int oh = __shfl_xor_sync(0xffffffffu, have ? 1 : 0, o);
+      if (oh && (!have || ok > bk || (ok == bk && oe < be))) {
+        bk = ok;
+        be = oe;
+        bs = os;
+        have = true;
+      }
+    }
+    if ((be & 31) == lane) taken |= 1u << (be >> 5);
+    if (lane == k) {
+      my_e = be;
+      my_s = bs;
+    }
+    sum = __fadd_rn(sum, bs);  // in the order chosen, as the reference's sum
+  }
+  if (!normalize) sum = 1.0f;
+  else sum = fmaxf(sum, kF16MinPositive);  // f32::max: a NaN sum gives the bound
+  if (lane < used) {
+    topk_idx[(size_t)t * used + lane] = my_e;
+    topk_w[(size_t)t * used + lane] = __fmul_rn(__fdiv_rn(my_s, sum), scale);
+  }
+}
+
+// Expert assignment lists (model.rs:695-701): for expert e, the tokens that
+// chose it in token order, as rows expert_off[e] .. expert_off[e + 1] of the
+// grouped activations: row_token (source token), row_weight (its routing
+// weight), and token_rows[t * used + k] = the row of token t's k-th choice.
+// One CTA; warp w scans tokens in order for experts w, w + 32, ...
+__global__ void __launch_bounds__(1024) group_kernel(const int32_t* __restrict__ topk_idx,
+                                                     const float* __restrict__ topk_w, int tokens, int experts,
+                                                     int used, int32_t* __restrict__ expert_off,
+                                                     int32_t* __restrict__ row_token, float* __restrict__ row_weight,
+                                                     int32_t* __restrict__ token_rows) {
+  extern __shared__ int32_t off_s[];  // experts + 1
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int pass = 0; pass < 2; ++pass) {
+    for (int e = warp; e < experts; e += nw) {
+      int run = pass ? off_s[e] : 0;
+      for (int t0 = 0; t0 < tokens; t0 += 32) {
+        const int t = t0 + lane;
+        int k_hit = -1;
+        if (t < tokens)
+          for (int k = 0; k < used; ++k)
+            if (topk_idx[(size_t)t * used + k] == e) k_hit = k;
+        const unsigned hits = __ballot_sync(0xffffffffu, k_hit >= 0);
+        if (pass && k_hit >= 0) {
+          const int row = run + __popc(hits & ((1u << lane) - 1u));
+          row_token[row] = t;
+          row_weight[row] = topk_w[(size_t)t * used + k_hit];
+          token_rows[(size_t)t * used + k_hit] = row;
+        }
+        run += __popc(hits);
+      }
+      if (!pass && lane == 0) off_s[e + 1] = run;  // count for now
+    }
+    __syncthreads();
+    if (!pass && threadIdx.x == 0) {
+      off_s[0] = 0;
+      for (int e = 0; e < experts; ++e) off_s[e + 1] += off_s[e];
+      for (int e = 0; e <= experts; ++e) expert_off[e] = off_s[e];
+    }
+    __syncthreads();
+  }
+}
+
+// output = shared; then for each expert in ascending order, output += weight
+// * value (model.rs:691, 715-723; separate f32 roundings).  One CTA per
+// token.
+__global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ shared, const float* __restrict__ y,
+                                                      int N, const int32_t* __restrict__ topk_idx,
+                                                      const int32_t* __restrict__ token_rows,
+                                                      const float* __restrict__ row_weight, int used,
+                                                      float* __restrict__ out) {
+  __shared__ int32_t ex_s[32], row_s[32];
+  __shared__ float w_s[32];
+  const int t = blockIdx.x;
+  if (threadIdx.x == 0) {
+    // the token's choices, sorted by expert (insertion sort of `used` items)
+    for (int k = 0; k < used; ++k) {
+      const int e = topk_idx[(size_t)t * used + k], r = token_rows[(size_t)t * used + k];
+      int i = k;
+      while (i > 0 && ex_s[i - 1] > e) {
+        ex_s[i] = ex_s[i - 1];
+        row_s[i] = row_s[i - 1];
+        --i;
+      }
+      ex_s[i] = e;
+      row_s[i] = r;
+    }
+    for (int k = 0; k < used; ++k) w_s[k] = row_weight[row_s[k]];
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < N; c += blockDim.x) {
+    float acc = shared[(size_t)t * N + c];
+    for (int k = 0; k < used; ++k) acc = __fadd_rn(acc, __fmul_rn(w_s[k], y[(size_t)row_s[k] * N + c]));
+    out[(size_t)t * N + c] = acc;
+  }
+}
+
+}  // namespace moe
+}  // namespace hyq
+
+extern "C" {
+
+int hyq_moe_router(const hyq_weight* router, const float* x, int64_t tokens, float* logits, void* stream) {
+  int dtype = 0, ndim = 0;
+  int64_t dims[3] = {};
+  const void* data = nullptr;
+  if (!router || !x || !logits) return hyq::api_fail(HYQ_E_INVALID, "moe_router: null pointer");
+  int rc = hyq_weight_info(router, &dtype, &ndim, dims, nullptr, &data);
+  if (rc) return rc;
+  if (dtype != HYQ_F32 || ndim != 2) return hyq::api_fail(HYQ_E_UNSUPPORTED, "moe_router: the router must be an F32 matrix");
+  const int64_t K = dims[0], E = dims[1];
+  if (tokens <= 0 || K <= 0 || K > hyq::moe::kRouterMaxK || E <= 0 || tokens > INT32_MAX)
+    return hyq::api_fail(HYQ_E_SHAPE, "moe_router: shape (input width at most %d)", hyq::moe::kRouterMaxK);
+  static int configured = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured != dev) {
+    cudaFuncSetAttribute(hyq::moe::router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         hyq::moe::kRouterMaxK * (int)sizeof(float));
+    configured = dev;
+  }
+  hyq::moe::router_kernel<<<(unsigned)tokens, 256, (size_t)K * sizeof(float), (cudaStream_t)stream>>>(
+      static_cast<const float*>(data), x, (int)K, (int)E, logits);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "moe_router: %s", cudaGetErrorString(e));
+}
+
+int hyq_moe_route(const float* logits, int64_t tokens, int experts, const float* bias, int used, int normalize,
+                  float scale, int32_t* topk_idx, float* topk_w, void* stream) {
+  if (!logits || !bias || !topk_idx || !topk_w) return hyq::api_fail(HYQ_E_INVALID, "moe_route: null pointer");
+  if (tokens <= 0 || tokens > INT32_MAX || experts <= 0 || experts > hyq::moe::kRouteMaxExperts || used <= 0 ||
+      used > experts || used > 32)
+    return hyq::api_fail(HYQ_E_SHAPE, "moe_route: shape (at most %d experts, 32 used)", hyq::moe::kRouteMaxExperts);
+  const unsigned blocks = (unsigned)((tokens + 7) / 8);
+  hyq::moe::route_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(logits, (int)tokens, experts, bias, used,
+                                                                   normalize, scale, topk_idx, topk_w);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "moe_route: %s", cudaGetErrorString(e));
+}
+
+int hyq_moe_group(const int32_t* topk_idx, const float* topk_w, int64_t tokens, int experts, int used,
+                  int32_t* expert_off, int32_t* row_token, float* row_weight, int32_t* token_rows, void* stream) {
+  if (!topk_idx || !topk_w || !expert_off || !row_token || !row_weight || !token_rows)
+    return hyq::api_fail(HYQ_E_INVALID, "moe_group: null pointer");
+  if (tokens <= 0 || tokens * used > INT32_MAX || experts <= 0 || experts > hyq::moe::kRouteMaxExperts || used <= 0 ||
+      used > 32)
+    return hyq::api_fail(HYQ_E_SHAPE, "moe_group: shape");
+  hyq::moe::group_kernel<<<1, 1024, (size_t)(experts + 1) * sizeof(int32_t), (cudaStream_t)stream>>>(
+      topk_idx, topk_w, (int)tokens, experts, used, expert_off, row_token, row_weight, token_rows);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "moe_group: %s", cudaGetErrorString(e));
+}
+
+int hyq_moe_combine(const float* shared, const float* expert_out, int64_t tokens, int64_t n, const int32_t* topk_idx,
+                    const int32_t* token_rows, const float* row_weight, int used, float* out, void* stream) {
+  if (!shared || !expert_out || !topk_idx || !token_rows || !row_weight || !out)
+    return hyq::api_fail(HYQ_E_INVALID, "moe_combine: null pointer");
+  if (tokens <= 0 || tokens > INT32_MAX || n <= 0 || n > INT32_MAX || used <= 0 || used > 32)
+    return hyq::api_fail(HYQ_E_SHAPE, "moe_combine: shape");
+  hyq::moe::combine_kernel<<<(unsigned)tokens, 256, 0, (cudaStream_t)stream>>>(shared, expert_out, (int)n, topk_idx,
+                                                                              token_rows, row_weight, used, out);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "moe_combine: %s", cudaGetErrorString(e));
+}
+
+}  // extern "C"

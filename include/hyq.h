@@ -277,6 +277,49 @@ int hyq_add_rms_norm(float* hidden, const float* delta, const float* w, int64_t 
 #define HYQ_ARGMAX_WORKSPACE_BYTES 16
 int hyq_argmax(const float* x, int64_t n, int32_t* token, int32_t* pos, void* workspace, void* stream);
 
+/* --- Mixture-of-experts layer (Moe::forward, model.rs:688-767) ----------
+ * The reference routes on the host and loops over experts with one small
+ * matmul each; these steps keep the routing, the expert token lists and the
+ * expert products on the device (no host round trip), in the reference's
+ * order of results:
+ *   hyq_moe_router      logits [tokens, experts] = x . router (F32 router,
+ *                       model.rs:223-227; each logit the batch-1 F32 row
+ *                       product, quant.rs:225-238, x86 dot order)
+ *   hyq_moe_route       route (model.rs:728-767) per token: sigmoid, top
+ *                       `used` of sigmoid + bias (f32::total_cmp, ties to the
+ *                       lower index), weights sigmoid / max(sum, f16
+ *                       MIN_POSITIVE) * scale (normalize) or sigmoid * scale;
+ *                       topk_idx/topk_w [tokens, used] in that order
+ *   hyq_moe_group       assignments (model.rs:695-701): the tokens of each
+ *                       expert in token order as rows expert_off[e] ..
+ *                       expert_off[e+1] of a grouped matrix (expert_off:
+ *                       experts + 1 ints; row_token, row_weight: tokens * used
+ *                       each; token_rows[t * used + k]: the row of token t's
+ *                       k-th choice)
+ *   hyq_matmul_experts_gate_up_silu / hyq_matmul_experts
+ *                       the expert FFN (DenseFfn::forward, model.rs:673-685)
+ *                       over the grouped rows on the tensor cores: weights are
+ *                       [K, N, experts] tensors (Weight::expert,
+ *                       quant.rs:144-154, gives expert e's slice); row i of
+ *                       the input is input row input_rows[i] (NULL: row i);
+ *                       output [rows, N] grouped; max_rows bounds any
+ *                       expert's rows (e.g. tokens).  fp16 operands, f32
+ *                       accumulation, as hyq_matmul at batch >= 16.
+ *   hyq_moe_combine     out = shared; out += weight * value per expert in
+ *                       ascending expert order (model.rs:691, 715-723). */
+int hyq_moe_router(const hyq_weight* router, const float* x, int64_t tokens, float* logits, void* stream);
+int hyq_moe_route(const float* logits, int64_t tokens, int experts, const float* bias, int used, int normalize,
+                  float scale, int32_t* topk_idx, float* topk_w, void* stream);
+int hyq_moe_group(const int32_t* topk_idx, const float* topk_w, int64_t tokens, int experts, int used,
+                  int32_t* expert_off, int32_t* row_token, float* row_weight, int32_t* token_rows, void* stream);
+int hyq_matmul_experts_gate_up_silu(const hyq_weight* gate, const hyq_weight* up, const float* input,
+                                    const int32_t* input_rows, int64_t rows, const int32_t* expert_off,
+                                    int64_t max_rows, float* out, void* stream);
+int hyq_matmul_experts(const hyq_weight* w, const float* input, const int32_t* input_rows, int64_t rows,
+                       const int32_t* expert_off, int64_t max_rows, float* out, void* stream);
+int hyq_moe_combine(const float* shared, const float* expert_out, int64_t tokens, int64_t n, const int32_t* topk_idx,
+                    const int32_t* token_rows, const float* row_weight, int used, float* out, void* stream);
+
 /* --- Tensor-parallel all-reduce over NVLink peer memory ------------------
  * No counterpart in the reference (CPU only).  Sums the row-parallel partial
  * products (O, down) of a tensor-parallel layer across the ranks of one node

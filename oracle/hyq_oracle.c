@@ -651,3 +651,49 @@ void hyo_attention(const float* q, const float* keys, const float* values, int h
   }
   free(scores);
 }
+
+/* route (model.rs:728-767) for one token: sigmoid with the reference's two
+ * branches; indices ordered by sigmoid + bias descending under
+ * f32::total_cmp (ties: lower index first); the first `used` kept; weights
+ * sigmoid / max(sum of the kept sigmoids in that order, f16 MIN_POSITIVE) *
+ * scale when normalize, else sigmoid / 1 * scale. */
+static int32_t hyo_total_key(float v) {
+  int32_t b;
+  memcpy(&b, &v, 4);
+  return b ^ (int32_t)((uint32_t)(b >> 31) >> 1);
+}
+
+void hyo_moe_route(const float* logits, int experts, const float* bias, int used, int normalize, float scale,
+                   int32_t* idx_out, float* w_out) {
+  float* sig = (float*)malloc(sizeof(float) * (size_t)experts);
+  int32_t* key = (int32_t*)malloc(sizeof(int32_t) * (size_t)experts);
+  char* taken = (char*)calloc((size_t)experts, 1);
+  for (int e = 0; e < experts; ++e) {
+    const float x = logits[e];
+    float s;
+    if (x >= 0.0f) {
+      s = 1.0f / (1.0f + expf(-x));
+    } else {
+      const float ev = expf(x);
+      s = ev / (1.0f + ev);
+    }
+    sig[e] = s;
+    key[e] = hyo_total_key(s + bias[e]);
+  }
+  float sum = 0.0f;
+  for (int k = 0; k < used; ++k) {
+    int best = -1;
+    for (int e = 0; e < experts; ++e)
+      if (!taken[e] && (best < 0 || key[e] > key[best])) best = e;  /* ties keep the lower index */
+    taken[best] = 1;
+    idx_out[k] = best;
+    sum += sig[best];
+  }
+  const float min_pos = 6.103515625e-05f; /* half::f16::MIN_POSITIVE */
+  if (!normalize) sum = 1.0f;
+  else if (!(sum >= min_pos)) sum = min_pos; /* f32::max: a NaN sum gives the bound */
+  for (int k = 0; k < used; ++k) w_out[k] = sig[idx_out[k]] / sum * scale;
+  free(sig);
+  free(key);
+  free(taken);
+}

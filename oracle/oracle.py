@@ -59,6 +59,8 @@ def lib():
                                           _f32p, C.c_int]
         L.hyo_gate_up_silu_q8.restype = None
         L.hyo_max_threads.argtypes = []
+        L.hyo_moe_route.argtypes = [_f32p, C.c_int, _f32p, C.c_int, C.c_int, C.c_float, C.POINTER(C.c_int32), _f32p]
+        L.hyo_moe_route.restype = None
         _LIB = L
     return _LIB
 
@@ -224,3 +226,17 @@ def attention(q, keys, values, heads, kv_heads, dim, past):
                         _p(np.ascontiguousarray(values, dtype=np.float32), _f32p), heads, kv_heads, dim, past,
                         _p(out, _f32p))
     return out
+
+
+def moe_route(logits, bias, used, normalize, scale):
+    """route (model.rs:728-767) per token of logits [tokens, experts]:
+    (indices [tokens, used] int32, weights [tokens, used] f32)."""
+    logits = np.ascontiguousarray(np.atleast_2d(logits), dtype=np.float32)
+    bias = np.ascontiguousarray(bias, dtype=np.float32)
+    T, E = logits.shape
+    idx = np.empty((T, used), dtype=np.int32)
+    w = np.empty((T, used), dtype=np.float32)
+    for t in range(T):
+        lib().hyo_moe_route(_p(logits[t], _f32p), E, _p(bias, _f32p), used, 1 if normalize else 0, scale,
+                            idx[t].ctypes.data_as(C.POINTER(C.c_int32)), _p(w[t], _f32p))
+    return idx, w

@@ -207,3 +207,39 @@ def test_matmul_batch_paths_agree():
         mag = np.abs(O.decode(t, w, N * K).reshape(N, K)).sum(1) * np.abs(x).max()
         assert np.all(np.abs(y3 - y1[:3]) <= 1e-5 * mag + 1e-6)
         assert np.all(np.abs(y9 - y1) <= 1e-5 * mag + 1e-6)
+
+
+def test_moe_route_matches_sort_semantics():
+    """hyo_moe_route (route, model.rs:728-767) against a Python restatement
+    with sorted(): total_cmp order of sigmoid + bias, ties to the lower
+    index, normalized weights with the f16 MIN_POSITIVE floor."""
+    import struct
+
+    def total_key(v):
+        b = struct.unpack("<i", struct.pack("<f", float(v)))[0]
+        return b ^ ((b >> 31) & 0x7FFFFFFF)
+
+    rng = np.random.default_rng(5)
+    E, used = 64, 8
+    logits = rng.standard_normal((20, E)).astype(np.float32) * 3
+    logits[0, :] = 0.0                       # every key tied: lowest indices win
+    logits[1, 5] = -100.0                    # sigmoid underflows toward 0
+    bias = (rng.standard_normal(E) * 0.1).astype(np.float32)
+    bias[7] = bias[9] = np.float32(0.0)
+    for normalize, scale in ((True, 2.5), (False, 1.0)):
+        idx, w = O.moe_route(logits, bias, used, normalize, scale)
+        for t in range(logits.shape[0]):
+            x = logits[t]
+            sig = np.where(x >= 0, np.float32(1) / (np.float32(1) + np.exp(-x)),
+                           np.exp(x) / (np.float32(1) + np.exp(x))).astype(np.float32)
+            keys = (sig + bias).astype(np.float32)
+            order = sorted(range(E), key=lambda i: (-total_key(keys[i]), i))[:used]
+            assert list(idx[t]) == order, t
+            s = np.float32(0)
+            for i in order:
+                s = np.float32(s + sig[i])
+            s = max(s, np.float32(6.103515625e-05)) if normalize else np.float32(1)
+            ref = np.array([np.float32(np.float32(sig[i] / s) * np.float32(scale)) for i in order], np.float32)
+            np.testing.assert_allclose(w[t], ref, rtol=2e-7)
+    idx0, _ = O.moe_route(logits[:1], np.zeros(E, np.float32), used, True, 1.0)
+    assert list(idx0[0]) == list(range(used))
