@@ -23,9 +23,23 @@ namespace moe {
 // Router logits [tokens, experts] of an F32 router (the reference requires
 // F32 for the sigmoid router, model.rs:223-227): each logit is the
 // reference's batch-1 F32 row product, dot(row, x) in the x86 order
-// (quant.rs:225-238).  One CTA per token, the token row staged in shared
-// memory, a half-warp per expert.
+// (quant.rs:225-238, 2562-2596).  One CTA per token with the token row in
+// shared memory; a half-warp per group of kRouterChains experts, lane l
+// carrying AVX2 accumulator lane l of each expert's dot (four independent
+// chains and unrolled loads keep the global reads in flight), then the
+// reference's lane sums.
 constexpr int kRouterMaxK = 16384;
+constexpr int kRouterChains = 4;
+
+__device__ __forceinline__ float x86_lane_sum(float acc, unsigned mask) {
+  // dot_avx2's reduction of its two 8-lane accumulators (K % 16 == 0)
+  const int lane = threadIdx.x & 31, l = lane & 15, base = lane & 16;
+  const float sum = __fadd_rn(acc, __shfl_sync(mask, acc, base + ((l + 8) & 15)));
+  float h = -0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) h = __fadd_rn(h, __shfl_sync(mask, sum, base + k));
+  return __fadd_rn(h, -0.0f);
+}
 
 __global__ void __launch_bounds__(256) router_kernel(const float* __restrict__ w, const float* __restrict__ x, int K,
                                                      int experts, float* __restrict__ logits) {
@@ -33,11 +47,34 @@ __global__ void __launch_bounds__(256) router_kernel(const float* __restrict__ w
   const float* xr = x + (size_t)blockIdx.x * K;
   for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = xr[i];
   __syncthreads();
-  const int hw = threadIdx.x >> 4, lane = threadIdx.x & 31;
+  const int hw = threadIdx.x >> 4, nhw = blockDim.x >> 4, lane = threadIdx.x & 31, l = lane & 15;
   const unsigned mask = (lane & 16) ? 0xffff0000u : 0x0000ffffu;
-  for (int e = hw; e < experts; e += blockDim.x / 16) {
-    const float d = dot_x86(w + (size_t)e * K, xs, K, mask);
-    if ((lane & 15) == 0) logits[(size_t)blockIdx.x * experts + e] = d;
+  if ((K & 15) == 0) {
+    for (int e0 = hw * kRouterChains; e0 < experts; e0 += nhw * kRouterChains) {
+      float acc[kRouterChains];
+      const float* wr[kRouterChains];
+#pragma unroll
+      for (int j = 0; j < kRouterChains; ++j) {
+        acc[j] = 0.f;
+        wr[j] = w + (size_t)min(e0 + j, experts - 1) * K + l;
+      }
+#pragma unroll 4
+      for (int c = 0; c < K / 16; ++c) {
+        const float xv = xs[16 * c + l];
+#pragma unroll
+        for (int j = 0; j < kRouterChains; ++j) acc[j] = fmaf(wr[j][16 * c], xv, acc[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < kRouterChains; ++j) {
+        const float d = x86_lane_sum(acc[j], mask);
+        if (l == 0 && e0 + j < experts) logits[(size_t)blockIdx.x * experts + e0 + j] = d;
+      }
+    }
+  } else {
+    for (int e = hw; e < experts; e += nhw) {
+      const float d = dot_x86(w + (size_t)e * K, xs, K, mask);
+      if (l == 0) logits[(size_t)blockIdx.x * experts + e] = d;
+    }
   }
 }
 
@@ -139,41 +176,77 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
 // chose it in token order, as rows expert_off[e] .. expert_off[e + 1] of the
 // grouped activations: row_token (source token), row_weight (its routing
 // weight), and token_rows[t * used + k] = the row of token t's k-th choice.
-// One CTA; warp w scans tokens in order for experts w, w + 32, ...
+// One CTA, tokens in chunks of kGroupChunk: a per-expert bitmap of the
+// chunk's tokens in shared memory gives each assignment its rank among the
+// expert's earlier tokens by prefix popcounts (pass 0 counts, pass 1 places).
+constexpr int kGroupChunk = 1024;
+constexpr int kGroupMaxExperts = 128;
+constexpr int kGroupWords = kGroupChunk / 32;
+
 __global__ void __launch_bounds__(1024) group_kernel(const int32_t* __restrict__ topk_idx,
                                                      const float* __restrict__ topk_w, int tokens, int experts,
                                                      int used, int32_t* __restrict__ expert_off,
                                                      int32_t* __restrict__ row_token, float* __restrict__ row_weight,
                                                      int32_t* __restrict__ token_rows) {
-  extern __shared__ int32_t off_s[];  // experts + 1
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __shared__ uint32_t bits[kGroupMaxExperts * kGroupWords];  // expert-major bitmaps of one chunk
+  __shared__ int32_t pre[kGroupMaxExperts * kGroupWords];    // tokens of the expert in earlier words
+  __shared__ int32_t base[kGroupMaxExperts + 1];             // rows of the expert placed so far (+ offset)
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const int nwords = experts * kGroupWords;
+  for (int e = tid; e <= experts; e += nt) base[e] = 0;
   for (int pass = 0; pass < 2; ++pass) {
-    for (int e = warp; e < experts; e += nw) {
-      int run = pass ? off_s[e] : 0;
-      for (int t0 = 0; t0 < tokens; t0 += 32) {
-        const int t = t0 + lane;
-        int k_hit = -1;
-        if (t < tokens)
-          for (int k = 0; k < used; ++k)
-            if (topk_idx[(size_t)t * used + k] == e) k_hit = k;
-        const unsigned hits = __ballot_sync(0xffffffffu, k_hit >= 0);
-        if (pass && k_hit >= 0) {
-          const int row = run + __popc(hits & ((1u << lane) - 1u));
-          row_token[row] = t;
-          row_weight[row] = topk_w[(size_t)t * used + k_hit];
-          token_rows[(size_t)t * used + k_hit] = row;
+    if (pass == 1) {
+      __syncthreads();
+      if (tid == 0) {
+        int run = 0;
+        for (int e = 0; e < experts; ++e) {
+          const int c = base[e];
+          base[e] = run;
+          expert_off[e] = run;
+          run += c;
         }
-        run += __popc(hits);
+        expert_off[experts] = run;
       }
-      if (!pass && lane == 0) off_s[e + 1] = run;  // count for now
     }
-    __syncthreads();
-    if (!pass && threadIdx.x == 0) {
-      off_s[0] = 0;
-      for (int e = 0; e < experts; ++e) off_s[e + 1] += off_s[e];
-      for (int e = 0; e <= experts; ++e) expert_off[e] = off_s[e];
+    for (int t0 = 0; t0 < tokens; t0 += kGroupChunk) {
+      __syncthreads();
+      for (int i = tid; i < nwords; i += nt) bits[i] = 0u;
+      __syncthreads();
+      const int t = t0 + tid;
+      const bool live = tid < kGroupChunk && t < tokens;
+      if (live)
+        for (int k = 0; k < used; ++k)
+          atomicOr(&bits[topk_idx[(size_t)t * used + k] * kGroupWords + (tid >> 5)], 1u << (tid & 31));
+      __syncthreads();
+      // prefix popcounts over each expert's words (one warp per expert row)
+      for (int e = tid >> 5; e < experts; e += nt >> 5) {
+        const int lane = tid & 31;
+        const int c = __popc(bits[e * kGroupWords + lane]);
+        int incl = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int v = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += v;
+        }
+        pre[e * kGroupWords + lane] = incl - c;
+      }
+      __syncthreads();
+      if (pass == 1 && live) {
+        for (int k = 0; k < used; ++k) {
+          const int e = topk_idx[(size_t)t * used + k];
+          const int wd = tid >> 5;
+          const int rank = pre[e * kGroupWords + wd] + __popc(bits[e * kGroupWords + wd] & ((1u << (tid & 31)) - 1u));
+          const int row = base[e] + rank;
+          row_token[row] = t;
+          row_weight[row] = topk_w[(size_t)t * used + k];
+          token_rows[(size_t)t * used + k] = row;
+        }
+      }
+      __syncthreads();
+      // this chunk's tokens per expert
+      for (int e = tid; e < experts; e += nt)
+        base[e] += pre[e * kGroupWords + kGroupWords - 1] + __popc(bits[e * kGroupWords + kGroupWords - 1]);
     }
-    __syncthreads();
   }
 }
 
@@ -258,10 +331,10 @@ int hyq_moe_group(const int32_t* topk_idx, const float* topk_w, int64_t tokens, 
                   int32_t* expert_off, int32_t* row_token, float* row_weight, int32_t* token_rows, void* stream) {
   if (!topk_idx || !topk_w || !expert_off || !row_token || !row_weight || !token_rows)
     return hyq::api_fail(HYQ_E_INVALID, "moe_group: null pointer");
-  if (tokens <= 0 || tokens * used > INT32_MAX || experts <= 0 || experts > hyq::moe::kRouteMaxExperts || used <= 0 ||
+  if (tokens <= 0 || tokens * used > INT32_MAX || experts <= 0 || experts > hyq::moe::kGroupMaxExperts || used <= 0 ||
       used > 32)
-    return hyq::api_fail(HYQ_E_SHAPE, "moe_group: shape");
-  hyq::moe::group_kernel<<<1, 1024, (size_t)(experts + 1) * sizeof(int32_t), (cudaStream_t)stream>>>(
+    return hyq::api_fail(HYQ_E_SHAPE, "moe_group: shape (at most %d experts)", hyq::moe::kGroupMaxExperts);
+  hyq::moe::group_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(
       topk_idx, topk_w, (int)tokens, experts, used, expert_off, row_token, row_weight, token_rows);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "moe_group: %s", cudaGetErrorString(e));

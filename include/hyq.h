@@ -293,7 +293,7 @@ int hyq_argmax(const float* x, int64_t n, int32_t* token, int32_t* pos, void* wo
  *   hyq_moe_group       assignments (model.rs:695-701): the tokens of each
  *                       expert in token order as rows expert_off[e] ..
  *                       expert_off[e+1] of a grouped matrix (expert_off:
- *                       experts + 1 ints; row_token, row_weight: tokens * used
+ *                       experts + 1 ints, at most 128 experts; row_token, row_weight: tokens * used
  *                       each; token_rows[t * used + k]: the row of token t's
  *                       k-th choice)
  *   hyq_matmul_experts_gate_up_silu / hyq_matmul_experts
