@@ -923,9 +923,8 @@ def model_arm(a):
             model.graph.replay()
         model.reset()
         e0.record(stream)
-        for i in range(n_prompt):  # the prompt, one step per token
-            model.token.copy_(ids[i:i + 1])
-            model.graph.replay()
+        for c0 in range(0, n_prompt, model.chunk):  # the prompt: batched forwards (model.rs:549-646)
+            model.prefill(ids[c0:c0 + model.chunk])
         e1.record(stream)
         stream.synchronize()
         sampler.start()
@@ -937,9 +936,8 @@ def model_arm(a):
         sampler.stop()
         # e2e: the serving loop reads every new token back to the host
         model.reset()
-        for i in range(n_prompt):
-            model.token.copy_(ids[i:i + 1])
-            model.graph.replay()
+        for c0 in range(0, n_prompt, model.chunk):
+            model.prefill(ids[c0:c0 + model.chunk])
         # one step of lookahead: step i+1 is enqueued before the host waits
         # for token i, as a streaming server does (it stops on a token it
         # has read, one step late)
@@ -958,6 +956,24 @@ def model_arm(a):
         done[n_new - 2].synchronize()
         got.append(int(tok_host[n_new - 2]))
         e2e_s = time.perf_counter() - t0
+        # one whole request from the host: prompt ids in, batched prefill,
+        # n_new - 1 greedy steps, every token read back
+        ids_host = torch.tensor(prompt, dtype=torch.int32).pin_memory()
+        ids_dev = torch.empty_like(ids_host, device=dev)
+        stream.synchronize()
+        t0 = time.perf_counter()
+        model.reset()
+        ids_dev.copy_(ids_host, non_blocking=True)
+        for c0 in range(0, n_prompt, model.chunk):
+            model.prefill(ids_dev[c0:c0 + model.chunk])
+        for i in range(n_new - 1):
+            model.graph.replay()
+            tok_host[i:i + 1].copy_(model.token, non_blocking=True)
+            done[i].record(stream)
+            if i:
+                done[i - 1].synchronize()
+        done[n_new - 2].synchronize()
+        request_s = time.perf_counter() - t0
     failed = device_failed(quant, dev)
     (ms_decode, ms_prompt, failed), clocks_all = reduce_over_ranks(
         [e1b.elapsed_time(e2), e0.elapsed_time(e1), failed + 0.0], sampler.summary(), dev)
@@ -990,13 +1006,17 @@ def model_arm(a):
                   "batch 1, greedy)",
         "value": round(tok_s, 1), "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": max(3, a.warmup),
         "ms_per_step": round(ms_decode / steps, 4), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32 activations x packed int weights; f32 KV cache",
+        # the reference's published 1.8B Q2_0C decode rate, one request (M2 Pro)
+        "vs_baseline": round(tok_s / 86.86, 2), "vs_baseline_number": "86.86 tokens/s, 1.8B Q2_0C, 1 request",
+        "dtype": "f32 activations x packed int weights; f32 KV cache",
         "data": "synthetic (seeded random-init weights, 256 seeded random prompt ids)",
         "config": {"workload": "hy-mt-rs config 4: 32 layers, hidden 2048, 16/4 heads x 128, SwiGLU 6144, "
-                               "vocab 120832, RoPE 10000; 256-token prompt (one step per token), 256 generated",
+                               "vocab 120832, RoPE 10000; 256-token prompt (batched prefill), 256 generated",
                    "concurrency": 1, "positions": cfg.positions, "launch_overlap": True,
                    "parallelism": f"replicas x{world}"},
         "prompt_ms": round(ms_prompt, 2),
+        "prompt": "256 tokens in one batched forward (tensor-core projections, causal attention)",
+        "request_ms": round(request_s * 1e3, 2),
         "weight_gb_s": round(token_bytes / (ms_decode / steps * 1e-3) / 1e9, 1),
         "roofline": {"bound": "hbm", "kernel": "whole decode step (weights per token)", "unit": "GB/s",
                      "achieved": round(token_bytes / (ms_decode / steps * 1e-3) / 1e9, 1), "peak": peak,

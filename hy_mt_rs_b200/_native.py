@@ -73,11 +73,11 @@ _SIGS = {
     "hyq_set_launch_overlap": ([C.c_int], C.c_int),
     "hyq_rope_table": ([_i64, C.c_int, C.c_float, _vp, _vp], C.c_int),
     "hyq_rms_norm": ([_vp, _vp, _i64, _i64, C.c_float, _vp, _vp], C.c_int),
-    "hyq_embed": ([_wp, _vp, _vp, _vp], C.c_int),
-    "hyq_rope_qk": ([_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _i64, _vp, _vp, _vp, C.c_float, C.c_int,
+    "hyq_embed": ([_wp, _vp, _i64, _vp, _vp], C.c_int),
+    "hyq_rope_qk": ([_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _i64, _vp, _i64, _vp, _vp, C.c_float, C.c_int,
                      _vp, _vp, _vp], C.c_int),
-    "hyq_attention_workspace_bytes": ([C.c_int, C.c_int, _i64, C.POINTER(C.c_size_t)], C.c_int),
-    "hyq_attention": ([_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _i64, _vp, _vp, _vp, _vp], C.c_int),
+    "hyq_attention_workspace_bytes": ([C.c_int, C.c_int, _i64, _i64, C.POINTER(C.c_size_t)], C.c_int),
+    "hyq_attention": ([_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _i64, _vp, _i64, _vp, _vp, _vp], C.c_int),
     "hyq_add": ([_vp, _vp, _i64, _vp], C.c_int),
     "hyq_moe_router": ([_vp, _vp, _i64, _vp, _vp], C.c_int),
     "hyq_moe_route": ([_vp, _i64, C.c_int, _vp, C.c_int, C.c_int, C.c_float, _vp, _vp, _vp], C.c_int),
@@ -85,8 +85,8 @@ _SIGS = {
     "hyq_matmul_experts_gate_up_silu": ([_vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _vp], C.c_int),
     "hyq_matmul_experts": ([_vp, _vp, _vp, _i64, _vp, _i64, _vp, _vp], C.c_int),
     "hyq_moe_combine": ([_vp, _vp, _i64, _i64, _vp, _vp, _vp, C.c_int, _vp, _vp], C.c_int),
-    "hyq_add_rms_norm": ([_vp, _vp, _vp, _i64, C.c_float, _vp, _vp], C.c_int),
-    "hyq_argmax": ([_vp, _i64, _vp, _vp, _vp, _vp], C.c_int),
+    "hyq_add_rms_norm": ([_vp, _vp, _vp, _i64, _i64, C.c_float, _vp, _vp], C.c_int),
+    "hyq_argmax": ([_vp, _i64, _vp, _vp, C.c_int, _vp, _vp], C.c_int),
     "hyq_peer_alloc": ([C.c_size_t, C.POINTER(_vp), _vp], C.c_int),
     "hyq_peer_open": ([_vp, C.POINTER(_vp)], C.c_int),
     "hyq_peer_close": ([_vp], C.c_int),

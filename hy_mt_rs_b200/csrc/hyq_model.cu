@@ -91,15 +91,16 @@ __global__ void __launch_bounds__(256) embed_kernel(const uint8_t* __restrict__ 
                                                      float* __restrict__ out, unsigned* status) {
   grid_dependency_wait();
   allow_dependents_launch();
-  const int64_t tok = *token;
+  const int64_t tok = token[blockIdx.y];  // output row blockIdx.y
   if (tok < 0 || tok >= rows) {
     if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(status, DEV_BAD_ARGS);
     return;
   }
   const uint8_t* row = w + tok * row_bytes;
+  float* o = out + (size_t)blockIdx.y * n;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t b = i / block_len(T);
-    out[i] = decode_elem<T>(row + b * block_bytes(T), (int)(i - b * block_len(T)));
+    o[i] = decode_elem<T>(row + b * block_bytes(T), (int)(i - b * block_len(T)));
   }
 }
 
@@ -152,14 +153,16 @@ __device__ void head_rope(float* hd, const float* c, const float* s, int dim) {
 __global__ void __launch_bounds__(32) rope_qk_kernel(const __grid_constant__ RopeArgs a) {
   grid_dependency_wait();
   allow_dependents_launch();
-  const int pos = *a.pos;
-  if (pos < 0 || pos >= a.positions) {
+  const int tok = blockIdx.y;  // token tok of the batch sits at position *pos + tok
+  const int pos = *a.pos + tok;
+  if (*a.pos < 0 || pos >= a.positions) {
     if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(a.status, DEV_BAD_ARGS);
     return;
   }
   const int h = blockIdx.x;
   const bool is_q = h < a.heads;
-  float* hd = is_q ? a.q + (size_t)h * a.dim : a.k + (size_t)(h - a.heads) * a.dim;
+  const size_t qrow = (size_t)tok * a.heads * a.dim, krow = (size_t)tok * a.kv_heads * a.dim;
+  float* hd = is_q ? a.q + qrow + (size_t)h * a.dim : a.k + krow + (size_t)(h - a.heads) * a.dim;
   const float* nw = is_q ? a.q_norm : a.k_norm;
   const float* c = a.cos_tab + (size_t)pos * (a.dim / 2);
   const float* s = a.sin_tab + (size_t)pos * (a.dim / 2);
@@ -175,7 +178,7 @@ __global__ void __launch_bounds__(32) rope_qk_kernel(const __grid_constant__ Rop
     const size_t width = (size_t)a.kv_heads * a.dim;
     float* kc = a.k_cache + (size_t)pos * width + (size_t)kh * a.dim;
     float* vc = a.v_cache + (size_t)pos * width + (size_t)kh * a.dim;
-    const float* vv = a.v + (size_t)kh * a.dim;
+    const float* vv = a.v + krow + (size_t)kh * a.dim;
     for (int i = threadIdx.x; i < a.dim; i += 32) {
       kc[i] = hs[i];
       vc[i] = vv[i];
@@ -196,8 +199,8 @@ constexpr int kAttnChunk = 64;
 constexpr int kAttnThreads = 128;
 constexpr int kAttnMaxDim = 256;
 
-// Per-head counters at the head of the workspace, padded to 256 bytes.
-inline size_t attn_counter_bytes(int heads) { return ((size_t)heads * sizeof(unsigned) + 255) / 256 * 256; }
+// Counters per (token, head) at the head of the workspace, padded to 256 bytes.
+inline size_t attn_counter_bytes(int64_t slots) { return ((size_t)slots * sizeof(unsigned) + 255) / 256 * 256; }
 
 struct AttnArgs {
   const float* q;
@@ -207,8 +210,8 @@ struct AttnArgs {
   const int32_t* pos;
   int positions;
   float* out;
-  float* ws;           // [heads][splits][2 + dim]
-  unsigned* counters;  // [heads], zero between calls
+  float* ws;           // [tokens][heads][splits][2 + dim]
+  unsigned* counters;  // [tokens][heads], zero between calls
   unsigned* status;
 };
 
@@ -220,8 +223,11 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
   __shared__ float cw_s[kMaxPositions / kAttnChunk];
   __shared__ float bc[2];
   __shared__ int last_s;
-  const int pos = *a.pos;
-  if (pos < 0 || pos >= a.positions) {
+  // token tok of the batch sits at position *pos + tok and sees positions
+  // 0 ..= it (causal, model.rs:959)
+  const int tok = blockIdx.z;
+  const int pos = *a.pos + tok;
+  if (*a.pos < 0 || pos >= a.positions) {
     if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) atomicOr(a.status, DEV_BAD_ARGS);
     return;
   }
@@ -234,7 +240,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
   const size_t width = (size_t)a.kv_heads * dim;
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)dim));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int d = threadIdx.x; d < dim; d += kAttnThreads) q_s[d] = a.q[(size_t)h * dim + d];
+  const size_t th = (size_t)tok * a.heads + h;  // (token, head) slot
+  for (int d = threadIdx.x; d < dim; d += kAttnThreads) q_s[d] = a.q[th * dim + d];
   __syncthreads();
   const int p0 = split * kAttnChunk;
   const int n = min(kAttnChunk, visible - p0);
@@ -268,7 +275,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
   }
   __syncthreads();
   const int nsplit = (a.positions + kAttnChunk - 1) / kAttnChunk;
-  float* w = a.ws + ((size_t)h * nsplit + split) * (2 + dim);
+  float* w = a.ws + (th * nsplit + split) * (2 + dim);
   for (int d = threadIdx.x; d < dim; d += kAttnThreads) {
     const float* vr = a.v_cache + (size_t)p0 * width + (size_t)kvh * dim + d;
     float o = 0.f;
@@ -282,12 +289,12 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
   // the last CTA of this head combines the splits
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) last_s = atomicAdd(&a.counters[h], 1u) == (unsigned)(used - 1);
+  if (threadIdx.x == 0) last_s = atomicAdd(&a.counters[th], 1u) == (unsigned)(used - 1);
   __syncthreads();
   if (!last_s) return;
   __threadfence();
   // partials of other CTAs are read past L1 (__ldcg)
-  const float* wh = a.ws + (size_t)h * nsplit * (2 + dim);
+  const float* wh = a.ws + th * nsplit * (2 + dim);
   const size_t stride = 2 + (size_t)dim;
   if (warp == 0) {
     float m = -INFINITY;
@@ -309,9 +316,9 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
   for (int d = threadIdx.x; d < dim; d += kAttnThreads) {
     float o = 0.f;
     for (int i = 0; i < used; ++i) o = fmaf(__ldcg(wh + i * stride + 2 + d), cw_s[i], o);
-    a.out[(size_t)h * dim + d] = o * inv;
+    a.out[th * dim + d] = o * inv;
   }
-  if (threadIdx.x == 0) a.counters[h] = 0;  // ready for the next call
+  if (threadIdx.x == 0) a.counters[th] = 0;  // ready for the next call
 }
 
 __global__ void __launch_bounds__(256) add_kernel(float* __restrict__ dst, const float* __restrict__ src, int64_t n) {
@@ -331,12 +338,14 @@ __global__ void __launch_bounds__(256) add_rms_norm_kernel(float* __restrict__ h
   grid_dependency_wait();
   allow_dependents_launch();
   extern __shared__ float xs[];
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = __fadd_rn(hidden[i], delta[i]);
-    hidden[i] = v;
-    xs[i] = v;
-  }
+  const size_t r = (size_t)blockIdx.x * n;  // one CTA per row
+  hidden += r;
+  delta += r;
+  out += r;
+#pragma unroll 4
+  for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = __fadd_rn(hidden[i], delta[i]);
   __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) hidden[i] = xs[i];
   const float scale = staged_rms_scale(xs, n, eps);
   for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(xs[i], scale), w[i]);
 }
@@ -357,7 +366,7 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, unsigned i) {
 }
 
 __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __restrict__ x, int n, int32_t* token,
-                                                                int32_t* pos, unsigned long long* ws) {
+                                                                int32_t* pos, int pos_step, unsigned long long* ws) {
   grid_dependency_wait();
   allow_dependents_launch();
   unsigned long long best = 0ull;
@@ -385,7 +394,7 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __r
       const unsigned long long k = atomicExch(&ws[0], 0ull);
       atomicExch(reinterpret_cast<unsigned*>(&ws[1]), 0u);
       *token = k ? (int32_t)(0xffffffffu - (unsigned)(k & 0xffffffffull)) : 0;
-      if (pos) *pos += 1;
+      if (pos) *pos += pos_step;
     }
   }
 }
@@ -425,7 +434,7 @@ int hyq_rms_norm(const float* x, const float* w, int64_t n, int64_t rows, float 
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "rms_norm: %s", cudaGetErrorString(e));
 }
 
-int hyq_embed(const hyq_weight* w, const int32_t* token, float* out, void* stream) {
+int hyq_embed(const hyq_weight* w, const int32_t* token, int64_t count, float* out, void* stream) {
   int dtype = 0, ndim = 0;
   int64_t dims[3] = {};
   const void* data = nullptr;
@@ -433,6 +442,7 @@ int hyq_embed(const hyq_weight* w, const int32_t* token, float* out, void* strea
   int rc = hyq_weight_info(w, &dtype, &ndim, dims, nullptr, &data);
   if (rc) return rc;
   if (ndim != 2) return hyq::api_fail(HYQ_E_SHAPE, "embed: weight is not a matrix");
+  if (count <= 0 || count > 65535) return hyq::api_fail(HYQ_E_SHAPE, "embed: 1 to 65535 tokens");
   unsigned* status = nullptr;
   if ((rc = hyq::api_status_word(&status))) return rc;
   const int64_t n = dims[0], rows = dims[1];
@@ -442,19 +452,19 @@ int hyq_embed(const hyq_weight* w, const int32_t* token, float* out, void* strea
   const uint8_t* wd = static_cast<const uint8_t*>(data);
   cudaError_t e = cudaSuccess;
   switch (dtype) {
-    case hyq::F32: e = hyq::model::launch(hyq::model::embed_kernel<hyq::F32>, dim3(blocks), dim3(256), 0, st, wd, rb, n, rows, token, out, status); break;
-    case hyq::F16: e = hyq::model::launch(hyq::model::embed_kernel<hyq::F16>, dim3(blocks), dim3(256), 0, st, wd, rb, n, rows, token, out, status); break;
-    case hyq::Q4_K: e = hyq::model::launch(hyq::model::embed_kernel<hyq::Q4_K>, dim3(blocks), dim3(256), 0, st, wd, rb, n, rows, token, out, status); break;
-    case hyq::Q6_K: e = hyq::model::launch(hyq::model::embed_kernel<hyq::Q6_K>, dim3(blocks), dim3(256), 0, st, wd, rb, n, rows, token, out, status); break;
-    case hyq::Q8_0: e = hyq::model::launch(hyq::model::embed_kernel<hyq::Q8_0>, dim3(blocks), dim3(256), 0, st, wd, rb, n, rows, token, out, status); break;
-    case hyq::Q2_0C: e = hyq::model::launch(hyq::model::embed_kernel<hyq::Q2_0C>, dim3(blocks), dim3(256), 0, st, wd, rb, n, rows, token, out, status); break;
-    default: e = hyq::model::launch(hyq::model::embed_kernel<hyq::STQ1_0>, dim3(blocks), dim3(256), 0, st, wd, rb, n, rows, token, out, status); break;
+    case hyq::F32: e = hyq::model::launch(hyq::model::embed_kernel<hyq::F32>, dim3(blocks, (unsigned)count), dim3(256), 0, st, wd, rb, n, rows, token, out, status); break;
+    case hyq::F16: e = hyq::model::launch(hyq::model::embed_kernel<hyq::F16>, dim3(blocks, (unsigned)count), dim3(256), 0, st, wd, rb, n, rows, token, out, status); break;
+    case hyq::Q4_K: e = hyq::model::launch(hyq::model::embed_kernel<hyq::Q4_K>, dim3(blocks, (unsigned)count), dim3(256), 0, st, wd, rb, n, rows, token, out, status); break;
+    case hyq::Q6_K: e = hyq::model::launch(hyq::model::embed_kernel<hyq::Q6_K>, dim3(blocks, (unsigned)count), dim3(256), 0, st, wd, rb, n, rows, token, out, status); break;
+    case hyq::Q8_0: e = hyq::model::launch(hyq::model::embed_kernel<hyq::Q8_0>, dim3(blocks, (unsigned)count), dim3(256), 0, st, wd, rb, n, rows, token, out, status); break;
+    case hyq::Q2_0C: e = hyq::model::launch(hyq::model::embed_kernel<hyq::Q2_0C>, dim3(blocks, (unsigned)count), dim3(256), 0, st, wd, rb, n, rows, token, out, status); break;
+    default: e = hyq::model::launch(hyq::model::embed_kernel<hyq::STQ1_0>, dim3(blocks, (unsigned)count), dim3(256), 0, st, wd, rb, n, rows, token, out, status); break;
   }
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "embed: %s", cudaGetErrorString(e));
 }
 
 int hyq_rope_qk(float* q, float* k, const float* v, int heads, int kv_heads, int head_dim, const float* cos_tab,
-                const float* sin_tab, int64_t positions, const int32_t* pos, const float* q_norm,
+                const float* sin_tab, int64_t positions, const int32_t* pos, int64_t tokens, const float* q_norm,
                 const float* k_norm, float eps, int norm_first, float* k_cache, float* v_cache, void* stream) {
   if (!q || !k || !v || !cos_tab || !sin_tab || !pos || !k_cache || !v_cache)
     return hyq::api_fail(HYQ_E_INVALID, "rope_qk: null pointer");
@@ -480,22 +490,27 @@ int hyq_rope_qk(float* q, float* k, const float* v, int heads, int kv_heads, int
   a.v_cache = v_cache;
   int rc = hyq::api_status_word(&a.status);
   if (rc) return rc;
-  const cudaError_t e = hyq::model::launch(hyq::model::rope_qk_kernel, dim3((unsigned)(heads + kv_heads)), dim3(32), 0,
-                                           (cudaStream_t)stream, a);
+  if (tokens <= 0 || tokens > 65535 || tokens > positions)
+    return hyq::api_fail(HYQ_E_SHAPE, "rope_qk: 1 to %d tokens", (int)(positions < 65535 ? positions : 65535));
+  const cudaError_t e = hyq::model::launch(hyq::model::rope_qk_kernel, dim3((unsigned)(heads + kv_heads),
+                                           (unsigned)tokens), dim3(32), 0, (cudaStream_t)stream, a);
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "rope_qk: %s", cudaGetErrorString(e));
 }
 
-int hyq_attention_workspace_bytes(int heads, int head_dim, int64_t positions, size_t* bytes) {
+int hyq_attention_workspace_bytes(int heads, int head_dim, int64_t positions, int64_t tokens, size_t* bytes) {
   if (!bytes) return hyq::api_fail(HYQ_E_INVALID, "attention_workspace_bytes: null pointer");
-  if (heads <= 0 || head_dim <= 0 || positions <= 0)
+  if (heads <= 0 || head_dim <= 0 || positions <= 0 || tokens <= 0)
     return hyq::api_fail(HYQ_E_SHAPE, "attention_workspace_bytes: shape");
   const int64_t splits = (positions + hyq::model::kAttnChunk - 1) / hyq::model::kAttnChunk;
-  *bytes = hyq::model::attn_counter_bytes(heads) + (size_t)heads * splits * (2 + head_dim) * sizeof(float);
+  // the counter region does not depend on the call's token count (at most
+  // `positions`), so calls with different counts share one workspace
+  *bytes = hyq::model::attn_counter_bytes(positions * heads) +
+           (size_t)tokens * heads * splits * (2 + head_dim) * sizeof(float);
   return HYQ_OK;
 }
 
 int hyq_attention(const float* q, const float* k_cache, const float* v_cache, int heads, int kv_heads,
-                  int head_dim, int64_t positions, const int32_t* pos, float* out, void* workspace,
+                  int head_dim, int64_t positions, const int32_t* pos, int64_t tokens, float* out, void* workspace,
                   void* stream) {
   if (!q || !k_cache || !v_cache || !pos || !out || !workspace)
     return hyq::api_fail(HYQ_E_INVALID, "attention: null pointer");
@@ -515,11 +530,13 @@ int hyq_attention(const float* q, const float* k_cache, const float* v_cache, in
   a.positions = (int)positions;
   a.out = out;
   a.counters = static_cast<unsigned*>(workspace);
-  a.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + hyq::model::attn_counter_bytes(heads));
+  if (tokens <= 0 || tokens > 65535 || tokens > positions)
+    return hyq::api_fail(HYQ_E_SHAPE, "attention: 1 to %d tokens", (int)(positions < 65535 ? positions : 65535));
+  a.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + hyq::model::attn_counter_bytes(positions * heads));
   int rc = hyq::api_status_word(&a.status);
   if (rc) return rc;
   const unsigned splits = (unsigned)((positions + hyq::model::kAttnChunk - 1) / hyq::model::kAttnChunk);
-  const cudaError_t e = hyq::model::launch(hyq::model::attention_kernel, dim3(splits, (unsigned)heads),
+  const cudaError_t e = hyq::model::launch(hyq::model::attention_kernel, dim3(splits, (unsigned)heads, (unsigned)tokens),
                                            dim3(hyq::model::kAttnThreads), 0, (cudaStream_t)stream, a);
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "attention: %s", cudaGetErrorString(e));
 }
@@ -532,19 +549,20 @@ int hyq_add(float* dst, const float* src, int64_t n, void* stream) {
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "add: %s", cudaGetErrorString(e));
 }
 
-int hyq_add_rms_norm(float* hidden, const float* delta, const float* w, int64_t n, float eps, float* out,
-                     void* stream) {
+int hyq_add_rms_norm(float* hidden, const float* delta, const float* w, int64_t n, int64_t rows, float eps,
+                     float* out, void* stream) {
   if (!hidden || !delta || !w || !out) return hyq::api_fail(HYQ_E_INVALID, "add_rms_norm: null pointer");
-  if (n <= 0 || n > hyq::model::kNormMaxN)
+  if (n <= 0 || n > hyq::model::kNormMaxN || rows <= 0 || rows > INT32_MAX)
     return hyq::api_fail(HYQ_E_SHAPE, "add_rms_norm: 1 to %d columns", hyq::model::kNormMaxN);
   hyq::model::norm_smem_limit(hyq::model::add_rms_norm_kernel);
-  const cudaError_t e = hyq::model::launch(hyq::model::add_rms_norm_kernel, dim3(1), dim3(256),
+  const cudaError_t e = hyq::model::launch(hyq::model::add_rms_norm_kernel, dim3((unsigned)rows), dim3(256),
                                            (size_t)n * sizeof(float), (cudaStream_t)stream, hidden, delta, w, (int)n,
                                            eps, out);
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "add_rms_norm: %s", cudaGetErrorString(e));
 }
 
-int hyq_argmax(const float* x, int64_t n, int32_t* token, int32_t* pos, void* workspace, void* stream) {
+int hyq_argmax(const float* x, int64_t n, int32_t* token, int32_t* pos, int pos_step, void* workspace,
+               void* stream) {
   if (!x || !token || !workspace) return hyq::api_fail(HYQ_E_INVALID, "argmax: null pointer");
   if (n <= 0 || n > INT32_MAX) return hyq::api_fail(HYQ_E_SHAPE, "argmax: length");
   if (reinterpret_cast<uintptr_t>(workspace) % 8) return hyq::api_fail(HYQ_E_INVALID, "argmax: workspace alignment");
@@ -556,7 +574,7 @@ int hyq_argmax(const float* x, int64_t n, int32_t* token, int32_t* pos, void* wo
   if (blocks > sms) blocks = sms;
   const cudaError_t e = hyq::model::launch(hyq::model::argmax_kernel, dim3((unsigned)blocks),
                                            dim3(hyq::model::kArgmaxThreads), 0, (cudaStream_t)stream, x, (int)n,
-                                           token, pos, static_cast<unsigned long long*>(workspace));
+                                           token, pos, pos_step, static_cast<unsigned long long*>(workspace));
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "argmax: %s", cudaGetErrorString(e));
 }
 

@@ -61,11 +61,26 @@ def _p(t):
     return C.c_void_p(t.data_ptr())
 
 
+PREFILL_CHUNK = 256  # tokens per batched forward (model.rs:18, 353)
+
+
+class _Acts:
+    """Activation buffers of a forward over M tokens (rows)."""
+
+    def __init__(self, cfg, M, device):
+        H, A, KV, F = cfg.hidden, cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim, cfg.ffn
+        z = lambda *n: torch.zeros(*n, device=device)  # noqa: E731
+        self.M = M
+        self.hidden, self.normalized, self.attended = z(M, H), z(M, H), z(M, A)
+        self.projected, self.ff, self.gate = z(M, H), z(M, H), z(M, F)
+        self.q, self.k, self.v = z(M, A), z(M, KV), z(M, KV)
+
+
 class DenseModel:
-    def __init__(self, cfg, weights, device):
+    def __init__(self, cfg, weights, device, prefill_chunk=PREFILL_CHUNK):
         self.cfg = cfg
         self.device = device
-        H, A, KV, F = cfg.hidden, cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim, cfg.ffn
+        H, KV = cfg.hidden, cfg.kv_heads * cfg.head_dim
         sh = weights["shapes"]
         self.layers = []
         for L in weights["layers"]:
@@ -76,10 +91,10 @@ class DenseModel:
             self.layers.append(W)
         self.embed = quant.Weight(weights["embed"], cfg.embed_dtype, [H, cfg.vocab], name="token_embd")
         self.output_norm = weights["output_norm"]
-        z = lambda n: torch.zeros(n, device=device)  # noqa: E731
-        self.hidden, self.normalized, self.attended = z(H), z(H), z(A)
-        self.projected, self.ff, self.gate = z(H), z(H), z(F)
-        self.q, self.k, self.v, self.logits = z(A), z(KV), z(KV), z(cfg.vocab)
+        self.one = _Acts(cfg, 1, device)          # the graph-captured single-token step
+        self.chunk = min(prefill_chunk, cfg.positions)
+        self._prefill_acts = {}
+        self.logits = torch.zeros(cfg.vocab, device=device)
         self.token = torch.zeros(1, dtype=torch.int32, device=device)
         self.pos = torch.zeros(1, dtype=torch.int32, device=device)
         half = cfg.head_dim // 2
@@ -90,8 +105,8 @@ class DenseModel:
         self.cos = torch.from_numpy(cos).to(device)
         self.sin = torch.from_numpy(sin).to(device)
         ws = C.c_size_t()
-        check(lib.hyq_attention_workspace_bytes(cfg.heads, cfg.head_dim, cfg.positions, C.byref(ws)))
-        # split partials + per-head counters; zero once, every call leaves it zero
+        check(lib.hyq_attention_workspace_bytes(cfg.heads, cfg.head_dim, cfg.positions, self.chunk, C.byref(ws)))
+        # split partials + per-(token, head) counters; zero once, every call leaves it zero
         self.attn_ws = torch.zeros(ws.value, dtype=torch.uint8, device=device)
         self.argmax_ws = torch.zeros(2, dtype=torch.int64, device=device)  # HYQ_ARGMAX_WORKSPACE_BYTES, zero
         self.graph = None
@@ -100,34 +115,62 @@ class DenseModel:
     def _stream(self):
         return C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
 
+    def _enqueue(self, acts, tokens):
+        """Forward of acts.M tokens (device int32 `tokens`) at positions
+        *pos ..: the layers of model.rs:374-547 (M = 1) or of the batched
+        forward model.rs:549-646 (M > 1, projections on the tensor cores),
+        then the lm_head of the last row and the greedy token; *pos += M."""
+        cfg, st, a, M = self.cfg, self._stream(), acts, acts.M
+        H = cfg.hidden
+        last = lambda t: C.c_void_p(t.data_ptr() + (M - 1) * t.stride(0) * t.element_size())  # noqa: E731
+        check(lib.hyq_embed(self.embed.handle, _p(tokens), M, _p(a.hidden), st))
+        check(lib.hyq_rms_norm(_p(a.hidden), _p(self.layers[0]["input_norm"]), H, M, cfg.eps, _p(a.normalized), st))
+        for i, W in enumerate(self.layers):
+            if M == 1:
+                check(lib.hyq_gemv_qkv(W["q"].handle, W["k"].handle, W["v"].handle, _p(a.normalized), _p(a.q),
+                                       _p(a.k), _p(a.v), st))
+            else:
+                check(lib.hyq_matmul_qkv(W["q"].handle, W["k"].handle, W["v"].handle, _p(a.normalized), M, _p(a.q),
+                                         _p(a.k), _p(a.v), st))
+            check(lib.hyq_rope_qk(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim, _p(self.cos),
+                                  _p(self.sin), cfg.positions, _p(self.pos), M, _p(W["q_norm"]), _p(W["k_norm"]),
+                                  cfg.eps, 0, _p(W["k_cache"]), _p(W["v_cache"]), st))
+            check(lib.hyq_attention(_p(a.q), _p(W["k_cache"]), _p(W["v_cache"]), cfg.heads, cfg.kv_heads,
+                                    cfg.head_dim, cfg.positions, _p(self.pos), M, _p(a.attended), _p(self.attn_ws),
+                                    st))
+            check(lib.hyq_matmul(W["o"].handle, _p(a.attended), M, _p(a.projected), st))
+            # residual add fused with the norm that follows it
+            check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.projected), _p(W["ffn_norm"]), H, M, cfg.eps,
+                                       _p(a.normalized), st))
+            if M == 1:
+                check(lib.hyq_matmul_gate_up_silu(W["gate"].handle, W["up"].handle, _p(a.normalized), _p(a.gate),
+                                                  st))
+            else:
+                check(lib.hyq_matmul_gate_up_silu_batch(W["gate"].handle, W["up"].handle, _p(a.normalized), M,
+                                                        _p(a.gate), st))
+            check(lib.hyq_matmul(W["down"].handle, _p(a.gate), M, _p(a.ff), st))
+            nxt = self.layers[i + 1]["input_norm"] if i + 1 < len(self.layers) else self.output_norm
+            check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.ff), _p(nxt), H, M, cfg.eps, _p(a.normalized), st))
+        # logits of the last token only (model.rs:619-622)
+        check(lib.hyq_matmul(self.embed.handle, last(a.normalized), 1, _p(self.logits), st))
+        check(lib.hyq_argmax(_p(self.logits), cfg.vocab, _p(self.token), _p(self.pos), M, _p(self.argmax_ws), st))
+
     def enqueue_step(self):
         """One token: reads self.token / self.pos, leaves the logits, the next
         greedy token in self.token, and pos + 1."""
-        cfg, st = self.cfg, self._stream()
-        H, A, KV = cfg.hidden, cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
-        check(lib.hyq_embed(self.embed.handle, _p(self.token), _p(self.hidden), st))
-        check(lib.hyq_rms_norm(_p(self.hidden), _p(self.layers[0]["input_norm"]), H, 1, cfg.eps, _p(self.normalized),
-                               st))
-        for i, W in enumerate(self.layers):
-            check(lib.hyq_gemv_qkv(W["q"].handle, W["k"].handle, W["v"].handle, _p(self.normalized), _p(self.q),
-                                   _p(self.k), _p(self.v), st))
-            check(lib.hyq_rope_qk(_p(self.q), _p(self.k), _p(self.v), cfg.heads, cfg.kv_heads, cfg.head_dim,
-                                  _p(self.cos), _p(self.sin), cfg.positions, _p(self.pos), _p(W["q_norm"]),
-                                  _p(W["k_norm"]), cfg.eps, 0, _p(W["k_cache"]), _p(W["v_cache"]), st))
-            check(lib.hyq_attention(_p(self.q), _p(W["k_cache"]), _p(W["v_cache"]), cfg.heads, cfg.kv_heads,
-                                    cfg.head_dim, cfg.positions, _p(self.pos), _p(self.attended), _p(self.attn_ws),
-                                    st))
-            check(lib.hyq_matmul(W["o"].handle, _p(self.attended), 1, _p(self.projected), st))
-            # residual add fused with the norm that follows it
-            check(lib.hyq_add_rms_norm(_p(self.hidden), _p(self.projected), _p(W["ffn_norm"]), H, cfg.eps,
-                                       _p(self.normalized), st))
-            check(lib.hyq_matmul_gate_up_silu(W["gate"].handle, W["up"].handle, _p(self.normalized), _p(self.gate),
-                                              st))
-            check(lib.hyq_matmul(W["down"].handle, _p(self.gate), 1, _p(self.ff), st))
-            nxt = self.layers[i + 1]["input_norm"] if i + 1 < len(self.layers) else self.output_norm
-            check(lib.hyq_add_rms_norm(_p(self.hidden), _p(self.ff), _p(nxt), H, cfg.eps, _p(self.normalized), st))
-        check(lib.hyq_matmul(self.embed.handle, _p(self.normalized), 1, _p(self.logits), st))
-        check(lib.hyq_argmax(_p(self.logits), cfg.vocab, _p(self.token), _p(self.pos), _p(self.argmax_ws), st))
+        self._enqueue(self.one, self.token)
+
+    def prefill(self, ids):
+        """Feed a prompt chunk of at most self.chunk tokens (a device int32
+        tensor) in one batched forward; leaves the logits of its last token,
+        the next greedy token in self.token and pos += len(ids)."""
+        M = int(ids.numel())
+        if not 0 < M <= self.chunk:
+            raise ValueError(f"prefill takes 1..{self.chunk} tokens")
+        acts = self._prefill_acts.get(M)
+        if acts is None:
+            acts = self._prefill_acts[M] = _Acts(self.cfg, M, self.device)
+        self._enqueue(acts, ids)
 
     # kernel launches of one enqueue_step
     def launches(self):
@@ -152,10 +195,11 @@ class DenseModel:
             W["k_cache"].zero_()
             W["v_cache"].zero_()
 
-    def generate(self, prompt, n_new, stream, logits_out=None):
-        """Greedy decode: feed `prompt` token by token, then `n_new` tokens.
-        Returns the generated ids (and fills logits_out[i] with the logits
-        that chose token i when given)."""
+    def generate(self, prompt, n_new, stream, logits_out=None, batched_prefill=False):
+        """Greedy decode: feed `prompt` (one graph step per token, or in
+        batched chunks with batched_prefill), then `n_new` tokens.  Returns the
+        generated ids (and fills logits_out[i] with the logits that chose
+        token i when given)."""
         if self.graph is None:
             self.capture(stream)
         if len(prompt) + n_new > self.cfg.positions:
@@ -164,11 +208,15 @@ class DenseModel:
         ids = torch.tensor(prompt, dtype=torch.int32).to(self.device)
         with torch.cuda.stream(stream):
             self.reset()
-            # after the step of the last prompt token, self.token holds
-            # generated token 0 and self.logits the logits that chose it
-            for i in range(len(prompt)):
-                self.token.copy_(ids[i:i + 1])
-                self.graph.replay()
+            # after the prompt, self.token holds generated token 0 and
+            # self.logits the logits that chose it
+            if batched_prefill:
+                for c0 in range(0, len(prompt), self.chunk):
+                    self.prefill(ids[c0:c0 + self.chunk])
+            else:
+                for i in range(len(prompt)):
+                    self.token.copy_(ids[i:i + 1])
+                    self.graph.replay()
             for i in range(n_new):
                 out[i:i + 1].copy_(self.token)
                 if logits_out is not None:

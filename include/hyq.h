@@ -236,29 +236,34 @@ int hyq_rope_table(int64_t positions, int head_dim, float rope_base, float* cos_
  * n is at most 16384 (the row is staged in shared memory). */
 int hyq_rms_norm(const float* x, const float* w, int64_t n, int64_t rows, float eps, float* out, void* stream);
 
-/* Weight::row_into (quant.rs:123-142) of the row *token (device int32). */
-int hyq_embed(const hyq_weight* w, const int32_t* token, float* out, void* stream);
+/* Weight::row_into (quant.rs:123-142) of rows token[0 .. count) (device
+ * int32) into out [count, K] (the embedding rows of a prompt chunk,
+ * model.rs:373-376). */
+int hyq_embed(const hyq_weight* w, const int32_t* token, int64_t count, float* out, void* stream);
 
-/* RoPE of q [heads, hd] and k [kv_heads, hd] at position *pos (tables from
+/* RoPE of q [tokens, heads, hd] and k [tokens, kv_heads, hd], token i at
+ * position *pos + i (rope, model.rs:919-947; tables from
  * hyq_rope_table, on the device), the per-head RMSNorm with q_norm/k_norm
  * after it (Dense, model.rs:435-446) or before it (norm_first: HyV3,
  * model.rs:425-434; NULL norms skip it), then KvCache::append of k and v
  * (model.rs:650-667) into row *pos of k_cache/v_cache [positions, kv_heads*hd]. */
 int hyq_rope_qk(float* q, float* k, const float* v, int heads, int kv_heads, int head_dim, const float* cos_tab,
-                const float* sin_tab, int64_t positions, const int32_t* pos, const float* q_norm,
+                const float* sin_tab, int64_t positions, const int32_t* pos, int64_t tokens, const float* q_norm,
                 const float* k_norm, float eps, int norm_first, float* k_cache, float* v_cache, void* stream);
 
-/* attention_into for one token (model.rs:949-1021) over cache rows 0..*pos
- * (grouped-query: head h reads kv head h / (heads / kv_heads)).  positions
- * is the cache capacity (at most 16384), head_dim at most 256.  The cached
- * positions are split into chunks of 64 whose partial softmax sums are
- * combined on the device; `workspace` holds those partials and one counter
- * per head: hyq_attention_workspace_bytes bytes, zero before the first call
- * (every call leaves it zero again).  Calls that share a workspace must not
- * overlap in time. */
-int hyq_attention_workspace_bytes(int heads, int head_dim, int64_t positions, size_t* bytes);
+/* attention_into (model.rs:949-1021) for q [tokens, heads, hd]: token i sits
+ * at position *pos + i and attends to cache rows 0 ..= *pos + i (causal;
+ * grouped-query: head h reads kv head h / (heads / kv_heads)); out [tokens,
+ * heads, hd].  positions is the cache capacity (at most 16384), head_dim at
+ * most 256.  The cached positions are split into chunks of 64 whose partial
+ * softmax sums are combined on the device; `workspace` holds those partials
+ * and one counter per (token, head): hyq_attention_workspace_bytes bytes for
+ * the largest token count used, zero before the first call (every call leaves
+ * it zero again; calls with fewer tokens share it).  Calls that share a
+ * workspace must not overlap in time. */
+int hyq_attention_workspace_bytes(int heads, int head_dim, int64_t positions, int64_t tokens, size_t* bytes);
 int hyq_attention(const float* q, const float* k_cache, const float* v_cache, int heads, int kv_heads,
-                  int head_dim, int64_t positions, const int32_t* pos, float* out, void* workspace,
+                  int head_dim, int64_t positions, const int32_t* pos, int64_t tokens, float* out, void* workspace,
                   void* stream);
 
 /* add (model.rs:1043-1071): dst += src. */
@@ -267,15 +272,16 @@ int hyq_add(float* dst, const float* src, int64_t n, void* stream);
 /* The residual add followed by the next rms_norm_into (model.rs:1043-1071,
  * 785-830) in one launch: hidden += delta; out = hidden * scale * w, with
  * scale from the updated hidden. */
-int hyq_add_rms_norm(float* hidden, const float* delta, const float* w, int64_t n, float eps, float* out,
-                     void* stream);
+int hyq_add_rms_norm(float* hidden, const float* delta, const float* w, int64_t n, int64_t rows, float eps,
+                     float* out, void* stream);
 
 /* Greedy token (generation.rs:281-290: first index of the largest value)
- * into *token; when pos is not NULL, *pos += 1.  `workspace`: 16 bytes,
+ * into *token; when pos is not NULL, *pos += pos_step.  `workspace`: 16 bytes,
  * 8-byte aligned, zero before the first call (every call leaves it zero);
  * calls that share one must not overlap in time. */
 #define HYQ_ARGMAX_WORKSPACE_BYTES 16
-int hyq_argmax(const float* x, int64_t n, int32_t* token, int32_t* pos, void* workspace, void* stream);
+int hyq_argmax(const float* x, int64_t n, int32_t* token, int32_t* pos, int pos_step, void* workspace,
+               void* stream);
 
 /* --- Mixture-of-experts layer (Moe::forward, model.rs:688-767) ----------
  * The reference routes on the host and loops over experts with one small

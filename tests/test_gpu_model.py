@@ -64,7 +64,7 @@ def test_attention_splits_match_oracle(cuda, pos):
     kc = torch.randn(positions, kv_heads * dim, generator=g)
     vc = torch.randn(positions, kv_heads * dim, generator=g)
     ws = C.c_size_t()
-    check(lib.hyq_attention_workspace_bytes(heads, dim, positions, C.byref(ws)))
+    check(lib.hyq_attention_workspace_bytes(heads, dim, positions, 1, C.byref(ws)))
     work = torch.zeros(ws.value, dtype=torch.uint8, device=cuda)
     d = [t.to(cuda) for t in (q, kc, vc)]
     p = torch.tensor([pos], dtype=torch.int32, device=cuda)
@@ -72,7 +72,7 @@ def test_attention_splits_match_oracle(cuda, pos):
     for _ in range(2):
         out = torch.full((heads * dim,), float("nan"), device=cuda)
         check(lib.hyq_attention(*(C.c_void_p(t.data_ptr()) for t in d), heads, kv_heads, dim, positions,
-                                C.c_void_p(p.data_ptr()), C.c_void_p(out.data_ptr()), C.c_void_p(work.data_ptr()),
+                                C.c_void_p(p.data_ptr()), 1, C.c_void_p(out.data_ptr()), C.c_void_p(work.data_ptr()),
                                 C.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)))
         outs.append(out.cpu().numpy())
     torch.cuda.synchronize()
@@ -97,7 +97,7 @@ def test_add_rms_norm_bit_exact(cuda):
     hd, dd, wd = (t.to(cuda) for t in (h, dlt, w))
     out = torch.empty(n, device=cuda)
     check(lib.hyq_add_rms_norm(C.c_void_p(hd.data_ptr()), C.c_void_p(dd.data_ptr()), C.c_void_p(wd.data_ptr()), n,
-                               1e-5, C.c_void_p(out.data_ptr()),
+                               1, 1e-5, C.c_void_p(out.data_ptr()),
                                C.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)))
     torch.cuda.synchronize()
     s = (h.numpy() + dlt.numpy()).astype(np.float32)
@@ -120,7 +120,7 @@ def test_argmax_ties_nan_and_workspace(cuda):
         ws = torch.zeros(2, dtype=torch.int64, device=cuda)
         for _ in range(2):
             check(lib.hyq_argmax(C.c_void_p(xd.data_ptr()), x.size, C.c_void_p(tok.data_ptr()),
-                                 C.c_void_p(pos.data_ptr()), C.c_void_p(ws.data_ptr()),
+                                 C.c_void_p(pos.data_ptr()), 1, C.c_void_p(ws.data_ptr()),
                                  C.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)))
         torch.cuda.synchronize()
         assert int(pos) == 2 and not ws.any()
@@ -140,3 +140,42 @@ def test_argmax_ties_nan_and_workspace(cuda):
     assert run(y) == 50
     assert run(np.full(1000, np.nan, dtype=np.float32)) == 0
     assert run(np.full(3000, -np.inf, dtype=np.float32)) == 0
+
+
+@pytest.mark.parametrize("prompt_len,rel_bound", [(6, 1e-4), (40, 2e-2)])
+def test_batched_prefill_matches_oracle(cuda, prompt_len, rel_bound):
+    """The batched forward (model.rs:549-646): the prompt in one chunk,
+    causal attention over it, RoPE at positions 0..M-1, logits of the last
+    token, then greedy steps.  Below 16 tokens the projections are the f32
+    batch-1 products (the 1e-4 bound of the step test); from 16 they run on
+    the fp16 tensor cores, held to the tolerance of that precision."""
+    import torch
+    from hy_mt_rs_b200 import quant
+    from hy_mt_rs_b200.model import DenseConfig, DenseModel, random_weights
+    from oracle.model import DenseOracle
+
+    cfg = DenseConfig(layers=4, positions=64)
+    weights = random_weights(cfg, cuda, seed=prompt_len)
+    torch.cuda.synchronize()
+    model = DenseModel(cfg, weights, cuda)
+    oracle = DenseOracle(cfg, weights)
+    prompt = np.random.default_rng(prompt_len).integers(0, cfg.vocab, prompt_len).tolist()
+    n_new = 6
+    stream = torch.cuda.Stream(cuda)
+    logits = torch.zeros(n_new, cfg.vocab, device=cuda)
+    try:
+        ids = model.generate(prompt, n_new, stream, logits_out=logits, batched_prefill=True)
+    finally:
+        quant.set_launch_overlap(False)
+    ref_ids, ref_logits = oracle.generate(prompt, n_new)
+    got = logits.cpu().numpy()
+    for i in range(n_new):
+        rel = np.linalg.norm(got[i] - ref_logits[i]) / np.linalg.norm(ref_logits[i])
+        assert rel < rel_bound, (i, rel)
+        if ids[i] != ref_ids[i]:
+            top = np.sort(ref_logits[i])[-2:]
+            margin = float(top[1] - top[0])
+            err = float(np.abs(got[i] - ref_logits[i]).max())
+            assert margin <= 2 * err, (i, ids[i], ref_ids[i], margin, err)
+            break
+    assert quant.device_status() == 0
