@@ -62,6 +62,8 @@ def args_parse():
     ap.add_argument("--sweep", action="store_true",
                     help="gemv: also measure every packed format at 6144x2048 and 120832x2048, both paths")
     ap.add_argument("--tokens", type=int, default=512, help="prefill: tokens M")
+    ap.add_argument("--model-kernels", action="store_true",
+                    help="model: one launch per operation instead of the persistent token-step kernel")
     return ap.parse_args()
 
 
@@ -911,7 +913,7 @@ def model_arm(a):
     cfg = DenseConfig(layers=N_LAYERS_MODEL, positions=n_prompt + n_new)
     weights = random_weights(cfg, dev, seed=1)
     torch.cuda.synchronize(dev)
-    model = DenseModel(cfg, weights, dev)
+    model = DenseModel(cfg, weights, dev, fused=not a.model_kernels)
     stream = torch.cuda.Stream(dev)
     model.capture(stream)
     prompt = np.random.default_rng(0).integers(0, cfg.vocab, n_prompt).tolist()
@@ -1013,6 +1015,7 @@ def model_arm(a):
         "config": {"workload": "hy-mt-rs config 4: 32 layers, hidden 2048, 16/4 heads x 128, SwiGLU 6144, "
                                "vocab 120832, RoPE 10000; 256-token prompt (batched prefill), 256 generated",
                    "concurrency": 1, "positions": cfg.positions, "launch_overlap": True,
+                   "step": "kernels" if a.model_kernels else "one persistent kernel per token (hyq_dense_step)",
                    "parallelism": f"replicas x{world}"},
         "prompt_ms": round(ms_prompt, 2),
         "prompt": "256 tokens in one batched forward (tensor-core projections, causal attention)",

@@ -79,6 +79,9 @@ _SIGS = {
     "hyq_attention_workspace_bytes": ([C.c_int, C.c_int, _i64, _i64, C.POINTER(C.c_size_t)], C.c_int),
     "hyq_attention": ([_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _i64, _vp, _i64, _vp, _vp, _vp], C.c_int),
     "hyq_add": ([_vp, _vp, _i64, _vp], C.c_int),
+    "hyq_dense_step_create": ([_vp, C.POINTER(C.c_void_p)], C.c_int),
+    "hyq_dense_step_enqueue": ([_vp, _vp], C.c_int),
+    "hyq_dense_step_free": ([_vp], None),
     "hyq_moe_router": ([_vp, _vp, _i64, _vp, _vp], C.c_int),
     "hyq_moe_route": ([_vp, _i64, C.c_int, _vp, C.c_int, C.c_int, C.c_float, _vp, _vp, _vp], C.c_int),
     "hyq_moe_group": ([_vp, _vp, _i64, C.c_int, C.c_int, _vp, _vp, _vp, _vp, _vp], C.c_int),

@@ -36,6 +36,7 @@ enum : unsigned {
   DEV_TIMEOUT_DRAIN = 4u,  // exit path gave up waiting for copies in flight
   DEV_BAD_ARGS = 8u,       // kernel saw arguments the host should have rejected
   DEV_TIMEOUT_PEER = 16u,  // a peer all-reduce gave up waiting for another rank's flag
+  DEV_TIMEOUT_GRID = 32u,  // a persistent kernel gave up waiting at a grid-wide barrier
 };
 
 // Bound on any single wait (nanoseconds of %globaltimer).
@@ -235,6 +236,18 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// dot_avx2's reduction of its two 8-lane accumulators (quant.rs:2562-2596)
+// when n % 16 == 0: lane l of the 16-lane group [b, b + 16) holds
+// accumulator lane l; every lane of the group returns the dot.
+__device__ __forceinline__ float x86_lane_sum(float acc, unsigned mask) {
+  const int lane = threadIdx.x & 31, l = lane & 15, base = lane & 16;
+  const float sum = __fadd_rn(acc, __shfl_sync(mask, acc, base + ((l + 8) & 15)));
+  float h = -0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) h = __fadd_rn(h, __shfl_sync(mask, sum, base + k));
+  return __fadd_rn(h, -0.0f);
+}
+
 // dot_avx2 order (quant.rs:2562-2596: two 8-lane FMA accumulators per 16
 // floats, their lane sums, a scalar tail) over n floats, by the 16 lanes
 // [b, b + 16) of a warp (b = lane & 16), one per AVX2 accumulator lane.  Every lane of the group returns
@@ -244,6 +257,7 @@ __device__ __forceinline__ float dot_x86(const float* a, const float* b, int n, 
   const int l = lane & 15, base = lane & 16;
   const int chunks = n / 16;
   float acc = 0.f;
+#pragma unroll 8
   for (int c = 0; c < chunks; ++c) acc = fmaf(a[16 * c + l], b[16 * c + l], acc);
   // sum[l] = s0[l] + s1[l] for l < 8
   float sum = __fadd_rn(acc, __shfl_sync(mask, acc, base + ((l + 8) & 15)));

@@ -31,16 +31,6 @@ namespace moe {
 constexpr int kRouterMaxK = 16384;
 constexpr int kRouterChains = 4;
 
-__device__ __forceinline__ float x86_lane_sum(float acc, unsigned mask) {
-  // dot_avx2's reduction of its two 8-lane accumulators (K % 16 == 0)
-  const int lane = threadIdx.x & 31, l = lane & 15, base = lane & 16;
-  const float sum = __fadd_rn(acc, __shfl_sync(mask, acc, base + ((l + 8) & 15)));
-  float h = -0.0f;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) h = __fadd_rn(h, __shfl_sync(mask, sum, base + k));
-  return __fadd_rn(h, -0.0f);
-}
-
 __global__ void __launch_bounds__(256) router_kernel(const float* __restrict__ w, const float* __restrict__ x, int K,
                                                      int experts, float* __restrict__ logits) {
   extern __shared__ float xs[];

@@ -64,6 +64,22 @@ def _p(t):
 PREFILL_CHUNK = 256  # tokens per batched forward (model.rs:18, 353)
 
 
+class _DenseLayerDesc(C.Structure):
+    """hyq_dense_layer (include/hyq.h)."""
+    _fields_ = [(n, C.c_void_p) for n in ("q", "k", "v", "o", "gate", "up", "down", "input_norm", "ffn_norm",
+                                          "q_norm", "k_norm", "k_cache", "v_cache")]
+
+
+class _DenseStepDesc(C.Structure):
+    """hyq_dense_step_desc (include/hyq.h)."""
+    _fields_ = [("layers", C.c_int), ("hidden", C.c_int), ("heads", C.c_int), ("kv_heads", C.c_int),
+                ("head_dim", C.c_int), ("ffn", C.c_int), ("positions", C.c_int64), ("eps", C.c_float),
+                ("layer", C.c_void_p), ("embed", C.c_void_p), ("output_norm", C.c_void_p), ("cos_tab", C.c_void_p),
+                ("sin_tab", C.c_void_p), ("hidden_state", C.c_void_p), ("q", C.c_void_p), ("k", C.c_void_p),
+                ("v", C.c_void_p), ("attended", C.c_void_p), ("gate", C.c_void_p), ("logits", C.c_void_p),
+                ("token", C.c_void_p), ("pos", C.c_void_p)]
+
+
 class _Acts:
     """Activation buffers of a forward over M tokens (rows)."""
 
@@ -77,7 +93,10 @@ class _Acts:
 
 
 class DenseModel:
-    def __init__(self, cfg, weights, device, prefill_chunk=PREFILL_CHUNK):
+    """fused: run each token step as one persistent kernel
+    (hyq_dense_step_enqueue) instead of ~8 launches per layer."""
+
+    def __init__(self, cfg, weights, device, prefill_chunk=PREFILL_CHUNK, fused=False):
         self.cfg = cfg
         self.device = device
         H, KV = cfg.hidden, cfg.kv_heads * cfg.head_dim
@@ -110,6 +129,34 @@ class DenseModel:
         self.attn_ws = torch.zeros(ws.value, dtype=torch.uint8, device=device)
         self.argmax_ws = torch.zeros(2, dtype=torch.int64, device=device)  # HYQ_ARGMAX_WORKSPACE_BYTES, zero
         self.graph = None
+        self._step = None
+        if fused:
+            self._make_fused_step()
+
+    def _make_fused_step(self):
+        cfg, a = self.cfg, self.one
+        arr = (_DenseLayerDesc * cfg.layers)()
+        for i, W in enumerate(self.layers):
+            arr[i] = _DenseLayerDesc(*(W[n].handle for n in ("q", "k", "v", "o", "gate", "up", "down")),
+                                     *(W[n].data_ptr() for n in ("input_norm", "ffn_norm", "q_norm", "k_norm",
+                                                                  "k_cache", "v_cache")))
+        d = _DenseStepDesc(cfg.layers, cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.ffn, cfg.positions,
+                           cfg.eps, C.cast(arr, C.c_void_p), self.embed.handle, self.output_norm.data_ptr(),
+                           self.cos.data_ptr(), self.sin.data_ptr(), a.hidden.data_ptr(), a.q.data_ptr(),
+                           a.k.data_ptr(), a.v.data_ptr(), a.attended.data_ptr(), a.gate.data_ptr(),
+                           self.logits.data_ptr(), self.token.data_ptr(), self.pos.data_ptr())
+        h = C.c_void_p()
+        check(lib.hyq_dense_step_create(C.byref(d), C.byref(h)))
+        self._step = h
+
+    def __del__(self):
+        h = getattr(self, "_step", None)
+        if h is not None:
+            try:
+                lib.hyq_dense_step_free(h)
+            except Exception:
+                pass
+            self._step = None
 
     # ----------------------------------------------------------------- step
     def _stream(self):
@@ -158,7 +205,10 @@ class DenseModel:
     def enqueue_step(self):
         """One token: reads self.token / self.pos, leaves the logits, the next
         greedy token in self.token, and pos + 1."""
-        self._enqueue(self.one, self.token)
+        if self._step is not None:
+            check(lib.hyq_dense_step_enqueue(self._step, self._stream()))
+        else:
+            self._enqueue(self.one, self.token)
 
     def prefill(self, ids):
         """Feed a prompt chunk of at most self.chunk tokens (a device int32
@@ -174,7 +224,7 @@ class DenseModel:
 
     # kernel launches of one enqueue_step
     def launches(self):
-        return 2 + 8 * self.cfg.layers + 2
+        return 1 if self._step is not None else 2 + 8 * self.cfg.layers + 2
 
     def capture(self, stream):
         """Capture enqueue_step as one CUDA graph on `stream`."""

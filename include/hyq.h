@@ -58,6 +58,7 @@ typedef enum hyq_profile {
 #define HYQ_DEV_TIMEOUT_DRAIN 4u /* exit path gave up waiting for copies in flight */
 #define HYQ_DEV_BAD_ARGS 8u      /* a kernel saw arguments the host should have rejected */
 #define HYQ_DEV_TIMEOUT_PEER 16u /* hyq_peer_allreduce gave up waiting for another rank */
+#define HYQ_DEV_TIMEOUT_GRID 32u /* hyq_dense_step_enqueue's kernel gave up at a grid-wide barrier */
 
 typedef struct hyq_weight hyq_weight;
 
@@ -282,6 +283,45 @@ int hyq_add_rms_norm(float* hidden, const float* delta, const float* w, int64_t 
 #define HYQ_ARGMAX_WORKSPACE_BYTES 16
 int hyq_argmax(const float* x, int64_t n, int32_t* token, int32_t* pos, int pos_step, void* workspace,
                void* stream);
+
+/* --- The whole Dense decoder token step as one persistent kernel --------
+ * model.rs:374-547 for one token: embedding row, per layer RMSNorm -> QKV ->
+ * RoPE + q/k norm + KV append -> attention -> O + residual -> RMSNorm ->
+ * gate/up-SiLU -> down + residual, then the output norm, the tied lm_head and
+ * the greedy token, in one cooperative launch (one CTA per SM; a grid-wide
+ * barrier between dependent phases instead of ~8 launches per layer).  Same
+ * arithmetic as the per-call entry points (x86-order norms, exact f32
+ * products).  Supported: Q2_0C layer products and a Q6_K tied embedding (the
+ * 1.8B architecture).  The step reads the token and position from device
+ * ints and writes the next token and position + 1 there, so a CUDA graph
+ * can replay it.  No reference counterpart as one call (the reference runs
+ * these steps on the host). */
+typedef struct hyq_dense_layer {
+  const hyq_weight *q, *k, *v, *o, *gate, *up, *down;
+  const float *input_norm, *ffn_norm, *q_norm, *k_norm;  /* device f32 */
+  float *k_cache, *v_cache;                              /* [positions, kv_heads * head_dim] */
+} hyq_dense_layer;
+
+typedef struct hyq_dense_step_desc {
+  int layers, hidden, heads, kv_heads, head_dim, ffn;
+  int64_t positions;                 /* KV-cache capacity, at most 16384 */
+  float eps;
+  const hyq_dense_layer* layer;      /* host array of `layers` */
+  const hyq_weight* embed;           /* Q6_K [hidden, vocab], tied lm_head */
+  const float* output_norm;
+  const float *cos_tab, *sin_tab;    /* hyq_rope_table, on the device */
+  /* device activations: hidden_state [hidden], q [heads*hd], k, v [kv*hd],
+   * attended [heads*hd], gate [ffn], logits [vocab]; token, pos: one int32 */
+  float *hidden_state, *q, *k, *v, *attended, *gate, *logits;
+  int32_t *token, *pos;
+} hyq_dense_step_desc;
+
+typedef struct hyq_dense_step hyq_dense_step;
+int hyq_dense_step_create(const hyq_dense_step_desc* desc, hyq_dense_step** out);
+/* One token step on `stream` (a zeroing copy of the step's 16-byte sync
+ * words, then the kernel).  Steps of one handle must not overlap in time. */
+int hyq_dense_step_enqueue(hyq_dense_step* step, void* stream);
+void hyq_dense_step_free(hyq_dense_step* step);
 
 /* --- Mixture-of-experts layer (Moe::forward, model.rs:688-767) ----------
  * The reference routes on the host and loops over experts with one small

@@ -179,3 +179,41 @@ def test_batched_prefill_matches_oracle(cuda, prompt_len, rel_bound):
             assert margin <= 2 * err, (i, ids[i], ref_ids[i], margin, err)
             break
     assert quant.device_status() == 0
+
+
+def test_fused_step_matches_oracle(cuda):
+    """hyq_dense_step_enqueue (the whole token step as one persistent kernel,
+    grid-wide barriers between phases) against the oracle model: logits of
+    every step within the 1e-4 bound of the per-call step, the same greedy
+    stream, twice in a row from one captured graph."""
+    import torch
+    from hy_mt_rs_b200 import quant
+    from hy_mt_rs_b200.model import DenseConfig, DenseModel, random_weights
+    from oracle.model import DenseOracle
+
+    cfg = DenseConfig(layers=4, positions=80)
+    weights = random_weights(cfg, cuda, seed=3)
+    torch.cuda.synchronize()
+    model = DenseModel(cfg, weights, cuda, fused=True)
+    assert model.launches() == 1
+    oracle = DenseOracle(cfg, weights)
+    prompt = [11, 4093, 77, 120000, 5, 42] + list(range(100, 160))   # crosses a 64-position chunk
+    n_new = 8
+    stream = torch.cuda.Stream(cuda)
+    logits = torch.zeros(n_new, cfg.vocab, device=cuda)
+    try:
+        ids = model.generate(prompt, n_new, stream, logits_out=logits)
+        again = model.generate(prompt, n_new, stream)
+    finally:
+        quant.set_launch_overlap(False)
+    ref_ids, ref_logits = oracle.generate(prompt, n_new)
+    got = logits.cpu().numpy()
+    for i in range(n_new):
+        rel = np.linalg.norm(got[i] - ref_logits[i]) / np.linalg.norm(ref_logits[i])
+        assert rel < 1e-4, (i, rel)
+        if ids[i] != ref_ids[i]:
+            top = np.sort(ref_logits[i])[-2:]
+            assert float(top[1] - top[0]) <= 2 * float(np.abs(got[i] - ref_logits[i]).max()), i
+            break
+    assert again == ids
+    assert quant.device_status() == 0
