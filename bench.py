@@ -1056,7 +1056,8 @@ def moe_arm(a):
 
     cfg = MoeConfig()
     weights = random_moe_weights(cfg, dev, seed=3)
-    layer = MoeLayer(cfg, weights)
+    # N > 1: expert parallelism (each rank E / N experts and its own tokens, NCCL all-to-all)
+    layer = MoeLayer(cfg, weights, ep=(rank, world, None) if world > 1 else None)
     H, E, M, S, U = cfg.hidden, cfg.experts, cfg.mid, cfg.shared_mid, cfg.used
     expert_bytes = 3 * M * row_bytes(cfg.dtype, H)  # gate + up + down of one expert (same byte count)
     shared_bytes = 3 * S * row_bytes(cfg.dtype, H)
@@ -1135,7 +1136,8 @@ def moe_arm(a):
         "data": "synthetic (seeded N(0,1) F32 router, N(0,0.1) bias, N(0,0.02) Q4_K experts; N(0,1) activations)",
         "config": {"workload": "hy-mt-rs config 5: one MoE FFN (router, sigmoid top-8 routing, 64 experts "
                                "2048->1024->2048 SwiGLU Q4_K, shared expert 2048->1024->2048), batch 64",
-                   "experts": E, "used": U, "parallelism": f"replicas x{world}",
+                   "experts": E, "used": U,
+                   "parallelism": f"expert parallel x{world} (NCCL all-to-all)" if world > 1 else "1 GPU",
                    "l2": "expert weights 226 MB per layer > L2"},
         "prefill": {"tokens": MOE_PREFILL_TOKENS, "ms_per_step": round(ms_pre, 4),
                     "tokens_per_s": round(MOE_PREFILL_TOKENS / (ms_pre * 1e-3) * world, 1),

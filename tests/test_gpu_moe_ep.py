@@ -1,0 +1,74 @@
+"""GPU check of expert parallelism for the MoE layer (MoeLayer with ep=...)
+on two GPUs: each rank holds half of the experts and its own tokens; token
+rows travel to the expert's rank and back by NCCL all-to-all.  Every
+expert output row is computed as on one GPU, so each rank's layer output
+equals the one-GPU layer on the same tokens bit for bit.  Each rank is a
+child process on its own GPU; NVLS is off.  Skipped with fewer than two
+GPUs."""
+import os
+import socket
+import sys
+from datetime import timedelta
+
+import pytest
+
+from conftest import ROOT
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, q):
+    sys.path.insert(0, ROOT)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    from hy_mt_rs_b200 import quant
+    from hy_mt_rs_b200.moe import MoeConfig, MoeLayer, random_moe_weights
+
+    ok = True
+    for T, cfg in ((37, MoeConfig(hidden=512, experts=8, used=2, mid=256, shared_mid=256)),
+                   (64, MoeConfig(hidden=2048, experts=16, used=4, mid=1024, shared_mid=1024))):
+        w = random_moe_weights(cfg, dev, seed=11)
+        full = MoeLayer(cfg, w)
+        ep = MoeLayer(cfg, w, ep=(rank, world, None))
+        x = torch.randn(T, cfg.hidden, generator=torch.Generator().manual_seed(100 + rank)).to(dev)
+        ref = full.forward(x, T).clone()
+        for _ in range(2):
+            got = ep.forward(x, T)
+            ok &= torch.equal(got, ref)
+        torch.cuda.synchronize(dev)
+    ok &= quant.device_status(dev) == 0
+    q.put((rank, bool(ok)))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_moe_expert_parallel_two_gpus():
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=240) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert res == {0: True, 1: True}

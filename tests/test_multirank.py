@@ -86,3 +86,19 @@ def test_reference_arm_other_ranks_exit_without_work():
                         "--steps", "1", "--warmup", "0"], env=env, capture_output=True, text=True, timeout=120)
     assert r.returncode == 0
     assert r.stdout.strip() == ""
+
+
+def test_expert_major_permutation():
+    """hy_mt_rs_b200.moe.expert_major: received rows (by source, then by
+    expert) reordered expert-major, and the inverse."""
+    import numpy as np
+    from hy_mt_rs_b200.moe import expert_major
+
+    counts = np.array([[2, 0, 1], [1, 3, 0]])       # 2 sources, 3 local experts
+    # received order: s0:e0 e0 e2 | s1:e0 e1 e1 e1
+    perm, inv, off = expert_major(counts)
+    assert list(off) == [0, 3, 6, 7]
+    assert list(perm) == [0, 1, 3, 4, 5, 6, 2]
+    assert list(perm[inv]) == list(range(7))
+    empty = expert_major(np.zeros((2, 2), dtype=np.int64))
+    assert empty[0].size == 0 and list(empty[2]) == [0, 0, 0]
