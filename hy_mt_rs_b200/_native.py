@@ -79,6 +79,22 @@ _SIGS = {
     "hyq_attention_workspace_bytes": ([C.c_int, C.c_int, _i64, _i64, C.POINTER(C.c_size_t)], C.c_int),
     "hyq_attention": ([_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _i64, _vp, _i64, _vp, _vp, _vp], C.c_int),
     "hyq_add": ([_vp, _vp, _i64, _vp], C.c_int),
+    "hyq_gguf_open": ([C.c_char_p, C.c_int, C.POINTER(C.c_void_p)], C.c_int),
+    "hyq_gguf_close": ([_vp], None),
+    "hyq_gguf_profile": ([_vp], C.c_int),
+    "hyq_gguf_tensor_count": ([_vp], _i64),
+    "hyq_gguf_tensor_name": ([_vp, _i64, C.POINTER(C.c_char_p)], C.c_int),
+    "hyq_gguf_tensor_info": ([_vp, C.c_char_p, C.POINTER(C.c_int), C.POINTER(C.c_uint32), C.POINTER(C.c_int),
+                              C.POINTER(C.c_int64), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)], C.c_int),
+    "hyq_gguf_tensor_data": ([_vp, C.c_char_p, C.POINTER(C.c_void_p), C.POINTER(C.c_size_t)], C.c_int),
+    "hyq_gguf_upload": ([_vp, C.c_char_p, C.POINTER(C.c_void_p)], C.c_int),
+    "hyq_gguf_meta_count": ([_vp], _i64),
+    "hyq_gguf_meta_key": ([_vp, _i64, C.POINTER(C.c_char_p), C.POINTER(C.c_int)], C.c_int),
+    "hyq_gguf_meta_u64": ([_vp, C.c_char_p, C.POINTER(C.c_uint64)], C.c_int),
+    "hyq_gguf_meta_f64": ([_vp, C.c_char_p, C.POINTER(C.c_double)], C.c_int),
+    "hyq_gguf_meta_bool": ([_vp, C.c_char_p, C.POINTER(C.c_int)], C.c_int),
+    "hyq_gguf_meta_str": ([_vp, C.c_char_p, C.POINTER(C.c_char_p), C.POINTER(C.c_size_t)], C.c_int),
+    "hyq_gguf_meta_array_len": ([_vp, C.c_char_p, C.POINTER(C.c_int64)], C.c_int),
     "hyq_dense_step_create": ([_vp, C.POINTER(C.c_void_p)], C.c_int),
     "hyq_dense_step_enqueue": ([_vp, _vp], C.c_int),
     "hyq_dense_step_free": ([_vp], None),

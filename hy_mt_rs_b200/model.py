@@ -102,13 +102,17 @@ class DenseModel:
         H, KV = cfg.hidden, cfg.kv_heads * cfg.head_dim
         sh = weights["shapes"]
         self.layers = []
+        # packed bytes (wrapped with the configured dtypes) or ready device weights
+        wrap = lambda v, t, dims, n: v if isinstance(v, quant.Weight) else quant.Weight(v, t, dims, name=n)  # noqa: E731
         for L in weights["layers"]:
-            W = {n: quant.Weight(L[n], cfg.linear_dtype, [sh[n][1], sh[n][0]], name=n) for n in sh}
+            W = {n: wrap(L[n], cfg.linear_dtype, [sh[n][1], sh[n][0]], n) for n in sh}
             W.update({n: L[n] for n in ("input_norm", "ffn_norm", "q_norm", "k_norm")})
             W["k_cache"] = torch.zeros(cfg.positions, KV, device=device)
             W["v_cache"] = torch.zeros(cfg.positions, KV, device=device)
             self.layers.append(W)
-        self.embed = quant.Weight(weights["embed"], cfg.embed_dtype, [H, cfg.vocab], name="token_embd")
+        self.embed = wrap(weights["embed"], cfg.embed_dtype, [H, cfg.vocab], "token_embd")
+        # lm_head: the tied embedding (model.rs:194-202), or a separate output.weight
+        self.output = weights.get("output") or self.embed
         self.output_norm = weights["output_norm"]
         self.one = _Acts(cfg, 1, device)          # the graph-captured single-token step
         self.chunk = min(prefill_chunk, cfg.positions)
@@ -135,6 +139,8 @@ class DenseModel:
 
     def _make_fused_step(self):
         cfg, a = self.cfg, self.one
+        if self.output is not self.embed:
+            raise ValueError("the persistent step takes a tied lm_head only")
         arr = (_DenseLayerDesc * cfg.layers)()
         for i, W in enumerate(self.layers):
             arr[i] = _DenseLayerDesc(*(W[n].handle for n in ("q", "k", "v", "o", "gate", "up", "down")),
@@ -148,6 +154,56 @@ class DenseModel:
         h = C.c_void_p()
         check(lib.hyq_dense_step_create(C.byref(d), C.byref(h)))
         self._step = h
+
+    @classmethod
+    def from_gguf(cls, path, device, positions=None, profile=0, fused=False):
+        """Model::from_gguf (model.rs:131-284) for the Dense architecture
+        (hunyuan-dense): configuration from the metadata, tensors uploaded
+        unchanged from the mapped file.  positions caps the KV cache (at most
+        the context length)."""
+        from . import gguf
+
+        g = gguf.Gguf(path, profile)
+        md = g.metadata
+        arch = md.get("general.architecture")
+        if arch != "hunyuan-dense":
+            raise ValueError(f"unsupported model architecture {arch} (the device runner takes hunyuan-dense)")
+        key = lambda s: md[f"{arch}.{s}"]  # noqa: E731
+        head_dim = int(key("attention.key_length"))
+        if int(key("attention.value_length")) != head_dim:
+            raise ValueError("different key/value dimensions are not supported")
+        if md.get(f"{arch}.rope.scaling.type", "none") != "none":
+            raise ValueError("GGUF must contain an effective RoPE base with no extra scaling")
+        if f"{arch}.rope.dimension_count" in md and int(key("rope.dimension_count")) != head_dim:
+            raise ValueError("partial rotary embeddings are not supported")
+        heads, kv = int(key("attention.head_count")), int(key("attention.head_count_kv"))
+        if heads <= 0 or kv <= 0 or heads % kv or head_dim % 2:
+            raise ValueError("invalid head counts or head dimension")
+        ctx = int(key("context_length"))
+        t = g.tensors
+        cfg = DenseConfig(layers=int(key("block_count")), hidden=int(key("embedding_length")), heads=heads,
+                          kv_heads=kv, head_dim=head_dim, ffn=t["blk.0.ffn_gate.weight"].dims[1],
+                          vocab=t["token_embd.weight"].dims[1], rope_base=float(key("rope.freq_base")),
+                          eps=float(key("attention.layer_norm_rms_epsilon")),
+                          positions=min(positions or ctx, ctx), linear_dtype=t["blk.0.attn_q.weight"].dtype,
+                          embed_dtype=t["token_embd.weight"].dtype)
+        names = {"q": "attn_q", "k": "attn_k", "v": "attn_v", "o": "attn_output", "gate": "ffn_gate",
+                 "up": "ffn_up", "down": "ffn_down"}
+        norms = {"input_norm": "attn_norm", "ffn_norm": "ffn_norm", "q_norm": "attn_q_norm",
+                 "k_norm": "attn_k_norm"}
+        to_dev = lambda n: torch.from_numpy(g.floats(n)).to(device)  # noqa: E731
+        layers = []
+        for i in range(cfg.layers):
+            L = {k: g.tensor(f"blk.{i}.{n}.weight") for k, n in names.items()}
+            L.update({k: to_dev(f"blk.{i}.{n}.weight") for k, n in norms.items()})
+            layers.append(L)
+        shapes = {k: (v.shape()[1], v.shape()[0]) for k, v in layers[0].items() if k in names}
+        weights = {"layers": layers, "embed": g.tensor("token_embd.weight"),
+                   "output": g.tensor("output.weight") if "output.weight" in t else None,
+                   "output_norm": to_dev("output_norm.weight"), "shapes": shapes}
+        model = cls(cfg, weights, device, fused=fused)
+        model.gguf = g  # keeps the mapping (and its metadata) alive with the model
+        return model
 
     def __del__(self):
         h = getattr(self, "_step", None)
@@ -199,7 +255,7 @@ class DenseModel:
             nxt = self.layers[i + 1]["input_norm"] if i + 1 < len(self.layers) else self.output_norm
             check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.ff), _p(nxt), H, M, cfg.eps, _p(a.normalized), st))
         # logits of the last token only (model.rs:619-622)
-        check(lib.hyq_matmul(self.embed.handle, last(a.normalized), 1, _p(self.logits), st))
+        check(lib.hyq_matmul(self.output.handle, last(a.normalized), 1, _p(self.logits), st))
         check(lib.hyq_argmax(_p(self.logits), cfg.vocab, _p(self.token), _p(self.pos), M, _p(self.argmax_ws), st))
 
     def enqueue_step(self):

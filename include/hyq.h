@@ -36,8 +36,11 @@ typedef enum hyq_dtype {
   HYQ_STQ1_0 = 6  /* Tencent STQ1 stride-16 sparse ternary: 256 weights per 42 bytes */
 } hyq_dtype;
 
-/* GGUF type-id profiles (gguf.rs:17-27, Profile; Auto is resolved by the caller). */
+/* GGUF type-id profiles (gguf.rs:17-27, Profile).  Auto (hyq_gguf_open only)
+ * resolves to Standard, or for files with legacy ids 40/42 to the Tencent
+ * profile whose known export the file's SHA-256 matches. */
 typedef enum hyq_profile {
+  HYQ_PROFILE_AUTO = 0,
   HYQ_PROFILE_STANDARD = 1,
   HYQ_PROFILE_TENCENT_Q2_0C = 2,
   HYQ_PROFILE_TENCENT_STQ1 = 3
@@ -283,6 +286,34 @@ int hyq_add_rms_norm(float* hidden, const float* delta, const float* w, int64_t 
 #define HYQ_ARGMAX_WORKSPACE_BYTES 16
 int hyq_argmax(const float* x, int64_t n, int32_t* token, int32_t* pos, int pos_step, void* workspace,
                void* stream);
+
+/* --- GGUF v3 model files (gguf.rs:50-210) --------------------------------
+ * hyq_gguf_open maps the file read-only and checks it as the reference does
+ * (header bounds, metadata types, alignment, tensor table, Tencent legacy
+ * profiles, truncated or overlapping tensors); errors are HYQ_E_* codes with
+ * the reason in hyq_last_error.  Tensor dims are in GGUF order (contiguous
+ * input first); offsets are absolute file offsets.  hyq_gguf_upload copies a
+ * tensor's packed bytes unchanged to a new device weight (hyq_upload).
+ * Metadata getters follow the reference's typed access: integers of any
+ * GGUF integer type that fit u64, floats of any numeric type, booleans,
+ * strings; array lengths.  The file must not change while it is open. */
+typedef struct hyq_gguf hyq_gguf;
+int hyq_gguf_open(const char* path, int profile, hyq_gguf** out);
+void hyq_gguf_close(hyq_gguf* g);
+int hyq_gguf_profile(const hyq_gguf* g);
+int64_t hyq_gguf_tensor_count(const hyq_gguf* g);
+int hyq_gguf_tensor_name(const hyq_gguf* g, int64_t index, const char** name);
+int hyq_gguf_tensor_info(const hyq_gguf* g, const char* name, int* dtype, uint32_t* type_id, int* ndim,
+                         int64_t* dims /* [4] */, uint64_t* offset, uint64_t* byte_len);
+int hyq_gguf_tensor_data(const hyq_gguf* g, const char* name, const void** data, size_t* bytes);
+int hyq_gguf_upload(const hyq_gguf* g, const char* name, hyq_weight** out);
+int64_t hyq_gguf_meta_count(const hyq_gguf* g);
+int hyq_gguf_meta_key(const hyq_gguf* g, int64_t index, const char** key, int* type);
+int hyq_gguf_meta_u64(const hyq_gguf* g, const char* key, uint64_t* out);
+int hyq_gguf_meta_f64(const hyq_gguf* g, const char* key, double* out);
+int hyq_gguf_meta_bool(const hyq_gguf* g, const char* key, int* out);
+int hyq_gguf_meta_str(const hyq_gguf* g, const char* key, const char** s, size_t* len);
+int hyq_gguf_meta_array_len(const hyq_gguf* g, const char* key, int64_t* n);
 
 /* --- The whole Dense decoder token step as one persistent kernel --------
  * model.rs:374-547 for one token: embedding row, per layer RMSNorm -> QKV ->
