@@ -62,6 +62,8 @@ def args_parse():
     ap.add_argument("--sweep", action="store_true",
                     help="gemv: also measure every packed format at 6144x2048 and 120832x2048, both paths")
     ap.add_argument("--tokens", type=int, default=512, help="prefill: tokens M")
+    ap.add_argument("--concurrency", type=int, default=1,
+                    help="model: independent requests decoded together (config 4 asks for 1 and 64)")
     ap.add_argument("--model-kernels", action="store_true",
                     help="model: one launch per operation instead of the persistent token-step kernel")
     return ap.parse_args()
@@ -901,6 +903,8 @@ def tp_arm(a):
 # Full-model greedy decode (config 4): random-init 1.8B architecture
 # ---------------------------------------------------------------------------
 def model_arm(a):
+    if a.concurrency > 1:
+        return batch_arm(a)
     import numpy as np
     import torch
 
@@ -1034,6 +1038,119 @@ def model_arm(a):
         "cpu_baseline": {"value": round(1.0 / cpu_s, 3), "unit": "tokens/s", "cores": host_threads(), "kind": "port",
                          "sample": f"{n_cpu} decode steps of the same model through oracle/model.py (x86 f32 "
                                    "order, OpenMP)"},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def batch_arm(a):
+    """Config 4 at concurrency B: B independent requests (256-token prompts,
+    256 generated each) decoded together, one token of every request per
+    step (DenseBatch, one CUDA graph per step)."""
+    import numpy as np
+    import torch
+
+    world, rank, dev = init_ranks()
+    import hy_mt_rs_b200  # noqa: F401
+    from hy_mt_rs_b200 import quant
+    from hy_mt_rs_b200.model import DenseBatch, DenseConfig, DenseModel, random_weights
+
+    B, n_prompt, n_new = a.concurrency, 256, 256
+    cfg = DenseConfig(layers=N_LAYERS_MODEL, positions=n_prompt + n_new)
+    weights = random_weights(cfg, dev, seed=1)
+    torch.cuda.synchronize(dev)
+    model = DenseModel(cfg, weights, dev)
+    batch = DenseBatch(model, B)
+    stream = torch.cuda.Stream(dev)
+    batch.capture(stream)
+    rng = np.random.default_rng(0)
+    prompts = [rng.integers(0, cfg.vocab, n_prompt).tolist() for _ in range(B)]
+    sampler = ClockSampler("GPU-" + str(torch.cuda.get_device_properties(dev).uuid))
+    e0, e1, e1b, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(4))
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, a.warmup)):
+            batch.graph.replay()
+        batch.reset()
+        ids = [torch.tensor(p, dtype=torch.int32).to(dev) for p in prompts]
+        stream.synchronize()
+        e0.record(stream)
+        for b in range(B):   # each request's prompt: batched forwards into its cache slice
+            caches = [(k[b], v[b]) for k, v in batch.caches]
+            for c0 in range(0, n_prompt, model.chunk):
+                model.prefill(ids[b][c0:c0 + model.chunk], caches=caches, pos=batch.pos[b:b + 1],
+                              token_out=batch.tokens[b:b + 1], logits=batch.logits[b])
+        e1.record(stream)
+        stream.synchronize()
+        sampler.start()
+        e1b.record(stream)
+        for _ in range(n_new - 1):
+            batch.graph.replay()
+        e2.record(stream)
+        stream.synchronize()
+        sampler.stop()
+        # e2e: every step's B tokens read back to the host, one step late
+        batch.reset()
+        batch.prefill_all(prompts)
+        tok_host = torch.empty(n_new, B, dtype=torch.int32).pin_memory()
+        done = [torch.cuda.Event() for _ in range(n_new)]
+        stream.synchronize()
+        t0 = time.perf_counter()
+        for i in range(n_new - 1):
+            batch.graph.replay()
+            tok_host[i].copy_(batch.tokens, non_blocking=True)
+            done[i].record(stream)
+            if i:
+                done[i - 1].synchronize()
+        done[n_new - 2].synchronize()
+        e2e_s = time.perf_counter() - t0
+    failed = device_failed(quant, dev)
+    (ms_decode, ms_prompt, failed), clocks_all = reduce_over_ranks(
+        [e1b.elapsed_time(e2), e0.elapsed_time(e1), failed + 0.0], sampler.summary(), dev)
+    if failed:
+        raise RuntimeError("a kernel reported an expired bounded wait (device status word) on some rank")
+    step_launches = batch.launches()
+    batch.graph = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    steps = n_new - 1
+    tok_s = B * steps / (ms_decode * 1e-3) * world
+    weight_bytes = N_LAYERS_MODEL * sum(N * row_bytes(5, K) for _, N, K in LAYER) + VOCAB * row_bytes(3, HIDDEN)
+    # KV cache bytes a step reads (f32 K and V rows of every visible position
+    # of every request) and writes (one row pair per request), per layer
+    kv_row = 2 * cfg.kv_heads * cfg.head_dim * 4
+    visible = sum(n_prompt + i + 1 for i in range(1, n_new)) / steps
+    kv_bytes = N_LAYERS_MODEL * B * (visible + 1) * kv_row
+    step_bytes = weight_bytes + kv_bytes
+    step_s = ms_decode / steps * 1e-3
+    peak, peak_kind = measured_peaks()
+    sm = [c["sm_mhz"] for c in clocks_all if c.get("sm_mhz")]
+    line = {
+        "metric": f"decode tokens/s (random-init Hy-MT2-1.8B architecture, Q2_0C linears, Q6_K tied embedding, "
+                  f"{B} concurrent requests, greedy)",
+        "value": round(tok_s, 1), "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": max(3, a.warmup),
+        "ms_per_step": round(ms_decode / steps, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32 activations; fp16 tensor-core products of the dequantized weights; f32 KV cache",
+        "data": f"synthetic (seeded random-init weights, {B} seeded random 256-token prompts)",
+        "config": {"workload": "hy-mt-rs config 4: 32 layers, hidden 2048, 16/4 heads x 128, SwiGLU 6144, "
+                               "vocab 120832, RoPE 10000; 256-token prompts (batched prefill), 256 generated each",
+                   "concurrency": B, "positions": cfg.positions, "parallelism": f"replicas x{world}"},
+        "prompt_ms": round(ms_prompt, 2),
+        "prompt": f"{B} prompts of 256 tokens, one batched forward each",
+        "roofline": {"bound": "hbm", "kernel": "whole decode step (weights + KV cache per step)", "unit": "GB/s",
+                     "achieved": round(step_bytes / step_s / 1e9, 1), "peak": peak, "peak_kind": peak_kind,
+                     "frac": round(step_bytes / step_s / 1e9 / peak, 4), "traffic": None,
+                     "algorithmic_bytes_per_launch": int(step_bytes), "weight_bytes": weight_bytes,
+                     "kv_bytes": int(kv_bytes)},
+        "e2e": {"value": round(B * steps / e2e_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 4 * B, "how": "graph replay per step, each step's tokens read back one step late"},
+        "gpu_launches": steps * step_launches,
+        "clocks": {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": clocks_all[0].get("sm_max_mhz"),
+                   "reasons": sorted({r for c in clocks_all for r in c.get("reasons", [])}),
+                   "samples": sum(c.get("samples", 0) for c in clocks_all)},
     }
     print(json.dumps(line), flush=True)
     return 0

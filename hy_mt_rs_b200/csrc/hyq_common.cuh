@@ -271,4 +271,49 @@ __device__ __forceinline__ float dot_x86(const float* a, const float* b, int n, 
   return __fadd_rn(h, t);
 }
 
+// The same dot_avx2 order (quant.rs:2562-2596) computed by one thread: the
+// sixteen accumulator lanes are registers, followed by the same pairwise lane
+// sums, horizontal sum and scalar tail as dot_x86.  a and b are 16-byte
+// aligned when n % 4 == 0 (float4 loads).
+__device__ __forceinline__ float dot_x86_thread(const float* a, const float* b, int n) {
+  float acc[16];
+#pragma unroll
+  for (int l = 0; l < 16; ++l) acc[l] = 0.f;
+  const int chunks = n / 16;
+  if ((n & 3) == 0) {
+    const float4* a4 = reinterpret_cast<const float4*>(a);
+    const float4* b4 = reinterpret_cast<const float4*>(b);
+#pragma unroll 2
+    for (int c = 0; c < chunks; ++c) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float4 x = a4[4 * c + j], y = b4[4 * c + j];
+        acc[4 * j] = fmaf(x.x, y.x, acc[4 * j]);
+        acc[4 * j + 1] = fmaf(x.y, y.y, acc[4 * j + 1]);
+        acc[4 * j + 2] = fmaf(x.z, y.z, acc[4 * j + 2]);
+        acc[4 * j + 3] = fmaf(x.w, y.w, acc[4 * j + 3]);
+      }
+    }
+  } else {
+    for (int c = 0; c < chunks; ++c) {
+#pragma unroll
+      for (int l = 0; l < 16; ++l) acc[l] = fmaf(a[16 * c + l], b[16 * c + l], acc[l]);
+    }
+  }
+  float sum[8];
+#pragma unroll
+  for (int l = 0; l < 8; ++l) sum[l] = __fadd_rn(acc[l], acc[l + 8]);
+  const int simd_end = chunks * 16, vec_end = n / 8 * 8;
+  if (vec_end > simd_end) {
+#pragma unroll
+    for (int l = 0; l < 8; ++l) sum[l] = fmaf(a[simd_end + l], b[simd_end + l], sum[l]);
+  }
+  float h = -0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) h = __fadd_rn(h, sum[k]);
+  float t = -0.0f;
+  for (int i = vec_end; i < n; ++i) t = __fadd_rn(t, __fmul_rn(a[i], b[i]));
+  return __fadd_rn(h, t);
+}
+
 }  // namespace hyq

@@ -423,6 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base_g + L::misc + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (p.expert_off) grid_dependency_wait();  // the expert offsets come from the previous grid
   int tok0 = blockIdx.y * BN;
   int tok_end = p.M;  // activation rows of this tile end here
   // row tile -> matrix and its first row (a gate/up tile covers 64 rows of each)
@@ -471,6 +472,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // set-up above overlaps the previous grid's tail (launch_ex); data after
+  grid_dependency_wait();
+  allow_dependents_launch();
 
   if (warp == 0) {
     // ------------------------------ TMA producer ----------------------------
@@ -975,6 +979,8 @@ template <int FMT>
 __global__ void __launch_bounds__(256) to_half_kernel(const float* __restrict__ x, __half2* __restrict__ h,
                                                        int64_t K, int64_t total_pairs,
                                                        const int32_t* __restrict__ rows) {
+  grid_dependency_wait();
+  allow_dependents_launch();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= total_pairs) return;
   const int64_t e = 2 * i;  // element index of the first slot
@@ -1077,8 +1083,7 @@ cudaError_t run(const CUtensorMap* tw, const CUtensorMap& tx, const Params& p, i
   }
   // token tiles: of all M rows, or (expert mode) of the most rows one expert can have
   dim3 grid((unsigned)tiles, (unsigned)((max_rows + BN - 1) / BN), (unsigned)splits);
-  k<<<grid, kThreads, smem, st>>>(tw[0], tw[1], tw[2], tx, p);
-  return cudaGetLastError();
+  return launch_ex(k, grid, dim3(kThreads), (size_t)smem, st, tw[0], tw[1], tw[2], tx, p);
 }
 
 // Sum of the split-K partials in slice order, written to the matrices'
@@ -1096,6 +1101,8 @@ struct ReduceArgs {
 };
 
 __global__ void __launch_bounds__(256) reduce_splits_kernel(const __grid_constant__ ReduceArgs a) {
+  grid_dependency_wait();
+  allow_dependents_launch();
   const int cols = a.gate_up ? a.seg_rows[0] : a.N;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= a.M * cols) return;
@@ -1126,14 +1133,16 @@ int device_sms() {
   return sms[dev] > 0 ? sms[dev] : 148;
 }
 
-// Split-K slices (in block columns) so that small grids still fill the GPU.
+// Split-K slices (in block columns) so that small grids still fill the GPU,
+// within one wave of CTAs (one per SM): a second, partial wave costs a whole
+// slice's time for a fraction of the SMs.
 int choose_splits(int64_t K, int64_t row_tiles, int64_t M, int wcol) {
   const int64_t bn = M >= 256 ? 256 : 128;
   const int64_t tiles = row_tiles * ((M + bn - 1) / bn);
   const int64_t nwb = K / wcol;
   const int64_t sms = device_sms();
   if (tiles >= sms) return 1;
-  int64_t z = (sms + tiles - 1) / tiles;
+  int64_t z = sms / tiles;
   if (z > nwb) z = nwb;
   if (z > 16) z = 16;
   return (int)(z < 1 ? 1 : z);
@@ -1226,14 +1235,14 @@ cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) 
     const int64_t pairs = K * M / 2;
     const unsigned blocks = (unsigned)((pairs + 255) / 256);
     __half2* xh2 = reinterpret_cast<__half2*>(xh);
+    cudaError_t e;
     switch (j.dtype) {
-      case Q4_K: to_half_kernel<Q4_K><<<blocks, 256, 0, st>>>(j.x, xh2, K, pairs, j.x_rows); break;
-      case Q6_K: to_half_kernel<Q6_K><<<blocks, 256, 0, st>>>(j.x, xh2, K, pairs, j.x_rows); break;
-      case Q8_0: to_half_kernel<Q8_0><<<blocks, 256, 0, st>>>(j.x, xh2, K, pairs, j.x_rows); break;
-      case Q2_0C: to_half_kernel<Q2_0C><<<blocks, 256, 0, st>>>(j.x, xh2, K, pairs, j.x_rows); break;
-      default: to_half_kernel<STQ1_0><<<blocks, 256, 0, st>>>(j.x, xh2, K, pairs, j.x_rows); break;
+      case Q4_K: e = launch_ex(to_half_kernel<Q4_K>, dim3(blocks), dim3(256), 0, st, j.x, xh2, K, pairs, j.x_rows); break;
+      case Q6_K: e = launch_ex(to_half_kernel<Q6_K>, dim3(blocks), dim3(256), 0, st, j.x, xh2, K, pairs, j.x_rows); break;
+      case Q8_0: e = launch_ex(to_half_kernel<Q8_0>, dim3(blocks), dim3(256), 0, st, j.x, xh2, K, pairs, j.x_rows); break;
+      case Q2_0C: e = launch_ex(to_half_kernel<Q2_0C>, dim3(blocks), dim3(256), 0, st, j.x, xh2, K, pairs, j.x_rows); break;
+      default: e = launch_ex(to_half_kernel<STQ1_0>, dim3(blocks), dim3(256), 0, st, j.x, xh2, K, pairs, j.x_rows); break;
     }
-    cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
   // expert mode: the typical rows per expert pick the token tile
@@ -1330,8 +1339,7 @@ cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) 
     r.ys[m] = p.ys[m];
   }
   const int64_t n = M * (j.gate_up ? j.rows[0] : lay.ncols);
-  reduce_splits_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(r);
-  return cudaGetLastError();
+  return launch_ex(reduce_splits_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, r);
 }
 
 // Single-matrix forms used by hyq_matmul and hyq_matmul_noalloc.

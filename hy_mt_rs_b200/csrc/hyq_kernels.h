@@ -85,4 +85,22 @@ int api_status_word(unsigned** out);
 // hyq_set_launch_overlap's switch, read at launch time.
 bool launch_overlap();
 
+// Launch with the programmatic-dependent attribute when launch_overlap() is
+// on: such kernels wait for their predecessor grid (griddepcontrol.wait)
+// before touching memory, and let their own dependents launch early.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_ex(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = launch_overlap() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+}
+
 }  // namespace hyq

@@ -23,41 +23,32 @@
 namespace hyq {
 namespace model {
 
-// Launch with the programmatic-dependent attribute when hyq_set_launch_overlap
-// is on: every kernel here waits for its predecessor grid before touching
-// memory (griddepcontrol.wait) and lets its own dependents launch at once.
+// Every kernel here waits for its predecessor grid before touching memory
+// (griddepcontrol.wait) and lets its own dependents launch at once.
+using hyq::launch_ex;
 template <typename... KArgs, typename... Args>
 cudaError_t launch(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cfg.attrs = attr;
-  cfg.numAttrs = launch_overlap() ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+  return launch_ex(k, grid, block, smem, st, args...);
 }
 
-// Dynamic shared memory of the norm kernels: up to kNormMaxN floats (set once
-// per device and kernel).
+// Dynamic shared memory of the norm kernels: up to 2 kNormMaxN floats (the
+// row and the weights; set once per device and kernel).
 template <typename K>
 void norm_smem_limit(K k) {
   static int done_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (done_dev != dev) {
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 16384 * (int)sizeof(float));
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 16384 * (int)sizeof(float));
     done_dev = dev;
   }
 }
 
 // RMSNorm of `rows` rows of n floats (rms_norm_into, model.rs:785-830; per
 // head, model.rs:832-872): variance = dot(x, x) / n, scale = 1 / sqrt(var +
-// eps), out = (x * scale) * w.  One CTA per row; the row is staged in shared
-// memory (n <= kNormMaxN) so that the 16-lane x86-order sum runs from there.
+// eps), out = (x * scale) * w.  One CTA per row; the row and the weights are
+// staged in shared memory in one batch of loads (n <= kNormMaxN) so that the
+// 16-lane x86-order sum runs from there.
 constexpr int kNormMaxN = 16384;
 
 __device__ __forceinline__ float staged_rms_scale(const float* xs, int n, float eps) {
@@ -74,13 +65,19 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const float* __restrict__
                                                         int n, float eps, float* __restrict__ out) {
   grid_dependency_wait();
   allow_dependents_launch();
-  extern __shared__ float xs[];
+  extern __shared__ float xs[];  // [n] row, [n] weights
+  float* wsm = xs + n;
   const float* xr = x + (size_t)blockIdx.x * n;
   float* orow = out + (size_t)blockIdx.x * n;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = xr[i];
+#pragma unroll 8
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = xr[i], wi = w[i];
+    xs[i] = v;
+    wsm[i] = wi;
+  }
   __syncthreads();
   const float scale = staged_rms_scale(xs, n, eps);
-  for (int i = threadIdx.x; i < n; i += blockDim.x) orow[i] = __fmul_rn(__fmul_rn(xs[i], scale), w[i]);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) orow[i] = __fmul_rn(__fmul_rn(xs[i], scale), wsm[i]);
 }
 
 // Embedding row (Weight::row_into, quant.rs:123-142) of the token held in
@@ -128,6 +125,10 @@ struct RopeArgs {
   float* k_cache;        // [positions, kv_heads * dim]
   float* v_cache;
   unsigned* status;
+  // independent sequences: token t is sequence t at position pos[t], its
+  // caches seq_stride floats further per sequence (0: one sequence, token t
+  // at position *pos + t)
+  int64_t seq_stride;
 };
 
 __device__ void head_norm(float* hd, const float* w, int dim, float eps) {
@@ -153,9 +154,10 @@ __device__ void head_rope(float* hd, const float* c, const float* s, int dim) {
 __global__ void __launch_bounds__(32) rope_qk_kernel(const __grid_constant__ RopeArgs a) {
   grid_dependency_wait();
   allow_dependents_launch();
-  const int tok = blockIdx.y;  // token tok of the batch sits at position *pos + tok
-  const int pos = *a.pos + tok;
-  if (*a.pos < 0 || pos >= a.positions) {
+  const int tok = blockIdx.y;
+  const int base = a.seq_stride ? a.pos[tok] : *a.pos;
+  const int pos = a.seq_stride ? base : base + tok;  // one sequence: token tok at *pos + tok
+  if (base < 0 || pos >= a.positions) {
     if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(a.status, DEV_BAD_ARGS);
     return;
   }
@@ -166,41 +168,72 @@ __global__ void __launch_bounds__(32) rope_qk_kernel(const __grid_constant__ Rop
   const float* nw = is_q ? a.q_norm : a.k_norm;
   const float* c = a.cos_tab + (size_t)pos * (a.dim / 2);
   const float* s = a.sin_tab + (size_t)pos * (a.dim / 2);
-  __shared__ float hs[kRopeMaxDim];  // the head, worked on in shared memory
-  for (int i = threadIdx.x; i < a.dim; i += 32) hs[i] = hd[i];
+  // the head, its norm weights, the table row (and for a kv head its value
+  // head) staged in shared memory in one batch of loads
+  __shared__ float hs[kRopeMaxDim], ws[kRopeMaxDim], cs[kRopeMaxDim / 2], sn[kRopeMaxDim / 2], vs[kRopeMaxDim];
+  const int kh = h - a.heads;
+  const float* vv = a.v + krow + (size_t)kh * a.dim;
+#pragma unroll 4
+  for (int i = threadIdx.x; i < a.dim; i += 32) {
+    hs[i] = hd[i];
+    if (nw) ws[i] = nw[i];
+    if (!is_q) vs[i] = vv[i];
+    if (i < a.dim / 2) {
+      cs[i] = c[i];
+      sn[i] = s[i];
+    }
+  }
   __syncwarp();
-  if (a.norm_first && nw) head_norm(hs, nw, a.dim, a.eps);
-  head_rope(hs, c, s, a.dim);
-  if (!a.norm_first && nw) head_norm(hs, nw, a.dim, a.eps);
+  if (a.norm_first && nw) head_norm(hs, ws, a.dim, a.eps);
+  head_rope(hs, cs, sn, a.dim);
+  if (!a.norm_first && nw) head_norm(hs, ws, a.dim, a.eps);
   for (int i = threadIdx.x; i < a.dim; i += 32) hd[i] = hs[i];
   if (!is_q) {
-    const int kh = h - a.heads;
     const size_t width = (size_t)a.kv_heads * a.dim;
-    float* kc = a.k_cache + (size_t)pos * width + (size_t)kh * a.dim;
-    float* vc = a.v_cache + (size_t)pos * width + (size_t)kh * a.dim;
-    const float* vv = a.v + krow + (size_t)kh * a.dim;
+    const size_t seq = a.seq_stride ? (size_t)tok * a.seq_stride : 0;
+    float* kc = a.k_cache + seq + (size_t)pos * width + (size_t)kh * a.dim;
+    float* vc = a.v_cache + seq + (size_t)pos * width + (size_t)kh * a.dim;
     for (int i = threadIdx.x; i < a.dim; i += 32) {
       kc[i] = hs[i];
-      vc[i] = vv[i];
+      vc[i] = vs[i];
     }
   }
 }
 
 // attention_into for one query token (model.rs:949-1021), split over the
-// cached positions as in flash decoding: CTA (split, head) takes positions
-// [64 split, 64 split + 64) of 0..pos, writes its local max m, exponential
-// sum l and unnormalised output to the workspace, and the last CTA of a head
-// to finish combines them: out = sum_i o_i e^(m_i - M) / sum_i l_i e^(m_i - M).
-// Scores are dot(q, k) * (1 / sqrt(dim)) in the reference's x86 dot order;
-// the exponentials come from the device expf and the sums follow the split
-// tree, so outputs match the reference to rounding, not bit for bit.
+// cached positions as in flash decoding.  CTA (split, kv head, token) takes
+// positions [64 split, 64 split + 64) of 0..pos for every query head that
+// shares the kv head (heads / kv_heads of them), so each K and V row is read
+// once: both chunks are staged in shared memory with cp.async (the scores
+// start on K while V lands).  Each query head's local max m, exponential sum
+// l and unnormalised output go to the workspace, and the last CTA of a (token,
+// kv head) to finish combines them per head:
+// out = sum_i o_i e^(m_i - M) / sum_i l_i e^(m_i - M).  Scores are dot(q, k) *
+// (1 / sqrt(dim)) in the reference's x86 dot order (one thread per position
+// and head); the exponentials come from the device expf and the sums follow
+// the split tree, so outputs match the reference to rounding, not bit for bit.
 constexpr int kMaxPositions = 16384;
 constexpr int kAttnChunk = 64;
 constexpr int kAttnThreads = 128;
 constexpr int kAttnMaxDim = 256;
+constexpr int kAttnMaxGroup = 16;  // query heads per kv head
+static_assert(kAttnThreads == 2 * kAttnChunk, "the score phase pairs two threads per position");
 
-// Counters per (token, head) at the head of the workspace, padded to 256 bytes.
+// Counters per (token, kv head) at the head of the workspace (sized for
+// positions x heads slots), padded to 256 bytes.
 inline size_t attn_counter_bytes(int64_t slots) { return ((size_t)slots * sizeof(unsigned) + 255) / 256 * 256; }
+
+// Shared memory of one CTA: K chunk (padded rows), V chunk, the group's query
+// heads (same padding), exponentials, combine weights and per-head inverse
+// sums.  The K region also holds the V phase's per-group partial outputs.
+// (dim % 4 == 0: the row stride in float4 units is 2 mod 8, so the thread
+// pairs of the score phase read 8 distinct 4-bank groups per quarter warp)
+__host__ __device__ inline int attn_kstride(int dim) { return (dim & 3) ? dim + 1 : dim + 4 * ((10 - (dim >> 2) % 8) % 8); }
+inline size_t attn_smem_bytes(int dim, int group, int nsplit) {
+  const size_t ks = (size_t)attn_kstride(dim);
+  return sizeof(float) * (kAttnChunk * ks + (size_t)kAttnChunk * dim + group * ks + (size_t)group * kAttnChunk +
+                          (size_t)group * nsplit + group);
+}
 
 struct AttnArgs {
   const float* q;
@@ -211,92 +244,280 @@ struct AttnArgs {
   int positions;
   float* out;
   float* ws;           // [tokens][heads][splits][2 + dim]
-  unsigned* counters;  // [tokens][heads], zero between calls
+  unsigned* counters;  // [tokens][kv_heads], zero between calls
   unsigned* status;
+  int64_t seq_stride;  // as RopeArgs: 0 one sequence, else per-token sequences
 };
 
-__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_constant__ AttnArgs a) {
+__device__ __forceinline__ void cp_async16(float* dst, const float* src) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(float* dst, const float* src) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// rows x dim floats from global rows `gstride` apart into shared rows
+// `sstride` apart (16-byte copies when every row start is 16-byte aligned).
+// DIM > 0: dim == DIM (16-byte copies), rows <= kAttnChunk, loops unrolled.
+template <int DIM>
+__device__ __forceinline__ void stage_rows(float* dst, int sstride, const float* src, size_t gstride, int rows,
+                                           int dim, bool vec) {
+  if constexpr (DIM > 0) {
+    constexpr int w = DIM / 4, per = kAttnThreads / w;
+    static_assert(kAttnThreads % w == 0, "whole rows per pass");
+    const int c = threadIdx.x % w, i0 = threadIdx.x / w;
+#pragma unroll
+    for (int k = 0; k < kAttnChunk / per; ++k) {
+      const int i = i0 + k * per;
+      if (i < rows) cp_async16(dst + i * sstride + 4 * c, src + i * gstride + 4 * c);
+    }
+    return;
+  }
+  // element t = i * w + c of the rows x w copies (w = dim / 4 or dim), walked
+  // with one division up front and carries after
+  const int w = vec ? dim >> 2 : dim;
+  int i = threadIdx.x / w, c = threadIdx.x - (threadIdx.x / w) * w;
+  const int di = kAttnThreads / w, dc = kAttnThreads - di * w;
+  for (; i < rows;) {
+    if (vec) cp_async16(dst + i * sstride + 4 * c, src + i * gstride + 4 * c);
+    else cp_async4(dst + i * sstride + c, src + i * gstride + c);
+    i += di;
+    c += dc;
+    if (c >= w) {
+      c -= w;
+      ++i;
+    }
+  }
+}
+
+// DIM, GRP > 0: a kernel for head size DIM and GRP query heads per kv head
+// (loops unrolled to constant offsets); 0: any shape.
+template <int DIM, int GRP>
+__global__ void __launch_bounds__(kAttnThreads, 3) attention_kernel(const __grid_constant__ AttnArgs a) {
+  static_assert(DIM == 0 || (DIM % 16 == 0 && kAttnThreads % (DIM / 4) == 0), "specialised head size");
   grid_dependency_wait();
   allow_dependents_launch();
-  __shared__ float q_s[kAttnMaxDim];
-  __shared__ float e_s[kAttnChunk];
-  __shared__ float cw_s[kMaxPositions / kAttnChunk];
-  __shared__ float bc[2];
+  extern __shared__ __align__(16) float attn_smem[];
   __shared__ int last_s;
   // token tok of the batch sits at position *pos + tok and sees positions
   // 0 ..= it (causal, model.rs:959)
   const int tok = blockIdx.z;
-  const int pos = *a.pos + tok;
-  if (*a.pos < 0 || pos >= a.positions) {
+  const int base = a.seq_stride ? a.pos[tok] : *a.pos;
+  const int pos = a.seq_stride ? base : base + tok;
+  if (base < 0 || pos >= a.positions) {
     if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) atomicOr(a.status, DEV_BAD_ARGS);
     return;
   }
   const int visible = pos + 1;
   const int used = (visible + kAttnChunk - 1) / kAttnChunk;  // splits with positions
-  const int split = blockIdx.x, h = blockIdx.y;
+  const int split = blockIdx.x, kvh = blockIdx.y;
   if (split >= used) return;
-  const int dim = a.dim;
-  const int kvh = h / (a.heads / a.kv_heads);
-  const size_t width = (size_t)a.kv_heads * dim;
-  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)dim));
+  const int dim = DIM ? DIM : a.dim, G = GRP ? GRP : a.heads / a.kv_heads, ks = attn_kstride(dim);
+  const int nsplit = (a.positions + kAttnChunk - 1) / kAttnChunk;
+  float* k_s = attn_smem;
+  float* v_s = k_s + kAttnChunk * ks;
+  float* q_s = v_s + kAttnChunk * dim;
+  float* e_s = q_s + G * ks;
+  float* cw_s = e_s + G * kAttnChunk;
+  float* inv_s = cw_s + G * nsplit;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const size_t th = (size_t)tok * a.heads + h;  // (token, head) slot
-  for (int d = threadIdx.x; d < dim; d += kAttnThreads) q_s[d] = a.q[th * dim + d];
-  __syncthreads();
+  const size_t width = (size_t)a.kv_heads * dim;
+  const size_t seq = a.seq_stride ? (size_t)tok * a.seq_stride : 0;
   const int p0 = split * kAttnChunk;
   const int n = min(kAttnChunk, visible - p0);
-  // scores of this chunk in the x86 dot order: a half-warp per position
-  for (int base = 2 * warp; base < n; base += kAttnThreads / 16) {
-    const int i = base + (lane >> 4);
-    const bool valid = i < n;
-    const float* kr = a.k_cache + (size_t)(p0 + (valid ? i : 0)) * width + (size_t)kvh * dim;
-    const float d = dot_x86(q_s, kr, dim, 0xffffffffu);
-    if (valid && (lane & 15) == 0) e_s[i] = __fmul_rn(d, scale);
+  const float* kg = a.k_cache + seq + (size_t)p0 * width + (size_t)kvh * dim;
+  const float* vg = a.v_cache + seq + (size_t)p0 * width + (size_t)kvh * dim;
+  const bool vec = (dim & 3) == 0 && (width & 3) == 0 && ((reinterpret_cast<uintptr_t>(kg) | reinterpret_cast<uintptr_t>(vg)) & 15) == 0;
+  // (the specialised kernel is launched only for 16-byte aligned caches)
+  stage_rows<DIM>(k_s, ks, kg, width, n, dim, vec);
+  cp_async_commit();
+  stage_rows<DIM>(v_s, dim, vg, width, n, dim, vec);
+  cp_async_commit();
+  const size_t h0 = (size_t)tok * a.heads + (size_t)kvh * G;  // (token, first head of the group)
+  const float* qg = a.q + h0 * dim;
+  if (vec && (reinterpret_cast<uintptr_t>(qg) & 15) == 0) {
+    const int q4 = dim >> 2;
+    for (int t = threadIdx.x; t < G * q4; t += kAttnThreads) {
+      const int g = t / q4;
+      *reinterpret_cast<float4*>(q_s + g * ks + 4 * (t - g * q4)) = *reinterpret_cast<const float4*>(qg + 4 * t);
+    }
+  } else {
+    for (int t = threadIdx.x; t < G * dim; t += kAttnThreads) {
+      const int g = t / dim;
+      q_s[g * ks + (t - g * dim)] = qg[t];
+    }
+  }
+  cp_async_wait<1>();  // this thread's K copies
+  __syncthreads();
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)dim));
+  if (vec && (dim & 15) == 0) {
+    // scores: a thread pair per position, each K row read once for every
+    // head of the group.  dot_avx2's 16 accumulator lanes (quant.rs:2562-2596)
+    // split as lanes {0-3, 8-11} (first thread: its pairwise sums are lanes
+    // 0-3 of the horizontal sum) and {4-7, 12-15} (second: lanes 4-7).
+    const int i = threadIdx.x >> 1, hh = threadIdx.x & 1;
+    const float* kr = k_s + i * ks + 4 * hh;
+    for (int g0 = 0; g0 < G; g0 += 4) {
+      float acc[4][8];
+#pragma unroll
+      for (int g = 0; g < 4; ++g)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[g][j] = 0.f;
+#pragma unroll
+      for (int c = 0; c < (DIM ? DIM : dim); c += 16) {
+        const float4 k0 = *reinterpret_cast<const float4*>(kr + c);
+        const float4 k1 = *reinterpret_cast<const float4*>(kr + c + 8);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          if (g0 + g < G) {
+            const float* qr = q_s + (g0 + g) * ks + 4 * hh + c;
+            const float4 q0 = *reinterpret_cast<const float4*>(qr);
+            const float4 q1 = *reinterpret_cast<const float4*>(qr + 8);
+            acc[g][0] = fmaf(q0.x, k0.x, acc[g][0]);
+            acc[g][1] = fmaf(q0.y, k0.y, acc[g][1]);
+            acc[g][2] = fmaf(q0.z, k0.z, acc[g][2]);
+            acc[g][3] = fmaf(q0.w, k0.w, acc[g][3]);
+            acc[g][4] = fmaf(q1.x, k1.x, acc[g][4]);
+            acc[g][5] = fmaf(q1.y, k1.y, acc[g][5]);
+            acc[g][6] = fmaf(q1.z, k1.z, acc[g][6]);
+            acc[g][7] = fmaf(q1.w, k1.w, acc[g][7]);
+          }
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        float sm[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sm[j] = __fadd_rn(acc[g][j], acc[g][4 + j]);  // lanes 4 hh + j
+        float h = -0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) h = __fadd_rn(h, sm[j]);
+        float hi[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) hi[j] = __shfl_xor_sync(0xffffffffu, sm[j], 1);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) h = __fadd_rn(h, hi[j]);
+        if (hh == 0 && i < n && g0 + g < G) e_s[(g0 + g) * kAttnChunk + i] = __fmul_rn(__fadd_rn(h, -0.0f), scale);
+      }
+    }
+  } else {
+    // scores: one thread per (head, position); a warp shares the head
+    for (int t = threadIdx.x; t < G * kAttnChunk; t += kAttnThreads) {
+      const int g = t / kAttnChunk, i = t - g * kAttnChunk;
+      if (i < n) e_s[t] = __fmul_rn(dot_x86_thread(q_s + g * ks, k_s + i * ks, dim), scale);
+    }
   }
   __syncthreads();
-  // local max and exponentials
-  if (warp == 0) {
+  // per head: local max, exponentials, their sum
+  for (int g = warp; g < G; g += kAttnThreads / 32) {
+    float* e = e_s + g * kAttnChunk;
     float m = -INFINITY;
-    for (int i = lane; i < n; i += 32) m = fmaxf(m, e_s[i]);
+    for (int i = lane; i < n; i += 32) m = fmaxf(m, e[i]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     float l = 0.f;
     for (int i = lane; i < n; i += 32) {
-      const float e = expf(__fsub_rn(e_s[i], m));
-      e_s[i] = e;
-      l += e;
+      const float x = expf(__fsub_rn(e[i], m));
+      e[i] = x;
+      l += x;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
     if (lane == 0) {
-      bc[0] = m;
-      bc[1] = l;
+      float* w = a.ws + ((h0 + g) * nsplit + split) * (2 + dim);
+      w[0] = m;
+      w[1] = l;
     }
   }
+  cp_async_wait<0>();
   __syncthreads();
-  const int nsplit = (a.positions + kAttnChunk - 1) / kAttnChunk;
-  float* w = a.ws + (th * nsplit + split) * (2 + dim);
-  for (int d = threadIdx.x; d < dim; d += kAttnThreads) {
-    const float* vr = a.v_cache + (size_t)p0 * width + (size_t)kvh * dim + d;
-    float o = 0.f;
-    for (int i = 0; i < n; ++i) o = fmaf(e_s[i], vr[(size_t)i * width], o);
-    w[2 + d] = o;
+  // unnormalised outputs per (head, dim): sum_i e_i v_i.  Thread (quad dq,
+  // group pg) takes four consecutive dims of every head over the positions
+  // of its group, in order; the groups' partials are then added in group
+  // order (through the K region, free after the scores).
+  const int outs = G * dim;
+  const int q4 = dim >> 2;
+  const int pgs = vec ? kAttnThreads / q4 : 0;  // position groups
+  if (vec && q4 * pgs == kAttnThreads && kAttnChunk % pgs == 0 && pgs * G * dim <= kAttnChunk * ks) {
+    const int per = kAttnChunk / pgs;
+    const int pg = threadIdx.x / q4, dq = threadIdx.x - pg * q4;
+    const int i0 = pg * per, i1 = min(i0 + per, n);
+    float* red = k_s;  // [pgs][G][dim]
+    for (int g0 = 0; g0 < G; g0 += 4) {
+      float4 o[4];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) o[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int ii = 0; ii < (DIM ? kAttnChunk / (kAttnThreads / (DIM / 4)) : per); ++ii) {
+        const int i = i0 + ii;
+        if (i >= i1) break;
+        const float4 v = *reinterpret_cast<const float4*>(v_s + i * dim + 4 * dq);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          if (g0 + g < G) {
+            const float ei = e_s[(g0 + g) * kAttnChunk + i];
+            o[g].x = fmaf(ei, v.x, o[g].x);
+            o[g].y = fmaf(ei, v.y, o[g].y);
+            o[g].z = fmaf(ei, v.z, o[g].z);
+            o[g].w = fmaf(ei, v.w, o[g].w);
+          }
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < 4; ++g)
+        if (g0 + g < G) *reinterpret_cast<float4*>(red + ((size_t)pg * G + g0 + g) * dim + 4 * dq) = o[g];
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < outs; t += kAttnThreads) {
+      float v = red[t];
+      for (int z = 1; z < pgs; ++z) v = __fadd_rn(v, red[(size_t)z * outs + t]);
+      const int g = t / dim;
+      a.ws[((h0 + g) * nsplit + split) * (2 + dim) + 2 + (t - g * dim)] = v;
+    }
+  } else {
+    // any head size: a thread per (head, dim), positions in order
+    for (int t0 = threadIdx.x; t0 < outs; t0 += 4 * kAttnThreads) {
+      int eo[4], vo[4];
+      float o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int t = min(t0 + j * kAttnThreads, outs - 1);
+        const int g = t / dim;
+        eo[j] = g * kAttnChunk;
+        vo[j] = t - g * dim;
+        o[j] = 0.f;
+      }
+      for (int i = 0; i < n; ++i) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[j] = fmaf(e_s[eo[j] + i], v_s[i * dim + vo[j]], o[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int t = t0 + j * kAttnThreads;
+        if (t < outs) a.ws[((h0 + t / dim) * nsplit + split) * (2 + dim) + 2 + vo[j]] = o[j];
+      }
+    }
   }
-  if (threadIdx.x == 0) {
-    w[0] = bc[0];
-    w[1] = bc[1];
-  }
-  // the last CTA of this head combines the splits
+  // the last CTA of this (token, kv head) combines the splits
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) last_s = atomicAdd(&a.counters[th], 1u) == (unsigned)(used - 1);
+  unsigned* counter = a.counters + (size_t)tok * a.kv_heads + kvh;
+  if (threadIdx.x == 0) last_s = atomicAdd(counter, 1u) == (unsigned)(used - 1);
   __syncthreads();
   if (!last_s) return;
   __threadfence();
   // partials of other CTAs are read past L1 (__ldcg)
-  const float* wh = a.ws + th * nsplit * (2 + dim);
   const size_t stride = 2 + (size_t)dim;
-  if (warp == 0) {
+  for (int g = warp; g < G; g += kAttnThreads / 32) {
+    const float* wh = a.ws + (h0 + g) * nsplit * stride;
+    float* cw = cw_s + g * nsplit;
     float m = -INFINITY;
     for (int i = lane; i < used; i += 32) m = fmaxf(m, __ldcg(wh + i * stride));
 #pragma unroll
@@ -304,21 +525,48 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
     float l = 0.f;
     for (int i = lane; i < used; i += 32) {
       const float c = expf(__ldcg(wh + i * stride) - m);
-      cw_s[i] = c;
+      cw[i] = c;
       l = fmaf(__ldcg(wh + i * stride + 1), c, l);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    if (lane == 0) bc[1] = 1.0f / l;
+    if (lane == 0) inv_s[g] = 1.0f / l;
   }
   __syncthreads();
-  const float inv = bc[1];
-  for (int d = threadIdx.x; d < dim; d += kAttnThreads) {
-    float o = 0.f;
-    for (int i = 0; i < used; ++i) o = fmaf(__ldcg(wh + i * stride + 2 + d), cw_s[i], o);
-    a.out[th * dim + d] = o * inv;
+  // four outputs per thread, their partials loaded eight splits at a time
+  // (independent loads in flight), accumulated in split order
+  for (int t0 = threadIdx.x; t0 < outs; t0 += 4 * kAttnThreads) {
+    const float* src[4];
+    const float* cw[4];
+    float o[4];
+    int gk[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int t = min(t0 + k * kAttnThreads, outs - 1);
+      gk[k] = t / dim;
+      src[k] = a.ws + (h0 + gk[k]) * nsplit * stride + 2 + (t - gk[k] * dim);
+      cw[k] = cw_s + gk[k] * nsplit;
+      o[k] = 0.f;
+    }
+    for (int i0 = 0; i0 < used; i0 += 8) {
+      float v[4][8];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[k][j] = i0 + j < used ? __ldcg(src[k] + (size_t)(i0 + j) * stride) : 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (i0 + j < used) o[k] = fmaf(v[k][j], cw[k][i0 + j], o[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int t = t0 + k * kAttnThreads;
+      if (t < outs) a.out[(h0 + gk[k]) * dim + (t - gk[k] * dim)] = o[k] * inv_s[gk[k]];
+    }
   }
-  if (threadIdx.x == 0) a.counters[th] = 0;  // ready for the next call
+  if (threadIdx.x == 0) *counter = 0;  // ready for the next call
 }
 
 __global__ void __launch_bounds__(256) add_kernel(float* __restrict__ dst, const float* __restrict__ src, int64_t n) {
@@ -337,17 +585,22 @@ __global__ void __launch_bounds__(256) add_rms_norm_kernel(float* __restrict__ h
                                                             float* __restrict__ out) {
   grid_dependency_wait();
   allow_dependents_launch();
-  extern __shared__ float xs[];
+  extern __shared__ float xs[];  // [n] row, [n] weights
+  float* wsm = xs + n;
   const size_t r = (size_t)blockIdx.x * n;  // one CTA per row
   hidden += r;
   delta += r;
   out += r;
-#pragma unroll 4
-  for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = __fadd_rn(hidden[i], delta[i]);
+#pragma unroll 8
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float h = hidden[i], d = delta[i], wi = w[i];
+    xs[i] = __fadd_rn(h, d);
+    wsm[i] = wi;
+  }
   __syncthreads();
   for (int i = threadIdx.x; i < n; i += blockDim.x) hidden[i] = xs[i];
   const float scale = staged_rms_scale(xs, n, eps);
-  for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(xs[i], scale), w[i]);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(xs[i], scale), wsm[i]);
 }
 
 // Greedy token (generation.rs:281-290): the first index of the largest value
@@ -399,6 +652,35 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __r
   }
 }
 
+// Greedy tokens of `rows` independent sequences (generation.rs:281-290 per
+// row): one CTA per row, the first index of the largest value (NaN never
+// wins, all-NaN gives 0); token[r] and pos[r] += 1.
+__global__ void __launch_bounds__(1024) argmax_rows_kernel(const float* __restrict__ x, int n, int32_t* token,
+                                                           int32_t* pos) {
+  grid_dependency_wait();
+  allow_dependents_launch();
+  const float* xr = x + (size_t)blockIdx.x * n;
+  unsigned long long best = 0ull;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const unsigned long long k = argmax_key(xr[i], (unsigned)i);
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
+    best = k > best ? k : best;
+  }
+  __shared__ unsigned long long wb[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) wb[warp] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = wb[w] > best ? wb[w] : best;
+    token[blockIdx.x] = best ? (int32_t)(0xffffffffu - (unsigned)(best & 0xffffffffull)) : 0;
+    if (pos) pos[blockIdx.x] += 1;
+  }
+}
+
 }  // namespace model
 }  // namespace hyq
 
@@ -429,7 +711,7 @@ int hyq_rms_norm(const float* x, const float* w, int64_t n, int64_t rows, float 
   if (n > hyq::model::kNormMaxN) return hyq::api_fail(HYQ_E_SHAPE, "rms_norm: at most %d columns", hyq::model::kNormMaxN);
   hyq::model::norm_smem_limit(hyq::model::rms_norm_kernel);
   const cudaError_t e =
-      hyq::model::launch(hyq::model::rms_norm_kernel, dim3((unsigned)rows), dim3(256), (size_t)n * sizeof(float),
+      hyq::model::launch(hyq::model::rms_norm_kernel, dim3((unsigned)rows), dim3(256), 2 * (size_t)n * sizeof(float),
                          (cudaStream_t)stream, x, w, (int)n, eps, out);
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "rms_norm: %s", cudaGetErrorString(e));
 }
@@ -463,9 +745,10 @@ int hyq_embed(const hyq_weight* w, const int32_t* token, int64_t count, float* o
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "embed: %s", cudaGetErrorString(e));
 }
 
-int hyq_rope_qk(float* q, float* k, const float* v, int heads, int kv_heads, int head_dim, const float* cos_tab,
-                const float* sin_tab, int64_t positions, const int32_t* pos, int64_t tokens, const float* q_norm,
-                const float* k_norm, float eps, int norm_first, float* k_cache, float* v_cache, void* stream) {
+static int rope_qk_impl(float* q, float* k, const float* v, int heads, int kv_heads, int head_dim,
+                        const float* cos_tab, const float* sin_tab, int64_t positions, const int32_t* pos,
+                        int64_t tokens, const float* q_norm, const float* k_norm, float eps, int norm_first,
+                        float* k_cache, float* v_cache, int64_t seq_stride, void* stream) {
   if (!q || !k || !v || !cos_tab || !sin_tab || !pos || !k_cache || !v_cache)
     return hyq::api_fail(HYQ_E_INVALID, "rope_qk: null pointer");
   if (heads <= 0 || kv_heads <= 0 || heads % kv_heads || head_dim <= 0 || (head_dim & 1) || positions <= 0 ||
@@ -488,6 +771,7 @@ int hyq_rope_qk(float* q, float* k, const float* v, int heads, int kv_heads, int
   a.norm_first = norm_first;
   a.k_cache = k_cache;
   a.v_cache = v_cache;
+  a.seq_stride = seq_stride;
   int rc = hyq::api_status_word(&a.status);
   if (rc) return rc;
   if (tokens <= 0 || tokens > 65535 || tokens > positions)
@@ -495,6 +779,23 @@ int hyq_rope_qk(float* q, float* k, const float* v, int heads, int kv_heads, int
   const cudaError_t e = hyq::model::launch(hyq::model::rope_qk_kernel, dim3((unsigned)(heads + kv_heads),
                                            (unsigned)tokens), dim3(32), 0, (cudaStream_t)stream, a);
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "rope_qk: %s", cudaGetErrorString(e));
+}
+
+int hyq_rope_qk(float* q, float* k, const float* v, int heads, int kv_heads, int head_dim, const float* cos_tab,
+                const float* sin_tab, int64_t positions, const int32_t* pos, int64_t tokens, const float* q_norm,
+                const float* k_norm, float eps, int norm_first, float* k_cache, float* v_cache, void* stream) {
+  return rope_qk_impl(q, k, v, heads, kv_heads, head_dim, cos_tab, sin_tab, positions, pos, tokens, q_norm, k_norm,
+                      eps, norm_first, k_cache, v_cache, 0, stream);
+}
+
+int hyq_rope_qk_seqs(float* q, float* k, const float* v, int heads, int kv_heads, int head_dim, const float* cos_tab,
+                     const float* sin_tab, int64_t positions, const int32_t* pos, int64_t seqs, const float* q_norm,
+                     const float* k_norm, float eps, int norm_first, float* k_cache, float* v_cache,
+                     int64_t seq_stride, void* stream) {
+  if (seq_stride < positions * kv_heads * head_dim)
+    return hyq::api_fail(HYQ_E_SHAPE, "rope_qk_seqs: sequences' caches overlap (stride %lld)", (long long)seq_stride);
+  return rope_qk_impl(q, k, v, heads, kv_heads, head_dim, cos_tab, sin_tab, positions, pos, seqs, q_norm, k_norm,
+                      eps, norm_first, k_cache, v_cache, seq_stride, stream);
 }
 
 int hyq_attention_workspace_bytes(int heads, int head_dim, int64_t positions, int64_t tokens, size_t* bytes) {
@@ -509,15 +810,17 @@ int hyq_attention_workspace_bytes(int heads, int head_dim, int64_t positions, in
   return HYQ_OK;
 }
 
-int hyq_attention(const float* q, const float* k_cache, const float* v_cache, int heads, int kv_heads,
-                  int head_dim, int64_t positions, const int32_t* pos, int64_t tokens, float* out, void* workspace,
-                  void* stream) {
+static int attention_impl(const float* q, const float* k_cache, const float* v_cache, int heads, int kv_heads,
+                          int head_dim, int64_t positions, const int32_t* pos, int64_t tokens, float* out,
+                          void* workspace, int64_t seq_stride, void* stream) {
   if (!q || !k_cache || !v_cache || !pos || !out || !workspace)
     return hyq::api_fail(HYQ_E_INVALID, "attention: null pointer");
-  if (heads <= 0 || kv_heads <= 0 || heads % kv_heads || head_dim <= 0 || head_dim > hyq::model::kAttnMaxDim ||
-      positions <= 0 || positions > hyq::model::kMaxPositions)
-    return hyq::api_fail(HYQ_E_SHAPE, "attention: shape (head_dim at most %d, at most %d positions)",
-                         hyq::model::kAttnMaxDim, hyq::model::kMaxPositions);
+  if (heads <= 0 || kv_heads <= 0 || heads % kv_heads || heads / kv_heads > hyq::model::kAttnMaxGroup ||
+      head_dim <= 0 || head_dim > hyq::model::kAttnMaxDim || positions <= 0 || positions > hyq::model::kMaxPositions)
+    return hyq::api_fail(HYQ_E_SHAPE,
+                         "attention: shape (head_dim at most %d, at most %d query heads per kv head, at most %d "
+                         "positions)",
+                         hyq::model::kAttnMaxDim, hyq::model::kAttnMaxGroup, hyq::model::kMaxPositions);
   if (reinterpret_cast<uintptr_t>(workspace) % 16) return hyq::api_fail(HYQ_E_INVALID, "attention: workspace alignment");
   hyq::model::AttnArgs a{};
   a.q = q;
@@ -530,15 +833,56 @@ int hyq_attention(const float* q, const float* k_cache, const float* v_cache, in
   a.positions = (int)positions;
   a.out = out;
   a.counters = static_cast<unsigned*>(workspace);
+  a.seq_stride = seq_stride;
   if (tokens <= 0 || tokens > 65535 || tokens > positions)
     return hyq::api_fail(HYQ_E_SHAPE, "attention: 1 to %d tokens", (int)(positions < 65535 ? positions : 65535));
   a.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + hyq::model::attn_counter_bytes(positions * heads));
   int rc = hyq::api_status_word(&a.status);
   if (rc) return rc;
   const unsigned splits = (unsigned)((positions + hyq::model::kAttnChunk - 1) / hyq::model::kAttnChunk);
-  const cudaError_t e = hyq::model::launch(hyq::model::attention_kernel, dim3(splits, (unsigned)heads, (unsigned)tokens),
-                                           dim3(hyq::model::kAttnThreads), 0, (cudaStream_t)stream, a);
+  const size_t smem = hyq::model::attn_smem_bytes(head_dim, heads / kv_heads, (int)splits);
+  // head size 128 with 4 query heads per kv head (the Dense and 7B shapes)
+  // over 16-byte aligned caches: the specialised kernel
+  const bool fixed = head_dim == 128 && heads == 4 * kv_heads &&
+                     ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15) == 0 &&
+                     (seq_stride & 3) == 0;
+  auto kern = fixed ? hyq::model::attention_kernel<128, 4> : hyq::model::attention_kernel<0, 0>;
+  static int smem_dev[2] = {-1, -1};  // the largest shape's shared memory, allowed once per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (smem_dev[fixed] != dev) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)hyq::model::attn_smem_bytes(hyq::model::kAttnMaxDim, hyq::model::kAttnMaxGroup,
+                                                          hyq::model::kMaxPositions / hyq::model::kAttnChunk));
+    smem_dev[fixed] = dev;
+  }
+  const cudaError_t e = hyq::model::launch(kern, dim3(splits, (unsigned)kv_heads, (unsigned)tokens),
+                                           dim3(hyq::model::kAttnThreads), smem, (cudaStream_t)stream, a);
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "attention: %s", cudaGetErrorString(e));
+}
+
+int hyq_attention(const float* q, const float* k_cache, const float* v_cache, int heads, int kv_heads,
+                  int head_dim, int64_t positions, const int32_t* pos, int64_t tokens, float* out, void* workspace,
+                  void* stream) {
+  return attention_impl(q, k_cache, v_cache, heads, kv_heads, head_dim, positions, pos, tokens, out, workspace, 0,
+                        stream);
+}
+
+int hyq_attention_seqs(const float* q, const float* k_cache, const float* v_cache, int heads, int kv_heads,
+                       int head_dim, int64_t positions, const int32_t* pos, int64_t seqs, int64_t seq_stride,
+                       float* out, void* workspace, void* stream) {
+  if (seq_stride < positions * kv_heads * head_dim)
+    return hyq::api_fail(HYQ_E_SHAPE, "attention_seqs: sequences' caches overlap (stride %lld)", (long long)seq_stride);
+  return attention_impl(q, k_cache, v_cache, heads, kv_heads, head_dim, positions, pos, seqs, out, workspace,
+                        seq_stride, stream);
+}
+
+int hyq_argmax_rows(const float* x, int64_t n, int64_t rows, int32_t* token, int32_t* pos, void* stream) {
+  if (!x || !token) return hyq::api_fail(HYQ_E_INVALID, "argmax_rows: null pointer");
+  if (n <= 0 || n > INT32_MAX || rows <= 0 || rows > INT32_MAX) return hyq::api_fail(HYQ_E_SHAPE, "argmax_rows: shape");
+  const cudaError_t e = hyq::model::launch(hyq::model::argmax_rows_kernel, dim3((unsigned)rows), dim3(1024), 0,
+                                           (cudaStream_t)stream, x, (int)n, token, pos);
+  return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "argmax_rows: %s", cudaGetErrorString(e));
 }
 
 int hyq_add(float* dst, const float* src, int64_t n, void* stream) {
@@ -556,7 +900,7 @@ int hyq_add_rms_norm(float* hidden, const float* delta, const float* w, int64_t 
     return hyq::api_fail(HYQ_E_SHAPE, "add_rms_norm: 1 to %d columns", hyq::model::kNormMaxN);
   hyq::model::norm_smem_limit(hyq::model::add_rms_norm_kernel);
   const cudaError_t e = hyq::model::launch(hyq::model::add_rms_norm_kernel, dim3((unsigned)rows), dim3(256),
-                                           (size_t)n * sizeof(float), (cudaStream_t)stream, hidden, delta, w, (int)n,
+                                           2 * (size_t)n * sizeof(float), (cudaStream_t)stream, hidden, delta, w, (int)n,
                                            eps, out);
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "add_rms_norm: %s", cudaGetErrorString(e));
 }

@@ -218,17 +218,23 @@ class DenseModel:
     def _stream(self):
         return C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
 
-    def _enqueue(self, acts, tokens):
+    def _enqueue(self, acts, tokens, caches=None, pos=None, token_out=None, logits=None):
         """Forward of acts.M tokens (device int32 `tokens`) at positions
         *pos ..: the layers of model.rs:374-547 (M = 1) or of the batched
         forward model.rs:549-646 (M > 1, projections on the tensor cores),
-        then the lm_head of the last row and the greedy token; *pos += M."""
+        then the lm_head of the last row and the greedy token; *pos += M.
+        caches (per layer (k, v)), pos, token_out and logits default to the
+        model's own (one request)."""
         cfg, st, a, M = self.cfg, self._stream(), acts, acts.M
+        pos = self.pos if pos is None else pos
+        token_out = self.token if token_out is None else token_out
+        logits = self.logits if logits is None else logits
         H = cfg.hidden
         last = lambda t: C.c_void_p(t.data_ptr() + (M - 1) * t.stride(0) * t.element_size())  # noqa: E731
         check(lib.hyq_embed(self.embed.handle, _p(tokens), M, _p(a.hidden), st))
         check(lib.hyq_rms_norm(_p(a.hidden), _p(self.layers[0]["input_norm"]), H, M, cfg.eps, _p(a.normalized), st))
         for i, W in enumerate(self.layers):
+            kc, vc = (W["k_cache"], W["v_cache"]) if caches is None else caches[i]
             if M == 1:
                 check(lib.hyq_gemv_qkv(W["q"].handle, W["k"].handle, W["v"].handle, _p(a.normalized), _p(a.q),
                                        _p(a.k), _p(a.v), st))
@@ -236,11 +242,10 @@ class DenseModel:
                 check(lib.hyq_matmul_qkv(W["q"].handle, W["k"].handle, W["v"].handle, _p(a.normalized), M, _p(a.q),
                                          _p(a.k), _p(a.v), st))
             check(lib.hyq_rope_qk(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim, _p(self.cos),
-                                  _p(self.sin), cfg.positions, _p(self.pos), M, _p(W["q_norm"]), _p(W["k_norm"]),
-                                  cfg.eps, 0, _p(W["k_cache"]), _p(W["v_cache"]), st))
-            check(lib.hyq_attention(_p(a.q), _p(W["k_cache"]), _p(W["v_cache"]), cfg.heads, cfg.kv_heads,
-                                    cfg.head_dim, cfg.positions, _p(self.pos), M, _p(a.attended), _p(self.attn_ws),
-                                    st))
+                                  _p(self.sin), cfg.positions, _p(pos), M, _p(W["q_norm"]), _p(W["k_norm"]),
+                                  cfg.eps, 0, _p(kc), _p(vc), st))
+            check(lib.hyq_attention(_p(a.q), _p(kc), _p(vc), cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.positions,
+                                    _p(pos), M, _p(a.attended), _p(self.attn_ws), st))
             check(lib.hyq_matmul(W["o"].handle, _p(a.attended), M, _p(a.projected), st))
             # residual add fused with the norm that follows it
             check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.projected), _p(W["ffn_norm"]), H, M, cfg.eps,
@@ -255,8 +260,8 @@ class DenseModel:
             nxt = self.layers[i + 1]["input_norm"] if i + 1 < len(self.layers) else self.output_norm
             check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.ff), _p(nxt), H, M, cfg.eps, _p(a.normalized), st))
         # logits of the last token only (model.rs:619-622)
-        check(lib.hyq_matmul(self.output.handle, last(a.normalized), 1, _p(self.logits), st))
-        check(lib.hyq_argmax(_p(self.logits), cfg.vocab, _p(self.token), _p(self.pos), M, _p(self.argmax_ws), st))
+        check(lib.hyq_matmul(self.output.handle, last(a.normalized), 1, _p(logits), st))
+        check(lib.hyq_argmax(_p(logits), cfg.vocab, _p(token_out), _p(pos), M, _p(self.argmax_ws), st))
 
     def enqueue_step(self):
         """One token: reads self.token / self.pos, leaves the logits, the next
@@ -266,17 +271,18 @@ class DenseModel:
         else:
             self._enqueue(self.one, self.token)
 
-    def prefill(self, ids):
+    def prefill(self, ids, **targets):
         """Feed a prompt chunk of at most self.chunk tokens (a device int32
         tensor) in one batched forward; leaves the logits of its last token,
-        the next greedy token in self.token and pos += len(ids)."""
+        the next greedy token in self.token and pos += len(ids) (or in the
+        caches / pos / token_out / logits given)."""
         M = int(ids.numel())
         if not 0 < M <= self.chunk:
             raise ValueError(f"prefill takes 1..{self.chunk} tokens")
         acts = self._prefill_acts.get(M)
         if acts is None:
             acts = self._prefill_acts[M] = _Acts(self.cfg, M, self.device)
-        self._enqueue(acts, ids)
+        self._enqueue(acts, ids, **targets)
 
     # kernel launches of one enqueue_step
     def launches(self):
@@ -331,3 +337,117 @@ class DenseModel:
                     self.graph.replay()
         stream.synchronize()
         return out.cpu().tolist()
+
+
+class DenseBatch:
+    """Concurrent greedy decoding of `batch` independent requests with one
+    model: each step runs model.rs:374-547 for one token of every request,
+    the projections as [batch, K] products (on the tensor cores from 16
+    requests), RoPE, KV append and attention per request over its own cache
+    (hyq_rope_qk_seqs, hyq_attention_seqs), and a greedy token per request
+    (hyq_argmax_rows).  Prompts are fed per request with the batched
+    forward, into that request's cache slice."""
+
+    def __init__(self, model, batch):
+        cfg, dev = model.cfg, model.device
+        if batch > cfg.positions:
+            raise ValueError("at most `positions` concurrent requests")
+        self.m, self.B = model, batch
+        KV = cfg.kv_heads * cfg.head_dim
+        self.caches = [(torch.zeros(batch, cfg.positions, KV, device=dev),
+                        torch.zeros(batch, cfg.positions, KV, device=dev)) for _ in model.layers]
+        self.stride = cfg.positions * KV
+        self.acts = _Acts(cfg, batch, dev)
+        self.logits = torch.zeros(batch, cfg.vocab, device=dev)
+        self.tokens = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(batch, dtype=torch.int32, device=dev)
+        ws = C.c_size_t()
+        check(lib.hyq_attention_workspace_bytes(cfg.heads, cfg.head_dim, cfg.positions, batch, C.byref(ws)))
+        self.attn_ws = torch.zeros(ws.value, dtype=torch.uint8, device=dev)
+        self.graph = None
+
+    def enqueue_step(self):
+        m, cfg, a, B = self.m, self.m.cfg, self.acts, self.B
+        st, H = m._stream(), cfg.hidden
+        check(lib.hyq_embed(m.embed.handle, _p(self.tokens), B, _p(a.hidden), st))
+        check(lib.hyq_rms_norm(_p(a.hidden), _p(m.layers[0]["input_norm"]), H, B, cfg.eps, _p(a.normalized), st))
+        for i, W in enumerate(m.layers):
+            kc, vc = self.caches[i]
+            check(lib.hyq_matmul_qkv(W["q"].handle, W["k"].handle, W["v"].handle, _p(a.normalized), B, _p(a.q),
+                                     _p(a.k), _p(a.v), st))
+            check(lib.hyq_rope_qk_seqs(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim,
+                                       _p(m.cos), _p(m.sin), cfg.positions, _p(self.pos), B, _p(W["q_norm"]),
+                                       _p(W["k_norm"]), cfg.eps, 0, _p(kc), _p(vc), self.stride, st))
+            check(lib.hyq_attention_seqs(_p(a.q), _p(kc), _p(vc), cfg.heads, cfg.kv_heads, cfg.head_dim,
+                                         cfg.positions, _p(self.pos), B, self.stride, _p(a.attended),
+                                         _p(self.attn_ws), st))
+            check(lib.hyq_matmul(W["o"].handle, _p(a.attended), B, _p(a.projected), st))
+            check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.projected), _p(W["ffn_norm"]), H, B, cfg.eps,
+                                       _p(a.normalized), st))
+            check(lib.hyq_matmul_gate_up_silu_batch(W["gate"].handle, W["up"].handle, _p(a.normalized), B,
+                                                    _p(a.gate), st))
+            check(lib.hyq_matmul(W["down"].handle, _p(a.gate), B, _p(a.ff), st))
+            nxt = m.layers[i + 1]["input_norm"] if i + 1 < len(m.layers) else m.output_norm
+            check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.ff), _p(nxt), H, B, cfg.eps, _p(a.normalized), st))
+        check(lib.hyq_matmul(m.output.handle, _p(a.normalized), B, _p(self.logits), st))
+        check(lib.hyq_argmax_rows(_p(self.logits), cfg.vocab, B, _p(self.tokens), _p(self.pos), st))
+
+    def launches(self):
+        """Kernel launches of one step: QKV / O / gate-up / down / lm_head as
+        batched products (2 launches each on the tensor cores from 16
+        requests: activation conversion + GEMM)."""
+        per_product = 2 if self.B >= 16 else self.B
+        return 2 + self.m.cfg.layers * (4 + 4 * per_product) + per_product + 1
+
+    def capture(self, stream):
+        quant.set_launch_overlap(True)
+        with torch.cuda.stream(stream):
+            saved = (self.tokens.clone(), self.pos.clone())
+            self.enqueue_step()  # warm every path outside the capture
+            stream.synchronize()
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph, stream=stream):
+                self.enqueue_step()
+            self.tokens.copy_(saved[0])
+            self.pos.copy_(saved[1])
+        return self.graph
+
+    def reset(self):
+        self.pos.zero_()
+        for k, v in self.caches:
+            k.zero_()
+            v.zero_()
+
+    def prefill_all(self, prompts):
+        """Feed each request's prompt (batched forwards into its cache
+        slice); leaves each request's first generated token in self.tokens."""
+        m = self.m
+        ids = [torch.tensor(p, dtype=torch.int32).to(m.device) for p in prompts]
+        for b, t in enumerate(ids):
+            caches = [(k[b], v[b]) for k, v in self.caches]
+            for c0 in range(0, t.numel(), m.chunk):
+                m.prefill(t[c0:c0 + m.chunk], caches=caches, pos=self.pos[b:b + 1],
+                          token_out=self.tokens[b:b + 1], logits=self.logits[b])
+
+    def generate(self, prompts, n_new, stream, logits_out=None):
+        """Greedy decode of len(prompts) == batch requests: per request the
+        n_new generated ids (and logits_out[i, b] the logits that chose
+        request b's token i)."""
+        if len(prompts) != self.B:
+            raise ValueError("one prompt per request")
+        if max(len(p) for p in prompts) + n_new > self.m.cfg.positions:
+            raise ValueError("prompt + generated tokens exceed the KV-cache capacity")
+        out = torch.empty(n_new, self.B, dtype=torch.int32, device=self.m.device)
+        with torch.cuda.stream(stream):
+            if self.graph is None:
+                self.capture(stream)   # its warm-up step writes logits and caches: before the prompts
+            self.reset()
+            self.prefill_all(prompts)
+            for i in range(n_new):
+                out[i].copy_(self.tokens)
+                if logits_out is not None:
+                    logits_out[i].copy_(self.logits)
+                if i < n_new - 1:
+                    self.graph.replay()
+        stream.synchronize()
+        return out.t().cpu().tolist()

@@ -8,12 +8,18 @@ tied Q6_K embedding), captures one token step as a CUDA graph, feeds
 `--prompt` tokens and then `--steps` greedy steps, one graph replay each.
 Every replay launches the same kernels in the same order (a launch list of
 one replay is one token step).
+
+    python -m hy_mt_rs_b200.profile_model --batch 64 --prompt 256 --steps 3
+
+With --batch B: B concurrent requests (DenseBatch), every request starting
+at position --prompt over zero caches (the step's work depends on the
+positions only, so no prompt is fed), then --steps replays of the batch step.
 """
 import argparse
 
 import torch
 
-from .model import DenseConfig, DenseModel, random_weights
+from .model import DenseBatch, DenseConfig, DenseModel, random_weights
 
 
 def main():
@@ -21,12 +27,23 @@ def main():
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--prompt", type=int, default=8)
     ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--batch", type=int, default=0)
     a = ap.parse_args()
     dev = torch.device("cuda", 0)
     cfg = DenseConfig(layers=a.layers, positions=a.prompt + a.steps + 1)
     model = DenseModel(cfg, random_weights(cfg, dev, seed=1), dev)
     torch.cuda.synchronize()
     stream = torch.cuda.Stream(dev)
+    if a.batch:
+        batch = DenseBatch(model, a.batch)
+        batch.capture(stream)
+        with torch.cuda.stream(stream):
+            batch.pos.fill_(a.prompt)
+            for _ in range(a.steps):
+                batch.graph.replay()
+        stream.synchronize()
+        print("tokens", batch.tokens.cpu().tolist())
+        return
     ids = model.generate(list(range(1, a.prompt + 1)), a.steps, stream)
     print("tokens", ids)
 

@@ -270,6 +270,22 @@ int hyq_attention(const float* q, const float* k_cache, const float* v_cache, in
                   int head_dim, int64_t positions, const int32_t* pos, int64_t tokens, float* out, void* workspace,
                   void* stream);
 
+/* The same for `seqs` independent sequences decoding one token each
+ * (concurrent requests): token t is sequence t at position pos[t] (device
+ * int32 [seqs]) with its caches at k_cache/v_cache + t * seq_stride floats
+ * (seq_stride >= positions * kv_heads * head_dim); seqs <= positions.  The
+ * attention workspace is hyq_attention_workspace_bytes(..., positions, seqs). */
+int hyq_rope_qk_seqs(float* q, float* k, const float* v, int heads, int kv_heads, int head_dim, const float* cos_tab,
+                     const float* sin_tab, int64_t positions, const int32_t* pos, int64_t seqs, const float* q_norm,
+                     const float* k_norm, float eps, int norm_first, float* k_cache, float* v_cache,
+                     int64_t seq_stride, void* stream);
+int hyq_attention_seqs(const float* q, const float* k_cache, const float* v_cache, int heads, int kv_heads,
+                       int head_dim, int64_t positions, const int32_t* pos, int64_t seqs, int64_t seq_stride,
+                       float* out, void* workspace, void* stream);
+/* Greedy token of each of `rows` rows of n logits (generation.rs:281-290):
+ * token[r]; pos[r] += 1 when pos is not NULL. */
+int hyq_argmax_rows(const float* x, int64_t n, int64_t rows, int32_t* token, int32_t* pos, void* stream);
+
 /* add (model.rs:1043-1071): dst += src. */
 int hyq_add(float* dst, const float* src, int64_t n, void* stream);
 

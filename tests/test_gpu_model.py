@@ -48,17 +48,25 @@ def test_dense_decode_matches_oracle(cuda):
     assert again == ids
 
 
-@pytest.mark.parametrize("pos", [0, 63, 64, 777, 4095])
-def test_attention_splits_match_oracle(cuda, pos):
+ATTN_SHAPES = [(16, 4, 128)] * 5 + [(8, 4, 64), (12, 4, 96), (6, 2, 40), (4, 4, 128)] * 3
+ATTN_POS = [0, 63, 64, 777, 4095] + [0, 64, 777] * 4
+
+
+@pytest.mark.parametrize("shape,pos", list(zip(ATTN_SHAPES, ATTN_POS)))
+def test_attention_splits_match_oracle(cuda, shape, pos):
     """hyq_attention over 64-position splits (one to 64 of them) against the
     oracle's single-pass softmax (model.rs:949-1021); two calls in a row on
-    the same workspace, so the per-head counters are seen to reset."""
+    the same workspace, so the per-head counters are seen to reset.  Head
+    size 128 with 4 query heads per kv head takes the specialised kernel; the
+    other shapes the general one (paired or per-thread scores, grouped or
+    per-dim value sums)."""
     import ctypes as C
     import torch
     from hy_mt_rs_b200._native import check, lib
     from oracle import oracle as O
 
-    heads, kv_heads, dim, positions = 16, 4, 128, 4096
+    heads, kv_heads, dim = shape
+    positions = 4096
     g = torch.Generator().manual_seed(pos)
     q = torch.randn(heads * dim, generator=g)
     kc = torch.randn(positions, kv_heads * dim, generator=g)
