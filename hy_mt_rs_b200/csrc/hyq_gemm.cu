@@ -5,7 +5,7 @@
 // src/quant.rs:272-343): Y[batch, N] = X[batch, K] . W^T, where the reference
 // decodes 64-row tiles to f32 and multiplies them with Candle's CPU GEMM.
 //
-// Tile: 128 weight rows (the MMA's M) x BN tokens (the MMA's N, 128 or 256)
+// Tile: 128 weight rows (the MMA's M) x BN tokens (the MMA's N: 64, 128 or 256)
 // x K, with D = W_tile . X_tile^T accumulated in f32 in tensor memory.
 // The decoded weights (operand A) never touch shared memory: each dequant
 // thread owns one weight row = one TMEM lane and stores its fp16 pairs with
@@ -21,11 +21,14 @@
 //             (SWIZZLE_128B);
 //   warp 1  : allocates TMEM and issues tcgen05.mma (one elected thread),
 //             releasing each stage with tcgen05.commit;
-//   warps 2-9: two groups of 4 warps taking alternate K steps; warp w serves
+//   warps 2-17: four groups of 4 warps taking K steps in turn; warp w serves
 //             TMEM lanes 32*(w%4).. (its rows), decodes the packed block
 //             column into the fp16 A stage in tensor memory, waits for the
-//             stores and signals the stage; warps 2-5 also run the epilogue
-//             (tcgen05.ld -> f32 stores of Y).
+//             stores and signals the stage (four steps' stores in flight
+//             hide their latency); all of them then run the epilogue
+//             (tcgen05.ld -> f32 stores of Y), a quarter of the columns per
+//             group.
+// (The 2-SM variant below keeps two groups: warps 2-9.)
 // Tensor memory (512 columns): accumulator in columns [0, BN), A stage s in
 // columns [BN + 32 s, BN + 32 s + 32) (128 lanes x 64 fp16).
 // Operands are fp16 (both), accumulation f32.  Weights are decoded with fp16
@@ -50,14 +53,30 @@ namespace gemm {
 constexpr int BM = 128;          // weight rows per tile (MMA M)
 constexpr int BK = 64;           // K per stage: one 128-byte swizzle row of fp16
 constexpr int WS = 2;            // packed weight block-column stages
-constexpr int kDequantWarps = 8;   // two groups of 4 warps; each group takes every other K step
+constexpr int kDequantWarps = 8;   // 2-SM kernel: two groups of 4 warps; each group takes every other K step
 constexpr int kGroupWarps = 4;     // one thread per weight row, 64 weights per step
 constexpr int kThreads = (2 + kDequantWarps) * 32;
+constexpr int kGroups = 4;         // 1-SM kernel: dequant groups taking K steps in turn
+constexpr int kThreads1 = (2 + kGroups * kGroupWarps) * 32;
 constexpr int kTmemCols = 512;
 
 // Activation / decoded-weight stages for a BN-token tile (shared memory
 // holds S activation tiles and two packed block columns).
 __host__ __device__ constexpr int stages_for(int bn) { return bn == 256 ? 5 : 8; }
+
+// Token tile (the MMA's N) for products of m activation rows (per expert in
+// expert mode): a 64-token tile for at most 64 rows, so that small batches
+// do not spend tensor-core time on zero-filled rows.
+inline int token_tile(int64_t m) { return m >= 256 ? 256 : m > 64 ? 128 : 64; }
+
+// K columns of one packed block column (the unit of a weight TMA load) and
+// its packed bytes per row.
+__host__ __device__ constexpr int wcol_for(int fmt) {
+  return fmt == Q8_0 ? 128 : fmt == Q2_0C ? 512 : 256;
+}
+__host__ __device__ constexpr int wbytes_for(int fmt) {
+  return fmt == Q4_K ? 144 : fmt == Q6_K ? 210 : fmt == Q8_0 ? 136 : fmt == Q2_0C ? 130 : 42;
+}
 
 // Bytes per row of the packed block-column tile (TMA box inner size).
 // (the 16-byte aligned window around one block column: packed bytes + skew)
@@ -117,6 +136,10 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       "[%4];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
       : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -400,7 +423,7 @@ __device__ __forceinline__ void decode64(uint32_t row, int j4, uint32_t (&o)[32]
 }
 
 template <int FMT, int BN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads1, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_constant__ CUtensorMap tmap_w1,
                 const __grid_constant__ CUtensorMap tmap_w2, const __grid_constant__ CUtensorMap tmap_x,
                 const __grid_constant__ Params p) {
@@ -423,6 +446,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base_g + L::misc + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 32) {
+    // the descriptors are kernel parameters: fetch them during the set-up
+    prefetch_tmap(&tmap_x);
+    prefetch_tmap(&tmap_w0);
+    if (p.n_seg > 1 || p.gate_up) prefetch_tmap(&tmap_w1);
+    if (p.n_seg > 2) prefetch_tmap(&tmap_w2);
+  }
   if (p.expert_off) grid_dependency_wait();  // the expert offsets come from the previous grid
   int tok0 = blockIdx.y * BN;
   int tok_end = p.M;  // activation rows of this tile end here
@@ -441,7 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     row0 = ((int)blockIdx.x % p.expert_tiles) * tile_rows;
     wrow0 = e * p.expert_rows + row0;
   }
-  const int steps_per_w = p.wcol / BK;
+  constexpr int steps_per_w = wcol_for(FMT) / BK;  // p.wcol
   // split-K slice of this CTA: K steps [kbeg, kbeg + nk)
   const int kbeg = blockIdx.z * p.steps_per_split;
   const int nk_all = p.K / BK;
@@ -455,7 +485,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < WS; ++s) {
       mbar_init(wfull(s), 1);
-      mbar_init(wempty(s), kDequantWarps);
+      // every group with a K step in the block column releases it
+      mbar_init(wempty(s), min(kGroups, p.wcol / BK) * kGroupWarps);
     }
     mbar_init(accfull, 1);
     *abort_flag = 0;
@@ -552,15 +583,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // --------------------------- dequant + epilogue ---------------------------
-    const int grp = (warp - 2) / kGroupWarps;           // 0: even K steps, 1: odd
+    const int grp = (warp - 2) / kGroupWarps;  // K steps grp, grp + kGroups, ...
     // A warp reaches only TMEM lanes 32*(warp%4)..+31: those are its rows.
     const int r = (warp & 3) * 32 + lane;  // weight row of the tile = TMEM lane
     const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
-    for (int ks = grp; ks < nk; ks += 2) {
-      const int wb = ks / steps_per_w, ws = wb % WS;
+    // TMEM lane r holds row rl of matrix mt (gate/up: lanes 16..31 of each
+    // quarter are the up rows); that row is row rl / g of row class rl % g
+    // in shared memory, its bytes `skew` into the class's aligned window.
+    constexpr int kSpw = steps_per_w;  // K steps per block column
+    const int gsh = p.g == 1 ? 0 : p.g == 2 ? 1 : p.g == 4 ? 2 : 3;  // g = 1, 2, 4 or 8
+    const int mt = p.gate_up ? ((r & 31) >> 4) : 0;
+    const int rl = p.gate_up ? 16 * (r >> 5) + (r & 15) : r;
+    const int jc = rl & (p.g - 1);
+    const uint32_t row_off = (uint32_t)((mt * tile_rows + jc * (tile_rows >> gsh) + (rl >> gsh)) * p.wbox);
+    const int64_t skew0 = (int64_t)jc * p.row_bytes;
+    const int64_t kb0 = kbeg / kSpw;  // split slices are whole block columns
+    for (int ks = grp; ks < nk; ks += kGroups) {
+      const int wb = ks / kSpw, ws = wb % WS;
       bool ok = true;
       // first step of this block column that this group handles
-      if (ks % steps_per_w == grp) ok = mbar_wait(wfull(ws), (wb / WS) & 1, abort_flag);
+      if (ks % kSpw < kGroups) ok = mbar_wait(wfull(ws), (wb / WS) & 1, abort_flag);
       const int s = ks % S;
       if (ok && ks >= S) ok = mbar_wait(empty(s), ((ks / S) - 1) & 1, abort_flag);
       if (!ok) {
@@ -569,18 +611,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();  // the MMAs that read this A stage are complete
-      // TMEM lane r holds row rl of matrix mt (gate/up: lanes 16..31 of each
-      // quarter are the up rows); that row is row rl / g of row class rl % g
-      // in shared memory, its bytes `skew` into the class's aligned window.
-      const int64_t kb = (kbeg + ks) / steps_per_w;
-      const int mt = p.gate_up ? ((r & 31) >> 4) : 0;
-      const int rl = p.gate_up ? 16 * (r >> 5) + (r & 15) : r;
-      const int jc = rl % p.g;
-      const int skew = (int)(((int64_t)jc * p.row_bytes + kb * p.wbytes) & 15);
-      const uint32_t rowp =
-          base + L::w + ws * L::w_stage + (mt * tile_rows + jc * (tile_rows / p.g) + rl / p.g) * p.wbox + skew;
+      const int skew = (int)((skew0 + (kb0 + wb) * wbytes_for(FMT)) & 15);
+      const uint32_t rowp = base + L::w + ws * L::w_stage + row_off + skew;
       uint32_t o[32];
-      decode64<FMT>(rowp, (kbeg + ks) % steps_per_w, o);
+      decode64<FMT>(rowp, ks % kSpw, o);
       tmem_st32(tmem + lane_base + (uint32_t)(BN + 32 * s), o);
       // Every writer waits for its tensor-memory stores and orders them
       // before the barrier; the warp then signals the stage once.
@@ -590,37 +624,52 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) {
         mbar_arrive(afull(s));
         // last step of this block column that this group handles
-        if (ks % steps_per_w >= steps_per_w - 2 || ks + 2 >= nk) mbar_arrive(wempty(ws));
+        if (ks % kSpw >= kSpw - kGroups || ks + kGroups >= nk) mbar_arrive(wempty(ws));
       }
     }
-    // Epilogue: all 8 dequant warps; warp w reads TMEM lanes 32*(w%4) ..
-    // +31, warps 2-5 the first half of the accumulator columns, warps 6-9
-    // the second.
+    // Epilogue: all dequant warps; warp w reads TMEM lanes 32*(w%4) .. +31,
+    // group g (warps 2 + 4g ..) the columns [g BN / kGroups, (g + 1) BN /
+    // kGroups), 32 at a time (two loads, one wait); columns past the tile's
+    // tokens are skipped.
     {
       const bool ok = mbar_wait(accfull, 0, nullptr);
       tc_fence_after();
       if (ok && !*abort_flag) {
         const int q = warp & 3;
-        const int cbeg = (warp < 6) ? 0 : BN / 2;
+        constexpr int kCols = BN / kGroups;
+        static_assert(kCols % 32 == 0 || kCols == 16, "16- or 32-column epilogue batches");
+        constexpr int kBatch = kCols < 32 ? 16 : 32;
+        const int cbeg = grp * kCols;
+        const int cend = min(cbeg + kCols, tok_end - tok0);
         const bool split = p.y != nullptr;
         const int rows_m = p.seg_rows[seg];
         float* yz = split ? p.y + (size_t)blockIdx.z * p.M * p.N : nullptr;
 #pragma unroll 1
-        for (int c0 = cbeg; c0 < cbeg + BN / 2; c0 += 16) {
-          uint32_t v[16];
+        for (int c0 = cbeg; c0 < cend; c0 += kBatch) {
+          uint32_t v[32];
+          const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0;
           asm volatile(
               "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
               "%14, %15}, [%16];"
               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
                 "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
                 "=r"(v[15])
-              : "r"(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0));
+              : "r"(ta));
+          if constexpr (kBatch == 32) {
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+                "%13, %14, %15}, [%16];"
+                : "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]),
+                  "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]),
+                  "=r"(v[30]), "=r"(v[31])
+                : "r"(ta + 16u));
+          }
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
           if (!p.gate_up) {
             const int row = row0 + 32 * q + lane;
             if (row < rows_m) {
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
+              for (int i = 0; i < kBatch; ++i) {
                 const int tok = tok0 + c0 + i;
                 if (tok >= tok_end) continue;
                 if (split) yz[(size_t)tok * p.N + p.seg_col0[seg] + row] = __uint_as_float(v[i]);
@@ -631,12 +680,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             // lanes 0..15: gate rows, lanes 16..31: the same up rows
             const int hi = lane >> 4;
             const int row = row0 + 16 * q + (lane & 15);
-            float u[16];
+            float u[kBatch];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) u[i] = __shfl_down_sync(0xffffffffu, __uint_as_float(v[i]), 16);
+            for (int i = 0; i < kBatch; ++i) u[i] = __shfl_down_sync(0xffffffffu, __uint_as_float(v[i]), 16);
             if (row < rows_m) {
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
+              for (int i = 0; i < kBatch; ++i) {
                 const int tok = tok0 + c0 + i;
                 if (tok >= tok_end) continue;
                 if (split) {
@@ -1019,11 +1068,14 @@ bool geometry(int dtype, int64_t K, int64_t N, int64_t row_bytes, Geometry& g) {
   g.rows = r == 0 ? 1 : (r % 8 == 0 ? 2 : (r % 4 == 0 ? 4 : 8));
   if (N % g.rows != 0) return false;
   switch (dtype) {
-    case Q4_K: g.wcol = 256; g.wbytes = 144; g.wbox = wbox_for(Q4_K); break;
-    case Q6_K: g.wcol = 256; g.wbytes = 210; g.wbox = wbox_for(Q6_K); break;
-    case Q8_0: g.wcol = 128; g.wbytes = 136; g.wbox = wbox_for(Q8_0); break;   // 4 blocks
-    case Q2_0C: g.wcol = 512; g.wbytes = 130; g.wbox = wbox_for(Q2_0C); break;
-    case STQ1_0: g.wcol = 256; g.wbytes = 42; g.wbox = wbox_for(STQ1_0); break;
+#define HYQ_GEOM(F) \
+  case F: g.wcol = wcol_for(F); g.wbytes = wbytes_for(F); g.wbox = wbox_for(F); break;
+    HYQ_GEOM(Q4_K)
+    HYQ_GEOM(Q6_K)
+    HYQ_GEOM(Q8_0)  // 4 blocks
+    HYQ_GEOM(Q2_0C)
+    HYQ_GEOM(STQ1_0)
+#undef HYQ_GEOM
     default: return false;
   }
   return K % g.wcol == 0;
@@ -1083,7 +1135,7 @@ cudaError_t run(const CUtensorMap* tw, const CUtensorMap& tx, const Params& p, i
   }
   // token tiles: of all M rows, or (expert mode) of the most rows one expert can have
   dim3 grid((unsigned)tiles, (unsigned)((max_rows + BN - 1) / BN), (unsigned)splits);
-  return launch_ex(k, grid, dim3(kThreads), (size_t)smem, st, tw[0], tw[1], tw[2], tx, p);
+  return launch_ex(k, grid, dim3(kThreads1), (size_t)smem, st, tw[0], tw[1], tw[2], tx, p);
 }
 
 // Sum of the split-K partials in slice order, written to the matrices'
@@ -1137,7 +1189,7 @@ int device_sms() {
 // within one wave of CTAs (one per SM): a second, partial wave costs a whole
 // slice's time for a fraction of the SMs.
 int choose_splits(int64_t K, int64_t row_tiles, int64_t M, int wcol) {
-  const int64_t bn = M >= 256 ? 256 : 128;
+  const int64_t bn = token_tile(M);
   const int64_t tiles = row_tiles * ((M + bn - 1) / bn);
   const int64_t nwb = K / wcol;
   const int64_t sms = device_sms();
@@ -1246,7 +1298,7 @@ cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) 
     if (e != cudaSuccess) return e;
   }
   // expert mode: the typical rows per expert pick the token tile
-  const int bn = (j.experts > 0 ? M / j.experts : M) >= 256 ? 256 : 128;
+  const int bn = token_tile(j.experts > 0 ? M / j.experts : M);
   const int tile_rows = j.gate_up ? BM / 2 : BM;
   const int64_t map_mats = j.experts > 0 ? j.experts : 1;  // expert mode: the maps cover every expert
   CUtensorMap tw[3], tx;
@@ -1313,8 +1365,9 @@ cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) 
     switch (j.dtype) {
 #define HYQ_RUN(F) \
   case F:          \
-    e = bn == 256 ? run<F, 256>(tw, tx, p, lay.tiles, splits, max_rows, st)                                        \
-                  : run<F, 128>(tw, tx, p, lay.tiles, splits, max_rows, st);                                       \
+    e = bn == 256   ? run<F, 256>(tw, tx, p, lay.tiles, splits, max_rows, st)                                      \
+        : bn == 128 ? run<F, 128>(tw, tx, p, lay.tiles, splits, max_rows, st)                                      \
+                    : run<F, 64>(tw, tx, p, lay.tiles, splits, max_rows, st);                                      \
     break;
       HYQ_RUN(Q4_K)
       HYQ_RUN(Q6_K)

@@ -134,18 +134,20 @@ def test_gate_up_silu_batch_matches_separate_products(cuda, t, N, K, M):
 # blocks, STQ1_0 ternary through the codebook), at small and 1.8B shapes.
 @pytest.mark.parametrize("t,N,K,M", [(Q8_0, 128, 256, 16), (Q8_0, 300, 1024, 37), (Q8_0, 2048, 2048, 512),
                                      (Q2_0C, 128, 512, 16), (Q2_0C, 300, 2048, 200), (Q2_0C, 2048, 6144, 512),
-                                     (STQ1_0, 128, 256, 16), (STQ1_0, 257, 2048, 130), (STQ1_0, 6144, 2048, 256)])
+                                     (STQ1_0, 128, 256, 16), (STQ1_0, 257, 2048, 130), (STQ1_0, 6144, 2048, 256),
+                                     (Q2_0C, 2048, 2048, 64), (Q2_0C, 2048, 6144, 64), (STQ1_0, 2048, 6144, 33),
+                                     (Q2_0C, 1024, 2048, 65)])
 def test_gemm_other_formats(cuda, t, N, K, M):
     run_case(cuda, t, N, K, M, seed=N + K + M + t)
 
 
-@pytest.mark.parametrize("t", [Q2_0C, STQ1_0])
-def test_gemm_1p8b_layer_calls(cuda, t):
-    """Grouped QKV and fused gate/up-SiLU on the 1.8B layer shapes."""
+@pytest.mark.parametrize("t,M", [(Q2_0C, 256), (STQ1_0, 256), (Q2_0C, 64), (Q2_0C, 20)])
+def test_gemm_1p8b_layer_calls(cuda, t, M):
+    """Grouped QKV and fused gate/up-SiLU on the 1.8B layer shapes (M <= 64:
+    the 64-token tile)."""
     import torch
     from hy_mt_rs_b200 import quant
 
-    M = 256
     q, k, v = _w(cuda, t, 2048, 2048, 1), _w(cuda, t, 512, 2048, 2), _w(cuda, t, 512, 2048, 3)
     x = torch.randn(M, 2048, generator=torch.Generator().manual_seed(8)).to(cuda)
     for w, y in zip((q, k, v), quant.Weight.matmul_qkv(q, k, v, x, M)):
