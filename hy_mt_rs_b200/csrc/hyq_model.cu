@@ -661,9 +661,38 @@ __global__ void __launch_bounds__(1024) argmax_rows_kernel(const float* __restri
   allow_dependents_launch();
   const float* xr = x + (size_t)blockIdx.x * n;
   unsigned long long best = 0ull;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const unsigned long long k = argmax_key(xr[i], (unsigned)i);
-    best = k > best ? k : best;
+  // float4 loads, four in flight per thread (the maximum does not depend on
+  // the order); the unaligned head and the tail one by one
+  const int head = min(n, (int)(((16u - (unsigned)(reinterpret_cast<uintptr_t>(xr) & 15u)) & 15u) / 4u));
+  const int n4 = (n - head) / 4;
+  const float4* x4 = reinterpret_cast<const float4*>(xr + head);
+  if ((reinterpret_cast<uintptr_t>(xr) & 3u) == 0) {
+#pragma unroll 4
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+      const float4 v = x4[i];
+      const unsigned j = (unsigned)(head + 4 * i);
+      unsigned long long k = argmax_key(v.x, j);
+      best = k > best ? k : best;
+      k = argmax_key(v.y, j + 1);
+      best = k > best ? k : best;
+      k = argmax_key(v.z, j + 2);
+      best = k > best ? k : best;
+      k = argmax_key(v.w, j + 3);
+      best = k > best ? k : best;
+    }
+    for (int i = threadIdx.x; i < head; i += blockDim.x) {
+      const unsigned long long k = argmax_key(xr[i], (unsigned)i);
+      best = k > best ? k : best;
+    }
+    for (int i = head + 4 * n4 + threadIdx.x; i < n; i += blockDim.x) {
+      const unsigned long long k = argmax_key(xr[i], (unsigned)i);
+      best = k > best ? k : best;
+    }
+  } else {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const unsigned long long k = argmax_key(xr[i], (unsigned)i);
+      best = k > best ? k : best;
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {

@@ -150,6 +150,47 @@ def test_argmax_ties_nan_and_workspace(cuda):
     assert run(np.full(3000, -np.inf, dtype=np.float32)) == 0
 
 
+@pytest.mark.parametrize("n", [1001, 120832])
+def test_argmax_rows_first_largest(cuda, n):
+    """hyq_argmax_rows (one greedy token per request, generation.rs:281-290
+    per row): the first index of the largest value, NaN never winning, an
+    all-NaN row giving 0, -0 tying with +0; every row's position advances by
+    one.  n = 1001 puts the rows' starts off 16-byte alignment."""
+    import ctypes as C
+    import torch
+    from hy_mt_rs_b200._native import check, lib
+
+    rng = np.random.default_rng(n)
+    rows = 9
+    x = rng.standard_normal((rows, n)).astype(np.float32)
+    x[1, 7] = x[1, n - 3] = 50.0                 # tie: the first wins
+    x[2, :] = np.nan                             # all NaN -> 0
+    x[3, :] = np.nan
+    x[3, n - 1] = -np.inf                        # NaN never wins, even over -inf
+    x[4, :] = 0.0
+    x[4, 5] = -0.0                               # -0 ties +0: index 0
+    x[5, 0] = np.nan
+    x[5, n // 2] = 1e30
+    x[6, n - 1] = 80.0                           # in the tail
+    x[7, 0] = 90.0                               # in the head
+    x[8, :] = -np.inf
+
+    def first_largest(r):
+        ok = ~np.isnan(r)
+        if not ok.any():
+            return 0
+        m = r[ok].max()
+        return int(np.flatnonzero(ok & (r == m))[0])
+
+    d = torch.from_numpy(x).to(cuda)
+    tok = torch.full((rows,), -5, dtype=torch.int32, device=cuda)
+    pos = torch.arange(rows, dtype=torch.int32, device=cuda)
+    check(lib.hyq_argmax_rows(C.c_void_p(d.data_ptr()), n, rows, C.c_void_p(tok.data_ptr()),
+                              C.c_void_p(pos.data_ptr()), C.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)))
+    assert tok.cpu().tolist() == [first_largest(x[r]) for r in range(rows)]
+    assert pos.cpu().tolist() == list(range(1, rows + 1))
+
+
 @pytest.mark.parametrize("prompt_len,rel_bound", [(6, 1e-4), (40, 2e-2)])
 def test_batched_prefill_matches_oracle(cuda, prompt_len, rel_bound):
     """The batched forward (model.rs:549-646): the prompt in one chunk,
