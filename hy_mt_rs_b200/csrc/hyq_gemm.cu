@@ -429,6 +429,12 @@ __global__ void __launch_bounds__(kThreads1, 1)
                 const __grid_constant__ Params p) {
   using L = Smem<FMT, BN>;
   constexpr int S = L::S;
+  // With an even number of stages the MMA thread releases them in pairs:
+  // one tcgen05.commit costs about as much issue time as two MMAs, so one
+  // commit per two K steps (on the pair's first barrier) saves it half the
+  // time.  Waiters of stage s wait on barrier rel(s).
+  constexpr bool kPairRelease = S % 2 == 0;
+  auto rel = [](int s) { return kPairRelease ? (s & ~1) : s; };
   static_assert(BN + 32 * S <= kTmemCols, "accumulator and A stages exceed tensor memory");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled tiles
@@ -536,7 +542,7 @@ __global__ void __launch_bounds__(kThreads1, 1)
           ++issued_w;
         }
         const int s = ks % S;
-        if (ks >= S && !mbar_wait(empty(s), ((ks / S) - 1) & 1, abort_flag)) {
+        if (ks >= S && !mbar_wait(empty(rel(s)), ((ks / S) - 1) & 1, abort_flag)) {
           ok = false;
           break;
         }
@@ -574,7 +580,7 @@ __global__ void __launch_bounds__(kThreads1, 1)
 #pragma unroll
         for (int k = 0; k < BK / 16; ++k)
           umma_f16_ts(tmem, a0 + 8 * k, sw128_desc(b0 + 32 * k), idesc, (ks > 0 || k > 0) ? 1u : 0u);
-        umma_commit(empty(s));
+        if (!kPairRelease || (ks & 1) || ks == nk - 1) umma_commit(empty(rel(s)));
       }
       __syncwarp();
     }
@@ -604,7 +610,7 @@ __global__ void __launch_bounds__(kThreads1, 1)
       // first step of this block column that this group handles
       if (ks % kSpw < kGroups) ok = mbar_wait(wfull(ws), (wb / WS) & 1, abort_flag);
       const int s = ks % S;
-      if (ok && ks >= S) ok = mbar_wait(empty(s), ((ks / S) - 1) & 1, abort_flag);
+      if (ok && ks >= S) ok = mbar_wait(empty(rel(s)), ((ks / S) - 1) & 1, abort_flag);
       if (!ok) {
         atomicOr(p.status, DEV_TIMEOUT_FULL);
         *abort_flag = 1;
