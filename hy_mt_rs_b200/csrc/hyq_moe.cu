@@ -68,6 +68,57 @@ __global__ void __launch_bounds__(256) router_kernel(const float* __restrict__ w
   }
 }
 
+// The same logits with both operands staged: CTA (expert group, token
+// group) loads kRouterChains router rows and up to kRouterTokens token rows
+// into shared memory with 16-byte loads, all in flight at once, then each
+// half-warp computes one token's kRouterChains dots from shared memory in
+// the same lane order (bit-identical to router_kernel).  For K a multiple of
+// 16 whose rows fit (router_tiled_tokens).
+constexpr int kRouterTokens = 16;
+constexpr int kRouterSmemBytes = 200 * 1024;
+
+inline int router_tiled_tokens(int64_t K) {
+  if (K % 16) return 0;
+  const int64_t room = kRouterSmemBytes / (K * (int64_t)sizeof(float)) - kRouterChains;
+  return (int)(room < 1 ? 0 : room > kRouterTokens ? kRouterTokens : room);
+}
+
+__global__ void __launch_bounds__(256) router_tiled_kernel(const float* __restrict__ w, const float* __restrict__ x,
+                                                           int K, int experts, int tokens, int tpc,
+                                                           float* __restrict__ logits) {
+  extern __shared__ __align__(16) float rs[];  // [kRouterChains][K] router rows, then [tpc][K] token rows
+  float* xs = rs + (size_t)kRouterChains * K;
+  const int e0 = blockIdx.x * kRouterChains, t0 = blockIdx.y * tpc;
+  const int ne = min(kRouterChains, experts - e0), nt = min(tpc, tokens - t0);
+  const int k4 = K / 4;
+  for (int i = threadIdx.x; i < (ne + nt) * k4; i += blockDim.x) {
+    const int r = i / k4, c = i - r * k4;
+    const float4* src = r < ne ? reinterpret_cast<const float4*>(w + (size_t)(e0 + r) * K)
+                               : reinterpret_cast<const float4*>(x + (size_t)(t0 + r - ne) * K);
+    float* dst = r < ne ? rs + (size_t)r * K : xs + (size_t)(r - ne) * K;
+    *reinterpret_cast<float4*>(dst + 4 * c) = __ldg(src + c);
+  }
+  __syncthreads();
+  const int hw = threadIdx.x >> 4, lane = threadIdx.x & 31, l = lane & 15;
+  const unsigned mask = (lane & 16) ? 0xffff0000u : 0x0000ffffu;
+  if (hw >= nt) return;  // whole half-warps leave together
+  const float* xr = xs + (size_t)hw * K + l;
+  float acc[kRouterChains];
+#pragma unroll
+  for (int j = 0; j < kRouterChains; ++j) acc[j] = 0.f;
+#pragma unroll 4
+  for (int c = 0; c < K / 16; ++c) {
+    const float xv = xr[16 * c];
+#pragma unroll
+    for (int j = 0; j < kRouterChains; ++j) acc[j] = fmaf(rs[(size_t)min(j, ne - 1) * K + 16 * c + l], xv, acc[j]);
+  }
+#pragma unroll
+  for (int j = 0; j < kRouterChains; ++j) {
+    const float d = x86_lane_sum(acc[j], mask);
+    if (l == 0 && j < ne) logits[(size_t)(t0 + hw) * experts + e0 + j] = d;
+  }
+}
+
 // route (model.rs:728-767) for one token per warp: sigmoid with the
 // reference's two branches, order by sigmoid + bias descending under
 // f32::total_cmp with ties to the lower index, keep `used`, then weights
@@ -296,10 +347,22 @@ int hyq_moe_router(const hyq_weight* router, const float* x, int64_t tokens, flo
   if (configured != dev) {
     cudaFuncSetAttribute(hyq::moe::router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          hyq::moe::kRouterMaxK * (int)sizeof(float));
+    cudaFuncSetAttribute(hyq::moe::router_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         hyq::moe::kRouterSmemBytes);
     configured = dev;
   }
-  hyq::moe::router_kernel<<<(unsigned)tokens, 256, (size_t)K * sizeof(float), (cudaStream_t)stream>>>(
-      static_cast<const float*>(data), x, (int)K, (int)E, logits);
+  const int tpc = hyq::moe::router_tiled_tokens(K);
+  const bool aligned16 = ((reinterpret_cast<uintptr_t>(data) | reinterpret_cast<uintptr_t>(x)) & 15) == 0;
+  if (tpc > 0 && aligned16) {
+    const dim3 grid((unsigned)((E + hyq::moe::kRouterChains - 1) / hyq::moe::kRouterChains),
+                    (unsigned)((tokens + tpc - 1) / tpc));
+    const size_t smem = (size_t)(hyq::moe::kRouterChains + tpc) * K * sizeof(float);
+    hyq::moe::router_tiled_kernel<<<grid, 256, smem, (cudaStream_t)stream>>>(
+        static_cast<const float*>(data), x, (int)K, (int)E, (int)tokens, tpc, logits);
+  } else {
+    hyq::moe::router_kernel<<<(unsigned)tokens, 256, (size_t)K * sizeof(float), (cudaStream_t)stream>>>(
+        static_cast<const float*>(data), x, (int)K, (int)E, logits);
+  }
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "moe_router: %s", cudaGetErrorString(e));
 }

@@ -29,6 +29,27 @@ def _stream(cuda):
     return C.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)
 
 
+@pytest.mark.parametrize("hidden,experts,T", [(2048, 62, 64), (2048, 64, 1), (16384, 6, 3)])
+def test_router_logits_bit_exact(cuda, hidden, experts, T):
+    """hyq_moe_router at the config-5 width (the tiled kernel: expert and
+    token rows staged in shared memory; 62 experts and 64 tokens leave
+    partial expert and token groups) and at a width too large to stage (the
+    per-token kernel): the oracle's x86-order logits bit for bit."""
+    import torch
+    from hy_mt_rs_b200 import quant
+    from hy_mt_rs_b200._native import check, lib
+    from oracle import moe as OM
+
+    g = torch.Generator().manual_seed(hidden + experts + T)
+    router = torch.randn(experts, hidden, generator=g)
+    w = quant.Weight(router.to(cuda).contiguous().view(torch.uint8).reshape(-1), quant.DType.F32, [hidden, experts])
+    x = torch.randn(T, hidden, generator=g).to(cuda)
+    logits = torch.full((T, experts), float("nan"), device=cuda)
+    check(lib.hyq_moe_router(w.handle, _p(x), T, _p(logits), _stream(cuda)))
+    ref = OM.router_logits(router.view(torch.uint8).reshape(-1).numpy(), hidden, experts, x.cpu().numpy())
+    np.testing.assert_array_equal(logits.cpu().numpy(), ref)
+
+
 @pytest.mark.parametrize("T", [1, 37])
 def test_router_route_group(cuda, T):
     import torch
