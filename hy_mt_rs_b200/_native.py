@@ -81,6 +81,10 @@ _SIGS = {
     "hyq_add": ([_vp, _vp, _i64, _vp], C.c_int),
     "hyq_rope_qk_seqs": ([_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _i64, _vp, _i64, _vp, _vp, C.c_float,
                           C.c_int, _vp, _vp, _i64, _vp], C.c_int),
+    "hyq_rope_attention": ([_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _i64, _vp, _vp, _vp, C.c_float,
+                            C.c_int, _vp, _vp, _vp, _vp, _vp], C.c_int),
+    "hyq_rope_attention_seqs": ([_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _i64, _vp, _i64, _vp, _vp,
+                                 C.c_float, C.c_int, _vp, _vp, _i64, _vp, _vp, _vp], C.c_int),
     "hyq_attention_seqs": ([_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _i64, _vp, _i64, _i64, _vp, _vp, _vp],
                            C.c_int),
     "hyq_argmax_rows": ([_vp, _i64, _i64, _vp, _vp, _vp], C.c_int),

@@ -271,6 +271,22 @@ __device__ __forceinline__ float dot_x86(const float* a, const float* b, int n, 
   return __fadd_rn(h, t);
 }
 
+// Asynchronous 16- and 4-byte copies global -> shared (cp.async), their
+// commit groups and waits (this thread's copies).
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // The same dot_avx2 order (quant.rs:2562-2596) computed by one thread: the
 // sixteen accumulator lanes are registers, followed by the same pairwise lane
 // sums, horizontal sum and scalar tail as dot_x86.  a and b are 16-byte

@@ -247,21 +247,31 @@ struct AttnArgs {
   unsigned* counters;  // [tokens][kv_heads], zero between calls
   unsigned* status;
   int64_t seq_stride;  // as RopeArgs: 0 one sequence, else per-token sequences
+  // fused RoPE + q/k RMSNorm + KV append (rope_qk of the step's token): the
+  // raw q in `q`, the raw key and value rows of each token in k_new / v_new
+  // ([tokens, kv_heads * dim]); the caches are written at the position
+  int fuse;
+  const float* k_new;
+  const float* v_new;
+  const float* cos_tab;
+  const float* sin_tab;
+  const float* q_norm;
+  const float* k_norm;
+  float eps;
+  int norm_first;
+  float* k_cache_w;
+  float* v_cache_w;
 };
 
-__device__ __forceinline__ void cp_async16(float* dst, const float* src) {
-  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+// RoPE of one head in shared memory with its RMSNorm before or after
+// (model.rs:429-446, as rope_qk_kernel); one warp.
+__device__ void rope_head(float* hd, const float* nw, const float* c, const float* sn, int dim, float eps,
+                          int norm_first) {
+  if (norm_first && nw) head_norm(hd, nw, dim, eps);
+  head_rope(hd, c, sn, dim);
+  if (!norm_first && nw) head_norm(hd, nw, dim, eps);
 }
-__device__ __forceinline__ void cp_async4(float* dst, const float* src) {
-  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
+
 
 // rows x dim floats from global rows `gstride` apart into shared rows
 // `sstride` apart (16-byte copies when every row start is 16-byte aligned).
@@ -336,9 +346,13 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attention_kernel(const __grid
   const float* vg = a.v_cache + seq + (size_t)p0 * width + (size_t)kvh * dim;
   const bool vec = (dim & 3) == 0 && (width & 3) == 0 && ((reinterpret_cast<uintptr_t>(kg) | reinterpret_cast<uintptr_t>(vg)) & 15) == 0;
   // (the specialised kernel is launched only for 16-byte aligned caches)
-  stage_rows<DIM>(k_s, ks, kg, width, n, dim, vec);
+  // fused step: the last chunk ends at the token's own position, whose key
+  // and value rows this CTA builds instead of reading them from the cache
+  const bool fresh = a.fuse && split == used - 1;
+  const int n_stage = fresh ? n - 1 : n;
+  stage_rows<DIM>(k_s, ks, kg, width, n_stage, dim, vec);
   cp_async_commit();
-  stage_rows<DIM>(v_s, dim, vg, width, n, dim, vec);
+  stage_rows<DIM>(v_s, dim, vg, width, n_stage, dim, vec);
   cp_async_commit();
   const size_t h0 = (size_t)tok * a.heads + (size_t)kvh * G;  // (token, first head of the group)
   const float* qg = a.q + h0 * dim;
@@ -352,6 +366,30 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attention_kernel(const __grid
     for (int t = threadIdx.x; t < G * dim; t += kAttnThreads) {
       const int g = t / dim;
       q_s[g * ks + (t - g * dim)] = qg[t];
+    }
+  }
+  if (a.fuse) {
+    __syncthreads();  // the raw query heads are in q_s
+    const float* c = a.cos_tab + (size_t)pos * (dim / 2);
+    const float* sn = a.sin_tab + (size_t)pos * (dim / 2);
+    for (int g = warp; g < G; g += kAttnThreads / 32) rope_head(q_s + g * ks, a.q_norm, c, sn, dim, a.eps, a.norm_first);
+    if (fresh && warp == 0) {
+      const size_t row = (size_t)tok * width + (size_t)kvh * dim;
+      float* kr = k_s + (size_t)(n - 1) * ks;
+      float* vr = v_s + (size_t)(n - 1) * dim;
+      for (int i = lane; i < dim; i += 32) {
+        kr[i] = a.k_new[row + i];
+        vr[i] = a.v_new[row + i];
+      }
+      __syncwarp();
+      rope_head(kr, a.k_norm, c, sn, dim, a.eps, a.norm_first);
+      // KV append (no other CTA of this call reads the row)
+      float* kc = a.k_cache_w + seq + (size_t)pos * width + (size_t)kvh * dim;
+      float* vc = a.v_cache_w + seq + (size_t)pos * width + (size_t)kvh * dim;
+      for (int i = lane; i < dim; i += 32) {
+        kc[i] = kr[i];
+        vc[i] = vr[i];
+      }
     }
   }
   cp_async_wait<1>();  // this thread's K copies
@@ -839,9 +877,23 @@ int hyq_attention_workspace_bytes(int heads, int head_dim, int64_t positions, in
   return HYQ_OK;
 }
 
+// RoPE + q/k RMSNorm + KV append folded into the attention launch.
+struct AttnFuse {
+  const float* k;
+  const float* v;
+  const float* cos_tab;
+  const float* sin_tab;
+  const float* q_norm;
+  const float* k_norm;
+  float eps;
+  int norm_first;
+  float* k_cache;
+  float* v_cache;
+};
+
 static int attention_impl(const float* q, const float* k_cache, const float* v_cache, int heads, int kv_heads,
                           int head_dim, int64_t positions, const int32_t* pos, int64_t tokens, float* out,
-                          void* workspace, int64_t seq_stride, void* stream) {
+                          void* workspace, int64_t seq_stride, void* stream, const AttnFuse* fuse = nullptr) {
   if (!q || !k_cache || !v_cache || !pos || !out || !workspace)
     return hyq::api_fail(HYQ_E_INVALID, "attention: null pointer");
   if (heads <= 0 || kv_heads <= 0 || heads % kv_heads || heads / kv_heads > hyq::model::kAttnMaxGroup ||
@@ -863,6 +915,25 @@ static int attention_impl(const float* q, const float* k_cache, const float* v_c
   a.out = out;
   a.counters = static_cast<unsigned*>(workspace);
   a.seq_stride = seq_stride;
+  if (fuse) {
+    if (!fuse->k || !fuse->v || !fuse->cos_tab || !fuse->sin_tab || !fuse->k_cache || !fuse->v_cache)
+      return hyq::api_fail(HYQ_E_INVALID, "rope_attention: null pointer");
+    if (head_dim & 1) return hyq::api_fail(HYQ_E_SHAPE, "rope_attention: odd head_dim");
+    // one sequence: one token (a prompt's tokens would read rows that other
+    // CTAs of the launch append; prefill runs hyq_rope_qk + hyq_attention)
+    if (!seq_stride && tokens != 1) return hyq::api_fail(HYQ_E_SHAPE, "rope_attention: one token per sequence");
+    a.fuse = 1;
+    a.k_new = fuse->k;
+    a.v_new = fuse->v;
+    a.cos_tab = fuse->cos_tab;
+    a.sin_tab = fuse->sin_tab;
+    a.q_norm = fuse->q_norm;
+    a.k_norm = fuse->k_norm;
+    a.eps = fuse->eps;
+    a.norm_first = fuse->norm_first;
+    a.k_cache_w = fuse->k_cache;
+    a.v_cache_w = fuse->v_cache;
+  }
   if (tokens <= 0 || tokens > 65535 || tokens > positions)
     return hyq::api_fail(HYQ_E_SHAPE, "attention: 1 to %d tokens", (int)(positions < 65535 ? positions : 65535));
   a.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + hyq::model::attn_counter_bytes(positions * heads));
@@ -904,6 +975,28 @@ int hyq_attention_seqs(const float* q, const float* k_cache, const float* v_cach
     return hyq::api_fail(HYQ_E_SHAPE, "attention_seqs: sequences' caches overlap (stride %lld)", (long long)seq_stride);
   return attention_impl(q, k_cache, v_cache, heads, kv_heads, head_dim, positions, pos, seqs, out, workspace,
                         seq_stride, stream);
+}
+
+int hyq_rope_attention(const float* q, const float* k, const float* v, int heads, int kv_heads, int head_dim,
+                       const float* cos_tab, const float* sin_tab, int64_t positions, const int32_t* pos,
+                       const float* q_norm, const float* k_norm, float eps, int norm_first, float* k_cache,
+                       float* v_cache, float* out, void* workspace, void* stream) {
+  const AttnFuse f{k, v, cos_tab, sin_tab, q_norm, k_norm, eps, norm_first, k_cache, v_cache};
+  return attention_impl(q, k_cache, v_cache, heads, kv_heads, head_dim, positions, pos, 1, out, workspace, 0, stream,
+                        &f);
+}
+
+int hyq_rope_attention_seqs(const float* q, const float* k, const float* v, int heads, int kv_heads, int head_dim,
+                            const float* cos_tab, const float* sin_tab, int64_t positions, const int32_t* pos,
+                            int64_t seqs, const float* q_norm, const float* k_norm, float eps, int norm_first,
+                            float* k_cache, float* v_cache, int64_t seq_stride, float* out, void* workspace,
+                            void* stream) {
+  if (seq_stride < positions * kv_heads * head_dim)
+    return hyq::api_fail(HYQ_E_SHAPE, "rope_attention_seqs: sequences' caches overlap (stride %lld)",
+                         (long long)seq_stride);
+  const AttnFuse f{k, v, cos_tab, sin_tab, q_norm, k_norm, eps, norm_first, k_cache, v_cache};
+  return attention_impl(q, k_cache, v_cache, heads, kv_heads, head_dim, positions, pos, seqs, out, workspace,
+                        seq_stride, stream, &f);
 }
 
 int hyq_argmax_rows(const float* x, int64_t n, int64_t rows, int32_t* token, int32_t* pos, void* stream) {

@@ -91,13 +91,14 @@ __global__ void __launch_bounds__(256) router_tiled_kernel(const float* __restri
   const int e0 = blockIdx.x * kRouterChains, t0 = blockIdx.y * tpc;
   const int ne = min(kRouterChains, experts - e0), nt = min(tpc, tokens - t0);
   const int k4 = K / 4;
-  for (int i = threadIdx.x; i < (ne + nt) * k4; i += blockDim.x) {
-    const int r = i / k4, c = i - r * k4;
-    const float4* src = r < ne ? reinterpret_cast<const float4*>(w + (size_t)(e0 + r) * K)
-                               : reinterpret_cast<const float4*>(x + (size_t)(t0 + r - ne) * K);
+  // asynchronous 16-byte copies: every load of the CTA in flight at once
+  for (int r = 0; r < ne + nt; ++r) {
+    const float* src = r < ne ? w + (size_t)(e0 + r) * K : x + (size_t)(t0 + r - ne) * K;
     float* dst = r < ne ? rs + (size_t)r * K : xs + (size_t)(r - ne) * K;
-    *reinterpret_cast<float4*>(dst + 4 * c) = __ldg(src + c);
+    for (int c = threadIdx.x; c < k4; c += blockDim.x) cp_async16(dst + 4 * c, src + 4 * c);
   }
+  cp_async_commit();
+  cp_async_wait<0>();
   __syncthreads();
   const int hw = threadIdx.x >> 4, lane = threadIdx.x & 31, l = lane & 15;
   const unsigned mask = (lane & 16) ? 0xffff0000u : 0x0000ffffu;
@@ -169,35 +170,33 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
   int my_e = 0;
   float my_s = 0.f;
   for (int k = 0; k < used; ++k) {
-    // the largest key, then the lowest expert index, among those not taken
-    int bk = INT_MIN, be = INT_MAX;
-    float bs = 0.f;
-    bool have = false;
+    // the largest key, then the lowest expert index, among those not taken:
+    // one 64-bit value per candidate (order-preserving key bits, then the
+    // complemented index), 0 for none, reduced with a maximum
+    unsigned long long best = 0ull;
+    float mine = 0.f;  // sigmoid of this lane's best candidate
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
       if (j < per) {
         const int e = lane + 32 * j;
-        if (e < experts && !((taken >> j) & 1u) && (!have || key[j] > bk || (key[j] == bk && e < be))) {
-          bk = key[j];
-          be = e;
-          bs = sig[j];
-          have = true;
+        if (e < experts && !((taken >> j) & 1u)) {
+          const unsigned long long c =
+              ((unsigned long long)((unsigned)key[j] ^ 0x80000000u) << 32) | (0xffffffffu - (unsigned)e);
+          if (c > best) {
+            best = c;
+            mine = sig[j];
+          }
         }
       }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-      const int ok = __shfl_xor_sync(0xffffffffu, bk, o);
-      const int oe = __shfl_xor_sync(0xffffffffu, be, o);
-      const float os = __shfl_xor_sync(0xffffffffu, bs, o);
-      const int oh = __shfl_xor_sync(0xffffffffu, have ? 1 : 0, o);
-      if (oh && (!have || ok > bk || (ok == bk && oe < be))) {
-        bk = ok;
-        be = oe;
-        bs = os;
-        have = true;
-      }
+      const unsigned long long c = __shfl_xor_sync(0xffffffffu, best, o);
+      best = c > best ? c : best;
     }
+    const int be = (int)(0xffffffffu - (unsigned)(best & 0xffffffffull));
+    // the winner's sigmoid, from the lane whose own best it is
+    const float bs = __shfl_sync(0xffffffffu, mine, be & 31);
     if ((be & 31) == lane) taken |= 1u << (be >> 5);
     if (lane == k) {
       my_e = be;
@@ -299,28 +298,47 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
                                                       const int32_t* __restrict__ token_rows,
                                                       const float* __restrict__ row_weight, int used,
                                                       float* __restrict__ out) {
-  __shared__ int32_t ex_s[32], row_s[32];
-  __shared__ float w_s[32];
+  __shared__ int32_t ex_s[32], row_s[32], in_e[32], in_r[32];
+  __shared__ float w_s[32], in_w[32];
   const int t = blockIdx.x;
+  // the token's choices and their weights, loaded by one lane each
+  if (threadIdx.x < used) {
+    const int r = token_rows[(size_t)t * used + threadIdx.x];
+    in_e[threadIdx.x] = topk_idx[(size_t)t * used + threadIdx.x];
+    in_r[threadIdx.x] = r;
+    in_w[threadIdx.x] = row_weight[r];
+  }
+  __syncthreads();
   if (threadIdx.x == 0) {
-    // the token's choices, sorted by expert (insertion sort of `used` items)
+    // sorted by expert (insertion sort of `used` items)
     for (int k = 0; k < used; ++k) {
-      const int e = topk_idx[(size_t)t * used + k], r = token_rows[(size_t)t * used + k];
+      const int e = in_e[k], r = in_r[k];
+      const float wk = in_w[k];
       int i = k;
       while (i > 0 && ex_s[i - 1] > e) {
         ex_s[i] = ex_s[i - 1];
         row_s[i] = row_s[i - 1];
+        w_s[i] = w_s[i - 1];
         --i;
       }
       ex_s[i] = e;
       row_s[i] = r;
+      w_s[i] = wk;
     }
-    for (int k = 0; k < used; ++k) w_s[k] = row_weight[row_s[k]];
   }
   __syncthreads();
+  // out = shared + sum over experts ascending of w * y, eight rows' loads in
+  // flight at a time
   for (int c = threadIdx.x; c < N; c += blockDim.x) {
     float acc = shared[(size_t)t * N + c];
-    for (int k = 0; k < used; ++k) acc = __fadd_rn(acc, __fmul_rn(w_s[k], y[(size_t)row_s[k] * N + c]));
+    for (int k0 = 0; k0 < used; k0 += 8) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = k0 + j < used ? y[(size_t)row_s[k0 + j] * N + c] : 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (k0 + j < used) acc = __fadd_rn(acc, __fmul_rn(w_s[k0 + j], v[j]));
+    }
     out[(size_t)t * N + c] = acc;
   }
 }

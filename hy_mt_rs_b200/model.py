@@ -94,10 +94,14 @@ class _Acts:
 
 class DenseModel:
     """fused: run each token step as one persistent kernel
-    (hyq_dense_step_enqueue) instead of ~8 launches per layer."""
+    (hyq_dense_step_enqueue) instead of 7 launches per layer.
+    rope_in_attention: single-token steps run RoPE + q/k norm + KV append
+    inside the attention launch (hyq_rope_attention, bit-identical to
+    hyq_rope_qk + hyq_attention)."""
 
-    def __init__(self, cfg, weights, device, prefill_chunk=PREFILL_CHUNK, fused=False):
+    def __init__(self, cfg, weights, device, prefill_chunk=PREFILL_CHUNK, fused=False, rope_in_attention=True):
         self.cfg = cfg
+        self.rope_in_attention = rope_in_attention
         self.device = device
         H, KV = cfg.hidden, cfg.kv_heads * cfg.head_dim
         sh = weights["shapes"]
@@ -241,11 +245,17 @@ class DenseModel:
             else:
                 check(lib.hyq_matmul_qkv(W["q"].handle, W["k"].handle, W["v"].handle, _p(a.normalized), M, _p(a.q),
                                          _p(a.k), _p(a.v), st))
-            check(lib.hyq_rope_qk(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim, _p(self.cos),
-                                  _p(self.sin), cfg.positions, _p(pos), M, _p(W["q_norm"]), _p(W["k_norm"]),
-                                  cfg.eps, 0, _p(kc), _p(vc), st))
-            check(lib.hyq_attention(_p(a.q), _p(kc), _p(vc), cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.positions,
-                                    _p(pos), M, _p(a.attended), _p(self.attn_ws), st))
+            if M == 1 and self.rope_in_attention:
+                check(lib.hyq_rope_attention(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim,
+                                             _p(self.cos), _p(self.sin), cfg.positions, _p(pos), _p(W["q_norm"]),
+                                             _p(W["k_norm"]), cfg.eps, 0, _p(kc), _p(vc), _p(a.attended),
+                                             _p(self.attn_ws), st))
+            else:
+                check(lib.hyq_rope_qk(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim,
+                                      _p(self.cos), _p(self.sin), cfg.positions, _p(pos), M, _p(W["q_norm"]),
+                                      _p(W["k_norm"]), cfg.eps, 0, _p(kc), _p(vc), st))
+                check(lib.hyq_attention(_p(a.q), _p(kc), _p(vc), cfg.heads, cfg.kv_heads, cfg.head_dim,
+                                        cfg.positions, _p(pos), M, _p(a.attended), _p(self.attn_ws), st))
             check(lib.hyq_matmul(W["o"].handle, _p(a.attended), M, _p(a.projected), st))
             # residual add fused with the norm that follows it
             check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.projected), _p(W["ffn_norm"]), H, M, cfg.eps,
@@ -286,7 +296,8 @@ class DenseModel:
 
     # kernel launches of one enqueue_step
     def launches(self):
-        return 1 if self._step is not None else 2 + 8 * self.cfg.layers + 2
+        per_layer = 7 if self.rope_in_attention else 8
+        return 1 if self._step is not None else 2 + per_layer * self.cfg.layers + 2
 
     def capture(self, stream):
         """Capture enqueue_step as one CUDA graph on `stream`."""
@@ -375,12 +386,18 @@ class DenseBatch:
             kc, vc = self.caches[i]
             check(lib.hyq_matmul_qkv(W["q"].handle, W["k"].handle, W["v"].handle, _p(a.normalized), B, _p(a.q),
                                      _p(a.k), _p(a.v), st))
-            check(lib.hyq_rope_qk_seqs(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim,
-                                       _p(m.cos), _p(m.sin), cfg.positions, _p(self.pos), B, _p(W["q_norm"]),
-                                       _p(W["k_norm"]), cfg.eps, 0, _p(kc), _p(vc), self.stride, st))
-            check(lib.hyq_attention_seqs(_p(a.q), _p(kc), _p(vc), cfg.heads, cfg.kv_heads, cfg.head_dim,
-                                         cfg.positions, _p(self.pos), B, self.stride, _p(a.attended),
-                                         _p(self.attn_ws), st))
+            if m.rope_in_attention:
+                check(lib.hyq_rope_attention_seqs(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim,
+                                                  _p(m.cos), _p(m.sin), cfg.positions, _p(self.pos), B,
+                                                  _p(W["q_norm"]), _p(W["k_norm"]), cfg.eps, 0, _p(kc), _p(vc),
+                                                  self.stride, _p(a.attended), _p(self.attn_ws), st))
+            else:
+                check(lib.hyq_rope_qk_seqs(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim,
+                                           _p(m.cos), _p(m.sin), cfg.positions, _p(self.pos), B, _p(W["q_norm"]),
+                                           _p(W["k_norm"]), cfg.eps, 0, _p(kc), _p(vc), self.stride, st))
+                check(lib.hyq_attention_seqs(_p(a.q), _p(kc), _p(vc), cfg.heads, cfg.kv_heads, cfg.head_dim,
+                                             cfg.positions, _p(self.pos), B, self.stride, _p(a.attended),
+                                             _p(self.attn_ws), st))
             check(lib.hyq_matmul(W["o"].handle, _p(a.attended), B, _p(a.projected), st))
             check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.projected), _p(W["ffn_norm"]), H, B, cfg.eps,
                                        _p(a.normalized), st))
@@ -397,7 +414,8 @@ class DenseBatch:
         batched products (2 launches each on the tensor cores from 16
         requests: activation conversion + GEMM)."""
         per_product = 2 if self.B >= 16 else self.B
-        return 2 + self.m.cfg.layers * (4 + 4 * per_product) + per_product + 1
+        per_layer = (3 if self.m.rope_in_attention else 4) + 4 * per_product
+        return 2 + self.m.cfg.layers * per_layer + per_product + 1
 
     def capture(self, stream):
         quant.set_launch_overlap(True)

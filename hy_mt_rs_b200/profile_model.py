@@ -5,7 +5,8 @@ captures.
 
 Builds the seeded random-init model with the 1.8B shapes (Q2_0C linears,
 tied Q6_K embedding), captures one token step as a CUDA graph, feeds
-`--prompt` tokens and then `--steps` greedy steps, one graph replay each.
+`--prompt` tokens in one batched forward and then `--steps` greedy steps,
+one graph replay each.
 Every replay launches the same kernels in the same order (a launch list of
 one replay is one token step).
 
@@ -44,7 +45,7 @@ def main():
         stream.synchronize()
         print("tokens", batch.tokens.cpu().tolist())
         return
-    ids = model.generate(list(range(1, a.prompt + 1)), a.steps, stream)
+    ids = model.generate(list(range(1, a.prompt + 1)), a.steps, stream, batched_prefill=True)
     print("tokens", ids)
 
 

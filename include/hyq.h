@@ -282,6 +282,29 @@ int hyq_rope_qk_seqs(float* q, float* k, const float* v, int heads, int kv_heads
 int hyq_attention_seqs(const float* q, const float* k_cache, const float* v_cache, int heads, int kv_heads,
                        int head_dim, int64_t positions, const int32_t* pos, int64_t seqs, int64_t seq_stride,
                        float* out, void* workspace, void* stream);
+
+/* One decode step's RoPE + q/k RMSNorm + KV append (hyq_rope_qk) and
+ * attention (hyq_attention) in one launch, bit-identical to the two calls:
+ * q, k and v are the step's raw projections (q [heads * head_dim], k and v
+ * [kv_heads * head_dim]; left unchanged), the position is read from `pos`,
+ * the rotated key and the value are appended to the caches at it, and the
+ * attention output goes to `out`.  One token of one sequence (a prompt's
+ * tokens use hyq_rope_qk and hyq_attention).  Workspace as hyq_attention
+ * with tokens = 1. */
+int hyq_rope_attention(const float* q, const float* k, const float* v, int heads, int kv_heads, int head_dim,
+                       const float* cos_tab, const float* sin_tab, int64_t positions, const int32_t* pos,
+                       const float* q_norm, const float* k_norm, float eps, int norm_first, float* k_cache,
+                       float* v_cache, float* out, void* workspace, void* stream);
+
+/* The same for `seqs` independent sequences, one token each (as
+ * hyq_rope_qk_seqs + hyq_attention_seqs: q [seqs, heads * head_dim], k and v
+ * [seqs, kv_heads * head_dim], sequence t at position pos[t] with its caches
+ * t * seq_stride floats further). */
+int hyq_rope_attention_seqs(const float* q, const float* k, const float* v, int heads, int kv_heads, int head_dim,
+                            const float* cos_tab, const float* sin_tab, int64_t positions, const int32_t* pos,
+                            int64_t seqs, const float* q_norm, const float* k_norm, float eps, int norm_first,
+                            float* k_cache, float* v_cache, int64_t seq_stride, float* out, void* workspace,
+                            void* stream);
 /* Greedy token of each of `rows` rows of n logits (generation.rs:281-290):
  * token[r]; pos[r] += 1 when pos is not NULL. */
 int hyq_argmax_rows(const float* x, int64_t n, int64_t rows, int32_t* token, int32_t* pos, void* stream);

@@ -91,6 +91,95 @@ def test_attention_splits_match_oracle(cuda, shape, pos):
     assert not counters.any()
 
 
+@pytest.mark.parametrize("shape,pos", [((16, 4, 128), 0), ((16, 4, 128), 63), ((16, 4, 128), 64),
+                                       ((16, 4, 128), 300), ((8, 4, 64), 77), ((6, 2, 40), 130)])
+@pytest.mark.parametrize("norm_first", [0, 1])
+def test_rope_attention_matches_separate_calls(cuda, shape, pos, norm_first):
+    """hyq_rope_attention (RoPE + q/k norm + KV append inside the attention
+    launch) against hyq_rope_qk followed by hyq_attention: the same output
+    and the same appended cache rows, bit for bit; its raw q/k/v inputs are
+    left unchanged."""
+    import ctypes as C
+    import torch
+    from hy_mt_rs_b200._native import check, lib
+
+    heads, kv_heads, dim = shape
+    positions = 512
+    g = torch.Generator().manual_seed(pos + dim)
+    q = torch.randn(heads * dim, generator=g).to(cuda)
+    k = torch.randn(kv_heads * dim, generator=g).to(cuda)
+    v = torch.randn(kv_heads * dim, generator=g).to(cuda)
+    qn = (1.0 + 0.1 * torch.randn(dim, generator=g)).to(cuda)
+    kn = (1.0 + 0.1 * torch.randn(dim, generator=g)).to(cuda)
+    half = dim // 2
+    cos = np.empty(positions * half, dtype=np.float32)
+    sin = np.empty_like(cos)
+    check(lib.hyq_rope_table(positions, dim, C.c_float(10000.0), cos.ctypes.data_as(C.c_void_p),
+                             sin.ctypes.data_as(C.c_void_p)))
+    cos_d, sin_d = torch.from_numpy(cos).to(cuda), torch.from_numpy(sin).to(cuda)
+    cache0 = torch.randn(2, positions, kv_heads * dim, generator=g).to(cuda)
+    ws_bytes = C.c_size_t()
+    check(lib.hyq_attention_workspace_bytes(heads, dim, positions, 1, C.byref(ws_bytes)))
+    st = C.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)
+    P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    p = torch.tensor([pos], dtype=torch.int32, device=cuda)
+
+    # separate calls (rope_qk rotates q and k in place)
+    q1, k1, cache1 = q.clone(), k.clone(), cache0.clone()
+    ws1 = torch.zeros(ws_bytes.value, dtype=torch.uint8, device=cuda)
+    out1 = torch.empty(heads * dim, device=cuda)
+    check(lib.hyq_rope_qk(P(q1), P(k1), P(v), heads, kv_heads, dim, P(cos_d), P(sin_d), positions, P(p), 1, P(qn),
+                          P(kn), C.c_float(1e-5), norm_first, P(cache1[0]), P(cache1[1]), st))
+    check(lib.hyq_attention(P(q1), P(cache1[0]), P(cache1[1]), heads, kv_heads, dim, positions, P(p), 1, P(out1),
+                            P(ws1), st))
+    # one launch, twice (the workspace counters reset)
+    q2, k2, v2, cache2 = q.clone(), k.clone(), v.clone(), cache0.clone()
+    ws2 = torch.zeros(ws_bytes.value, dtype=torch.uint8, device=cuda)
+    outs = []
+    for _ in range(2):
+        out2 = torch.full((heads * dim,), float("nan"), device=cuda)
+        check(lib.hyq_rope_attention(P(q2), P(k2), P(v2), heads, kv_heads, dim, P(cos_d), P(sin_d), positions, P(p),
+                                     P(qn), P(kn), C.c_float(1e-5), norm_first, P(cache2[0]), P(cache2[1]), P(out2),
+                                     P(ws2), st))
+        outs.append(out2)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], out1) and torch.equal(outs[1], out1)
+    assert torch.equal(cache2, cache1)
+    assert torch.equal(q2, q) and torch.equal(k2, k) and torch.equal(v2, v)
+    assert not ws2[:positions * heads * 4].any()  # the per-(token, kv head) counters are left zero
+
+
+def test_rope_in_attention_model_stream_identical(cuda):
+    """DenseModel and DenseBatch with RoPE inside the attention launch give
+    the same greedy streams and logits as with the separate RoPE launch."""
+    import torch
+    from hy_mt_rs_b200 import quant
+    from hy_mt_rs_b200.model import DenseBatch, DenseConfig, DenseModel, random_weights
+
+    cfg = DenseConfig(layers=3, positions=96)
+    weights = random_weights(cfg, cuda, seed=21)
+    torch.cuda.synchronize()
+    rng = np.random.default_rng(21)
+    prompts = [rng.integers(0, cfg.vocab, n).tolist() for n in (60, 5, 70)]   # steps cross the 64 split
+    n_new = 10
+    stream = torch.cuda.Stream(cuda)
+    res = []
+    try:
+        for flag in (False, True):
+            model = DenseModel(cfg, weights, cuda, rope_in_attention=flag)
+            lg = torch.zeros(n_new, cfg.vocab, device=cuda)
+            ids = model.generate(prompts[0], n_new, stream, logits_out=lg, batched_prefill=True)
+            blg = torch.zeros(n_new, len(prompts), cfg.vocab, device=cuda)
+            bids = DenseBatch(model, len(prompts)).generate(prompts, n_new, stream, logits_out=blg)
+            res.append((ids, lg.cpu(), bids, blg.cpu()))
+    finally:
+        quant.set_launch_overlap(False)
+    (a_ids, a_lg, a_bids, a_blg), (b_ids, b_lg, b_bids, b_blg) = res
+    assert a_ids == b_ids and torch.equal(a_lg, b_lg)
+    assert a_bids == b_bids and torch.equal(a_blg, b_blg)
+    assert quant.device_status() == 0
+
+
 def test_add_rms_norm_bit_exact(cuda):
     """hyq_add_rms_norm = the residual add then rms_norm_into (model.rs:
     1043-1071, 785-830), bit for bit against the oracle's x86 order."""
