@@ -94,12 +94,15 @@ class _Acts:
 
 class DenseModel:
     """fused: run each token step as one persistent kernel
-    (hyq_dense_step_enqueue) instead of 7 launches per layer.
+    (hyq_dense_step_enqueue) instead of 8 launches per layer.
     rope_in_attention: single-token steps run RoPE + q/k norm + KV append
     inside the attention launch (hyq_rope_attention, bit-identical to
-    hyq_rope_qk + hyq_attention)."""
+    hyq_rope_qk + hyq_attention).  Off by default: every split CTA then
+    repeats the query heads' norm and RoPE on its own critical path, which
+    measured slower than the separate launch (1.528 vs 1.514 ms per token,
+    3.89 vs 3.69 ms per step of 64 requests)."""
 
-    def __init__(self, cfg, weights, device, prefill_chunk=PREFILL_CHUNK, fused=False, rope_in_attention=True):
+    def __init__(self, cfg, weights, device, prefill_chunk=PREFILL_CHUNK, fused=False, rope_in_attention=False):
         self.cfg = cfg
         self.rope_in_attention = rope_in_attention
         self.device = device
