@@ -826,12 +826,15 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
 }
 
 template <int FMT>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads1, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                  const __grid_constant__ Params p) {
   using L = Smem2<FMT>;
   constexpr int S = L::S;
   constexpr int NACC = 2 * kPairHalf;  // accumulator columns (the pair's tokens)
+  // stages released in pairs (one commit per two K steps), as gemm_kernel
+  static_assert(S % 2 == 0, "paired stage release");
+  auto rel = [](int s) { return s & ~1; };
   static_assert(NACC + 32 * S <= kTmemCols, "accumulator and A stages exceed tensor memory");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t raw_s = smem_addr(smem_raw);
@@ -852,7 +855,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = blockIdx.x * BM;  // this CTA's 128 rows (the pair covers 2 x 128)
   const int tokp = blockIdx.y * NACC;  // the pair's first token
-  const int steps_per_w = p.wcol / BK;
+  constexpr int steps_per_w = wcol_for(FMT) / BK;  // p.wcol
   const int kbeg = blockIdx.z * p.steps_per_split;
   const int nk = min(p.steps_per_split, p.K / BK - kbeg);
 
@@ -864,7 +867,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < WS; ++s) {
       mbar_init(wfull(s), 1);
-      mbar_init(wempty(s), kDequantWarps);
+      // every group with a K step in the block column releases it
+      mbar_init(wempty(s), min(kGroups, steps_per_w) * kGroupWarps);
     }
     mbar_init(accfull, 1);
     *abort_flag = 0;
@@ -904,7 +908,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++issued_w;
         }
         const int s = ks % S;
-        if (ks >= S && !mbar_wait(empty(s), ((ks / S) - 1) & 1, abort_flag)) {
+        if (ks >= S && !mbar_wait(empty(rel(s)), ((ks / S) - 1) & 1, abort_flag)) {
           ok = false;
           break;
         }
@@ -947,7 +951,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
             umma_f16_ts_pair(tmem, a0 + 8 * k, sw128_desc(b0 + 32 * k), idesc, (ks > 0 || k > 0) ? 1u : 0u);
-          umma_commit_pair(empty(s));
+          if ((ks & 1) || ks == nk - 1) umma_commit_pair(empty(rel(s)));
         }
         __syncwarp();
       }
@@ -956,57 +960,73 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // --------------------------- dequant + epilogue ---------------------------
-    const int grp = (warp - 2) / kGroupWarps;
+    const int grp = (warp - 2) / kGroupWarps;  // K steps grp, grp + kGroups, ...
     const int r = (warp & 3) * 32 + lane;  // weight row of this CTA's half = TMEM lane
     const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
-    for (int ks = grp; ks < nk; ks += 2) {
+    const int gsh = p.g == 1 ? 0 : p.g == 2 ? 1 : p.g == 4 ? 2 : 3;  // g = 1, 2, 4 or 8
+    const int jc = r & (p.g - 1);
+    const uint32_t row_off = (uint32_t)((jc * (BM >> gsh) + (r >> gsh)) * p.wbox);
+    const int64_t skew0 = (int64_t)jc * p.row_bytes;
+    const int64_t kb0 = kbeg / steps_per_w;
+    for (int ks = grp; ks < nk; ks += kGroups) {
       const int wb = ks / steps_per_w, ws = wb % WS;
       bool ok = true;
-      if (ks % steps_per_w == grp) ok = mbar_wait(wfull(ws), (wb / WS) & 1, abort_flag);
+      if (ks % steps_per_w < kGroups) ok = mbar_wait(wfull(ws), (wb / WS) & 1, abort_flag);
       const int s = ks % S;
-      if (ok && ks >= S) ok = mbar_wait(empty(s), ((ks / S) - 1) & 1, abort_flag);
+      if (ok && ks >= S) ok = mbar_wait(empty(rel(s)), ((ks / S) - 1) & 1, abort_flag);
       if (!ok) {
         atomicOr(p.status, DEV_TIMEOUT_FULL);
         *abort_flag = 1;
         break;
       }
       tc_fence_after();
-      const int64_t kb = (kbeg + ks) / steps_per_w;
-      const int jc = r % p.g;
-      const int skew = (int)(((int64_t)jc * p.row_bytes + kb * p.wbytes) & 15);
-      const uint32_t rowp = base + L::w + ws * L::w_stage + (jc * (BM / p.g) + r / p.g) * p.wbox + skew;
+      const int skew = (int)((skew0 + (kb0 + wb) * wbytes_for(FMT)) & 15);
+      const uint32_t rowp = base + L::w + ws * L::w_stage + row_off + skew;
       uint32_t o[32];
-      decode64<FMT>(rowp, (kbeg + ks) % steps_per_w, o);
+      decode64<FMT>(rowp, ks % steps_per_w, o);
       tmem_st32(tmem + lane_base + (uint32_t)(NACC + 32 * s), o);
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive_cluster(afull(s), 0);
-        if (ks % steps_per_w >= steps_per_w - 2 || ks + 2 >= nk) mbar_arrive(wempty(ws));
+        if (ks % steps_per_w >= steps_per_w - kGroups || ks + kGroups >= nk) mbar_arrive(wempty(ws));
       }
     }
-    if (warp < 6) {
+    {
+      // all dequant warps: group g reads the pair's token columns [g NACC /
+      // kGroups, (g + 1) NACC / kGroups), 32 at a time (two loads, one wait)
       const bool ok = mbar_wait(accfull, 0, nullptr);
       tc_fence_after();
       if (ok && !*abort_flag) {
         const int q = warp & 3;
         const int row = row0 + 32 * q + lane;
         float* yz = p.y + (size_t)blockIdx.z * p.M * p.N;
+        constexpr int kCols = NACC / kGroups;
+        static_assert(kCols % 32 == 0, "32-column epilogue batches");
+        const int cbeg = grp * kCols, cend = min(cbeg + kCols, p.M - tokp);
 #pragma unroll 1
-        for (int c0 = 0; c0 < NACC; c0 += 16) {
-          uint32_t v[16];
+        for (int c0 = cbeg; c0 < cend; c0 += 32) {
+          uint32_t v[32];
+          const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0;
           asm volatile(
               "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
               "%14, %15}, [%16];"
               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
                 "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
                 "=r"(v[15])
-              : "r"(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0));
+              : "r"(ta));
+          asm volatile(
+              "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+              "%14, %15}, [%16];"
+              : "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]),
+                "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]),
+                "=r"(v[30]), "=r"(v[31])
+              : "r"(ta + 16u));
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
           if (row < p.N) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
+            for (int i = 0; i < 32; ++i) {
               const int tok = tokp + c0 + i;
               if (tok < p.M) yz[(size_t)tok * p.N + row] = __uint_as_float(v[i]);
             }
@@ -1106,7 +1126,7 @@ cudaError_t run_pair(const CUtensorMap& tw, const CUtensorMap& tx, const Params&
   attr[0].val.clusterDim.z = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(p.N / BM), (unsigned)((p.M + 2 * kPairHalf - 1) / (2 * kPairHalf)), (unsigned)splits);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(kThreads1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cfg.attrs = attr;
@@ -1114,14 +1134,15 @@ cudaError_t run_pair(const CUtensorMap& tw, const CUtensorMap& tx, const Params&
   return cudaLaunchKernelEx(&cfg, k, tw, tx, p);
 }
 
-// The 2-SM kernel serves tiles of 256 tokens when the rows pair up and the
-// process opted in (HYQ_GEMM_PAIR=1): measured on B200 it ties the 1-SM
-// kernel at 2048 tokens (gate 311 vs 309 us, down 376 vs 383 us) and trails
-// it at 512-1024 tokens, so the 1-SM kernel stays the default.
+// The 2-SM kernel serves single-matrix Q4_K / Q6_K products of at least 256
+// tokens whose rows pair up: with four dequant groups it does twice the
+// weights per MMA instruction and measured 777 vs 753 TFLOP/s (7B layer at
+// 2048 tokens) and 575 vs 560 (512 tokens) against the 1-SM kernel.
+// HYQ_GEMM_PAIR=0 turns it off.
 bool use_pair(int64_t N, int64_t M) {
   static const int enabled = [] {
     const char* e = getenv("HYQ_GEMM_PAIR");
-    return (e && e[0] == '1') ? 1 : 0;
+    return (e && e[0] == '0') ? 0 : 1;
   }();
   return enabled && M >= 256 && N % (2 * BM) == 0;
 }

@@ -53,9 +53,11 @@ def test_gemm_7b_shapes(cuda, t, N, K, M):
 PAIR_CASES = [(Q4_K, 512, 1024, 256), (Q6_K, 768, 1024, 300), (Q6_K, 2048, 7168, 512), (Q4_K, 1024, 4096, 1000)]
 
 
-def test_gemm_pair_tiles(cuda):
-    """The opt-in 2-SM kernel (HYQ_GEMM_PAIR=1 is read once per process, so
-    the cases run in a child process)."""
+@pytest.mark.parametrize("pair", ["1", "0"])
+def test_gemm_pair_tiles(cuda, pair):
+    """Single-matrix Q4_K / Q6_K products from 256 tokens on the 2-SM kernel
+    (the default) and, with HYQ_GEMM_PAIR=0, on the 1-SM kernel.  The switch
+    is read once per process, so the cases run in a child process."""
     import os
     import subprocess
     import sys
@@ -67,7 +69,7 @@ def test_gemm_pair_tiles(cuda):
             "dev = torch.device('cuda', 0)\n"
             "for c in T.PAIR_CASES: T.run_case(dev, *c, seed=c[1] + c[3])\n"
             "print('ok')\n") % (ROOT, os.path.join(ROOT, "tests"))
-    env = dict(os.environ, HYQ_GEMM_PAIR="1")
+    env = dict(os.environ, HYQ_GEMM_PAIR=pair)
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-3000:]
 
