@@ -1177,12 +1177,42 @@ struct ReduceArgs {
   int seg_col0[3];
   int seg_rows[3];
   float* ys[3];
+  int vec4;  // four columns per thread (every column boundary and output 16-byte aligned)
 };
+
+__device__ __forceinline__ float4 add4(float4 a, float4 b) {
+  return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+}
+__device__ __forceinline__ float silu_mul(float g, float u) { return __fdividef(g, 1.0f + __expf(-g)) * u; }
 
 __global__ void __launch_bounds__(256) reduce_splits_kernel(const __grid_constant__ ReduceArgs a) {
   grid_dependency_wait();
   allow_dependents_launch();
   const int cols = a.gate_up ? a.seg_rows[0] : a.N;
+  if (a.vec4) {
+    // the same sums, four columns at a time (16-byte loads in flight)
+    const int c4 = cols >> 2;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= a.M * c4) return;
+    const int64_t tok = i / c4;
+    const int c = 4 * (int)(i - tok * c4);
+    const int64_t n = a.M * a.N;
+    const float* src = a.part + tok * a.N + c;
+    float4 s = *reinterpret_cast<const float4*>(src);
+    for (int z = 1; z < a.splits; ++z) s = add4(s, *reinterpret_cast<const float4*>(src + (int64_t)z * n));
+    if (a.gate_up) {
+      const float* su = src + a.seg_rows[0];
+      float4 u = *reinterpret_cast<const float4*>(su);
+      for (int z = 1; z < a.splits; ++z) u = add4(u, *reinterpret_cast<const float4*>(su + (int64_t)z * n));
+      *reinterpret_cast<float4*>(a.ys[0] + tok * a.seg_rows[0] + c) =
+          make_float4(silu_mul(s.x, u.x), silu_mul(s.y, u.y), silu_mul(s.z, u.z), silu_mul(s.w, u.w));
+      return;
+    }
+    int m = 0;
+    while (m + 1 < a.n_seg && c >= a.seg_col0[m + 1]) ++m;
+    *reinterpret_cast<float4*>(a.ys[m] + tok * a.seg_rows[m] + (c - a.seg_col0[m])) = s;
+    return;
+  }
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= a.M * cols) return;
   const int64_t tok = i / cols;
@@ -1195,7 +1225,7 @@ __global__ void __launch_bounds__(256) reduce_splits_kernel(const __grid_constan
     const float* su = src + a.seg_rows[0];
     float u = su[0];
     for (int z = 1; z < a.splits; ++z) u += su[(int64_t)z * n];
-    a.ys[0][tok * a.seg_rows[0] + c] = __fdividef(s, 1.0f + __expf(-s)) * u;  // as in the GEMM epilogue
+    a.ys[0][tok * a.seg_rows[0] + c] = silu_mul(s, u);  // as in the GEMM epilogue
     return;
   }
   int m = 0;
@@ -1418,7 +1448,13 @@ cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) 
     r.seg_rows[m] = p.seg_rows[m];
     r.ys[m] = p.ys[m];
   }
-  const int64_t n = M * (j.gate_up ? j.rows[0] : lay.ncols);
+  // four columns per thread when no float4 crosses a matrix boundary and
+  // every output row starts 16-byte aligned
+  bool v4 = lay.ncols % 4 == 0;
+  for (int m = 0; m < r.n_seg; ++m)
+    v4 = v4 && r.seg_col0[m] % 4 == 0 && r.seg_rows[m] % 4 == 0 && (reinterpret_cast<uintptr_t>(r.ys[m]) & 15) == 0;
+  r.vec4 = v4 ? 1 : 0;
+  const int64_t n = M * (j.gate_up ? j.rows[0] : lay.ncols) / (v4 ? 4 : 1);
   return launch_ex(reduce_splits_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, r);
 }
 
