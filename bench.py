@@ -1013,7 +1013,8 @@ def model_arm(a):
                   "batch 1, greedy)",
         "value": round(tok_s, 1), "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": max(3, a.warmup),
         "ms_per_step": round(ms_decode / steps, 4), "higher_is_better": True, "scaling": "weak",
-        # the reference's published 1.8B Q2_0C decode rate, one request (M2 Pro)
+        # the reference's published 1.8B Q2_0C decode rate, one request on an M2 Pro
+        # (docs/validation.md:70-71 of hy-mt-rs)
         "vs_baseline": round(tok_s / 86.86, 2), "vs_baseline_number": "86.86 tokens/s, 1.8B Q2_0C, 1 request",
         "dtype": "f32 activations x packed int weights; f32 KV cache",
         "data": "synthetic (seeded random-init weights, 256 seeded random prompt ids)",

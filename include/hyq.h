@@ -92,7 +92,8 @@ int hyq_weight_wrap(const void* packed_device, size_t byte_len, int dtype, int n
 int hyq_weight_expert(const hyq_weight* w, int64_t index, hyq_weight** out);
 
 /* Tensor-parallel shard of a [K, N] matrix (no counterpart in the CPU
- * reference; the split SURVEY's dense TP plan uses for 7B layers).
+ * reference; the split a dense tensor-parallel 7B layer uses: column-parallel
+ * QKV / gate / up / lm_head, row-parallel O / down).
  *   axis 0 (column-parallel: QKV, gate/up, lm_head): output rows
  *     [part*N/parts, (part+1)*N/parts), a view of the parent's bytes (the
  *     parent must outlive it); N % parts == 0.
