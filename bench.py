@@ -614,10 +614,27 @@ def prefill_arm(a):
     stream.synchronize()
     torch.cuda.synchronize(dev)
     sampler.stop()
+    # e2e: every step copies its activations in from pinned host memory, runs
+    # the layer's products through the public calls and reads the layer's
+    # output (the down projection) back
+    xh = {K: v.cpu().pin_memory() for K, v in xs.items()}
+    yh = torch.empty(M, 4096).pin_memory()
+    e2e_steps = max(3, a.steps // 4)
+    with torch.cuda.stream(stream):
+        stream.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            for K in xs:
+                xs[K].copy_(xh[K], non_blocking=True)
+            step()
+            yh.copy_(outs["ffn_down"], non_blocking=True)
+        stream.synchronize()
+        e2e_s = (time.perf_counter() - t0) / e2e_steps
+    h2d = sum(v.numel() * 4 for v in xs.values())
     if world > 1:
         dist.barrier()
-    (ms_total, failed), clocks_all = reduce_over_ranks([e0.elapsed_time(e1), device_failed(quant, dev)],
-                                                       sampler.summary(), dev)
+    (ms_total, failed, e2e_s), clocks_all = reduce_over_ranks(
+        [e0.elapsed_time(e1), device_failed(quant, dev), e2e_s], sampler.summary(), dev)
     if failed:
         raise RuntimeError("a kernel reported an expired bounded wait (device status word) on some rank")
     ms = ms_total / a.steps
@@ -658,6 +675,10 @@ def prefill_arm(a):
                      "traffic": profile_traffic(f"gemm_gate_up_m{M}"), "avg_launch_ms": round(gate, 5)},
         "per_projection_ms": {k: round(v, 5) for k, v in per_ms.items()},
         "prefill_tok_s_layer": round(job_rate(M, 1, world, ms), 1),
+        "e2e": {"value": round(job_rate(flops, 1, world, e2e_s * 1e3) / 1e12, 2), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": M * 4096 * 4,
+                "how": "each step: both activation matrices in from pinned host memory, the four layer calls, "
+                       "the down projection's output back"},
         "gpu_launches": launches,
         "clocks": clocks,
     }
@@ -1130,6 +1151,17 @@ def batch_arm(a):
     step_s = ms_decode / steps * 1e-3
     peak, peak_kind = measured_peaks()
     sm = [c["sm_mhz"] for c in clocks_all if c.get("sm_mhz")]
+    # CPU baseline: the reference serves concurrent requests as separate
+    # sessions on the host cores; the oracle's x86 step on all host threads,
+    # a bounded sample of one request's steps
+    from oracle.model import DenseOracle
+    oracle = DenseOracle(DenseConfig(layers=N_LAYERS_MODEL, positions=8), weights, threads=host_threads())
+    t0 = time.perf_counter()
+    n_cpu = 0
+    while n_cpu < 8 and (n_cpu == 0 or time.perf_counter() - t0 < 20.0):
+        oracle.step(prompts[0][n_cpu], n_cpu)
+        n_cpu += 1
+    cpu_s = (time.perf_counter() - t0) / n_cpu
     line = {
         "metric": f"decode tokens/s (random-init Hy-MT2-1.8B architecture, Q2_0C linears, Q6_K tied embedding, "
                   f"{B} concurrent requests, greedy)",
@@ -1154,6 +1186,9 @@ def batch_arm(a):
         "clocks": {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": clocks_all[0].get("sm_max_mhz"),
                    "reasons": sorted({r for c in clocks_all for r in c.get("reasons", [])}),
                    "samples": sum(c.get("samples", 0) for c in clocks_all)},
+        "cpu_baseline": {"value": round(1.0 / cpu_s, 3), "unit": "tokens/s", "cores": host_threads(), "kind": "port",
+                         "sample": f"{n_cpu} decode steps of one request through oracle/model.py (x86 f32 order, "
+                                   "OpenMP over all host threads; concurrent sessions share those cores)"},
     }
     print(json.dumps(line), flush=True)
     return 0
