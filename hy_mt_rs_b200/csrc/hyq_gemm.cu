@@ -1135,10 +1135,10 @@ cudaError_t run_pair(const CUtensorMap& tw, const CUtensorMap& tx, const Params&
 }
 
 // The 2-SM kernel serves single-matrix Q4_K / Q6_K products of at least 256
-// tokens whose rows pair up: with four dequant groups it does twice the
-// weights per MMA instruction and measured 777 vs 753 TFLOP/s (7B layer at
-// 2048 tokens) and 575 vs 560 (512 tokens) against the 1-SM kernel.
-// HYQ_GEMM_PAIR=0 turns it off.
+// tokens whose rows pair up.  With four dequant groups the 7B layer measured
+// 777 vs 753 TFLOP/s (2048 tokens) and 575 vs 560 (512 tokens) against the
+// 1-SM kernel; per SM its K step takes the same time (the tensor pipe is
+// throughput-bound at N = 256).  HYQ_GEMM_PAIR=0 turns it off.
 bool use_pair(int64_t N, int64_t M) {
   static const int enabled = [] {
     const char* e = getenv("HYQ_GEMM_PAIR");
