@@ -541,19 +541,12 @@ LAYER_7B = [("attn_q", 4096, 4096, 2), ("attn_k", 1024, 4096, 2), ("attn_v", 102
             ("ffn_down", 4096, 14336, 3)]  # (name, N, K, dtype): Q4_K_M-style, Q6_K down
 
 
-def gemm_launches(row_tiles, K, M, sms):
+def gemm_launches(row_tiles, K, M, sms, dtype=2):
     """Kernel launches of one batched product in libhyq (hyq_gemm.cu): the
-    fp16 activation copy, the GEMM, and the split-K reduction when the grid
-    of row tiles x (256|128)-token tiles is smaller than the SM count."""
-    bn = 256 if M >= 256 else 128
-    tiles = row_tiles * -(-M // bn)
-    nwb = K // 256
-    z = 1
-    if tiles < sms:
-        z = max(1, min(-(-sms // tiles), nwb, 16))
-    per = -(-nwb // z)
-    splits = -(-nwb // per)
-    return 2 + (1 if splits > 1 else 0)
+    fp16 activation copy, the GEMM, and the split-K reduction when it splits
+    (the library's rule, mirrored in hy_mt_rs_b200.quant.gemm_splits)."""
+    from hy_mt_rs_b200 import quant
+    return quant.gemm_launches(row_tiles, K, M, dtype, sms)
 
 
 def prefill_arm(a):
@@ -648,7 +641,7 @@ def prefill_arm(a):
               "samples": sum(c.get("samples", 0) for c in clocks_all)}
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     launches = (gemm_launches(32 + 8 + 8, 4096, M, sms) + gemm_launches(32, 4096, M, sms)
-                + gemm_launches(14336 // 64, 4096, M, sms) + gemm_launches(32, 14336, M, sms)) * a.steps
+                + gemm_launches(14336 // 64, 4096, M, sms) + gemm_launches(32, 14336, M, sms, dtype=3)) * a.steps
     per_ms = {k: statistics.fmean(b.elapsed_time(c) for b, c in v) for k, v in per.items()}
     gate = per_ms["ffn_gate_up_silu"]
     gate_flops = 2 * 2 * M * 14336 * 4096

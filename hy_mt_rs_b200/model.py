@@ -412,13 +412,23 @@ class DenseBatch:
         check(lib.hyq_matmul(m.output.handle, _p(a.normalized), B, _p(self.logits), st))
         check(lib.hyq_argmax_rows(_p(self.logits), cfg.vocab, B, _p(self.tokens), _p(self.pos), st))
 
-    def launches(self):
+    def launches(self, sms=148):
         """Kernel launches of one step: QKV / O / gate-up / down / lm_head as
-        batched products (2 launches each on the tensor cores from 16
-        requests: activation conversion + GEMM)."""
-        per_product = 2 if self.B >= 16 else self.B
-        per_layer = (3 if self.m.rope_in_attention else 4) + 4 * per_product
-        return 2 + self.m.cfg.layers * per_layer + per_product + 1
+        batched products (on the tensor cores from 16 requests: activation
+        conversion + GEMM + split-K reduction when the product splits;
+        below 16, one batch-1 product per request)."""
+        cfg, B = self.m.cfg, self.B
+        t = cfg.linear_dtype
+        KV = cfg.kv_heads * cfg.head_dim
+        if B >= 16:
+            g = lambda tiles, K, dt=t: quant.gemm_launches(tiles, K, B, dt, sms)  # noqa: E731
+            products = (g((cfg.heads * cfg.head_dim + 2 * KV) // 128, cfg.hidden) + g(cfg.hidden // 128, cfg.hidden)
+                        + g(2 * cfg.ffn // 128, cfg.hidden) + g(cfg.hidden // 128, cfg.ffn))
+            lm_head = g(-(-cfg.vocab // 128), cfg.hidden, cfg.embed_dtype)
+        else:
+            products, lm_head = 4 * B, B
+        per_layer = (3 if self.m.rope_in_attention else 4) + products
+        return 2 + cfg.layers * per_layer + lm_head + 1
 
     def capture(self, stream):
         quant.set_launch_overlap(True)

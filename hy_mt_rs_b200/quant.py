@@ -393,3 +393,28 @@ def device_status(device=None):
 
 
 del _native
+
+
+# K columns of one packed block column of the tensor-core GEMM (hyq_gemm.cu wcol_for)
+GEMM_BLOCK_COLUMN = {DType.Q8_0: 128, DType.Q2_0C: 512, DType.Q4_K: 256, DType.Q6_K: 256, DType.STQ1_0: 256}
+
+
+def gemm_splits(row_tiles, K, M, dtype, sms=148):
+    """Split-K slices the tensor-core product takes (hyq_gemm.cu
+    choose_splits): token tiles of 64 / 128 / 256 by batch size; a grid of
+    row tiles x token tiles smaller than the SM count is split into whole
+    block columns, within one wave of CTAs, at most 16 ways."""
+    bn = 256 if M >= 256 else 128 if M > 64 else 64
+    tiles = row_tiles * -(-M // bn)
+    nwb = K // GEMM_BLOCK_COLUMN[dtype]
+    if tiles >= sms:
+        return 1
+    z = max(1, min(sms // tiles, nwb, 16))
+    per = -(-nwb // z)
+    return -(-nwb // per)
+
+
+def gemm_launches(row_tiles, K, M, dtype, sms=148):
+    """Kernel launches of one tensor-core product (batch >= 16): the fp16
+    activation copy, the GEMM, and the split-K reduction when it splits."""
+    return 2 + (1 if gemm_splits(row_tiles, K, M, dtype, sms) > 1 else 0)

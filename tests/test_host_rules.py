@@ -1,0 +1,32 @@
+"""Host-side rules mirrored in Python, on CPU: the tensor-core product's
+split-K choice (hyq_gemm.cu choose_splits / token_tile) that the bench's
+launch counts rely on, checked against the grids the ncu launch lists of
+the 64-request decode step and of MoE decode recorded (grid.z = slices)."""
+import pytest
+
+from hy_mt_rs_b200.quant import DType, gemm_launches, gemm_splits
+
+Q2C, Q4K, Q6K = DType.Q2_0C, DType.Q4_K, DType.Q6_K
+
+
+@pytest.mark.parametrize("tiles,K,M,dtype,splits", [
+    (24, 2048, 64, Q2C, 4),     # 1.8B QKV at 64 requests: grid (24, 1, 4)
+    (16, 2048, 64, Q2C, 4),     # O: (16, 1, 4)
+    (96, 2048, 64, Q2C, 1),     # gate/up pair tiles: (96, 1, 1)
+    (16, 6144, 64, Q2C, 6),     # down: (16, 1, 6)
+    (944, 2048, 64, Q6K, 1),    # lm_head: (944, 1, 1)
+    (16, 2048, 64, Q4K, 8),     # MoE shared gate/up at 64 tokens: (16, 1, 8)
+    (16, 1024, 64, Q4K, 4),     # MoE shared down: (16, 1, 4)
+    (48, 4096, 2048, Q4K, 1),   # 7B QKV at 2048 tokens: 384 tiles, no split
+    (32, 4096, 512, Q4K, 2),    # 7B O at 512 tokens: 64 tiles, two slices in one wave
+])
+def test_gemm_splits_match_recorded_grids(tiles, K, M, dtype, splits):
+    assert gemm_splits(tiles, K, M, dtype) == splits
+    assert gemm_launches(tiles, K, M, dtype) == 2 + (splits > 1)
+
+
+def test_split_grid_stays_within_one_wave():
+    for tiles in range(1, 148):
+        for K, dtype in ((2048, Q2C), (6144, Q2C), (4096, Q4K), (14336, Q6K)):
+            z = gemm_splits(tiles, K, 64, dtype)
+            assert 1 <= z <= 16 and tiles * z <= max(148, tiles)
