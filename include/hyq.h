@@ -272,7 +272,9 @@ int hyq_attention(const float* q, const float* k_cache, const float* v_cache, in
                   void* stream);
 
 /* The same for `seqs` independent sequences decoding one token each
- * (concurrent requests): token t is sequence t at position pos[t] (device
+ * (concurrent requests: separate Sessions over one shared Model,
+ * README.md:139-141; per sequence, rope_with_cache model.rs:874-913 and
+ * attention_into model.rs:949-1021): token t is sequence t at position pos[t] (device
  * int32 [seqs]) with its caches at k_cache/v_cache + t * seq_stride floats
  * (seq_stride >= positions * kv_heads * head_dim); seqs <= positions.  The
  * attention workspace is hyq_attention_workspace_bytes(..., positions, seqs). */
@@ -284,8 +286,9 @@ int hyq_attention_seqs(const float* q, const float* k_cache, const float* v_cach
                        int head_dim, int64_t positions, const int32_t* pos, int64_t seqs, int64_t seq_stride,
                        float* out, void* workspace, void* stream);
 
-/* One decode step's RoPE + q/k RMSNorm + KV append (hyq_rope_qk) and
- * attention (hyq_attention) in one launch, bit-identical to the two calls:
+/* One decode step's RoPE + q/k RMSNorm + KV append (hyq_rope_qk;
+ * model.rs:429-446, 874-913) and attention (hyq_attention; model.rs:949-1021)
+ * in one launch, bit-identical to the two calls:
  * q, k and v are the step's raw projections (q [heads * head_dim], k and v
  * [kv_heads * head_dim]; left unchanged), the position is read from `pos`,
  * the rotated key and the value are appended to the caches at it, and the
