@@ -232,17 +232,35 @@ def run_cpu(seconds, lm_rows):
         if el >= seconds:
             break
     gbs = n * cpu_step_bytes(lm_rows) / el / 1e9
+    what = "the whole chain" if lm_rows == VOCAB else f"the chain with the lm_head cut to {lm_rows} of {VOCAB} rows"
     return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{n} passes of the full chain with the lm_head cut to {lm_rows} of {VOCAB} rows "
-                      f"({el:.1f} s); oracle/hyq_oracle.c x86 f32 order, OpenMP"}
+            "sample": f"{n} passes of {what} ({el:.1f} s); oracle/hyq_oracle.c x86 f32 order, OpenMP"}
+
+
+METRIC = "quantized GEMV HBM GB/s (1.8B layer projections Q2_0C+STQ1_0 + Q6_K lm_head, batch 1)"
+
+
+def decode_config(a, world):
+    """The `config` of the default line, shared verbatim by both arms."""
+    return {"workload": "hy-mt-rs config 2: 1.8B decoder-layer projections (Q2_0C, STQ1_0) + "
+                        "Q6_K lm_head 120832x2048, batch 1",
+            "path": a.path, "layer_copies": max(1, a.copies),
+            "step_bytes": layer_bytes(5) + layer_bytes(6) + gemv_bytes(3, VOCAB, HIDDEN),
+            "launch_overlap": not a.no_overlap,
+            "l2": "inputs larger than L2: every step streams the 203 MB lm_head; layers rotate copies",
+            "parallelism": f"replicas x{world} (rows are independent; no collective)"}
 
 
 def reference_arm(a):
+    """The reference's CPU path (the oracle port of its x86 f32 path, all host
+    threads) on the default line's workload: every step is the whole chain,
+    both layers and all 120832 lm_head rows.  Under torchrun rank 0 alone
+    runs it.  Loads no GPU library."""
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return 0
-    lm_rows = VOCAB // 16
-    layers, lm, lm_rows, x = cpu_workload(lm_rows=lm_rows)
+    layers, lm, lm_rows, x = cpu_workload()
     threads = host_threads()
     for _ in range(a.warmup):
         cpu_step(layers, lm, lm_rows, x, threads)
@@ -251,15 +269,16 @@ def reference_arm(a):
         cpu_step(layers, lm, lm_rows, x, threads)
     el = time.perf_counter() - t0
     gbs = a.steps * cpu_step_bytes(lm_rows) / el / 1e9
-    sample = (f"each step: both layers in full + lm_head rows 0..{lm_rows} of {VOCAB} "
-              f"(CPU port of the reference's x86 f32 path, oracle/hyq_oracle.c)")
+    sample = (f"each step: the whole chain (both layers, all {VOCAB} lm_head rows), the CPU port of the "
+              f"reference's x86 f32 path (oracle/hyq_oracle.c, OpenMP)")
     line = {
-        "metric": "quantized GEMV HBM GB/s (1.8B layer projections Q2_0C+STQ1_0 + Q6_K lm_head, batch 1)",
-        "value": round(gbs, 3), "unit": "GB/s", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
-        "ms_per_step": round(el / a.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "hy-mt-rs config 2: 1.8B decoder-layer projections (Q2_0C, STQ1_0) + Q6_K lm_head "
-                               "120832x2048, batch 1", "path": "f32"},
+        "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": a.gpus, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": round(el / a.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 activations x packed int weights (f32 accumulate)" if a.path == "f32"
+                 else "int8 activations (Q8, per-256 scale) x packed int weights",
+        "data": "synthetic (seeded N(0,0.02) weights packed by hy_mt_rs_b200.synth; N(0,1) activations)",
+        "config": decode_config(a, world),
         "impl": "reference",
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": sample},
@@ -367,7 +386,7 @@ def gpu_arm(a):
 
     world, rank, dev = init_ranks()
 
-    import hy_mt_rs_b200  # noqa: F401
+    import hy_mt_rs_b200.quant  # noqa: F401  (loads libhyq.so or raises)
     from hy_mt_rs_b200 import quant
 
     copies = max(1, a.copies)
@@ -491,19 +510,14 @@ def gpu_arm(a):
         reasons = sorted({r for c in clocks_all for r in c.get("reasons", [])})
         kernel_key = f"lm_head_{path}"
         line = {
-            "metric": "quantized GEMV HBM GB/s (1.8B layer projections Q2_0C+STQ1_0 + Q6_K lm_head, batch 1)",
+            "metric": METRIC,
             "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
             "ms_per_step": round(ms / a.steps, 5), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None,
-            "dtype": "f32 activations x packed int weights (exact int32 dp4a, f32 accumulate)" if path == "f32"
+            "dtype": "f32 activations x packed int weights (f32 accumulate)" if path == "f32"
                      else "int8 activations (Q8, per-256 scale) x packed int weights",
             "data": "synthetic (seeded N(0,0.02) weights packed by hy_mt_rs_b200.synth; N(0,1) activations)",
-            "config": {"workload": "hy-mt-rs config 2: 1.8B decoder-layer projections (Q2_0C, STQ1_0) + "
-                                   "Q6_K lm_head 120832x2048, batch 1",
-                       "path": path, "layer_copies": copies, "step_bytes": step_bytes,
-                       "launch_overlap": not a.no_overlap,
-                       "l2": "inputs larger than L2: every step streams the 203 MB lm_head; layers rotate copies",
-                       "parallelism": f"replicas x{world} (rows are independent; no collective)"},
+            "config": decode_config(a, world),
             "roofline": {"bound": "hbm", "kernel": f"lm_head Q6_K {path} GEMV", "achieved": round(achieved, 1),
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": profile_traffic(kernel_key),
@@ -523,7 +537,7 @@ def gpu_arm(a):
                        "samples": sum(c.get("samples", 0) for c in clocks_all)},
         }
         if world == 1:
-            line["cpu_baseline"] = run_cpu(a.cpu_seconds, VOCAB // 16)
+            line["cpu_baseline"] = run_cpu(a.cpu_seconds, VOCAB)
         print(json.dumps(line), flush=True)
     for g in list(graphs.values()) + [g_lm]:
         del g
@@ -554,7 +568,7 @@ def prefill_arm(a):
     import torch.distributed as dist
 
     world, rank, dev = init_ranks()
-    import hy_mt_rs_b200  # noqa: F401
+    import hy_mt_rs_b200.quant  # noqa: F401  (loads libhyq.so or raises)
     from hy_mt_rs_b200 import quant, synth
 
     M = a.tokens
@@ -737,7 +751,7 @@ def gemv_arm(a):
     import torch
 
     world, rank, dev = init_ranks()
-    import hy_mt_rs_b200  # noqa: F401
+    import hy_mt_rs_b200.quant  # noqa: F401  (loads libhyq.so or raises)
 
     peak, peak_kind = measured_peaks()
     sampler = ClockSampler("GPU-" + str(torch.cuda.get_device_properties(dev).uuid))
@@ -800,7 +814,7 @@ def tp_arm(a):
     import torch.distributed as dist
 
     world, rank, dev = init_ranks()
-    import hy_mt_rs_b200  # noqa: F401
+    import hy_mt_rs_b200.quant  # noqa: F401  (loads libhyq.so or raises)
     from hy_mt_rs_b200 import quant, synth
 
     full = {}
@@ -924,7 +938,7 @@ def model_arm(a):
     import torch
 
     world, rank, dev = init_ranks()
-    import hy_mt_rs_b200  # noqa: F401
+    import hy_mt_rs_b200.quant  # noqa: F401  (loads libhyq.so or raises)
     from hy_mt_rs_b200 import quant
     from hy_mt_rs_b200.model import DenseConfig, DenseModel, random_weights
 
@@ -1068,7 +1082,7 @@ def batch_arm(a):
     import torch
 
     world, rank, dev = init_ranks()
-    import hy_mt_rs_b200  # noqa: F401
+    import hy_mt_rs_b200.quant  # noqa: F401  (loads libhyq.so or raises)
     from hy_mt_rs_b200 import quant
     from hy_mt_rs_b200.model import DenseBatch, DenseConfig, DenseModel, random_weights
 
@@ -1198,7 +1212,7 @@ def moe_arm(a):
     import torch
 
     world, rank, dev = init_ranks()
-    import hy_mt_rs_b200  # noqa: F401
+    import hy_mt_rs_b200.quant  # noqa: F401  (loads libhyq.so or raises)
     from hy_mt_rs_b200 import quant
     from hy_mt_rs_b200.moe import MoeConfig, MoeLayer, random_moe_weights
 

@@ -70,18 +70,39 @@ int status_ptr(unsigned** out) {
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-// Keep stream-ordered workspace memory cached in the device's default pool
-// between calls instead of returning it to the driver at every sync.
-void ensure_pool() {
-  static bool done[kMaxDevices] = {};
+// Stream-ordered workspace of the tensor-core products.  Outside stream
+// capture it comes from a memory pool the library owns (one per device,
+// created on first use, its release threshold at the maximum so that freed
+// workspace stays cached between calls instead of going back to the driver
+// at every synchronization).  The device's default pool, and its settings,
+// belong to the caller and are left alone.  Under capture the allocation
+// becomes a graph memory node (graph-owned memory), as cudaMallocAsync gives.
+cudaError_t ws_alloc(void** p, size_t bytes, cudaStream_t st) {
+  static std::mutex mu;
+  static cudaMemPool_t pools[kMaxDevices] = {};
+  static bool made[kMaxDevices] = {};
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(st, &cap);
+  if (e != cudaSuccess) return e;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices || done[dev]) return;
-  cudaMemPool_t pool;
-  if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
-    uint64_t keep = UINT64_MAX;
-    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if (cap != cudaStreamCaptureStatusNone || dev < 0 || dev >= kMaxDevices) return cudaMallocAsync(p, bytes, st);
+  cudaMemPool_t pool = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!made[dev]) {
+      cudaMemPoolProps props = {};
+      props.allocType = cudaMemAllocationTypePinned;
+      props.location.type = cudaMemLocationTypeDevice;
+      props.location.id = dev;
+      if ((e = cudaMemPoolCreate(&pools[dev], &props)) != cudaSuccess) return e;
+      uint64_t keep = UINT64_MAX;
+      if ((e = cudaMemPoolSetAttribute(pools[dev], cudaMemPoolAttrReleaseThreshold, &keep)) != cudaSuccess) return e;
+      made[dev] = true;
+    }
+    pool = pools[dev];
   }
-  done[dev] = true;
+  return cudaMallocFromPoolAsync(p, bytes, pool, st);
 }
 
 // hyq_set_launch_overlap: batch-1 products launch as programmatic dependents
@@ -382,8 +403,7 @@ int hyq_matmul(const hyq_weight* w, const float* input, int64_t batch, float* ou
     if ((rc = status_ptr(&status))) return rc;
     cudaStream_t st = (cudaStream_t)stream;
     void* ws = nullptr;
-    ensure_pool();
-    cudaError_t e = cudaMallocAsync(&ws, hyq::gemm_workspace_bytes(w->dtype, K, N, batch), st);
+    cudaError_t e = ws_alloc(&ws, hyq::gemm_workspace_bytes(w->dtype, K, N, batch), st);
     if (e != cudaSuccess) return fail(HYQ_E_NOMEM, "matmul workspace: %s", cudaGetErrorString(e));
     e = hyq::launch_gemm(w->dtype, w->data, K, N, input, batch, out, ws, status, st);
     cudaError_t e2 = cudaFreeAsync(ws, st);
@@ -460,8 +480,7 @@ static int run_gemm_job(const hyq::GemmJob& j, cudaStream_t st, const char* name
   hyq::GemmJob jj = j;
   jj.status = status;
   void* ws = nullptr;
-  ensure_pool();
-  cudaError_t e = cudaMallocAsync(&ws, hyq::gemm_job_workspace_bytes(jj), st);
+  cudaError_t e = ws_alloc(&ws, hyq::gemm_job_workspace_bytes(jj), st);
   if (e != cudaSuccess) return fail(HYQ_E_NOMEM, "%s workspace: %s", name, cudaGetErrorString(e));
   e = hyq::launch_gemm_job(jj, ws, st);
   const cudaError_t e2 = cudaFreeAsync(ws, st);

@@ -5,8 +5,8 @@
 // Some callers cannot take a device allocation on every product: a serving
 // process that gives all free HBM to its own cache when it starts (an
 // allocation in the middle of a request could then fail), or a host that
-// manages the device's default memory pool itself and so cannot accept the
-// pool setting hyq_matmul makes to keep its workspace cached.  This entry
+// accounts for every byte of device memory itself and so cannot accept the
+// workspace pool hyq_matmul keeps cached until the process exits.  This entry
 // point allocates nothing: the array below belongs to the module image, and
 // every GPU that loads the module holds it until the process exits.
 //

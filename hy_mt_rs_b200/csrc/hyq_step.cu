@@ -541,6 +541,17 @@ __global__ void __launch_bounds__(gemv::kThreads, 1) step_kernel(const __grid_co
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 16 * gemv::kMaxStages);
   uint8_t* stages = smem + a.stage_off;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // The position comes from device memory (a graph replays the step), so the
+  // host cannot check it.  A position outside the cache ends the launch
+  // before any phase runs: no cache row, table row or token is touched, pos
+  // is not advanced, and HYQ_DEV_BAD_ARGS is raised.  Every thread of every
+  // CTA reads pos here, before the first grid barrier; the only write to it
+  // (finish_phase) comes after the last one, so all CTAs agree.
+  const int pos0 = *a.pos;
+  if (pos0 < 0 || pos0 >= a.positions) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(a.status, DEV_BAD_ARGS);
+    return;
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < a.stages; ++s) {
       mbar_init(smem_addr(&full[s]), 1);

@@ -11,14 +11,25 @@ out exactly as the decoders of quant.rs:2405-2486 read them.
 """
 import torch
 
-from .quant import DType
-
 __all__ = ["encode", "random_weights", "random_packed", "row_bytes"]
+
+# DType values and their block geometry (quant.rs:19-27, 43-62), kept here so
+# that synthesising weights needs no GPU library (the CPU benchmark arms and
+# the fixture scripts import this module without loading libhyq.so).
+F32, F16, Q4_K, Q6_K, Q8_0, Q2_0C, STQ1_0 = range(7)
+_GEOMETRY = {F32: (1, 4), F16: (1, 2), Q4_K: (256, 144), Q6_K: (256, 210), Q8_0: (32, 34), Q2_0C: (512, 130),
+             STQ1_0: (256, 42)}
+
+
+def _block(dtype):
+    if int(dtype) not in _GEOMETRY:
+        raise ValueError(f"unsupported tensor type {dtype}")
+    return _GEOMETRY[int(dtype)]
 
 
 def row_bytes(dtype, K):
-    dtype = DType(dtype)
-    return K // dtype.block_len() * dtype.block_bytes()
+    bl, bb = _block(dtype)
+    return K // bl * bb
 
 
 def _f16_bytes(v):
@@ -126,16 +137,17 @@ def _q6_k(w):
 
 def encode(dtype, w):
     """Pack f32 weights [N, K] into `dtype` rows (flat uint8 tensor)."""
-    dtype = DType(dtype)
+    dtype = int(dtype)
+    bl = _block(dtype)[0]
     w = w.to(torch.float32).contiguous()
     N, K = w.shape
-    if K % dtype.block_len():
-        raise ValueError(f"K={K} is not a multiple of {dtype.block_len()}")
-    if dtype == DType.F32:
+    if K % bl:
+        raise ValueError(f"K={K} is not a multiple of {bl}")
+    if dtype == F32:
         return w.view(torch.uint8).reshape(-1).clone()
-    if dtype == DType.F16:
+    if dtype == F16:
         return w.to(torch.float16).view(torch.uint8).reshape(-1).clone()
-    fn = {DType.Q8_0: _q8_0, DType.Q2_0C: _q2_0c, DType.STQ1_0: _stq1_0, DType.Q4_K: _q4_k, DType.Q6_K: _q6_k}
+    fn = {Q8_0: _q8_0, Q2_0C: _q2_0c, STQ1_0: _stq1_0, Q4_K: _q4_k, Q6_K: _q6_k}
     out = fn[dtype](w)
     assert out.numel() == N * row_bytes(dtype, K)
     return out

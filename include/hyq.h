@@ -122,7 +122,11 @@ int hyq_weight_row_into(const hyq_weight* w, int64_t row, float* out, int64_t ou
 int hyq_dot(const float* a, const float* b, size_t n, float* out, void* stream);
 
 /* Weight::matmul (quant.rs:159-344): out[batch, N] = input[batch, K] . W^T
- * with f32 activations. */
+ * with f32 activations.  From batch 16 the tensor-core path takes a
+ * stream-ordered workspace (fp16 activations, split-K partials) from a memory
+ * pool the library creates per device; freed workspace stays cached in that
+ * pool until the process exits.  The device's default memory pool is not
+ * touched.  Under stream capture the workspace is a graph allocation. */
 int hyq_matmul(const hyq_weight* w, const float* input, int64_t batch, float* out, void* stream);
 
 /* Weight::gemv_qkv (quant.rs:658-721): three batch-1 projections of one
@@ -211,8 +215,9 @@ int hyq_set_launch_overlap(int enable);
  * works in host memory.  It serves callers that may not allocate device
  * memory per call: a server that hands all free HBM to its own cache at
  * start-up (where a per-call allocation could fail mid request), and hosts
- * that own the device's default memory pool (hyq_matmul raises that pool's
- * release threshold to keep its workspace cached).
+ * that account for every byte of device memory themselves (hyq_matmul's
+ * workspace pool keeps freed workspace cached until the process exits, out of
+ * that host's sight).
  * Limits:
  *   - a batch whose scratch would exceed HYQ_NOALLOC_SCRATCH_BYTES
  *     (K * batch * 2 bytes plus split-K partials) fails with HYQ_E_SHAPE;
@@ -393,7 +398,11 @@ typedef struct hyq_dense_step_desc {
 typedef struct hyq_dense_step hyq_dense_step;
 int hyq_dense_step_create(const hyq_dense_step_desc* desc, hyq_dense_step** out);
 /* One token step on `stream` (a zeroing copy of the step's 16-byte sync
- * words, then the kernel).  Steps of one handle must not overlap in time. */
+ * words, then the kernel).  Steps of one handle must not overlap in time.
+ * The kernel checks the device position first: when *pos is outside
+ * [0, positions) (e.g. a graph replayed past the cache's capacity) the step
+ * does nothing -- no cache row, rotary row or token is touched and *pos is
+ * not advanced -- and raises HYQ_DEV_BAD_ARGS (see hyq_device_status). */
 int hyq_dense_step_enqueue(hyq_dense_step* step, void* stream);
 void hyq_dense_step_free(hyq_dense_step* step);
 
@@ -454,7 +463,13 @@ int hyq_moe_combine(const float* shared, const float* expert_out, int64_t tokens
  *   every rank).  Every rank makes the same sequence of calls; a call waits
  *   (bounded, 5 s -> HYQ_DEV_TIMEOUT_PEER) for the other ranks' flags, so the
  *   ranks' streams must all reach it.  At most 8 ranks; the partial may be
- *   rewritten once the call has completed on the stream.  */
+ *   rewritten once the call has completed on the stream.
+ *   After HYQ_DEV_TIMEOUT_PEER on any rank, `out` of that call is undefined on
+ *   every rank, and so are the results of all later calls on the same regions:
+ *   a rank that gave up has left its flags for that epoch behind, so a late
+ *   peer may sum a partial its owner has since overwritten.  Free and
+ *   re-create the regions on every rank (hyq_peer_free / hyq_peer_alloc /
+ *   hyq_peer_open) before the next call.  */
 #define HYQ_PEER_DATA_OFFSET 1024
 int hyq_peer_alloc(size_t data_bytes, void** region, void* ipc_handle);
 int hyq_peer_open(const void* ipc_handle, void** region);

@@ -37,5 +37,5 @@ def cuda():
     import torch
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
-    import hy_mt_rs_b200  # noqa: F401  (loads libhyq.so or raises)
+    import hy_mt_rs_b200.quant  # noqa: F401  (loads libhyq.so or raises)
     return torch.device("cuda", 0)

@@ -355,3 +355,34 @@ def test_fused_step_matches_oracle(cuda):
             break
     assert again == ids
     assert quant.device_status() == 0
+
+
+def test_fused_step_refuses_position_past_cache(cuda):
+    """A persistent step whose device position is outside the KV cache
+    (a graph replayed once too often) must do nothing: the kernel checks the
+    position before any phase, raises HYQ_DEV_BAD_ARGS, and leaves the
+    position, the token and every cache row unchanged.  The check sits at the
+    top of the kernel, ahead of every access that depends on the position."""
+    import torch
+    from hy_mt_rs_b200 import quant
+    from hy_mt_rs_b200.model import DenseConfig, DenseModel, random_weights
+
+    cfg = DenseConfig(layers=2, positions=16)
+    weights = random_weights(cfg, cuda, seed=9)
+    torch.cuda.synchronize()
+    model = DenseModel(cfg, weights, cuda, fused=True)
+    assert quant.device_status() == 0
+    for bad in (cfg.positions, -1):
+        model.token.fill_(7)
+        model.pos.fill_(bad)
+        before = [W["k_cache"].clone() for W in model.layers] + [W["v_cache"].clone() for W in model.layers]
+        model.enqueue_step()
+        assert quant.device_status() == 8      # HYQ_DEV_BAD_ARGS, and the word is cleared
+        assert model.pos.item() == bad and model.token.item() == 7
+        after = [W["k_cache"] for W in model.layers] + [W["v_cache"] for W in model.layers]
+        assert all(torch.equal(a, b) for a, b in zip(after, before))
+    # a valid position still steps normally afterwards
+    model.pos.zero_()
+    model.enqueue_step()
+    assert quant.device_status() == 0
+    assert model.pos.item() == 1

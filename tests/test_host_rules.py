@@ -30,3 +30,28 @@ def test_split_grid_stays_within_one_wave():
         for K, dtype in ((2048, Q2C), (6144, Q2C), (4096, Q4K), (14336, Q6K)):
             z = gemm_splits(tiles, K, 64, dtype)
             assert 1 <= z <= 16 and tiles * z <= max(148, tiles)
+
+
+def test_reference_arm_runs_without_the_gpu_library():
+    """The reference arm times the CPU port only: one step of it, in a fresh
+    process, must not map libhyq.so, and its line carries the GPU arm's
+    `config` dict verbatim (decode_config) with the whole lm_head."""
+    import json
+    import os
+    import subprocess
+    import sys
+
+    code = (
+        "import json, sys, types, bench\n"
+        "a = types.SimpleNamespace(steps=1, warmup=0, gpus=1, path='f32', copies=4, no_overlap=False)\n"
+        "bench.reference_arm(a)\n"
+        "maps = open('/proc/self/maps').read()\n"
+        "print(json.dumps({'libhyq': 'libhyq.so' in maps, 'native': 'hy_mt_rs_b200._native' in sys.modules,\n"
+        "                  'config': bench.decode_config(a, 1)}))\n")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    res = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0, res.stderr
+    line, probe = [json.loads(x) for x in res.stdout.strip().splitlines()[-2:]]
+    assert not probe["libhyq"] and not probe["native"]
+    assert line["impl"] == "reference" and line["config"] == probe["config"]
+    assert "all 120832 lm_head rows" in line["cpu_baseline"]["sample"]

@@ -54,6 +54,12 @@ CASES = [(Q6_K, 1024, 14336, 64), (Q4_K, 14336, 4096, 512), (Q4_K, 512, 2048, 5)
 def test_noalloc_matches_matmul_on_consecutive_calls(cuda):
     from hy_mt_rs_b200 import _native, quant
 
+    # the first case must reach the partial-sum region of the array (more
+    # than one split-K slice), the second must not, the third stays below
+    # the tensor-core batch threshold
+    assert quant.gemm_splits(CASES[0][1] // 128, CASES[0][2], CASES[0][3], CASES[0][0]) > 1
+    assert quant.gemm_splits(CASES[1][1] // 128, CASES[1][2], CASES[1][3], CASES[1][0]) == 1
+    assert CASES[2][3] < 16
     runs = []
     for i, (t, N, K, M) in enumerate(CASES):
         w, x = make(cuda, t, N, K, M, seed=11 + i)
@@ -74,7 +80,10 @@ def test_noalloc_rejects_batch_beyond_scratch(cuda):
     from hy_mt_rs_b200 import _native
 
     K, N = 14336, 128
-    M = SCRATCH_BYTES // (2 * K) + 16  # the fp16 activation copy alone exceeds the array
+    # the fp16 activation copy alone exceeds the array; a whole number of
+    # 256-token tiles, so the batch takes the tensor-core path for certain
+    M = (SCRATCH_BYTES // (2 * K) // 256 + 1) * 256
+    assert 2 * K * M > SCRATCH_BYTES
     w, x = make(cuda, Q6_K, N, K, M, seed=3)
     rc, _ = noalloc(w, x, M)
     assert rc == HYQ_E_SHAPE
