@@ -109,6 +109,9 @@ cudaError_t ws_alloc(void** p, size_t bytes, cudaStream_t st) {
 // of the preceding grid in their stream.
 std::atomic<int> g_launch_overlap{0};
 
+// hyq_set_gemm_precision: batched products on split fp16 operands.
+std::atomic<int> g_gemm_precision{HYQ_GEMM_FP16};
+
 // Batches from this size up go to the tensor-core GEMM when the format and
 // shape allow it; smaller batches run batch-1 products.
 constexpr int64_t kGemmMinBatch = 16;
@@ -235,6 +238,7 @@ int api_fail(int code, const char* fmt, ...) {
 int api_status_word(unsigned** out) { return status_ptr(out); }
 
 bool launch_overlap() { return g_launch_overlap.load(std::memory_order_relaxed) != 0; }
+bool gemm_split() { return g_gemm_precision.load(std::memory_order_relaxed) == HYQ_GEMM_F32; }
 
 }  // namespace hyq
 
@@ -403,9 +407,10 @@ int hyq_matmul(const hyq_weight* w, const float* input, int64_t batch, float* ou
     if ((rc = status_ptr(&status))) return rc;
     cudaStream_t st = (cudaStream_t)stream;
     void* ws = nullptr;
-    cudaError_t e = ws_alloc(&ws, hyq::gemm_workspace_bytes(w->dtype, K, N, batch), st);
+    const bool split = hyq::gemm_split();
+    cudaError_t e = ws_alloc(&ws, hyq::gemm_workspace_bytes(w->dtype, K, N, batch, split), st);
     if (e != cudaSuccess) return fail(HYQ_E_NOMEM, "matmul workspace: %s", cudaGetErrorString(e));
-    e = hyq::launch_gemm(w->dtype, w->data, K, N, input, batch, out, ws, status, st);
+    e = hyq::launch_gemm(w->dtype, w->data, K, N, input, batch, out, ws, status, st, split);
     cudaError_t e2 = cudaFreeAsync(ws, st);
     if (e != cudaSuccess) return cuda_fail(e, "matmul (tensor-core GEMM)");
     if (e2 != cudaSuccess) return cuda_fail(e2, "matmul workspace free");
@@ -479,6 +484,7 @@ static int run_gemm_job(const hyq::GemmJob& j, cudaStream_t st, const char* name
   if (rc) return rc;
   hyq::GemmJob jj = j;
   jj.status = status;
+  jj.split = hyq::gemm_split();
   void* ws = nullptr;
   cudaError_t e = ws_alloc(&ws, hyq::gemm_job_workspace_bytes(jj), st);
   if (e != cudaSuccess) return fail(HYQ_E_NOMEM, "%s workspace: %s", name, cudaGetErrorString(e));
@@ -687,6 +693,13 @@ int hyq_matmul_gate_up_silu_int8(const hyq_weight* gate, const hyq_weight* up, c
   a.quantize = true;
   if ((rc = check_act(a, "gate_up_silu_int8"))) return rc;
   return run_gemv(1, &gate, &out, up, a, (cudaStream_t)stream, "gate_up_silu_int8");
+}
+
+int hyq_set_gemm_precision(int precision) {
+  if (precision != HYQ_GEMM_FP16 && precision != HYQ_GEMM_F32)
+    return fail(HYQ_E_INVALID, "set_gemm_precision: unknown precision %d", precision);
+  g_gemm_precision.store(precision, std::memory_order_relaxed);
+  return HYQ_OK;
 }
 
 int hyq_set_launch_overlap(int enable) {

@@ -61,8 +61,26 @@ constexpr int kThreads1 = (2 + kGroups * kGroupWarps) * 32;
 constexpr int kTmemCols = 512;
 
 // Activation / decoded-weight stages for a BN-token tile (shared memory
-// holds S activation tiles and two packed block columns).
-__host__ __device__ constexpr int stages_for(int bn) { return bn == 256 ? 5 : 8; }
+// holds S activation tiles and two packed block columns).  The split-operand
+// form (below) holds two activation tiles and two A stages per step and
+// keeps two accumulators: 4 stages at 128 tokens, 6 at 64.
+__host__ __device__ constexpr int stages_for(int bn, bool split = false) {
+  return split ? (bn == 128 ? 4 : 6) : (bn == 256 ? 5 : 8);
+}
+
+// Split-operand form (hyq_set_gemm_precision(HYQ_GEMM_F32)): every weight w
+// (decoded exactly in f32, as decode_unchecked) and every activation x is
+// written as hi + lo / 2^11 with hi = fp16(w) and lo = fp16((w - hi) * 2^11)
+// (w - hi is exact, and the scale keeps lo a normal fp16 number), so each
+// operand carries 22 significant bits.  Per 16-column K chunk three MMAs run:
+// hi.hi into the main accumulator, hi.lo and lo.hi into a correction
+// accumulator; the epilogue returns main + correction / 2^11.  Only the
+// lo.lo term (2^-22 relative) is left out, so products reach f32 accuracy
+// at three times the tensor-core instructions (Ootomo and Yokota, "Recovering
+// single precision accuracy from Tensor Cores while surpassing the FP32
+// theoretical peak performance", 2022, with the scaled low part).
+constexpr float kSplitScale = 2048.0f;
+constexpr float kSplitInv = 1.0f / 2048.0f;
 
 // Token tile (the MMA's N) for products of m activation rows (per expert in
 // expert mode): a 64-token tile for at most 64 rows, so that small batches
@@ -115,10 +133,11 @@ struct Params {
   int expert_rows;
 };
 
-template <int FMT, int BN>
+template <int FMT, int BN, bool SPLIT = false>
 struct Smem {
-  static constexpr int S = stages_for(BN);
-  static constexpr int x_tile = BN * 128;
+  static constexpr int S = stages_for(BN, SPLIT);
+  static constexpr int x_half = BN * 128;                   // one fp16 activation tile
+  static constexpr int x_tile = x_half * (SPLIT ? 2 : 1);   // hi tile, then the lo tile
   // offsets from the 1024-aligned base
   static constexpr int x = 0;
   static constexpr int w = x + S * x_tile;
@@ -422,20 +441,48 @@ __device__ __forceinline__ void decode64(uint32_t row, int j4, uint32_t (&o)[32]
   }
 }
 
-template <int FMT, int BN>
+// Split-operand decode: the row's 64 weights of K step j4 in k_perm order,
+// each decoded exactly in f32 (decode_elem: the reference's operation order)
+// and split into hi / scaled lo fp16 pairs (word P = slots 2P, 2P + 1).
+// `row` is the generic address of the row's packed block column.
+template <int FMT>
+__device__ __forceinline__ void decode64_split(const uint8_t* __restrict__ row, int j4, uint32_t (&hi)[32],
+                                               uint32_t (&lo)[32]) {
+#pragma unroll
+  for (int P = 0; P < 32; ++P) {
+    float h[2], l[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int o = 64 * j4 + k_perm(FMT, 2 * P + e);
+      float v;
+      if constexpr (FMT == Q8_0) v = decode_elem<Q8_0>(row + 34 * (o >> 5), o & 31);
+      else v = decode_elem<FMT>(row, o);
+      h[e] = __half2float(__float2half_rn(v));
+      l[e] = __fmul_rn(__fsub_rn(v, h[e]), kSplitScale);
+    }
+    hi[P] = pack_h2(h[0], h[1]);
+    lo[P] = pack_h2(l[0], l[1]);
+  }
+}
+
+template <int FMT, int BN, bool SPLIT>
 __global__ void __launch_bounds__(kThreads1, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_constant__ CUtensorMap tmap_w1,
                 const __grid_constant__ CUtensorMap tmap_w2, const __grid_constant__ CUtensorMap tmap_x,
-                const __grid_constant__ Params p) {
-  using L = Smem<FMT, BN>;
+                const __grid_constant__ CUtensorMap tmap_xlo, const __grid_constant__ Params p) {
+  using L = Smem<FMT, BN, SPLIT>;
   constexpr int S = L::S;
+  // Tensor memory: the accumulator(s) in columns [0, kAcc), A stage s (hi,
+  // and for SPLIT the scaled lo after it) at kAcc + kAStage * s.
+  constexpr int kAcc = SPLIT ? 2 * BN : BN;
+  constexpr int kAStage = SPLIT ? 64 : 32;
   // With an even number of stages the MMA thread releases them in pairs:
   // one tcgen05.commit costs about as much issue time as two MMAs, so one
   // commit per two K steps (on the pair's first barrier) saves it half the
   // time.  Waiters of stage s wait on barrier rel(s).
   constexpr bool kPairRelease = S % 2 == 0;
   auto rel = [](int s) { return kPairRelease ? (s & ~1) : s; };
-  static_assert(BN + 32 * S <= kTmemCols, "accumulator and A stages exceed tensor memory");
+  static_assert(kAcc + kAStage * S <= kTmemCols, "accumulators and A stages exceed tensor memory");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled tiles
   const uint32_t raw_s = smem_addr(smem_raw);
@@ -455,6 +502,7 @@ __global__ void __launch_bounds__(kThreads1, 1)
   if (threadIdx.x == 32) {
     // the descriptors are kernel parameters: fetch them during the set-up
     prefetch_tmap(&tmap_x);
+    if (SPLIT) prefetch_tmap(&tmap_xlo);
     prefetch_tmap(&tmap_w0);
     if (p.n_seg > 1 || p.gate_up) prefetch_tmap(&tmap_w1);
     if (p.n_seg > 2) prefetch_tmap(&tmap_w2);
@@ -548,6 +596,7 @@ __global__ void __launch_bounds__(kThreads1, 1)
         }
         mbar_arrive_expect_tx(xfull(s), (uint32_t)L::x_tile);
         tma_load_2d(base + L::x + s * L::x_tile, &tmap_x, (kbeg + ks) * BK, tok0, xfull(s));
+        if (SPLIT) tma_load_2d(base + L::x + s * L::x_tile + L::x_half, &tmap_xlo, (kbeg + ks) * BK, tok0, xfull(s));
         ++issued_x;
       }
       if (!ok) {
@@ -575,11 +624,18 @@ __global__ void __launch_bounds__(kThreads1, 1)
       }
       tc_fence_after();
       if (lane == 0) {
-        const uint32_t a0 = tmem + (uint32_t)(BN + 32 * s);
+        const uint32_t a0 = tmem + (uint32_t)(kAcc + kAStage * s);
         const uint32_t b0 = base + L::x + s * L::x_tile;
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k)
-          umma_f16_ts(tmem, a0 + 8 * k, sw128_desc(b0 + 32 * k), idesc, (ks > 0 || k > 0) ? 1u : 0u);
+        for (int k = 0; k < BK / 16; ++k) {
+          const uint32_t acc = (ks > 0 || k > 0) ? 1u : 0u;
+          umma_f16_ts(tmem, a0 + 8 * k, sw128_desc(b0 + 32 * k), idesc, acc);
+          if constexpr (SPLIT) {
+            // correction accumulator: hi.lo + lo.hi
+            umma_f16_ts(tmem + BN, a0 + 8 * k, sw128_desc(b0 + L::x_half + 32 * k), idesc, acc);
+            umma_f16_ts(tmem + BN, a0 + 32 + 8 * k, sw128_desc(b0 + 32 * k), idesc, 1u);
+          }
+        }
         if (!kPairRelease || (ks & 1) || ks == nk - 1) umma_commit(empty(rel(s)));
       }
       __syncwarp();
@@ -619,9 +675,16 @@ __global__ void __launch_bounds__(kThreads1, 1)
       tc_fence_after();  // the MMAs that read this A stage are complete
       const int skew = (int)((skew0 + (kb0 + wb) * wbytes_for(FMT)) & 15);
       const uint32_t rowp = base + L::w + ws * L::w_stage + row_off + skew;
-      uint32_t o[32];
-      decode64<FMT>(rowp, ks % kSpw, o);
-      tmem_st32(tmem + lane_base + (uint32_t)(BN + 32 * s), o);
+      if constexpr (SPLIT) {
+        uint32_t hi[32], lo[32];
+        decode64_split<FMT>(base_g + (rowp - base), ks % kSpw, hi, lo);
+        tmem_st32(tmem + lane_base + (uint32_t)(kAcc + kAStage * s), hi);
+        tmem_st32(tmem + lane_base + (uint32_t)(kAcc + kAStage * s + 32), lo);
+      } else {
+        uint32_t o[32];
+        decode64<FMT>(rowp, ks % kSpw, o);
+        tmem_st32(tmem + lane_base + (uint32_t)(kAcc + kAStage * s), o);
+      }
       // Every writer waits for its tensor-memory stores and orders them
       // before the barrier; the warp then signals the stage once.
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
@@ -644,7 +707,8 @@ __global__ void __launch_bounds__(kThreads1, 1)
         const int q = warp & 3;
         constexpr int kCols = BN / kGroups;
         static_assert(kCols % 32 == 0 || kCols == 16, "16- or 32-column epilogue batches");
-        constexpr int kBatch = kCols < 32 ? 16 : 32;
+        // SPLIT: 16 columns of each accumulator per wait
+        constexpr int kBatch = (kCols < 32 || SPLIT) ? 16 : 32;
         const int cbeg = grp * kCols;
         const int cend = min(cbeg + kCols, tok_end - tok0);
         const bool split = p.y != nullptr;
@@ -661,16 +725,22 @@ __global__ void __launch_bounds__(kThreads1, 1)
                 "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
                 "=r"(v[15])
               : "r"(ta));
-          if constexpr (kBatch == 32) {
+          if constexpr (kBatch == 32 || SPLIT) {
+            // the next 16 columns, or (SPLIT) the same 16 of the correction accumulator
             asm volatile(
                 "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
                 "%13, %14, %15}, [%16];"
                 : "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]),
                   "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]),
                   "=r"(v[30]), "=r"(v[31])
-                : "r"(ta + 16u));
+                : "r"(ta + (SPLIT ? (uint32_t)BN : 16u)));
           }
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          if constexpr (SPLIT) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              v[i] = __float_as_uint(__fadd_rn(__uint_as_float(v[i]), __fmul_rn(__uint_as_float(v[16 + i]), kSplitInv)));
+          }
           if (!p.gate_up) {
             const int row = row0 + 32 * q + lane;
             if (row < rows_m) {
@@ -698,9 +768,11 @@ __global__ void __launch_bounds__(kThreads1, 1)
                   yz[(size_t)tok * p.N + hi * rows_m + row] = __uint_as_float(v[i]);
                 } else if (!hi) {
                   // silu(g) * u = g / (1 + e^-g) * u (quant.rs:573-574), with
-                  // the fast exponential and division: the operands are fp16
+                  // the fast exponential and division when the operands are
+                  // fp16; SPLIT as the batch-1 products compute it
                   const float g = __uint_as_float(v[i]);
-                  p.ys[0][(size_t)tok * rows_m + row] = __fdividef(g, 1.0f + __expf(-g)) * u[i];
+                  p.ys[0][(size_t)tok * rows_m + row] =
+                      SPLIT ? (g / (1.0f + expf(-g))) * u[i] : __fdividef(g, 1.0f + __expf(-g)) * u[i];
                 }
               }
             }
@@ -1067,6 +1139,30 @@ __global__ void __launch_bounds__(256) to_half_kernel(const float* __restrict__ 
   h[i] = __floats2half2_rn(row[k_perm(FMT, slot)], row[k_perm(FMT, slot + 1)]);
 }
 
+// Split-operand form: the hi copy at h[0 .. total_pairs) and the scaled lo
+// copy (fp16((x - hi) * 2^11)) at h[total_pairs ..), both in k_perm order.
+template <int FMT>
+__global__ void __launch_bounds__(256) to_half_split_kernel(const float* __restrict__ x, __half2* __restrict__ h,
+                                                             int64_t K, int64_t total_pairs,
+                                                             const int32_t* __restrict__ rows) {
+  grid_dependency_wait();
+  allow_dependents_launch();
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total_pairs) return;
+  const int64_t e = 2 * i;
+  const int64_t tok = e / K;
+  const int64_t kk = e - tok * K;
+  const int64_t step0 = kk & ~int64_t(63);
+  const int slot = (int)(kk & 63);
+  const float* row = x + (rows ? (int64_t)rows[tok] : tok) * K + step0;
+  const float a = row[k_perm(FMT, slot)], b = row[k_perm(FMT, slot + 1)];
+  const __half2 hi = __floats2half2_rn(a, b);
+  const float ah = __low2float(hi), bh = __high2float(hi);
+  h[i] = hi;
+  h[total_pairs + i] =
+      __floats2half2_rn(__fmul_rn(__fsub_rn(a, ah), kSplitScale), __fmul_rn(__fsub_rn(b, bh), kSplitScale));
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -1147,14 +1243,14 @@ bool use_pair(int64_t N, int64_t M) {
   return enabled && M >= 256 && N % (2 * BM) == 0;
 }
 
-template <int FMT, int BN>
-cudaError_t run(const CUtensorMap* tw, const CUtensorMap& tx, const Params& p, int tiles, int splits,
-                int64_t max_rows, cudaStream_t st) {
-  auto k = gemm_kernel<FMT, BN>;
+template <int FMT, int BN, bool SPLIT>
+cudaError_t run(const CUtensorMap* tw, const CUtensorMap& tx, const CUtensorMap& txlo, const Params& p, int tiles,
+                int splits, int64_t max_rows, cudaStream_t st) {
+  auto k = gemm_kernel<FMT, BN, SPLIT>;
   static int configured_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
-  const int smem = Smem<FMT, BN>::total + 1024;
+  const int smem = Smem<FMT, BN, SPLIT>::total + 1024;
   if (configured_dev != dev) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
@@ -1162,7 +1258,7 @@ cudaError_t run(const CUtensorMap* tw, const CUtensorMap& tx, const Params& p, i
   }
   // token tiles: of all M rows, or (expert mode) of the most rows one expert can have
   dim3 grid((unsigned)tiles, (unsigned)((max_rows + BN - 1) / BN), (unsigned)splits);
-  return launch_ex(k, grid, dim3(kThreads1), (size_t)smem, st, tw[0], tw[1], tw[2], tx, p);
+  return launch_ex(k, grid, dim3(kThreads1), (size_t)smem, st, tw[0], tw[1], tw[2], tx, txlo, p);
 }
 
 // Sum of the split-K partials in slice order, written to the matrices'
@@ -1177,13 +1273,16 @@ struct ReduceArgs {
   int seg_col0[3];
   int seg_rows[3];
   float* ys[3];
-  int vec4;  // four columns per thread (every column boundary and output 16-byte aligned)
+  int vec4;     // four columns per thread (every column boundary and output 16-byte aligned)
+  int precise;  // gate/up SiLU with expf and IEEE division (split-operand products)
 };
 
 __device__ __forceinline__ float4 add4(float4 a, float4 b) {
   return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
 }
-__device__ __forceinline__ float silu_mul(float g, float u) { return __fdividef(g, 1.0f + __expf(-g)) * u; }
+__device__ __forceinline__ float silu_mul(float g, float u, int precise) {
+  return precise ? (g / (1.0f + expf(-g))) * u : __fdividef(g, 1.0f + __expf(-g)) * u;
+}
 
 __global__ void __launch_bounds__(256) reduce_splits_kernel(const __grid_constant__ ReduceArgs a) {
   grid_dependency_wait();
@@ -1205,7 +1304,8 @@ __global__ void __launch_bounds__(256) reduce_splits_kernel(const __grid_constan
       float4 u = *reinterpret_cast<const float4*>(su);
       for (int z = 1; z < a.splits; ++z) u = add4(u, *reinterpret_cast<const float4*>(su + (int64_t)z * n));
       *reinterpret_cast<float4*>(a.ys[0] + tok * a.seg_rows[0] + c) =
-          make_float4(silu_mul(s.x, u.x), silu_mul(s.y, u.y), silu_mul(s.z, u.z), silu_mul(s.w, u.w));
+          make_float4(silu_mul(s.x, u.x, a.precise), silu_mul(s.y, u.y, a.precise), silu_mul(s.z, u.z, a.precise),
+                      silu_mul(s.w, u.w, a.precise));
       return;
     }
     int m = 0;
@@ -1225,7 +1325,7 @@ __global__ void __launch_bounds__(256) reduce_splits_kernel(const __grid_constan
     const float* su = src + a.seg_rows[0];
     float u = su[0];
     for (int z = 1; z < a.splits; ++z) u += su[(int64_t)z * n];
-    a.ys[0][tok * a.seg_rows[0] + c] = silu_mul(s, u);  // as in the GEMM epilogue
+    a.ys[0][tok * a.seg_rows[0] + c] = silu_mul(s, u, a.precise);  // as in the GEMM epilogue
     return;
   }
   int m = 0;
@@ -1245,8 +1345,7 @@ int device_sms() {
 // Split-K slices (in block columns) so that small grids still fill the GPU,
 // within one wave of CTAs (one per SM): a second, partial wave costs a whole
 // slice's time for a fraction of the SMs.
-int choose_splits(int64_t K, int64_t row_tiles, int64_t M, int wcol) {
-  const int64_t bn = token_tile(M);
+int choose_splits(int64_t K, int64_t row_tiles, int64_t M, int wcol, int64_t bn) {
   const int64_t tiles = row_tiles * ((M + bn - 1) / bn);
   const int64_t nwb = K / wcol;
   const int64_t sms = device_sms();
@@ -1308,7 +1407,18 @@ bool job_geometry(const GemmJob& j, Geometry& g) {
   return j.M <= INT32_MAX / 2;
 }
 
-size_t x_bytes(int64_t K, int64_t M) { return ((size_t)(K * M) * sizeof(__half) + 255) / 256 * 256; }
+// fp16 activation copy (split-operand form: hi and lo copies)
+size_t x_bytes(int64_t K, int64_t M, bool split) {
+  return ((size_t)(K * M) * sizeof(__half) * (split ? 2 : 1) + 255) / 256 * 256;
+}
+
+// Token tile of a job: by batch size (expert mode: the typical rows per
+// expert), at most 128 in the split-operand form (its two accumulators and
+// doubled A stages do not fit tensor memory at 256).
+int job_token_tile(const GemmJob& j) {
+  const int bn = token_tile(j.experts > 0 ? j.M / j.experts : j.M);
+  return j.split && bn > 128 ? 128 : bn;
+}
 
 }  // namespace gemm
 
@@ -1324,8 +1434,8 @@ size_t gemm_job_workspace_bytes(const GemmJob& j) {
   gemm::Geometry g;
   if (!gemm::job_geometry(j, g)) return 0;
   const gemm::Layout L = gemm::layout_of(j);
-  const int z = j.experts > 0 ? 1 : gemm::choose_splits(j.K, L.tiles, j.M, g.wcol);
-  return gemm::x_bytes(j.K, j.M) + (z > 1 ? (size_t)z * j.M * L.ncols * sizeof(float) : 0) + 16;
+  const int z = j.experts > 0 ? 1 : gemm::choose_splits(j.K, L.tiles, j.M, g.wcol, gemm::job_token_tile(j));
+  return gemm::x_bytes(j.K, j.M, j.split) + (z > 1 ? (size_t)z * j.M * L.ncols * sizeof(float) : 0) + 16;
 }
 
 cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) {
@@ -1337,14 +1447,28 @@ cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) 
   const int64_t K = j.K, M = j.M;
   const int64_t row_bytes = K / block_len(j.dtype) * block_bytes(j.dtype);
   const Layout lay = layout_of(j);
-  const bool pair = j.experts == 0 && !j.gate_up && j.n_mat == 1 && (j.dtype == Q4_K || j.dtype == Q6_K) &&
-                    use_pair(j.rows[0], M);
+  const bool pair = !j.split && j.experts == 0 && !j.gate_up && j.n_mat == 1 &&
+                    (j.dtype == Q4_K || j.dtype == Q6_K) && use_pair(j.rows[0], M);
   __half* xh = static_cast<__half*>(workspace);
   {
     const int64_t pairs = K * M / 2;
     const unsigned blocks = (unsigned)((pairs + 255) / 256);
     __half2* xh2 = reinterpret_cast<__half2*>(xh);
     cudaError_t e;
+    if (j.split) {
+      switch (j.dtype) {
+#define HYQ_SPLIT_X(F) \
+  case F: e = launch_ex(to_half_split_kernel<F>, dim3(blocks), dim3(256), 0, st, j.x, xh2, K, pairs, j.x_rows); break;
+        HYQ_SPLIT_X(Q4_K)
+        HYQ_SPLIT_X(Q6_K)
+        HYQ_SPLIT_X(Q8_0)
+        HYQ_SPLIT_X(Q2_0C)
+        HYQ_SPLIT_X(STQ1_0)
+#undef HYQ_SPLIT_X
+        default: return cudaErrorNotSupported;
+      }
+      if (e != cudaSuccess) return e;
+    } else
     switch (j.dtype) {
       case Q4_K: e = launch_ex(to_half_kernel<Q4_K>, dim3(blocks), dim3(256), 0, st, j.x, xh2, K, pairs, j.x_rows); break;
       case Q6_K: e = launch_ex(to_half_kernel<Q6_K>, dim3(blocks), dim3(256), 0, st, j.x, xh2, K, pairs, j.x_rows); break;
@@ -1355,10 +1479,10 @@ cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) 
     if (e != cudaSuccess) return e;
   }
   // expert mode: the typical rows per expert pick the token tile
-  const int bn = token_tile(j.experts > 0 ? M / j.experts : M);
+  const int bn = job_token_tile(j);
   const int tile_rows = j.gate_up ? BM / 2 : BM;
   const int64_t map_mats = j.experts > 0 ? j.experts : 1;  // expert mode: the maps cover every expert
-  CUtensorMap tw[3], tx;
+  CUtensorMap tw[3], tx, txlo;
   for (int m = 0; m < 3; ++m) {
     const int mm = m < j.n_mat ? m : 0;  // unused maps repeat the first
     const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes * g.rows), (cuuint64_t)(map_mats * j.rows[mm] / g.rows)};
@@ -1379,14 +1503,20 @@ cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) 
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
         CUDA_SUCCESS)
       return cudaErrorInvalidValue;
+    // the split-operand lo copy follows the hi copy (K * M halves further)
+    txlo = tx;
+    if (j.split && enc(&txlo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xh + K * M, dims, strides, box, es,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
   }
   const int nwb = (int)(K / g.wcol);
-  const int z = j.experts > 0 ? 1 : choose_splits(K, lay.tiles, M, g.wcol);
+  const int z = j.experts > 0 ? 1 : choose_splits(K, lay.tiles, M, g.wcol, bn);
   const int wb_per_split = (nwb + z - 1) / z;
   // slices actually launched (rounding to whole block columns can drop some)
   const int splits = (nwb + wb_per_split - 1) / wb_per_split;
   float* partials =
-      splits > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + x_bytes(K, M)) : nullptr;
+      splits > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + x_bytes(K, M, j.split)) : nullptr;
   Params p{};
   p.K = (int)K;
   p.N = lay.ncols;
@@ -1420,11 +1550,15 @@ cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) 
     e = j.dtype == Q4_K ? run_pair<Q4_K>(tw[0], tx, p, splits, st) : run_pair<Q6_K>(tw[0], tx, p, splits, st);
   } else {
     switch (j.dtype) {
-#define HYQ_RUN(F) \
-  case F:          \
-    e = bn == 256   ? run<F, 256>(tw, tx, p, lay.tiles, splits, max_rows, st)                                      \
-        : bn == 128 ? run<F, 128>(tw, tx, p, lay.tiles, splits, max_rows, st)                                      \
-                    : run<F, 64>(tw, tx, p, lay.tiles, splits, max_rows, st);                                      \
+#define HYQ_RUN(F)                                                                                  \
+  case F:                                                                                           \
+    if (j.split)                                                                                    \
+      e = bn == 128 ? run<F, 128, true>(tw, tx, txlo, p, lay.tiles, splits, max_rows, st)           \
+                    : run<F, 64, true>(tw, tx, txlo, p, lay.tiles, splits, max_rows, st);           \
+    else                                                                                            \
+      e = bn == 256   ? run<F, 256, false>(tw, tx, txlo, p, lay.tiles, splits, max_rows, st)        \
+          : bn == 128 ? run<F, 128, false>(tw, tx, txlo, p, lay.tiles, splits, max_rows, st)        \
+                      : run<F, 64, false>(tw, tx, txlo, p, lay.tiles, splits, max_rows, st);        \
     break;
       HYQ_RUN(Q4_K)
       HYQ_RUN(Q6_K)
@@ -1442,6 +1576,7 @@ cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) 
   r.N = lay.ncols;
   r.splits = splits;
   r.gate_up = p.gate_up;
+  r.precise = j.split ? 1 : 0;
   r.n_seg = p.n_seg;
   for (int m = 0; m < 3; ++m) {
     r.seg_col0[m] = p.seg_col0[m];
@@ -1460,8 +1595,9 @@ cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) 
 
 // Single-matrix forms used by hyq_matmul and hyq_matmul_noalloc.
 static GemmJob single_job(int dtype, const uint8_t* w, int64_t K, int64_t N, const float* x, int64_t M, float* y,
-                          unsigned* status) {
+                          unsigned* status, bool split) {
   GemmJob j;
+  j.split = split;
   j.dtype = dtype;
   j.n_mat = 1;
   j.w[0] = w;
@@ -1475,16 +1611,17 @@ static GemmJob single_job(int dtype, const uint8_t* w, int64_t K, int64_t N, con
 }
 
 bool gemm_supported(int dtype, int64_t K, int64_t N, int64_t M, const void* w) {
-  return gemm_job_supported(single_job(dtype, static_cast<const uint8_t*>(w), K, N, nullptr, M, nullptr, nullptr));
+  return gemm_job_supported(
+      single_job(dtype, static_cast<const uint8_t*>(w), K, N, nullptr, M, nullptr, nullptr, false));
 }
 
-size_t gemm_workspace_bytes(int dtype, int64_t K, int64_t N, int64_t M) {
-  return gemm_job_workspace_bytes(single_job(dtype, nullptr, K, N, nullptr, M, nullptr, nullptr));
+size_t gemm_workspace_bytes(int dtype, int64_t K, int64_t N, int64_t M, bool split) {
+  return gemm_job_workspace_bytes(single_job(dtype, nullptr, K, N, nullptr, M, nullptr, nullptr, split));
 }
 
 cudaError_t launch_gemm(int dtype, const uint8_t* w, int64_t K, int64_t N, const float* x, int64_t M, float* y,
-                        void* workspace, unsigned* status, cudaStream_t st) {
-  return launch_gemm_job(single_job(dtype, w, K, N, x, M, y, status), workspace, st);
+                        void* workspace, unsigned* status, cudaStream_t st, bool split) {
+  return launch_gemm_job(single_job(dtype, w, K, N, x, M, y, status, split), workspace, st);
 }
 
 }  // namespace hyq

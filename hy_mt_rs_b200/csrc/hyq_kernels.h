@@ -68,15 +68,22 @@ struct GemmJob {
   const int32_t* expert_off = nullptr;
   int64_t expert_max_rows = 0;
   const int32_t* x_rows = nullptr;
+  // Split-operand form (hi + lo fp16 operands, three MMAs per K chunk, f32
+  // accuracy); the workspace then holds two activation copies.
+  bool split = false;
 };
 bool gemm_job_supported(const GemmJob& job);
 size_t gemm_job_workspace_bytes(const GemmJob& job);
 cudaError_t launch_gemm_job(const GemmJob& job, void* workspace, cudaStream_t st);
 
 bool gemm_supported(int dtype, int64_t K, int64_t N, int64_t M, const void* w);
-size_t gemm_workspace_bytes(int dtype, int64_t K, int64_t N, int64_t M);
+size_t gemm_workspace_bytes(int dtype, int64_t K, int64_t N, int64_t M, bool split);
 cudaError_t launch_gemm(int dtype, const uint8_t* w, int64_t K, int64_t N, const float* x, int64_t M, float* y,
-                        void* workspace, unsigned* status, cudaStream_t st);
+                        void* workspace, unsigned* status, cudaStream_t st, bool split);
+
+// hyq_set_gemm_precision's switch (HYQ_GEMM_F32: split-operand products),
+// read once per call by the entry points that launch batched products.
+bool gemm_split();
 
 // C-ABI plumbing (hyq_api.cu): set the calling thread's hyq_last_error text
 // and return `code`; the current device's status word.

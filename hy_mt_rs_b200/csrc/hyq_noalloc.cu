@@ -77,7 +77,8 @@ extern "C" int hyq_matmul_noalloc(const hyq_weight* w, const float* input, int64
   const int64_t K = dims[0], N = dims[1];
   cudaStream_t st = (cudaStream_t)stream;
   if (batch >= kGemmMinBatch && hyq::gemm_supported(dtype, K, N, batch, data) && aligned(input, 16)) {
-    const size_t need = hyq::gemm_workspace_bytes(dtype, K, N, batch);
+    const bool split = hyq::gemm_split();
+    const size_t need = hyq::gemm_workspace_bytes(dtype, K, N, batch, split);
     if (need > HYQ_NOALLOC_SCRATCH_BYTES)
       return hyq::api_fail(HYQ_E_SHAPE,
                            "matmul_noalloc: batch %lld x K %lld (N %lld) needs %zu bytes of scratch, more than the "
@@ -86,7 +87,7 @@ extern "C" int hyq_matmul_noalloc(const hyq_weight* w, const float* input, int64
     unsigned* status = nullptr;
     if ((rc = hyq::api_status_word(&status))) return rc;
     const cudaError_t e =
-        hyq::launch_gemm(dtype, static_cast<const uint8_t*>(data), K, N, input, batch, out, scratch, status, st);
+        hyq::launch_gemm(dtype, static_cast<const uint8_t*>(data), K, N, input, batch, out, scratch, status, st, split);
     if (e != cudaSuccess)
       return hyq::api_fail(HYQ_E_CUDA, "matmul_noalloc (tensor-core GEMM): %s", cudaGetErrorString(e));
     return HYQ_OK;

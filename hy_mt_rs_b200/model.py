@@ -57,6 +57,26 @@ def random_weights(cfg, device, seed=0):
     return {"layers": layers, "embed": embed, "output_norm": norm(H), "shapes": shapes}
 
 
+def weights_digest(weights):
+    """SHA-256 over a random_weights() dict: every layer's packed linears
+    (q, k, v, o, gate, up, down) and f32 norms in that order, then the
+    embedding and the output norm.  Identifies the model bytes on any device
+    (the parity fixtures record it)."""
+    import hashlib
+
+    h = hashlib.sha256()
+
+    def add(t):
+        h.update(t.detach().contiguous().cpu().numpy().tobytes())
+
+    for L in weights["layers"]:
+        for n in ("q", "k", "v", "o", "gate", "up", "down", "input_norm", "ffn_norm", "q_norm", "k_norm"):
+            add(L[n])
+    add(weights["embed"])
+    add(weights["output_norm"])
+    return h.hexdigest()
+
+
 def _p(t):
     return C.c_void_p(t.data_ptr())
 
@@ -100,11 +120,18 @@ class DenseModel:
     hyq_rope_qk + hyq_attention).  Off by default: every split CTA then
     repeats the query heads' norm and RoPE on its own critical path, which
     measured slower than the separate launch (1.528 vs 1.514 ms per token,
-    3.89 vs 3.69 ms per step of 64 requests)."""
+    3.89 vs 3.69 ms per step of 64 requests).
+    gemm_precision: arithmetic of the batched products (prompt chunks of 16
+    tokens and more, DenseBatch steps of 16 requests and more):
+    quant.GEMM_FP16 (fp16 operands, the fastest) or quant.GEMM_F32 (split
+    operands, f32-accurate like the batch-1 products).  Graphs keep the
+    precision they were captured with."""
 
-    def __init__(self, cfg, weights, device, prefill_chunk=PREFILL_CHUNK, fused=False, rope_in_attention=False):
+    def __init__(self, cfg, weights, device, prefill_chunk=PREFILL_CHUNK, fused=False, rope_in_attention=False,
+                 gemm_precision=quant.GEMM_FP16):
         self.cfg = cfg
         self.rope_in_attention = rope_in_attention
+        self.precision = gemm_precision
         self.device = device
         H, KV = cfg.hidden, cfg.kv_heads * cfg.head_dim
         sh = weights["shapes"]
@@ -232,6 +259,10 @@ class DenseModel:
         then the lm_head of the last row and the greedy token; *pos += M.
         caches (per layer (k, v)), pos, token_out and logits default to the
         model's own (one request)."""
+        with quant.gemm_precision(self.precision):
+            self._enqueue_layers(acts, tokens, caches, pos, token_out, logits)
+
+    def _enqueue_layers(self, acts, tokens, caches, pos, token_out, logits):
         cfg, st, a, M = self.cfg, self._stream(), acts, acts.M
         pos = self.pos if pos is None else pos
         token_out = self.token if token_out is None else token_out
@@ -381,6 +412,10 @@ class DenseBatch:
         self.graph = None
 
     def enqueue_step(self):
+        with quant.gemm_precision(self.m.precision):
+            self._enqueue_step()
+
+    def _enqueue_step(self):
         m, cfg, a, B = self.m, self.m.cfg, self.acts, self.B
         st, H = m._stream(), cfg.hidden
         check(lib.hyq_embed(m.embed.handle, _p(self.tokens), B, _p(a.hidden), st))

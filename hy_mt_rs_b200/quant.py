@@ -383,6 +383,37 @@ def set_launch_overlap(enable):
     check(lib.hyq_set_launch_overlap(1 if enable else 0))
 
 
+GEMM_FP16, GEMM_F32 = 0, 1
+_gemm_precision = GEMM_FP16  # the value last set through this module
+
+
+def set_gemm_precision(precision):
+    """hyq_set_gemm_precision: GEMM_FP16 (default) or GEMM_F32, the
+    split-operand tensor-core products that agree with an f32 GEMM (three
+    MMAs per K chunk).  Process-wide; captured graphs keep the precision they
+    were captured with."""
+    global _gemm_precision
+    check(lib.hyq_set_gemm_precision(int(precision)))
+    _gemm_precision = int(precision)
+
+
+class gemm_precision:
+    """Context manager: batched products issued inside run at `precision`;
+    the previous setting comes back on exit."""
+
+    def __init__(self, precision):
+        self.precision = precision
+
+    def __enter__(self):
+        self._prev = _gemm_precision
+        set_gemm_precision(self.precision)
+        return self
+
+    def __exit__(self, *exc):
+        set_gemm_precision(self._prev)
+        return False
+
+
 def device_status(device=None):
     """Synchronize, then read and clear the device status word (0 = ok)."""
     v = C.c_uint32()

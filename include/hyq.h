@@ -203,6 +203,26 @@ int hyq_matmul_gate_up_silu_int8(const hyq_weight* gate, const hyq_weight* up, c
  * Process-wide; default 0 (plain stream order). */
 int hyq_set_launch_overlap(int enable);
 
+/* Arithmetic of the batched tensor-core products (hyq_matmul and
+ * hyq_matmul_noalloc from batch 16, hyq_matmul_qkv, the batched gate/up, the
+ * expert products).  No counterpart in the reference, whose batched path is
+ * an f32 GEMM on the host (quant.rs:272-311, Candle).
+ *   HYQ_GEMM_FP16 (default): activations and decoded weights rounded to fp16,
+ *     f32 accumulation; about 1e-3 relative L2 against an f64 product.
+ *   HYQ_GEMM_F32: split operands -- each activation and each weight (decoded
+ *     exactly in f32) as hi + lo / 2^11, both fp16; three MMAs per K chunk
+ *     (hi.hi, hi.lo, lo.hi) into f32 accumulators -- which keeps 22
+ *     significant bits of every operand: products agree with an f32 GEMM to
+ *     about 1e-6 relative, at about three times the tensor-core instructions
+ *     and twice the activation bytes (token tiles of at most 128, no 2-SM
+ *     form).  The gate/up SiLU then uses expf and IEEE division, as the
+ *     batch-1 products do.  Activations must stay below 65504 in magnitude.
+ * Process-wide, read when a call is issued: a captured CUDA graph keeps the
+ * precision its calls were captured with. */
+#define HYQ_GEMM_FP16 0
+#define HYQ_GEMM_F32 1
+int hyq_set_gemm_precision(int precision);
+
 /* Bytes of the fixed device scratch behind hyq_matmul_noalloc (64 MiB). */
 #define HYQ_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)
 

@@ -83,3 +83,43 @@ def test_batch_64_tensor_cores(cuda):
     # token 0 comes from the prompt forward, the same call on both sides
     assert [r[0] for r in ids] == [r[0] for r in ref_ids]
     assert quant.device_status() == 0
+
+
+def test_batch_64_split_operands_match_oracle(cuda):
+    """64 concurrent requests with f32-accurate batched products
+    (GEMM_F32: split fp16 operands on the tensor cores): requests 0, 21, 42
+    and 63 against the CPU oracle model decoding each request on its own
+    (oracle/model.py), not against the GPU: logits of every step within the
+    1e-4 bound of the f32 single-request path, identical greedy tokens (a
+    divergence only at a near-tie the numerics cannot order)."""
+    import torch
+    from hy_mt_rs_b200 import quant
+    from hy_mt_rs_b200.model import DenseBatch, DenseConfig, DenseModel, random_weights
+    from oracle.model import DenseOracle
+
+    cfg = DenseConfig(layers=2, positions=96)
+    weights = random_weights(cfg, cuda, seed=65)
+    torch.cuda.synchronize()
+    model = DenseModel(cfg, weights, cuda, gemm_precision=quant.GEMM_F32)
+    rng = np.random.default_rng(65)
+    B, n_new = 64, 5
+    prompts = [rng.integers(0, cfg.vocab, int(n)).tolist() for n in rng.integers(1, 40, B)]
+    stream = torch.cuda.Stream(cuda)
+    try:
+        batch = DenseBatch(model, B)
+        logits = torch.zeros(n_new, B, cfg.vocab, device=cuda)
+        ids = batch.generate(prompts, n_new, stream, logits_out=logits)
+    finally:
+        quant.set_launch_overlap(False)
+    got = logits.cpu().numpy()
+    for b in (0, 21, 42, 63):
+        ref_ids, ref_logits = DenseOracle(cfg, weights).generate(prompts[b], n_new)
+        for i in range(n_new):
+            rel = np.linalg.norm(got[i, b] - ref_logits[i]) / np.linalg.norm(ref_logits[i])
+            assert rel < 1e-4, (b, i, rel)
+            if ids[b][i] != ref_ids[i]:
+                top = np.sort(ref_logits[i])[-2:]
+                err = float(np.abs(got[i, b] - ref_logits[i]).max())
+                assert float(top[1] - top[0]) <= 2 * err, (b, i)
+                break
+    assert quant.device_status() == 0

@@ -280,22 +280,24 @@ def test_argmax_rows_first_largest(cuda, n):
     assert pos.cpu().tolist() == list(range(1, rows + 1))
 
 
-@pytest.mark.parametrize("prompt_len,rel_bound", [(6, 1e-4), (40, 2e-2)])
-def test_batched_prefill_matches_oracle(cuda, prompt_len, rel_bound):
+@pytest.mark.parametrize("prompt_len,rel_bound,split", [(6, 1e-4, False), (40, 2e-2, False), (40, 1e-4, True),
+                                                       (64, 1e-4, True)])
+def test_batched_prefill_matches_oracle(cuda, prompt_len, rel_bound, split):
     """The batched forward (model.rs:549-646): the prompt in one chunk,
     causal attention over it, RoPE at positions 0..M-1, logits of the last
     token, then greedy steps.  Below 16 tokens the projections are the f32
     batch-1 products (the 1e-4 bound of the step test); from 16 they run on
-    the fp16 tensor cores, held to the tolerance of that precision."""
+    the tensor cores: with fp16 operands held to the tolerance of that
+    precision, with split operands (GEMM_F32) to the f32 bound of 1e-4."""
     import torch
     from hy_mt_rs_b200 import quant
     from hy_mt_rs_b200.model import DenseConfig, DenseModel, random_weights
     from oracle.model import DenseOracle
 
-    cfg = DenseConfig(layers=4, positions=64)
+    cfg = DenseConfig(layers=4, positions=80)
     weights = random_weights(cfg, cuda, seed=prompt_len)
     torch.cuda.synchronize()
-    model = DenseModel(cfg, weights, cuda)
+    model = DenseModel(cfg, weights, cuda, gemm_precision=quant.GEMM_F32 if split else quant.GEMM_FP16)
     oracle = DenseOracle(cfg, weights)
     prompt = np.random.default_rng(prompt_len).integers(0, cfg.vocab, prompt_len).tolist()
     n_new = 6
