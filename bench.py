@@ -67,6 +67,11 @@ def args_parse():
     ap.add_argument("--model-fused", action="store_true",
                     help="model: run each token step as one persistent kernel (hyq_dense_step) instead of the "
                          "per-kernel graph (the default, which measures faster)")
+    ap.add_argument("--gemm-precision", choices=["fp16", "f32"], default=None,
+                    help="batched tensor-core products: fp16 operands, or split operands (f32-accurate, "
+                         "hyq_set_gemm_precision); default fp16 for prefill, f32 for concurrent decode")
+    ap.add_argument("--no-suite", action="store_true",
+                    help="decode: print the config-2 line alone, without the other configs' measurements")
     return ap.parse_args()
 
 
@@ -259,7 +264,7 @@ def reference_arm(a):
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
-        return 0
+        return None
     layers, lm, lm_rows, x = cpu_workload()
     threads = host_threads()
     for _ in range(a.warmup):
@@ -284,8 +289,7 @@ def reference_arm(a):
                          "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
-    return 0
+    return line
 
 
 # ---------------------------------------------------------------------------
@@ -362,6 +366,47 @@ def job_rate(unit_per_step, steps, world, ms):
     return unit_per_step * steps * world / (ms * 1e-3)
 
 
+def finish_ranks():
+    """End the process group once, after every arm of the run."""
+    import torch.distributed as dist
+
+    if dist.is_available() and dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def sub_args(a, **kw):
+    import copy
+
+    b = copy.copy(a)
+    b.__dict__.update(kw)
+    return b
+
+
+def run_suite(a):
+    """The other BASELINE configs, measured in the same run after the config-2
+    line (every rank runs every arm; rank 0 collects the lines).  Each keeps
+    its own step count so that the whole run stays within a few minutes, and
+    each reports its value, roofline, e2e, clocks and (one GPU) CPU baseline.
+    At N > 1 config 3 is the tensor-parallel layer (NCCL all-reduce of the
+    row-parallel partials) and config 5 expert-parallel (NCCL all-to-all)."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    out = {"config1": gemv_arm(sub_args(a, sweep=False))}
+    if world == 1:
+        out["config3"] = {f"M{M}": prefill_arm(sub_args(a, tokens=M, steps=10, warmup=3, gemm_precision="fp16"))
+                          for M in (128, 512, 2048)}
+        out["config3"]["M2048_f32_products"] = prefill_arm(
+            sub_args(a, tokens=2048, steps=5, warmup=3, gemm_precision="f32", cpu_seconds=0))
+    else:
+        out["config3"] = {"M2048_tp": tp_arm(sub_args(a, tp_mode="prefill", tokens=2048, steps=10, warmup=3))}
+    out["config4"] = {"concurrency_1": model_arm(sub_args(a, concurrency=1, model_fused=False, warmup=3)),
+                      "concurrency_64": model_arm(sub_args(a, concurrency=64, warmup=3, gemm_precision="f32")),
+                      "concurrency_64_fp16_products": model_arm(
+                          sub_args(a, concurrency=64, warmup=3, gemm_precision="fp16", cpu_seconds=0))}
+    out["config5"] = moe_arm(sub_args(a, steps=20, warmup=3))
+    return out
+
+
 def init_ranks():
     """One process per GPU (torchrun's RANK / LOCAL_RANK / WORLD_SIZE); NCCL
     only for the barriers and the max-over-ranks timing."""
@@ -371,7 +416,7 @@ def init_ranks():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
+    if world > 1 and not dist.is_initialized():   # the suite's arms share one process group
         from datetime import timedelta
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
@@ -538,13 +583,10 @@ def gpu_arm(a):
         }
         if world == 1:
             line["cpu_baseline"] = run_cpu(a.cpu_seconds, VOCAB)
-        print(json.dumps(line), flush=True)
     for g in list(graphs.values()) + [g_lm]:
         del g
     graphs.clear()
-    if world > 1:
-        dist.destroy_process_group()
-    return 0
+    return line if rank == 0 else None
 
 
 # ---------------------------------------------------------------------------
@@ -596,6 +638,9 @@ def prefill_arm(a):
         for name, f in calls.items():
             outs[name] = f()
 
+    # fp16 operands (default), or split operands that agree with an f32 GEMM
+    split = a.gemm_precision == "f32"
+    quant.set_gemm_precision(quant.GEMM_F32 if split else quant.GEMM_FP16)
     sampler = ClockSampler("GPU-" + str(torch.cuda.get_device_properties(dev).uuid))
     with torch.cuda.stream(stream):
         for _ in range(a.warmup):
@@ -638,6 +683,7 @@ def prefill_arm(a):
         stream.synchronize()
         e2e_s = (time.perf_counter() - t0) / e2e_steps
     h2d = sum(v.numel() * 4 for v in xs.values())
+    quant.set_gemm_precision(quant.GEMM_FP16)
     if world > 1:
         dist.barrier()
     (ms_total, failed, e2e_s), clocks_all = reduce_over_ranks(
@@ -645,10 +691,8 @@ def prefill_arm(a):
     if failed:
         raise RuntimeError("a kernel reported an expired bounded wait (device status word) on some rank")
     ms = ms_total / a.steps
-    if world > 1:
-        dist.destroy_process_group()
     if rank != 0:
-        return 0
+        return None
     sm = [c["sm_mhz"] for c in clocks_all if c.get("sm_mhz")]
     clocks = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": clocks_all[0].get("sm_max_mhz"),
               "reasons": sorted({r for c in clocks_all for r in c.get("reasons", [])}),
@@ -667,11 +711,14 @@ def prefill_arm(a):
         pass
     peak = float(peaks.get("bf16_tflops", 1590.0))
     line = {
-        "metric": "prefill GEMM TFLOP/s (7B layer projections, Q4_K + Q6_K down, fp16 tensor cores)",
+        "metric": "prefill GEMM TFLOP/s (7B layer projections, Q4_K + Q6_K down, "
+                  + ("split-operand f32-accurate tensor cores)" if split else "fp16 tensor cores)"),
         "value": round(job_rate(flops, 1, world, ms) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": world,
         "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "fp16 operands (decoded weights, activations), f32 accumulate",
+        "vs_baseline": None,
+        "dtype": "split fp16 operands (hi + lo / 2^11 of f32 weights and activations, 3 MMAs), f32 accumulate"
+                 if split else "fp16 operands (decoded weights, activations), f32 accumulate",
         "data": "synthetic", "config": {"workload": f"hy-mt-rs config 3: 7B layer projections, M={M}",
                                         "tokens": M, "flops_per_step": flops, "weight_bytes": wbytes,
                                         "parallelism": f"replicas x{world} (independent token batches)"},
@@ -689,8 +736,34 @@ def prefill_arm(a):
         "gpu_launches": launches,
         "clocks": clocks,
     }
-    print(json.dumps(line), flush=True)
-    return 0
+    if world == 1 and a.cpu_seconds > 0:
+        line["cpu_baseline"] = prefill_cpu(M)
+    return line
+
+
+def prefill_cpu(M):
+    """CPU baseline of config 3: the reference's batch >= 8 path
+    (quant.rs:272-343) -- every projection's rows decoded to f32 (the oracle's
+    decoders, all host threads), then an f32 GEMM (numpy's BLAS, all host
+    threads, standing in for Candle's gemm crate) -- for the 7B layer's four
+    calls at M tokens, once."""
+    import numpy as np
+
+    from hy_mt_rs_b200 import synth
+    from oracle import oracle as O
+
+    threads = host_threads()
+    ws = [(N, K, t, synth.random_packed(t, N, K, seed=50 + i).numpy()) for i, (_, N, K, t) in enumerate(LAYER_7B)]
+    xs = {K: np.random.default_rng(K).standard_normal((M, K)).astype(np.float32) for K in (4096, 14336)}
+    flops = sum(2 * M * N * K for N, K, _, _ in ws)
+    t0 = time.perf_counter()
+    for N, K, t, w in ws:
+        wd = O.decode_rows(t, w, K, N, threads)
+        np.matmul(xs[K], wd.T)
+    el = time.perf_counter() - t0
+    return {"value": round(flops / el / 1e12, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"the 7B layer's seven products at M={M} once ({el:.2f} s): oracle decoders + numpy f32 "
+                      f"GEMM (BLAS) in place of Candle's"}
 
 
 # ---------------------------------------------------------------------------
@@ -747,6 +820,58 @@ def time_products(dtype, N, K, path, dev, min_bytes=256 << 20, reps=1000, seed=0
     return one, ms, copies
 
 
+def gemv_e2e(dev, n=300):
+    """Config 1 through the public call with host buffers: every product
+    copies x in from pinned host memory, runs hyq_matmul on the next of
+    several weight copies (> L2 in total) and reads y back, synchronizing."""
+    import torch
+    from hy_mt_rs_b200 import quant, synth
+
+    N, K = 6144, 2048
+    copies = max(2, -(-(256 << 20) // (N * row_bytes(2, K))))
+    ws = [quant.Weight(synth.random_packed(2, N, K, seed=c, device=dev), 2, [K, N]) for c in range(copies)]
+    xh = torch.randn(K, generator=torch.Generator().manual_seed(5)).pin_memory()
+    yh = torch.empty(N).pin_memory()
+    xd, yd = torch.empty(K, device=dev), torch.empty(N, device=dev)
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for i in range(3 + n):
+            if i == 3:
+                stream.synchronize()
+                t0 = time.perf_counter()
+            xd.copy_(xh, non_blocking=True)
+            ws[i % copies].matmul(xd, 1, out=yd)
+            yh.copy_(yd, non_blocking=True)
+            stream.synchronize()
+        el = time.perf_counter() - t0
+    return {"value": round(n * gemv_bytes(2, N, K) / el / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": 4 * K,
+            "d2h_bytes_per_step": 4 * N, "ms_per_step": round(el / n * 1e3, 5),
+            "how": "pinned host x -> device, hyq_matmul (batch 1) over rotating weight copies, y -> pinned host, "
+                   "stream sync per product"}
+
+
+def gemv_cpu(seconds=3.0):
+    """The oracle port of the reference's x86 f32 Q4_K product on all host
+    threads, for about `seconds`."""
+    import numpy as np
+
+    from hy_mt_rs_b200 import synth
+    from oracle import oracle as O
+
+    N, K = 6144, 2048
+    w = synth.random_packed(2, N, K, seed=0).numpy()
+    x = np.random.default_rng(0).standard_normal(K).astype(np.float32)
+    threads = host_threads()
+    O.matmul(2, w, K, N, x, 1, threads)
+    n, t0 = 0, time.perf_counter()
+    while n == 0 or time.perf_counter() - t0 < seconds:
+        O.matmul(2, w, K, N, x, 1, threads)
+        n += 1
+    el = time.perf_counter() - t0
+    return {"value": round(n * gemv_bytes(2, N, K) / el / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} Q4_K 6144x2048 products ({el:.1f} s); oracle/hyq_oracle.c x86 f32 order, OpenMP"}
+
+
 def gemv_arm(a):
     import torch
 
@@ -785,7 +910,8 @@ def gemv_arm(a):
                    "launch_overlap": True},
         "paths": res,
         "roofline": {"bound": "hbm", "kernel": "Q4_K 6144x2048 f32 GEMV", "achieved": f32["gb_s"], "peak": peak,
-                     "peak_kind": peak_kind, "unit": "GB/s", "frac": f32["frac_of_hbm"], "traffic": None,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": f32["frac_of_hbm"],
+                     "traffic": profile_traffic("gemv_q4k_6144x2048_f32"),
                      "algorithmic_bytes_per_launch": b, "avg_launch_ms": round(f32["us_per_product"] / 1e3, 6)},
         "gpu_launches": 1000,
         "clocks": {"sm_mhz": clocks.get("sm_mhz"), "sm_max_mhz": clocks.get("sm_max_mhz"),
@@ -793,9 +919,11 @@ def gemv_arm(a):
     }
     if sweep:
         line["sweep"] = sweep
+    line["e2e"] = gemv_e2e(dev)
     if rank == 0:
-        print(json.dumps(line), flush=True)
-    return 0
+        if world == 1 and a.cpu_seconds > 0:
+            line["cpu_baseline"] = gemv_cpu(min(a.cpu_seconds, 5.0))
+        return line
 
 
 # ---------------------------------------------------------------------------
@@ -907,9 +1035,8 @@ def tp_arm(a):
         ar.close()
     if world > 1:
         dist.barrier()
-        dist.destroy_process_group()
     if rank != 0:
-        return 0
+        return None
     if a.tp_mode == "decode":
         line = {"metric": "7B layer projections, batch-1 decode, tensor-parallel: weight GB/s",
                 "value": round(wbytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
@@ -924,8 +1051,7 @@ def tp_arm(a):
                             "parallelism": f"tp{world}: QKV, gate/up column-parallel; O, down row-parallel "
                                            f"+ all-reduce ({'NCCL' if (a.tp_mode == 'prefill' or a.tp_allreduce == 'nccl') else 'hyq_peer_allreduce over NVLink peer memory'})",
                             "weight_bytes": wbytes}})
-    print(json.dumps(line), flush=True)
-    return 0
+    return line
 
 
 # ---------------------------------------------------------------------------
@@ -946,7 +1072,10 @@ def model_arm(a):
     cfg = DenseConfig(layers=N_LAYERS_MODEL, positions=n_prompt + n_new)
     weights = random_weights(cfg, dev, seed=1)
     torch.cuda.synchronize(dev)
-    model = DenseModel(cfg, weights, dev, fused=a.model_fused)
+    # the prompt's batched products: split operands (f32-accurate, the
+    # parity-tested setting) unless fp16 is asked for
+    prec = quant.GEMM_FP16 if a.gemm_precision == "fp16" else quant.GEMM_F32
+    model = DenseModel(cfg, weights, dev, fused=a.model_fused, gemm_precision=prec)
     stream = torch.cuda.Stream(dev)
     model.capture(stream)
     prompt = np.random.default_rng(0).integers(0, cfg.vocab, n_prompt).tolist()
@@ -1016,25 +1145,13 @@ def model_arm(a):
         raise RuntimeError("a kernel reported an expired bounded wait (device status word) on some rank")
     model_launches = model.launches()
     model.graph = None
-    if world > 1:
-        import torch.distributed as dist
-        dist.destroy_process_group()
     if rank != 0:
-        return 0
+        return None
     steps = n_new - 1
     tok_s = steps / (ms_decode * 1e-3) * world
     token_bytes = N_LAYERS_MODEL * sum(N * row_bytes(5, K) for _, N, K in LAYER) + VOCAB * row_bytes(3, HIDDEN)
     peak, peak_kind = measured_peaks()
-    # CPU baseline: the oracle's x86 step on all host cores, a bounded sample
-    from oracle.model import DenseOracle
-    ocfg = DenseConfig(layers=N_LAYERS_MODEL, positions=8)
-    oracle = DenseOracle(ocfg, weights, threads=host_threads())
-    t0 = time.perf_counter()
-    n_cpu = 0
-    while n_cpu < 8 and (n_cpu == 0 or time.perf_counter() - t0 < 20.0):
-        oracle.step(prompt[n_cpu], n_cpu)
-        n_cpu += 1
-    cpu_s = (time.perf_counter() - t0) / n_cpu
+    cpu = model_cpu(cfg, weights, prompt) if world == 1 and a.cpu_seconds > 0 else None
     sm = [c["sm_mhz"] for c in clocks_all if c.get("sm_mhz")]
     line = {
         "metric": "decode tokens/s (random-init Hy-MT2-1.8B architecture, Q2_0C linears, Q6_K tied embedding, "
@@ -1044,7 +1161,8 @@ def model_arm(a):
         # the reference's published 1.8B Q2_0C decode rate, one request on an M2 Pro
         # (docs/validation.md:70-71 of hy-mt-rs)
         "vs_baseline": round(tok_s / 86.86, 2), "vs_baseline_number": "86.86 tokens/s, 1.8B Q2_0C, 1 request",
-        "dtype": "f32 activations x packed int weights; f32 KV cache",
+        "dtype": "f32 activations x packed int weights; f32 KV cache; prompt products "
+                 + ("fp16 tensor-core operands" if prec == quant.GEMM_FP16 else "split-operand f32-accurate"),
         "data": "synthetic (seeded random-init weights, 256 seeded random prompt ids)",
         "config": {"workload": "hy-mt-rs config 4: 32 layers, hidden 2048, 16/4 heads x 128, SwiGLU 6144, "
                                "vocab 120832, RoPE 10000; 256-token prompt (batched prefill), 256 generated",
@@ -1066,12 +1184,30 @@ def model_arm(a):
         "clocks": {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": clocks_all[0].get("sm_max_mhz"),
                    "reasons": sorted({r for c in clocks_all for r in c.get("reasons", [])}),
                    "samples": sum(c.get("samples", 0) for c in clocks_all)},
-        "cpu_baseline": {"value": round(1.0 / cpu_s, 3), "unit": "tokens/s", "cores": host_threads(), "kind": "port",
-                         "sample": f"{n_cpu} decode steps of the same model through oracle/model.py (x86 f32 "
-                                   "order, OpenMP)"},
     }
-    print(json.dumps(line), flush=True)
-    return 0
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    return line
+
+
+def model_cpu(cfg, weights, prompt):
+    """CPU baseline of config 4: the oracle's single-token step (the
+    reference's x86 decode path, oracle/model.py) of the same model on all
+    host threads, a bounded sample of steps; one request (the reference
+    serves concurrent requests as separate sessions on the same cores)."""
+    from hy_mt_rs_b200.model import DenseConfig
+    from oracle.model import DenseOracle
+
+    oracle = DenseOracle(DenseConfig(layers=cfg.layers, positions=8), weights, threads=host_threads())
+    t0 = time.perf_counter()
+    n = 0
+    while n < 8 and (n == 0 or time.perf_counter() - t0 < 20.0):
+        oracle.step(prompt[n], n)
+        n += 1
+    el = time.perf_counter() - t0
+    return {"value": round(n / el, 3), "unit": "tokens/s", "cores": host_threads(), "kind": "port",
+            "sample": f"{n} decode steps of one request of the same model through oracle/model.py (x86 f32 order, "
+                      f"OpenMP over all host threads; {el:.1f} s)"}
 
 
 def batch_arm(a):
@@ -1090,7 +1226,10 @@ def batch_arm(a):
     cfg = DenseConfig(layers=N_LAYERS_MODEL, positions=n_prompt + n_new)
     weights = random_weights(cfg, dev, seed=1)
     torch.cuda.synchronize(dev)
-    model = DenseModel(cfg, weights, dev)
+    # the batched products: split operands (f32-accurate; the setting whose
+    # token streams the parity tests pin to the oracle) unless fp16 is asked for
+    prec = quant.GEMM_FP16 if a.gemm_precision == "fp16" else quant.GEMM_F32
+    model = DenseModel(cfg, weights, dev, gemm_precision=prec)
     batch = DenseBatch(model, B)
     stream = torch.cuda.Stream(dev)
     batch.capture(stream)
@@ -1141,11 +1280,8 @@ def batch_arm(a):
         raise RuntimeError("a kernel reported an expired bounded wait (device status word) on some rank")
     step_launches = batch.launches()
     batch.graph = None
-    if world > 1:
-        import torch.distributed as dist
-        dist.destroy_process_group()
     if rank != 0:
-        return 0
+        return None
     steps = n_new - 1
     tok_s = B * steps / (ms_decode * 1e-3) * world
     weight_bytes = N_LAYERS_MODEL * sum(N * row_bytes(5, K) for _, N, K in LAYER) + VOCAB * row_bytes(3, HIDDEN)
@@ -1158,24 +1294,17 @@ def batch_arm(a):
     step_s = ms_decode / steps * 1e-3
     peak, peak_kind = measured_peaks()
     sm = [c["sm_mhz"] for c in clocks_all if c.get("sm_mhz")]
-    # CPU baseline: the reference serves concurrent requests as separate
-    # sessions on the host cores; the oracle's x86 step on all host threads,
-    # a bounded sample of one request's steps
-    from oracle.model import DenseOracle
-    oracle = DenseOracle(DenseConfig(layers=N_LAYERS_MODEL, positions=8), weights, threads=host_threads())
-    t0 = time.perf_counter()
-    n_cpu = 0
-    while n_cpu < 8 and (n_cpu == 0 or time.perf_counter() - t0 < 20.0):
-        oracle.step(prompts[0][n_cpu], n_cpu)
-        n_cpu += 1
-    cpu_s = (time.perf_counter() - t0) / n_cpu
+    cpu = model_cpu(cfg, weights, prompts[0]) if world == 1 and a.cpu_seconds > 0 else None
     line = {
         "metric": f"decode tokens/s (random-init Hy-MT2-1.8B architecture, Q2_0C linears, Q6_K tied embedding, "
                   f"{B} concurrent requests, greedy)",
         "value": round(tok_s, 1), "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": max(3, a.warmup),
         "ms_per_step": round(ms_decode / steps, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "f32 activations; fp16 tensor-core products of the dequantized weights; f32 KV cache",
+        "dtype": "f32 activations; "
+                 + ("fp16 tensor-core operands" if prec == quant.GEMM_FP16
+                    else "split-operand f32-accurate tensor-core products (3 MMAs per K chunk)")
+                 + " of the dequantized weights; f32 KV cache",
         "data": f"synthetic (seeded random-init weights, {B} seeded random 256-token prompts)",
         "config": {"workload": "hy-mt-rs config 4: 32 layers, hidden 2048, 16/4 heads x 128, SwiGLU 6144, "
                                "vocab 120832, RoPE 10000; 256-token prompts (batched prefill), 256 generated each",
@@ -1193,12 +1322,10 @@ def batch_arm(a):
         "clocks": {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": clocks_all[0].get("sm_max_mhz"),
                    "reasons": sorted({r for c in clocks_all for r in c.get("reasons", [])}),
                    "samples": sum(c.get("samples", 0) for c in clocks_all)},
-        "cpu_baseline": {"value": round(1.0 / cpu_s, 3), "unit": "tokens/s", "cores": host_threads(), "kind": "port",
-                         "sample": f"{n_cpu} decode steps of one request through oracle/model.py (x86 f32 order, "
-                                   "OpenMP over all host threads; concurrent sessions share those cores)"},
     }
-    print(json.dumps(line), flush=True)
-    return 0
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    return line
 
 
 # ---------------------------------------------------------------------------
@@ -1226,6 +1353,10 @@ def moe_arm(a):
     stream = torch.cuda.Stream(dev)
     sampler = ClockSampler("GPU-" + str(torch.cuda.get_device_properties(dev).uuid))
     res = {}
+    # The experts one step reads (those the router picks, about 100 MB with
+    # the saturated N(0, 1) router) fit in L2, so L2 is flushed between timed
+    # steps by writing a buffer twice its size, outside the timed events.
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     for T in (MOE_DECODE_TOKENS, MOE_PREFILL_TOKENS):
         x = torch.randn(T, H, generator=torch.Generator().manual_seed(T)).to(dev)
         out = torch.empty(T, H, device=dev)
@@ -1235,11 +1366,13 @@ def moe_arm(a):
             stream.synchronize()
             if T == MOE_DECODE_TOKENS:
                 sampler.start()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            for _ in range(a.steps):
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(a.steps)]
+            for b, c in evs:
+                flush.fill_(1)
+                b.record(stream)
                 layer.forward(x, T, out)
-            e1.record(stream)
+                c.record(stream)
             stream.synchronize()
             if T == MOE_DECODE_TOKENS:
                 sampler.stop()
@@ -1257,7 +1390,7 @@ def moe_arm(a):
                 stream.synchronize()
             e2e_s = (time.perf_counter() - t0) / a.steps
         hit = int((np.diff(off) > 0).sum())
-        res[T] = {"ms": e0.elapsed_time(e1) / a.steps, "e2e_s": e2e_s, "experts_hit": hit,
+        res[T] = {"ms": statistics.fmean(b.elapsed_time(c) for b, c in evs), "e2e_s": e2e_s, "experts_hit": hit,
                   "bytes": hit * expert_bytes + shared_bytes + E * H * 4,
                   "flops": 2 * T * (U * 3 * M * H + 3 * S * H + E * H)}
     failed = device_failed(quant, dev)
@@ -1266,11 +1399,8 @@ def moe_arm(a):
     if failed:
         raise RuntimeError("a kernel reported an expired bounded wait (device status word) on some rank")
     launches = layer.launches(MOE_DECODE_TOKENS) * a.steps
-    if world > 1:
-        import torch.distributed as dist
-        dist.destroy_process_group()
     if rank != 0:
-        return 0
+        return None
     dec, pre = res[MOE_DECODE_TOKENS], res[MOE_PREFILL_TOKENS]
     peak, peak_kind = measured_peaks()
     peaks = {}
@@ -1281,13 +1411,15 @@ def moe_arm(a):
         pass
     tpeak = float(peaks.get("bf16_tflops", 1590.0))
     gbs = dec["bytes"] / (ms_dec * 1e-3) / 1e9
-    # CPU baseline: the oracle port of the reference's Moe::forward on a sample
-    from oracle.moe import moe_forward_port
-    wn = {k: v.cpu().numpy() for k, v in weights.items()}
-    xs = np.random.default_rng(0).standard_normal((8, H)).astype(np.float32)
-    t0 = time.perf_counter()
-    moe_forward_port(cfg, wn, xs, host_threads())
-    cpu_tok_s = xs.shape[0] / (time.perf_counter() - t0)
+    cpu_tok_s = None
+    if world == 1 and a.cpu_seconds > 0:
+        # CPU baseline: the oracle port of the reference's Moe::forward on a sample
+        from oracle.moe import moe_forward_port
+        wn = {k: v.cpu().numpy() for k, v in weights.items()}
+        xs = np.random.default_rng(0).standard_normal((8, H)).astype(np.float32)
+        t0 = time.perf_counter()
+        moe_forward_port(cfg, wn, xs, host_threads())
+        cpu_tok_s = xs.shape[0] / (time.perf_counter() - t0)
     sm = [c["sm_mhz"] for c in clocks_all if c.get("sm_mhz")]
     line = {
         "metric": "MoE FFN decode tokens/s (config 5: 64 experts top-8, 2048->1024->2048 Q4_K, batch 64)",
@@ -1300,7 +1432,7 @@ def moe_arm(a):
                                "2048->1024->2048 SwiGLU Q4_K, shared expert 2048->1024->2048), batch 64",
                    "experts": E, "used": U,
                    "parallelism": f"expert parallel x{world} (NCCL all-to-all)" if world > 1 else "1 GPU",
-                   "l2": "expert weights 226 MB per layer > L2"},
+                   "l2": "L2 flushed between timed steps (256 MB written outside the timed events)"},
         "prefill": {"tokens": MOE_PREFILL_TOKENS, "ms_per_step": round(ms_pre, 4),
                     "tokens_per_s": round(MOE_PREFILL_TOKENS / (ms_pre * 1e-3) * world, 1),
                     "tflops": round(pre["flops"] / (ms_pre * 1e-3) / 1e12, 2),
@@ -1315,29 +1447,31 @@ def moe_arm(a):
         "clocks": {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": clocks_all[0].get("sm_max_mhz"),
                    "reasons": sorted({r for c in clocks_all for r in c.get("reasons", [])}),
                    "samples": sum(c.get("samples", 0) for c in clocks_all)},
-        "cpu_baseline": {"value": round(cpu_tok_s, 3), "unit": "tokens/s", "cores": host_threads(), "kind": "port",
-                         "sample": "8 tokens through oracle/moe.py moe_forward_port (the reference's expert loop, "
-                                   "x86 f32 order; f64 accumulation in the batch >= 8 products)"},
     }
-    print(json.dumps(line), flush=True)
-    return 0
+    if cpu_tok_s is not None:
+        line["cpu_baseline"] = {"value": round(cpu_tok_s, 3), "unit": "tokens/s", "cores": host_threads(),
+                                "kind": "port",
+                                "sample": "8 tokens through oracle/moe.py moe_forward_port (the reference's expert "
+                                          "loop, x86 f32 order; f64 accumulation in the batch >= 8 products)"}
+    return line
 
 
 def main():
     a = args_parse()
     if a.impl == "reference":
-        return reference_arm(a)
-    if a.workload == "prefill":
-        return prefill_arm(a)
-    if a.workload == "gemv":
-        return gemv_arm(a)
-    if a.workload == "tp":
-        return tp_arm(a)
-    if a.workload == "model":
-        return model_arm(a)
-    if a.workload == "moe":
-        return moe_arm(a)
-    return gpu_arm(a)
+        line = reference_arm(a)
+    else:
+        arm = {"prefill": prefill_arm, "gemv": gemv_arm, "tp": tp_arm, "model": model_arm, "moe": moe_arm}.get(
+            a.workload, gpu_arm)
+        line = arm(a)
+        if arm is gpu_arm and not a.no_suite:
+            suite = run_suite(a)
+            if line is not None:
+                line["configs"] = suite
+        finish_ranks()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
 
 
 if __name__ == "__main__":

@@ -335,6 +335,21 @@ void hyo_matmul(int t, const uint8_t* w, int64_t K, int64_t N, const float* x, i
   }
 }
 
+/* The decode half of the batch >= 8 branch of Weight::matmul
+ * (quant.rs:280-296): rows decoded to f32 (decode_unchecked per row) in
+ * parallel, out[r * K ..] = row r.  The benchmark's CPU arm multiplies the
+ * result with a BLAS f32 GEMM in place of Candle's. */
+void hyo_decode_rows(int t, const uint8_t* w, int64_t K, int64_t N, float* out, int threads) {
+  size_t rb = row_bytes_of(t, K);
+#ifdef _OPENMP
+  if (threads > 0) omp_set_num_threads(threads);
+#else
+  (void)threads;
+#endif
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < N; ++r) hyo_decode(t, w + r * rb, rb, out + r * K, (size_t)K);
+}
+
 /* SiLU gate as written at quant.rs:573-574 (and every other arm). */
 static inline float silu_mul(float g, float u) {
   float silu = g / (1.0f + expf(-g));

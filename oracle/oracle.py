@@ -58,6 +58,8 @@ def lib():
         L.hyo_gate_up_silu_q8.argtypes = [C.c_int, _u8p, _u8p, C.c_int64, C.c_int64, _i8p, _f32p, _i8p,
                                           _f32p, C.c_int]
         L.hyo_gate_up_silu_q8.restype = None
+        L.hyo_decode_rows.argtypes = [C.c_int, _u8p, C.c_int64, C.c_int64, _f32p, C.c_int]
+        L.hyo_decode_rows.restype = None
         L.hyo_max_threads.argtypes = []
         L.hyo_moe_route.argtypes = [_f32p, C.c_int, _f32p, C.c_int, C.c_int, C.c_float, C.POINTER(C.c_int32), _f32p]
         L.hyo_moe_route.restype = None
@@ -127,6 +129,15 @@ def matmul(t, w, K, N, x, batch, threads=0):
     y = np.empty(batch * N, dtype=np.float32)
     lib().hyo_matmul(int(t), _p(w, _u8p), K, N, _p(x, _f32p), batch, _p(y, _f32p), threads)
     return y.reshape(batch, N)
+
+
+def decode_rows(t, w, K, N, threads=0):
+    """Rows of a packed [K, N] weight decoded to f32 [N, K], in parallel (the
+    decode half of quant.rs:280-296)."""
+    w = _u8(w)
+    out = np.empty((N, K), dtype=np.float32)
+    lib().hyo_decode_rows(int(t), _p(w, _u8p), K, N, _p(out, _f32p), threads)
+    return out
 
 
 def gate_up_silu(t, gate, up, K, N, x, threads=0):

@@ -44,7 +44,7 @@ def test_reference_arm_runs_without_the_gpu_library():
     code = (
         "import json, sys, types, bench\n"
         "a = types.SimpleNamespace(steps=1, warmup=0, gpus=1, path='f32', copies=4, no_overlap=False)\n"
-        "bench.reference_arm(a)\n"
+        "print(json.dumps(bench.reference_arm(a)))\n"
         "maps = open('/proc/self/maps').read()\n"
         "print(json.dumps({'libhyq': 'libhyq.so' in maps, 'native': 'hy_mt_rs_b200._native' in sys.modules,\n"
         "                  'config': bench.decode_config(a, 1)}))\n")
