@@ -441,27 +441,144 @@ __device__ __forceinline__ void decode64(uint32_t row, int j4, uint32_t (&o)[32]
   }
 }
 
-// Split-operand decode: the row's 64 weights of K step j4 in k_perm order,
-// each decoded exactly in f32 (decode_elem: the reference's operation order)
-// and split into hi / scaled lo fp16 pairs (word P = slots 2P, 2P + 1).
-// `row` is the generic address of the row's packed block column.
+// Split-operand decode: the row's 64 weights of K step j4 as decode64
+// orders them, each as hi (word P of `hi`) plus lo / 2^11 (word P of `lo`),
+// where hi + lo / 2^11 equals the reference's f32 weight (decode_unchecked)
+// to 22 significant bits.
+//   Q8_0, Q2_0C: the weight is an integer code k (|k| <= 128) times the fp16
+//     block scale d; hi = fp16(k d) and the residual k d - hi is a multiple of
+//     ulp(d) with at most 8 significant bits, so fma.rn.f16x2(k, d, -hi) is
+//     exact and lo = 2^11 times it: hi + lo / 2^11 = k d exactly.
+//   STQ1_0: k is -1, 0 or 1, so hi = k d exactly and lo = 0 (no lo MMA).
+//   Q4_K, Q6_K: the reference rounds in f32 (d sc q - dmin m, d sc (q - 32)),
+//     so the weight is computed in f32 with those roundings and split.
+__device__ __forceinline__ void split2(float a, float b, uint32_t& h, uint32_t& l) {
+  const __half2 hh = __floats2half2_rn(a, b);
+  const float2 hf = __half22float2(hh);
+  h = *reinterpret_cast<const uint32_t*>(&hh);
+  l = pack_h2(__fmul_rn(__fsub_rn(a, hf.x), kSplitScale), __fmul_rn(__fsub_rn(b, hf.y), kSplitScale));
+}
+
+// exact f32 of the 16-bit integers in the two halves of v (each < 2^16), less `off`
+__device__ __forceinline__ float2 u16x2_to_f32(uint32_t v, float off) {
+  return make_float2(__fsub_rn(__uint_as_float((v & 0xffffu) | 0x4B000000u), 8388608.0f + off),
+                     __fsub_rn(__uint_as_float((v >> 16) | 0x4B000000u), 8388608.0f + off));
+}
+
 template <int FMT>
-__device__ __forceinline__ void decode64_split(const uint8_t* __restrict__ row, int j4, uint32_t (&hi)[32],
-                                               uint32_t (&lo)[32]) {
+__device__ __forceinline__ void decode64_split(uint32_t row, int j4, uint32_t (&hi)[32], uint32_t (&lo)[32]) {
+  constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024 in both halves
+  constexpr uint32_t kNeg = 0x80008000u;
+  constexpr uint32_t k2048 = 0x68006800u;   // fp16 2^11 in both halves
+  if constexpr (FMT == Q8_0) {
+    const uint32_t k1152 = 0x64806480u;
 #pragma unroll
-  for (int P = 0; P < 32; ++P) {
-    float h[2], l[2];
+    for (int b = 0; b < 2; ++b) {
+      const uint32_t blk = row + (2 * j4 + b) * 34;
+      const uint32_t d = ld_s16(blk);
+      const uint32_t d2 = d | (d << 16);
+      uint32_t w[8];
+      ld_s_words<8>(blk + 2, w);
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int o = 64 * j4 + k_perm(FMT, 2 * P + e);
-      float v;
-      if constexpr (FMT == Q8_0) v = decode_elem<Q8_0>(row + 34 * (o >> 5), o & 31);
-      else v = decode_elem<FMT>(row, o);
-      h[e] = __half2float(__float2half_rn(v));
-      l[e] = __fmul_rn(__fsub_rn(v, h[e]), kSplitScale);
+      for (int t = 0; t < 8; ++t) {
+        const uint32_t u = w[t] ^ 0x80808080u;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t q = hsub2_u(prmt_b32(u, 0x64646464u, h ? 0x4342u : 0x4140u), k1152);
+          const uint32_t x = hmul2_u(q, d2);
+          hi[16 * b + 2 * t + h] = x;
+          lo[16 * b + 2 * t + h] = hmul2_u(hfma2_u(q, d2, x ^ kNeg), k2048);
+        }
+      }
     }
-    hi[P] = pack_h2(h[0], h[1]);
-    lo[P] = pack_h2(l[0], l[1]);
+  } else if constexpr (FMT == Q2_0C) {
+    const uint32_t d = ld_s16(row);
+    const uint32_t d2 = d | (d << 16);
+    uint32_t w[4];
+    ld_s_words<4>(row + 2 + 16 * j4, w);
+    const uint32_t k2 = 0x40004000u, km3 = 0xC200C200u;  // fp16 2, -3
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+#pragma unroll
+        for (int ab = 0; ab < 2; ++ab) {
+          const uint32_t v = ((w[t] >> (2 * k + 8 * ab)) & 0x00030003u) | kMagic;
+          const uint32_t c = hfma2_u(hsub2_u(v, kMagic), k2, km3);  // 2c - 3, exact
+          const uint32_t x = hmul2_u(c, d2);
+          hi[8 * t + 2 * k + ab] = x;
+          lo[8 * t + 2 * k + ab] = hmul2_u(hfma2_u(c, d2, x ^ kNeg), k2048);
+        }
+      }
+    }
+  } else if constexpr (FMT == STQ1_0) {
+    decode64<STQ1_0>(row, j4, hi);  // (digit - 1) d is exact in fp16
+#pragma unroll
+    for (int P = 0; P < 32; ++P) lo[P] = 0u;
+  } else if constexpr (FMT == Q4_K) {
+    const int g = j4;
+    const uint4 hd = ld_s128(row);
+    const float d = half_to_f32(hd.x & 0xffffu), dmin = half_to_f32(hd.x >> 16);
+    float sm[2], mm[2];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int j = 2 * g + hh;
+      uint32_t sc, mn;
+      if (j < 4) {
+        sc = (hd.y >> (8 * j)) & 63u;
+        mn = (hd.z >> (8 * j)) & 63u;
+      } else {
+        const int k = j - 4;
+        const uint32_t hi8 = (hd.w >> (8 * k)) & 0xffu;
+        sc = (hi8 & 15u) | ((((hd.y >> (8 * k)) & 0xffu) >> 6) << 4);
+        mn = (hi8 >> 4) | ((((hd.z >> (8 * k)) & 0xffu) >> 6) << 4);
+      }
+      sm[hh] = __fmul_rn(d, (float)sc);     // exact
+      mm[hh] = __fmul_rn(dmin, (float)mn);  // exact
+    }
+    const uint4 q0 = ld_s128(row + 16 + 32 * g), q1 = ld_s128(row + 32 + 32 * g);
+    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int h = j & 1;
+        const float2 q = u16x2_to_f32((w[c] >> (4 * j)) & 0x000f000fu, 0.0f);
+        split2(__fsub_rn(__fmul_rn(sm[h], q.x), mm[h]), __fsub_rn(__fmul_rn(sm[h], q.y), mm[h]), hi[4 * c + j],
+               lo[4 * c + j]);
+      }
+    }
+  } else {  // Q6_K
+    static_assert(FMT == Q6_K, "format without a split decoder");
+    const int chunk = j4 >> 1, p0 = 2 * (j4 & 1);
+    const int nsh = (p0 >> 1) * 4;
+    uint32_t A[8], B[8], H[8];
+    ld_s_words<8>(row + chunk * 64, A);
+    ld_s_words<8>(row + chunk * 64 + 32, B);
+    ld_s_words<8>(row + 128 + chunk * 32, H);
+    const float d = half_to_f32(ld_s16(row + 208));
+    const uint32_t sc0 = ld_s16(row + 192 + chunk * 8 + 2 * p0);
+    const uint32_t sc1 = ld_s16(row + 192 + chunk * 8 + 2 * p0 + 2);
+    float sv[2][2];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      sv[0][hh] = __fmul_rn(d, (float)(int8_t)((sc0 >> (8 * hh)) & 0xffu));  // exact
+      sv[1][hh] = __fmul_rn(d, (float)(int8_t)((sc1 >> (8 * hh)) & 0xffu));
+    }
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const int hh = c >> 2;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t src = j < 2 ? A[c] : B[c];
+        const int bsh = 8 * (j & 1);
+        const int hsh = 2 * (p0 + (j >> 1));
+        const uint32_t q6 = ((src >> (nsh + bsh)) & 0x000f000fu) | (((H[c] >> (hsh + bsh)) & 0x00030003u) << 4);
+        const float2 q = u16x2_to_f32(q6, 32.0f);  // q - 32
+        const float s = sv[j >> 1][hh];
+        split2(__fmul_rn(s, q.x), __fmul_rn(s, q.y), hi[4 * c + j], lo[4 * c + j]);
+      }
+    }
   }
 }
 
@@ -631,9 +748,9 @@ __global__ void __launch_bounds__(kThreads1, 1)
           const uint32_t acc = (ks > 0 || k > 0) ? 1u : 0u;
           umma_f16_ts(tmem, a0 + 8 * k, sw128_desc(b0 + 32 * k), idesc, acc);
           if constexpr (SPLIT) {
-            // correction accumulator: hi.lo + lo.hi
+            // correction accumulator: hi.lo + lo.hi (STQ1_0 weights have no lo part)
             umma_f16_ts(tmem + BN, a0 + 8 * k, sw128_desc(b0 + L::x_half + 32 * k), idesc, acc);
-            umma_f16_ts(tmem + BN, a0 + 32 + 8 * k, sw128_desc(b0 + 32 * k), idesc, 1u);
+            if constexpr (FMT != STQ1_0) umma_f16_ts(tmem + BN, a0 + 32 + 8 * k, sw128_desc(b0 + 32 * k), idesc, 1u);
           }
         }
         if (!kPairRelease || (ks & 1) || ks == nk - 1) umma_commit(empty(rel(s)));
@@ -677,9 +794,9 @@ __global__ void __launch_bounds__(kThreads1, 1)
       const uint32_t rowp = base + L::w + ws * L::w_stage + row_off + skew;
       if constexpr (SPLIT) {
         uint32_t hi[32], lo[32];
-        decode64_split<FMT>(base_g + (rowp - base), ks % kSpw, hi, lo);
+        decode64_split<FMT>(rowp, ks % kSpw, hi, lo);
         tmem_st32(tmem + lane_base + (uint32_t)(kAcc + kAStage * s), hi);
-        tmem_st32(tmem + lane_base + (uint32_t)(kAcc + kAStage * s + 32), lo);
+        if constexpr (FMT != STQ1_0) tmem_st32(tmem + lane_base + (uint32_t)(kAcc + kAStage * s + 32), lo);
       } else {
         uint32_t o[32];
         decode64<FMT>(rowp, ks % kSpw, o);
