@@ -70,6 +70,8 @@ def args_parse():
     ap.add_argument("--gemm-precision", choices=["fp16", "f32"], default=None,
                     help="batched tensor-core products: fp16 operands, or split operands (f32-accurate, "
                          "hyq_set_gemm_precision); default fp16 for prefill, f32 for concurrent decode")
+    ap.add_argument("--kv16", action="store_true",
+                    help="model: f16 KV cache (BASELINE config 4) instead of the reference's f32 cache")
     ap.add_argument("--no-suite", action="store_true",
                     help="decode: print the config-2 line alone, without the other configs' measurements")
     return ap.parse_args()
@@ -399,10 +401,18 @@ def run_suite(a):
             sub_args(a, tokens=2048, steps=5, warmup=3, gemm_precision="f32", cpu_seconds=0))
     else:
         out["config3"] = {"M2048_tp": tp_arm(sub_args(a, tp_mode="prefill", tokens=2048, steps=10, warmup=3))}
-    out["config4"] = {"concurrency_1": model_arm(sub_args(a, concurrency=1, model_fused=False, warmup=3)),
-                      "concurrency_64": model_arm(sub_args(a, concurrency=64, warmup=3, gemm_precision="f32")),
-                      "concurrency_64_fp16_products": model_arm(
-                          sub_args(a, concurrency=64, warmup=3, gemm_precision="fp16", cpu_seconds=0))}
+    # config 4 as BASELINE names it (f16 KV cache) with split-operand products
+    # (the setting the token-stream tests pin), then labelled variants: the
+    # reference's f32 cache, and fp16 tensor-core operands
+    out["config4"] = {
+        "concurrency_1": model_arm(sub_args(a, concurrency=1, model_fused=False, warmup=3, kv16=True)),
+        "concurrency_64": model_arm(sub_args(a, concurrency=64, warmup=3, gemm_precision="f32", kv16=True)),
+        "concurrency_1_f32_kv": model_arm(sub_args(a, concurrency=1, model_fused=False, warmup=3, kv16=False,
+                                                   cpu_seconds=0)),
+        "concurrency_64_f32_kv": model_arm(sub_args(a, concurrency=64, warmup=3, gemm_precision="f32", kv16=False,
+                                                    cpu_seconds=0)),
+        "concurrency_64_fp16_products": model_arm(sub_args(a, concurrency=64, warmup=3, gemm_precision="fp16",
+                                                           kv16=True, cpu_seconds=0))}
     out["config5"] = moe_arm(sub_args(a, steps=20, warmup=3))
     return out
 
@@ -646,6 +656,16 @@ def prefill_arm(a):
         for _ in range(a.warmup):
             step()
         stream.synchronize()
+        # each call captured once and replayed, so that host-side work
+        # (argument checks, tensor maps, workspace) stays out of the timing
+        graphs = {}
+        for name, f in calls.items():
+            graphs[name] = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graphs[name], stream=stream):
+                outs[name] = f()
+        for g in graphs.values():
+            g.replay()
+        stream.synchronize()
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
@@ -655,15 +675,16 @@ def prefill_arm(a):
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(a.steps):
-            for name, f in calls.items():
+            for name, g in graphs.items():
                 b = torch.cuda.Event(enable_timing=True)
                 c = torch.cuda.Event(enable_timing=True)
                 b.record(stream)
-                f()
+                g.replay()
                 c.record(stream)
                 per[name].append((b, c))
         e1.record(stream)
     stream.synchronize()
+    del graphs
     torch.cuda.synchronize(dev)
     sampler.stop()
     # e2e: every step copies its activations in from pinned host memory, runs
@@ -671,16 +692,17 @@ def prefill_arm(a):
     # output (the down projection) back
     xh = {K: v.cpu().pin_memory() for K, v in xs.items()}
     yh = torch.empty(M, 4096).pin_memory()
-    e2e_steps = max(3, a.steps // 4)
+    e2e_steps = max(5, a.steps // 2)
     with torch.cuda.stream(stream):
-        stream.synchronize()
-        t0 = time.perf_counter()
-        for _ in range(e2e_steps):
+        for i in range(2 + e2e_steps):  # two untimed warm-up passes of the eager calls
+            if i == 2:
+                stream.synchronize()
+                t0 = time.perf_counter()
             for K in xs:
                 xs[K].copy_(xh[K], non_blocking=True)
             step()
             yh.copy_(outs["ffn_down"], non_blocking=True)
-        stream.synchronize()
+            stream.synchronize()
         e2e_s = (time.perf_counter() - t0) / e2e_steps
     h2d = sum(v.numel() * 4 for v in xs.values())
     quant.set_gemm_precision(quant.GEMM_FP16)
@@ -1075,7 +1097,8 @@ def model_arm(a):
     # the prompt's batched products: split operands (f32-accurate, the
     # parity-tested setting) unless fp16 is asked for
     prec = quant.GEMM_FP16 if a.gemm_precision == "fp16" else quant.GEMM_F32
-    model = DenseModel(cfg, weights, dev, fused=a.model_fused, gemm_precision=prec)
+    kv16 = a.kv16 and not a.model_fused
+    model = DenseModel(cfg, weights, dev, fused=a.model_fused, gemm_precision=prec, kv16=kv16)
     stream = torch.cuda.Stream(dev)
     model.capture(stream)
     prompt = np.random.default_rng(0).integers(0, cfg.vocab, n_prompt).tolist()
@@ -1161,12 +1184,13 @@ def model_arm(a):
         # the reference's published 1.8B Q2_0C decode rate, one request on an M2 Pro
         # (docs/validation.md:70-71 of hy-mt-rs)
         "vs_baseline": round(tok_s / 86.86, 2), "vs_baseline_number": "86.86 tokens/s, 1.8B Q2_0C, 1 request",
-        "dtype": "f32 activations x packed int weights; f32 KV cache; prompt products "
+        "dtype": "f32 activations x packed int weights; " + ("f16" if kv16 else "f32") + " KV cache; prompt products "
                  + ("fp16 tensor-core operands" if prec == quant.GEMM_FP16 else "split-operand f32-accurate"),
         "data": "synthetic (seeded random-init weights, 256 seeded random prompt ids)",
         "config": {"workload": "hy-mt-rs config 4: 32 layers, hidden 2048, 16/4 heads x 128, SwiGLU 6144, "
                                "vocab 120832, RoPE 10000; 256-token prompt (batched prefill), 256 generated",
                    "concurrency": 1, "positions": cfg.positions, "launch_overlap": True,
+                   "kv_cache": "f16" if kv16 else "f32",
                    "step": "one persistent kernel per token (hyq_dense_step)" if a.model_fused
                    else "per-kernel CUDA graph (~260 launches per token, programmatic dependent launch)",
                    "parallelism": f"replicas x{world}"},
@@ -1229,7 +1253,7 @@ def batch_arm(a):
     # the batched products: split operands (f32-accurate; the setting whose
     # token streams the parity tests pin to the oracle) unless fp16 is asked for
     prec = quant.GEMM_FP16 if a.gemm_precision == "fp16" else quant.GEMM_F32
-    model = DenseModel(cfg, weights, dev, gemm_precision=prec)
+    model = DenseModel(cfg, weights, dev, gemm_precision=prec, kv16=a.kv16)
     batch = DenseBatch(model, B)
     stream = torch.cuda.Stream(dev)
     batch.capture(stream)
@@ -1285,9 +1309,9 @@ def batch_arm(a):
     steps = n_new - 1
     tok_s = B * steps / (ms_decode * 1e-3) * world
     weight_bytes = N_LAYERS_MODEL * sum(N * row_bytes(5, K) for _, N, K in LAYER) + VOCAB * row_bytes(3, HIDDEN)
-    # KV cache bytes a step reads (f32 K and V rows of every visible position
+    # KV cache bytes a step reads (K and V rows, f32 or f16, of every visible position
     # of every request) and writes (one row pair per request), per layer
-    kv_row = 2 * cfg.kv_heads * cfg.head_dim * 4
+    kv_row = 2 * cfg.kv_heads * cfg.head_dim * (2 if a.kv16 else 4)
     visible = sum(n_prompt + i + 1 for i in range(1, n_new)) / steps
     kv_bytes = N_LAYERS_MODEL * B * (visible + 1) * kv_row
     step_bytes = weight_bytes + kv_bytes
@@ -1304,11 +1328,12 @@ def batch_arm(a):
         "dtype": "f32 activations; "
                  + ("fp16 tensor-core operands" if prec == quant.GEMM_FP16
                     else "split-operand f32-accurate tensor-core products (3 MMAs per K chunk)")
-                 + " of the dequantized weights; f32 KV cache",
+                 + " of the dequantized weights; " + ("f16" if a.kv16 else "f32") + " KV cache",
         "data": f"synthetic (seeded random-init weights, {B} seeded random 256-token prompts)",
         "config": {"workload": "hy-mt-rs config 4: 32 layers, hidden 2048, 16/4 heads x 128, SwiGLU 6144, "
                                "vocab 120832, RoPE 10000; 256-token prompts (batched prefill), 256 generated each",
-                   "concurrency": B, "positions": cfg.positions, "parallelism": f"replicas x{world}"},
+                   "concurrency": B, "positions": cfg.positions, "kv_cache": "f16" if a.kv16 else "f32",
+                   "parallelism": f"replicas x{world}"},
         "prompt_ms": round(ms_prompt, 2),
         "prompt": f"{B} prompts of 256 tokens, one batched forward each",
         "roofline": {"bound": "hbm", "kernel": "whole decode step (weights + KV cache per step)", "unit": "GB/s",

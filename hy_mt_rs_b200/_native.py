@@ -89,6 +89,13 @@ _SIGS = {
     "hyq_attention_seqs": ([_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _i64, _vp, _i64, _i64, _vp, _vp, _vp],
                            C.c_int),
     "hyq_argmax_rows": ([_vp, _i64, _i64, _vp, _vp, _vp], C.c_int),
+    "hyq_rope_qk_kv16": ([_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _i64, _vp, _i64, _vp, _vp, C.c_float,
+                          C.c_int, _vp, _vp, _vp], C.c_int),
+    "hyq_rope_qk_seqs_kv16": ([_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _i64, _vp, _i64, _vp, _vp,
+                               C.c_float, C.c_int, _vp, _vp, _i64, _vp], C.c_int),
+    "hyq_attention_kv16": ([_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _i64, _vp, _i64, _vp, _vp, _vp], C.c_int),
+    "hyq_attention_seqs_kv16": ([_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _i64, _vp, _i64, _i64, _vp, _vp, _vp],
+                                C.c_int),
     "hyq_gguf_open": ([C.c_char_p, C.c_int, C.POINTER(C.c_void_p)], C.c_int),
     "hyq_gguf_close": ([_vp], None),
     "hyq_gguf_profile": ([_vp], C.c_int),

@@ -11,6 +11,7 @@
 // 8-wide tail, a sequential lane sum from -0, the scalar tail); elementwise
 // products are rounded separately as Rust does (no contraction).  Only the
 // softmax exponential differs from the reference's libm expf.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -122,8 +123,9 @@ struct RopeArgs {
   const float* k_norm;
   float eps;
   int norm_first;
-  float* k_cache;        // [positions, kv_heads * dim]
-  float* v_cache;
+  void* k_cache;         // [positions, kv_heads * dim], f32 or (kv16) binary16
+  void* v_cache;
+  int kv16;
   unsigned* status;
   // independent sequences: token t is sequence t at position pos[t], its
   // caches seq_stride floats further per sequence (0: one sequence, token t
@@ -191,11 +193,22 @@ __global__ void __launch_bounds__(32) rope_qk_kernel(const __grid_constant__ Rop
   if (!is_q) {
     const size_t width = (size_t)a.kv_heads * a.dim;
     const size_t seq = a.seq_stride ? (size_t)tok * a.seq_stride : 0;
-    float* kc = a.k_cache + seq + (size_t)pos * width + (size_t)kh * a.dim;
-    float* vc = a.v_cache + seq + (size_t)pos * width + (size_t)kh * a.dim;
-    for (int i = threadIdx.x; i < a.dim; i += 32) {
-      kc[i] = hs[i];
-      vc[i] = vs[i];
+    const size_t off = seq + (size_t)pos * width + (size_t)kh * a.dim;
+    if (a.kv16) {
+      // f16 cache: each value rounded to nearest binary16
+      __half* kc = static_cast<__half*>(a.k_cache) + off;
+      __half* vc = static_cast<__half*>(a.v_cache) + off;
+      for (int i = threadIdx.x; i < a.dim; i += 32) {
+        kc[i] = __float2half_rn(hs[i]);
+        vc[i] = __float2half_rn(vs[i]);
+      }
+    } else {
+      float* kc = static_cast<float*>(a.k_cache) + off;
+      float* vc = static_cast<float*>(a.v_cache) + off;
+      for (int i = threadIdx.x; i < a.dim; i += 32) {
+        kc[i] = hs[i];
+        vc[i] = vs[i];
+      }
     }
   }
 }
@@ -237,8 +250,8 @@ inline size_t attn_smem_bytes(int dim, int group, int nsplit) {
 
 struct AttnArgs {
   const float* q;
-  const float* k_cache;
-  const float* v_cache;
+  const void* k_cache;   // f32, or binary16 in the KV16 kernels
+  const void* v_cache;
   int heads, kv_heads, dim;
   const int32_t* pos;
   int positions;
@@ -307,9 +320,42 @@ __device__ __forceinline__ void stage_rows(float* dst, int sstride, const float*
   }
 }
 
+// eight binary16 values (one 16-byte load) widened to f32 at dst (16-byte aligned)
+__device__ __forceinline__ void widen8(float* d, uint4 u) {
+  const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+  const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+  const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&u.z));
+  const float2 f3 = __half22float2(*reinterpret_cast<const __half2*>(&u.w));
+  *reinterpret_cast<float4*>(d) = make_float4(f0.x, f0.y, f1.x, f1.y);
+  *reinterpret_cast<float4*>(d + 4) = make_float4(f2.x, f2.y, f3.x, f3.y);
+}
+
+// binary16 cache rows widened to f32 in shared memory: rows x dim halves from
+// global rows `gstride` apart into f32 rows `sstride` apart, eight values per
+// 16-byte load when `vec` (dim % 8 == 0 and 16-byte aligned rows), else one
+// at a time.  Plain loads, complete when the function returns.
+template <int DIM>
+__device__ __forceinline__ void stage_rows_h(float* dst, int sstride, const __half* src, size_t gstride, int rows,
+                                             int dim, bool vec) {
+  if (vec) {
+    const int w = (DIM ? DIM : dim) >> 3;
+    for (int t = threadIdx.x; t < rows * w; t += kAttnThreads) {
+      const int i = t / w, c = t - i * w;
+      widen8(dst + i * sstride + 8 * c, *reinterpret_cast<const uint4*>(src + i * gstride + 8 * c));
+    }
+    return;
+  }
+  for (int t = threadIdx.x; t < rows * dim; t += kAttnThreads) {
+    const int i = t / dim, c = t - i * dim;
+    dst[i * sstride + c] = __half2float(src[i * gstride + c]);
+  }
+}
+
 // DIM, GRP > 0: a kernel for head size DIM and GRP query heads per kv head
-// (loops unrolled to constant offsets); 0: any shape.
-template <int DIM, int GRP>
+// (loops unrolled to constant offsets); 0: any shape.  KV16: the caches hold
+// binary16 values (widened to f32 as they are staged; the arithmetic after
+// that is the same).
+template <int DIM, int GRP, bool KV16>
 __global__ void __launch_bounds__(kAttnThreads, 3) attention_kernel(const __grid_constant__ AttnArgs a) {
   static_assert(DIM == 0 || (DIM % 16 == 0 && kAttnThreads % (DIM / 4) == 0), "specialised head size");
   grid_dependency_wait();
@@ -342,18 +388,54 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attention_kernel(const __grid
   const size_t seq = a.seq_stride ? (size_t)tok * a.seq_stride : 0;
   const int p0 = split * kAttnChunk;
   const int n = min(kAttnChunk, visible - p0);
-  const float* kg = a.k_cache + seq + (size_t)p0 * width + (size_t)kvh * dim;
-  const float* vg = a.v_cache + seq + (size_t)p0 * width + (size_t)kvh * dim;
-  const bool vec = (dim & 3) == 0 && (width & 3) == 0 && ((reinterpret_cast<uintptr_t>(kg) | reinterpret_cast<uintptr_t>(vg)) & 15) == 0;
-  // (the specialised kernel is launched only for 16-byte aligned caches)
-  // fused step: the last chunk ends at the token's own position, whose key
-  // and value rows this CTA builds instead of reading them from the cache
+  const size_t c0 = seq + (size_t)p0 * width + (size_t)kvh * dim;  // element offset of the chunk
   const bool fresh = a.fuse && split == used - 1;
   const int n_stage = fresh ? n - 1 : n;
-  stage_rows<DIM>(k_s, ks, kg, width, n_stage, dim, vec);
-  cp_async_commit();
-  stage_rows<DIM>(v_s, dim, vg, width, n_stage, dim, vec);
-  cp_async_commit();
+  bool vec;
+  // KV16, specialised head size: every 16-byte load of the chunk's K and V
+  // rows is issued up front into registers; K is widened into shared memory
+  // here, V after the scores, so the V loads overlap the score phase.
+  constexpr int kHW = DIM > 0 ? DIM / 8 : 1, kHPer = kAttnThreads / kHW, kHIt = DIM > 0 ? kAttnChunk / kHPer : 1;
+  uint4 vreg[kHIt];
+  bool v8 = false;
+  if constexpr (KV16) {
+    const __half* kg = static_cast<const __half*>(a.k_cache) + c0;
+    const __half* vg = static_cast<const __half*>(a.v_cache) + c0;
+    v8 = (dim & 7) == 0 && (width & 7) == 0 &&
+         ((reinterpret_cast<uintptr_t>(kg) | reinterpret_cast<uintptr_t>(vg)) & 15) == 0;
+    vec = (dim & 3) == 0;  // the f32 rows in shared memory take float4 reads
+    if (DIM > 0 && v8) {
+      static_assert(DIM == 0 || (kAttnThreads % kHW == 0 && kAttnChunk % kHPer == 0), "whole rows per pass");
+      const int c = threadIdx.x % kHW, i0 = threadIdx.x / kHW;
+      uint4 kreg[kHIt];
+#pragma unroll
+      for (int it = 0; it < kHIt; ++it) {
+        const int i = i0 + it * kHPer;
+        kreg[it] = i < n_stage ? *reinterpret_cast<const uint4*>(kg + i * width + 8 * c) : make_uint4(0, 0, 0, 0);
+        vreg[it] = i < n_stage ? *reinterpret_cast<const uint4*>(vg + i * width + 8 * c) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int it = 0; it < kHIt; ++it) {
+        const int i = i0 + it * kHPer;
+        if (i < n_stage) widen8(k_s + i * ks + 8 * c, kreg[it]);
+      }
+    } else {
+      stage_rows_h<DIM>(k_s, ks, kg, width, n_stage, dim, v8);
+      stage_rows_h<DIM>(v_s, dim, vg, width, n_stage, dim, v8);
+    }
+  } else {
+    const float* kg = static_cast<const float*>(a.k_cache) + c0;
+    const float* vg = static_cast<const float*>(a.v_cache) + c0;
+    vec = (dim & 3) == 0 && (width & 3) == 0 &&
+          ((reinterpret_cast<uintptr_t>(kg) | reinterpret_cast<uintptr_t>(vg)) & 15) == 0;
+    // (the specialised kernel is launched only for 16-byte aligned caches)
+    // fused step: the last chunk ends at the token's own position, whose key
+    // and value rows this CTA builds instead of reading them from the cache
+    stage_rows<DIM>(k_s, ks, kg, width, n_stage, dim, vec);
+    cp_async_commit();
+    stage_rows<DIM>(v_s, dim, vg, width, n_stage, dim, vec);
+    cp_async_commit();
+  }
   const size_t h0 = (size_t)tok * a.heads + (size_t)kvh * G;  // (token, first head of the group)
   const float* qg = a.q + h0 * dim;
   if (vec && (reinterpret_cast<uintptr_t>(qg) & 15) == 0) {
@@ -383,7 +465,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attention_kernel(const __grid
       }
       __syncwarp();
       rope_head(kr, a.k_norm, c, sn, dim, a.eps, a.norm_first);
-      // KV append (no other CTA of this call reads the row)
+      // KV append (no other CTA of this call reads the row; f32 caches only)
       float* kc = a.k_cache_w + seq + (size_t)pos * width + (size_t)kvh * dim;
       float* vc = a.v_cache_w + seq + (size_t)pos * width + (size_t)kvh * dim;
       for (int i = lane; i < dim; i += 32) {
@@ -392,7 +474,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attention_kernel(const __grid
       }
     }
   }
-  cp_async_wait<1>();  // this thread's K copies
+  if constexpr (!KV16) cp_async_wait<1>();  // this thread's K copies
   __syncthreads();
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)dim));
   if (vec && (dim & 15) == 0) {
@@ -474,7 +556,17 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attention_kernel(const __grid
       w[1] = l;
     }
   }
-  cp_async_wait<0>();
+  if constexpr (!KV16) cp_async_wait<0>();
+  if constexpr (KV16 && DIM > 0) {
+    if (v8) {
+      const int c = threadIdx.x % kHW, i0 = threadIdx.x / kHW;
+#pragma unroll
+      for (int it = 0; it < kHIt; ++it) {
+        const int i = i0 + it * kHPer;
+        if (i < n_stage) widen8(v_s + i * dim + 8 * c, vreg[it]);
+      }
+    }
+  }
   __syncthreads();
   // unnormalised outputs per (head, dim): sum_i e_i v_i.  Thread (quad dq,
   // group pg) takes four consecutive dims of every head over the positions
@@ -815,7 +907,7 @@ int hyq_embed(const hyq_weight* w, const int32_t* token, int64_t count, float* o
 static int rope_qk_impl(float* q, float* k, const float* v, int heads, int kv_heads, int head_dim,
                         const float* cos_tab, const float* sin_tab, int64_t positions, const int32_t* pos,
                         int64_t tokens, const float* q_norm, const float* k_norm, float eps, int norm_first,
-                        float* k_cache, float* v_cache, int64_t seq_stride, void* stream) {
+                        void* k_cache, void* v_cache, int64_t seq_stride, void* stream, int kv16 = 0) {
   if (!q || !k || !v || !cos_tab || !sin_tab || !pos || !k_cache || !v_cache)
     return hyq::api_fail(HYQ_E_INVALID, "rope_qk: null pointer");
   if (heads <= 0 || kv_heads <= 0 || heads % kv_heads || head_dim <= 0 || (head_dim & 1) || positions <= 0 ||
@@ -838,6 +930,7 @@ static int rope_qk_impl(float* q, float* k, const float* v, int heads, int kv_he
   a.norm_first = norm_first;
   a.k_cache = k_cache;
   a.v_cache = v_cache;
+  a.kv16 = kv16;
   a.seq_stride = seq_stride;
   int rc = hyq::api_status_word(&a.status);
   if (rc) return rc;
@@ -863,6 +956,25 @@ int hyq_rope_qk_seqs(float* q, float* k, const float* v, int heads, int kv_heads
     return hyq::api_fail(HYQ_E_SHAPE, "rope_qk_seqs: sequences' caches overlap (stride %lld)", (long long)seq_stride);
   return rope_qk_impl(q, k, v, heads, kv_heads, head_dim, cos_tab, sin_tab, positions, pos, seqs, q_norm, k_norm,
                       eps, norm_first, k_cache, v_cache, seq_stride, stream);
+}
+
+int hyq_rope_qk_kv16(float* q, float* k, const float* v, int heads, int kv_heads, int head_dim, const float* cos_tab,
+                     const float* sin_tab, int64_t positions, const int32_t* pos, int64_t tokens, const float* q_norm,
+                     const float* k_norm, float eps, int norm_first, uint16_t* k_cache, uint16_t* v_cache,
+                     void* stream) {
+  return rope_qk_impl(q, k, v, heads, kv_heads, head_dim, cos_tab, sin_tab, positions, pos, tokens, q_norm, k_norm,
+                      eps, norm_first, k_cache, v_cache, 0, stream, 1);
+}
+
+int hyq_rope_qk_seqs_kv16(float* q, float* k, const float* v, int heads, int kv_heads, int head_dim,
+                          const float* cos_tab, const float* sin_tab, int64_t positions, const int32_t* pos,
+                          int64_t seqs, const float* q_norm, const float* k_norm, float eps, int norm_first,
+                          uint16_t* k_cache, uint16_t* v_cache, int64_t seq_stride, void* stream) {
+  if (seq_stride < positions * kv_heads * head_dim)
+    return hyq::api_fail(HYQ_E_SHAPE, "rope_qk_seqs_kv16: sequences' caches overlap (stride %lld)",
+                         (long long)seq_stride);
+  return rope_qk_impl(q, k, v, heads, kv_heads, head_dim, cos_tab, sin_tab, positions, pos, seqs, q_norm, k_norm,
+                      eps, norm_first, k_cache, v_cache, seq_stride, stream, 1);
 }
 
 int hyq_attention_workspace_bytes(int heads, int head_dim, int64_t positions, int64_t tokens, size_t* bytes) {
@@ -891,9 +1003,9 @@ struct AttnFuse {
   float* v_cache;
 };
 
-static int attention_impl(const float* q, const float* k_cache, const float* v_cache, int heads, int kv_heads,
+static int attention_impl(const void* k_cache, const void* v_cache, const float* q, int heads, int kv_heads,
                           int head_dim, int64_t positions, const int32_t* pos, int64_t tokens, float* out,
-                          void* workspace, int64_t seq_stride, void* stream, const AttnFuse* fuse = nullptr) {
+                          void* workspace, int64_t seq_stride, void* stream, const AttnFuse* fuse, bool kv16) {
   if (!q || !k_cache || !v_cache || !pos || !out || !workspace)
     return hyq::api_fail(HYQ_E_INVALID, "attention: null pointer");
   if (heads <= 0 || kv_heads <= 0 || heads % kv_heads || heads / kv_heads > hyq::model::kAttnMaxGroup ||
@@ -945,16 +1057,18 @@ static int attention_impl(const float* q, const float* k_cache, const float* v_c
   // over 16-byte aligned caches: the specialised kernel
   const bool fixed = head_dim == 128 && heads == 4 * kv_heads &&
                      ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15) == 0 &&
-                     (seq_stride & 3) == 0;
-  auto kern = fixed ? hyq::model::attention_kernel<128, 4> : hyq::model::attention_kernel<0, 0>;
-  static int smem_dev[2] = {-1, -1};  // the largest shape's shared memory, allowed once per device
+                     (seq_stride & (kv16 ? 7 : 3)) == 0;
+  auto kern = kv16 ? (fixed ? hyq::model::attention_kernel<128, 4, true> : hyq::model::attention_kernel<0, 0, true>)
+                   : (fixed ? hyq::model::attention_kernel<128, 4, false> : hyq::model::attention_kernel<0, 0, false>);
+  const int kid = (kv16 ? 2 : 0) + (fixed ? 1 : 0);
+  static int smem_dev[4] = {-1, -1, -1, -1};  // the largest shape's shared memory, allowed once per device
   int dev = 0;
   cudaGetDevice(&dev);
-  if (smem_dev[fixed] != dev) {
+  if (smem_dev[kid] != dev) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)hyq::model::attn_smem_bytes(hyq::model::kAttnMaxDim, hyq::model::kAttnMaxGroup,
                                                           hyq::model::kMaxPositions / hyq::model::kAttnChunk));
-    smem_dev[fixed] = dev;
+    smem_dev[kid] = dev;
   }
   const cudaError_t e = hyq::model::launch(kern, dim3(splits, (unsigned)kv_heads, (unsigned)tokens),
                                            dim3(hyq::model::kAttnThreads), smem, (cudaStream_t)stream, a);
@@ -964,8 +1078,25 @@ static int attention_impl(const float* q, const float* k_cache, const float* v_c
 int hyq_attention(const float* q, const float* k_cache, const float* v_cache, int heads, int kv_heads,
                   int head_dim, int64_t positions, const int32_t* pos, int64_t tokens, float* out, void* workspace,
                   void* stream) {
-  return attention_impl(q, k_cache, v_cache, heads, kv_heads, head_dim, positions, pos, tokens, out, workspace, 0,
-                        stream);
+  return attention_impl(k_cache, v_cache, q, heads, kv_heads, head_dim, positions, pos, tokens, out, workspace, 0,
+                        stream, nullptr, false);
+}
+
+int hyq_attention_kv16(const float* q, const uint16_t* k_cache, const uint16_t* v_cache, int heads, int kv_heads,
+                       int head_dim, int64_t positions, const int32_t* pos, int64_t tokens, float* out,
+                       void* workspace, void* stream) {
+  return attention_impl(k_cache, v_cache, q, heads, kv_heads, head_dim, positions, pos, tokens, out, workspace, 0,
+                        stream, nullptr, true);
+}
+
+int hyq_attention_seqs_kv16(const float* q, const uint16_t* k_cache, const uint16_t* v_cache, int heads,
+                            int kv_heads, int head_dim, int64_t positions, const int32_t* pos, int64_t seqs,
+                            int64_t seq_stride, float* out, void* workspace, void* stream) {
+  if (seq_stride < positions * kv_heads * head_dim)
+    return hyq::api_fail(HYQ_E_SHAPE, "attention_seqs_kv16: sequences' caches overlap (stride %lld)",
+                         (long long)seq_stride);
+  return attention_impl(k_cache, v_cache, q, heads, kv_heads, head_dim, positions, pos, seqs, out, workspace,
+                        seq_stride, stream, nullptr, true);
 }
 
 int hyq_attention_seqs(const float* q, const float* k_cache, const float* v_cache, int heads, int kv_heads,
@@ -973,8 +1104,8 @@ int hyq_attention_seqs(const float* q, const float* k_cache, const float* v_cach
                        float* out, void* workspace, void* stream) {
   if (seq_stride < positions * kv_heads * head_dim)
     return hyq::api_fail(HYQ_E_SHAPE, "attention_seqs: sequences' caches overlap (stride %lld)", (long long)seq_stride);
-  return attention_impl(q, k_cache, v_cache, heads, kv_heads, head_dim, positions, pos, seqs, out, workspace,
-                        seq_stride, stream);
+  return attention_impl(k_cache, v_cache, q, heads, kv_heads, head_dim, positions, pos, seqs, out, workspace,
+                        seq_stride, stream, nullptr, false);
 }
 
 int hyq_rope_attention(const float* q, const float* k, const float* v, int heads, int kv_heads, int head_dim,
@@ -982,8 +1113,8 @@ int hyq_rope_attention(const float* q, const float* k, const float* v, int heads
                        const float* q_norm, const float* k_norm, float eps, int norm_first, float* k_cache,
                        float* v_cache, float* out, void* workspace, void* stream) {
   const AttnFuse f{k, v, cos_tab, sin_tab, q_norm, k_norm, eps, norm_first, k_cache, v_cache};
-  return attention_impl(q, k_cache, v_cache, heads, kv_heads, head_dim, positions, pos, 1, out, workspace, 0, stream,
-                        &f);
+  return attention_impl(k_cache, v_cache, q, heads, kv_heads, head_dim, positions, pos, 1, out, workspace, 0, stream,
+                        &f, false);
 }
 
 int hyq_rope_attention_seqs(const float* q, const float* k, const float* v, int heads, int kv_heads, int head_dim,
@@ -995,8 +1126,8 @@ int hyq_rope_attention_seqs(const float* q, const float* k, const float* v, int 
     return hyq::api_fail(HYQ_E_SHAPE, "rope_attention_seqs: sequences' caches overlap (stride %lld)",
                          (long long)seq_stride);
   const AttnFuse f{k, v, cos_tab, sin_tab, q_norm, k_norm, eps, norm_first, k_cache, v_cache};
-  return attention_impl(q, k_cache, v_cache, heads, kv_heads, head_dim, positions, pos, seqs, out, workspace,
-                        seq_stride, stream, &f);
+  return attention_impl(k_cache, v_cache, q, heads, kv_heads, head_dim, positions, pos, seqs, out, workspace,
+                        seq_stride, stream, &f, false);
 }
 
 int hyq_argmax_rows(const float* x, int64_t n, int64_t rows, int32_t* token, int32_t* pos, void* stream) {

@@ -125,13 +125,20 @@ class DenseModel:
     tokens and more, DenseBatch steps of 16 requests and more):
     quant.GEMM_FP16 (fp16 operands, the fastest) or quant.GEMM_F32 (split
     operands, f32-accurate like the batch-1 products).  Graphs keep the
-    precision they were captured with."""
+    precision they were captured with.
+    kv16: keep the KV cache in f16 (hyq_rope_qk(_seqs)_kv16 append rounds each
+    key and value to binary16, hyq_attention(_seqs)_kv16 reads it), half the
+    cache bytes of the reference's f32 cache; per-kernel steps only."""
 
     def __init__(self, cfg, weights, device, prefill_chunk=PREFILL_CHUNK, fused=False, rope_in_attention=False,
-                 gemm_precision=quant.GEMM_FP16):
+                 gemm_precision=quant.GEMM_FP16, kv16=False):
+        if kv16 and (fused or rope_in_attention):
+            raise ValueError("the f16 KV cache runs with the per-kernel step (fused=False, rope_in_attention=False)")
         self.cfg = cfg
         self.rope_in_attention = rope_in_attention
         self.precision = gemm_precision
+        self.kv16 = kv16
+        self.kv_dtype = torch.float16 if kv16 else torch.float32
         self.device = device
         H, KV = cfg.hidden, cfg.kv_heads * cfg.head_dim
         sh = weights["shapes"]
@@ -141,8 +148,8 @@ class DenseModel:
         for L in weights["layers"]:
             W = {n: wrap(L[n], cfg.linear_dtype, [sh[n][1], sh[n][0]], n) for n in sh}
             W.update({n: L[n] for n in ("input_norm", "ffn_norm", "q_norm", "k_norm")})
-            W["k_cache"] = torch.zeros(cfg.positions, KV, device=device)
-            W["v_cache"] = torch.zeros(cfg.positions, KV, device=device)
+            W["k_cache"] = torch.zeros(cfg.positions, KV, device=device, dtype=self.kv_dtype)
+            W["v_cache"] = torch.zeros(cfg.positions, KV, device=device, dtype=self.kv_dtype)
             self.layers.append(W)
         self.embed = wrap(weights["embed"], cfg.embed_dtype, [H, cfg.vocab], "token_embd")
         # lm_head: the tied embedding (model.rs:194-202), or a separate output.weight
@@ -285,11 +292,13 @@ class DenseModel:
                                              _p(W["k_norm"]), cfg.eps, 0, _p(kc), _p(vc), _p(a.attended),
                                              _p(self.attn_ws), st))
             else:
-                check(lib.hyq_rope_qk(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim,
-                                      _p(self.cos), _p(self.sin), cfg.positions, _p(pos), M, _p(W["q_norm"]),
-                                      _p(W["k_norm"]), cfg.eps, 0, _p(kc), _p(vc), st))
-                check(lib.hyq_attention(_p(a.q), _p(kc), _p(vc), cfg.heads, cfg.kv_heads, cfg.head_dim,
-                                        cfg.positions, _p(pos), M, _p(a.attended), _p(self.attn_ws), st))
+                rope = lib.hyq_rope_qk_kv16 if self.kv16 else lib.hyq_rope_qk
+                attention = lib.hyq_attention_kv16 if self.kv16 else lib.hyq_attention
+                check(rope(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim, _p(self.cos),
+                           _p(self.sin), cfg.positions, _p(pos), M, _p(W["q_norm"]), _p(W["k_norm"]), cfg.eps, 0,
+                           _p(kc), _p(vc), st))
+                check(attention(_p(a.q), _p(kc), _p(vc), cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.positions,
+                                _p(pos), M, _p(a.attended), _p(self.attn_ws), st))
             check(lib.hyq_matmul(W["o"].handle, _p(a.attended), M, _p(a.projected), st))
             # residual add fused with the norm that follows it
             check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.projected), _p(W["ffn_norm"]), H, M, cfg.eps,
@@ -399,8 +408,8 @@ class DenseBatch:
             raise ValueError("at most `positions` concurrent requests")
         self.m, self.B = model, batch
         KV = cfg.kv_heads * cfg.head_dim
-        self.caches = [(torch.zeros(batch, cfg.positions, KV, device=dev),
-                        torch.zeros(batch, cfg.positions, KV, device=dev)) for _ in model.layers]
+        self.caches = [(torch.zeros(batch, cfg.positions, KV, device=dev, dtype=model.kv_dtype),
+                        torch.zeros(batch, cfg.positions, KV, device=dev, dtype=model.kv_dtype)) for _ in model.layers]
         self.stride = cfg.positions * KV
         self.acts = _Acts(cfg, batch, dev)
         self.logits = torch.zeros(batch, cfg.vocab, device=dev)
@@ -430,12 +439,13 @@ class DenseBatch:
                                                   _p(W["q_norm"]), _p(W["k_norm"]), cfg.eps, 0, _p(kc), _p(vc),
                                                   self.stride, _p(a.attended), _p(self.attn_ws), st))
             else:
-                check(lib.hyq_rope_qk_seqs(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim,
-                                           _p(m.cos), _p(m.sin), cfg.positions, _p(self.pos), B, _p(W["q_norm"]),
-                                           _p(W["k_norm"]), cfg.eps, 0, _p(kc), _p(vc), self.stride, st))
-                check(lib.hyq_attention_seqs(_p(a.q), _p(kc), _p(vc), cfg.heads, cfg.kv_heads, cfg.head_dim,
-                                             cfg.positions, _p(self.pos), B, self.stride, _p(a.attended),
-                                             _p(self.attn_ws), st))
+                rope = lib.hyq_rope_qk_seqs_kv16 if m.kv16 else lib.hyq_rope_qk_seqs
+                attention = lib.hyq_attention_seqs_kv16 if m.kv16 else lib.hyq_attention_seqs
+                check(rope(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim, _p(m.cos), _p(m.sin),
+                           cfg.positions, _p(self.pos), B, _p(W["q_norm"]), _p(W["k_norm"]), cfg.eps, 0, _p(kc),
+                           _p(vc), self.stride, st))
+                check(attention(_p(a.q), _p(kc), _p(vc), cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.positions,
+                                _p(self.pos), B, self.stride, _p(a.attended), _p(self.attn_ws), st))
             check(lib.hyq_matmul(W["o"].handle, _p(a.attended), B, _p(a.projected), st))
             check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.projected), _p(W["ffn_norm"]), H, B, cfg.eps,
                                        _p(a.normalized), st))

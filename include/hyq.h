@@ -334,6 +334,28 @@ int hyq_rope_attention_seqs(const float* q, const float* k, const float* v, int 
                             int64_t seqs, const float* q_norm, const float* k_norm, float eps, int norm_first,
                             float* k_cache, float* v_cache, int64_t seq_stride, float* out, void* workspace,
                             void* stream);
+/* The same calls over an f16 KV cache (BASELINE config 4 asks for one; the
+ * reference's KvCache is f32, model.rs:116-120): k_cache / v_cache hold IEEE
+ * binary16 values (uint16_t bit patterns) in the same [positions, kv_heads *
+ * head_dim] layout, seq_stride counts elements.  The append rounds each
+ * rotated key and value to the nearest binary16; attention widens the
+ * cached rows to f32 as it loads them and computes as the f32 calls do, so
+ * the only difference is that rounding.  Half the cache bytes per step. */
+int hyq_rope_qk_kv16(float* q, float* k, const float* v, int heads, int kv_heads, int head_dim, const float* cos_tab,
+                     const float* sin_tab, int64_t positions, const int32_t* pos, int64_t tokens, const float* q_norm,
+                     const float* k_norm, float eps, int norm_first, uint16_t* k_cache, uint16_t* v_cache,
+                     void* stream);
+int hyq_rope_qk_seqs_kv16(float* q, float* k, const float* v, int heads, int kv_heads, int head_dim,
+                          const float* cos_tab, const float* sin_tab, int64_t positions, const int32_t* pos,
+                          int64_t seqs, const float* q_norm, const float* k_norm, float eps, int norm_first,
+                          uint16_t* k_cache, uint16_t* v_cache, int64_t seq_stride, void* stream);
+int hyq_attention_kv16(const float* q, const uint16_t* k_cache, const uint16_t* v_cache, int heads, int kv_heads,
+                       int head_dim, int64_t positions, const int32_t* pos, int64_t tokens, float* out,
+                       void* workspace, void* stream);
+int hyq_attention_seqs_kv16(const float* q, const uint16_t* k_cache, const uint16_t* v_cache, int heads,
+                            int kv_heads, int head_dim, int64_t positions, const int32_t* pos, int64_t seqs,
+                            int64_t seq_stride, float* out, void* workspace, void* stream);
+
 /* Greedy token of each of `rows` rows of n logits (generation.rs:281-290):
  * token[r]; pos[r] += 1 when pos is not NULL. */
 int hyq_argmax_rows(const float* x, int64_t n, int64_t rows, int32_t* token, int32_t* pos, void* stream);

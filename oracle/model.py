@@ -14,9 +14,13 @@ class DenseOracle:
     """Weights as numpy arrays (packed uint8 linears, f32 norms), from the same
     bytes the device model uploads."""
 
-    def __init__(self, cfg, weights, threads=0):
+    def __init__(self, cfg, weights, threads=0, kv16=False):
+        """kv16: store every cached key and value rounded to the nearest
+        binary16 (the device's f16 KV cache), everything else as the
+        reference."""
         self.cfg = cfg
         self.threads = threads
+        self.kv16 = kv16
         self.layers = [{k: (v.cpu().numpy() if hasattr(v, "cpu") else v) for k, v in L.items()}
                        for L in weights["layers"]]
         self.embed = weights["embed"].cpu().numpy()
@@ -44,6 +48,9 @@ class DenseOracle:
             k = O.rope(k, c.kv_heads, c.head_dim, cos, sin)
             q = O.rms_norm_rows(q, L["q_norm"], c.eps)  # Dense: after RoPE (model.rs:443-446)
             k = O.rms_norm_rows(k, L["k_norm"], c.eps)
+            if self.kv16:
+                k = k.astype(np.float16).astype(np.float32)
+                v = v.astype(np.float16).astype(np.float32)
             self.k_cache[i][pos] = k
             self.v_cache[i][pos] = v
             attended = O.attention(q, self.k_cache[i][:pos + 1], self.v_cache[i][:pos + 1], c.heads, c.kv_heads,

@@ -123,3 +123,41 @@ def test_batch_64_split_operands_match_oracle(cuda):
                 assert float(top[1] - top[0]) <= 2 * err, (b, i)
                 break
     assert quant.device_status() == 0
+
+
+def test_batch_64_kv16_matches_oracle(cuda):
+    """64 concurrent requests with f16 KV caches and split-operand products:
+    requests 0, 21, 42 and 63 against the oracle model with the same binary16
+    rounding of its cache (DenseOracle(kv16=True)), within 3e-4 (see
+    test_kv16_decode_matches_oracle), same tokens."""
+    import torch
+    from hy_mt_rs_b200 import quant
+    from hy_mt_rs_b200.model import DenseBatch, DenseConfig, DenseModel, random_weights
+    from oracle.model import DenseOracle
+
+    cfg = DenseConfig(layers=2, positions=96)
+    weights = random_weights(cfg, cuda, seed=66)
+    torch.cuda.synchronize()
+    model = DenseModel(cfg, weights, cuda, gemm_precision=quant.GEMM_F32, kv16=True)
+    rng = np.random.default_rng(66)
+    B, n_new = 64, 5
+    prompts = [rng.integers(0, cfg.vocab, int(n)).tolist() for n in rng.integers(1, 40, B)]
+    stream = torch.cuda.Stream(cuda)
+    try:
+        batch = DenseBatch(model, B)
+        assert batch.caches[0][0].dtype == torch.float16
+        logits = torch.zeros(n_new, B, cfg.vocab, device=cuda)
+        ids = batch.generate(prompts, n_new, stream, logits_out=logits)
+    finally:
+        quant.set_launch_overlap(False)
+    got = logits.cpu().numpy()
+    for b in (0, 21, 42, 63):
+        ref_ids, ref_logits = DenseOracle(cfg, weights, kv16=True).generate(prompts[b], n_new)
+        for i in range(n_new):
+            rel = np.linalg.norm(got[i, b] - ref_logits[i]) / np.linalg.norm(ref_logits[i])
+            assert rel < 3e-4, (b, i, rel)
+            if ids[b][i] != ref_ids[i]:
+                top = np.sort(ref_logits[i])[-2:]
+                assert float(top[1] - top[0]) <= 2 * float(np.abs(got[i, b] - ref_logits[i]).max()), (b, i)
+                break
+    assert quant.device_status() == 0

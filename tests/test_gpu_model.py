@@ -388,3 +388,73 @@ def test_fused_step_refuses_position_past_cache(cuda):
     model.enqueue_step()
     assert quant.device_status() == 0
     assert model.pos.item() == 1
+
+
+@pytest.mark.parametrize("shape,pos", [((16, 4, 128), 0), ((16, 4, 128), 777), ((8, 4, 64), 64), ((6, 2, 40), 130)])
+def test_attention_kv16_matches_oracle(cuda, shape, pos):
+    """hyq_attention_kv16 over binary16 caches (the specialised head-128
+    kernel and the general one) against the oracle's attention over the same
+    cached values widened to f32: the f32 bound of the f32-cache test."""
+    import ctypes as C
+    import torch
+    from hy_mt_rs_b200._native import check, lib
+    from oracle import oracle as O
+
+    heads, kv_heads, dim = shape
+    positions = 1024
+    g = torch.Generator().manual_seed(pos + dim)
+    q = torch.randn(heads * dim, generator=g)
+    kc = torch.randn(positions, kv_heads * dim, generator=g).half()
+    vc = torch.randn(positions, kv_heads * dim, generator=g).half()
+    ws = C.c_size_t()
+    check(lib.hyq_attention_workspace_bytes(heads, dim, positions, 1, C.byref(ws)))
+    work = torch.zeros(ws.value, dtype=torch.uint8, device=cuda)
+    d = [t.to(cuda) for t in (q, kc, vc)]
+    p = torch.tensor([pos], dtype=torch.int32, device=cuda)
+    out = torch.full((heads * dim,), float("nan"), device=cuda)
+    check(lib.hyq_attention_kv16(*(C.c_void_p(t.data_ptr()) for t in d), heads, kv_heads, dim, positions,
+                                 C.c_void_p(p.data_ptr()), 1, C.c_void_p(out.data_ptr()), C.c_void_p(work.data_ptr()),
+                                 C.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)))
+    ref = O.attention(q.numpy(), kc[:pos + 1].float().numpy(), vc[:pos + 1].float().numpy(), heads, kv_heads, dim,
+                      pos)
+    np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=2e-5, atol=2e-6)
+
+
+@pytest.mark.parametrize("batched", [False, True])
+def test_kv16_decode_matches_oracle(cuda, batched):
+    """The Dense step with an f16 KV cache (DenseModel(kv16=True)) against the
+    oracle model that rounds its cached keys and values to binary16 the same
+    way (DenseOracle(kv16=True)): logits of every step within 3e-4 (a key
+    whose f32 value differs in its last bit between the two sides can round
+    to the neighbouring binary16 value; the f32-cache path is held to 1e-4),
+    the same greedy stream; the prompt token by token or in one batched
+    forward with split-operand products."""
+    import torch
+    from hy_mt_rs_b200 import quant
+    from hy_mt_rs_b200.model import DenseConfig, DenseModel, random_weights
+    from oracle.model import DenseOracle
+
+    cfg = DenseConfig(layers=4, positions=80)
+    weights = random_weights(cfg, cuda, seed=16)
+    torch.cuda.synchronize()
+    model = DenseModel(cfg, weights, cuda, kv16=True, gemm_precision=quant.GEMM_F32)
+    assert model.layers[0]["k_cache"].dtype == torch.float16
+    oracle = DenseOracle(cfg, weights, kv16=True)
+    prompt = np.random.default_rng(16).integers(0, cfg.vocab, 40).tolist()
+    n_new = 8
+    stream = torch.cuda.Stream(cuda)
+    logits = torch.zeros(n_new, cfg.vocab, device=cuda)
+    try:
+        ids = model.generate(prompt, n_new, stream, logits_out=logits, batched_prefill=batched)
+    finally:
+        quant.set_launch_overlap(False)
+    ref_ids, ref_logits = oracle.generate(prompt, n_new)
+    got = logits.cpu().numpy()
+    for i in range(n_new):
+        rel = np.linalg.norm(got[i] - ref_logits[i]) / np.linalg.norm(ref_logits[i])
+        assert rel < 3e-4, (i, rel)
+        if ids[i] != ref_ids[i]:
+            top = np.sort(ref_logits[i])[-2:]
+            assert float(top[1] - top[0]) <= 2 * float(np.abs(got[i] - ref_logits[i]).max()), i
+            break
+    assert quant.device_status() == 0
