@@ -72,6 +72,7 @@ _SIGS = {
     "hyq_matmul_noalloc": ([_wp, _vp, _i64, _vp, _vp], C.c_int),
     "hyq_set_launch_overlap": ([C.c_int], C.c_int),
     "hyq_set_gemm_precision": ([C.c_int], C.c_int),
+    "hyq_set_peer_timeout_ms": ([C.c_int], C.c_int),
     "hyq_rope_table": ([_i64, C.c_int, C.c_float, _vp, _vp], C.c_int),
     "hyq_rms_norm": ([_vp, _vp, _i64, _i64, C.c_float, _vp, _vp], C.c_int),
     "hyq_embed": ([_wp, _vp, _i64, _vp, _vp], C.c_int),

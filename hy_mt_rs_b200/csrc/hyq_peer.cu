@@ -20,10 +20,12 @@
 //      every rank computes bit-identical totals;
 //   5. set done[rank] = epoch in every peer and wait for all done flags, so
 //      no rank overwrites its partial while a peer still reads it.
-// A wait that runs out sets HYQ_DEV_TIMEOUT_PEER in the status word and the
-// call returns without writing `out`.
+// A wait that runs out (after hyq_set_peer_timeout_ms, 5 s by default) sets
+// HYQ_DEV_TIMEOUT_PEER in the status word and the call returns without
+// writing `out`.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstring>
 
 #include "../../include/hyq.h"
@@ -35,7 +37,9 @@ namespace {
 
 constexpr int kMaxPeers = 8;
 constexpr int kPeerDataOffset = HYQ_PEER_DATA_OFFSET;
-constexpr uint64_t kPeerWaitNs = 5000000000ull;  // 5 s
+// How long a call waits for the other ranks' flags (hyq_set_peer_timeout_ms;
+// 5 s by default), read when the call is issued.
+std::atomic<uint64_t> g_peer_wait_ns{5000000000ull};
 
 struct PeerArgs {
   uint64_t region[kMaxPeers];
@@ -43,6 +47,7 @@ struct PeerArgs {
   int64_t n;
   float* out;
   unsigned* status;
+  uint64_t wait_ns;
 };
 
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
@@ -71,13 +76,13 @@ __device__ __forceinline__ float ld_volatile_f(const float* p) {
 }
 
 // Wait (one thread) until flags[q] >= epoch for every peer q != rank.
-__device__ bool wait_flags(const unsigned* flags, int rank, int world, unsigned epoch) {
+__device__ bool wait_flags(const unsigned* flags, int rank, int world, unsigned epoch, uint64_t wait_ns) {
   const uint64_t t0 = globaltimer_ns();
   for (int q = 0; q < world; ++q) {
     if (q == rank) continue;
     for (uint32_t it = 0;; ++it) {
       if ((int)(ld_acquire_sys(flags + q) - epoch) >= 0) break;
-      if ((it & 255u) == 255u && globaltimer_ns() - t0 > kPeerWaitNs) return false;
+      if ((it & 255u) == 255u && globaltimer_ns() - t0 > wait_ns) return false;
     }
   }
   return true;
@@ -95,7 +100,7 @@ __global__ void __launch_bounds__(512) peer_allreduce_kernel(const __grid_consta
     __threadfence_system();  // the partial written before this kernel, system-wide
     for (int q = 0; q < a.world; ++q)
       if (q != a.rank) st_release_sys(reinterpret_cast<unsigned*>(a.region[q]) + a.rank, e);
-    ok_s = wait_flags(reinterpret_cast<const unsigned*>(mine), a.rank, a.world, e) ? 1 : 0;
+    ok_s = wait_flags(reinterpret_cast<const unsigned*>(mine), a.rank, a.world, e, a.wait_ns) ? 1 : 0;
     if (!ok_s) atomicOr(a.status, DEV_TIMEOUT_PEER);
   }
   __syncthreads();
@@ -123,7 +128,7 @@ __global__ void __launch_bounds__(512) peer_allreduce_kernel(const __grid_consta
     const unsigned e = epoch_s;
     for (int q = 0; q < a.world; ++q)
       if (q != a.rank) st_release_sys(reinterpret_cast<unsigned*>(a.region[q] + 256) + a.rank, e);
-    if (!wait_flags(reinterpret_cast<const unsigned*>(mine + 256), a.rank, a.world, e))
+    if (!wait_flags(reinterpret_cast<const unsigned*>(mine + 256), a.rank, a.world, e, a.wait_ns))
       atomicOr(a.status, DEV_TIMEOUT_PEER);
   }
 }
@@ -132,6 +137,12 @@ __global__ void __launch_bounds__(512) peer_allreduce_kernel(const __grid_consta
 }  // namespace hyq
 
 extern "C" {
+
+int hyq_set_peer_timeout_ms(int ms) {
+  if (ms < 1 || ms > 600000) return hyq::api_fail(HYQ_E_INVALID, "set_peer_timeout_ms: %d ms (1 .. 600000)", ms);
+  hyq::g_peer_wait_ns.store((uint64_t)ms * 1000000ull, std::memory_order_relaxed);
+  return HYQ_OK;
+}
 
 int hyq_peer_alloc(size_t data_bytes, void** region, void* ipc_handle) {
   if (!region || !ipc_handle) return hyq::api_fail(HYQ_E_INVALID, "peer_alloc: null output");
@@ -188,6 +199,7 @@ int hyq_peer_allreduce(const uint64_t* regions, int rank, int world, int64_t n, 
   a.world = world;
   a.n = n;
   a.out = out;
+  a.wait_ns = hyq::g_peer_wait_ns.load(std::memory_order_relaxed);
   int rc = hyq::api_status_word(&a.status);
   if (rc) return rc;
   hyq::peer_allreduce_kernel<<<1, 512, 0, (cudaStream_t)stream>>>(a);

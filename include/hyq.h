@@ -503,7 +503,8 @@ int hyq_moe_combine(const float* shared, const float* expert_out, int64_t tokens
  *   (regions[rank] = the own one); out[0..n) = sum of the n partials at
  *   region + HYQ_PEER_DATA_OFFSET over all ranks, in rank order (identical on
  *   every rank).  Every rank makes the same sequence of calls; a call waits
- *   (bounded, 5 s -> HYQ_DEV_TIMEOUT_PEER) for the other ranks' flags, so the
+ *   (bounded, 5 s unless hyq_set_peer_timeout_ms says otherwise ->
+ *   HYQ_DEV_TIMEOUT_PEER) for the other ranks' flags, so the
  *   ranks' streams must all reach it.  At most 8 ranks; the partial may be
  *   rewritten once the call has completed on the stream.
  *   After HYQ_DEV_TIMEOUT_PEER on any rank, `out` of that call is undefined on
@@ -518,6 +519,10 @@ int hyq_peer_open(const void* ipc_handle, void** region);
 int hyq_peer_close(void* region);
 int hyq_peer_free(void* region);
 int hyq_peer_allreduce(const uint64_t* regions, int rank, int world, int64_t n, float* out, void* stream);
+/* How long hyq_peer_allreduce waits for the other ranks' flags before it
+ * gives up with HYQ_DEV_TIMEOUT_PEER: 1 .. 600000 ms, 5000 by default;
+ * process-wide, read when a call is issued. */
+int hyq_set_peer_timeout_ms(int ms);
 
 /* Synchronize `stream`, then return (and clear) the device status word of
  * the current device: 0, or HYQ_DEV_* bits from kernels whose bounded waits

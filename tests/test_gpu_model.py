@@ -458,3 +458,39 @@ def test_kv16_decode_matches_oracle(cuda, batched):
             assert float(top[1] - top[0]) <= 2 * float(np.abs(got[i] - ref_logits[i]).max()), i
             break
     assert quant.device_status() == 0
+
+
+@pytest.mark.parametrize("chunk", [1, 3, 8, 13, 256])
+def test_chunked_prefill_matches_token_by_token(cuda, chunk):
+    """Prefill in chunks (the reference checks chunk sizes 1, 3, 8 and 13
+    against full-prefix prefill, tests/inference.rs:10-33; 256 is its
+    PREFILL_CHUNK, model.rs:18) of a 300-token prompt, so every size crosses
+    chunk boundaries: the logits after the prompt and of the next steps within
+    1e-4 of feeding the prompt token by token (f32 products; chunks of 16
+    tokens and more on split-operand tensor-core products), the same greedy
+    tokens."""
+    import torch
+    from hy_mt_rs_b200 import quant
+    from hy_mt_rs_b200.model import DenseConfig, DenseModel, random_weights
+
+    cfg = DenseConfig(layers=2, positions=320)
+    weights = random_weights(cfg, cuda, seed=300)
+    torch.cuda.synchronize()
+    prompt = np.random.default_rng(300).integers(0, cfg.vocab, 300).tolist()
+    n_new = 4
+    stream = torch.cuda.Stream(cuda)
+    runs = []
+    try:
+        for c, batched in ((cfg.positions, False), (chunk, True)):
+            model = DenseModel(cfg, weights, cuda, prefill_chunk=c, gemm_precision=quant.GEMM_F32)
+            logits = torch.zeros(n_new, cfg.vocab, device=cuda)
+            ids = model.generate(prompt, n_new, stream, logits_out=logits, batched_prefill=batched)
+            runs.append((ids, logits.cpu().numpy()))
+    finally:
+        quant.set_launch_overlap(False)
+    (ref_ids, ref), (ids, got) = runs
+    for i in range(n_new):
+        rel = np.linalg.norm(got[i] - ref[i]) / np.linalg.norm(ref[i])
+        assert rel < 1e-4, (i, rel)
+    assert ids == ref_ids
+    assert quant.device_status() == 0

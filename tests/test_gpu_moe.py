@@ -118,3 +118,31 @@ def test_moe_forward_matches_oracle(cuda, hidden, experts, used, mid, T):
     # the routing weights and the combine order are the reference's: with the
     # device's expert outputs, the combine is exact
     del wt
+
+
+@pytest.mark.parametrize("T,split", [(64, False), (64, True), (200, True)])
+def test_moe_config5_shape_matches_oracle(cuda, T, split):
+    """BASELINE config 5's real layer shape -- hidden 2048, 64 experts, top 8,
+    expert and shared FFN 2048 -> 1024 -> 2048 in Q4_K -- against the oracle
+    port of Moe::forward (oracle/moe.py): routing indices identical, the
+    layer within 2e-3 relative L2 with fp16 tensor-core operands and within
+    2e-5 with split operands (GEMM_F32), whose expert products agree with an
+    f32 GEMM."""
+    import torch
+    from hy_mt_rs_b200 import quant
+    from hy_mt_rs_b200.moe import MoeConfig
+    from oracle import moe as OM
+
+    cfg = MoeConfig()
+    assert (cfg.hidden, cfg.experts, cfg.used, cfg.mid, cfg.shared_mid) == (2048, 64, 8, 1024, 1024)
+    layer, wn = _setup(cuda, cfg, seed=5 + T)
+    x = torch.randn(T, cfg.hidden, generator=torch.Generator().manual_seed(T)).to(cuda)
+    with quant.gemm_precision(quant.GEMM_F32 if split else quant.GEMM_FP16):
+        out = layer.forward(x, T)
+    idx = layer._buffers(T, cuda)["idx"].cpu().numpy()
+    ref, ridx, _ = OM.moe_forward(cfg, wn, x.cpu().numpy())
+    assert (idx == ridx).all()
+    got = out.cpu().numpy().astype(np.float64)
+    rel = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+    assert rel < (2e-5 if split else 2e-3), rel
+    assert quant.device_status() == 0

@@ -95,3 +95,48 @@ def test_peer_allreduce_two_gpus():
         p.join(timeout=60)
         assert p.exitcode == 0
     assert res == {0: True, 1: True}
+
+
+def test_peer_wait_runs_out_and_reports(cuda):
+    """Failure detection of a bounded device wait, on one GPU with no peer:
+    rank 0 of a two-rank all-reduce whose second region is a local buffer
+    that no rank ever flags.  The kernel's wait for that rank's ready flag
+    must give up after the limit set by hyq_set_peer_timeout_ms (200 ms
+    here), raise HYQ_DEV_TIMEOUT_PEER in the status word and return without
+    writing `out`; the context stays usable (a product afterwards runs
+    clean).  Both regions are this process's own device memory: no IPC
+    mapping, no second GPU, no multicast."""
+    import ctypes as C
+    import time
+
+    import torch
+    from hy_mt_rs_b200 import quant, synth
+    from hy_mt_rs_b200._native import check, lib
+
+    n = 1024
+    regions, handles = [], []
+    for _ in range(2):
+        r, h = C.c_void_p(), (C.c_uint8 * 64)()
+        check(lib.hyq_peer_alloc(4 * n, C.byref(r), h))
+        regions.append(r.value)
+        handles.append(h)
+    arr = (C.c_uint64 * 2)(*regions)
+    out = torch.full((n,), float("nan"), device=cuda)
+    stream = torch.cuda.current_stream(cuda)
+    try:
+        check(lib.hyq_set_peer_timeout_ms(200))
+        t0 = time.perf_counter()
+        check(lib.hyq_peer_allreduce(arr, 0, 2, n, C.c_void_p(out.data_ptr()), C.c_void_p(stream.cuda_stream)))
+        status = quant.device_status(cuda)    # synchronizes: the kernel has returned
+        waited = time.perf_counter() - t0
+        assert status == 16, status           # HYQ_DEV_TIMEOUT_PEER
+        assert 0.15 < waited < 5.0, waited
+        assert torch.isnan(out).all()         # nothing written
+        # the context still works
+        w = quant.Weight(synth.random_packed(5, 256, 2048, seed=1, device=cuda), 5, [2048, 256])
+        y = w.matmul(torch.randn(2048, device=cuda), 1)
+        assert torch.isfinite(y).all() and quant.device_status(cuda) == 0
+    finally:
+        check(lib.hyq_set_peer_timeout_ms(5000))
+        for r in regions:
+            check(lib.hyq_peer_free(C.c_void_p(r)))
