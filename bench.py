@@ -52,7 +52,8 @@ def args_parse():
     ap.add_argument("--no-overlap", action="store_true",
                     help="decode: plain stream order instead of overlapped launches (hyq_set_launch_overlap)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
-    ap.add_argument("--workload", choices=["decode", "prefill", "gemv", "tp", "model", "moe"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "gemv", "tp", "model", "moe", "moe-stack"],
+                    default="decode",
                     help="decode: config 2 (default line); prefill: config 3 (7B layer GEMMs); "
                          "gemv: config 1 (one 6144x2048 product, L2 defeated by rotating copies)")
     ap.add_argument("--tp-mode", choices=["decode", "prefill"], default="decode",
@@ -413,7 +414,8 @@ def run_suite(a):
                                                     cpu_seconds=0)),
         "concurrency_64_fp16_products": model_arm(sub_args(a, concurrency=64, warmup=3, gemm_precision="fp16",
                                                            kv16=True, cpu_seconds=0))}
-    out["config5"] = moe_arm(sub_args(a, steps=20, warmup=3))
+    out["config5"] = {"moe_ffn": moe_arm(sub_args(a, steps=20, warmup=3)),
+                      "layer_stack": moe_stack_arm(sub_args(a, warmup=3))}
     return out
 
 
@@ -1219,10 +1221,11 @@ def model_cpu(cfg, weights, prompt):
     reference's x86 decode path, oracle/model.py) of the same model on all
     host threads, a bounded sample of steps; one request (the reference
     serves concurrent requests as separate sessions on the same cores)."""
-    from hy_mt_rs_b200.model import DenseConfig
+    import dataclasses
+
     from oracle.model import DenseOracle
 
-    oracle = DenseOracle(DenseConfig(layers=cfg.layers, positions=8), weights, threads=host_threads())
+    oracle = DenseOracle(dataclasses.replace(cfg, positions=8), weights, threads=host_threads())
     t0 = time.perf_counter()
     n = 0
     while n < 8 and (n == 0 or time.perf_counter() - t0 < 20.0):
@@ -1481,13 +1484,156 @@ def moe_arm(a):
     return line
 
 
+MOE_STACK_LAYERS = 8
+
+
+def moe_stack_arm(a):
+    """Config 5's layer stack: a random-init HyV3 decoder (model.rs:210-231,
+    684-726) of MOE_STACK_LAYERS layers -- hidden 2048, attention 16 / 4 heads
+    of 128, layer 0 a dense SwiGLU FFN of 6144, layers 1.. the MoE FFN (64
+    experts top 8, 2048 -> 1024 -> 2048, shared expert 1024), Q4_K linears and
+    experts, Q6_K embedding and output of 120832 -- decoding 64 requests
+    (64-token prompts, 64 steps) and prefilling 1024 tokens (four 256-token
+    chunks).  Split-operand products (the setting the HyV3 parity tests pin)."""
+    import numpy as np
+    import torch
+
+    world, rank, dev = init_ranks()
+    import hy_mt_rs_b200.quant  # noqa: F401  (loads libhyq.so or raises)
+    from hy_mt_rs_b200 import quant
+    from hy_mt_rs_b200.model import DenseBatch, DenseConfig, DenseModel, random_weights
+
+    B, n_prompt, n_new, M = 64, 64, 64, 1024
+    cfg = DenseConfig(arch="hyv3", layers=MOE_STACK_LAYERS, ffn=6144, linear_dtype=2, embed_dtype=3,
+                      positions=M + 8)
+    weights = random_weights(cfg, dev, seed=5)
+    torch.cuda.synchronize(dev)
+    model = DenseModel(cfg, weights, dev, gemm_precision=quant.GEMM_F32)
+    stream = torch.cuda.Stream(dev)
+    sampler = ClockSampler("GPU-" + str(torch.cuda.get_device_properties(dev).uuid))
+    # ---- prefill: 1024 tokens of one request, the reference's 256-token chunks
+    ids = torch.from_numpy(np.random.default_rng(5).integers(0, cfg.vocab, M).astype(np.int32)).to(dev)
+    with torch.cuda.stream(stream):
+        for _ in range(max(2, a.warmup)):
+            model.reset()
+            for c0 in range(0, M, model.chunk):
+                model.prefill(ids[c0:c0 + model.chunk])
+        stream.synchronize()
+        evs = []
+        for _ in range(3):
+            model.reset()
+            b, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            b.record(stream)
+            for c0 in range(0, M, model.chunk):
+                model.prefill(ids[c0:c0 + model.chunk])
+            c.record(stream)
+            evs.append((b, c))
+        stream.synchronize()
+    ms_prefill = statistics.fmean(b.elapsed_time(c) for b, c in evs)
+    # ---- decode: 64 requests
+    batch = DenseBatch(model, B)
+    rng = np.random.default_rng(6)
+    prompts = [rng.integers(0, cfg.vocab, n_prompt).tolist() for _ in range(B)]
+    with torch.cuda.stream(stream):
+        batch.capture(stream)
+        batch.reset()
+        batch.prefill_all(prompts)
+        for _ in range(3):
+            batch.graph.replay()
+        batch.reset()
+        batch.prefill_all(prompts)
+        stream.synchronize()
+        sampler.start()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n_new - 1):
+            batch.graph.replay()
+        e1.record(stream)
+        stream.synchronize()
+        sampler.stop()
+        # experts each MoE layer read in the last step (its routing)
+        hit = [int((torch.diff(W["moe"]._buffers(B, dev)["off"]) > 0).sum()) for W in model.layers if "moe" in W]
+        # e2e: every step's tokens read back to the host, one step late
+        batch.reset()
+        batch.prefill_all(prompts)
+        tok_host = torch.empty(n_new, B, dtype=torch.int32).pin_memory()
+        done = [torch.cuda.Event() for _ in range(n_new)]
+        stream.synchronize()
+        t0 = time.perf_counter()
+        for i in range(n_new - 1):
+            batch.graph.replay()
+            tok_host[i].copy_(batch.tokens, non_blocking=True)
+            done[i].record(stream)
+            if i:
+                done[i - 1].synchronize()
+        done[n_new - 2].synchronize()
+        e2e_s = time.perf_counter() - t0
+    failed = device_failed(quant, dev)
+    steps = n_new - 1
+    (ms_decode, ms_prefill, failed), clocks_all = reduce_over_ranks([e0.elapsed_time(e1), ms_prefill, failed + 0.0],
+                                                                     sampler.summary(), dev)
+    if failed:
+        raise RuntimeError("a kernel reported an expired bounded wait (device status word) on some rank")
+    launches = batch.launches()
+    batch.graph = None
+    if rank != 0:
+        return None
+    H, A, KV = cfg.hidden, cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
+    attn_bytes = (A + 2 * KV) * row_bytes(2, H) + H * row_bytes(2, A)
+    mc = cfg.moe_config()
+    expert_bytes = 3 * mc.mid * row_bytes(2, H)
+    moe_fixed = 3 * mc.shared_mid * row_bytes(2, H) + mc.experts * H * 4     # shared expert + F32 router
+    dense_ffn = 3 * cfg.ffn * row_bytes(2, H)
+    out_bytes = cfg.vocab * row_bytes(3, H)
+    kv_row = 2 * KV * 4
+    kv_bytes = cfg.layers * B * (n_prompt + n_new / 2) * kv_row
+    step_bytes = (cfg.layers * attn_bytes + dense_ffn + sum(h * expert_bytes + moe_fixed for h in hit) + out_bytes
+                  + kv_bytes)
+    step_s = ms_decode / steps * 1e-3
+    peak, peak_kind = measured_peaks()
+    moe_layers = cfg.layers - 1
+    flops_tok = 2 * (cfg.layers * (A + 2 * KV) * H + cfg.layers * H * A + 3 * cfg.ffn * H
+                     + moe_layers * (mc.used * 3 * mc.mid * H + 3 * mc.shared_mid * H + mc.experts * H))
+    sm = [c["sm_mhz"] for c in clocks_all if c.get("sm_mhz")]
+    line = {
+        "metric": f"MoE layer-stack decode tokens/s (config 5: {cfg.layers} HyV3 layers, 64 experts top-8, "
+                  f"16/4 x 128 attention; 64 requests)",
+        "value": round(B / step_s * world, 1), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "warmup": 3, "ms_per_step": round(ms_decode / steps, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "split-operand f32-accurate tensor-core products (experts, batched projections); f32 KV cache",
+        "data": "synthetic (seeded random-init HyV3 weights, N(0,1) F32 routers; seeded prompts)",
+        "config": {"workload": f"hy-mt-rs config 5 layer stack: {cfg.layers} HyV3 layers (layer 0 dense FFN 6144, "
+                               "layers 1.. MoE 64 experts top 8 2048->1024->2048 + shared 1024), attention 16/4 x "
+                               "128 Q4_K, Q6_K embedding and output 120832; decode 64 requests with 64-token "
+                               "prompts, prefill 1024 tokens",
+                   "layers": cfg.layers, "concurrency": B, "parallelism": f"replicas x{world}"},
+        "prefill": {"tokens": M, "ms": round(ms_prefill, 3), "tokens_per_s": round(M / (ms_prefill * 1e-3), 1),
+                    "tflops": round(flops_tok * M / (ms_prefill * 1e-3) / 1e12, 2),
+                    "how": "four 256-token batched forwards (model.rs:640-646), CUDA events"},
+        "roofline": {"bound": "hbm", "kernel": "whole decode step (weights read + experts hit + KV cache)",
+                     "unit": "GB/s", "achieved": round(step_bytes / step_s / 1e9, 1), "peak": peak,
+                     "peak_kind": peak_kind, "frac": round(step_bytes / step_s / 1e9 / peak, 4), "traffic": None,
+                     "algorithmic_bytes_per_launch": int(step_bytes), "experts_hit_per_layer": hit},
+        "e2e": {"value": round(B * steps / e2e_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 4 * B, "how": "graph replay per step, each step's tokens read back one step late"},
+        "gpu_launches": steps * launches,
+        "clocks": {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": clocks_all[0].get("sm_max_mhz"),
+                   "reasons": sorted({r for c in clocks_all for r in c.get("reasons", [])}),
+                   "samples": sum(c.get("samples", 0) for c in clocks_all)},
+    }
+    if world == 1 and a.cpu_seconds > 0:
+        line["cpu_baseline"] = model_cpu(cfg, weights, prompts[0])
+    return line
+
+
 def main():
     a = args_parse()
     if a.impl == "reference":
         line = reference_arm(a)
     else:
-        arm = {"prefill": prefill_arm, "gemv": gemv_arm, "tp": tp_arm, "model": model_arm, "moe": moe_arm}.get(
-            a.workload, gpu_arm)
+        arm = {"prefill": prefill_arm, "gemv": gemv_arm, "tp": tp_arm, "model": model_arm, "moe": moe_arm,
+               "moe-stack": moe_stack_arm}.get(a.workload, gpu_arm)
         line = arm(a)
         if arm is gpu_arm and not a.no_suite:
             suite = run_suite(a)

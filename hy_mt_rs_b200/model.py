@@ -5,6 +5,11 @@ gate/up-SiLU -> down + residual, then the output norm, the lm_head product
 and the greedy argmax.  The position and the token live in device memory,
 so one captured CUDA graph replays a whole token step.
 
+The HyV3 architecture (hy_v3, model.rs:139-140, 210-231) runs through the
+same runner: the q/k RMSNorm before RoPE (model.rs:425-428), the MoE FFN
+(Moe::forward, model.rs:684-726; hy_mt_rs_b200.moe.MoeLayer) in every layer
+but the first, and an output matrix of its own.
+
 Weights are packed GGUF bytes (any hyq_dtype for the linears; the embedding
 is tied to the lm_head as in the 1.8B model); norms are f32.  The KV cache is
 f32, as in the reference (model.rs:116-120).
@@ -33,6 +38,22 @@ class DenseConfig:
     positions: int = 512        # KV-cache capacity (prompt + generated tokens)
     linear_dtype: int = 5       # Q2_0C
     embed_dtype: int = 3        # Q6_K
+    # "dense" (hunyuan-dense) or "hyv3" (hy_v3: MoE FFN from layer 1, q/k
+    # norm before RoPE, separate output matrix); MoE shapes for hyv3
+    arch: str = "dense"
+    experts: int = 64
+    experts_used: int = 8
+    expert_ffn: int = 1024
+    shared_ffn: int = 1024
+    expert_scale: float = 1.0
+    expert_normalize: bool = True
+    expert_dtype: int = 2       # Q4_K
+
+    def moe_config(self):
+        from .moe import MoeConfig
+        return MoeConfig(hidden=self.hidden, experts=self.experts, used=self.experts_used, mid=self.expert_ffn,
+                         shared_mid=self.shared_ffn, normalize=self.expert_normalize, scale=self.expert_scale,
+                         dtype=self.expert_dtype)
 
 
 def random_weights(cfg, device, seed=0):
@@ -49,12 +70,19 @@ def random_weights(cfg, device, seed=0):
     shapes = {"q": (A, H), "k": (KV, H), "v": (KV, H), "o": (H, A), "gate": (F, H), "up": (F, H), "down": (H, F)}
     layers = []
     for i in range(cfg.layers):
+        moe = cfg.arch == "hyv3" and i > 0   # HyV3: every layer but the first (model.rs:210)
         L = {n: synth.random_packed(cfg.linear_dtype, N, K, seed=seed + 1000 * i + j, device=device)
-             for j, (n, (N, K)) in enumerate(shapes.items())}
+             for j, (n, (N, K)) in enumerate(shapes.items()) if not (moe and n in ("gate", "up", "down"))}
+        if moe:
+            from .moe import random_moe_weights
+            L["moe"] = random_moe_weights(cfg.moe_config(), device, seed=seed + 1000 * i + 500)
         L.update(input_norm=norm(H), ffn_norm=norm(H), q_norm=norm(cfg.head_dim), k_norm=norm(cfg.head_dim))
         layers.append(L)
     embed = synth.random_packed(cfg.embed_dtype, cfg.vocab, H, seed=seed + 7, device=device)
-    return {"layers": layers, "embed": embed, "output_norm": norm(H), "shapes": shapes}
+    out = {"layers": layers, "embed": embed, "output_norm": norm(H), "shapes": shapes}
+    if cfg.arch == "hyv3":   # HyV3 requires separate output weights (model.rs:198-201)
+        out["output"] = synth.random_packed(cfg.embed_dtype, cfg.vocab, H, seed=seed + 9, device=device)
+    return out
 
 
 def weights_digest(weights):
@@ -71,8 +99,13 @@ def weights_digest(weights):
 
     for L in weights["layers"]:
         for n in ("q", "k", "v", "o", "gate", "up", "down", "input_norm", "ffn_norm", "q_norm", "k_norm"):
-            add(L[n])
+            if n in L:
+                add(L[n])
+        for n in sorted(L.get("moe", {})):
+            add(L["moe"][n])
     add(weights["embed"])
+    if weights.get("output") is not None:
+        add(weights["output"])
     add(weights["output_norm"])
     return h.hexdigest()
 
@@ -134,6 +167,11 @@ class DenseModel:
                  gemm_precision=quant.GEMM_FP16, kv16=False):
         if kv16 and (fused or rope_in_attention):
             raise ValueError("the f16 KV cache runs with the per-kernel step (fused=False, rope_in_attention=False)")
+        if cfg.arch not in ("dense", "hyv3"):
+            raise ValueError(f"unknown architecture {cfg.arch}")
+        if fused and cfg.arch != "dense":
+            raise ValueError("the persistent step kernel runs the Dense architecture")
+        self.norm_first = 1 if cfg.arch == "hyv3" else 0   # q/k norm before RoPE (model.rs:425-428)
         self.cfg = cfg
         self.rope_in_attention = rope_in_attention
         self.precision = gemm_precision
@@ -146,14 +184,18 @@ class DenseModel:
         # packed bytes (wrapped with the configured dtypes) or ready device weights
         wrap = lambda v, t, dims, n: v if isinstance(v, quant.Weight) else quant.Weight(v, t, dims, name=n)  # noqa: E731
         for L in weights["layers"]:
-            W = {n: wrap(L[n], cfg.linear_dtype, [sh[n][1], sh[n][0]], n) for n in sh}
+            W = {n: wrap(L[n], cfg.linear_dtype, [sh[n][1], sh[n][0]], n) for n in sh if n in L}
             W.update({n: L[n] for n in ("input_norm", "ffn_norm", "q_norm", "k_norm")})
+            if "moe" in L:
+                from .moe import MoeLayer
+                W["moe"] = L["moe"] if isinstance(L["moe"], MoeLayer) else MoeLayer(cfg.moe_config(), L["moe"])
             W["k_cache"] = torch.zeros(cfg.positions, KV, device=device, dtype=self.kv_dtype)
             W["v_cache"] = torch.zeros(cfg.positions, KV, device=device, dtype=self.kv_dtype)
             self.layers.append(W)
         self.embed = wrap(weights["embed"], cfg.embed_dtype, [H, cfg.vocab], "token_embd")
         # lm_head: the tied embedding (model.rs:194-202), or a separate output.weight
-        self.output = weights.get("output") or self.embed
+        out_w = weights.get("output")
+        self.output = self.embed if out_w is None else wrap(out_w, cfg.embed_dtype, [H, cfg.vocab], "output")
         self.output_norm = weights["output_norm"]
         self.one = _Acts(cfg, 1, device)          # the graph-captured single-token step
         self.chunk = min(prefill_chunk, cfg.positions)
@@ -289,13 +331,14 @@ class DenseModel:
             if M == 1 and self.rope_in_attention:
                 check(lib.hyq_rope_attention(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim,
                                              _p(self.cos), _p(self.sin), cfg.positions, _p(pos), _p(W["q_norm"]),
-                                             _p(W["k_norm"]), cfg.eps, 0, _p(kc), _p(vc), _p(a.attended),
+                                             _p(W["k_norm"]), cfg.eps, self.norm_first, _p(kc), _p(vc), _p(a.attended),
                                              _p(self.attn_ws), st))
             else:
                 rope = lib.hyq_rope_qk_kv16 if self.kv16 else lib.hyq_rope_qk
                 attention = lib.hyq_attention_kv16 if self.kv16 else lib.hyq_attention
                 check(rope(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim, _p(self.cos),
-                           _p(self.sin), cfg.positions, _p(pos), M, _p(W["q_norm"]), _p(W["k_norm"]), cfg.eps, 0,
+                           _p(self.sin), cfg.positions, _p(pos), M, _p(W["q_norm"]), _p(W["k_norm"]), cfg.eps,
+                           self.norm_first,
                            _p(kc), _p(vc), st))
                 check(attention(_p(a.q), _p(kc), _p(vc), cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.positions,
                                 _p(pos), M, _p(a.attended), _p(self.attn_ws), st))
@@ -303,13 +346,16 @@ class DenseModel:
             # residual add fused with the norm that follows it
             check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.projected), _p(W["ffn_norm"]), H, M, cfg.eps,
                                        _p(a.normalized), st))
-            if M == 1:
+            if "moe" in W:      # Moe::forward (model.rs:688-726)
+                W["moe"].forward(a.normalized, M, out=a.ff)
+            elif M == 1:
                 check(lib.hyq_matmul_gate_up_silu(W["gate"].handle, W["up"].handle, _p(a.normalized), _p(a.gate),
                                                   st))
             else:
                 check(lib.hyq_matmul_gate_up_silu_batch(W["gate"].handle, W["up"].handle, _p(a.normalized), M,
                                                         _p(a.gate), st))
-            check(lib.hyq_matmul(W["down"].handle, _p(a.gate), M, _p(a.ff), st))
+            if "moe" not in W:
+                check(lib.hyq_matmul(W["down"].handle, _p(a.gate), M, _p(a.ff), st))
             nxt = self.layers[i + 1]["input_norm"] if i + 1 < len(self.layers) else self.output_norm
             check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.ff), _p(nxt), H, M, cfg.eps, _p(a.normalized), st))
         # logits of the last token only (model.rs:619-622)
@@ -339,8 +385,11 @@ class DenseModel:
 
     # kernel launches of one enqueue_step
     def launches(self):
+        if self._step is not None:
+            return 1
         per_layer = 7 if self.rope_in_attention else 8
-        return 1 if self._step is not None else 2 + per_layer * self.cfg.layers + 2
+        # a MoE layer runs MoeLayer's launches in place of gate/up and down
+        return 4 + sum(per_layer + (W["moe"].launches(1) - 2 if "moe" in W else 0) for W in self.layers)
 
     def capture(self, stream):
         """Capture enqueue_step as one CUDA graph on `stream`."""
@@ -436,22 +485,26 @@ class DenseBatch:
             if m.rope_in_attention:
                 check(lib.hyq_rope_attention_seqs(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim,
                                                   _p(m.cos), _p(m.sin), cfg.positions, _p(self.pos), B,
-                                                  _p(W["q_norm"]), _p(W["k_norm"]), cfg.eps, 0, _p(kc), _p(vc),
+                                                  _p(W["q_norm"]), _p(W["k_norm"]), cfg.eps, m.norm_first, _p(kc), _p(vc),
                                                   self.stride, _p(a.attended), _p(self.attn_ws), st))
             else:
                 rope = lib.hyq_rope_qk_seqs_kv16 if m.kv16 else lib.hyq_rope_qk_seqs
                 attention = lib.hyq_attention_seqs_kv16 if m.kv16 else lib.hyq_attention_seqs
                 check(rope(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim, _p(m.cos), _p(m.sin),
-                           cfg.positions, _p(self.pos), B, _p(W["q_norm"]), _p(W["k_norm"]), cfg.eps, 0, _p(kc),
+                           cfg.positions, _p(self.pos), B, _p(W["q_norm"]), _p(W["k_norm"]), cfg.eps, m.norm_first,
+                           _p(kc),
                            _p(vc), self.stride, st))
                 check(attention(_p(a.q), _p(kc), _p(vc), cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.positions,
                                 _p(self.pos), B, self.stride, _p(a.attended), _p(self.attn_ws), st))
             check(lib.hyq_matmul(W["o"].handle, _p(a.attended), B, _p(a.projected), st))
             check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.projected), _p(W["ffn_norm"]), H, B, cfg.eps,
                                        _p(a.normalized), st))
-            check(lib.hyq_matmul_gate_up_silu_batch(W["gate"].handle, W["up"].handle, _p(a.normalized), B,
-                                                    _p(a.gate), st))
-            check(lib.hyq_matmul(W["down"].handle, _p(a.gate), B, _p(a.ff), st))
+            if "moe" in W:      # Moe::forward over the requests' rows
+                W["moe"].forward(a.normalized, B, out=a.ff)
+            else:
+                check(lib.hyq_matmul_gate_up_silu_batch(W["gate"].handle, W["up"].handle, _p(a.normalized), B,
+                                                        _p(a.gate), st))
+                check(lib.hyq_matmul(W["down"].handle, _p(a.gate), B, _p(a.ff), st))
             nxt = m.layers[i + 1]["input_norm"] if i + 1 < len(m.layers) else m.output_norm
             check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.ff), _p(nxt), H, B, cfg.eps, _p(a.normalized), st))
         check(lib.hyq_matmul(m.output.handle, _p(a.normalized), B, _p(self.logits), st))
@@ -467,13 +520,14 @@ class DenseBatch:
         KV = cfg.kv_heads * cfg.head_dim
         if B >= 16:
             g = lambda tiles, K, dt=t: quant.gemm_launches(tiles, K, B, dt, sms)  # noqa: E731
-            products = (g((cfg.heads * cfg.head_dim + 2 * KV) // 128, cfg.hidden) + g(cfg.hidden // 128, cfg.hidden)
-                        + g(2 * cfg.ffn // 128, cfg.hidden) + g(cfg.hidden // 128, cfg.ffn))
+            attn = g((cfg.heads * cfg.head_dim + 2 * KV) // 128, cfg.hidden) + g(cfg.hidden // 128, cfg.hidden)
+            ffn = g(2 * cfg.ffn // 128, cfg.hidden) + g(cfg.hidden // 128, cfg.ffn)
             lm_head = g(-(-cfg.vocab // 128), cfg.hidden, cfg.embed_dtype)
         else:
-            products, lm_head = 4 * B, B
-        per_layer = (3 if self.m.rope_in_attention else 4) + products
-        return 2 + cfg.layers * per_layer + lm_head + 1
+            attn, ffn, lm_head = 2 * B, 2 * B, B
+        base = 3 if self.m.rope_in_attention else 4
+        layers = sum(base + attn + (W["moe"].launches(B) if "moe" in W else ffn) for W in self.m.layers)
+        return 2 + layers + lm_head + 1
 
     def capture(self, stream):
         quant.set_launch_overlap(True)

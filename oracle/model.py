@@ -15,6 +15,10 @@ class DenseOracle:
     bytes the device model uploads."""
 
     def __init__(self, cfg, weights, threads=0, kv16=False):
+        """cfg.arch "hyv3": the q/k norm before RoPE (model.rs:425-428), the
+        MoE FFN of layers with a "moe" entry (Moe::forward at batch 1 with
+        the x86-order batch-1 products, oracle/moe.py moe_forward_port), and
+        the separate output matrix."""
         """kv16: store every cached key and value rounded to the nearest
         binary16 (the device's f16 KV cache), everything else as the
         reference."""
@@ -24,6 +28,11 @@ class DenseOracle:
         self.layers = [{k: (v.cpu().numpy() if hasattr(v, "cpu") else v) for k, v in L.items()}
                        for L in weights["layers"]]
         self.embed = weights["embed"].cpu().numpy()
+        self.output = weights["output"].cpu().numpy() if weights.get("output") is not None else self.embed
+        self.moe_cfg = cfg.moe_config() if getattr(cfg, "arch", "dense") == "hyv3" else None
+        for L in self.layers:
+            if "moe" in L:
+                L["moe"] = {k: v.cpu().numpy() for k, v in L["moe"].items()}
         self.output_norm = weights["output_norm"].cpu().numpy()
         kv = cfg.kv_heads * cfg.head_dim
         self.k_cache = [np.zeros((cfg.positions, kv), np.float32) for _ in range(cfg.layers)]
@@ -44,10 +53,14 @@ class DenseOracle:
             q = self._mm(L["q"], H, A, normalized)
             k = self._mm(L["k"], H, KV, normalized)
             v = self._mm(L["v"], H, KV, normalized)
+            if self.moe_cfg is not None:   # HyV3: before RoPE (model.rs:425-428)
+                q = O.rms_norm_rows(q, L["q_norm"], c.eps)
+                k = O.rms_norm_rows(k, L["k_norm"], c.eps)
             q = O.rope(q, c.heads, c.head_dim, cos, sin)
             k = O.rope(k, c.kv_heads, c.head_dim, cos, sin)
-            q = O.rms_norm_rows(q, L["q_norm"], c.eps)  # Dense: after RoPE (model.rs:443-446)
-            k = O.rms_norm_rows(k, L["k_norm"], c.eps)
+            if self.moe_cfg is None:       # Dense: after RoPE (model.rs:443-446)
+                q = O.rms_norm_rows(q, L["q_norm"], c.eps)
+                k = O.rms_norm_rows(k, L["k_norm"], c.eps)
             if self.kv16:
                 k = k.astype(np.float16).astype(np.float32)
                 v = v.astype(np.float16).astype(np.float32)
@@ -57,10 +70,15 @@ class DenseOracle:
                                    c.head_dim, pos)
             hidden = (hidden + self._mm(L["o"], A, H, attended)).astype(np.float32)
             normalized = O.rms_norm(hidden, L["ffn_norm"], c.eps)
-            gate = O.gate_up_silu(c.linear_dtype, L["gate"], L["up"], H, F, normalized, self.threads)
-            hidden = (hidden + self._mm(L["down"], F, H, gate)).astype(np.float32)
+            if "moe" in L:
+                from .moe import moe_forward_port
+                ff = moe_forward_port(self.moe_cfg, L["moe"], normalized[None], self.threads)[0]
+            else:
+                gate = O.gate_up_silu(c.linear_dtype, L["gate"], L["up"], H, F, normalized, self.threads)
+                ff = self._mm(L["down"], F, H, gate)
+            hidden = (hidden + ff).astype(np.float32)
         hidden = O.rms_norm(hidden, self.output_norm, c.eps)
-        return O.matmul(c.embed_dtype, self.embed, H, c.vocab, hidden, 1, self.threads)[0]
+        return O.matmul(c.embed_dtype, self.output, H, c.vocab, hidden, 1, self.threads)[0]
 
     def generate(self, prompt, n_new):
         """Greedy ids and the logits that chose each (generation.rs:281-290)."""

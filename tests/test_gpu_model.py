@@ -494,3 +494,86 @@ def test_chunked_prefill_matches_token_by_token(cuda, chunk):
         assert rel < 1e-4, (i, rel)
     assert ids == ref_ids
     assert quant.device_status() == 0
+
+
+def _hyv3_cfg(layers, positions):
+    from hy_mt_rs_b200.model import DenseConfig
+
+    # config 5's shapes: hidden 2048, 16/4 heads of 128, 64 experts top 8,
+    # expert and shared FFN 1024, Q4_K linears and experts; a small vocabulary
+    return DenseConfig(arch="hyv3", layers=layers, ffn=2048, vocab=8192, positions=positions, linear_dtype=2,
+                       embed_dtype=3, experts=64, experts_used=8, expert_ffn=1024, shared_ffn=1024)
+
+
+@pytest.mark.parametrize("batched", [False, True])
+def test_hyv3_decode_matches_oracle(cuda, batched):
+    """The HyV3 decoder (model.rs:210-231, 684-726: q/k norm before RoPE, MoE
+    FFN from layer 1, separate output matrix) on the device against the
+    oracle model: logits of every step within 1e-4, the same greedy stream;
+    the prompt token by token or in one batched forward; split-operand
+    tensor-core products for the experts and batches."""
+    import torch
+    from hy_mt_rs_b200 import quant
+    from hy_mt_rs_b200.model import DenseModel, random_weights
+    from oracle.model import DenseOracle
+
+    cfg = _hyv3_cfg(layers=3, positions=64)
+    weights = random_weights(cfg, cuda, seed=33)
+    torch.cuda.synchronize()
+    model = DenseModel(cfg, weights, cuda, gemm_precision=quant.GEMM_F32)
+    assert "moe" in model.layers[1] and "moe" not in model.layers[0] and model.output is not model.embed
+    oracle = DenseOracle(cfg, weights)
+    prompt = np.random.default_rng(33).integers(0, cfg.vocab, 20).tolist()
+    n_new = 8
+    stream = torch.cuda.Stream(cuda)
+    logits = torch.zeros(n_new, cfg.vocab, device=cuda)
+    try:
+        ids = model.generate(prompt, n_new, stream, logits_out=logits, batched_prefill=batched)
+    finally:
+        quant.set_launch_overlap(False)
+    ref_ids, ref_logits = oracle.generate(prompt, n_new)
+    got = logits.cpu().numpy()
+    for i in range(n_new):
+        rel = np.linalg.norm(got[i] - ref_logits[i]) / np.linalg.norm(ref_logits[i])
+        assert rel < 1e-4, (i, rel)
+        if ids[i] != ref_ids[i]:
+            top = np.sort(ref_logits[i])[-2:]
+            assert float(top[1] - top[0]) <= 2 * float(np.abs(got[i] - ref_logits[i]).max()), i
+            break
+    assert quant.device_status() == 0
+
+
+def test_hyv3_64_requests_match_oracle(cuda):
+    """64 concurrent HyV3 requests (DenseBatch: the MoE FFN over the
+    requests' rows) against the oracle decoding requests 0, 21, 42 and 63 on
+    their own: within 1e-4, the same greedy tokens."""
+    import torch
+    from hy_mt_rs_b200 import quant
+    from hy_mt_rs_b200.model import DenseBatch, DenseModel, random_weights
+    from oracle.model import DenseOracle
+
+    cfg = _hyv3_cfg(layers=2, positions=80)   # at least the 64 requests
+    weights = random_weights(cfg, cuda, seed=34)
+    torch.cuda.synchronize()
+    model = DenseModel(cfg, weights, cuda, gemm_precision=quant.GEMM_F32)
+    rng = np.random.default_rng(34)
+    B, n_new = 64, 4
+    prompts = [rng.integers(0, cfg.vocab, int(n)).tolist() for n in rng.integers(1, 24, B)]
+    stream = torch.cuda.Stream(cuda)
+    try:
+        batch = DenseBatch(model, B)
+        logits = torch.zeros(n_new, B, cfg.vocab, device=cuda)
+        ids = batch.generate(prompts, n_new, stream, logits_out=logits)
+    finally:
+        quant.set_launch_overlap(False)
+    got = logits.cpu().numpy()
+    for b in (0, 21, 42, 63):
+        ref_ids, ref_logits = DenseOracle(cfg, weights).generate(prompts[b], n_new)
+        for i in range(n_new):
+            rel = np.linalg.norm(got[i, b] - ref_logits[i]) / np.linalg.norm(ref_logits[i])
+            assert rel < 1e-4, (b, i, rel)
+            if ids[b][i] != ref_ids[i]:
+                top = np.sort(ref_logits[i])[-2:]
+                assert float(top[1] - top[0]) <= 2 * float(np.abs(got[i, b] - ref_logits[i]).max()), (b, i)
+                break
+    assert quant.device_status() == 0
