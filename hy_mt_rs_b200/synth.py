@@ -41,6 +41,13 @@ def _f16_round(v):
     return v.to(torch.float16).to(torch.float32)
 
 
+def _div(a, c):
+    """a / c, divided (IEEE) on every device: a CUDA tensor divided by a
+    Python scalar is multiplied by the scalar's reciprocal instead, which
+    rounds differently; a 0-dim tensor on a's device divides."""
+    return a / torch.full((), c, dtype=a.dtype, device=a.device)
+
+
 def _safe_div(a, b):
     return torch.where(b != 0, a / torch.where(b != 0, b, torch.ones_like(b)), torch.zeros_like(a))
 
@@ -48,7 +55,7 @@ def _safe_div(a, b):
 def _q8_0(w):
     N, K = w.shape
     b = w.reshape(N, K // 32, 32)
-    d = _f16_round(b.abs().amax(-1) / 127.0)
+    d = _f16_round(_div(b.abs().amax(-1), 127.0))
     q = torch.round(_safe_div(b, d[..., None])).clamp(-127, 127).to(torch.int8)
     out = torch.cat([_f16_bytes(d), q.view(torch.uint8)], dim=-1)
     return out.reshape(-1)
@@ -57,8 +64,8 @@ def _q8_0(w):
 def _q2_0c(w):
     N, K = w.shape
     b = w.reshape(N, K // 512, 512)
-    d = _f16_round(b.abs().amax(-1) / 3.0)
-    c = torch.round((_safe_div(b, d[..., None]) + 3.0) / 2.0).clamp(0, 3).to(torch.int32)
+    d = _f16_round(_div(b.abs().amax(-1), 3.0))
+    c = torch.round(_div(_safe_div(b, d[..., None]) + 3.0, 2.0)).clamp(0, 3).to(torch.int32)
     c = c.reshape(N, K // 512, 128, 4)
     payload = (c[..., 0] | (c[..., 1] << 2) | (c[..., 2] << 4) | (c[..., 3] << 6)).to(torch.uint8)
     return torch.cat([_f16_bytes(d), payload], dim=-1).reshape(-1)
@@ -68,7 +75,8 @@ def _stq1_0(w):
     N, K = w.shape
     nb = K // 256
     b = w.reshape(N, nb, 4, 4, 16)  # [.., chunk, lane p, group-in-chunk j]; column 64c + 16p + j
-    d = _f16_round(b.abs().mean(dim=(-1, -2, -3)))
+    # summed in f64 so that the order of the device's reduction cannot change the f32 mean
+    d = _f16_round(b.abs().double().mean(dim=(-1, -2, -3)).float())
     lanes = b.permute(0, 1, 2, 4, 3).reshape(N, nb, 64, 4)  # group g = 16c + j, lanes p
     z = lanes.abs().argmin(dim=-1)  # the zero lane
     neg = lanes < 0
@@ -95,10 +103,10 @@ def _q4_k(w):
     sub = w.reshape(N, nb, 8, 32)
     mn = sub.amin(-1).clamp(max=0.0)
     mx = sub.amax(-1)
-    scale = (mx - mn) / 15.0
+    scale = _div(mx - mn, 15.0)
     minv = -mn
-    d = _f16_round(scale.amax(-1) / 63.0)
-    dmin = _f16_round(minv.amax(-1) / 63.0)
+    d = _f16_round(_div(scale.amax(-1), 63.0))
+    dmin = _f16_round(_div(minv.amax(-1), 63.0))
     s6 = torch.round(_safe_div(scale, d[..., None])).clamp(0, 63).to(torch.int32)
     m6 = torch.round(_safe_div(minv, dmin[..., None])).clamp(0, 63).to(torch.int32)
     eff_s = d[..., None] * s6.to(torch.float32)
@@ -118,8 +126,8 @@ def _q6_k(w):
     N, K = w.shape
     nb = K // 256
     sub = w.reshape(N, nb, 16, 16)  # sub-block s covers outputs 16s..16s+15 -> scale sc[s]
-    scale = sub.abs().amax(-1) / 31.0
-    d = _f16_round(scale.abs().amax(-1) / 127.0)
+    scale = _div(sub.abs().amax(-1), 31.0)
+    d = _f16_round(_div(scale.abs().amax(-1), 127.0))
     sc = torch.round(_safe_div(scale, d[..., None])).clamp(-128, 127).to(torch.int32)
     eff = d[..., None] * sc.to(torch.float32)
     q = (torch.round(_safe_div(sub, eff[..., None])).clamp(-32, 31) + 32).to(torch.int32)

@@ -137,3 +137,18 @@ def test_dot(cuda):
         b = np.cos(np.arange(n, dtype=np.float32) * np.float32(0.9)).astype(np.float32)
         got = float(quant.dot(to_dev(a, cuda), to_dev(b, cuda)).cpu())
         assert abs(got - O.dot_scalar(a, b)) < 1e-4, n
+
+
+@pytest.mark.parametrize("t", [2, 3, 4, 5, 6])
+def test_synthetic_encoding_same_bytes_on_every_device(cuda, t):
+    """hy_mt_rs_b200.synth packs the same bytes on the GPU as on the CPU (the
+    config-4 fixture was made on the CPU and the GPU tests rebuild its model
+    on the device; both are checked through the model's SHA-256)."""
+    import torch
+    from hy_mt_rs_b200 import synth
+
+    K = 2048
+    for seed in (1, 2):
+        cpu = synth.random_packed(t, 300, K, seed=seed)
+        gpu = synth.random_packed(t, 300, K, seed=seed, device=cuda).cpu()
+        assert torch.equal(cpu, gpu), (t, seed)
