@@ -750,7 +750,8 @@ def prefill_arm(a):
                      "achieved": round(gate_flops / (gate * 1e-3) / 1e12, 2), "peak": peak,
                      "peak_kind": "measured" if peaks else "fallback", "unit": "TFLOP/s",
                      "frac": round(gate_flops / (gate * 1e-3) / 1e12 / peak, 4),
-                     "traffic": profile_traffic(f"gemm_gate_up_m{M}"), "avg_launch_ms": round(gate, 5)},
+                     "traffic": profile_traffic(f"gemm_gate_up_m{M}" + ("_f32" if split else "")),
+                     "avg_launch_ms": round(gate, 5)},
         "per_projection_ms": {k: round(v, 5) for k, v in per_ms.items()},
         "prefill_tok_s_layer": round(job_rate(M, 1, world, ms), 1),
         "e2e": {"value": round(job_rate(flops, 1, world, e2e_s * 1e3) / 1e12, 2), "unit": "TFLOP/s",

@@ -22,14 +22,23 @@ def main():
     ap.add_argument("--path", choices=["f32", "q8", "int8"], default="f32")
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--batch", type=int, default=1, help="> 1: batched product (tensor-core GEMM)")
+    ap.add_argument("--gate-up", action="store_true",
+                    help="batched: the fused gate/up-SiLU product of two such matrices (the 7B layer's FFN call)")
+    ap.add_argument("--precision", choices=["fp16", "f32"], default="fp16",
+                    help="batched: fp16 operands or split operands (hyq_set_gemm_precision)")
     a = ap.parse_args()
     dev = torch.device("cuda", 0)
     t = quant.DType[a.dtype]
     w = quant.Weight(synth.random_packed(t, a.rows, a.cols, seed=1, device=dev), t, [a.cols, a.rows])
+    up = quant.Weight(synth.random_packed(t, a.rows, a.cols, seed=2, device=dev), t, [a.cols, a.rows]) \
+        if a.gate_up else None
     x = torch.randn(a.batch * a.cols, generator=torch.Generator().manual_seed(0)).to(dev)
     q8 = quant.Q8(a.cols, dev)
+    quant.set_gemm_precision(quant.GEMM_F32 if a.precision == "f32" else quant.GEMM_FP16)
     for _ in range(a.iters):
-        if a.batch > 1:
+        if a.batch > 1 and up is not None:
+            w.matmul_gate_up_silu_batch(up, x, a.batch)
+        elif a.batch > 1:
             w.matmul(x, a.batch)
         elif a.path == "f32":
             w.matmul(x, 1)
