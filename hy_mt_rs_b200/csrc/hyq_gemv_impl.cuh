@@ -163,6 +163,7 @@ struct WUnit {
   uint32_t c[16];
   float s[4];
   float m[2];
+  int si[4];  // the same sub-block scales as integers (Q4_K: scale / min codes, Q6_K: int8 scales)
 };
 
 // ---------------------------------------------------------------------------
@@ -378,7 +379,11 @@ __device__ __forceinline__ void decode_unit(uint32_t row, int u, WUnit& wu) {
       }
       wu.s[hh] = d * (float)s;
       wu.m[hh] = dmin * (float)m;
+      wu.si[hh] = (int)s;
+      wu.si[2 + hh] = (int)m;
     }
+    wu.s[2] = d;     // the f32 path applies d and dmin once per unit (combine)
+    wu.s[3] = dmin;
     const uint4 q0 = ld_s128(blk + 16 + 32 * g);
     const uint4 q1 = ld_s128(blk + 32 + 32 * g);
     const uint32_t q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
@@ -397,10 +402,12 @@ __device__ __forceinline__ void decode_unit(uint32_t row, int u, WUnit& wu) {
     const uint32_t s01 = ld_s16(blk + 192 + 8 * c + 2 * pp);
     const uint32_t s45 = ld_s16(blk + 196 + 8 * c + 2 * pp);
     wu.m[0] = half_to_f32(ld_s16(blk + 208));
-    wu.s[0] = (float)(int8_t)(s01 & 0xffu);
-    wu.s[1] = (float)(int8_t)(s01 >> 8);
-    wu.s[2] = (float)(int8_t)(s45 & 0xffu);
-    wu.s[3] = (float)(int8_t)(s45 >> 8);
+    wu.si[0] = (int)(int8_t)(s01 & 0xffu);
+    wu.si[1] = (int)(int8_t)(s01 >> 8);
+    wu.si[2] = (int)(int8_t)(s45 & 0xffu);
+    wu.si[3] = (int)(int8_t)(s45 >> 8);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) wu.s[k] = (float)wu.si[k];
     // code = low nibble | (2 high bits << 4): the high bits of plane pp sit
     // at bits 2pp..2pp+1 of each qh byte, those of plane pp+2 four bits up.
 #pragma unroll
@@ -493,6 +500,29 @@ __device__ __forceinline__ float combine(const WUnit& wu, const XUnit<NP>& xu, f
     if (NP == 1) return fmaf((float)((int)plane_dot64_np<FMT, NP>(wu, xu) - xu.xsum[0]), wu.s[0] * xu.sg, acc);
     const long long v = plane_dot64_np<FMT, NP>(wu, xu) - (long long)C * xu.xsum[0];
     return fmaf(__ll2float_rn(v), wu.s[0] * xu.sg, acc);
+  } else if (FMT == Q4_K && NP == 3) {
+    // f32 path: sum (d s_h q - dmin m_h) X over the unit's two 32-column
+    // sub-blocks = d sum_h s_h (sum q X)_h - dmin sum_h m_h (sum X)_h, with
+    // s_h, m_h the 6-bit scale and min codes: two exact integers, one
+    // conversion and one scale each.
+    int A[3] = {0, 0, 0};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      int a0 = 0, a1 = 0, a2 = 0;
+#pragma unroll
+      for (int j = 8 * h; j < 8 * h + 8; ++j) {
+        a0 = dp4<FMT>(wu.c[j], xu.w[0][j], a0);
+        a1 = dp4<FMT>(wu.c[j], xu.w[NP > 1 ? 1 : 0][j], a1);
+        a2 = dp4<FMT>(wu.c[j], xu.w[NP > 2 ? 2 : 0][j], a2);
+      }
+      A[0] += wu.si[h] * a0;
+      A[1] += wu.si[h] * a1;
+      A[2] += wu.si[h] * a2;
+    }
+    const long long qx = (long long)A[0] + ((long long)A[1] << 8) + ((long long)A[2] << 16);
+    const long long mx = (long long)wu.si[2] * xu.xsum[0] + (long long)wu.si[3] * xu.xsum[1];
+    const float t = __fsub_rn(__fmul_rn(wu.s[2], __ll2float_rn(qx)), __fmul_rn(wu.s[3], __ll2float_rn(mx)));
+    return fmaf(t, xu.sg, acc);
   } else if (FMT == Q4_K) {
     // sum (d1 q - m1) x = d1 sum q x - m1 sum x, per 32-column sub-block
     const float a0 = to_f<NP>(seg_dot<FMT, NP>(wu, xu, 0, 8));
@@ -500,6 +530,28 @@ __device__ __forceinline__ float combine(const WUnit& wu, const XUnit<NP>& xu, f
     float t = wu.s[0] * a0 - wu.m[0] * (float)xu.xsum[0];
     t += wu.s[1] * a1 - wu.m[1] * (float)xu.xsum[1];
     return fmaf(t, xu.sg, acc);
+  } else if (FMT == Q6_K && NP == 3) {
+    // f32 path: the four 16-weight planes' scales are int8, so the unit's
+    // sum_s sc_s sum_i (q_i - 32) X_i is one exact integer (per activation
+    // byte plane |sum| < 2^25), converted once and scaled by d * s_x.
+    int A[3] = {0, 0, 0};
+    long long xs = 0;
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      int a0 = 0, a1 = 0, a2 = 0;
+#pragma unroll
+      for (int j = 4 * s; j < 4 * s + 4; ++j) {
+        a0 = dp4<FMT>(wu.c[j], xu.w[0][j], a0);
+        a1 = dp4<FMT>(wu.c[j], xu.w[NP > 1 ? 1 : 0][j], a1);
+        a2 = dp4<FMT>(wu.c[j], xu.w[NP > 2 ? 2 : 0][j], a2);
+      }
+      A[0] += wu.si[s] * a0;
+      A[1] += wu.si[s] * a1;
+      A[2] += wu.si[s] * a2;
+      xs += (long long)wu.si[s] * xu.xsum[s];
+    }
+    const long long t = (long long)A[0] + ((long long)A[1] << 8) + ((long long)A[2] << 16) - 32ll * xs;
+    return fmaf(__ll2float_rn(t), wu.m[0] * xu.sg, acc);
   } else if (FMT == Q6_K) {
     // per 16-weight plane: (q - 32) x, scaled by (d * s_x) * sc
     const float ds = wu.m[0] * xu.sg;

@@ -86,6 +86,44 @@ def expert_major(counts):
     return perm, inv, off
 
 
+def ep_send_index(off, world, local_experts, cap):
+    """Expert parallelism, sending side, on the device: this rank's grouped
+    rows are expert-major, so the rows for rank r's experts are grouped rows
+    off[r El] .. off[(r + 1) El].  Returns (idx [world, cap], valid [world,
+    cap]): block r of the fixed-capacity send buffer holds grouped rows
+    idx[r, :count_r] (the rest is padding, idx 0)."""
+    r = torch.arange(world, device=off.device)
+    starts = off[r * local_experts].long()
+    n = off[(r + 1) * local_experts].long() - starts
+    i = torch.arange(cap, device=off.device)
+    valid = i[None, :] < n[:, None]
+    return torch.where(valid, starts[:, None] + i[None, :], torch.zeros_like(starts)[:, None]), valid
+
+
+def ep_recv_perm(counts, cap):
+    """Expert parallelism, receiving side, on the device: counts [world,
+    local experts] = rows source s sent for local expert e, each source's
+    rows in its block s * cap .. in expert order.  Returns (perm [world cap],
+    valid [world cap], off [experts + 1]): expert-major row t (expert e's
+    rows from source 0, then 1, ...) is received row perm[t] for valid t, and
+    local expert e owns expert-major rows off[e] .. off[e + 1] (the order of
+    expert_major, without a host round trip)."""
+    counts = counts.long()
+    W, El = counts.shape
+    dev = counts.device
+    src_off = torch.cumsum(counts, 1) - counts                 # first row of (s, e) in source s's block
+    seg = counts.t().reshape(-1)                               # segments in (e, s) order
+    seg_end = torch.cumsum(seg, 0)
+    seg_start = seg_end - seg
+    t = torch.arange(W * cap, device=dev)
+    k = torch.searchsorted(seg_end, t, right=True).clamp(max=W * El - 1)
+    e, src = k // W, k % W
+    perm = src * cap + src_off[src, e] + (t - seg_start[k])
+    valid = t < seg_end[-1]
+    off = torch.cat([torch.zeros(1, dtype=torch.long, device=dev), torch.cumsum(counts.sum(0), 0)])
+    return torch.where(valid, perm, torch.zeros_like(perm)), valid, off
+
+
 class MoeLayer:
     """Moe::forward for `tokens` rows of normalized activations.
 
@@ -93,7 +131,10 @@ class MoeLayer:
     ranks (one per GPU); this rank holds experts [rank * E / world, (rank +
     1) * E / world) and its own tokens.  Token rows travel to the rank of
     each chosen expert and back by NCCL all-to-all; routing, shared expert
-    and combine stay local, so the result equals the one-GPU layer."""
+    and combine stay local, so the result equals the one-GPU layer.  The
+    exchange has a fixed capacity (tokens * used rows per destination, the
+    most a rank can send) and carries the per-expert counts in-band, so no
+    count reaches the host and the layer can be captured in a CUDA graph."""
 
     def __init__(self, cfg, weights, ep=None):
         self.cfg = cfg
@@ -136,7 +177,7 @@ class MoeLayer:
                 "row_weight": torch.empty(R, **f),
                 "token_rows": torch.empty(R, dtype=torch.int32, **f),
                 "h": torch.empty(R, c.mid, **f),
-                "y": torch.empty(R, c.hidden, **f),
+                "y": torch.empty(R + 1, c.hidden, **f),   # + one row that absorbs padded returns
                 "sh": torch.empty(T, c.shared_mid, **f),
                 "shared": torch.empty(T, c.hidden, **f),
             }
@@ -177,36 +218,42 @@ class MoeLayer:
     def _experts_ep(self, x, b, st):
         """The expert products of this rank's tokens under expert
         parallelism: b["y"] gets the same rows, in the same grouped order, as
-        the one-GPU products would."""
+        the one-GPU products would.  Three NCCL all-to-alls of equal splits:
+        per-expert counts, then cap = tokens * used rows to every rank (the
+        rows for its experts, padded), then the results back."""
         import torch.distributed as dist
 
         rank, world, group = self.ep
         c, El = self.cfg, self.local_experts
-        off = b["off"].cpu()  # split sizes of the exchange live on the host
-        per_expert = (off[1:] - off[:-1]).to(torch.int32)
-        send_rows = [int(off[(r + 1) * El] - off[r * El]) for r in range(world)]
-        # rows each source sends for each of this rank's experts
-        recv_cnt = torch.empty(world * El, dtype=torch.int32, device=x.device)
-        dist.all_to_all_single(recv_cnt, per_expert.to(x.device), group=group)
-        counts = recv_cnt.cpu().view(world, El)
-        recv_rows = [int(v) for v in counts.sum(dim=1)]
-        xg = x.index_select(0, b["row_token"].long())           # this rank's rows, grouped by expert
-        recv = torch.empty(sum(recv_rows), c.hidden, device=x.device)
-        dist.all_to_all_single(recv, xg, recv_rows, send_rows, group=group)
-        perm, inv, loff = expert_major(counts.numpy())
-        Rr = int(perm.size)
-        yr = torch.empty(Rr, c.hidden, device=x.device)
-        if Rr:
-            dev = x.device
-            perm_d = torch.from_numpy(perm.astype("int32")).to(dev)
-            off_d = torch.from_numpy(loff.astype("int32")).to(dev)
-            h = torch.empty(Rr, c.mid, device=dev)
-            y = torch.empty(Rr, c.hidden, device=dev)
-            check(lib.hyq_matmul_experts_gate_up_silu(self.gate.handle, self.up.handle, _p(recv), _p(perm_d), Rr,
-                                                      _p(off_d), Rr, _p(h), st))
-            check(lib.hyq_matmul_experts(self.down.handle, _p(h), None, Rr, _p(off_d), Rr, _p(y), st))
-            yr = y.index_select(0, torch.from_numpy(inv).to(dev))  # back in received order
-        dist.all_to_all_single(b["y"][:sum(send_rows)], yr, send_rows, recv_rows, group=group)
+        T = x.shape[0]
+        cap = T * c.used
+        dev = x.device
+        off = b["off"]
+        per_expert = off[1:] - off[:-1]                        # [E] rows per expert, this rank's tokens
+        recv_cnt = torch.empty(world * El, dtype=per_expert.dtype, device=dev)
+        dist.all_to_all_single(recv_cnt, per_expert, group=group)
+        send_idx, send_valid = ep_send_index(off, world, El, cap)
+        rows = b["row_token"].long()[send_idx.reshape(-1)]
+        send = x.index_select(0, rows)                         # [world * cap, hidden]
+        recv = torch.empty(world * cap, c.hidden, device=dev)
+        dist.all_to_all_single(recv, send, group=group)
+        perm, valid, loff = ep_recv_perm(recv_cnt.view(world, El), cap)
+        perm_d, off_d = perm.to(torch.int32), loff.to(torch.int32)
+        Rr = world * cap
+        h = torch.empty(Rr, c.mid, device=dev)
+        y = torch.empty(Rr, c.hidden, device=dev)
+        # any local expert sees at most every rank's tokens once
+        check(lib.hyq_matmul_experts_gate_up_silu(self.gate.handle, self.up.handle, _p(recv), _p(perm_d), Rr,
+                                                  _p(off_d), world * T, _p(h), st))
+        check(lib.hyq_matmul_experts(self.down.handle, _p(h), None, Rr, _p(off_d), world * T, _p(y), st))
+        # back into received order (padding rows go to a spare row), then home
+        yr = torch.empty(Rr + 1, c.hidden, device=dev)
+        yr.index_copy_(0, torch.where(valid, perm, torch.full_like(perm, Rr)), y)
+        back = torch.empty(Rr, c.hidden, device=dev)
+        dist.all_to_all_single(back, yr[:Rr], group=group)
+        R = T * c.used
+        dest = torch.where(send_valid, send_idx, torch.full_like(send_idx, R)).reshape(-1)
+        b["y"].index_copy_(0, dest, back)
 
     def launches(self, tokens):
         """Kernel launches of one forward (for the bench's count)."""

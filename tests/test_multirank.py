@@ -102,3 +102,51 @@ def test_expert_major_permutation():
     assert list(perm[inv]) == list(range(7))
     empty = expert_major(np.zeros((2, 2), dtype=np.int64))
     assert empty[0].size == 0 and list(empty[2]) == [0, 0, 0]
+
+
+def test_ep_device_index_math_round_trip():
+    """Expert parallelism without host round trips (hy_mt_rs_b200.moe
+    ep_send_index / ep_recv_perm), simulated on the CPU for 3 ranks with
+    random routing: the fixed-capacity all-to-all moved as blocks, the
+    receivers' expert-major order equal to expert_major's (host version),
+    and every row's result back at its own grouped position on its sender."""
+    import numpy as np
+    import torch
+
+    from hy_mt_rs_b200.moe import ep_recv_perm, ep_send_index, expert_major
+
+    W, El, T, used = 3, 4, 5, 2
+    E, cap = W * El, T * used
+    rng = np.random.default_rng(7)
+    counts_src = [rng.multinomial(cap, [1.0 / E] * E) for _ in range(W)]
+    offs = [torch.tensor(np.concatenate([[0], np.cumsum(c)]), dtype=torch.int32) for c in counts_src]
+    # sender s's grouped row g carries the value 1000 s + g
+    sends = []
+    for s in range(W):
+        idx, valid = ep_send_index(offs[s], W, El, cap)
+        assert valid.sum().item() == cap
+        for r in range(W):
+            n = int(counts_src[s][r * El:(r + 1) * El].sum())
+            assert valid[r].tolist() == [True] * n + [False] * (cap - n)
+            assert idx[r, :n].tolist() == list(range(int(offs[s][r * El]), int(offs[s][r * El]) + n))
+        sends.append((idx, valid, (1000 * s + idx).float()))           # [W, cap] values to each rank
+    backs = [torch.zeros(W, cap) for _ in range(W)]
+    for r in range(W):
+        recv = torch.cat([sends[s][2][r] for s in range(W)])          # block s = what s sent to r
+        counts = torch.tensor(np.stack([counts_src[s][r * El:(r + 1) * El] for s in range(W)]))
+        perm, valid, off = ep_recv_perm(counts, cap)
+        hp, _, hoff = expert_major(counts.numpy())
+        base = np.concatenate([[0], np.cumsum(counts.numpy().sum(axis=1))[:-1]])
+        src = np.searchsorted(np.cumsum(counts.numpy().sum(axis=1)), hp, side="right")
+        assert perm[:len(hp)].tolist() == (src * cap + hp - base[src]).tolist()
+        assert off.tolist() == hoff.tolist() and int(valid.sum()) == len(hp)
+        y = recv[perm]                                                # "expert results" in expert-major order
+        yr = torch.zeros(W * cap + 1)
+        yr.index_copy_(0, torch.where(valid, perm, torch.full_like(perm, W * cap)), y)
+        for s in range(W):
+            backs[s][r] = yr[s * cap:(s + 1) * cap]
+    for s in range(W):
+        idx, valid, vals = sends[s]
+        out = torch.full((cap + 1,), -1.0)
+        out.index_copy_(0, torch.where(valid, idx, torch.full_like(idx, cap)).reshape(-1), backs[s].reshape(-1))
+        assert out[:cap].tolist() == [1000.0 * s + g for g in range(cap)]
