@@ -1363,6 +1363,31 @@ def batch_arm(a):
 MOE_DECODE_TOKENS, MOE_PREFILL_TOKENS = 64, 1024
 
 
+def moe_graph(layer, x, T, out, stream, world, dev):
+    """Capture layer.forward(x, T, out) as one CUDA graph on `stream`; None
+    (and eager calls) unless every rank captured it."""
+    import torch
+    import torch.distributed as dist
+
+    graph = torch.cuda.CUDAGraph()
+    try:
+        with torch.cuda.graph(graph, stream=stream):
+            layer.forward(x, T, out)
+        ok = 1.0
+    except Exception:
+        graph, ok = None, 0.0
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        flag = torch.tensor([ok], device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        ok = float(flag.item())
+    if ok < 1.0:
+        return None
+    graph.replay()
+    stream.synchronize()
+    return graph
+
+
 def moe_arm(a):
     import numpy as np
     import torch
@@ -1386,6 +1411,7 @@ def moe_arm(a):
     # the saturated N(0, 1) router) fit in L2, so L2 is flushed between timed
     # steps by writing a buffer twice its size, outside the timed events.
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    graphed = {}
     for T in (MOE_DECODE_TOKENS, MOE_PREFILL_TOKENS):
         x = torch.randn(T, H, generator=torch.Generator().manual_seed(T)).to(dev)
         out = torch.empty(T, H, device=dev)
@@ -1393,6 +1419,10 @@ def moe_arm(a):
             for _ in range(max(3, a.warmup)):
                 layer.forward(x, T, out)
             stream.synchronize()
+            # the layer as one CUDA graph (routing, counts and the expert
+            # exchange stay on the device, so it captures), replayed per step;
+            # every rank must capture, else all run the calls eagerly
+            graph = moe_graph(layer, x, T, out, stream, world, dev)
             if T == MOE_DECODE_TOKENS:
                 sampler.start()
             evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -1400,7 +1430,7 @@ def moe_arm(a):
             for b, c in evs:
                 flush.fill_(1)
                 b.record(stream)
-                layer.forward(x, T, out)
+                graph.replay() if graph is not None else layer.forward(x, T, out)
                 c.record(stream)
             stream.synchronize()
             if T == MOE_DECODE_TOKENS:
@@ -1413,11 +1443,13 @@ def moe_arm(a):
             torch.cuda.synchronize(dev)
             t0 = time.perf_counter()
             for _ in range(a.steps):
-                xd.copy_(xh, non_blocking=True)
-                layer.forward(xd, T, out)
+                (x if graph is not None else xd).copy_(xh, non_blocking=True)
+                graph.replay() if graph is not None else layer.forward(xd, T, out)
                 oh.copy_(out, non_blocking=True)
                 stream.synchronize()
             e2e_s = (time.perf_counter() - t0) / a.steps
+            graphed[T] = graph is not None
+            del graph
         hit = int((np.diff(off) > 0).sum())
         res[T] = {"ms": statistics.fmean(b.elapsed_time(c) for b, c in evs), "e2e_s": e2e_s, "experts_hit": hit,
                   "bytes": hit * expert_bytes + shared_bytes + E * H * 4,
@@ -1461,7 +1493,8 @@ def moe_arm(a):
                                "2048->1024->2048 SwiGLU Q4_K, shared expert 2048->1024->2048), batch 64",
                    "experts": E, "used": U,
                    "parallelism": f"expert parallel x{world} (NCCL all-to-all)" if world > 1 else "1 GPU",
-                   "l2": "L2 flushed between timed steps (256 MB written outside the timed events)"},
+                   "l2": "L2 flushed between timed steps (256 MB written outside the timed events)",
+                   "step": "one CUDA graph of the layer" if graphed.get(MOE_DECODE_TOKENS) else "eager calls"},
         "prefill": {"tokens": MOE_PREFILL_TOKENS, "ms_per_step": round(ms_pre, 4),
                     "tokens_per_s": round(MOE_PREFILL_TOKENS / (ms_pre * 1e-3) * world, 1),
                     "tflops": round(pre["flops"] / (ms_pre * 1e-3) / 1e12, 2),

@@ -29,10 +29,15 @@ def main():
     ap.add_argument("--prompt", type=int, default=8)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--batch", type=int, default=0)
+    ap.add_argument("--kv16", action="store_true", help="f16 KV cache")
+    ap.add_argument("--precision", choices=["fp16", "f32"], default="fp16",
+                    help="batched products: fp16 operands or split operands")
     a = ap.parse_args()
     dev = torch.device("cuda", 0)
     cfg = DenseConfig(layers=a.layers, positions=a.prompt + a.steps + 1)
-    model = DenseModel(cfg, random_weights(cfg, dev, seed=1), dev)
+    from . import quant
+    prec = quant.GEMM_F32 if a.precision == "f32" else quant.GEMM_FP16
+    model = DenseModel(cfg, random_weights(cfg, dev, seed=1), dev, kv16=a.kv16, gemm_precision=prec)
     torch.cuda.synchronize()
     stream = torch.cuda.Stream(dev)
     if a.batch:
