@@ -248,6 +248,27 @@ inline size_t attn_smem_bytes(int dim, int group, int nsplit) {
                           (size_t)group * nsplit + group);
 }
 
+// The specialised head-size kernel over an f16 cache keeps the chunk's K and
+// V rows in binary16 in shared memory (widened to f32 where they are read):
+// K rows padded to a stride of DIM + 8 halves (272 bytes at 128, so the
+// score phase's 8-byte reads of 8 rows x 2 threads hit 32 distinct banks),
+// V rows unpadded, then the f32 query heads, exponentials and combine
+// weights as in the f32 layout.  Half the footprint: more CTAs per SM.
+__host__ __device__ constexpr int attn_kstride_h(int dim) { return dim + 8; }
+inline size_t attn_smem_bytes_h(int dim, int group, int nsplit) {
+  const size_t ks = (size_t)attn_kstride(dim);
+  return sizeof(__half) * (size_t)kAttnChunk * (attn_kstride_h(dim) + dim) +
+         sizeof(float) * (group * ks + (size_t)group * kAttnChunk + (size_t)group * nsplit + group);
+}
+
+// four binary16 values (one 8-byte shared load) as f32
+__device__ __forceinline__ float4 ld_h4(const __half* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
 struct AttnArgs {
   const float* q;
   const void* k_cache;   // f32, or binary16 in the KV16 kernels
@@ -356,7 +377,8 @@ __device__ __forceinline__ void stage_rows_h(float* dst, int sstride, const __ha
 // binary16 values (widened to f32 as they are staged; the arithmetic after
 // that is the same).
 template <int DIM, int GRP, bool KV16>
-__global__ void __launch_bounds__(kAttnThreads, 3) attention_kernel(const __grid_constant__ AttnArgs a) {
+__global__ void __launch_bounds__(kAttnThreads, (KV16 && DIM > 0) ? 5 : 3)
+    attention_kernel(const __grid_constant__ AttnArgs a) {
   static_assert(DIM == 0 || (DIM % 16 == 0 && kAttnThreads % (DIM / 4) == 0), "specialised head size");
   grid_dependency_wait();
   allow_dependents_launch();
@@ -377,9 +399,14 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attention_kernel(const __grid
   if (split >= used) return;
   const int dim = DIM ? DIM : a.dim, G = GRP ? GRP : a.heads / a.kv_heads, ks = attn_kstride(dim);
   const int nsplit = (a.positions + kAttnChunk - 1) / kAttnChunk;
+  // f16 rows in shared memory (KV16, specialised head size), else f32 rows
+  constexpr bool kHalf = KV16 && DIM > 0;
+  constexpr int ksh = attn_kstride_h(DIM > 0 ? DIM : 8);
+  __half* k_h = reinterpret_cast<__half*>(attn_smem);
+  __half* v_h = k_h + kAttnChunk * ksh;
   float* k_s = attn_smem;
   float* v_s = k_s + kAttnChunk * ks;
-  float* q_s = v_s + kAttnChunk * dim;
+  float* q_s = kHalf ? reinterpret_cast<float*>(v_h + kAttnChunk * (DIM > 0 ? DIM : 8)) : v_s + kAttnChunk * dim;
   float* e_s = q_s + G * ks;
   float* cw_s = e_s + G * kAttnChunk;
   float* inv_s = cw_s + G * nsplit;
@@ -392,33 +419,34 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attention_kernel(const __grid
   const bool fresh = a.fuse && split == used - 1;
   const int n_stage = fresh ? n - 1 : n;
   bool vec;
-  // KV16, specialised head size: every 16-byte load of the chunk's K and V
-  // rows is issued up front into registers; K is widened into shared memory
-  // here, V after the scores, so the V loads overlap the score phase.
-  constexpr int kHW = DIM > 0 ? DIM / 8 : 1, kHPer = kAttnThreads / kHW, kHIt = DIM > 0 ? kAttnChunk / kHPer : 1;
-  uint4 vreg[kHIt];
-  bool v8 = false;
   if constexpr (KV16) {
     const __half* kg = static_cast<const __half*>(a.k_cache) + c0;
     const __half* vg = static_cast<const __half*>(a.v_cache) + c0;
-    v8 = (dim & 7) == 0 && (width & 7) == 0 &&
-         ((reinterpret_cast<uintptr_t>(kg) | reinterpret_cast<uintptr_t>(vg)) & 15) == 0;
-    vec = (dim & 3) == 0;  // the f32 rows in shared memory take float4 reads
-    if (DIM > 0 && v8) {
-      static_assert(DIM == 0 || (kAttnThreads % kHW == 0 && kAttnChunk % kHPer == 0), "whole rows per pass");
-      const int c = threadIdx.x % kHW, i0 = threadIdx.x / kHW;
-      uint4 kreg[kHIt];
-#pragma unroll
-      for (int it = 0; it < kHIt; ++it) {
-        const int i = i0 + it * kHPer;
-        kreg[it] = i < n_stage ? *reinterpret_cast<const uint4*>(kg + i * width + 8 * c) : make_uint4(0, 0, 0, 0);
-        vreg[it] = i < n_stage ? *reinterpret_cast<const uint4*>(vg + i * width + 8 * c) : make_uint4(0, 0, 0, 0);
+    const bool v8 = (dim & 7) == 0 && (width & 7) == 0 &&
+                    ((reinterpret_cast<uintptr_t>(kg) | reinterpret_cast<uintptr_t>(vg)) & 15) == 0;
+    vec = (dim & 3) == 0;
+    if constexpr (kHalf) {
+      // the host launches this kernel for 16-byte aligned rows only
+      if (!v8) {
+        if (threadIdx.x == 0) atomicOr(a.status, DEV_BAD_ARGS);
+        return;
       }
+      // raw binary16 rows by cp.async, K then V (the scores start on K while V lands)
+      constexpr int w = (DIM > 0 ? DIM : 8) / 8, per = kAttnThreads / w;
+      static_assert(kAttnThreads % w == 0 && kAttnChunk % per == 0, "whole rows per pass");
+      const int c = threadIdx.x % w, i0 = threadIdx.x / w;
 #pragma unroll
-      for (int it = 0; it < kHIt; ++it) {
-        const int i = i0 + it * kHPer;
-        if (i < n_stage) widen8(k_s + i * ks + 8 * c, kreg[it]);
+      for (int k = 0; k < kAttnChunk / per; ++k) {
+        const int i = i0 + k * per;
+        if (i < n_stage) cp_async16(k_h + i * ksh + 8 * c, kg + i * width + 8 * c);
       }
+      cp_async_commit();
+#pragma unroll
+      for (int k = 0; k < kAttnChunk / per; ++k) {
+        const int i = i0 + k * per;
+        if (i < n_stage) cp_async16(v_h + i * (DIM > 0 ? DIM : 8) + 8 * c, vg + i * width + 8 * c);
+      }
+      cp_async_commit();
     } else {
       stage_rows_h<DIM>(k_s, ks, kg, width, n_stage, dim, v8);
       stage_rows_h<DIM>(v_s, dim, vg, width, n_stage, dim, v8);
@@ -450,7 +478,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attention_kernel(const __grid
       q_s[g * ks + (t - g * dim)] = qg[t];
     }
   }
-  if (a.fuse) {
+  if (!KV16 && a.fuse) {
     __syncthreads();  // the raw query heads are in q_s
     const float* c = a.cos_tab + (size_t)pos * (dim / 2);
     const float* sn = a.sin_tab + (size_t)pos * (dim / 2);
@@ -474,7 +502,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attention_kernel(const __grid
       }
     }
   }
-  if constexpr (!KV16) cp_async_wait<1>();  // this thread's K copies
+  if constexpr (!KV16 || kHalf) cp_async_wait<1>();  // this thread's K copies
   __syncthreads();
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)dim));
   if (vec && (dim & 15) == 0) {
@@ -484,6 +512,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attention_kernel(const __grid
     // 0-3 of the horizontal sum) and {4-7, 12-15} (second: lanes 4-7).
     const int i = threadIdx.x >> 1, hh = threadIdx.x & 1;
     const float* kr = k_s + i * ks + 4 * hh;
+    const __half* krh = k_h + i * ksh + 4 * hh;
     for (int g0 = 0; g0 < G; g0 += 4) {
       float acc[4][8];
 #pragma unroll
@@ -492,8 +521,8 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attention_kernel(const __grid
         for (int j = 0; j < 8; ++j) acc[g][j] = 0.f;
 #pragma unroll
       for (int c = 0; c < (DIM ? DIM : dim); c += 16) {
-        const float4 k0 = *reinterpret_cast<const float4*>(kr + c);
-        const float4 k1 = *reinterpret_cast<const float4*>(kr + c + 8);
+        const float4 k0 = kHalf ? ld_h4(krh + c) : *reinterpret_cast<const float4*>(kr + c);
+        const float4 k1 = kHalf ? ld_h4(krh + c + 8) : *reinterpret_cast<const float4*>(kr + c + 8);
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
           if (g0 + g < G) {
@@ -556,17 +585,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attention_kernel(const __grid
       w[1] = l;
     }
   }
-  if constexpr (!KV16) cp_async_wait<0>();
-  if constexpr (KV16 && DIM > 0) {
-    if (v8) {
-      const int c = threadIdx.x % kHW, i0 = threadIdx.x / kHW;
-#pragma unroll
-      for (int it = 0; it < kHIt; ++it) {
-        const int i = i0 + it * kHPer;
-        if (i < n_stage) widen8(v_s + i * dim + 8 * c, vreg[it]);
-      }
-    }
-  }
+  if constexpr (!KV16 || kHalf) cp_async_wait<0>();
   __syncthreads();
   // unnormalised outputs per (head, dim): sum_i e_i v_i.  Thread (quad dq,
   // group pg) takes four consecutive dims of every head over the positions
@@ -575,7 +594,8 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attention_kernel(const __grid
   const int outs = G * dim;
   const int q4 = dim >> 2;
   const int pgs = vec ? kAttnThreads / q4 : 0;  // position groups
-  if (vec && q4 * pgs == kAttnThreads && kAttnChunk % pgs == 0 && pgs * G * dim <= kAttnChunk * ks) {
+  if (vec && q4 * pgs == kAttnThreads && kAttnChunk % pgs == 0 &&
+      pgs * G * dim <= (kHalf ? kAttnChunk * ksh / 2 : kAttnChunk * ks)) {
     const int per = kAttnChunk / pgs;
     const int pg = threadIdx.x / q4, dq = threadIdx.x - pg * q4;
     const int i0 = pg * per, i1 = min(i0 + per, n);
@@ -588,7 +608,8 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attention_kernel(const __grid
       for (int ii = 0; ii < (DIM ? kAttnChunk / (kAttnThreads / (DIM / 4)) : per); ++ii) {
         const int i = i0 + ii;
         if (i >= i1) break;
-        const float4 v = *reinterpret_cast<const float4*>(v_s + i * dim + 4 * dq);
+        const float4 v = kHalf ? ld_h4(v_h + i * (DIM > 0 ? DIM : 8) + 4 * dq)
+                               : *reinterpret_cast<const float4*>(v_s + i * dim + 4 * dq);
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
           if (g0 + g < G) {
@@ -1052,7 +1073,7 @@ static int attention_impl(const void* k_cache, const void* v_cache, const float*
   int rc = hyq::api_status_word(&a.status);
   if (rc) return rc;
   const unsigned splits = (unsigned)((positions + hyq::model::kAttnChunk - 1) / hyq::model::kAttnChunk);
-  const size_t smem = hyq::model::attn_smem_bytes(head_dim, heads / kv_heads, (int)splits);
+  size_t smem = hyq::model::attn_smem_bytes(head_dim, heads / kv_heads, (int)splits);
   // head size 128 with 4 query heads per kv head (the Dense and 7B shapes)
   // over 16-byte aligned caches: the specialised kernel
   const bool fixed = head_dim == 128 && heads == 4 * kv_heads &&
@@ -1060,6 +1081,7 @@ static int attention_impl(const void* k_cache, const void* v_cache, const float*
                      (seq_stride & (kv16 ? 7 : 3)) == 0;
   auto kern = kv16 ? (fixed ? hyq::model::attention_kernel<128, 4, true> : hyq::model::attention_kernel<0, 0, true>)
                    : (fixed ? hyq::model::attention_kernel<128, 4, false> : hyq::model::attention_kernel<0, 0, false>);
+  if (kv16 && fixed) smem = hyq::model::attn_smem_bytes_h(head_dim, heads / kv_heads, (int)splits);
   const int kid = (kv16 ? 2 : 0) + (fixed ? 1 : 0);
   static int smem_dev[4] = {-1, -1, -1, -1};  // the largest shape's shared memory, allowed once per device
   int dev = 0;
