@@ -256,6 +256,7 @@ def decode_config(a, world):
             "step_bytes": layer_bytes(5) + layer_bytes(6) + gemv_bytes(3, VOCAB, HIDDEN),
             "launch_overlap": not a.no_overlap,
             "l2": "inputs larger than L2: every step streams the 203 MB lm_head; layers rotate copies",
+            "step": "one CUDA graph per pass of the chain (one per weight copy)",
             "parallelism": f"replicas x{world} (rows are independent; no collective)"}
 
 
@@ -484,6 +485,19 @@ def gpu_arm(a):
         g_lm = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g_lm, stream=stream):
             logits = lm_head(lm, h_last, path, q8h)
+        # The whole chain of one copy as one graph (the timed step): each
+        # stage's first product then launches as a programmatic dependent of
+        # the previous stage's last one, as inside a stage.  The per-stage
+        # graphs above time the stages for the breakdown and the roofline.
+        full, logits_full = [], []
+        for c in range(copies):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                h = x_static
+                for fmt in (5, 6):
+                    h = layer_chain(layers[fmt][c], h, path, q8h, q8f)
+                logits_full.append(lm_head(lm, h, path, q8h))
+            full.append(g)
     launches_per_step = 4 * 2 + 1
 
     def step(i, evs=None):
@@ -503,6 +517,7 @@ def gpu_arm(a):
     with torch.cuda.stream(stream):
         for i in range(a.warmup):
             step(i)
+            full[i % copies].replay()
     stream.synchronize()
 
     sampler = ClockSampler("GPU-" + str(torch.cuda.get_device_properties(dev).uuid))
@@ -516,8 +531,10 @@ def gpu_arm(a):
     with torch.cuda.stream(stream):
         start.record(stream)
         for i in range(a.steps):
-            step(i, evs[i])
+            full[i % copies].replay()
         end.record(stream)
+        for i in range(a.steps):   # the stage breakdown
+            step(i, evs[i])
     stream.synchronize()
     torch.cuda.synchronize(dev)
     sampler.stop()
@@ -538,14 +555,14 @@ def gpu_arm(a):
     with torch.cuda.stream(stream):
         for i in range(3):
             x_static.copy_(x_host, non_blocking=True)
-            step(i)
-            logits_host.copy_(logits, non_blocking=True)
+            full[i % copies].replay()
+            logits_host.copy_(logits_full[i % copies], non_blocking=True)
         stream.synchronize()
         e0.record(stream)
         for i in range(e2e_steps):
             x_static.copy_(x_host, non_blocking=True)
-            step(i)
-            logits_host.copy_(logits, non_blocking=True)
+            full[i % copies].replay()
+            logits_host.copy_(logits_full[i % copies], non_blocking=True)
             stream.synchronize()  # a decode loop needs the logits on the host every token
         e1.record(stream)
     stream.synchronize()
@@ -595,9 +612,10 @@ def gpu_arm(a):
         }
         if world == 1:
             line["cpu_baseline"] = run_cpu(a.cpu_seconds, VOCAB)
-    for g in list(graphs.values()) + [g_lm]:
+    for g in list(graphs.values()) + [g_lm] + full:
         del g
     graphs.clear()
+    full.clear()
     return line if rank == 0 else None
 
 
