@@ -1213,7 +1213,8 @@ def model_arm(a):
                    "concurrency": 1, "positions": cfg.positions, "launch_overlap": True,
                    "kv_cache": "f16" if kv16 else "f32",
                    "step": "one persistent kernel per token (hyq_dense_step)" if a.model_fused
-                   else "per-kernel CUDA graph (~260 launches per token, programmatic dependent launch)",
+                   else (f"per-kernel CUDA graph ({model_launches} launches per token, programmatic dependent "
+                         "launch" + (", norms and residual adds inside the products)" if model.fuse_norms else ")")),
                    "parallelism": f"replicas x{world}"},
         "prompt_ms": round(ms_prompt, 2),
         "prompt": "256 tokens in one batched forward (tensor-core projections, causal attention)",

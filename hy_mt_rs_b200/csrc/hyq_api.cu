@@ -180,10 +180,12 @@ struct Act {
   const int8_t* xq = nullptr;
   const float* xs = nullptr;
   bool quantize = false;  // x is quantized to Q8 inside the kernel
+  const float* norm_w = nullptr;  // fused RMSNorm of x (hyq_gemv_*_norm)
+  float eps = 0.f;
 };
 
 int run_gemv(int n_mat, const hyq_weight* const* ws, float* const* ys, const hyq_weight* up, const Act& a,
-             cudaStream_t st, const char* name) {
+             cudaStream_t st, const char* name, bool residual = false) {
   unsigned* status = nullptr;
   int rc = status_ptr(&status);
   if (rc) return rc;
@@ -201,8 +203,16 @@ int run_gemv(int n_mat, const hyq_weight* const* ws, float* const* ys, const hyq
   j.xq = a.xq;
   j.xs = a.xs;
   j.quantize_q8 = a.quantize;
+  j.norm_w = a.norm_w;
+  j.eps = a.eps;
+  j.residual = residual;
   j.status = status;
   j.overlap = g_launch_overlap.load(std::memory_order_relaxed) != 0;
+  if ((a.norm_w || residual) && !hyq::gemv_fusable(j))
+    return fail(HYQ_E_UNSUPPORTED,
+                "%s: the fused norm / residual forms need a packed format, K a multiple of 256 and at most 6144, "
+                "and 16-byte aligned weights and input",
+                name);
   const cudaError_t e = hyq::launch_gemv(j, st);
   if (e == cudaErrorNotSupported)
     return fail(HYQ_E_UNSUPPORTED, "%s: in-kernel Q8 needs K to be a multiple of 256 for this buffer layout", name);
@@ -457,6 +467,59 @@ int hyq_gemv_qkv(const hyq_weight* q, const hyq_weight* k, const hyq_weight* v, 
   return qkv_run(q, k, v, a, q_out, k_out, v_out, (cudaStream_t)stream);
 }
 
+static int norm_act(Act& a, const float* hidden, const float* norm_w, float eps, const char* name) {
+  if (!hidden || !norm_w) return fail(HYQ_E_INVALID, "%s: null pointer", name);
+  if (!aligned(norm_w, 4)) return fail(HYQ_E_ALIGN, "%s: norm weights not 4-byte aligned", name);
+  a.x = hidden;
+  a.norm_w = norm_w;
+  a.eps = eps;
+  return check_act(a, name);
+}
+
+int hyq_gemv_qkv_norm(const hyq_weight* q, const hyq_weight* k, const hyq_weight* v, const float* hidden,
+                      const float* norm_w, float eps, float* q_out, float* k_out, float* v_out, void* stream) {
+  int rc = qkv_checks(q, k, v);
+  if (rc) return rc;
+  Act a;
+  if ((rc = norm_act(a, hidden, norm_w, eps, "qkv_norm"))) return rc;
+  return qkv_run(q, k, v, a, q_out, k_out, v_out, (cudaStream_t)stream);
+}
+
+int hyq_gemv_norm(const hyq_weight* w, const float* hidden, const float* norm_w, float eps, float* out,
+                  void* stream) {
+  int rc = check_matrix(w, "gemv_norm");
+  if (rc) return rc;
+  if (!out) return fail(HYQ_E_INVALID, "gemv_norm: null output");
+  Act a;
+  if ((rc = norm_act(a, hidden, norm_w, eps, "gemv_norm"))) return rc;
+  return run_gemv(1, &w, &out, nullptr, a, (cudaStream_t)stream, "gemv_norm");
+}
+
+int hyq_gemv_residual(const hyq_weight* w, const float* input, float* hidden, void* stream) {
+  int rc = check_matrix(w, "gemv_residual");
+  if (rc) return rc;
+  if (!input || !hidden) return fail(HYQ_E_INVALID, "gemv_residual: null pointer");
+  if (!aligned(hidden, 4)) return fail(HYQ_E_ALIGN, "gemv_residual: hidden not 4-byte aligned");
+  Act a;
+  a.x = input;
+  if ((rc = check_act(a, "gemv_residual"))) return rc;
+  return run_gemv(1, &w, &hidden, nullptr, a, (cudaStream_t)stream, "gemv_residual", true);
+}
+
+int hyq_gemv_fusable(const hyq_weight* w, int* out) {
+  int rc = check_matrix(w, "gemv_fusable");
+  if (rc) return rc;
+  if (!out) return fail(HYQ_E_INVALID, "gemv_fusable: null output");
+  hyq::GemvJob j;
+  j.dtype = w->dtype;
+  j.w[0] = w->data;
+  j.rows[0] = w->dims[1];
+  j.K = w->dims[0];
+  j.x = reinterpret_cast<const float*>(uintptr_t{256});  // any 16-byte aligned input
+  *out = hyq::gemv_fusable(j) ? 1 : 0;
+  return HYQ_OK;
+}
+
 static int gate_up_checks(const hyq_weight* gate, const hyq_weight* up) {
   int rc = check_matrix(gate, "gate");
   if (rc) return rc;
@@ -475,6 +538,16 @@ int hyq_matmul_gate_up_silu(const hyq_weight* gate, const hyq_weight* up, const 
   a.x = input;
   if ((rc = check_act(a, "gate_up_silu"))) return rc;
   return run_gemv(1, &gate, &out, up, a, (cudaStream_t)stream, "gate_up_silu");
+}
+
+int hyq_gemv_gate_up_silu_norm(const hyq_weight* gate, const hyq_weight* up, const float* hidden,
+                               const float* norm_w, float eps, float* out, void* stream) {
+  int rc = gate_up_checks(gate, up);
+  if (rc) return rc;
+  if (!out) return fail(HYQ_E_INVALID, "gate_up_silu_norm: null output");
+  Act a;
+  if ((rc = norm_act(a, hidden, norm_w, eps, "gate_up_silu_norm"))) return rc;
+  return run_gemv(1, &gate, &out, up, a, (cudaStream_t)stream, "gate_up_silu_norm");
 }
 
 // A grouped tensor-core product with a stream-ordered workspace.

@@ -232,6 +232,12 @@ using gemv::make_plan;
 
 int gemv_engine(const GemvJob& job) { return make_plan(job).streaming ? 0 : 1; }
 
+bool gemv_fusable(const GemvJob& job) {
+  if (!job.x || job.K > gemv::kNormMaxPerThread * gemv::kCW * 32) return false;
+  const gemv::Plan pl = make_plan(job);
+  return pl.streaming && pl.x_raw_bytes > 0;
+}
+
 cudaError_t launch_gemv(const GemvJob& j, cudaStream_t st) {
   using namespace gemv;
   Params p{};
@@ -252,7 +258,11 @@ cudaError_t launch_gemv(const GemvJob& j, cudaStream_t st) {
   p.xq = j.xq;
   p.xs = j.xs;
   p.xmode = j.x ? (j.quantize_q8 ? XQ8F : XF32) : XQ8;
+  p.norm_w = j.norm_w;
+  p.eps = j.eps;
+  p.residual = j.residual ? 1 : 0;
   p.status = j.status;
+  if ((j.norm_w || j.residual) && !gemv_fusable(j)) return cudaErrorNotSupported;
   const bool pair = j.up != nullptr;
   Plan pl = make_plan(j);
   pl.overlap = j.overlap;

@@ -46,6 +46,8 @@ constexpr int kMaxStages = 32;
 constexpr int kRedOffset = 528;            // partial sums: 2 copies x 12 warps x 4 rows x (gate, up)
 constexpr int kHeaderBytes = 2048;         // barriers [0,512), abort flag, partial sums [528,1296), x barrier
 constexpr int kXBarOffset = 1296;          // mbarrier of the activation copy
+constexpr int kNormScaleOffset = 1312;     // the RMSNorm scale of the fused-norm form
+constexpr int kNormMaxPerThread = 16;      // fused norm: K <= kNormMaxPerThread * kCW * 32
 constexpr int kXStageMax = 32768;          // f32 activations up to this many bytes arrive by one bulk copy
 constexpr int kConsumerBarrier = 15;       // named barrier of the 12 consumer warps
 
@@ -113,6 +115,13 @@ struct Params {
   const float* x;      // XF32 / XQ8F
   const int8_t* xq;    // XQ8
   const float* xs;     // XQ8
+  // Fused forms (f32 activations staged in shared memory only): with norm_w
+  // set, the staged x is replaced by RMSNorm(x) * norm_w before use
+  // (rms_norm_into, model.rs:785-830); with residual set, every output adds
+  // into y instead of replacing it (add, model.rs:1043-1071).
+  const float* norm_w;
+  float eps;
+  int residual;
   unsigned* status;
 };
 
@@ -203,6 +212,38 @@ __device__ void prepare_x(const Params& p, uint8_t* smem) {
       }
     }
     xsrc = raw;
+    if (p.norm_w) {
+      // RMSNorm of the staged row, as the separate norm kernel computes it:
+      // dot(x, x) in the x86 order (lane l of 16 accumulates columns l,
+      // l + 16, ... in sequence; K % 16 == 0), scale = 1 / sqrt(d / K + eps),
+      // x = (x * scale) * w.  The norm weights of this thread's columns load
+      // while lanes 0-15 sum.
+      float* scale_s = reinterpret_cast<float*>(smem + kNormScaleOffset);
+      const int nt = kCW * 32, K = p.K;
+      float wv[kNormMaxPerThread];
+#pragma unroll
+      for (int j = 0; j < kNormMaxPerThread; ++j) wv[j] = (ctid + j * nt < K) ? p.norm_w[ctid + j * nt] : 0.f;
+      if (ctid < 16) {
+        float acc = 0.f;
+        for (int c0 = 0; c0 < K / 16; c0 += 16) {
+          float v[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = raw[16 * (c0 + j) + ctid];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc = fmaf(v[j], v[j], acc);
+        }
+        const float d = x86_lane_sum(acc, 0xffffu);
+        if (ctid == 0) *scale_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(d, (float)K), p.eps)));
+      }
+      consumers_sync();
+      const float scale = *scale_s;
+#pragma unroll
+      for (int j = 0; j < kNormMaxPerThread; ++j) {
+        const int i = ctid + j * nt;
+        if (i < K) raw[i] = __fmul_rn(__fmul_rn(raw[i], scale), wv[j]);
+      }
+      consumers_sync();
+    }
   }
   if (p.xmode == XQ8) {
     for (int g = ctid; g < G; g += kCW * 32) sg[g] = p.xs[g];
@@ -289,6 +330,12 @@ __device__ void prepare_x(const Params& p, uint8_t* smem) {
     }
   }
   consumers_sync();
+}
+
+// One output row: stored, or added into y in the residual form.
+__device__ __forceinline__ void emit_row(const Params& p, int m, int64_t row, float out) {
+  float* y = p.mat[m].y + row;
+  *y = p.residual ? __fadd_rn(__ldcg(y), out) : out;
 }
 
 template <int FMT, int NP>
@@ -821,7 +868,7 @@ __global__ void __launch_bounds__(kThreads, DUAL ? 2 : 1) gemv_kernel(const __gr
       if (writer && r < nrows) {
         float out = g[0];
         if (PAIR) out = (g[0] / (1.0f + expf(-g[0]))) * u[0];  // quant.rs:573-574
-        p.mat[m].y[row0 + r] = out;
+        emit_row(p, m, row0 + r, out);
       }
     } else {
       // Partial sums of the ks warps of each row, double-buffered by tile
@@ -841,7 +888,7 @@ __global__ void __launch_bounds__(kThreads, DUAL ? 2 : 1) gemv_kernel(const __gr
         }
         float out = gs;
         if (PAIR) out = (gs / (1.0f + expf(-gs))) * us;
-        p.mat[m].y[row0 + r] = out;
+        emit_row(p, m, row0 + r, out);
       }
     }
     __syncwarp();

@@ -30,6 +30,11 @@ struct GemvJob {
   // With x set: quantize it to Q8 inside the kernel (gemv_q8, quant.rs:348)
   // instead of multiplying the f32 values.
   bool quantize_q8 = false;
+  // Fused forms (see gemv_fusable): normalise x in the prologue
+  // (RMSNorm with these weights and eps), add every output into y.
+  const float* norm_w = nullptr;
+  float eps = 0.f;
+  bool residual = false;
   unsigned* status = nullptr;     // device status word (bounded-wait failures)
   // Launch as a programmatic dependent of the preceding grid in the stream
   // (hyq_set_launch_overlap); weights must not be written by work in flight.
@@ -41,6 +46,9 @@ cudaError_t launch_gemv(const GemvJob& job, cudaStream_t st);
 // Which engine launch_gemv picks for a job (for tests and the bench):
 // 0 = streaming bulk-copy kernel, 1 = per-element fallback.
 int gemv_engine(const GemvJob& job);
+// Whether the fused forms (norm_w / residual) accept a job: the streaming
+// engine with f32 activations staged in shared memory, K <= 6144.
+bool gemv_fusable(const GemvJob& job);
 
 // Batched products (Weight::matmul, batch >= 2) on tcgen05 tensor cores.
 // The activations are first rounded to fp16 into `workspace`

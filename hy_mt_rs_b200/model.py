@@ -161,10 +161,15 @@ class DenseModel:
     precision they were captured with.
     kv16: keep the KV cache in f16 (hyq_rope_qk(_seqs)_kv16 append rounds each
     key and value to binary16, hyq_attention(_seqs)_kv16 reads it), half the
-    cache bytes of the reference's f32 cache; per-kernel steps only."""
+    cache bytes of the reference's f32 cache; per-kernel steps only.
+    fuse_norms: single-token steps of Dense layers run each RMSNorm in the
+    activation prologue of the product that reads it and each residual add
+    in the output step of the product that feeds it (hyq_gemv_*_norm,
+    hyq_gemv_residual): two launches fewer per layer, bit-identical.
+    Used when every product weight qualifies (hyq_gemv_fusable)."""
 
     def __init__(self, cfg, weights, device, prefill_chunk=PREFILL_CHUNK, fused=False, rope_in_attention=False,
-                 gemm_precision=quant.GEMM_FP16, kv16=False):
+                 gemm_precision=quant.GEMM_FP16, kv16=False, fuse_norms=True):
         if kv16 and (fused or rope_in_attention):
             raise ValueError("the f16 KV cache runs with the per-kernel step (fused=False, rope_in_attention=False)")
         if cfg.arch not in ("dense", "hyv3"):
@@ -217,8 +222,20 @@ class DenseModel:
         self.argmax_ws = torch.zeros(2, dtype=torch.int64, device=device)  # HYQ_ARGMAX_WORKSPACE_BYTES, zero
         self.graph = None
         self._step = None
+        self.fuse_norms = fuse_norms and self._fusable()
         if fused:
             self._make_fused_step()
+
+    def _fusable(self):
+        if any("moe" in W for W in self.layers):
+            return False
+        names = ("q", "k", "v", "o", "gate", "up", "down")
+        ok = C.c_int()
+        for w in [self.output] + [W[n] for W in self.layers for n in names]:
+            check(lib.hyq_gemv_fusable(w.handle, C.byref(ok)))
+            if not ok.value:
+                return False
+        return True
 
     def _make_fused_step(self):
         cfg, a = self.cfg, self.one
@@ -319,6 +336,9 @@ class DenseModel:
         H = cfg.hidden
         last = lambda t: C.c_void_p(t.data_ptr() + (M - 1) * t.stride(0) * t.element_size())  # noqa: E731
         check(lib.hyq_embed(self.embed.handle, _p(tokens), M, _p(a.hidden), st))
+        if M == 1 and self.fuse_norms:
+            self._enqueue_fused_norms(a, caches, pos, token_out, logits)
+            return
         check(lib.hyq_rms_norm(_p(a.hidden), _p(self.layers[0]["input_norm"]), H, M, cfg.eps, _p(a.normalized), st))
         for i, W in enumerate(self.layers):
             kc, vc = (W["k_cache"], W["v_cache"]) if caches is None else caches[i]
@@ -362,6 +382,40 @@ class DenseModel:
         check(lib.hyq_matmul(self.output.handle, last(a.normalized), 1, _p(logits), st))
         check(lib.hyq_argmax(_p(logits), cfg.vocab, _p(token_out), _p(pos), M, _p(self.argmax_ws), st))
 
+    def _attention_one(self, W, a, kc, vc, pos):
+        cfg, st = self.cfg, self._stream()
+        if self.rope_in_attention:
+            check(lib.hyq_rope_attention(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim,
+                                         _p(self.cos), _p(self.sin), cfg.positions, _p(pos), _p(W["q_norm"]),
+                                         _p(W["k_norm"]), cfg.eps, self.norm_first, _p(kc), _p(vc), _p(a.attended),
+                                         _p(self.attn_ws), st))
+            return
+        rope = lib.hyq_rope_qk_kv16 if self.kv16 else lib.hyq_rope_qk
+        attention = lib.hyq_attention_kv16 if self.kv16 else lib.hyq_attention
+        check(rope(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim, _p(self.cos), _p(self.sin),
+                   cfg.positions, _p(pos), 1, _p(W["q_norm"]), _p(W["k_norm"]), cfg.eps, self.norm_first, _p(kc),
+                   _p(vc), st))
+        check(attention(_p(a.q), _p(kc), _p(vc), cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.positions, _p(pos), 1,
+                        _p(a.attended), _p(self.attn_ws), st))
+
+    def _enqueue_fused_norms(self, a, caches, pos, token_out, logits):
+        """The single-token chain of Model::forward (model.rs:1007-1041) with
+        every RMSNorm in the prologue of the product that reads it and every
+        residual add in the output step of the product that feeds it; the
+        hidden row is the only residual-stream buffer."""
+        cfg, st = self.cfg, self._stream()
+        for i, W in enumerate(self.layers):
+            kc, vc = (W["k_cache"], W["v_cache"]) if caches is None else caches[i]
+            check(lib.hyq_gemv_qkv_norm(W["q"].handle, W["k"].handle, W["v"].handle, _p(a.hidden),
+                                        _p(W["input_norm"]), cfg.eps, _p(a.q), _p(a.k), _p(a.v), st))
+            self._attention_one(W, a, kc, vc, pos)
+            check(lib.hyq_gemv_residual(W["o"].handle, _p(a.attended), _p(a.hidden), st))
+            check(lib.hyq_gemv_gate_up_silu_norm(W["gate"].handle, W["up"].handle, _p(a.hidden),
+                                                 _p(W["ffn_norm"]), cfg.eps, _p(a.gate), st))
+            check(lib.hyq_gemv_residual(W["down"].handle, _p(a.gate), _p(a.hidden), st))
+        check(lib.hyq_gemv_norm(self.output.handle, _p(a.hidden), _p(self.output_norm), cfg.eps, _p(logits), st))
+        check(lib.hyq_argmax(_p(logits), cfg.vocab, _p(token_out), _p(pos), 1, _p(self.argmax_ws), st))
+
     def enqueue_step(self):
         """One token: reads self.token / self.pos, leaves the logits, the next
         greedy token in self.token, and pos + 1."""
@@ -387,6 +441,8 @@ class DenseModel:
     def launches(self):
         if self._step is not None:
             return 1
+        if self.fuse_norms:   # embed; QKV, (RoPE,) attention, O, gate/up, down per layer; lm_head, argmax
+            return 3 + (5 if self.rope_in_attention else 6) * len(self.layers)
         per_layer = 7 if self.rope_in_attention else 8
         # a MoE layer runs MoeLayer's launches in place of gate/up and down
         return 4 + sum(per_layer + (W["moe"].launches(1) - 2 if "moe" in W else 0) for W in self.layers)

@@ -138,6 +138,27 @@ int hyq_gemv_qkv(const hyq_weight* q, const hyq_weight* k, const hyq_weight* v, 
 int hyq_matmul_gate_up_silu(const hyq_weight* gate, const hyq_weight* up, const float* input, float* out,
                             void* stream);
 
+/* Batch-1 products fused with the decoder's residual-stream steps (the
+ * per-token chain of model.rs:1007-1041: rms_norm_into, a projection, add).
+ * Each is one launch of the batch-1 product whose activation prologue or
+ * output step does the extra work, with the same arithmetic as the separate
+ * calls (results bit-identical to hyq_rms_norm / hyq_add + the plain product):
+ *   _norm forms: the product of RMSNorm(hidden) * norm_w (rms_norm_into,
+ *     model.rs:785-830; hidden[K] is not modified);
+ *   hyq_gemv_residual: hidden[N] += W . input (add, model.rs:1043-1071).
+ * They need the streaming engine with staged f32 activations: a packed
+ * format (not F32/F16), K a multiple of 256 and at most 6144, 16-byte aligned
+ * weights and input; HYQ_E_UNSUPPORTED otherwise.  hyq_gemv_fusable reports
+ * whether a weight qualifies (*out = 1) for 16-byte aligned activations. */
+int hyq_gemv_qkv_norm(const hyq_weight* q, const hyq_weight* k, const hyq_weight* v, const float* hidden,
+                      const float* norm_w, float eps, float* q_out, float* k_out, float* v_out, void* stream);
+int hyq_gemv_gate_up_silu_norm(const hyq_weight* gate, const hyq_weight* up, const float* hidden,
+                               const float* norm_w, float eps, float* out, void* stream);
+int hyq_gemv_norm(const hyq_weight* w, const float* hidden, const float* norm_w, float eps, float* out,
+                  void* stream);
+int hyq_gemv_residual(const hyq_weight* w, const float* input, float* hidden, void* stream);
+int hyq_gemv_fusable(const hyq_weight* w, int* out);
+
 /* Batched Weight::gemv_qkv: q/k/v_out[batch, N_q|N_k|N_v] = input[batch, K] .
  * {Q,K,V}^T.  The reference runs gemv_qkv per token (quant.rs:658-721) and
  * three Weight::matmul calls for prefill (model.rs:559-565); here one

@@ -243,3 +243,90 @@ def test_fused_int8_entry_points(cuda, t):
         assert torch.equal(a, b)
     assert torch.equal(g.matmul_gate_up_silu_int8(u, xd), g.matmul_gate_up_silu_fast(u, q8))
     assert quant.device_status() == 0
+
+
+@pytest.mark.parametrize("t", PACKED)
+def test_fused_norm_and_residual_forms(cuda, t):
+    """hyq_gemv_*_norm = hyq_rms_norm then the plain batch-1 product, and
+    hyq_gemv_residual = the plain product then hyq_add, bit for bit (the
+    decoder chain of model.rs:1007-1041 with the norm and the residual add
+    inside the products); the norm itself equals the oracle's x86 order."""
+    import ctypes as C
+    import torch
+    from hy_mt_rs_b200._native import lib
+
+    def P(a):
+        return C.c_void_p(a.data_ptr())
+
+    def ok(rc):
+        assert rc == 0, lib.hyq_last_error().decode()
+
+    K, F, eps = 2048, 6144, 1e-6
+    _, q = make(t, 2048, K, 31, cuda)
+    _, k = make(t, 512, K, 32, cuda)
+    _, v = make(t, 512, K, 33, cuda)
+    _, g = make(t, F, K, 34, cuda)
+    _, u = make(t, F, K, 35, cuda)
+    _, down = make(t, K, F, 36, cuda)
+    rng = np.random.default_rng(40 + t)
+    h = (rng.standard_normal(K) * 3).astype(np.float32)
+    nw = rng.standard_normal(K).astype(np.float32)
+    hd, nwd = to_dev(h, cuda), to_dev(nw, cuda)
+    st = C.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)
+    fus = C.c_int()
+    for w in (q, k, v, g, u, down):
+        ok(lib.hyq_gemv_fusable(w.handle, C.byref(fus)))
+        assert fus.value == 1
+    normalized = torch.empty(K, device=cuda)
+    ok(lib.hyq_rms_norm(P(hd), P(nwd), K, 1, eps, P(normalized), st))
+    a = [torch.empty(n, device=cuda) for n in (2048, 512, 512)]
+    b = [torch.empty(n, device=cuda) for n in (2048, 512, 512)]
+    ok(lib.hyq_gemv_qkv(q.handle, k.handle, v.handle, P(normalized), *map(P, a), st))
+    ok(lib.hyq_gemv_qkv_norm(q.handle, k.handle, v.handle, P(hd), P(nwd), eps, *map(P, b), st))
+    y1, y2 = torch.empty(2048, device=cuda), torch.empty(2048, device=cuda)
+    ok(lib.hyq_matmul(q.handle, P(normalized), 1, P(y1), st))
+    ok(lib.hyq_gemv_norm(q.handle, P(hd), P(nwd), eps, P(y2), st))
+    s1, s2 = torch.empty(F, device=cuda), torch.empty(F, device=cuda)
+    ok(lib.hyq_matmul_gate_up_silu(g.handle, u.handle, P(normalized), P(s1), st))
+    ok(lib.hyq_gemv_gate_up_silu_norm(g.handle, u.handle, P(hd), P(nwd), eps, P(s2), st))
+    xf = to_dev(rng.standard_normal(F).astype(np.float32), cuda)
+    h1, h2, dy = hd.clone(), hd.clone(), torch.empty(K, device=cuda)
+    ok(lib.hyq_matmul(down.handle, P(xf), 1, P(dy), st))
+    ok(lib.hyq_add(P(h1), P(dy), K, st))
+    ok(lib.hyq_gemv_residual(down.handle, P(xf), P(h2), st))
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(normalized.cpu().numpy(), O.rms_norm(h, nw, eps))
+    for x, y in zip(a + [y1, s1, h1], b + [y2, s2, h2]):
+        assert torch.equal(x, y)
+    assert torch.equal(hd.cpu(), torch.from_numpy(h))   # the norm forms leave hidden as it was
+    assert not torch.equal(h2, hd)
+
+
+def test_fused_forms_refuse_unqualified_inputs(cuda):
+    """The fused norm / residual forms run only on the streaming engine with
+    staged activations: F32 weights, K off the 256 grid or above 6144, and an
+    input that is not 16-byte aligned give HYQ_E_UNSUPPORTED, and
+    hyq_gemv_fusable says so beforehand."""
+    import ctypes as C
+    import torch
+    from hy_mt_rs_b200._native import lib
+
+    st = C.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)
+    fus = C.c_int()
+    for t, N, K in ((F32, 64, 2048), (Q8_0, 64, 2080), (Q4_K, 64, 6400)):
+        _, w = make(t, N, K, 50, cuda)
+        assert lib.hyq_gemv_fusable(w.handle, C.byref(fus)) == 0 and fus.value == 0
+        x = torch.ones(K, device=cuda)
+        y = torch.zeros(N, device=cuda)
+        rc = lib.hyq_gemv_norm(w.handle, C.c_void_p(x.data_ptr()), C.c_void_p(x.data_ptr()), 1e-6,
+                               C.c_void_p(y.data_ptr()), st)
+        assert rc == -6, (t, K, rc)
+        assert lib.hyq_gemv_residual(w.handle, C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr()), st) == -6
+    _, w = make(Q2_0C, 64, 2048, 51, cuda)
+    buf = torch.ones(2048 + 4, device=cuda)
+    y = torch.zeros(64, device=cuda)
+    off = C.c_void_p(buf.data_ptr() + 4)   # 4-byte aligned, not 16
+    assert lib.hyq_gemv_norm(w.handle, off, off, 1e-6, C.c_void_p(y.data_ptr()), st) == -6
+    assert lib.hyq_gemv_residual(w.handle, off, C.c_void_p(y.data_ptr()), st) == -6
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(y).item() == 0

@@ -180,6 +180,37 @@ def test_rope_in_attention_model_stream_identical(cuda):
     assert quant.device_status() == 0
 
 
+@pytest.mark.parametrize("rope_in_attention", [False, True])
+def test_fused_norm_chain_stream_identical(cuda, rope_in_attention):
+    """Single-token steps with the norms and residual adds inside the
+    products (fuse_norms, 2 launches fewer per layer) give the same greedy
+    stream and bit-identical logits as the separate norm launches."""
+    import torch
+    from hy_mt_rs_b200 import quant
+    from hy_mt_rs_b200.model import DenseConfig, DenseModel, random_weights
+
+    cfg = DenseConfig(layers=3, positions=96)
+    weights = random_weights(cfg, cuda, seed=23)
+    torch.cuda.synchronize()
+    prompt = np.random.default_rng(23).integers(0, cfg.vocab, 40).tolist()
+    n_new = 12
+    stream = torch.cuda.Stream(cuda)
+    res = []
+    try:
+        for flag in (False, True):
+            model = DenseModel(cfg, weights, cuda, rope_in_attention=rope_in_attention, fuse_norms=flag)
+            assert model.fuse_norms == flag
+            assert model.launches() == (3 if flag else 4) + cfg.layers * (
+                (5 if rope_in_attention else 6) + (0 if flag else 2))
+            lg = torch.zeros(n_new, cfg.vocab, device=cuda)
+            ids = model.generate(prompt, n_new, stream, logits_out=lg)
+            res.append((ids, lg.cpu()))
+    finally:
+        quant.set_launch_overlap(False)
+    assert res[0][0] == res[1][0] and torch.equal(res[0][1], res[1][1])
+    assert quant.device_status() == 0
+
+
 def test_add_rms_norm_bit_exact(cuda):
     """hyq_add_rms_norm = the residual add then rms_norm_into (model.rs:
     1043-1071, 785-830), bit for bit against the oracle's x86 order."""
