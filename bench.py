@@ -71,6 +71,9 @@ def args_parse():
     ap.add_argument("--gemm-precision", choices=["fp16", "f32"], default=None,
                     help="batched tensor-core products: fp16 operands, or split operands (f32-accurate, "
                          "hyq_set_gemm_precision); default fp16 for prefill, f32 for concurrent decode")
+    ap.add_argument("--activations", choices=["f32", "q8"], default="f32",
+                    help="model, one request: the single-token products' activations -- f32 (the reference's x86 "
+                         "branch) or Q8 (its aarch64 SDOT branch, gemv_q8_fast and friends)")
     ap.add_argument("--kv16", action="store_true",
                     help="model: f16 KV cache (BASELINE config 4) instead of the reference's f32 cache")
     ap.add_argument("--no-suite", action="store_true",
@@ -411,6 +414,8 @@ def run_suite(a):
         "concurrency_64": model_arm(sub_args(a, concurrency=64, warmup=3, gemm_precision="f32", kv16=True)),
         "concurrency_1_f32_kv": model_arm(sub_args(a, concurrency=1, model_fused=False, warmup=3, kv16=False,
                                                    cpu_seconds=0)),
+        "concurrency_1_q8_activations": model_arm(sub_args(a, concurrency=1, model_fused=False, warmup=3, kv16=True,
+                                                           activations="q8", cpu_seconds=0)),
         "concurrency_64_f32_kv": model_arm(sub_args(a, concurrency=64, warmup=3, gemm_precision="f32", kv16=False,
                                                     cpu_seconds=0)),
         "concurrency_64_fp16_products": model_arm(sub_args(a, concurrency=64, warmup=3, gemm_precision="fp16",
@@ -1119,7 +1124,9 @@ def model_arm(a):
     # parity-tested setting) unless fp16 is asked for
     prec = quant.GEMM_FP16 if a.gemm_precision == "fp16" else quant.GEMM_F32
     kv16 = a.kv16 and not a.model_fused
-    model = DenseModel(cfg, weights, dev, fused=a.model_fused, gemm_precision=prec, kv16=kv16)
+    q8 = a.activations == "q8" and not a.model_fused
+    model = DenseModel(cfg, weights, dev, fused=a.model_fused, gemm_precision=prec, kv16=kv16,
+                       activations="q8" if q8 else "f32")
     stream = torch.cuda.Stream(dev)
     model.capture(stream)
     prompt = np.random.default_rng(0).integers(0, cfg.vocab, n_prompt).tolist()
@@ -1129,6 +1136,10 @@ def model_arm(a):
     with torch.cuda.stream(stream):
         for _ in range(max(3, a.warmup)):
             model.graph.replay()
+        # the prompt's kernels once untimed (a kernel's first launch loads its module)
+        model.reset()
+        for c0 in range(0, n_prompt, model.chunk):
+            model.prefill(ids[c0:c0 + model.chunk])
         model.reset()
         e0.record(stream)
         for c0 in range(0, n_prompt, model.chunk):  # the prompt: batched forwards (model.rs:549-646)
@@ -1195,7 +1206,7 @@ def model_arm(a):
     tok_s = steps / (ms_decode * 1e-3) * world
     token_bytes = N_LAYERS_MODEL * sum(N * row_bytes(5, K) for _, N, K in LAYER) + VOCAB * row_bytes(3, HIDDEN)
     peak, peak_kind = measured_peaks()
-    cpu = model_cpu(cfg, weights, prompt) if world == 1 and a.cpu_seconds > 0 else None
+    cpu = model_cpu(cfg, weights, prompt, "q8" if q8 else "f32") if world == 1 and a.cpu_seconds > 0 else None
     sm = [c["sm_mhz"] for c in clocks_all if c.get("sm_mhz")]
     line = {
         "metric": "decode tokens/s (random-init Hy-MT2-1.8B architecture, Q2_0C linears, Q6_K tied embedding, "
@@ -1205,7 +1216,8 @@ def model_arm(a):
         # the reference's published 1.8B Q2_0C decode rate, one request on an M2 Pro
         # (docs/validation.md:70-71 of hy-mt-rs)
         "vs_baseline": round(tok_s / 86.86, 2), "vs_baseline_number": "86.86 tokens/s, 1.8B Q2_0C, 1 request",
-        "dtype": "f32 activations x packed int weights; " + ("f16" if kv16 else "f32") + " KV cache; prompt products "
+        "dtype": ("Q8 activations (the reference's aarch64 SDOT branch)" if q8 else "f32 activations")
+                 + " x packed int weights; " + ("f16" if kv16 else "f32") + " KV cache; prompt products "
                  + ("fp16 tensor-core operands" if prec == quant.GEMM_FP16 else "split-operand f32-accurate"),
         "data": "synthetic (seeded random-init weights, 256 seeded random prompt ids)",
         "config": {"workload": "hy-mt-rs config 4: 32 layers, hidden 2048, 16/4 heads x 128, SwiGLU 6144, "
@@ -1236,16 +1248,18 @@ def model_arm(a):
     return line
 
 
-def model_cpu(cfg, weights, prompt):
+def model_cpu(cfg, weights, prompt, activations="f32"):
     """CPU baseline of config 4: the oracle's single-token step (the
-    reference's x86 decode path, oracle/model.py) of the same model on all
-    host threads, a bounded sample of steps; one request (the reference
-    serves concurrent requests as separate sessions on the same cores)."""
+    reference's x86 decode path, or with activations "q8" its aarch64 SDOT
+    path, oracle/model.py) of the same model on all host threads, a bounded
+    sample of steps; one request (the reference serves concurrent requests
+    as separate sessions on the same cores)."""
     import dataclasses
 
     from oracle.model import DenseOracle
 
-    oracle = DenseOracle(dataclasses.replace(cfg, positions=8), weights, threads=host_threads())
+    oracle = DenseOracle(dataclasses.replace(cfg, positions=8), weights, threads=host_threads(),
+                         activations=activations)
     t0 = time.perf_counter()
     n = 0
     while n < 8 and (n == 0 or time.perf_counter() - t0 < 20.0):
@@ -1253,8 +1267,9 @@ def model_cpu(cfg, weights, prompt):
         n += 1
     el = time.perf_counter() - t0
     return {"value": round(n / el, 3), "unit": "tokens/s", "cores": host_threads(), "kind": "port",
-            "sample": f"{n} decode steps of one request of the same model through oracle/model.py (x86 f32 order, "
-                      f"OpenMP over all host threads; {el:.1f} s)"}
+            "sample": f"{n} decode steps of one request of the same model through oracle/model.py ("
+                      + ("Q8 activations, SDOT order" if activations == "q8" else "x86 f32 order")
+                      + f", OpenMP over all host threads; {el:.1f} s)"}
 
 
 def batch_arm(a):

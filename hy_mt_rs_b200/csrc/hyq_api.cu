@@ -467,9 +467,17 @@ int hyq_gemv_qkv(const hyq_weight* q, const hyq_weight* k, const hyq_weight* v, 
   return qkv_run(q, k, v, a, q_out, k_out, v_out, (cudaStream_t)stream);
 }
 
-static int norm_act(Act& a, const float* hidden, const float* norm_w, float eps, const char* name) {
+static int act_mode(Act& a, int act, const char* name) {
+  if (act != HYQ_ACT_F32 && act != HYQ_ACT_Q8) return fail(HYQ_E_INVALID, "%s: unknown activation mode %d", name, act);
+  a.quantize = act == HYQ_ACT_Q8;
+  return HYQ_OK;
+}
+
+static int norm_act(Act& a, const float* hidden, const float* norm_w, float eps, int act, const char* name) {
   if (!hidden || !norm_w) return fail(HYQ_E_INVALID, "%s: null pointer", name);
   if (!aligned(norm_w, 4)) return fail(HYQ_E_ALIGN, "%s: norm weights not 4-byte aligned", name);
+  int rc = act_mode(a, act, name);
+  if (rc) return rc;
   a.x = hidden;
   a.norm_w = norm_w;
   a.eps = eps;
@@ -477,30 +485,32 @@ static int norm_act(Act& a, const float* hidden, const float* norm_w, float eps,
 }
 
 int hyq_gemv_qkv_norm(const hyq_weight* q, const hyq_weight* k, const hyq_weight* v, const float* hidden,
-                      const float* norm_w, float eps, float* q_out, float* k_out, float* v_out, void* stream) {
+                      const float* norm_w, float eps, int act, float* q_out, float* k_out, float* v_out,
+                      void* stream) {
   int rc = qkv_checks(q, k, v);
   if (rc) return rc;
   Act a;
-  if ((rc = norm_act(a, hidden, norm_w, eps, "qkv_norm"))) return rc;
+  if ((rc = norm_act(a, hidden, norm_w, eps, act, "qkv_norm"))) return rc;
   return qkv_run(q, k, v, a, q_out, k_out, v_out, (cudaStream_t)stream);
 }
 
-int hyq_gemv_norm(const hyq_weight* w, const float* hidden, const float* norm_w, float eps, float* out,
+int hyq_gemv_norm(const hyq_weight* w, const float* hidden, const float* norm_w, float eps, int act, float* out,
                   void* stream) {
   int rc = check_matrix(w, "gemv_norm");
   if (rc) return rc;
   if (!out) return fail(HYQ_E_INVALID, "gemv_norm: null output");
   Act a;
-  if ((rc = norm_act(a, hidden, norm_w, eps, "gemv_norm"))) return rc;
+  if ((rc = norm_act(a, hidden, norm_w, eps, act, "gemv_norm"))) return rc;
   return run_gemv(1, &w, &out, nullptr, a, (cudaStream_t)stream, "gemv_norm");
 }
 
-int hyq_gemv_residual(const hyq_weight* w, const float* input, float* hidden, void* stream) {
+int hyq_gemv_residual(const hyq_weight* w, const float* input, int act, float* hidden, void* stream) {
   int rc = check_matrix(w, "gemv_residual");
   if (rc) return rc;
   if (!input || !hidden) return fail(HYQ_E_INVALID, "gemv_residual: null pointer");
   if (!aligned(hidden, 4)) return fail(HYQ_E_ALIGN, "gemv_residual: hidden not 4-byte aligned");
   Act a;
+  if ((rc = act_mode(a, act, "gemv_residual"))) return rc;
   a.x = input;
   if ((rc = check_act(a, "gemv_residual"))) return rc;
   return run_gemv(1, &w, &hidden, nullptr, a, (cudaStream_t)stream, "gemv_residual", true);
@@ -541,12 +551,12 @@ int hyq_matmul_gate_up_silu(const hyq_weight* gate, const hyq_weight* up, const 
 }
 
 int hyq_gemv_gate_up_silu_norm(const hyq_weight* gate, const hyq_weight* up, const float* hidden,
-                               const float* norm_w, float eps, float* out, void* stream) {
+                               const float* norm_w, float eps, int act, float* out, void* stream) {
   int rc = gate_up_checks(gate, up);
   if (rc) return rc;
   if (!out) return fail(HYQ_E_INVALID, "gate_up_silu_norm: null output");
   Act a;
-  if ((rc = norm_act(a, hidden, norm_w, eps, "gate_up_silu_norm"))) return rc;
+  if ((rc = norm_act(a, hidden, norm_w, eps, act, "gate_up_silu_norm"))) return rc;
   return run_gemv(1, &gate, &out, up, a, (cudaStream_t)stream, "gate_up_silu_norm");
 }
 

@@ -664,20 +664,46 @@ __global__ void __launch_bounds__(kAttnThreads, (KV16 && DIM > 0) ? 5 : 3)
   __syncthreads();
   if (!last_s) return;
   __threadfence();
-  // partials of other CTAs are read past L1 (__ldcg)
+  // partials of other CTAs are read past L1 (__ldcg).  The loads of the
+  // first eight splits' partial outputs of this thread's first four outputs
+  // are issued before the combine weights are computed, and every lane
+  // loads the (max, sum) pairs of its splits at once: one round trip to L2
+  // for a combine of up to eight splits.
   const size_t stride = 2 + (size_t)dim;
+  float pre[4][8];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int t = min((int)threadIdx.x + k * kAttnThreads, outs - 1);
+    const int g = t / dim;
+    const float* src = a.ws + (h0 + g) * nsplit * stride + 2 + (t - g * dim);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) pre[k][j] = j < used ? __ldcg(src + (size_t)j * stride) : 0.f;
+  }
   for (int g = warp; g < G; g += kAttnThreads / 32) {
     const float* wh = a.ws + (h0 + g) * nsplit * stride;
     float* cw = cw_s + g * nsplit;
-    float m = -INFINITY;
-    for (int i = lane; i < used; i += 32) m = fmaxf(m, __ldcg(wh + i * stride));
+    float m = -INFINITY, l = 0.f;
+    if (used <= 32) {
+      // one split per lane: its (max, sum) pair in one load round
+      const float mi = lane < used ? __ldcg(wh + lane * stride) : -INFINITY;
+      const float li = lane < used ? __ldcg(wh + lane * stride + 1) : 0.f;
+      m = mi;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float l = 0.f;
-    for (int i = lane; i < used; i += 32) {
-      const float c = expf(__ldcg(wh + i * stride) - m);
-      cw[i] = c;
-      l = fmaf(__ldcg(wh + i * stride + 1), c, l);
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (lane < used) {
+        const float c = expf(mi - m);
+        cw[lane] = c;
+        l = fmaf(li, c, l);
+      }
+    } else {
+      for (int i = lane; i < used; i += 32) m = fmaxf(m, __ldcg(wh + i * stride));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      for (int i = lane; i < used; i += 32) {
+        const float c = expf(__ldcg(wh + i * stride) - m);
+        cw[i] = c;
+        l = fmaf(__ldcg(wh + i * stride + 1), c, l);
+      }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
@@ -701,10 +727,12 @@ __global__ void __launch_bounds__(kAttnThreads, (KV16 && DIM > 0) ? 5 : 3)
     }
     for (int i0 = 0; i0 < used; i0 += 8) {
       float v[4][8];
+      const bool first = t0 == (int)threadIdx.x && i0 == 0;  // the prefetched batch
 #pragma unroll
       for (int k = 0; k < 4; ++k)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[k][j] = i0 + j < used ? __ldcg(src[k] + (size_t)(i0 + j) * stride) : 0.f;
+        for (int j = 0; j < 8; ++j)
+          v[k][j] = first ? pre[k][j] : (i0 + j < used ? __ldcg(src[k] + (size_t)(i0 + j) * stride) : 0.f);
 #pragma unroll
       for (int k = 0; k < 4; ++k)
 #pragma unroll

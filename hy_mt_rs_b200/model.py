@@ -115,6 +115,10 @@ def _p(t):
 
 
 PREFILL_CHUNK = 256  # tokens per batched forward (model.rs:18, 353)
+_F32, _Q8 = 0, 1     # HYQ_ACT_F32, HYQ_ACT_Q8
+# weight types whose single-token products take Q8 activations on the
+# reference's aarch64 SDOT branch (model.rs:403-404)
+_SDOT_TYPES = (quant.DType.STQ1_0, quant.DType.Q6_K, quant.DType.Q2_0C)
 
 
 class _DenseLayerDesc(C.Structure):
@@ -165,11 +169,21 @@ class DenseModel:
     fuse_norms: single-token steps of Dense layers run each RMSNorm in the
     activation prologue of the product that reads it and each residual add
     in the output step of the product that feeds it (hyq_gemv_*_norm,
-    hyq_gemv_residual): two launches fewer per layer, bit-identical.
-    Used when every product weight qualifies (hyq_gemv_fusable)."""
+    hyq_gemv_residual): two launches fewer per layer, bit-identical.  Used
+    when every product weight qualifies (hyq_gemv_fusable).
+    activations: "f32" (the reference's x86 branch of the single-token step)
+    or "q8" (its aarch64 SDOT branch, model.rs:403-529: the products of
+    STQ1_0, Q6_K and Q2_0C weights take their input quantized to Q8 --
+    gemv_qkv_fast, gemv_q8_fast, matmul_gate_up_silu_fast -- under the
+    reference's per-product conditions; other formats stay f32).
+    Single-token steps only (the batched forward is f32 in both)."""
 
     def __init__(self, cfg, weights, device, prefill_chunk=PREFILL_CHUNK, fused=False, rope_in_attention=False,
-                 gemm_precision=quant.GEMM_FP16, kv16=False, fuse_norms=True):
+                 gemm_precision=quant.GEMM_FP16, kv16=False, fuse_norms=True, activations="f32"):
+        if activations not in ("f32", "q8"):
+            raise ValueError(f"activations must be 'f32' or 'q8', not {activations!r}")
+        if activations == "q8" and fused:
+            raise ValueError("the persistent step kernel runs f32 activations")
         if kv16 and (fused or rope_in_attention):
             raise ValueError("the f16 KV cache runs with the per-kernel step (fused=False, rope_in_attention=False)")
         if cfg.arch not in ("dense", "hyv3"):
@@ -223,8 +237,25 @@ class DenseModel:
         self.graph = None
         self._step = None
         self.fuse_norms = fuse_norms and self._fusable()
+        self.activations = activations
+        self._acts = [self._sdot_modes(W) for W in self.layers]
+        self._act_head = _Q8 if activations == "q8" and self.output.dtype in _SDOT_TYPES else _F32
         if fused:
             self._make_fused_step()
+
+    def _sdot_modes(self, W):
+        """(QKV, O, FFN) activation modes of a layer's single-token products:
+        Q8 where the reference's aarch64 branch takes the SDOT kernel
+        (model.rs:403-404, 462-466, 486-490), else f32."""
+        if self.activations != "q8":
+            return _F32, _F32, _F32
+        qkv = _Q8 if W["q"].dtype in _SDOT_TYPES else _F32
+        o = _Q8 if W["o"].dtype in _SDOT_TYPES else _F32
+        ffn = _F32
+        if "moe" not in W and W["gate"].dtype in _SDOT_TYPES and W["gate"].dtype == W["up"].dtype \
+                and W["down"].dtype in _SDOT_TYPES:
+            ffn = _Q8
+        return qkv, o, ffn
 
     def _fusable(self):
         if any("moe" in W for W in self.layers):
@@ -342,9 +373,11 @@ class DenseModel:
         check(lib.hyq_rms_norm(_p(a.hidden), _p(self.layers[0]["input_norm"]), H, M, cfg.eps, _p(a.normalized), st))
         for i, W in enumerate(self.layers):
             kc, vc = (W["k_cache"], W["v_cache"]) if caches is None else caches[i]
+            act_qkv, act_o, act_ffn = self._acts[i] if M == 1 else (_F32, _F32, _F32)
             if M == 1:
-                check(lib.hyq_gemv_qkv(W["q"].handle, W["k"].handle, W["v"].handle, _p(a.normalized), _p(a.q),
-                                       _p(a.k), _p(a.v), st))
+                qkv = lib.hyq_gemv_qkv_int8 if act_qkv == _Q8 else lib.hyq_gemv_qkv
+                check(qkv(W["q"].handle, W["k"].handle, W["v"].handle, _p(a.normalized), _p(a.q), _p(a.k), _p(a.v),
+                          st))
             else:
                 check(lib.hyq_matmul_qkv(W["q"].handle, W["k"].handle, W["v"].handle, _p(a.normalized), M, _p(a.q),
                                          _p(a.k), _p(a.v), st))
@@ -362,24 +395,32 @@ class DenseModel:
                            _p(kc), _p(vc), st))
                 check(attention(_p(a.q), _p(kc), _p(vc), cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.positions,
                                 _p(pos), M, _p(a.attended), _p(self.attn_ws), st))
-            check(lib.hyq_matmul(W["o"].handle, _p(a.attended), M, _p(a.projected), st))
+            if act_o == _Q8:
+                check(lib.hyq_gemv_int8(W["o"].handle, _p(a.attended), _p(a.projected), st))
+            else:
+                check(lib.hyq_matmul(W["o"].handle, _p(a.attended), M, _p(a.projected), st))
             # residual add fused with the norm that follows it
             check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.projected), _p(W["ffn_norm"]), H, M, cfg.eps,
                                        _p(a.normalized), st))
             if "moe" in W:      # Moe::forward (model.rs:688-726)
                 W["moe"].forward(a.normalized, M, out=a.ff)
             elif M == 1:
-                check(lib.hyq_matmul_gate_up_silu(W["gate"].handle, W["up"].handle, _p(a.normalized), _p(a.gate),
-                                                  st))
+                gate_up = lib.hyq_matmul_gate_up_silu_int8 if act_ffn == _Q8 else lib.hyq_matmul_gate_up_silu
+                check(gate_up(W["gate"].handle, W["up"].handle, _p(a.normalized), _p(a.gate), st))
             else:
                 check(lib.hyq_matmul_gate_up_silu_batch(W["gate"].handle, W["up"].handle, _p(a.normalized), M,
                                                         _p(a.gate), st))
-            if "moe" not in W:
+            if "moe" not in W and act_ffn == _Q8:
+                check(lib.hyq_gemv_int8(W["down"].handle, _p(a.gate), _p(a.ff), st))
+            elif "moe" not in W:
                 check(lib.hyq_matmul(W["down"].handle, _p(a.gate), M, _p(a.ff), st))
             nxt = self.layers[i + 1]["input_norm"] if i + 1 < len(self.layers) else self.output_norm
             check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.ff), _p(nxt), H, M, cfg.eps, _p(a.normalized), st))
         # logits of the last token only (model.rs:619-622)
-        check(lib.hyq_matmul(self.output.handle, last(a.normalized), 1, _p(logits), st))
+        if M == 1 and self._act_head == _Q8:
+            check(lib.hyq_gemv_int8(self.output.handle, last(a.normalized), _p(logits), st))
+        else:
+            check(lib.hyq_matmul(self.output.handle, last(a.normalized), 1, _p(logits), st))
         check(lib.hyq_argmax(_p(logits), cfg.vocab, _p(token_out), _p(pos), M, _p(self.argmax_ws), st))
 
     def _attention_one(self, W, a, kc, vc, pos):
@@ -406,14 +447,16 @@ class DenseModel:
         cfg, st = self.cfg, self._stream()
         for i, W in enumerate(self.layers):
             kc, vc = (W["k_cache"], W["v_cache"]) if caches is None else caches[i]
+            act_qkv, act_o, act_ffn = self._acts[i]
             check(lib.hyq_gemv_qkv_norm(W["q"].handle, W["k"].handle, W["v"].handle, _p(a.hidden),
-                                        _p(W["input_norm"]), cfg.eps, _p(a.q), _p(a.k), _p(a.v), st))
+                                        _p(W["input_norm"]), cfg.eps, act_qkv, _p(a.q), _p(a.k), _p(a.v), st))
             self._attention_one(W, a, kc, vc, pos)
-            check(lib.hyq_gemv_residual(W["o"].handle, _p(a.attended), _p(a.hidden), st))
+            check(lib.hyq_gemv_residual(W["o"].handle, _p(a.attended), act_o, _p(a.hidden), st))
             check(lib.hyq_gemv_gate_up_silu_norm(W["gate"].handle, W["up"].handle, _p(a.hidden),
-                                                 _p(W["ffn_norm"]), cfg.eps, _p(a.gate), st))
-            check(lib.hyq_gemv_residual(W["down"].handle, _p(a.gate), _p(a.hidden), st))
-        check(lib.hyq_gemv_norm(self.output.handle, _p(a.hidden), _p(self.output_norm), cfg.eps, _p(logits), st))
+                                                 _p(W["ffn_norm"]), cfg.eps, act_ffn, _p(a.gate), st))
+            check(lib.hyq_gemv_residual(W["down"].handle, _p(a.gate), act_ffn, _p(a.hidden), st))
+        check(lib.hyq_gemv_norm(self.output.handle, _p(a.hidden), _p(self.output_norm), cfg.eps, self._act_head,
+                                _p(logits), st))
         check(lib.hyq_argmax(_p(logits), cfg.vocab, _p(token_out), _p(pos), 1, _p(self.argmax_ws), st))
 
     def enqueue_step(self):

@@ -146,17 +146,27 @@ int hyq_matmul_gate_up_silu(const hyq_weight* gate, const hyq_weight* up, const 
  *   _norm forms: the product of RMSNorm(hidden) * norm_w (rms_norm_into,
  *     model.rs:785-830; hidden[K] is not modified);
  *   hyq_gemv_residual: hidden[N] += W . input (add, model.rs:1043-1071).
+ * `act` picks the product's activations, as the reference's two decode
+ * branches do (model.rs:395-529):
+ *   HYQ_ACT_F32: f32 activations (x86: gemv_qkv, matmul, matmul_gate_up_silu);
+ *   HYQ_ACT_Q8: the (normalised) input quantized to Q8 inside the kernel
+ *     exactly as Q8::quantize_into, then the SDOT-order product (aarch64:
+ *     gemv_qkv_fast, gemv_q8_fast, matmul_gate_up_silu_fast; the same
+ *     results as hyq_q8_quantize followed by the _q8 entry points).
  * They need the streaming engine with staged f32 activations: a packed
  * format (not F32/F16), K a multiple of 256 and at most 6144, 16-byte aligned
  * weights and input; HYQ_E_UNSUPPORTED otherwise.  hyq_gemv_fusable reports
  * whether a weight qualifies (*out = 1) for 16-byte aligned activations. */
+#define HYQ_ACT_F32 0
+#define HYQ_ACT_Q8 1
 int hyq_gemv_qkv_norm(const hyq_weight* q, const hyq_weight* k, const hyq_weight* v, const float* hidden,
-                      const float* norm_w, float eps, float* q_out, float* k_out, float* v_out, void* stream);
+                      const float* norm_w, float eps, int act, float* q_out, float* k_out, float* v_out,
+                      void* stream);
 int hyq_gemv_gate_up_silu_norm(const hyq_weight* gate, const hyq_weight* up, const float* hidden,
-                               const float* norm_w, float eps, float* out, void* stream);
-int hyq_gemv_norm(const hyq_weight* w, const float* hidden, const float* norm_w, float eps, float* out,
+                               const float* norm_w, float eps, int act, float* out, void* stream);
+int hyq_gemv_norm(const hyq_weight* w, const float* hidden, const float* norm_w, float eps, int act, float* out,
                   void* stream);
-int hyq_gemv_residual(const hyq_weight* w, const float* input, float* hidden, void* stream);
+int hyq_gemv_residual(const hyq_weight* w, const float* input, int act, float* hidden, void* stream);
 int hyq_gemv_fusable(const hyq_weight* w, int* out);
 
 /* Batched Weight::gemv_qkv: q/k/v_out[batch, N_q|N_k|N_v] = input[batch, K] .

@@ -245,12 +245,14 @@ def test_fused_int8_entry_points(cuda, t):
     assert quant.device_status() == 0
 
 
+@pytest.mark.parametrize("act", [0, 1])
 @pytest.mark.parametrize("t", PACKED)
-def test_fused_norm_and_residual_forms(cuda, t):
+def test_fused_norm_and_residual_forms(cuda, t, act):
     """hyq_gemv_*_norm = hyq_rms_norm then the plain batch-1 product, and
     hyq_gemv_residual = the plain product then hyq_add, bit for bit (the
     decoder chain of model.rs:1007-1041 with the norm and the residual add
-    inside the products); the norm itself equals the oracle's x86 order."""
+    inside the products); the norm itself equals the oracle's x86 order.
+    act 1 (HYQ_ACT_Q8): the products are the in-kernel-Q8 forms (_int8)."""
     import ctypes as C
     import torch
     from hy_mt_rs_b200._native import lib
@@ -281,19 +283,25 @@ def test_fused_norm_and_residual_forms(cuda, t):
     ok(lib.hyq_rms_norm(P(hd), P(nwd), K, 1, eps, P(normalized), st))
     a = [torch.empty(n, device=cuda) for n in (2048, 512, 512)]
     b = [torch.empty(n, device=cuda) for n in (2048, 512, 512)]
-    ok(lib.hyq_gemv_qkv(q.handle, k.handle, v.handle, P(normalized), *map(P, a), st))
-    ok(lib.hyq_gemv_qkv_norm(q.handle, k.handle, v.handle, P(hd), P(nwd), eps, *map(P, b), st))
+    qkv = lib.hyq_gemv_qkv_int8 if act else lib.hyq_gemv_qkv
+    ok(qkv(q.handle, k.handle, v.handle, P(normalized), *map(P, a), st))
+    ok(lib.hyq_gemv_qkv_norm(q.handle, k.handle, v.handle, P(hd), P(nwd), eps, act, *map(P, b), st))
+
+    def gemv(w, x, y):
+        return lib.hyq_gemv_int8(w.handle, P(x), P(y), st) if act else lib.hyq_matmul(w.handle, P(x), 1, P(y), st)
+
     y1, y2 = torch.empty(2048, device=cuda), torch.empty(2048, device=cuda)
-    ok(lib.hyq_matmul(q.handle, P(normalized), 1, P(y1), st))
-    ok(lib.hyq_gemv_norm(q.handle, P(hd), P(nwd), eps, P(y2), st))
+    ok(gemv(q, normalized, y1))
+    ok(lib.hyq_gemv_norm(q.handle, P(hd), P(nwd), eps, act, P(y2), st))
     s1, s2 = torch.empty(F, device=cuda), torch.empty(F, device=cuda)
-    ok(lib.hyq_matmul_gate_up_silu(g.handle, u.handle, P(normalized), P(s1), st))
-    ok(lib.hyq_gemv_gate_up_silu_norm(g.handle, u.handle, P(hd), P(nwd), eps, P(s2), st))
+    gate_up = lib.hyq_matmul_gate_up_silu_int8 if act else lib.hyq_matmul_gate_up_silu
+    ok(gate_up(g.handle, u.handle, P(normalized), P(s1), st))
+    ok(lib.hyq_gemv_gate_up_silu_norm(g.handle, u.handle, P(hd), P(nwd), eps, act, P(s2), st))
     xf = to_dev(rng.standard_normal(F).astype(np.float32), cuda)
     h1, h2, dy = hd.clone(), hd.clone(), torch.empty(K, device=cuda)
-    ok(lib.hyq_matmul(down.handle, P(xf), 1, P(dy), st))
+    ok(gemv(down, xf, dy))
     ok(lib.hyq_add(P(h1), P(dy), K, st))
-    ok(lib.hyq_gemv_residual(down.handle, P(xf), P(h2), st))
+    ok(lib.hyq_gemv_residual(down.handle, P(xf), act, P(h2), st))
     torch.cuda.synchronize()
     np.testing.assert_array_equal(normalized.cpu().numpy(), O.rms_norm(h, nw, eps))
     for x, y in zip(a + [y1, s1, h1], b + [y2, s2, h2]):
@@ -318,15 +326,17 @@ def test_fused_forms_refuse_unqualified_inputs(cuda):
         assert lib.hyq_gemv_fusable(w.handle, C.byref(fus)) == 0 and fus.value == 0
         x = torch.ones(K, device=cuda)
         y = torch.zeros(N, device=cuda)
-        rc = lib.hyq_gemv_norm(w.handle, C.c_void_p(x.data_ptr()), C.c_void_p(x.data_ptr()), 1e-6,
+        rc = lib.hyq_gemv_norm(w.handle, C.c_void_p(x.data_ptr()), C.c_void_p(x.data_ptr()), 1e-6, 0,
                                C.c_void_p(y.data_ptr()), st)
         assert rc == -6, (t, K, rc)
-        assert lib.hyq_gemv_residual(w.handle, C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr()), st) == -6
+        assert lib.hyq_gemv_residual(w.handle, C.c_void_p(x.data_ptr()), 0, C.c_void_p(y.data_ptr()), st) == -6
     _, w = make(Q2_0C, 64, 2048, 51, cuda)
     buf = torch.ones(2048 + 4, device=cuda)
     y = torch.zeros(64, device=cuda)
     off = C.c_void_p(buf.data_ptr() + 4)   # 4-byte aligned, not 16
-    assert lib.hyq_gemv_norm(w.handle, off, off, 1e-6, C.c_void_p(y.data_ptr()), st) == -6
-    assert lib.hyq_gemv_residual(w.handle, off, C.c_void_p(y.data_ptr()), st) == -6
+    assert lib.hyq_gemv_norm(w.handle, off, off, 1e-6, 0, C.c_void_p(y.data_ptr()), st) == -6
+    assert lib.hyq_gemv_residual(w.handle, off, 0, C.c_void_p(y.data_ptr()), st) == -6
+    aligned = C.c_void_p(buf.data_ptr())
+    assert lib.hyq_gemv_residual(w.handle, aligned, 2, C.c_void_p(y.data_ptr()), st) == -1   # unknown mode
     torch.cuda.synchronize()
     assert torch.count_nonzero(y).item() == 0

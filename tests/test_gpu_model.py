@@ -211,6 +211,55 @@ def test_fused_norm_chain_stream_identical(cuda, rope_in_attention):
     assert quant.device_status() == 0
 
 
+def test_sdot_branch_decode_matches_oracle(cuda):
+    """activations="q8": the reference's aarch64 SDOT branch of the
+    single-token step (model.rs:403-529) against the oracle's restatement
+    of it.  At position 0 (attention over one position is exact) the 4-layer
+    step's logits are within 1e-5 of the oracle's.  Over a stream the branch
+    is not compared at a tight bound: one activation that rounds to the
+    neighbouring int8 value (inputs that differ in the last f32 bit, e.g.
+    from the device exponential) moves this random-init model's logits by
+    1-2 % after 4 layers, in the oracle itself -- the reference holds its own
+    Q8 path to 0.03 of its f32 path (tests/models.rs:52-54).  The stream
+    checks that the branch is taken and that the fused-norm chain is
+    bit-identical to the separate launches."""
+    import torch
+    from hy_mt_rs_b200 import quant
+    from hy_mt_rs_b200.model import DenseConfig, DenseModel, random_weights
+    from oracle.model import DenseOracle
+
+    cfg = DenseConfig(layers=4, positions=64)
+    weights = random_weights(cfg, cuda, seed=5)
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(cuda)
+    prompt = [9, 17, 120831, 3000, 64, 2]
+    n_new = 12
+    res = []
+    try:
+        model = DenseModel(cfg, weights, cuda, activations="q8", kv16=True)
+        first = torch.zeros(1, cfg.vocab, device=cuda)
+        model.generate(prompt[:1], 1, stream, logits_out=first)
+        for fuse in (True, False):
+            model = DenseModel(cfg, weights, cuda, activations="q8", kv16=True, fuse_norms=fuse)
+            lg = torch.zeros(n_new, cfg.vocab, device=cuda)
+            res.append((model.generate(prompt, n_new, stream, logits_out=lg), lg.cpu()))
+        f32 = DenseModel(cfg, weights, cuda, kv16=True)
+        lg32 = torch.zeros(1, cfg.vocab, device=cuda)
+        f32.generate(prompt[:1], 1, stream, logits_out=lg32)
+    finally:
+        quant.set_launch_overlap(False)
+    assert res[0][0] == res[1][0] and torch.equal(res[0][1], res[1][1])
+    oracle = DenseOracle(cfg, weights, kv16=True, activations="q8")
+    ref = oracle.step(prompt[0], 0)
+    got = first[0].cpu().numpy()
+    assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 1e-5
+    # the branch is taken: Q8 activations move the logits off the f32 branch's
+    g32 = lg32[0].cpu().numpy()
+    assert np.linalg.norm(got - g32) / np.linalg.norm(g32) > 1e-3
+    assert np.isfinite(res[0][1].numpy()).all()
+    assert quant.device_status() == 0
+
+
 def test_add_rms_norm_bit_exact(cuda):
     """hyq_add_rms_norm = the residual add then rms_norm_into (model.rs:
     1043-1071, 785-830), bit for bit against the oracle's x86 order."""
