@@ -65,6 +65,9 @@ _SIGS = {
     "hyq_gemv_norm": ([_wp, _vp, _vp, C.c_float, C.c_int, _vp, _vp], C.c_int),
     "hyq_gemv_residual": ([_wp, _vp, C.c_int, _vp, _vp], C.c_int),
     "hyq_gemv_fusable": ([_wp, C.POINTER(C.c_int)], C.c_int),
+    "hyq_matmul_qkv_norm": ([_wp, _wp, _wp, _vp, _vp, _vp, C.c_float, _i64, _vp, _vp, _vp, _vp], C.c_int),
+    "hyq_matmul_gate_up_silu_norm": ([_wp, _wp, _vp, _vp, _vp, C.c_float, _i64, _vp, _vp], C.c_int),
+    "hyq_matmul_norm": ([_wp, _vp, _vp, _vp, C.c_float, _i64, _vp, _vp], C.c_int),
     "hyq_matmul_qkv": ([_wp, _wp, _wp, _vp, _i64, _vp, _vp, _vp, _vp], C.c_int),
     "hyq_matmul_gate_up_silu_batch": ([_wp, _wp, _vp, _i64, _vp, _vp], C.c_int),
     "hyq_q8_quantize": ([_vp, _i64, _vp, _vp, _vp, _vp], C.c_int),

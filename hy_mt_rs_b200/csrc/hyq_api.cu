@@ -7,6 +7,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <functional>
 #include <mutex>
 #include <string>
 
@@ -693,6 +694,130 @@ int hyq_matmul_gate_up_silu_batch(const hyq_weight* gate, const hyq_weight* up, 
     if ((rc = run_gemv(1, &gate, &y, up, ab, st, "gate_up_silu_batch"))) return rc;
   }
   return HYQ_OK;
+}
+
+// The residual-stream input of the fused batched forms: hidden [batch, K]
+// (+= delta when given), normalised with norm_w.
+struct NormIn {
+  float* hidden;
+  const float* delta;
+  const float* w;
+  float eps;
+};
+
+static int norm_in_checks(const NormIn& n, int64_t batch, const char* name) {
+  if (batch <= 0) return fail(HYQ_E_SHAPE, "%s: invalid activation shape", name);
+  if (!n.hidden || !n.w) return fail(HYQ_E_INVALID, "%s: null pointer", name);
+  if (!aligned(n.hidden, 4) || !aligned(n.w, 4) || (n.delta && !aligned(n.delta, 4)))
+    return fail(HYQ_E_ALIGN, "%s: f32 buffers must be 4-byte aligned", name);
+  return HYQ_OK;
+}
+
+static void set_norm(hyq::GemmJob& j, const NormIn& n) {
+  j.x = n.hidden;
+  j.norm_x = n.hidden;
+  j.norm_delta = n.delta;
+  j.norm_w = n.w;
+  j.norm_eps = n.eps;
+}
+
+// The separate add + norm (or norm) kernel into a pool buffer, then `run` on
+// it: the fused batched forms below 16 rows and for shapes the tensor-core
+// conversion does not take.
+static int norm_then(const NormIn& n, int64_t batch, int64_t K, cudaStream_t st, const char* name,
+                     const std::function<int(const float*)>& run) {
+  void* buf = nullptr;
+  const cudaError_t e = ws_alloc(&buf, (size_t)batch * K * sizeof(float) + 16, st);
+  if (e != cudaSuccess) return fail(HYQ_E_NOMEM, "%s workspace: %s", name, cudaGetErrorString(e));
+  float* x = static_cast<float*>(buf);
+  int rc = n.delta ? hyq_add_rms_norm(n.hidden, n.delta, n.w, K, batch, n.eps, x, st)
+                   : hyq_rms_norm(n.hidden, n.w, K, batch, n.eps, x, st);
+  if (!rc) rc = run(static_cast<const float*>(x));
+  const cudaError_t e2 = cudaFreeAsync(buf, st);
+  if (rc) return rc;
+  if (e2 != cudaSuccess) return cuda_fail(e2, name);
+  return HYQ_OK;
+}
+
+int hyq_matmul_qkv_norm(const hyq_weight* q, const hyq_weight* k, const hyq_weight* v, float* hidden,
+                        const float* delta, const float* norm_w, float eps, int64_t batch, float* q_out,
+                        float* k_out, float* v_out, void* stream) {
+  int rc = qkv_checks(q, k, v);
+  if (rc) return rc;
+  const NormIn n{hidden, delta, norm_w, eps};
+  if ((rc = norm_in_checks(n, batch, "matmul_qkv_norm"))) return rc;
+  if (!q_out || !k_out || !v_out) return fail(HYQ_E_INVALID, "matmul_qkv_norm: null output");
+  const int64_t K = q->dims[0];
+  cudaStream_t st = (cudaStream_t)stream;
+  hyq::GemmJob j;
+  j.dtype = q->dtype;
+  j.n_mat = 3;
+  const hyq_weight* ws[3] = {q, k, v};
+  float* ys[3] = {q_out, k_out, v_out};
+  for (int m = 0; m < 3; ++m) {
+    j.w[m] = ws[m]->data;
+    j.rows[m] = ws[m]->dims[1];
+    j.y[m] = ys[m];
+  }
+  j.K = K;
+  j.M = batch;
+  set_norm(j, n);
+  if (batch >= kGemmMinBatch && k->dtype == q->dtype && v->dtype == q->dtype && hyq::gemm_job_supported(j))
+    return run_gemm_job(j, st, "matmul_qkv_norm (tensor-core GEMM)");
+  return norm_then(n, batch, K, st, "matmul_qkv_norm", [&](const float* x) {
+    return hyq_matmul_qkv(q, k, v, x, batch, q_out, k_out, v_out, stream);
+  });
+}
+
+int hyq_matmul_gate_up_silu_norm(const hyq_weight* gate, const hyq_weight* up, float* hidden, const float* delta,
+                                 const float* norm_w, float eps, int64_t batch, float* out, void* stream) {
+  int rc = gate_up_checks(gate, up);
+  if (rc) return rc;
+  const NormIn n{hidden, delta, norm_w, eps};
+  if ((rc = norm_in_checks(n, batch, "gate_up_silu_norm"))) return rc;
+  if (!out) return fail(HYQ_E_INVALID, "gate_up_silu_norm: null output");
+  const int64_t K = gate->dims[0], N = gate->dims[1];
+  cudaStream_t st = (cudaStream_t)stream;
+  hyq::GemmJob j;
+  j.dtype = gate->dtype;
+  j.n_mat = 2;
+  j.gate_up = true;
+  j.w[0] = gate->data;
+  j.w[1] = up->data;
+  j.rows[0] = j.rows[1] = N;
+  j.y[0] = out;
+  j.K = K;
+  j.M = batch;
+  set_norm(j, n);
+  if (batch >= kGemmMinBatch && hyq::gemm_job_supported(j))
+    return run_gemm_job(j, st, "gate_up_silu_norm (tensor-core GEMM)");
+  return norm_then(n, batch, K, st, "gate_up_silu_norm", [&](const float* x) {
+    return hyq_matmul_gate_up_silu_batch(gate, up, x, batch, out, stream);
+  });
+}
+
+int hyq_matmul_norm(const hyq_weight* w, float* hidden, const float* delta, const float* norm_w, float eps,
+                    int64_t batch, float* out, void* stream) {
+  int rc = check_matrix(w, "matmul_norm");
+  if (rc) return rc;
+  const NormIn n{hidden, delta, norm_w, eps};
+  if ((rc = norm_in_checks(n, batch, "matmul_norm"))) return rc;
+  if (!out) return fail(HYQ_E_INVALID, "matmul_norm: null output");
+  const int64_t K = w->dims[0];
+  cudaStream_t st = (cudaStream_t)stream;
+  hyq::GemmJob j;
+  j.dtype = w->dtype;
+  j.n_mat = 1;
+  j.w[0] = w->data;
+  j.rows[0] = w->dims[1];
+  j.y[0] = out;
+  j.K = K;
+  j.M = batch;
+  set_norm(j, n);
+  if (batch >= kGemmMinBatch && hyq::gemm_job_supported(j))
+    return run_gemm_job(j, st, "matmul_norm (tensor-core GEMM)");
+  return norm_then(n, batch, K, st, "matmul_norm",
+                   [&](const float* x) { return hyq_matmul(w, x, batch, out, stream); });
 }
 
 int hyq_q8_quantize(const float* input, int64_t len, int8_t* values, float* scales, int8_t* values_q2c,

@@ -1280,6 +1280,78 @@ __global__ void __launch_bounds__(256) to_half_split_kernel(const float* __restr
       __floats2half2_rn(__fmul_rn(__fsub_rn(a, ah), kSplitScale), __fmul_rn(__fsub_rn(b, bh), kSplitScale));
 }
 
+// Conversion with the decoder's residual-stream steps in front (the batched
+// forward, model.rs:569-616): one CTA per activation row stages the row
+// (hidden, plus delta when given: add, model.rs:1043-1071, written back to
+// hidden) and the norm weights in shared memory, computes the RMSNorm scale
+// with the x86-order sum of squares (rms_norm_into, model.rs:785-830; the
+// arithmetic of the separate add + norm kernel) and converts (x * scale) * w
+// as to_half(_split)_kernel converts x.  Shared memory: 2 K floats.
+constexpr int kNormConvertMaxK = 16384;
+
+template <int FMT, bool SPLIT>
+__global__ void __launch_bounds__(256) to_half_norm_kernel(float* __restrict__ hidden, const float* __restrict__ delta,
+                                                            const float* __restrict__ w, float eps,
+                                                            __half2* __restrict__ h, int64_t K, int64_t total_pairs) {
+  grid_dependency_wait();
+  allow_dependents_launch();
+  extern __shared__ float norm_smem[];  // [K] row, [K] weights
+  __shared__ float scale_s;
+  float* xs = norm_smem;
+  float* ws = norm_smem + K;
+  const int64_t tok = blockIdx.x;
+  float* row = hidden + tok * K;
+  const float* drow = delta ? delta + tok * K : nullptr;
+#pragma unroll 8
+  for (int64_t i = threadIdx.x; i < K; i += blockDim.x) {
+    const float v = row[i];
+    xs[i] = drow ? __fadd_rn(v, drow[i]) : v;
+    ws[i] = w[i];
+  }
+  __syncthreads();
+  if (drow)
+    for (int64_t i = threadIdx.x; i < K; i += blockDim.x) row[i] = xs[i];
+  if (threadIdx.x < 16) {
+    const float d = dot_x86(xs, xs, (int)K, 0xffffu);
+    if (threadIdx.x == 0) scale_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(d, (float)K), eps)));
+  }
+  __syncthreads();
+  const float scale = scale_s;
+  const int64_t half_k = K / 2;
+  for (int64_t p = threadIdx.x; p < half_k; p += blockDim.x) {
+    const int64_t e = 2 * p;
+    const int64_t step0 = e & ~int64_t(63);
+    const int slot = (int)(e & 63);
+    const int64_t ia = step0 + k_perm(FMT, slot), ib = step0 + k_perm(FMT, slot + 1);
+    const float a = __fmul_rn(__fmul_rn(xs[ia], scale), ws[ia]);
+    const float b = __fmul_rn(__fmul_rn(xs[ib], scale), ws[ib]);
+    const __half2 hi = __floats2half2_rn(a, b);
+    const int64_t i = tok * half_k + p;
+    h[i] = hi;
+    if (SPLIT) {
+      const float ah = __low2float(hi), bh = __high2float(hi);
+      h[total_pairs + i] =
+          __floats2half2_rn(__fmul_rn(__fsub_rn(a, ah), kSplitScale), __fmul_rn(__fsub_rn(b, bh), kSplitScale));
+    }
+  }
+}
+
+template <int FMT, bool SPLIT>
+cudaError_t launch_norm_convert(const GemmJob& j, __half2* xh2, int64_t pairs, cudaStream_t st) {
+  auto k = to_half_norm_kernel<FMT, SPLIT>;
+  static int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         2 * kNormConvertMaxK * (int)sizeof(float));
+    if (e != cudaSuccess) return e;
+    configured_dev = dev;
+  }
+  return launch_ex(k, dim3((unsigned)j.M), dim3(256), 2 * (size_t)j.K * sizeof(float), st, j.norm_x, j.norm_delta,
+                   j.norm_w, j.norm_eps, xh2, j.K, pairs);
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -1542,6 +1614,7 @@ int job_token_tile(const GemmJob& j) {
 bool gemm_job_supported(const GemmJob& j) {
   gemm::Geometry g;
   if (!gemm::job_geometry(j, g)) return false;
+  if (j.norm_w && (j.experts > 0 || j.x_rows || !j.norm_x || j.K > gemm::kNormConvertMaxK)) return false;
   for (int m = 0; m < j.n_mat; ++m)
     if (!j.w[m] || (reinterpret_cast<uintptr_t>(j.w[m]) & 15) != 0) return false;
   return gemm::encode_fn() != nullptr;
@@ -1572,7 +1645,22 @@ cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) 
     const unsigned blocks = (unsigned)((pairs + 255) / 256);
     __half2* xh2 = reinterpret_cast<__half2*>(xh);
     cudaError_t e;
-    if (j.split) {
+    if (j.norm_w) {
+      switch (j.dtype) {
+#define HYQ_NORM_X(F)                                                                                  \
+  case F:                                                                                              \
+    e = j.split ? launch_norm_convert<F, true>(j, xh2, pairs, st) : launch_norm_convert<F, false>(j, xh2, pairs, st); \
+    break;
+        HYQ_NORM_X(Q4_K)
+        HYQ_NORM_X(Q6_K)
+        HYQ_NORM_X(Q8_0)
+        HYQ_NORM_X(Q2_0C)
+        HYQ_NORM_X(STQ1_0)
+#undef HYQ_NORM_X
+        default: return cudaErrorNotSupported;
+      }
+      if (e != cudaSuccess) return e;
+    } else if (j.split) {
       switch (j.dtype) {
 #define HYQ_SPLIT_X(F) \
   case F: e = launch_ex(to_half_split_kernel<F>, dim3(blocks), dim3(256), 0, st, j.x, xh2, K, pairs, j.x_rows); break;

@@ -332,10 +332,9 @@ __device__ void prepare_x(const Params& p, uint8_t* smem) {
   consumers_sync();
 }
 
-// One output row: stored, or added into y in the residual form.
-__device__ __forceinline__ void emit_row(const Params& p, int m, int64_t row, float out) {
-  float* y = p.mat[m].y + row;
-  *y = p.residual ? __fadd_rn(__ldcg(y), out) : out;
+// One output row: stored, or (residual form) added to the row's value y_old.
+__device__ __forceinline__ void emit_row(const Params& p, int m, int64_t row, float out, float y_old) {
+  p.mat[m].y[row] = p.residual ? __fadd_rn(y_old, out) : out;
 }
 
 template <int FMT, int NP>
@@ -836,6 +835,13 @@ __global__ void __launch_bounds__(kThreads, DUAL ? 2 : 1) gemv_kernel(const __gr
   uint32_t par = 0;
   int64_t it = 0;
   for (int64_t bt = blockIdx.x; bt < p.total_batches; bt += gridDim.x, ++it) {
+    int m, nrows;
+    int64_t row0;
+    batch_of(p, bt, R, m, row0, nrows);
+    const int r = rgi + p.rg * ridx;  // the row this lane holds after the reduction
+    const bool emits = writer && r < nrows && (p.ks == 1 || ksi == 0);
+    // residual form: the row's current value, loaded while the tile computes
+    const float y_old = (p.residual && emits) ? __ldcg(p.mat[m].y + row0 + r) : 0.f;
     bool ok = mbar_wait(smem_addr(&full[s]), par, abort_flag);
     // The warps that share a row leave together, or the named barrier below
     // would wait for a warp that is gone.
@@ -845,9 +851,6 @@ __global__ void __launch_bounds__(kThreads, DUAL ? 2 : 1) gemv_kernel(const __gr
       *abort_flag = 1;
       break;
     }
-    int m, nrows;
-    int64_t row0;
-    batch_of(p, bt, R, m, row0, nrows);
     const uint32_t tile = stages_s + (uint32_t)s * (uint32_t)p.stage_bytes;
     const uint32_t base = tile + (uint32_t)(reinterpret_cast<uintptr_t>(p.mat[m].w + row0 * row_bytes) & 15);
     const uint32_t baseu =
@@ -863,12 +866,11 @@ __global__ void __launch_bounds__(kThreads, DUAL ? 2 : 1) gemv_kernel(const __gr
       tile_rows<FMT, NP, UPL, RW, PAIR, true>(base, baseu, row_bytes, rg, rgi, nrows, ui, uv, xu, g, u);
     warp_reduce_multi<RW>(g, lane);
     if (PAIR) warp_reduce_multi<RW>(u, lane);
-    const int r = rgi + p.rg * ridx;  // the row this lane now holds
     if (p.ks == 1) {
-      if (writer && r < nrows) {
+      if (emits) {
         float out = g[0];
         if (PAIR) out = (g[0] / (1.0f + expf(-g[0]))) * u[0];  // quant.rs:573-574
-        emit_row(p, m, row0 + r, out);
+        emit_row(p, m, row0 + r, out, y_old);
       }
     } else {
       // Partial sums of the ks warps of each row, double-buffered by tile
@@ -880,7 +882,7 @@ __global__ void __launch_bounds__(kThreads, DUAL ? 2 : 1) gemv_kernel(const __gr
         rb[((rgi * RW + ridx) * p.ks + ksi) * 2 + 1] = PAIR ? u[0] : 0.f;
       }
       bar_sync_named(1 + rgi, p.ks * 32);
-      if (ksi == 0 && writer && r < nrows) {
+      if (emits) {
         float gs = 0.f, us = 0.f;
         for (int k = 0; k < p.ks; ++k) {
           gs += rb[((rgi * RW + ridx) * p.ks + k) * 2];
@@ -888,7 +890,7 @@ __global__ void __launch_bounds__(kThreads, DUAL ? 2 : 1) gemv_kernel(const __gr
         }
         float out = gs;
         if (PAIR) out = (gs / (1.0f + expf(-gs))) * us;
-        emit_row(p, m, row0 + r, out);
+        emit_row(p, m, row0 + r, out, y_old);
       }
     }
     __syncwarp();

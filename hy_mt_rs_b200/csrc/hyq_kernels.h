@@ -79,6 +79,13 @@ struct GemmJob {
   // Split-operand form (hi + lo fp16 operands, three MMAs per K chunk, f32
   // accuracy); the workspace then holds two activation copies.
   bool split = false;
+  // Fused input (not with experts or x_rows): with norm_w set the product
+  // reads RMSNorm(norm_x rows) * norm_w; with norm_delta set too, norm_x +=
+  // norm_delta first (written back).  K at most 16384.
+  float* norm_x = nullptr;
+  const float* norm_delta = nullptr;
+  const float* norm_w = nullptr;
+  float norm_eps = 0.f;
 };
 bool gemm_job_supported(const GemmJob& job);
 size_t gemm_job_workspace_bytes(const GemmJob& job);

@@ -372,10 +372,13 @@ __device__ __forceinline__ void stage_rows_h(float* dst, int sstride, const __ha
   }
 }
 
-// DIM, GRP > 0: a kernel for head size DIM and GRP query heads per kv head
-// (loops unrolled to constant offsets); 0: any shape.  KV16: the caches hold
-// binary16 values (widened to f32 as they are staged; the arithmetic after
-// that is the same).
+// DIM, GRP > 0: a kernel for head size DIM whose CTAs take GRP query heads
+// that share a kv head (loops unrolled to constant offsets; GRP may be a
+// divisor of the heads per kv head, so that a small launch spreads over more
+// CTAs: grid.y = heads / GRP); 0: any shape, a CTA per kv head.  KV16: the
+// caches hold binary16 values (widened to f32 as they are staged; the
+// arithmetic after that is the same).  Each head's arithmetic does not
+// depend on how the heads are grouped.
 template <int DIM, int GRP, bool KV16>
 __global__ void __launch_bounds__(kAttnThreads, (KV16 && DIM > 0) ? 5 : 3)
     attention_kernel(const __grid_constant__ AttnArgs a) {
@@ -395,9 +398,10 @@ __global__ void __launch_bounds__(kAttnThreads, (KV16 && DIM > 0) ? 5 : 3)
   }
   const int visible = pos + 1;
   const int used = (visible + kAttnChunk - 1) / kAttnChunk;  // splits with positions
-  const int split = blockIdx.x, kvh = blockIdx.y;
+  const int split = blockIdx.x, hblk = blockIdx.y;  // chunk, head group
   if (split >= used) return;
   const int dim = DIM ? DIM : a.dim, G = GRP ? GRP : a.heads / a.kv_heads, ks = attn_kstride(dim);
+  const int kvh = hblk * G / (a.heads / a.kv_heads);  // the group's kv head
   const int nsplit = (a.positions + kAttnChunk - 1) / kAttnChunk;
   // f16 rows in shared memory (KV16, specialised head size), else f32 rows
   constexpr bool kHalf = KV16 && DIM > 0;
@@ -464,7 +468,7 @@ __global__ void __launch_bounds__(kAttnThreads, (KV16 && DIM > 0) ? 5 : 3)
     stage_rows<DIM>(v_s, dim, vg, width, n_stage, dim, vec);
     cp_async_commit();
   }
-  const size_t h0 = (size_t)tok * a.heads + (size_t)kvh * G;  // (token, first head of the group)
+  const size_t h0 = (size_t)tok * a.heads + (size_t)hblk * G;  // (token, first head of the group)
   const float* qg = a.q + h0 * dim;
   if (vec && (reinterpret_cast<uintptr_t>(qg) & 15) == 0) {
     const int q4 = dim >> 2;
@@ -656,11 +660,15 @@ __global__ void __launch_bounds__(kAttnThreads, (KV16 && DIM > 0) ? 5 : 3)
       }
     }
   }
-  // the last CTA of this (token, kv head) combines the splits
-  __threadfence();
+  // the last CTA of this (token, kv head) combines the splits: the CTA's
+  // partials are ordered before the count by the barrier and thread 0's
+  // device-scope fence
   __syncthreads();
-  unsigned* counter = a.counters + (size_t)tok * a.kv_heads + kvh;
-  if (threadIdx.x == 0) last_s = atomicAdd(counter, 1u) == (unsigned)(used - 1);
+  unsigned* counter = a.counters + (size_t)tok * gridDim.y + hblk;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last_s = atomicAdd(counter, 1u) == (unsigned)(used - 1);
+  }
   __syncthreads();
   if (!last_s) return;
   __threadfence();
@@ -895,6 +903,15 @@ __global__ void __launch_bounds__(1024) argmax_rows_kernel(const float* __restri
 // ---------------------------------------------------------------------------
 // C ABI
 // ---------------------------------------------------------------------------
+namespace {
+// SMs of the current device (148 if the query fails)
+int sm_count() {
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+}  // namespace
+
 extern "C" {
 
 int hyq_rope_table(int64_t positions, int head_dim, float rope_base, float* cos_out, float* sin_out) {
@@ -1103,15 +1120,25 @@ static int attention_impl(const void* k_cache, const void* v_cache, const float*
   const unsigned splits = (unsigned)((positions + hyq::model::kAttnChunk - 1) / hyq::model::kAttnChunk);
   size_t smem = hyq::model::attn_smem_bytes(head_dim, heads / kv_heads, (int)splits);
   // head size 128 with 4 query heads per kv head (the Dense and 7B shapes)
-  // over 16-byte aligned caches: the specialised kernel
+  // over 16-byte aligned caches: the specialised kernel.  A launch with few
+  // CTAs (a single request: kv heads x chunks well under the SM count) gives
+  // each CTA one query head instead of the kv head's four, so that the
+  // scores and values of a chunk are spread over four times the CTAs (the
+  // K/V chunk is then read by four CTAs, from L2).
   const bool fixed = head_dim == 128 && heads == 4 * kv_heads &&
                      ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15) == 0 &&
                      (seq_stride & (kv16 ? 7 : 3)) == 0;
-  auto kern = kv16 ? (fixed ? hyq::model::attention_kernel<128, 4, true> : hyq::model::attention_kernel<0, 0, true>)
-                   : (fixed ? hyq::model::attention_kernel<128, 4, false> : hyq::model::attention_kernel<0, 0, false>);
-  if (kv16 && fixed) smem = hyq::model::attn_smem_bytes_h(head_dim, heads / kv_heads, (int)splits);
-  const int kid = (kv16 ? 2 : 0) + (fixed ? 1 : 0);
-  static int smem_dev[4] = {-1, -1, -1, -1};  // the largest shape's shared memory, allowed once per device
+  const bool single = fixed && !fuse && tokens * heads * (int64_t)splits <= 2 * (int64_t)sm_count();
+  auto kern = kv16 ? (single ? hyq::model::attention_kernel<128, 1, true>
+                             : fixed ? hyq::model::attention_kernel<128, 4, true> : hyq::model::attention_kernel<0, 0, true>)
+                   : (single ? hyq::model::attention_kernel<128, 1, false>
+                             : fixed ? hyq::model::attention_kernel<128, 4, false>
+                                     : hyq::model::attention_kernel<0, 0, false>);
+  const int group = single ? 1 : heads / kv_heads;  // query heads per CTA
+  smem = (kv16 && fixed) ? hyq::model::attn_smem_bytes_h(head_dim, group, (int)splits)
+                         : hyq::model::attn_smem_bytes(head_dim, group, (int)splits);
+  const int kid = (kv16 ? 3 : 0) + (single ? 2 : fixed ? 1 : 0);
+  static int smem_dev[6] = {-1, -1, -1, -1, -1, -1};  // the largest shape's shared memory, allowed once per device
   int dev = 0;
   cudaGetDevice(&dev);
   if (smem_dev[kid] != dev) {
@@ -1120,7 +1147,7 @@ static int attention_impl(const void* k_cache, const void* v_cache, const float*
                                                           hyq::model::kMaxPositions / hyq::model::kAttnChunk));
     smem_dev[kid] = dev;
   }
-  const cudaError_t e = hyq::model::launch(kern, dim3(splits, (unsigned)kv_heads, (unsigned)tokens),
+  const cudaError_t e = hyq::model::launch(kern, dim3(splits, (unsigned)(heads / group), (unsigned)tokens),
                                            dim3(hyq::model::kAttnThreads), smem, (cudaStream_t)stream, a);
   return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "attention: %s", cudaGetErrorString(e));
 }

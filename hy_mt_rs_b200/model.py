@@ -364,64 +364,85 @@ class DenseModel:
         pos = self.pos if pos is None else pos
         token_out = self.token if token_out is None else token_out
         logits = self.logits if logits is None else logits
-        H = cfg.hidden
-        last = lambda t: C.c_void_p(t.data_ptr() + (M - 1) * t.stride(0) * t.element_size())  # noqa: E731
         check(lib.hyq_embed(self.embed.handle, _p(tokens), M, _p(a.hidden), st))
-        if M == 1 and self.fuse_norms:
+        if M > 1:
+            self._enqueue_batched(a, caches, pos, token_out, logits)
+        elif self.fuse_norms:
             self._enqueue_fused_norms(a, caches, pos, token_out, logits)
-            return
-        check(lib.hyq_rms_norm(_p(a.hidden), _p(self.layers[0]["input_norm"]), H, M, cfg.eps, _p(a.normalized), st))
+        else:
+            self._enqueue_separate_norms(a, caches, pos, token_out, logits)
+
+    def _enqueue_batched(self, a, caches, pos, token_out, logits):
+        """The batched forward (model.rs:549-646) of a.M > 1 tokens at *pos ..:
+        every residual add and RMSNorm runs in the activation conversion of
+        the batched product that follows it (hyq_matmul_qkv_norm,
+        hyq_matmul_gate_up_silu_norm, hyq_matmul_norm; bit-identical to the
+        separate add + norm kernel), the MoE FFN takes the separate one."""
+        cfg, st, M, H = self.cfg, self._stream(), a.M, self.cfg.hidden
+        delta = None   # the residual add the next fused norm applies
         for i, W in enumerate(self.layers):
             kc, vc = (W["k_cache"], W["v_cache"]) if caches is None else caches[i]
-            act_qkv, act_o, act_ffn = self._acts[i] if M == 1 else (_F32, _F32, _F32)
-            if M == 1:
-                qkv = lib.hyq_gemv_qkv_int8 if act_qkv == _Q8 else lib.hyq_gemv_qkv
-                check(qkv(W["q"].handle, W["k"].handle, W["v"].handle, _p(a.normalized), _p(a.q), _p(a.k), _p(a.v),
-                          st))
+            check(lib.hyq_matmul_qkv_norm(W["q"].handle, W["k"].handle, W["v"].handle, _p(a.hidden), delta,
+                                          _p(W["input_norm"]), cfg.eps, M, _p(a.q), _p(a.k), _p(a.v), st))
+            rope = lib.hyq_rope_qk_kv16 if self.kv16 else lib.hyq_rope_qk
+            attention = lib.hyq_attention_kv16 if self.kv16 else lib.hyq_attention
+            check(rope(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim, _p(self.cos), _p(self.sin),
+                       cfg.positions, _p(pos), M, _p(W["q_norm"]), _p(W["k_norm"]), cfg.eps, self.norm_first, _p(kc),
+                       _p(vc), st))
+            check(attention(_p(a.q), _p(kc), _p(vc), cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.positions, _p(pos),
+                            M, _p(a.attended), _p(self.attn_ws), st))
+            check(lib.hyq_matmul(W["o"].handle, _p(a.attended), M, _p(a.projected), st))
+            if "moe" in W:      # Moe::forward (model.rs:688-726)
+                check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.projected), _p(W["ffn_norm"]), H, M, cfg.eps,
+                                           _p(a.normalized), st))
+                W["moe"].forward(a.normalized, M, out=a.ff)
             else:
-                check(lib.hyq_matmul_qkv(W["q"].handle, W["k"].handle, W["v"].handle, _p(a.normalized), M, _p(a.q),
-                                         _p(a.k), _p(a.v), st))
-            if M == 1 and self.rope_in_attention:
-                check(lib.hyq_rope_attention(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim,
-                                             _p(self.cos), _p(self.sin), cfg.positions, _p(pos), _p(W["q_norm"]),
-                                             _p(W["k_norm"]), cfg.eps, self.norm_first, _p(kc), _p(vc), _p(a.attended),
-                                             _p(self.attn_ws), st))
-            else:
-                rope = lib.hyq_rope_qk_kv16 if self.kv16 else lib.hyq_rope_qk
-                attention = lib.hyq_attention_kv16 if self.kv16 else lib.hyq_attention
-                check(rope(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim, _p(self.cos),
-                           _p(self.sin), cfg.positions, _p(pos), M, _p(W["q_norm"]), _p(W["k_norm"]), cfg.eps,
-                           self.norm_first,
-                           _p(kc), _p(vc), st))
-                check(attention(_p(a.q), _p(kc), _p(vc), cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.positions,
-                                _p(pos), M, _p(a.attended), _p(self.attn_ws), st))
+                check(lib.hyq_matmul_gate_up_silu_norm(W["gate"].handle, W["up"].handle, _p(a.hidden),
+                                                       _p(a.projected), _p(W["ffn_norm"]), cfg.eps, M, _p(a.gate),
+                                                       st))
+                check(lib.hyq_matmul(W["down"].handle, _p(a.gate), M, _p(a.ff), st))
+            delta = _p(a.ff)
+        # logits of the last token only (model.rs:619-622): its residual add
+        # and norm, then the lm_head
+        last = lambda t: C.c_void_p(t.data_ptr() + (M - 1) * t.stride(0) * t.element_size())  # noqa: E731
+        check(lib.hyq_matmul_norm(self.output.handle, last(a.hidden), last(a.ff), _p(self.output_norm), cfg.eps, 1,
+                                  _p(logits), st))
+        check(lib.hyq_argmax(_p(logits), cfg.vocab, _p(token_out), _p(pos), M, _p(self.argmax_ws), st))
+
+    def _enqueue_separate_norms(self, a, caches, pos, token_out, logits):
+        """The single-token step with each RMSNorm and residual add as its own
+        launch (fuse_norms=False)."""
+        cfg, st, H = self.cfg, self._stream(), self.cfg.hidden
+        check(lib.hyq_rms_norm(_p(a.hidden), _p(self.layers[0]["input_norm"]), H, 1, cfg.eps, _p(a.normalized), st))
+        for i, W in enumerate(self.layers):
+            kc, vc = (W["k_cache"], W["v_cache"]) if caches is None else caches[i]
+            act_qkv, act_o, act_ffn = self._acts[i]
+            qkv = lib.hyq_gemv_qkv_int8 if act_qkv == _Q8 else lib.hyq_gemv_qkv
+            check(qkv(W["q"].handle, W["k"].handle, W["v"].handle, _p(a.normalized), _p(a.q), _p(a.k), _p(a.v), st))
+            self._attention_one(W, a, kc, vc, pos)
             if act_o == _Q8:
                 check(lib.hyq_gemv_int8(W["o"].handle, _p(a.attended), _p(a.projected), st))
             else:
-                check(lib.hyq_matmul(W["o"].handle, _p(a.attended), M, _p(a.projected), st))
+                check(lib.hyq_matmul(W["o"].handle, _p(a.attended), 1, _p(a.projected), st))
             # residual add fused with the norm that follows it
-            check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.projected), _p(W["ffn_norm"]), H, M, cfg.eps,
+            check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.projected), _p(W["ffn_norm"]), H, 1, cfg.eps,
                                        _p(a.normalized), st))
             if "moe" in W:      # Moe::forward (model.rs:688-726)
-                W["moe"].forward(a.normalized, M, out=a.ff)
-            elif M == 1:
+                W["moe"].forward(a.normalized, 1, out=a.ff)
+            else:
                 gate_up = lib.hyq_matmul_gate_up_silu_int8 if act_ffn == _Q8 else lib.hyq_matmul_gate_up_silu
                 check(gate_up(W["gate"].handle, W["up"].handle, _p(a.normalized), _p(a.gate), st))
-            else:
-                check(lib.hyq_matmul_gate_up_silu_batch(W["gate"].handle, W["up"].handle, _p(a.normalized), M,
-                                                        _p(a.gate), st))
-            if "moe" not in W and act_ffn == _Q8:
-                check(lib.hyq_gemv_int8(W["down"].handle, _p(a.gate), _p(a.ff), st))
-            elif "moe" not in W:
-                check(lib.hyq_matmul(W["down"].handle, _p(a.gate), M, _p(a.ff), st))
+                if act_ffn == _Q8:
+                    check(lib.hyq_gemv_int8(W["down"].handle, _p(a.gate), _p(a.ff), st))
+                else:
+                    check(lib.hyq_matmul(W["down"].handle, _p(a.gate), 1, _p(a.ff), st))
             nxt = self.layers[i + 1]["input_norm"] if i + 1 < len(self.layers) else self.output_norm
-            check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.ff), _p(nxt), H, M, cfg.eps, _p(a.normalized), st))
-        # logits of the last token only (model.rs:619-622)
-        if M == 1 and self._act_head == _Q8:
-            check(lib.hyq_gemv_int8(self.output.handle, last(a.normalized), _p(logits), st))
+            check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.ff), _p(nxt), H, 1, cfg.eps, _p(a.normalized), st))
+        if self._act_head == _Q8:
+            check(lib.hyq_gemv_int8(self.output.handle, _p(a.normalized), _p(logits), st))
         else:
-            check(lib.hyq_matmul(self.output.handle, last(a.normalized), 1, _p(logits), st))
-        check(lib.hyq_argmax(_p(logits), cfg.vocab, _p(token_out), _p(pos), M, _p(self.argmax_ws), st))
+            check(lib.hyq_matmul(self.output.handle, _p(a.normalized), 1, _p(logits), st))
+        check(lib.hyq_argmax(_p(logits), cfg.vocab, _p(token_out), _p(pos), 1, _p(self.argmax_ws), st))
 
     def _attention_one(self, W, a, kc, vc, pos):
         cfg, st = self.cfg, self._stream()
@@ -576,11 +597,13 @@ class DenseBatch:
         m, cfg, a, B = self.m, self.m.cfg, self.acts, self.B
         st, H = m._stream(), cfg.hidden
         check(lib.hyq_embed(m.embed.handle, _p(self.tokens), B, _p(a.hidden), st))
-        check(lib.hyq_rms_norm(_p(a.hidden), _p(m.layers[0]["input_norm"]), H, B, cfg.eps, _p(a.normalized), st))
+        # every residual add and RMSNorm runs in the activation conversion of
+        # the product that follows it (the MoE FFN takes the separate kernel)
+        delta = None
         for i, W in enumerate(m.layers):
             kc, vc = self.caches[i]
-            check(lib.hyq_matmul_qkv(W["q"].handle, W["k"].handle, W["v"].handle, _p(a.normalized), B, _p(a.q),
-                                     _p(a.k), _p(a.v), st))
+            check(lib.hyq_matmul_qkv_norm(W["q"].handle, W["k"].handle, W["v"].handle, _p(a.hidden), delta,
+                                          _p(W["input_norm"]), cfg.eps, B, _p(a.q), _p(a.k), _p(a.v), st))
             if m.rope_in_attention:
                 check(lib.hyq_rope_attention_seqs(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim,
                                                   _p(m.cos), _p(m.sin), cfg.positions, _p(self.pos), B,
@@ -596,17 +619,18 @@ class DenseBatch:
                 check(attention(_p(a.q), _p(kc), _p(vc), cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.positions,
                                 _p(self.pos), B, self.stride, _p(a.attended), _p(self.attn_ws), st))
             check(lib.hyq_matmul(W["o"].handle, _p(a.attended), B, _p(a.projected), st))
-            check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.projected), _p(W["ffn_norm"]), H, B, cfg.eps,
-                                       _p(a.normalized), st))
             if "moe" in W:      # Moe::forward over the requests' rows
+                check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.projected), _p(W["ffn_norm"]), H, B, cfg.eps,
+                                           _p(a.normalized), st))
                 W["moe"].forward(a.normalized, B, out=a.ff)
             else:
-                check(lib.hyq_matmul_gate_up_silu_batch(W["gate"].handle, W["up"].handle, _p(a.normalized), B,
-                                                        _p(a.gate), st))
+                check(lib.hyq_matmul_gate_up_silu_norm(W["gate"].handle, W["up"].handle, _p(a.hidden),
+                                                       _p(a.projected), _p(W["ffn_norm"]), cfg.eps, B, _p(a.gate),
+                                                       st))
                 check(lib.hyq_matmul(W["down"].handle, _p(a.gate), B, _p(a.ff), st))
-            nxt = m.layers[i + 1]["input_norm"] if i + 1 < len(m.layers) else m.output_norm
-            check(lib.hyq_add_rms_norm(_p(a.hidden), _p(a.ff), _p(nxt), H, B, cfg.eps, _p(a.normalized), st))
-        check(lib.hyq_matmul(m.output.handle, _p(a.normalized), B, _p(self.logits), st))
+            delta = _p(a.ff)
+        check(lib.hyq_matmul_norm(m.output.handle, _p(a.hidden), delta, _p(m.output_norm), cfg.eps, B,
+                                  _p(self.logits), st))
         check(lib.hyq_argmax_rows(_p(self.logits), cfg.vocab, B, _p(self.tokens), _p(self.pos), st))
 
     def launches(self, sms=148):
@@ -618,15 +642,23 @@ class DenseBatch:
         t = cfg.linear_dtype
         KV = cfg.kv_heads * cfg.head_dim
         if B >= 16:
+            # the norms run in the conversions of QKV, gate/up and lm_head
             g = lambda tiles, K, dt=t: quant.gemm_launches(tiles, K, B, dt, sms)  # noqa: E731
             attn = g((cfg.heads * cfg.head_dim + 2 * KV) // 128, cfg.hidden) + g(cfg.hidden // 128, cfg.hidden)
             ffn = g(2 * cfg.ffn // 128, cfg.hidden) + g(cfg.hidden // 128, cfg.ffn)
             lm_head = g(-(-cfg.vocab // 128), cfg.hidden, cfg.embed_dtype)
+            norm = 0
         else:
+            # batch-1 products; each fused form runs its add + norm kernel first
             attn, ffn, lm_head = 2 * B, 2 * B, B
-        base = 3 if self.m.rope_in_attention else 4
-        layers = sum(base + attn + (W["moe"].launches(B) if "moe" in W else ffn) for W in self.m.layers)
-        return 2 + layers + lm_head + 1
+            norm = 1
+        ra = 1 if self.m.rope_in_attention else 2   # (RoPE +) attention
+        # embedding; per layer QKV (+ norm), (RoPE,) attention, O, then gate/up
+        # (+ norm) and down, or the MoE layer after its add + norm kernel;
+        # lm_head (+ norm); argmax
+        layers = sum(norm + ra + attn + (1 + W["moe"].launches(B) if "moe" in W else norm + ffn)
+                     for W in self.m.layers)
+        return 1 + layers + norm + lm_head + 1
 
     def capture(self, stream):
         quant.set_launch_overlap(True)

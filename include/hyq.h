@@ -186,6 +186,24 @@ int hyq_matmul_qkv(const hyq_weight* q, const hyq_weight* k, const hyq_weight* v
 int hyq_matmul_gate_up_silu_batch(const hyq_weight* gate, const hyq_weight* up, const float* input, int64_t batch,
                                   float* out, void* stream);
 
+/* Batched products fused with the residual-stream steps in front of them
+ * (the batched forward, model.rs:569-616): hidden [batch, K] += delta (when
+ * delta is not NULL; add, model.rs:1043-1071, written back to hidden), then
+ * the product of RMSNorm(hidden rows) * norm_w (rms_norm_into,
+ * model.rs:785-830).  From 16 rows the tensor-core path does the add and the
+ * norm in its activation conversion (one CTA per row, K at most 16384);
+ * below that, and for shapes it does not take, the separate add + norm
+ * kernel writes a pool buffer that the plain forms read.  Either way the
+ * results and hidden are bit-identical to hyq_add_rms_norm / hyq_rms_norm
+ * followed by hyq_matmul_qkv, hyq_matmul_gate_up_silu_batch or hyq_matmul. */
+int hyq_matmul_qkv_norm(const hyq_weight* q, const hyq_weight* k, const hyq_weight* v, float* hidden,
+                        const float* delta, const float* norm_w, float eps, int64_t batch, float* q_out,
+                        float* k_out, float* v_out, void* stream);
+int hyq_matmul_gate_up_silu_norm(const hyq_weight* gate, const hyq_weight* up, float* hidden, const float* delta,
+                                 const float* norm_w, float eps, int64_t batch, float* out, void* stream);
+int hyq_matmul_norm(const hyq_weight* w, float* hidden, const float* delta, const float* norm_w, float eps,
+                    int64_t batch, float* out, void* stream);
+
 /* Q8::quantize_into (quant.rs:904-922): int8 activations, one f32 scale per
  * 256 values, and the Q2_0C de-interleaved copy (values_q2c may be NULL).
  * Bit-exact with the reference.  scales has ceil(len/256) entries. */

@@ -201,3 +201,74 @@ def test_gemm_split_layer_calls_match_batch1_products(cuda, t, M):
     rows = torch.stack([gate.matmul_gate_up_silu(up, x[i].contiguous()) for i in range(M)])
     assert _rel(got_gu, rows) < 1e-5, _rel(got_gu, rows)
     assert quant.device_status() == 0
+
+
+@pytest.mark.parametrize("t,M,split,delta", [(Q2_0C, 64, True, True), (Q2_0C, 64, False, False),
+                                             (Q4_K, 40, True, False), (STQ1_0, 256, False, True),
+                                             (Q2_0C, 5, True, True), (Q6_K, 1, False, True)])
+def test_batched_norm_forms_match_separate_calls(cuda, t, M, split, delta):
+    """hyq_matmul_qkv_norm / hyq_matmul_gate_up_silu_norm / hyq_matmul_norm
+    (the residual add and the RMSNorm inside the tensor-core conversion from
+    16 rows, the separate kernel below) = hyq_add_rms_norm (or hyq_rms_norm)
+    followed by the plain batched product: outputs and the updated hidden
+    rows bit-identical, both operand precisions."""
+    import ctypes as C
+    import torch
+    from hy_mt_rs_b200 import quant, synth
+    from hy_mt_rs_b200._native import lib
+
+    def P(x):
+        return C.c_void_p(x.data_ptr()) if x is not None else None
+
+    def ok(rc):
+        assert rc == 0, lib.hyq_last_error().decode()
+
+    K, Nq, Nkv, F = 2048, 2048, 512, 1024
+
+    def weight(N, seed):
+        packed = synth.encode(t, synth.random_weights(N, K, seed))
+        return quant.Weight(packed.to(cuda), t, [K, N])
+
+    q, k, v, g, u, o = weight(Nq, 1), weight(Nkv, 2), weight(Nkv, 3), weight(F, 4), weight(F, 5), weight(Nq, 6)
+    rng = np.random.default_rng(M)
+    h0 = to_dev((rng.standard_normal((M, K)) * 2).astype(np.float32), cuda)
+    d = to_dev(rng.standard_normal((M, K)).astype(np.float32), cuda) if delta else None
+    w = to_dev(rng.standard_normal(K).astype(np.float32), cuda)
+    st = C.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)
+    eps = 1e-6
+    res = []
+    with quant.gemm_precision(quant.GEMM_F32 if split else quant.GEMM_FP16):
+        for fused in (False, True):
+            outs = [torch.empty(M, n, device=cuda) for n in (Nq, Nkv, Nkv, F, Nq)]
+            hids = [h0.clone() for _ in range(3)]
+            for j in range(3):
+                if fused:
+                    if j == 0:
+                        ok(lib.hyq_matmul_qkv_norm(q.handle, k.handle, v.handle, P(hids[0]), P(d), P(w), eps, M,
+                                                   *map(P, outs[:3]), st))
+                    elif j == 1:
+                        ok(lib.hyq_matmul_gate_up_silu_norm(g.handle, u.handle, P(hids[1]), P(d), P(w), eps, M,
+                                                            P(outs[3]), st))
+                    else:
+                        ok(lib.hyq_matmul_norm(o.handle, P(hids[2]), P(d), P(w), eps, M, P(outs[4]), st))
+                else:
+                    x = torch.empty(M, K, device=cuda)
+                    if delta:
+                        ok(lib.hyq_add_rms_norm(P(hids[j]), P(d), P(w), K, M, eps, P(x), st))
+                    else:
+                        ok(lib.hyq_rms_norm(P(hids[j]), P(w), K, M, eps, P(x), st))
+                    if j == 0:
+                        ok(lib.hyq_matmul_qkv(q.handle, k.handle, v.handle, P(x), M, *map(P, outs[:3]), st))
+                    elif j == 1:
+                        ok(lib.hyq_matmul_gate_up_silu_batch(g.handle, u.handle, P(x), M, P(outs[3]), st))
+                    else:
+                        ok(lib.hyq_matmul(o.handle, P(x), M, P(outs[4]), st))
+            res.append(outs + hids)
+    torch.cuda.synchronize()
+    for a, b in zip(*res):
+        assert torch.equal(a, b)
+    if delta:
+        assert torch.equal(res[1][5], h0 + d)
+    else:
+        assert torch.equal(res[1][5], h0)
+    assert quant.device_status() == 0

@@ -91,6 +91,48 @@ def test_attention_splits_match_oracle(cuda, shape, pos):
     assert not counters.any()
 
 
+@pytest.mark.parametrize("kv16", [False, True])
+def test_attention_head_groups_bit_identical(cuda, kv16):
+    """A small launch (one token, a 512-position cache: 16 heads x 8 chunks)
+    gives each CTA one query head; a 4096-position cache keeps a CTA per kv
+    head.  Each head's arithmetic is the same either way: the outputs at the
+    same position over the same rows are bit-identical, and they match the
+    oracle."""
+    import ctypes as C
+    import torch
+    from hy_mt_rs_b200._native import check, lib
+    from oracle import oracle as O
+
+    heads, kv_heads, dim = 16, 4, 128
+    g = torch.Generator().manual_seed(7)
+    q = torch.randn(heads * dim, generator=g)
+    kc = torch.randn(4096, kv_heads * dim, generator=g)
+    vc = torch.randn(4096, kv_heads * dim, generator=g)
+    if kv16:
+        kc, vc = kc.half(), vc.half()
+    d = [t.to(cuda) for t in (q, kc, vc)]
+    attention = lib.hyq_attention_kv16 if kv16 else lib.hyq_attention
+    st = C.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)
+    for pos in (0, 63, 200, 511):
+        p = torch.tensor([pos], dtype=torch.int32, device=cuda)
+        outs = []
+        for positions in (512, 4096):
+            ws = C.c_size_t()
+            check(lib.hyq_attention_workspace_bytes(heads, dim, positions, 1, C.byref(ws)))
+            work = torch.zeros(ws.value, dtype=torch.uint8, device=cuda)
+            out = torch.full((heads * dim,), float("nan"), device=cuda)
+            check(attention(*(C.c_void_p(t.data_ptr()) for t in d), heads, kv_heads, dim, positions,
+                            C.c_void_p(p.data_ptr()), 1, C.c_void_p(out.data_ptr()), C.c_void_p(work.data_ptr()),
+                            st))
+            torch.cuda.synchronize()
+            assert not work[:heads * 4 * 8].any()   # counters left zero
+            outs.append(out.cpu())
+        assert torch.equal(outs[0], outs[1]), pos
+        ref = O.attention(q.numpy(), kc[:pos + 1].float().numpy(), vc[:pos + 1].float().numpy(), heads, kv_heads,
+                          dim, pos)
+        np.testing.assert_allclose(outs[0].numpy(), ref, rtol=2e-5, atol=2e-6)
+
+
 @pytest.mark.parametrize("shape,pos", [((16, 4, 128), 0), ((16, 4, 128), 63), ((16, 4, 128), 64),
                                        ((16, 4, 128), 300), ((8, 4, 64), 77), ((6, 2, 40), 130)])
 @pytest.mark.parametrize("norm_first", [0, 1])
