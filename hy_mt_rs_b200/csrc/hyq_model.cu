@@ -372,6 +372,110 @@ __device__ __forceinline__ void stage_rows_h(float* dst, int sstride, const __ha
   }
 }
 
+// The end of every attention CTA: once this CTA's partials (max, sum and
+// unnormalised output per head, in the workspace) are written, count the
+// CTA; the last CTA of a (token, head group) combines the chunks per head:
+// out = sum_i o_i e^(m_i - M) / sum_i l_i e^(m_i - M).
+__device__ void attn_finish(const AttnArgs& a, int tok, int hblk, int G, int dim, int used, int nsplit, size_t h0,
+                            float* cw_s, float* inv_s) {
+  __shared__ int last_s;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int outs = G * dim;
+  // the CTA's partials are ordered before the count by the barrier and
+  // thread 0's device-scope fence
+  __syncthreads();
+  unsigned* counter = a.counters + (size_t)tok * gridDim.y + hblk;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last_s = atomicAdd(counter, 1u) == (unsigned)(used - 1);
+  }
+  __syncthreads();
+  if (!last_s) return;
+  __threadfence();
+  // partials of other CTAs are read past L1 (__ldcg).  The loads of the
+  // first eight splits' partial outputs of this thread's first four outputs
+  // are issued before the combine weights are computed, and every lane
+  // loads the (max, sum) pairs of its splits at once: one round trip to L2
+  // for a combine of up to eight splits.
+  const size_t stride = 2 + (size_t)dim;
+  float pre[4][8];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int t = min((int)threadIdx.x + k * kAttnThreads, outs - 1);
+    const int g = t / dim;
+    const float* src = a.ws + (h0 + g) * nsplit * stride + 2 + (t - g * dim);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) pre[k][j] = j < used ? __ldcg(src + (size_t)j * stride) : 0.f;
+  }
+  for (int g = warp; g < G; g += kAttnThreads / 32) {
+    const float* wh = a.ws + (h0 + g) * nsplit * stride;
+    float* cw = cw_s + g * nsplit;
+    float m = -INFINITY, l = 0.f;
+    if (used <= 32) {
+      // one split per lane: its (max, sum) pair in one load round
+      const float mi = lane < used ? __ldcg(wh + lane * stride) : -INFINITY;
+      const float li = lane < used ? __ldcg(wh + lane * stride + 1) : 0.f;
+      m = mi;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (lane < used) {
+        const float c = expf(mi - m);
+        cw[lane] = c;
+        l = fmaf(li, c, l);
+      }
+    } else {
+      for (int i = lane; i < used; i += 32) m = fmaxf(m, __ldcg(wh + i * stride));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      for (int i = lane; i < used; i += 32) {
+        const float c = expf(__ldcg(wh + i * stride) - m);
+        cw[i] = c;
+        l = fmaf(__ldcg(wh + i * stride + 1), c, l);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    if (lane == 0) inv_s[g] = 1.0f / l;
+  }
+  __syncthreads();
+  // four outputs per thread, their partials loaded eight splits at a time
+  // (independent loads in flight), accumulated in split order
+  for (int t0 = threadIdx.x; t0 < outs; t0 += 4 * kAttnThreads) {
+    const float* src[4];
+    const float* cw[4];
+    float o[4];
+    int gk[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int t = min(t0 + k * kAttnThreads, outs - 1);
+      gk[k] = t / dim;
+      src[k] = a.ws + (h0 + gk[k]) * nsplit * stride + 2 + (t - gk[k] * dim);
+      cw[k] = cw_s + gk[k] * nsplit;
+      o[k] = 0.f;
+    }
+    for (int i0 = 0; i0 < used; i0 += 8) {
+      float v[4][8];
+      const bool first = t0 == (int)threadIdx.x && i0 == 0;  // the prefetched batch
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          v[k][j] = first ? pre[k][j] : (i0 + j < used ? __ldcg(src[k] + (size_t)(i0 + j) * stride) : 0.f);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (i0 + j < used) o[k] = fmaf(v[k][j], cw[k][i0 + j], o[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int t = t0 + k * kAttnThreads;
+      if (t < outs) a.out[(h0 + gk[k]) * dim + (t - gk[k] * dim)] = o[k] * inv_s[gk[k]];
+    }
+  }
+  if (threadIdx.x == 0) *counter = 0;  // ready for the next call
+}
+
 // DIM, GRP > 0: a kernel for head size DIM whose CTAs take GRP query heads
 // that share a kv head (loops unrolled to constant offsets; GRP may be a
 // divisor of the heads per kv head, so that a small launch spreads over more
@@ -386,7 +490,6 @@ __global__ void __launch_bounds__(kAttnThreads, (KV16 && DIM > 0) ? 5 : 3)
   grid_dependency_wait();
   allow_dependents_launch();
   extern __shared__ __align__(16) float attn_smem[];
-  __shared__ int last_s;
   // token tok of the batch sits at position *pos + tok and sees positions
   // 0 ..= it (causal, model.rs:959)
   const int tok = blockIdx.z;
@@ -660,100 +763,7 @@ __global__ void __launch_bounds__(kAttnThreads, (KV16 && DIM > 0) ? 5 : 3)
       }
     }
   }
-  // the last CTA of this (token, kv head) combines the splits: the CTA's
-  // partials are ordered before the count by the barrier and thread 0's
-  // device-scope fence
-  __syncthreads();
-  unsigned* counter = a.counters + (size_t)tok * gridDim.y + hblk;
-  if (threadIdx.x == 0) {
-    __threadfence();
-    last_s = atomicAdd(counter, 1u) == (unsigned)(used - 1);
-  }
-  __syncthreads();
-  if (!last_s) return;
-  __threadfence();
-  // partials of other CTAs are read past L1 (__ldcg).  The loads of the
-  // first eight splits' partial outputs of this thread's first four outputs
-  // are issued before the combine weights are computed, and every lane
-  // loads the (max, sum) pairs of its splits at once: one round trip to L2
-  // for a combine of up to eight splits.
-  const size_t stride = 2 + (size_t)dim;
-  float pre[4][8];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int t = min((int)threadIdx.x + k * kAttnThreads, outs - 1);
-    const int g = t / dim;
-    const float* src = a.ws + (h0 + g) * nsplit * stride + 2 + (t - g * dim);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) pre[k][j] = j < used ? __ldcg(src + (size_t)j * stride) : 0.f;
-  }
-  for (int g = warp; g < G; g += kAttnThreads / 32) {
-    const float* wh = a.ws + (h0 + g) * nsplit * stride;
-    float* cw = cw_s + g * nsplit;
-    float m = -INFINITY, l = 0.f;
-    if (used <= 32) {
-      // one split per lane: its (max, sum) pair in one load round
-      const float mi = lane < used ? __ldcg(wh + lane * stride) : -INFINITY;
-      const float li = lane < used ? __ldcg(wh + lane * stride + 1) : 0.f;
-      m = mi;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      if (lane < used) {
-        const float c = expf(mi - m);
-        cw[lane] = c;
-        l = fmaf(li, c, l);
-      }
-    } else {
-      for (int i = lane; i < used; i += 32) m = fmaxf(m, __ldcg(wh + i * stride));
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      for (int i = lane; i < used; i += 32) {
-        const float c = expf(__ldcg(wh + i * stride) - m);
-        cw[i] = c;
-        l = fmaf(__ldcg(wh + i * stride + 1), c, l);
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    if (lane == 0) inv_s[g] = 1.0f / l;
-  }
-  __syncthreads();
-  // four outputs per thread, their partials loaded eight splits at a time
-  // (independent loads in flight), accumulated in split order
-  for (int t0 = threadIdx.x; t0 < outs; t0 += 4 * kAttnThreads) {
-    const float* src[4];
-    const float* cw[4];
-    float o[4];
-    int gk[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int t = min(t0 + k * kAttnThreads, outs - 1);
-      gk[k] = t / dim;
-      src[k] = a.ws + (h0 + gk[k]) * nsplit * stride + 2 + (t - gk[k] * dim);
-      cw[k] = cw_s + gk[k] * nsplit;
-      o[k] = 0.f;
-    }
-    for (int i0 = 0; i0 < used; i0 += 8) {
-      float v[4][8];
-      const bool first = t0 == (int)threadIdx.x && i0 == 0;  // the prefetched batch
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          v[k][j] = first ? pre[k][j] : (i0 + j < used ? __ldcg(src[k] + (size_t)(i0 + j) * stride) : 0.f);
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          if (i0 + j < used) o[k] = fmaf(v[k][j], cw[k][i0 + j], o[k]);
-    }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int t = t0 + k * kAttnThreads;
-      if (t < outs) a.out[(h0 + gk[k]) * dim + (t - gk[k] * dim)] = o[k] * inv_s[gk[k]];
-    }
-  }
-  if (threadIdx.x == 0) *counter = 0;  // ready for the next call
+  attn_finish(a, tok, hblk, G, dim, used, nsplit, h0, cw_s, inv_s);
 }
 
 __global__ void __launch_bounds__(256) add_kernel(float* __restrict__ dst, const float* __restrict__ src, int64_t n) {
