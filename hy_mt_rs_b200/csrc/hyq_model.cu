@@ -590,7 +590,8 @@ __global__ void __launch_bounds__(kAttnThreads, (KV16 && DIM > 0) ? 5 : 3)
     const float* c = a.cos_tab + (size_t)pos * (dim / 2);
     const float* sn = a.sin_tab + (size_t)pos * (dim / 2);
     for (int g = warp; g < G; g += kAttnThreads / 32) rope_head(q_s + g * ks, a.q_norm, c, sn, dim, a.eps, a.norm_first);
-    if (fresh && warp == 0) {
+    // the new key row: a warp without a query head when there is one
+    if (fresh && warp == (G < kAttnThreads / 32 ? G : 0)) {
       const size_t row = (size_t)tok * width + (size_t)kvh * dim;
       float* kr = k_s + (size_t)(n - 1) * ks;
       float* vr = v_s + (size_t)(n - 1) * dim;
@@ -600,12 +601,15 @@ __global__ void __launch_bounds__(kAttnThreads, (KV16 && DIM > 0) ? 5 : 3)
       }
       __syncwarp();
       rope_head(kr, a.k_norm, c, sn, dim, a.eps, a.norm_first);
-      // KV append (no other CTA of this call reads the row; f32 caches only)
-      float* kc = a.k_cache_w + seq + (size_t)pos * width + (size_t)kvh * dim;
-      float* vc = a.v_cache_w + seq + (size_t)pos * width + (size_t)kvh * dim;
-      for (int i = lane; i < dim; i += 32) {
-        kc[i] = kr[i];
-        vc[i] = vr[i];
+      // KV append (no other CTA of this call reads the row; f32 caches
+      // only); with several head groups per kv head the first one writes
+      if (hblk % ((a.heads / a.kv_heads) / G) == 0) {
+        float* kc = a.k_cache_w + seq + (size_t)pos * width + (size_t)kvh * dim;
+        float* vc = a.v_cache_w + seq + (size_t)pos * width + (size_t)kvh * dim;
+        for (int i = lane; i < dim; i += 32) {
+          kc[i] = kr[i];
+          vc[i] = vr[i];
+        }
       }
     }
   }
@@ -1138,7 +1142,7 @@ static int attention_impl(const void* k_cache, const void* v_cache, const float*
   const bool fixed = head_dim == 128 && heads == 4 * kv_heads &&
                      ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15) == 0 &&
                      (seq_stride & (kv16 ? 7 : 3)) == 0;
-  const bool single = fixed && !fuse && tokens * heads * (int64_t)splits <= 2 * (int64_t)sm_count();
+  const bool single = fixed && tokens * heads * (int64_t)splits <= 2 * (int64_t)sm_count();
   auto kern = kv16 ? (single ? hyq::model::attention_kernel<128, 1, true>
                              : fixed ? hyq::model::attention_kernel<128, 4, true> : hyq::model::attention_kernel<0, 0, true>)
                    : (single ? hyq::model::attention_kernel<128, 1, false>

@@ -156,8 +156,9 @@ class DenseModel:
     inside the attention launch (hyq_rope_attention, bit-identical to
     hyq_rope_qk + hyq_attention).  Off by default: every split CTA then
     repeats the query heads' norm and RoPE on its own critical path, which
-    measured slower than the separate launch (1.528 vs 1.514 ms per token,
-    3.89 vs 3.69 ms per step of 64 requests).
+    measured slower than the separate launch (1.318 vs 1.302 ms per token
+    with one query head per CTA and f32 KV, 3.89 vs 3.69 ms per step of 64
+    requests).
     gemm_precision: arithmetic of the batched products (prompt chunks of 16
     tokens and more, DenseBatch steps of 16 requests and more):
     quant.GEMM_FP16 (fp16 operands, the fastest) or quant.GEMM_F32 (split
