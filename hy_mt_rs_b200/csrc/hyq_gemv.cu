@@ -136,7 +136,11 @@ Plan make_plan(const GemvJob& j) {
   // f32 activations staged by one bulk copy when they are small
   pl.x_raw_bytes = (j.x && j.K * 4 <= kXStageMax) ? (int)(j.K * 4) : 0;
   pl.x_raw_off = pl.x_raw_bytes ? (kHeaderBytes + pl.x_bytes + 15) / 16 * 16 : 0;
-  const int stage_off = (kHeaderBytes + pl.x_bytes + (pl.x_raw_bytes ? 16 + pl.x_raw_bytes : 0) + 127) / 128 * 128;
+  // padded copy of the staged activations: 65 floats per 64-column unit
+  const int x_pad_bytes = pl.x_raw_bytes ? (int)(j.K / 64 * 65 * 4) : 0;
+  pl.x_pad_off = pl.x_raw_bytes ? pl.x_raw_off + pl.x_raw_bytes : 0;
+  const int stage_off =
+      (kHeaderBytes + pl.x_bytes + (pl.x_raw_bytes ? 16 + pl.x_raw_bytes + x_pad_bytes : 0) + 127) / 128 * 128;
   const int upl_max = np == 1 ? 4 : 1;
   const int64_t row_bytes = j.K / block_len(t) * block_bytes(t);
   int64_t total_rows = 0;
@@ -289,6 +293,7 @@ cudaError_t launch_gemv(const GemvJob& j, cudaStream_t st) {
   p.stage_bytes = pl.stage_bytes;
   p.x_off = kHeaderBytes;
   p.x_raw_off = pl.x_raw_off;
+  p.x_pad_off = pl.x_pad_off;
   p.stage_off = (int)(pl.smem - (size_t)pl.stages * pl.stage_bytes);
   switch (j.dtype) {
     case Q4_K: return dispatch_fmt<Q4_K>(p, pl, pair, st);

@@ -110,6 +110,7 @@ struct Params {
   int stage_bytes;
   int x_off;           // shared-memory offset of the prepared activations
   int x_raw_off;       // shared-memory offset of the f32 activation copy (0: read x from global memory)
+  int x_pad_off;       // shared-memory offset of its padded copy (65 floats per 64-column unit; 0: none)
   int stage_off;       // shared-memory offset of stage 0
   int xmode;
   const float* x;      // XF32 / XQ8F
@@ -245,6 +246,12 @@ __device__ void prepare_x(const Params& p, uint8_t* smem) {
       consumers_sync();
     }
   }
+  // The activation words read the four columns of a unit's code word, for
+  // the units of consecutive lanes: in the staged copy those sit 64 floats
+  // apart, one shared-memory bank.  The group-maxima pass therefore also
+  // writes a copy with one float of padding per 64-column unit, where they
+  // fall in consecutive banks.
+  float* xpad = (p.x_pad_off && p.xmode != XQ8) ? reinterpret_cast<float*>(smem + p.x_pad_off) : nullptr;
   if (p.xmode == XQ8) {
     for (int g = ctid; g < G; g += kCW * 32) sg[g] = p.xs[g];
   } else {
@@ -253,6 +260,14 @@ __device__ void prepare_x(const Params& p, uint8_t* smem) {
       const float4* src = reinterpret_cast<const float4*>(xsrc + 256 * g);
       const float4 a = src[lane], b = src[32 + lane];
       const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      if (xpad) {
+        const int c0 = 256 * g + 4 * lane, c1 = c0 + 128;  // column c -> c + c / 64
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          xpad[c0 + (c0 >> 6) + e] = v[e];
+          xpad[c1 + (c1 >> 6) + e] = v[4 + e];
+        }
+      }
       float m = 0.f;
       int bad = 0;
 #pragma unroll
@@ -304,16 +319,17 @@ __device__ void prepare_x(const Params& p, uint8_t* smem) {
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
       const int col = unit_col<FMT>(u, rel<FMT>(j, b));
+      const float xc = p.xmode == XQ8 ? 0.f : (xpad ? xpad[col + (col >> 6)] : xsrc[col]);
       if (p.xmode == XQ8) {
         w0 |= ((uint32_t)(uint8_t)p.xq[col]) << (8 * b);
       } else if (p.xmode == XQ8F) {
         // vcvtnq_s32_f32 + saturating narrows: nearest-even, NaN -> 0.
-        const float s = __fmul_rn(xsrc[col], gaux[u >> 2]);
+        const float s = __fmul_rn(xc, gaux[u >> 2]);
         const int q = isnan(s) ? 0 : max(-128, min(127, __float2int_rn(s)));
         w0 |= ((uint32_t)q & 0xffu) << (8 * b);
       } else {
         const float sc = gaux[u >> 2];
-        const int X = sc == 0.f ? 0 : __float2int_rn(xsrc[col] * sc);
+        const int X = sc == 0.f ? 0 : __float2int_rn(xc * sc);
         const int p0 = (int)(int8_t)(X & 0xff);
         const int t = (X - p0) >> 8;
         const int p1 = (int)(int8_t)(t & 0xff);
@@ -908,6 +924,7 @@ struct Plan {
   int ks = 1, slice = 0, upl = 1, rw = 1, stages = 0, half_bytes = 0, stage_bytes = 0;
   int x_bytes = 0;
   int x_raw_bytes = 0, x_raw_off = 0;  // staged f32 activations (0: none)
+  int x_pad_off = 0;                    // their padded copy (with the staged copy)
   int64_t total_batches = 0;
   int64_t batch_begin[3] = {};
   size_t smem = 0;

@@ -80,7 +80,7 @@ struct StepArgs {
   unsigned* attn_counters;   // [heads], zero between launches
   unsigned* sync;            // [0] barrier arrivals, [1] abort, [2..3] argmax key: zero at launch
   unsigned* status;
-  int stages, stage_bytes, stage_off, x_off, x_raw_off;
+  int stages, stage_bytes, stage_off, x_off, x_raw_off, x_pad_off;
 };
 
 constexpr int kAttnChunk = 32;
@@ -245,6 +245,7 @@ __device__ bool gemv_phase(const StepArgs& a, const Phase& P, uint8_t* smem, uin
   gp.U = P.K / 64;
   gp.x_off = a.x_off;
   gp.x_raw_off = 0;
+  gp.x_pad_off = a.x_pad_off;
   gp.xmode = gemv::XF32;
   gp.x = raw;
   gp.status = a.status;
@@ -743,7 +744,8 @@ int hyq_dense_step_create(const hyq_dense_step_desc* d, hyq_dense_step** out) {
   const int x_bytes = (3 * 16 * Umax + 2 * (Umax / 4)) * 4;  // prepare_x: three planes of words, scales
   const int x_off = gemv::kHeaderBytes;
   const int x_raw_off = (x_off + x_bytes + 15) / 16 * 16;
-  const int stage_off = (x_raw_off + d->ffn * 4 + 127) / 128 * 128;
+  const int x_pad_off = (x_raw_off + d->ffn * 4 + 15) / 16 * 16;  // prepare_x's padded copy
+  const int stage_off = (x_pad_off + Umax * 65 * 4 + 127) / 128 * 128;
   if (stage_off - x_off < 2 * step::kAttnChunk * d->head_dim * 4)
     return api_fail(HYQ_E_UNSUPPORTED, "dense_step: attention scratch does not fit");
   int dev = 0, optin = 0, sms = 0;
@@ -808,6 +810,7 @@ int hyq_dense_step_create(const hyq_dense_step_desc* d, hyq_dense_step** out) {
   a.stage_off = stage_off;
   a.x_off = x_off;
   a.x_raw_off = x_raw_off;
+  a.x_pad_off = x_pad_off;
   st->grid = sms;
   st->smem = (size_t)stage_off + (size_t)stages * stage;
   *out = st;
