@@ -313,36 +313,51 @@ __device__ void prepare_x(const Params& p, uint8_t* smem) {
     }
     consumers_sync();
   }
-  for (int idx = ctid; idx < 16 * U; idx += kCW * 32) {
-    const int u = idx % U, j = idx / U;
-    uint32_t w0 = 0, w1 = 0, w2 = 0;
+  // Item (j, u) is word j of unit u, items u-fastest over the consumer
+  // threads; (j, u) advance by increments (no division per item).  A signed
+  // 24-bit X = p0 + 2^8 p1 + 2^16 p2 (signed bytes) has p0 = X mod 2^8 as a
+  // byte, p1 = ((X + 2^7) >> 8) mod 2^8 and p2 = ((X + 2^7 + 2^15) >> 16).
+  const float* xw = xpad ? xpad : xsrc;
+  const int padsh = xpad ? 6 : 31;  // column c reads xw[c + (c >> padsh)]
+  const int du = (kCW * 32) % U, dj = (kCW * 32) / U;
+  for (int u = ctid % U, j = ctid / U; j < 16;) {
+    if (p.xmode == XQ8) {
+      uint32_t w0 = 0;
 #pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      const int col = unit_col<FMT>(u, rel<FMT>(j, b));
-      const float xc = p.xmode == XQ8 ? 0.f : (xpad ? xpad[col + (col >> 6)] : xsrc[col]);
-      if (p.xmode == XQ8) {
-        w0 |= ((uint32_t)(uint8_t)p.xq[col]) << (8 * b);
-      } else if (p.xmode == XQ8F) {
-        // vcvtnq_s32_f32 + saturating narrows: nearest-even, NaN -> 0.
-        const float s = __fmul_rn(xc, gaux[u >> 2]);
-        const int q = isnan(s) ? 0 : max(-128, min(127, __float2int_rn(s)));
-        w0 |= ((uint32_t)q & 0xffu) << (8 * b);
-      } else {
-        const float sc = gaux[u >> 2];
-        const int X = sc == 0.f ? 0 : __float2int_rn(xc * sc);
-        const int p0 = (int)(int8_t)(X & 0xff);
-        const int t = (X - p0) >> 8;
-        const int p1 = (int)(int8_t)(t & 0xff);
-        const int p2 = (t - p1) >> 8;
-        w0 |= ((uint32_t)p0 & 0xffu) << (8 * b);
-        w1 |= ((uint32_t)p1 & 0xffu) << (8 * b);
-        w2 |= ((uint32_t)p2 & 0xffu) << (8 * b);
+      for (int b = 0; b < 4; ++b) w0 |= ((uint32_t)(uint8_t)p.xq[unit_col<FMT>(u, rel<FMT>(j, b))]) << (8 * b);
+      words[j * U + u] = w0;
+    } else {
+      const float sc = gaux[u >> 2];
+      int X[4];
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const int col = unit_col<FMT>(u, rel<FMT>(j, b));
+        const float xc = xw[col + (col >> padsh)];
+        if (p.xmode == XQ8F) {
+          // vcvtnq_s32_f32 + saturating narrows: nearest-even, NaN -> 0.
+          const float q = __fmul_rn(xc, sc);
+          X[b] = isnan(q) ? 0 : max(-128, min(127, __float2int_rn(q)));
+        } else {
+          X[b] = sc == 0.f ? 0 : __float2int_rn(xc * sc);
+        }
+      }
+      words[j * U + u] = __byte_perm(__byte_perm(X[0], X[1], 0x0040), __byte_perm(X[2], X[3], 0x0040), 0x5410);
+      if (NP == 3) {
+#pragma unroll
+        for (int b = 0; b < 4; ++b) X[b] = (X[b] + 128) >> 8;
+        words[(16 + j) * U + u] =
+            __byte_perm(__byte_perm(X[0], X[1], 0x0040), __byte_perm(X[2], X[3], 0x0040), 0x5410);
+#pragma unroll
+        for (int b = 0; b < 4; ++b) X[b] = (X[b] + 128) >> 8;
+        words[(32 + j) * U + u] =
+            __byte_perm(__byte_perm(X[0], X[1], 0x0040), __byte_perm(X[2], X[3], 0x0040), 0x5410);
       }
     }
-    words[j * U + u] = w0;
-    if (NP == 3) {
-      words[(16 + j) * U + u] = w1;
-      words[(32 + j) * U + u] = w2;
+    u += du;
+    j += dj;
+    if (u >= U) {
+      u -= U;
+      ++j;
     }
   }
   consumers_sync();
