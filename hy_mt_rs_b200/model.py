@@ -137,6 +137,46 @@ class _DenseStepDesc(C.Structure):
                 ("token", C.c_void_p), ("pos", C.c_void_p)]
 
 
+# The batched forward's residual adds and RMSNorms (model.rs:569-616): with
+# split-operand products inside the products' activation conversions
+# (hyq_matmul_*_norm, one launch fewer each); with fp16 operands as the
+# separate add + norm kernel, which measured faster there (fusing gate/up's
+# norm added 0.38 ms to a 64-request step).  hidden += delta when delta is
+# given (a pointer), then the product of RMSNorm(hidden) * norm_w; the same
+# bits either way.
+def _add_norm(hidden, delta, norm_w, K, M, eps, normalized, st):
+    if delta is None:
+        check(lib.hyq_rms_norm(hidden, norm_w, K, M, eps, normalized, st))
+    else:
+        check(lib.hyq_add_rms_norm(hidden, delta, norm_w, K, M, eps, normalized, st))
+
+
+def _qkv_normed(fused, W, hidden, delta, norm_w, eps, M, normalized, outs, st):
+    if fused:
+        check(lib.hyq_matmul_qkv_norm(W["q"].handle, W["k"].handle, W["v"].handle, hidden, delta, norm_w, eps, M,
+                                      *outs, st))
+    else:
+        _add_norm(hidden, delta, norm_w, W["q"].shape()[0], M, eps, normalized, st)
+        check(lib.hyq_matmul_qkv(W["q"].handle, W["k"].handle, W["v"].handle, normalized, M, *outs, st))
+
+
+def _gate_up_normed(fused, W, hidden, delta, norm_w, eps, M, normalized, out, st):
+    if fused:
+        check(lib.hyq_matmul_gate_up_silu_norm(W["gate"].handle, W["up"].handle, hidden, delta, norm_w, eps, M, out,
+                                               st))
+    else:
+        _add_norm(hidden, delta, norm_w, W["gate"].shape()[0], M, eps, normalized, st)
+        check(lib.hyq_matmul_gate_up_silu_batch(W["gate"].handle, W["up"].handle, normalized, M, out, st))
+
+
+def _matmul_normed(fused, w, hidden, delta, norm_w, eps, M, normalized, out, st):
+    if fused:
+        check(lib.hyq_matmul_norm(w.handle, hidden, delta, norm_w, eps, M, out, st))
+    else:
+        _add_norm(hidden, delta, norm_w, w.shape()[0], M, eps, normalized, st)
+        check(lib.hyq_matmul(w.handle, normalized, M, out, st))
+
+
 class _Acts:
     """Activation buffers of a forward over M tokens (rows)."""
 
@@ -380,11 +420,12 @@ class DenseModel:
         hyq_matmul_gate_up_silu_norm, hyq_matmul_norm; bit-identical to the
         separate add + norm kernel), the MoE FFN takes the separate one."""
         cfg, st, M, H = self.cfg, self._stream(), a.M, self.cfg.hidden
-        delta = None   # the residual add the next fused norm applies
+        fused = self.precision == quant.GEMM_F32
+        delta = None   # the residual add the next norm applies
         for i, W in enumerate(self.layers):
             kc, vc = (W["k_cache"], W["v_cache"]) if caches is None else caches[i]
-            check(lib.hyq_matmul_qkv_norm(W["q"].handle, W["k"].handle, W["v"].handle, _p(a.hidden), delta,
-                                          _p(W["input_norm"]), cfg.eps, M, _p(a.q), _p(a.k), _p(a.v), st))
+            _qkv_normed(fused, W, _p(a.hidden), delta, _p(W["input_norm"]), cfg.eps, M, _p(a.normalized),
+                        (_p(a.q), _p(a.k), _p(a.v)), st)
             rope = lib.hyq_rope_qk_kv16 if self.kv16 else lib.hyq_rope_qk
             attention = lib.hyq_attention_kv16 if self.kv16 else lib.hyq_attention
             check(rope(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim, _p(self.cos), _p(self.sin),
@@ -398,16 +439,15 @@ class DenseModel:
                                            _p(a.normalized), st))
                 W["moe"].forward(a.normalized, M, out=a.ff)
             else:
-                check(lib.hyq_matmul_gate_up_silu_norm(W["gate"].handle, W["up"].handle, _p(a.hidden),
-                                                       _p(a.projected), _p(W["ffn_norm"]), cfg.eps, M, _p(a.gate),
-                                                       st))
+                _gate_up_normed(fused, W, _p(a.hidden), _p(a.projected), _p(W["ffn_norm"]), cfg.eps, M,
+                                _p(a.normalized), _p(a.gate), st)
                 check(lib.hyq_matmul(W["down"].handle, _p(a.gate), M, _p(a.ff), st))
             delta = _p(a.ff)
         # logits of the last token only (model.rs:619-622): its residual add
         # and norm, then the lm_head
         last = lambda t: C.c_void_p(t.data_ptr() + (M - 1) * t.stride(0) * t.element_size())  # noqa: E731
-        check(lib.hyq_matmul_norm(self.output.handle, last(a.hidden), last(a.ff), _p(self.output_norm), cfg.eps, 1,
-                                  _p(logits), st))
+        _matmul_normed(fused, self.output, last(a.hidden), last(a.ff), _p(self.output_norm), cfg.eps, 1,
+                       last(a.normalized), _p(logits), st)
         check(lib.hyq_argmax(_p(logits), cfg.vocab, _p(token_out), _p(pos), M, _p(self.argmax_ws), st))
 
     def _enqueue_separate_norms(self, a, caches, pos, token_out, logits):
@@ -598,13 +638,14 @@ class DenseBatch:
         m, cfg, a, B = self.m, self.m.cfg, self.acts, self.B
         st, H = m._stream(), cfg.hidden
         check(lib.hyq_embed(m.embed.handle, _p(self.tokens), B, _p(a.hidden), st))
-        # every residual add and RMSNorm runs in the activation conversion of
-        # the product that follows it (the MoE FFN takes the separate kernel)
+        # the residual adds and RMSNorms with the products (_qkv_normed and
+        # friends; the MoE FFN takes the separate kernel)
+        fused = m.precision == quant.GEMM_F32
         delta = None
         for i, W in enumerate(m.layers):
             kc, vc = self.caches[i]
-            check(lib.hyq_matmul_qkv_norm(W["q"].handle, W["k"].handle, W["v"].handle, _p(a.hidden), delta,
-                                          _p(W["input_norm"]), cfg.eps, B, _p(a.q), _p(a.k), _p(a.v), st))
+            _qkv_normed(fused, W, _p(a.hidden), delta, _p(W["input_norm"]), cfg.eps, B, _p(a.normalized),
+                        (_p(a.q), _p(a.k), _p(a.v)), st)
             if m.rope_in_attention:
                 check(lib.hyq_rope_attention_seqs(_p(a.q), _p(a.k), _p(a.v), cfg.heads, cfg.kv_heads, cfg.head_dim,
                                                   _p(m.cos), _p(m.sin), cfg.positions, _p(self.pos), B,
@@ -625,13 +666,12 @@ class DenseBatch:
                                            _p(a.normalized), st))
                 W["moe"].forward(a.normalized, B, out=a.ff)
             else:
-                check(lib.hyq_matmul_gate_up_silu_norm(W["gate"].handle, W["up"].handle, _p(a.hidden),
-                                                       _p(a.projected), _p(W["ffn_norm"]), cfg.eps, B, _p(a.gate),
-                                                       st))
+                _gate_up_normed(fused, W, _p(a.hidden), _p(a.projected), _p(W["ffn_norm"]), cfg.eps, B,
+                                _p(a.normalized), _p(a.gate), st)
                 check(lib.hyq_matmul(W["down"].handle, _p(a.gate), B, _p(a.ff), st))
             delta = _p(a.ff)
-        check(lib.hyq_matmul_norm(m.output.handle, _p(a.hidden), delta, _p(m.output_norm), cfg.eps, B,
-                                  _p(self.logits), st))
+        _matmul_normed(fused, m.output, _p(a.hidden), delta, _p(m.output_norm), cfg.eps, B, _p(a.normalized),
+                       _p(self.logits), st)
         check(lib.hyq_argmax_rows(_p(self.logits), cfg.vocab, B, _p(self.tokens), _p(self.pos), st))
 
     def launches(self, sms=148):
@@ -643,12 +683,13 @@ class DenseBatch:
         t = cfg.linear_dtype
         KV = cfg.kv_heads * cfg.head_dim
         if B >= 16:
-            # the norms run in the conversions of QKV, gate/up and lm_head
+            # split operands: the norms run in the conversions of QKV,
+            # gate/up and lm_head; fp16 operands: a separate norm kernel each
             g = lambda tiles, K, dt=t: quant.gemm_launches(tiles, K, B, dt, sms)  # noqa: E731
             attn = g((cfg.heads * cfg.head_dim + 2 * KV) // 128, cfg.hidden) + g(cfg.hidden // 128, cfg.hidden)
             ffn = g(2 * cfg.ffn // 128, cfg.hidden) + g(cfg.hidden // 128, cfg.ffn)
             lm_head = g(-(-cfg.vocab // 128), cfg.hidden, cfg.embed_dtype)
-            norm = 0
+            norm = 0 if self.m.precision == quant.GEMM_F32 else 1
         else:
             # batch-1 products; each fused form runs its add + norm kernel first
             attn, ffn, lm_head = 2 * B, 2 * B, B
