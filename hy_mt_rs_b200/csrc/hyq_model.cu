@@ -261,6 +261,14 @@ inline size_t attn_smem_bytes_h(int dim, int group, int nsplit) {
          sizeof(float) * (group * ks + (size_t)group * kAttnChunk + (size_t)group * nsplit + group);
 }
 
+// a = x0 * y0 + a, b = x1 * y1 + b in one packed instruction (fma.rn.f32x2:
+// each lane rounded as fmaf)
+__device__ __forceinline__ void ffma2_into(float& a, float& b, float x0, float x1, float y0, float y1) {
+  const float2 r = __ffma2_rn(make_float2(x0, x1), make_float2(y0, y1), make_float2(a, b));
+  a = r.x;
+  b = r.y;
+}
+
 // four binary16 values (one 8-byte shared load) as f32
 __device__ __forceinline__ float4 ld_h4(const __half* p) {
   const uint2 u = *reinterpret_cast<const uint2*>(p);
@@ -640,14 +648,10 @@ __global__ void __launch_bounds__(kAttnThreads, (KV16 && DIM > 0) ? 5 : 3)
             const float* qr = q_s + (g0 + g) * ks + 4 * hh + c;
             const float4 q0 = *reinterpret_cast<const float4*>(qr);
             const float4 q1 = *reinterpret_cast<const float4*>(qr + 8);
-            acc[g][0] = fmaf(q0.x, k0.x, acc[g][0]);
-            acc[g][1] = fmaf(q0.y, k0.y, acc[g][1]);
-            acc[g][2] = fmaf(q0.z, k0.z, acc[g][2]);
-            acc[g][3] = fmaf(q0.w, k0.w, acc[g][3]);
-            acc[g][4] = fmaf(q1.x, k1.x, acc[g][4]);
-            acc[g][5] = fmaf(q1.y, k1.y, acc[g][5]);
-            acc[g][6] = fmaf(q1.z, k1.z, acc[g][6]);
-            acc[g][7] = fmaf(q1.w, k1.w, acc[g][7]);
+            ffma2_into(acc[g][0], acc[g][1], q0.x, q0.y, k0.x, k0.y);
+            ffma2_into(acc[g][2], acc[g][3], q0.z, q0.w, k0.z, k0.w);
+            ffma2_into(acc[g][4], acc[g][5], q1.x, q1.y, k1.x, k1.y);
+            ffma2_into(acc[g][6], acc[g][7], q1.z, q1.w, k1.z, k1.w);
           }
         }
       }
@@ -725,10 +729,8 @@ __global__ void __launch_bounds__(kAttnThreads, (KV16 && DIM > 0) ? 5 : 3)
         for (int g = 0; g < 4; ++g) {
           if (g0 + g < G) {
             const float ei = e_s[(g0 + g) * kAttnChunk + i];
-            o[g].x = fmaf(ei, v.x, o[g].x);
-            o[g].y = fmaf(ei, v.y, o[g].y);
-            o[g].z = fmaf(ei, v.z, o[g].z);
-            o[g].w = fmaf(ei, v.w, o[g].w);
+            ffma2_into(o[g].x, o[g].y, ei, ei, v.x, v.y);
+            ffma2_into(o[g].z, o[g].w, ei, ei, v.z, v.w);
           }
         }
       }

@@ -542,6 +542,63 @@ def test_attention_kv16_matches_oracle(cuda, shape, pos):
     np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=2e-5, atol=2e-6)
 
 
+@pytest.mark.parametrize("seqs", [64, 256])
+def test_attention_seqs_kv16_bit_identical_per_sequence(cuda, seqs):
+    """Concurrent sequences over f16 caches (hyq_attention_seqs_kv16: a CTA
+    per (chunk, kv head, sequence), the group's four query heads together)
+    give, per sequence, bit for bit what a call for that sequence alone gives
+    (few CTAs: one query head per CTA), at positions that end inside, at the
+    end of and past a 64-position chunk, up to 8 chunks; one sequence is also
+    checked against the oracle.  The call is made twice on one workspace, so
+    the chunk counters are seen to return to zero."""
+    import ctypes as C
+    import torch
+    from hy_mt_rs_b200._native import check, lib
+    from oracle import oracle as O
+
+    heads, kv_heads, dim, positions = 16, 4, 128, 512
+    g = torch.Generator().manual_seed(seqs)
+    q = torch.randn(seqs, heads * dim, generator=g)
+    kc = torch.randn(seqs, positions, kv_heads * dim, generator=g).half()
+    vc = torch.randn(seqs, positions, kv_heads * dim, generator=g).half()
+    fixed = [0, 1, 62, 63, 64, 65, 127, 128, 300, 447, 448, 511]
+    pos = torch.tensor(fixed + torch.randint(0, positions, (seqs - len(fixed),), generator=g).tolist(),
+                       dtype=torch.int32)
+    d = [t.to(cuda) for t in (q, kc, vc)]
+    pd = pos.to(cuda)
+    st = C.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)
+    ws = C.c_size_t()
+    check(lib.hyq_attention_workspace_bytes(heads, dim, positions, seqs, C.byref(ws)))
+    work = torch.zeros(ws.value, dtype=torch.uint8, device=cuda)
+    outs = []
+    for _ in range(2):
+        out = torch.full((seqs, heads * dim), float("nan"), device=cuda)
+        check(lib.hyq_attention_seqs_kv16(*(C.c_void_p(t.data_ptr()) for t in d), heads, kv_heads, dim, positions,
+                                          C.c_void_p(pd.data_ptr()), seqs, positions * kv_heads * dim,
+                                          C.c_void_p(out.data_ptr()), C.c_void_p(work.data_ptr()), st))
+        torch.cuda.synchronize()
+        assert not work[:seqs * heads * 4].any()  # counters back to zero
+        outs.append(out.cpu())
+    assert torch.equal(outs[0], outs[1])
+    ws1 = C.c_size_t()
+    check(lib.hyq_attention_workspace_bytes(heads, dim, positions, 1, C.byref(ws1)))
+    work1 = torch.zeros(ws1.value, dtype=torch.uint8, device=cuda)
+    for s in range(seqs):
+        one = torch.full((heads * dim,), float("nan"), device=cuda)
+        p1 = pd[s:s + 1]
+        check(lib.hyq_attention_kv16(C.c_void_p(d[0][s].data_ptr()), C.c_void_p(d[1][s].data_ptr()),
+                                     C.c_void_p(d[2][s].data_ptr()), heads, kv_heads, dim, positions,
+                                     C.c_void_p(p1.data_ptr()), 1, C.c_void_p(one.data_ptr()),
+                                     C.c_void_p(work1.data_ptr()), st))
+        torch.cuda.synchronize()
+        assert torch.equal(one.cpu(), outs[0][s]), (s, int(pos[s]))
+    s = 8  # position 300
+    p = int(pos[s])
+    ref = O.attention(q[s].numpy(), kc[s, :p + 1].float().numpy(), vc[s, :p + 1].float().numpy(), heads, kv_heads,
+                      dim, p)
+    np.testing.assert_allclose(outs[0][s].numpy(), ref, rtol=2e-5, atol=2e-6)
+
+
 @pytest.mark.parametrize("batched", [False, True])
 def test_kv16_decode_matches_oracle(cuda, batched):
     """The Dense step with an f16 KV cache (DenseModel(kv16=True)) against the
