@@ -632,12 +632,12 @@ LAYER_7B = [("attn_q", 4096, 4096, 2), ("attn_k", 1024, 4096, 2), ("attn_v", 102
             ("ffn_down", 4096, 14336, 3)]  # (name, N, K, dtype): Q4_K_M-style, Q6_K down
 
 
-def gemm_launches(row_tiles, K, M, sms, dtype=2):
+def gemm_launches(row_tiles, K, M, sms, dtype=2, split=False, pair=False):
     """Kernel launches of one batched product in libhyq (hyq_gemm.cu): the
-    fp16 activation copy, the GEMM, and the split-K reduction when it splits
-    (the library's rule, mirrored in hy_mt_rs_b200.quant.gemm_splits)."""
+    fp16 activation copy, the GEMM, and the split-K or tail reduction when
+    it takes one (the library's rules, mirrored in hy_mt_rs_b200.quant)."""
     from hy_mt_rs_b200 import quant
-    return quant.gemm_launches(row_tiles, K, M, dtype, sms)
+    return quant.gemm_launches(row_tiles, K, M, dtype, sms, split=split, pair=pair)
 
 
 def prefill_arm(a):
@@ -745,8 +745,12 @@ def prefill_arm(a):
               "reasons": sorted({r for c in clocks_all for r in c.get("reasons", [])}),
               "samples": sum(c.get("samples", 0) for c in clocks_all)}
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    launches = (gemm_launches(32 + 8 + 8, 4096, M, sms) + gemm_launches(32, 4096, M, sms)
-                + gemm_launches(14336 // 64, 4096, M, sms) + gemm_launches(32, 14336, M, sms, dtype=3)) * a.steps
+    split = a.gemm_precision == "f32"
+    pair = M >= 256 and not split  # O and down (single matrices, 4096 rows) on the 2-SM kernel
+    launches = (gemm_launches(32 + 8 + 8, 4096, M, sms, split=split) + gemm_launches(32, 4096, M, sms, split=split,
+                                                                                     pair=pair)
+                + gemm_launches(14336 // 64, 4096, M, sms, split=split)
+                + gemm_launches(32, 14336, M, sms, dtype=3, split=split, pair=pair)) * a.steps
     per_ms = {k: statistics.fmean(b.elapsed_time(c) for b, c in v) for k, v in per.items()}
     gate = per_ms["ffn_gate_up_silu"]
     gate_flops = 2 * 2 * M * 14336 * 4096

@@ -131,6 +131,17 @@ struct Params {
   const int32_t* expert_off;
   int expert_tiles;
   int expert_rows;
+  // Tail split (tail_z > 1; 1-SM kernel, 1-D grid): CTAs [0, tail_begin)
+  // take whole tiles t = CTA index (row tile t % tiles_x, token tile t /
+  // tiles_x); the last tiles t >= tail_begin, which would run as a thin last
+  // wave, are cut into tail_z K-slices of tail_steps steps, one CTA each.  A
+  // slice writes its partial tile to tail_part [tail tile][slice][BN tokens]
+  // [BM tile rows] for tail_reduce_kernel.
+  int tail_z;
+  int tail_begin;
+  int tail_steps;
+  int tiles_x;
+  float* tail_part;
 };
 
 template <int FMT, int BN, bool SPLIT = false>
@@ -625,28 +636,43 @@ __global__ void __launch_bounds__(kThreads1, 1)
     if (p.n_seg > 2) prefetch_tmap(&tmap_w2);
   }
   if (p.expert_off) grid_dependency_wait();  // the expert offsets come from the previous grid
-  int tok0 = blockIdx.y * BN;
+  // this CTA's row tile, token tile and K-slice
+  int bx = (int)blockIdx.x, by = (int)blockIdx.y, bz = (int)blockIdx.z;
+  int tail = -1;  // tail split: index of this CTA's tail tile
+  if (p.tail_z > 1) {
+    int t = bx;
+    if (t >= p.tail_begin) {
+      const int j = t - p.tail_begin;
+      tail = j / p.tail_z;
+      bz = j - tail * p.tail_z;
+      t = p.tail_begin + tail;
+    }
+    by = t / p.tiles_x;
+    bx = t - by * p.tiles_x;
+  }
+  int tok0 = by * BN;
   int tok_end = p.M;  // activation rows of this tile end here
   // row tile -> matrix and its first row (a gate/up tile covers 64 rows of each)
   int seg = 0;
-  while (seg + 1 < p.n_seg && (int)blockIdx.x >= p.seg_tile0[seg + 1]) ++seg;
+  while (seg + 1 < p.n_seg && bx >= p.seg_tile0[seg + 1]) ++seg;
   const int tile_rows = p.gate_up ? BM / 2 : BM;
-  int row0 = ((int)blockIdx.x - p.seg_tile0[seg]) * tile_rows;
+  int row0 = (bx - p.seg_tile0[seg]) * tile_rows;
   int wrow0 = row0;  // first row in the weight tensor map
   if (p.expert_off) {
-    const int e = (int)blockIdx.x / p.expert_tiles;
+    const int e = bx / p.expert_tiles;
     const int t_end = p.expert_off[e + 1];
-    tok0 = p.expert_off[e] + (int)blockIdx.y * BN;
+    tok0 = p.expert_off[e] + by * BN;
     if (tok0 >= t_end) return;  // nothing allocated or armed yet
     tok_end = t_end;
-    row0 = ((int)blockIdx.x % p.expert_tiles) * tile_rows;
+    row0 = (bx % p.expert_tiles) * tile_rows;
     wrow0 = e * p.expert_rows + row0;
   }
   constexpr int steps_per_w = wcol_for(FMT) / BK;  // p.wcol
   // split-K slice of this CTA: K steps [kbeg, kbeg + nk)
-  const int kbeg = blockIdx.z * p.steps_per_split;
+  const int slice_steps = tail >= 0 ? p.tail_steps : p.steps_per_split;
+  const int kbeg = bz * slice_steps;
   const int nk_all = p.K / BK;
-  const int nk = min(p.steps_per_split, nk_all - kbeg);
+  const int nk = min(slice_steps, nk_all - kbeg);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -830,7 +856,9 @@ __global__ void __launch_bounds__(kThreads1, 1)
         const int cend = min(cbeg + kCols, tok_end - tok0);
         const bool split = p.y != nullptr;
         const int rows_m = p.seg_rows[seg];
-        float* yz = split ? p.y + (size_t)blockIdx.z * p.M * p.N : nullptr;
+        float* yz = split ? p.y + (size_t)bz * p.M * p.N : nullptr;
+        // tail slice: this CTA's partial tile, [BN tokens][BM tile rows]
+        float* tp = tail >= 0 ? p.tail_part + ((size_t)tail * p.tail_z + bz) * BN * BM : nullptr;
 #pragma unroll 1
         for (int c0 = cbeg; c0 < cend; c0 += kBatch) {
           uint32_t v[32];
@@ -858,7 +886,14 @@ __global__ void __launch_bounds__(kThreads1, 1)
             for (int i = 0; i < 16; ++i)
               v[i] = __float_as_uint(__fadd_rn(__uint_as_float(v[i]), __fmul_rn(__uint_as_float(v[16 + i]), kSplitInv)));
           }
-          if (!p.gate_up) {
+          if (tp) {
+            // TMEM lane 32 q + lane is tile row 32 q + lane (gate/up: lanes
+            // 16..31 of each quarter are up rows, kept at tile rows 64..)
+            const int lr = p.gate_up ? 64 * (lane >> 4) + 16 * q + (lane & 15) : 32 * q + lane;
+#pragma unroll
+            for (int i = 0; i < kBatch; ++i)
+              if (tok0 + c0 + i < tok_end) tp[(size_t)(c0 + i) * BM + lr] = __uint_as_float(v[i]);
+          } else if (!p.gate_up) {
             const int row = row0 + 32 * q + lane;
             if (row < rows_m) {
 #pragma unroll
@@ -1434,7 +1469,7 @@ bool use_pair(int64_t N, int64_t M) {
 
 template <int FMT, int BN, bool SPLIT>
 cudaError_t run(const CUtensorMap* tw, const CUtensorMap& tx, const CUtensorMap& txlo, const Params& p, int tiles,
-                int splits, int64_t max_rows, cudaStream_t st) {
+                int splits, int64_t max_rows, cudaStream_t st, int ctas_1d = 0) {
   auto k = gemm_kernel<FMT, BN, SPLIT>;
   static int configured_dev = -1;
   int dev = 0;
@@ -1447,6 +1482,7 @@ cudaError_t run(const CUtensorMap* tw, const CUtensorMap& tx, const CUtensorMap&
   }
   // token tiles: of all M rows, or (expert mode) of the most rows one expert can have
   dim3 grid((unsigned)tiles, (unsigned)((max_rows + BN - 1) / BN), (unsigned)splits);
+  if (ctas_1d > 0) grid = dim3((unsigned)ctas_1d);  // tail split: tiles and tail slices in one dimension
   return launch_ex(k, grid, dim3(kThreads1), (size_t)smem, st, tw[0], tw[1], tw[2], tx, txlo, p);
 }
 
@@ -1522,6 +1558,47 @@ __global__ void __launch_bounds__(256) reduce_splits_kernel(const __grid_constan
   a.ys[m][tok * a.seg_rows[m] + (c - a.seg_col0[m])] = s;
 }
 
+// Tail split: each tail tile's K-slice partials summed in slice order and
+// written as the GEMM epilogue writes a whole tile (gate/up: silu(gate) *
+// up).  Block (x, t): tail tile t, 256 (token, tile column) pairs.
+struct TailArgs {
+  const float* part;  // [tail tiles][z][bn tokens][BM tile rows]
+  int z, bn, begin, tiles_x, M;
+  int gate_up, n_seg, precise;
+  int seg_tile0[4];
+  int seg_rows[3];
+  float* ys[3];
+};
+
+__global__ void __launch_bounds__(256) tail_reduce_kernel(const __grid_constant__ TailArgs a) {
+  grid_dependency_wait();
+  allow_dependents_launch();
+  const int tt = (int)blockIdx.y;
+  const int t = a.begin + tt;
+  const int by = t / a.tiles_x, bx = t - by * a.tiles_x;
+  int seg = 0;
+  while (seg + 1 < a.n_seg && bx >= a.seg_tile0[seg + 1]) ++seg;
+  const int cols = a.gate_up ? BM / 2 : BM;  // output rows of the tile
+  const int i = (int)(blockIdx.x * blockDim.x + threadIdx.x);
+  if (i >= a.bn * cols) return;
+  const int tl = i / cols, c = i - tl * cols;
+  const int tok = by * a.bn + tl;
+  const int rows_m = a.seg_rows[seg];
+  const int row = (bx - a.seg_tile0[seg]) * cols + c;
+  if (tok >= a.M || row >= rows_m) return;
+  const size_t stride = (size_t)a.bn * BM;
+  const float* src = a.part + (size_t)tt * a.z * stride + (size_t)tl * BM + c;
+  float s = src[0];
+  for (int z = 1; z < a.z; ++z) s += src[(size_t)z * stride];
+  if (a.gate_up) {
+    float u = src[BM / 2];
+    for (int z = 1; z < a.z; ++z) u += src[(size_t)z * stride + BM / 2];
+    a.ys[0][(size_t)tok * rows_m + row] = silu_mul(s, u, a.precise);
+    return;
+  }
+  a.ys[seg][(size_t)tok * rows_m + row] = s;
+}
+
 int device_sms() {
   static int sms[64] = {};
   int dev = 0;
@@ -1543,6 +1620,39 @@ int choose_splits(int64_t K, int64_t row_tiles, int64_t M, int wcol, int64_t bn)
   if (z > nwb) z = nwb;
   if (z > 16) z = 16;
   return (int)(z < 1 ? 1 : z);
+}
+
+// Tail split of a grid of at least one wave (fp16 operands, 1-SM kernel):
+// when the tiles past the last full wave fill at most half the SMs, they
+// are cut into K-slices of whole block columns (up to 16) that run side by
+// side in that last wave instead of one tile per SM for a whole tile's
+// time.
+struct TailPlan {
+  int z = 1;      // slices per tail tile (1: no tail split)
+  int begin = 0;  // first tail tile
+  int tiles = 0;  // tail tiles
+  int wb = 0;     // block columns per slice
+};
+
+TailPlan tail_plan(int64_t K, int64_t row_tiles, int64_t M, int wcol, int64_t bn) {
+  TailPlan t;
+  const int64_t tiles = row_tiles * ((M + bn - 1) / bn);
+  const int64_t nwb = K / wcol;
+  const int64_t sms = device_sms();
+  if (tiles < sms || nwb < 2) return t;
+  const int64_t rem = tiles % sms;
+  if (rem == 0 || 2 * rem > sms) return t;
+  int64_t z = sms / rem;
+  if (z > nwb) z = nwb;
+  if (z > 16) z = 16;
+  const int64_t per = (nwb + z - 1) / z;
+  z = (nwb + per - 1) / per;
+  if (z < 2) return t;
+  t.z = (int)z;
+  t.begin = (int)(tiles - rem);
+  t.tiles = (int)rem;
+  t.wb = (int)per;
+  return t;
 }
 
 // Row tiles of a job and the columns of its split-K partials.
@@ -1624,8 +1734,14 @@ size_t gemm_job_workspace_bytes(const GemmJob& j) {
   gemm::Geometry g;
   if (!gemm::job_geometry(j, g)) return 0;
   const gemm::Layout L = gemm::layout_of(j);
-  const int z = j.experts > 0 ? 1 : gemm::choose_splits(j.K, L.tiles, j.M, g.wcol, gemm::job_token_tile(j));
-  return gemm::x_bytes(j.K, j.M, j.split) + (z > 1 ? (size_t)z * j.M * L.ncols * sizeof(float) : 0) + 16;
+  const int bn = gemm::job_token_tile(j);
+  const int z = j.experts > 0 ? 1 : gemm::choose_splits(j.K, L.tiles, j.M, g.wcol, bn);
+  size_t part = z > 1 ? (size_t)z * j.M * L.ncols * sizeof(float) : 0;
+  if (j.experts == 0 && !j.split && z == 1) {
+    const gemm::TailPlan t = gemm::tail_plan(j.K, L.tiles, j.M, g.wcol, bn);
+    if (t.z > 1) part = (size_t)t.tiles * t.z * bn * gemm::BM * sizeof(float);
+  }
+  return gemm::x_bytes(j.K, j.M, j.split) + part + 16;
 }
 
 cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) {
@@ -1722,6 +1838,9 @@ cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) 
   const int splits = (nwb + wb_per_split - 1) / wb_per_split;
   float* partials =
       splits > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + x_bytes(K, M, j.split)) : nullptr;
+  // whole tiles, then the thin last wave cut into K-slices (fp16 operands)
+  const TailPlan tail = (j.experts == 0 && !j.split && !pair && splits == 1)
+                            ? tail_plan(K, lay.tiles, M, g.wcol, bn) : TailPlan{};
   Params p{};
   p.K = (int)K;
   p.N = lay.ncols;
@@ -1742,6 +1861,13 @@ cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) 
     p.ys[m] = m < j.n_mat ? j.y[m] : nullptr;
   }
   p.gate_up = j.gate_up ? 1 : 0;
+  if (tail.z > 1) {
+    p.tail_z = tail.z;
+    p.tail_begin = tail.begin;
+    p.tail_steps = tail.wb * (g.wcol / BK);
+    p.tiles_x = lay.tiles;
+    p.tail_part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + x_bytes(K, M, j.split));
+  }
   if (j.experts > 0) {
     p.expert_off = j.expert_off;
     p.expert_tiles = lay.tiles / j.experts;
@@ -1749,6 +1875,7 @@ cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) 
   }
   const int64_t max_rows = j.experts > 0 ? (j.expert_max_rows < M ? j.expert_max_rows : M) : M;
   cudaError_t e;
+  const int ctas = tail.z > 1 ? tail.begin + tail.tiles * tail.z : 0;
   if (pair) {
     p.N = (int)j.rows[0];
     p.y = splits > 1 ? partials : j.y[0];
@@ -1761,9 +1888,9 @@ cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) 
       e = bn == 128 ? run<F, 128, true>(tw, tx, txlo, p, lay.tiles, splits, max_rows, st)           \
                     : run<F, 64, true>(tw, tx, txlo, p, lay.tiles, splits, max_rows, st);           \
     else                                                                                            \
-      e = bn == 256   ? run<F, 256, false>(tw, tx, txlo, p, lay.tiles, splits, max_rows, st)        \
-          : bn == 128 ? run<F, 128, false>(tw, tx, txlo, p, lay.tiles, splits, max_rows, st)        \
-                      : run<F, 64, false>(tw, tx, txlo, p, lay.tiles, splits, max_rows, st);        \
+      e = bn == 256   ? run<F, 256, false>(tw, tx, txlo, p, lay.tiles, splits, max_rows, st, ctas)  \
+          : bn == 128 ? run<F, 128, false>(tw, tx, txlo, p, lay.tiles, splits, max_rows, st, ctas)  \
+                      : run<F, 64, false>(tw, tx, txlo, p, lay.tiles, splits, max_rows, st, ctas);  \
     break;
       HYQ_RUN(Q4_K)
       HYQ_RUN(Q6_K)
@@ -1774,7 +1901,28 @@ cudaError_t launch_gemm_job(const GemmJob& j, void* workspace, cudaStream_t st) 
       default: return cudaErrorNotSupported;
     }
   }
-  if (e != cudaSuccess || splits == 1) return e;
+  if (e != cudaSuccess) return e;
+  if (tail.z > 1) {
+    TailArgs t{};
+    t.part = p.tail_part;
+    t.z = tail.z;
+    t.bn = bn;
+    t.begin = tail.begin;
+    t.tiles_x = lay.tiles;
+    t.M = (int)M;
+    t.gate_up = p.gate_up;
+    t.n_seg = p.n_seg;
+    t.precise = 0;  // fp16 operands: the epilogue's fast SiLU
+    for (int m = 0; m < 4; ++m) t.seg_tile0[m] = p.seg_tile0[m];
+    for (int m = 0; m < 3; ++m) {
+      t.seg_rows[m] = p.seg_rows[m];
+      t.ys[m] = p.ys[m];
+    }
+    const int per_tile = bn * (j.gate_up ? BM / 2 : BM);
+    return launch_ex(tail_reduce_kernel, dim3((unsigned)((per_tile + 255) / 256), (unsigned)tail.tiles), dim3(256), 0,
+                     st, t);
+  }
+  if (splits == 1) return e;
   ReduceArgs r{};
   r.part = partials;
   r.M = M;

@@ -685,7 +685,8 @@ class DenseBatch:
         if B >= 16:
             # split operands: the norms run in the conversions of QKV,
             # gate/up and lm_head; fp16 operands: a separate norm kernel each
-            g = lambda tiles, K, dt=t: quant.gemm_launches(tiles, K, B, dt, sms)  # noqa: E731
+            split = self.m.precision == quant.GEMM_F32
+            g = lambda tiles, K, dt=t: quant.gemm_launches(tiles, K, B, dt, sms, split=split)  # noqa: E731
             attn = g((cfg.heads * cfg.head_dim + 2 * KV) // 128, cfg.hidden) + g(cfg.hidden // 128, cfg.hidden)
             ffn = g(2 * cfg.ffn // 128, cfg.hidden) + g(cfg.hidden // 128, cfg.ffn)
             lm_head = g(-(-cfg.vocab // 128), cfg.hidden, cfg.embed_dtype)

@@ -430,13 +430,19 @@ del _native
 GEMM_BLOCK_COLUMN = {DType.Q8_0: 128, DType.Q2_0C: 512, DType.Q4_K: 256, DType.Q6_K: 256, DType.STQ1_0: 256}
 
 
-def gemm_splits(row_tiles, K, M, dtype, sms=148):
-    """Split-K slices the tensor-core product takes (hyq_gemm.cu
-    choose_splits): token tiles of 64 / 128 / 256 by batch size; a grid of
-    row tiles x token tiles smaller than the SM count is split into whole
-    block columns, within one wave of CTAs, at most 16 ways."""
+def _token_tile(M, split=False):
+    """hyq_gemm.cu token_tile / job_token_tile: 64 / 128 / 256 tokens by
+    batch size, at most 128 with split operands."""
     bn = 256 if M >= 256 else 128 if M > 64 else 64
-    tiles = row_tiles * -(-M // bn)
+    return min(bn, 128) if split else bn
+
+
+def gemm_splits(row_tiles, K, M, dtype, sms=148, split=False):
+    """Split-K slices the tensor-core product takes (hyq_gemm.cu
+    choose_splits): a grid of row tiles x token tiles smaller than the SM
+    count is split into whole block columns, within one wave of CTAs, at
+    most 16 ways."""
+    tiles = row_tiles * -(-M // _token_tile(M, split))
     nwb = K // GEMM_BLOCK_COLUMN[dtype]
     if tiles >= sms:
         return 1
@@ -445,7 +451,30 @@ def gemm_splits(row_tiles, K, M, dtype, sms=148):
     return -(-nwb // per)
 
 
-def gemm_launches(row_tiles, K, M, dtype, sms=148):
+def gemm_tail_slices(row_tiles, K, M, dtype, sms=148, split=False, pair=False):
+    """K-slices of each tile of the thin last wave (hyq_gemm.cu tail_plan),
+    1 when the product takes no tail split: fp16 operands on the 1-SM
+    kernel, a grid of at least one wave whose tiles past the last full wave
+    fill at most half the SMs, cut into whole block columns, at most 16."""
+    if split or pair:
+        return 1
+    tiles = row_tiles * -(-M // _token_tile(M))
+    nwb = K // GEMM_BLOCK_COLUMN[dtype]
+    if tiles < sms or nwb < 2:
+        return 1
+    rem = tiles % sms
+    if rem == 0 or 2 * rem > sms:
+        return 1
+    z = min(sms // rem, nwb, 16)
+    per = -(-nwb // z)
+    z = -(-nwb // per)
+    return z if z >= 2 else 1
+
+
+def gemm_launches(row_tiles, K, M, dtype, sms=148, split=False, pair=False):
     """Kernel launches of one tensor-core product (batch >= 16): the fp16
-    activation copy, the GEMM, and the split-K reduction when it splits."""
-    return 2 + (1 if gemm_splits(row_tiles, K, M, dtype, sms) > 1 else 0)
+    activation copy, the GEMM, and the split-K or tail reduction when it
+    takes one (`split`: split operands; `pair`: the product runs on the 2-SM
+    kernel, which takes no tail split)."""
+    return (2 + (1 if gemm_splits(row_tiles, K, M, dtype, sms, split) > 1 else 0)
+            + (1 if gemm_tail_slices(row_tiles, K, M, dtype, sms, split, pair) > 1 else 0))

@@ -121,8 +121,43 @@ def test_matmul_qkv_matches_separate_products(cuda, t, K, Nq, Nkv, M):
     assert quant.device_status() == 0
 
 
-@pytest.mark.parametrize("t,N,K,M", [(Q4_K, 14336, 4096, 512), (Q4_K, 1024, 2048, 64), (Q6_K, 768, 1024, 200),
-                                     (Q4_K, 512, 1024, 9)])
+# Tail split (fp16 operands, at least one wave of tiles): the tiles past the
+# last full wave run as K-slices summed by a second kernel.  A partial last
+# row tile and token tile in the tail (Q8_0, 149 tiles at 50 tokens), a whole
+# one (Q4_K at 128 tokens, 150 tiles), both against the f64 oracle.
+TAIL_CASES = [(Q8_0, 148 * 128 + 37, 2048, 50), (Q4_K, 150 * 128, 4096, 128)]
+
+
+@pytest.mark.parametrize("t,N,K,M", TAIL_CASES)
+def test_gemm_tail_split(cuda, t, N, K, M):
+    import torch
+    from hy_mt_rs_b200 import quant
+
+    sms = torch.cuda.get_device_properties(cuda).multi_processor_count
+    assert quant.gemm_tail_slices(-(-N // 128), K, M, t, sms) > 1
+    run_case(cuda, t, N, K, M, seed=N + M)
+
+
+def test_matmul_qkv_tail_split_matches_separate_products(cuda):
+    """A grouped QKV launch whose last tile (the v matrix's) falls past the
+    first wave: it runs as K-slices, and the three outputs still equal three
+    separate products (which take split-K or whole tiles)."""
+    import torch
+    from hy_mt_rs_b200 import quant
+
+    t, K, Nq, Nkv, M = Q4_K, 2048, 133 * 128, 1024, 64
+    assert quant.gemm_tail_slices(Nq // 128 + 2 * Nkv // 128, K, M, t) > 1
+    q, k, v = _w(cuda, t, Nq, K, 1), _w(cuda, t, Nkv, K, 2), _w(cuda, t, Nkv, K, 3)
+    x = torch.randn(M, K, generator=torch.Generator().manual_seed(4)).to(cuda)
+    got = quant.Weight.matmul_qkv(q, k, v, x, M)
+    for w, y in zip((q, k, v), got):
+        ref = w.matmul(x, M)
+        assert _rel(y, ref) < 1e-5, _rel(y, ref)
+    assert quant.device_status() == 0
+
+
+@pytest.mark.parametrize("t,N,K,M", [(Q4_K, 14336, 4096, 512), (Q4_K, 14336, 4096, 2048), (Q4_K, 1024, 2048, 64),
+                                     (Q6_K, 768, 1024, 200), (Q4_K, 512, 1024, 9)])
 def test_gate_up_silu_batch_matches_separate_products(cuda, t, N, K, M):
     """silu(gate) * up from one fused launch equals the reference's batched
     DenseFfn (two products, then the elementwise combination)."""

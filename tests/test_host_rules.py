@@ -4,7 +4,7 @@ launch counts rely on, checked against the grids the ncu launch lists of
 the 64-request decode step and of MoE decode recorded (grid.z = slices)."""
 import pytest
 
-from hy_mt_rs_b200.quant import DType, gemm_launches, gemm_splits
+from hy_mt_rs_b200.quant import DType, gemm_launches, gemm_splits, gemm_tail_slices
 
 Q2C, Q4K, Q6K = DType.Q2_0C, DType.Q4_K, DType.Q6_K
 
@@ -14,7 +14,7 @@ Q2C, Q4K, Q6K = DType.Q2_0C, DType.Q4_K, DType.Q6_K
     (16, 2048, 64, Q2C, 4),     # O: (16, 1, 4)
     (96, 2048, 64, Q2C, 1),     # gate/up pair tiles: (96, 1, 1)
     (16, 6144, 64, Q2C, 6),     # down: (16, 1, 6)
-    (944, 2048, 64, Q6K, 1),    # lm_head: (944, 1, 1)
+    (944, 2048, 64, Q6K, 1),    # lm_head, split operands: (944, 1, 1)
     (16, 2048, 64, Q4K, 8),     # MoE shared gate/up at 64 tokens: (16, 1, 8)
     (16, 1024, 64, Q4K, 4),     # MoE shared down: (16, 1, 4)
     (48, 4096, 2048, Q4K, 1),   # 7B QKV at 2048 tokens: 384 tiles, no split
@@ -22,7 +22,43 @@ Q2C, Q4K, Q6K = DType.Q2_0C, DType.Q4_K, DType.Q6_K
 ])
 def test_gemm_splits_match_recorded_grids(tiles, K, M, dtype, splits):
     assert gemm_splits(tiles, K, M, dtype) == splits
-    assert gemm_launches(tiles, K, M, dtype) == 2 + (splits > 1)
+    if M <= 128:  # split operands take the same token tile here
+        assert gemm_splits(tiles, K, M, dtype, split=True) == splits
+        assert gemm_launches(tiles, K, M, dtype, split=True) == 2 + (splits > 1)
+    tail = gemm_tail_slices(tiles, K, M, dtype) > 1  # fp16 lm_head at 64 rows: its last wave is split
+    assert gemm_launches(tiles, K, M, dtype) == 2 + (splits > 1) + tail
+
+
+@pytest.mark.parametrize("tiles,K,M,dtype,z", [
+    (224, 4096, 512, Q4K, 16),   # 7B gate/up at 512 tokens: 448 tiles, 4 past three waves, 16 slices each
+    (224, 4096, 2048, Q4K, 8),   # 7B gate/up at 2048: 1792 tiles, 16 past twelve waves, 9 -> 8 whole slices
+    (48, 4096, 2048, Q4K, 1),    # 7B QKV at 2048: 88 tiles past two waves (more than half): whole tiles
+    (224, 4096, 128, Q4K, 1),    # 7B gate/up at 128: 76 past one wave
+    (944, 2048, 64, Q6K, 2),     # lm_head at 64 rows, fp16 operands: 56 past six waves
+    (96, 2048, 64, Q2C, 1),      # under one wave: split-K instead
+])
+def test_tail_split_rule(tiles, K, M, dtype, z):
+    assert gemm_tail_slices(tiles, K, M, dtype) == z
+    assert gemm_tail_slices(tiles, K, M, dtype, split=True) == 1
+    assert gemm_tail_slices(tiles, K, M, dtype, pair=True) == 1
+    assert gemm_launches(tiles, K, M, dtype) == 2 + (gemm_splits(tiles, K, M, dtype) > 1) + (z > 1)
+
+
+def test_tail_slices_fit_the_last_wave():
+    """The tail's slices never need more than the SMs left idle by the last
+    full wave, each slice is whole block columns, and there are at least two."""
+    for tiles in range(148, 2000, 7):
+        for K, dtype in ((2048, Q2C), (4096, Q4K), (14336, Q6K), (2048, Q6K)):
+            for M in (64, 128, 512):
+                bn = 256 if M >= 256 else 128 if M > 64 else 64
+                row_tiles = -(-tiles // -(-M // bn))
+                z = gemm_tail_slices(row_tiles, K, M, dtype)
+                grid = row_tiles * -(-M // bn)
+                rem = grid % 148
+                nwb = K // {Q2C: 512, Q4K: 256, Q6K: 256}[dtype]
+                if z > 1:
+                    assert 0 < rem <= 74 and rem * z <= 148 and z <= min(nwb, 16)
+                    assert (nwb + z - 1) // z * (z - 1) < nwb  # every slice has a block column
 
 
 def test_split_grid_stays_within_one_wave():
