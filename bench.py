@@ -60,6 +60,9 @@ def args_parse():
                     help="tp: batch-1 layer chain (decode) or the layer's GEMMs at --tokens (prefill)")
     ap.add_argument("--tp-allreduce", choices=["peer", "nccl"], default="peer",
                     help="tp decode: all-reduce by hyq_peer_allreduce (NVLink peer memory) or NCCL")
+    ap.add_argument("--ep-exchange", choices=["peer", "nccl"], default="peer",
+                    help="moe at N > 1: expert-parallel row exchange by hyq_peer_exchange (NVLink peer memory) "
+                         "or NCCL all-to-all")
     ap.add_argument("--sweep", action="store_true",
                     help="gemv: also measure every packed format at 6144x2048 and 120832x2048, both paths")
     ap.add_argument("--tokens", type=int, default=512, help="prefill: tokens M")
@@ -1437,8 +1440,13 @@ def moe_arm(a):
 
     cfg = MoeConfig()
     weights = random_moe_weights(cfg, dev, seed=3)
-    # N > 1: expert parallelism (each rank E / N experts and its own tokens, NCCL all-to-all)
-    layer = MoeLayer(cfg, weights, ep=(rank, world, None) if world > 1 else None)
+    # N > 1: expert parallelism (each rank E / N experts and its own tokens), rows
+    # exchanged through NVLink peer memory (hyq_peer_exchange) or NCCL all-to-all
+    xchg = None
+    if world > 1 and getattr(a, "ep_exchange", "peer") == "peer":
+        from hy_mt_rs_b200.peer import PeerExchange
+        xchg = PeerExchange((MOE_PREFILL_TOKENS * cfg.used + 1) * cfg.hidden, device=dev)
+    layer = MoeLayer(cfg, weights, ep=(rank, world, None) if world > 1 else None, exchange=xchg)
     H, E, M, S, U = cfg.hidden, cfg.experts, cfg.mid, cfg.shared_mid, cfg.used
     expert_bytes = 3 * M * row_bytes(cfg.dtype, H)  # gate + up + down of one expert (same byte count)
     shared_bytes = 3 * S * row_bytes(cfg.dtype, H)
@@ -1495,6 +1503,8 @@ def moe_arm(a):
     failed = device_failed(quant, dev)
     (ms_dec, ms_pre, failed), clocks_all = reduce_over_ranks(
         [res[MOE_DECODE_TOKENS]["ms"], res[MOE_PREFILL_TOKENS]["ms"], failed + 0.0], sampler.summary(), dev)
+    if xchg is not None:
+        xchg.close()  # every rank, after the graphs that use the regions are gone
     if failed:
         raise RuntimeError("a kernel reported an expired bounded wait (device status word) on some rank")
     launches = layer.launches(MOE_DECODE_TOKENS) * a.steps
@@ -1530,7 +1540,9 @@ def moe_arm(a):
         "config": {"workload": "hy-mt-rs config 5: one MoE FFN (router, sigmoid top-8 routing, 64 experts "
                                "2048->1024->2048 SwiGLU Q4_K, shared expert 2048->1024->2048), batch 64",
                    "experts": E, "used": U,
-                   "parallelism": f"expert parallel x{world} (NCCL all-to-all)" if world > 1 else "1 GPU",
+                   "parallelism": (f"expert parallel x{world} ("
+                                   + ("NVLink peer-memory exchange" if xchg is not None else "NCCL all-to-all") + ")")
+                                  if world > 1 else "1 GPU",
                    "l2": "L2 flushed between timed steps (256 MB written outside the timed events)",
                    "step": "one CUDA graph of the layer" if graphed.get(MOE_DECODE_TOKENS) else "eager calls"},
         "prefill": {"tokens": MOE_PREFILL_TOKENS, "ms_per_step": round(ms_pre, 4),

@@ -137,6 +137,8 @@ _SIGS = {
     "hyq_peer_close": ([_vp], C.c_int),
     "hyq_peer_free": ([_vp], C.c_int),
     "hyq_peer_allreduce": ([C.POINTER(C.c_uint64), C.c_int, C.c_int, _i64, _vp, _vp], C.c_int),
+    "hyq_peer_exchange": ([C.POINTER(C.c_uint64), C.c_int, C.c_int, C.c_size_t, _vp, C.c_int, C.c_int, _vp, C.c_int,
+                           _i64, _vp], C.c_int),
     "hyq_device_status": ([_vp, C.POINTER(C.c_uint32)], C.c_int),
 }
 

@@ -124,22 +124,63 @@ def ep_recv_perm(counts, cap):
     return torch.where(valid, perm, torch.zeros_like(perm)), valid, off
 
 
+def ep_pack(x, rows, per_expert, world, local_experts, cap):
+    """Expert parallelism, sending side: the send buffer of one all-to-all
+    that carries, for each destination rank r, its cap rows (rows[r * cap ..],
+    token rows of x) followed by one row whose first local_experts floats
+    hold the int32 bit patterns of r's experts' row counts
+    (per_expert[r El .. (r + 1) El]).  [world * (cap + 1), hidden]."""
+    hidden = x.shape[1]
+    if hidden < local_experts:
+        raise ValueError("expert parallelism: hidden size below the experts per rank")
+    ext = torch.cat([rows.view(world, cap), rows.new_zeros(world, 1)], 1).reshape(-1)
+    send = x.index_select(0, ext)
+    counts = per_expert.to(torch.int32).view(world, local_experts).view(torch.float32)
+    send.view(world, cap + 1, hidden)[:, cap, :local_experts] = counts
+    return send
+
+
+def ep_unpack_counts(recv, world, local_experts, cap, stride=None):
+    """Receiving side of ep_pack: counts [world, local experts] (int64) of
+    the rows each source sent for this rank's experts.  Source s's block
+    starts at row s * stride (cap + 1 by default: blocks back to back)."""
+    hidden = recv.shape[1]
+    stride = cap + 1 if stride is None else stride
+    c = recv.view(world, stride, hidden)[:, cap, :local_experts].contiguous()
+    return c.view(torch.int32).long()
+
+
+def ep_packed_rows(perm, cap, stride=None):
+    """Received row s * cap + i of the unpacked layout sits at row
+    s * stride + i of a layout whose source blocks start `stride` rows apart
+    (ep_pack's: cap + 1, one count row per block)."""
+    stride = cap + 1 if stride is None else stride
+    return (perm // cap) * stride + perm % cap
+
+
 class MoeLayer:
     """Moe::forward for `tokens` rows of normalized activations.
 
     ep = (rank, world, process_group): expert parallelism over `world`
     ranks (one per GPU); this rank holds experts [rank * E / world, (rank +
     1) * E / world) and its own tokens.  Token rows travel to the rank of
-    each chosen expert and back by NCCL all-to-all; routing, shared expert
-    and combine stay local, so the result equals the one-GPU layer.  The
-    exchange has a fixed capacity (tokens * used rows per destination, the
-    most a rank can send) and carries the per-expert counts in-band, so no
-    count reaches the host and the layer can be captured in a CUDA graph."""
+    each chosen expert and back by NCCL all-to-all, or, with `exchange` (a
+    hy_mt_rs_b200.peer.PeerExchange), by pushes into the other ranks'
+    NVLink peer-memory regions (only the valid rows travel); routing, shared
+    expert and combine stay local, so the result equals the one-GPU layer.
+    The exchange has a fixed capacity (tokens * used rows per destination,
+    the most a rank can send) and carries the per-expert counts in-band, so
+    no count reaches the host and the layer can be captured in a CUDA graph.
+    Every rank passes the same token count."""
 
-    def __init__(self, cfg, weights, ep=None):
+    def __init__(self, cfg, weights, ep=None, exchange=None):
         self.cfg = cfg
         H, E, M, S, t = cfg.hidden, cfg.experts, cfg.mid, cfg.shared_mid, cfg.dtype
         self.ep = ep
+        # expert parallelism over NVLink peer memory instead of NCCL: a
+        # hy_mt_rs_b200.peer.PeerExchange whose slots hold (tokens * used +
+        # 1) x hidden floats for the largest token count the layer will see
+        self.xchg = exchange
         self.router = quant.Weight(weights["router"], quant.DType.F32, [H, E], name="ffn_gate_inp")
         self.bias = weights["bias"]
         gate, up, down, El = weights["gate"], weights["up"], weights["down"], E
@@ -218,9 +259,10 @@ class MoeLayer:
     def _experts_ep(self, x, b, st):
         """The expert products of this rank's tokens under expert
         parallelism: b["y"] gets the same rows, in the same grouped order, as
-        the one-GPU products would.  Three NCCL all-to-alls of equal splits:
-        per-expert counts, then cap = tokens * used rows to every rank (the
-        rows for its experts, padded), then the results back."""
+        the one-GPU products would.  Two NCCL all-to-alls of equal splits:
+        cap = tokens * used rows to every rank (the rows for its experts,
+        padded) with the per-expert counts in one extra row per block
+        (ep_pack), then the results back."""
         import torch.distributed as dist
 
         rank, world, group = self.ep
@@ -230,15 +272,25 @@ class MoeLayer:
         dev = x.device
         off = b["off"]
         per_expert = off[1:] - off[:-1]                        # [E] rows per expert, this rank's tokens
-        recv_cnt = torch.empty(world * El, dtype=per_expert.dtype, device=dev)
-        dist.all_to_all_single(recv_cnt, per_expert, group=group)
         send_idx, send_valid = ep_send_index(off, world, El, cap)
         rows = b["row_token"].long()[send_idx.reshape(-1)]
-        send = x.index_select(0, rows)                         # [world * cap, hidden]
-        recv = torch.empty(world * cap, c.hidden, device=dev)
-        dist.all_to_all_single(recv, send, group=group)
-        perm, valid, loff = ep_recv_perm(recv_cnt.view(world, El), cap)
-        perm_d, off_d = perm.to(torch.int32), loff.to(torch.int32)
+        send = ep_pack(x, rows, per_expert, world, El, cap)    # [world * (cap + 1), hidden]
+        if self.xchg is not None:
+            # peer memory: only each block's valid rows and its count row
+            # cross NVLink, into the destination's region (slot = this rank)
+            X = self.xchg
+            stride = X.slot // c.hidden
+            if stride < cap + 1 or stride * c.hidden != X.slot:
+                raise ValueError("expert parallelism: the exchange's slots are too small for this token count")
+            X.exchange(send, cap + 1, send_valid.sum(1).to(torch.int32), last_row=True)
+            recv = X.recv(stride, c.hidden)
+        else:
+            stride = cap + 1
+            recv = torch.empty(world * stride, c.hidden, device=dev)
+            dist.all_to_all_single(recv, send, group=group)
+        counts = ep_unpack_counts(recv, world, El, cap, stride)
+        perm, valid, loff = ep_recv_perm(counts, cap)
+        perm_d, off_d = ep_packed_rows(perm, cap, stride).to(torch.int32), loff.to(torch.int32)
         Rr = world * cap
         h = torch.empty(Rr, c.mid, device=dev)
         y = torch.empty(Rr, c.hidden, device=dev)
@@ -249,13 +301,19 @@ class MoeLayer:
         # back into received order (padding rows go to a spare row), then home
         yr = torch.empty(Rr + 1, c.hidden, device=dev)
         yr.index_copy_(0, torch.where(valid, perm, torch.full_like(perm, Rr)), y)
-        back = torch.empty(Rr, c.hidden, device=dev)
-        dist.all_to_all_single(back, yr[:Rr], group=group)
+        if self.xchg is not None:
+            # each source gets back as many rows as it sent here
+            self.xchg.exchange(yr[:Rr], cap, counts.sum(1).to(torch.int32))
+            back = self.xchg.recv(stride, c.hidden).view(world, stride, c.hidden)[:, :cap].reshape(Rr, c.hidden)
+        else:
+            back = torch.empty(Rr, c.hidden, device=dev)
+            dist.all_to_all_single(back, yr[:Rr], group=group)
         R = T * c.used
         dest = torch.where(send_valid, send_idx, torch.full_like(send_idx, R)).reshape(-1)
         b["y"].index_copy_(0, dest, back)
 
     def launches(self, tokens):
-        """Kernel launches of one forward (for the bench's count)."""
-        # router, route, group, 2 x (conversion + expert GEMM), shared FFN, combine
-        return 3 + 4 + (2 if tokens == 1 else 4) + 1
+        """Kernel launches of the library in one forward (for the bench's
+        count): router, route, group, 2 x (conversion + expert GEMM), shared
+        FFN, combine; with the peer-memory exchange its 2 x 2 launches."""
+        return 3 + 4 + (2 if tokens == 1 else 4) + 1 + (4 if self.xchg is not None else 0)

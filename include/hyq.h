@@ -568,6 +568,24 @@ int hyq_peer_open(const void* ipc_handle, void** region);
 int hyq_peer_close(void* region);
 int hyq_peer_free(void* region);
 int hyq_peer_allreduce(const uint64_t* regions, int rank, int world, int64_t n, float* out, void* stream);
+/* Expert-parallel row exchange over the same kind of regions (no
+ * counterpart in the reference; it replaces the NCCL all-to-all of the
+ * expert-parallel MoE layer).  send = [world][rows][row_floats] floats, block
+ * q for rank q; rows [0, valid[q]) of block q (all rows when valid is NULL)
+ * and, with last_row, the block's last row are stored into rank q's region
+ * at HYQ_PEER_DATA_OFFSET + 4 * rank * slot_floats bytes, at the same row
+ * offsets.  When the call has completed on the stream, this rank's region
+ * holds every source's block (source s at slot s).  region_data_bytes = the
+ * data_bytes every rank passed to hyq_peer_alloc, at least world *
+ * slot_floats * 4; slot_floats >= rows * row_floats.  Two launches: the
+ * first waits (bounded, as hyq_peer_allreduce) until every rank has reached
+ * the same call, so no rank overwrites data a peer has not consumed; the
+ * second pushes and waits for every peer's push.  Use its own regions (not
+ * shared with hyq_peer_allreduce); every rank makes the same calls in the
+ * same order; after HYQ_DEV_TIMEOUT_PEER the regions must be re-created. */
+int hyq_peer_exchange(const uint64_t* regions, int rank, int world, size_t region_data_bytes, const float* send,
+                      int rows, int row_floats, const int32_t* valid, int last_row, int64_t slot_floats,
+                      void* stream);
 /* How long hyq_peer_allreduce waits for the other ranks' flags before it
  * gives up with HYQ_DEV_TIMEOUT_PEER: 1 .. 600000 ms, 5000 by default;
  * process-wide, read when a call is issued. */

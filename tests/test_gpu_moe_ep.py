@@ -1,6 +1,7 @@
 """GPU check of expert parallelism for the MoE layer (MoeLayer with ep=...)
 on two GPUs: each rank holds half of the experts and its own tokens; token
-rows travel to the expert's rank and back by NCCL all-to-all.  Every
+rows travel to the expert's rank and back by NCCL all-to-all or, with a
+PeerExchange, by pushes into the other rank's peer-memory region.  Every
 expert output row is computed as on one GPU, so each rank's layer output
 equals the one-GPU layer on the same tokens bit for bit.  Each rank is a
 child process on its own GPU; NVLS is off.  Skipped with fewer than two
@@ -23,7 +24,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, q):
+def _rank_main(rank, world, port, q, peer=False):
     sys.path.insert(0, ROOT)
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -36,13 +37,19 @@ def _rank_main(rank, world, port, q):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
     from hy_mt_rs_b200 import quant
     from hy_mt_rs_b200.moe import MoeConfig, MoeLayer, random_moe_weights
+    from hy_mt_rs_b200.peer import PeerExchange
 
     ok = True
+    xchgs = []
     for T, cfg in ((37, MoeConfig(hidden=512, experts=8, used=2, mid=256, shared_mid=256)),
                    (64, MoeConfig(hidden=2048, experts=16, used=4, mid=1024, shared_mid=1024))):
         w = random_moe_weights(cfg, dev, seed=11)
         full = MoeLayer(cfg, w)
-        ep = MoeLayer(cfg, w, ep=(rank, world, None))
+        # the peer slots are sized for more tokens than this call has
+        xchg = PeerExchange((2 * T * cfg.used + 1) * cfg.hidden, device=dev) if peer else None
+        if xchg is not None:
+            xchgs.append(xchg)
+        ep = MoeLayer(cfg, w, ep=(rank, world, None), exchange=xchg)
         x = torch.randn(T, cfg.hidden, generator=torch.Generator().manual_seed(100 + rank)).to(dev)
         ref = full.forward(x, T).clone()
         for _ in range(2):
@@ -50,12 +57,15 @@ def _rank_main(rank, world, port, q):
             ok &= torch.equal(got, ref)
         torch.cuda.synchronize(dev)
     ok &= quant.device_status(dev) == 0
+    for xchg in xchgs:
+        xchg.close()
     q.put((rank, bool(ok)))
     dist.barrier()
     dist.destroy_process_group()
 
 
-def test_moe_expert_parallel_two_gpus():
+@pytest.mark.parametrize("peer", [False, True])
+def test_moe_expert_parallel_two_gpus(peer):
     import torch
     import torch.multiprocessing as mp
 
@@ -64,7 +74,7 @@ def test_moe_expert_parallel_two_gpus():
     world, port = 2, _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q, peer)) for r in range(world)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=240) for _ in range(world))

@@ -150,3 +150,78 @@ def test_ep_device_index_math_round_trip():
         out = torch.full((cap + 1,), -1.0)
         out.index_copy_(0, torch.where(valid, idx, torch.full_like(idx, cap)).reshape(-1), backs[s].reshape(-1))
         assert out[:cap].tolist() == [1000.0 * s + g for g in range(cap)]
+
+
+def test_ep_counts_travel_with_the_rows():
+    """The expert-parallel send buffer carries each destination's per-expert
+    counts in one extra row per block (hy_mt_rs_b200.moe ep_pack), so one
+    all-to-all replaces two: simulated on the CPU for 3 ranks, every
+    receiver recovers the counts bit for bit, and the packed row indices
+    (ep_packed_rows) reach the same token rows as the unpacked layout."""
+    import numpy as np
+    import torch
+
+    from hy_mt_rs_b200.moe import ep_pack, ep_packed_rows, ep_recv_perm, ep_send_index, ep_unpack_counts
+
+    W, El, T, used, hidden = 3, 4, 5, 2, 8
+    E, cap = W * El, T * used
+    rng = np.random.default_rng(11)
+    counts_src = [rng.multinomial(cap, [1.0 / E] * E) for _ in range(W)]
+    xs = [torch.randn(T, hidden, generator=torch.Generator().manual_seed(s)) for s in range(W)]
+    sends, plain = [], []
+    for s in range(W):
+        off = torch.tensor(np.concatenate([[0], np.cumsum(counts_src[s])]), dtype=torch.int32)
+        per_expert = off[1:] - off[:-1]
+        idx, _ = ep_send_index(off, W, El, cap)
+        rows = (idx.reshape(-1) % T).long()       # grouped row -> token row (any map will do here)
+        packed = ep_pack(xs[s], rows, per_expert, W, El, cap)
+        assert packed.shape == (W * (cap + 1), hidden)
+        sends.append(packed.view(W, cap + 1, hidden))
+        plain.append(xs[s].index_select(0, rows).view(W, cap, hidden))
+    for r in range(W):
+        recv = torch.cat([sends[s][r] for s in range(W)])             # block s = what s sent to r
+        counts = ep_unpack_counts(recv, W, El, cap)
+        want = np.stack([counts_src[s][r * El:(r + 1) * El] for s in range(W)])
+        assert counts.tolist() == want.tolist()
+        perm, valid, _ = ep_recv_perm(counts, cap)
+        unpacked = torch.cat([plain[s][r] for s in range(W)])         # the two-all-to-all layout
+        assert torch.equal(recv[ep_packed_rows(perm, cap)][valid], unpacked[perm][valid])
+
+
+def test_ep_peer_slot_layout():
+    """The peer-memory exchange (hy_mt_rs_b200.peer.PeerExchange) leaves
+    source s's block at row s * stride of the receiver's region, with only
+    its valid rows and its count row written (the rest is whatever an
+    earlier exchange left): simulated on the CPU for 3 ranks with a slot
+    wider than one block, the counts and the packed row indices still reach
+    the right rows."""
+    import numpy as np
+    import torch
+
+    from hy_mt_rs_b200.moe import ep_pack, ep_packed_rows, ep_recv_perm, ep_send_index, ep_unpack_counts
+
+    W, El, T, used, hidden = 3, 2, 4, 2, 4
+    E, cap = W * El, T * used
+    stride = cap + 1 + 3
+    rng = np.random.default_rng(5)
+    counts_src = [rng.multinomial(cap, [1.0 / E] * E) for _ in range(W)]
+    regions = [torch.full((W * stride, hidden), float("nan")) for _ in range(W)]
+    plain = []
+    for s in range(W):
+        off = torch.tensor(np.concatenate([[0], np.cumsum(counts_src[s])]), dtype=torch.int32)
+        idx, valid = ep_send_index(off, W, El, cap)
+        rows = (idx.reshape(-1) % T).long()
+        x = torch.randn(T, hidden, generator=torch.Generator().manual_seed(10 + s))
+        send = ep_pack(x, rows, off[1:] - off[:-1], W, El, cap).view(W, cap + 1, hidden)
+        n = valid.sum(1)
+        for q in range(W):   # what the push kernel writes into q's region, slot s
+            regions[q][s * stride:s * stride + int(n[q])] = send[q, :int(n[q])]
+            regions[q][s * stride + cap] = send[q, cap]
+        plain.append(x.index_select(0, rows).view(W, cap, hidden))
+    for r in range(W):
+        counts = ep_unpack_counts(regions[r], W, El, cap, stride)
+        assert counts.tolist() == np.stack([counts_src[s][r * El:(r + 1) * El] for s in range(W)]).tolist()
+        perm, valid, _ = ep_recv_perm(counts, cap)
+        unpacked = torch.cat([plain[s][r] for s in range(W)])
+        got = regions[r][ep_packed_rows(perm, cap, stride)][valid]
+        assert torch.equal(got, unpacked[perm][valid])
