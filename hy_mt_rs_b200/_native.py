@@ -139,6 +139,14 @@ _SIGS = {
     "hyq_peer_allreduce": ([C.POINTER(C.c_uint64), C.c_int, C.c_int, _i64, _vp, _vp], C.c_int),
     "hyq_peer_exchange": ([C.POINTER(C.c_uint64), C.c_int, C.c_int, C.c_size_t, _vp, C.c_int, C.c_int, _vp, C.c_int,
                            _i64, _vp], C.c_int),
+    "hyq_moe_ep_dispatch": ([C.POINTER(C.c_uint64), C.c_int, C.c_int, C.c_size_t, _i64, _vp, C.c_int, C.c_int, _vp,
+                             _vp, C.c_int, C.c_int, _vp], C.c_int),
+    "hyq_moe_ep_plan": ([C.POINTER(C.c_uint64), C.c_int, C.c_int, C.c_size_t, _i64, C.c_int, C.c_int, C.c_int, _vp,
+                         _vp, _vp, _vp, _vp], C.c_int),
+    "hyq_moe_ep_return": ([C.POINTER(C.c_uint64), C.c_int, C.c_int, C.c_size_t, _i64, _vp, C.c_int, _vp, _vp,
+                           C.c_int, _vp], C.c_int),
+    "hyq_moe_ep_home": ([C.POINTER(C.c_uint64), C.c_int, C.c_int, C.c_size_t, _i64, C.c_int, _vp, C.c_int, C.c_int,
+                         _vp, _vp], C.c_int),
     "hyq_device_status": ([_vp, C.POINTER(C.c_uint32)], C.c_int),
 }
 

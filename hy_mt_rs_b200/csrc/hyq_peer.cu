@@ -161,6 +161,20 @@ struct XchgArgs {
   int64_t slot;          // floats between slots of a region's data area
   unsigned* status;
   uint64_t wait_ns;
+  // Row sources other than a packed send buffer (mode):
+  //   0: block q row i = send[(q rows + i)];
+  //   1 (expert dispatch): block q holds this rank's grouped rows for q's
+  //     experts, off[q El] .. off[(q + 1) El], row i = send[row_token[off[q
+  //     El] + i]] (send = the layer's token rows, `src_rows` of them), and
+  //     its last row starts with the int32 bit patterns of q's experts' row
+  //     counts;
+  //   2 (expert return): block q row i = send[gather[q (rows) + i]] for i <
+  //     valid[q] (send = the expert outputs, `src_rows` of them).
+  int mode;
+  const int32_t* off;
+  const int32_t* gather;  // mode 1: row_token; mode 2: inverse permutation
+  int el;                 // experts per rank (mode 1)
+  int src_rows;
 };
 
 __global__ void peer_xchg_open_kernel(const __grid_constant__ XchgArgs a) {
@@ -182,15 +196,33 @@ __global__ void __launch_bounds__(512) peer_xchg_push_kernel(const __grid_consta
   const unsigned e = *reinterpret_cast<volatile unsigned*>(mine + 512) + 1;
   const int q = (int)blockIdx.y;
   if (!aborted) {
-    int n = a.valid ? a.valid[q] : a.rows;
-    n = n < 0 ? 0 : (n > a.rows ? a.rows : n);
-    const float* src = a.send + (size_t)q * a.rows * a.row_floats;
     float* dst = reinterpret_cast<float*>(a.region[q] + kPeerDataOffset) + (size_t)a.rank * a.slot;
-    const bool v4 = (a.row_floats & 3) == 0 && ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst) |
+    int n, g0 = 0;
+    if (a.mode == 1) {
+      // grouped rows of q's experts, then (first CTA) the count row
+      g0 = a.off[q * a.el];
+      n = a.off[(q + 1) * a.el] - g0;
+      if (blockIdx.x == 0)
+        for (int e = threadIdx.x; e < a.el; e += blockDim.x)
+          reinterpret_cast<int32_t*>(dst + (size_t)(a.rows - 1) * a.row_floats)[e] =
+              a.off[q * a.el + e + 1] - a.off[q * a.el + e];
+    } else {
+      n = a.valid ? a.valid[q] : a.rows;
+    }
+    const int cap_rows = a.mode == 1 ? a.rows - 1 : a.rows;
+    n = n < 0 ? 0 : (n > cap_rows ? cap_rows : n);
+    const float* src = a.send + (a.mode == 0 ? (size_t)q * a.rows * a.row_floats : 0);
+    const bool v4 = (a.row_floats & 3) == 0 && ((reinterpret_cast<uintptr_t>(a.send) | reinterpret_cast<uintptr_t>(dst) |
                                                  (uintptr_t)(a.slot * 4)) & 15) == 0;
-    for (int r = (int)blockIdx.x; r < n + (a.last_row && n < a.rows ? 1 : 0); r += (int)gridDim.x) {
+    const bool extra = a.mode == 0 && a.last_row && n < a.rows;
+    for (int r = (int)blockIdx.x; r < n + (extra ? 1 : 0); r += (int)gridDim.x) {
       const int row = r < n ? r : a.rows - 1;  // the block's last row, after the valid ones
-      const float* s = src + (size_t)row * a.row_floats;
+      int sr = row;  // source row
+      if (a.mode != 0) {
+        sr = a.mode == 1 ? a.gather[g0 + row] : a.gather[(size_t)q * a.rows + row];
+        sr = sr < 0 ? 0 : (sr >= a.src_rows ? a.src_rows - 1 : sr);
+      }
+      const float* s = src + (size_t)sr * a.row_floats;
       float* d = dst + (size_t)row * a.row_floats;
       if (v4) {
         for (int i = threadIdx.x; i < a.row_floats / 4; i += blockDim.x)
@@ -217,6 +249,146 @@ __global__ void __launch_bounds__(512) peer_xchg_push_kernel(const __grid_consta
       atomicOr(a.status, DEV_TIMEOUT_PEER);
   }
   *reinterpret_cast<volatile unsigned*>(mine + 512) = e;
+}
+
+// Receive side of the expert exchange, one CTA: from the count rows the
+// sources left in this rank's region (source s's block at row s * stride,
+// its count row at row cap), the expert-major gather index of the expert
+// products, the local experts' row offsets, the inverse (expert-major row of
+// each received row, for the return) and the rows received from each source.
+constexpr int kPlanMax = 1024;  // world x experts per rank
+struct PlanArgs {
+  const float* data;  // this rank's region data
+  int world, el, cap, hidden;
+  int64_t slot;
+  int32_t* perm;      // [world cap]
+  int32_t* off;       // [el + 1]
+  int32_t* inv;       // [world cap]
+  int32_t* back;      // [world]
+};
+
+__global__ void __launch_bounds__(1024) moe_ep_plan_kernel(const __grid_constant__ PlanArgs a) {
+  __shared__ int cnt[kPlanMax];   // [s][e]
+  __shared__ int src0[kPlanMax];  // first row of (s, e) in source s's block
+  __shared__ int base[kPlanMax];  // first expert-major row of (e, s), in (e, s) order
+  __shared__ int total_s;
+  const int W = a.world, El = a.el, n = W * El;
+  const int64_t stride = a.slot / a.hidden;
+  for (int k = threadIdx.x; k < n; k += blockDim.x) {
+    const int s = k / El, e = k - s * El;
+    const int32_t* row = reinterpret_cast<const int32_t*>(a.data + (size_t)s * a.slot + (size_t)a.cap * a.hidden);
+    const int c = row[e];
+    cnt[k] = c < 0 ? 0 : (c > a.cap ? a.cap : c);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < W; ++s) {
+      int acc = 0;
+      for (int e = 0; e < El; ++e) {
+        // a source never sends more than cap rows in all
+        const int c = acc + cnt[s * El + e] > a.cap ? a.cap - acc : cnt[s * El + e];
+        cnt[s * El + e] = c;
+        src0[s * El + e] = acc;
+        acc += c;
+      }
+      a.back[s] = acc;
+    }
+    int t = 0;
+    for (int e = 0; e < El; ++e) {
+      a.off[e] = t;
+      for (int s = 0; s < W; ++s) {
+        base[e * W + s] = t;
+        t += cnt[s * El + e];
+      }
+    }
+    a.off[El] = t;
+    total_s = t;
+  }
+  __syncthreads();
+  const int total = total_s, R = W * a.cap;
+  for (int t = threadIdx.x; t < R; t += blockDim.x) {
+    if (t >= total) {
+      a.perm[t] = 0;
+      continue;
+    }
+    int lo = 0, hi = n - 1;  // last (e, s) whose base <= t
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (base[mid] <= t) lo = mid;
+      else hi = mid - 1;
+    }
+    while (lo + 1 < n && base[lo + 1] <= t) ++lo;  // skip empty runs that share a base
+    const int e = lo / W, s = lo - e * W;
+    const int i = src0[s * El + e] + (t - base[lo]);
+    a.perm[t] = (int32_t)(s * stride + i);
+    a.inv[s * a.cap + i] = t;
+  }
+}
+
+// The returned rows home: the rows this rank sent to rank q come back into
+// its region at slot q, row i = grouped row off[q El] + i of `out`.
+struct HomeArgs {
+  const float* data;
+  const int32_t* off;
+  int world, el, cap, hidden;
+  int64_t slot;
+  float* out;
+};
+
+__global__ void __launch_bounds__(512) moe_ep_home_kernel(const __grid_constant__ HomeArgs a) {
+  const int q = (int)blockIdx.y;
+  const int g0 = a.off[q * a.el];
+  int n = a.off[(q + 1) * a.el] - g0;
+  n = n < 0 ? 0 : (n > a.cap ? a.cap : n);
+  const bool v4 = (a.hidden & 3) == 0 && ((reinterpret_cast<uintptr_t>(a.data) | reinterpret_cast<uintptr_t>(a.out) |
+                                           (uintptr_t)(a.slot * 4)) & 15) == 0;
+  for (int r = (int)blockIdx.x; r < n; r += (int)gridDim.x) {
+    const float* s = a.data + (size_t)q * a.slot + (size_t)r * a.hidden;
+    float* d = a.out + (size_t)(g0 + r) * a.hidden;
+    if (v4) {
+      for (int i = threadIdx.x; i < a.hidden / 4; i += blockDim.x)
+        reinterpret_cast<float4*>(d)[i] = reinterpret_cast<const float4*>(s)[i];
+    } else {
+      for (int i = threadIdx.x; i < a.hidden; i += blockDim.x) d[i] = s[i];
+    }
+  }
+}
+
+// Regions, rank and sizes shared by the exchange entry points.
+int xchg_setup(const uint64_t* regions, int rank, int world, size_t region_data_bytes, int64_t slot_floats,
+               int64_t need_floats, const char* what, XchgArgs& a) {
+  if (!regions) return api_fail(HYQ_E_INVALID, "%s: null regions", what);
+  if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world)
+    return api_fail(HYQ_E_INVALID, "%s: rank %d of %d (at most %d ranks)", what, rank, world, kMaxPeers);
+  if (need_floats < 1 || slot_floats < need_floats)
+    return api_fail(HYQ_E_SHAPE, "%s: a block of %lld floats does not fit a slot of %lld floats", what,
+                    (long long)need_floats, (long long)slot_floats);
+  if ((size_t)world * (size_t)slot_floats * sizeof(float) > region_data_bytes)
+    return api_fail(HYQ_E_SHAPE, "%s: %d slots of %lld floats exceed the regions' %zu data bytes", what, world,
+                    (long long)slot_floats, region_data_bytes);
+  a = XchgArgs{};
+  for (int q = 0; q < world; ++q) {
+    if (!regions[q] || (regions[q] & 255)) return api_fail(HYQ_E_ALIGN, "%s: region %d", what, q);
+    a.region[q] = regions[q];
+  }
+  a.rank = rank;
+  a.world = world;
+  a.slot = slot_floats;
+  a.wait_ns = g_peer_wait_ns.load(std::memory_order_relaxed);
+  return api_status_word(&a.status);
+}
+
+int xchg_launch(const XchgArgs& a, void* stream, const char* what) {
+  cudaStream_t st = (cudaStream_t)stream;
+  peer_xchg_open_kernel<<<1, 32, 0, st>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) {
+    const unsigned gx = (unsigned)(a.rows < 64 ? a.rows : 64);
+    peer_xchg_push_kernel<<<dim3(gx, (unsigned)a.world), 512, 0, st>>>(a);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) return api_fail(HYQ_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return HYQ_OK;
 }
 
 }  // namespace
@@ -297,42 +469,111 @@ int hyq_peer_allreduce(const uint64_t* regions, int rank, int world, int64_t n, 
 int hyq_peer_exchange(const uint64_t* regions, int rank, int world, size_t region_data_bytes, const float* send,
                       int rows, int row_floats, const int32_t* valid, int last_row, int64_t slot_floats,
                       void* stream) {
-  if (!regions || !send) return hyq::api_fail(HYQ_E_INVALID, "peer_exchange: null argument");
-  if (world < 1 || world > hyq::kMaxPeers || rank < 0 || rank >= world)
-    return hyq::api_fail(HYQ_E_INVALID, "peer_exchange: rank %d of %d (at most %d ranks)", rank, world,
-                         hyq::kMaxPeers);
-  if (rows < 1 || row_floats < 1 || slot_floats < (int64_t)rows * row_floats)
-    return hyq::api_fail(HYQ_E_SHAPE, "peer_exchange: %d rows of %d floats do not fit a slot of %lld floats", rows,
-                         row_floats, (long long)slot_floats);
-  if ((size_t)world * (size_t)slot_floats * sizeof(float) > region_data_bytes)
-    return hyq::api_fail(HYQ_E_SHAPE, "peer_exchange: %d slots of %lld floats exceed the regions' %zu data bytes",
-                         world, (long long)slot_floats, region_data_bytes);
-  hyq::XchgArgs a{};
-  for (int q = 0; q < world; ++q) {
-    if (!regions[q] || (regions[q] & 255)) return hyq::api_fail(HYQ_E_ALIGN, "peer_exchange: region %d", q);
-    a.region[q] = regions[q];
-  }
-  a.rank = rank;
-  a.world = world;
+  if (!send) return hyq::api_fail(HYQ_E_INVALID, "peer_exchange: null send");
+  if (rows < 1 || row_floats < 1) return hyq::api_fail(HYQ_E_SHAPE, "peer_exchange: %d rows of %d floats", rows, row_floats);
+  hyq::XchgArgs a;
+  int rc = hyq::xchg_setup(regions, rank, world, region_data_bytes, slot_floats, (int64_t)rows * row_floats,
+                           "peer_exchange", a);
+  if (rc) return rc;
   a.send = send;
   a.valid = valid;
   a.rows = rows;
   a.row_floats = row_floats;
   a.last_row = last_row ? 1 : 0;
-  a.slot = slot_floats;
-  a.wait_ns = hyq::g_peer_wait_ns.load(std::memory_order_relaxed);
-  int rc = hyq::api_status_word(&a.status);
+  return hyq::xchg_launch(a, stream, "peer_exchange");
+}
+
+int hyq_moe_ep_dispatch(const uint64_t* regions, int rank, int world, size_t region_data_bytes, int64_t slot_floats,
+                        const float* x, int tokens, int hidden, const int32_t* off, const int32_t* row_token,
+                        int experts_per_rank, int cap, void* stream) {
+  if (!x || !off || !row_token) return hyq::api_fail(HYQ_E_INVALID, "moe_ep_dispatch: null argument");
+  if (tokens < 1 || hidden < 1 || cap < 1 || experts_per_rank < 1 || experts_per_rank > hidden)
+    return hyq::api_fail(HYQ_E_SHAPE, "moe_ep_dispatch: %d tokens, hidden %d, cap %d, %d experts per rank", tokens,
+                         hidden, cap, experts_per_rank);
+  hyq::XchgArgs a;
+  int rc = hyq::xchg_setup(regions, rank, world, region_data_bytes, slot_floats, (int64_t)(cap + 1) * hidden,
+                           "moe_ep_dispatch", a);
   if (rc) return rc;
-  cudaStream_t st = (cudaStream_t)stream;
-  hyq::peer_xchg_open_kernel<<<1, 32, 0, st>>>(a);
-  cudaError_t e = cudaGetLastError();
-  if (e == cudaSuccess) {
-    const unsigned gx = (unsigned)(rows < 64 ? rows : 64);
-    hyq::peer_xchg_push_kernel<<<dim3(gx, (unsigned)world), 512, 0, st>>>(a);
-    e = cudaGetLastError();
-  }
-  if (e != cudaSuccess) return hyq::api_fail(HYQ_E_CUDA, "peer_exchange: %s", cudaGetErrorString(e));
-  return HYQ_OK;
+  a.mode = 1;
+  a.send = x;
+  a.src_rows = tokens;
+  a.off = off;
+  a.gather = row_token;
+  a.el = experts_per_rank;
+  a.rows = cap + 1;
+  a.row_floats = hidden;
+  return hyq::xchg_launch(a, stream, "moe_ep_dispatch");
+}
+
+int hyq_moe_ep_plan(const uint64_t* regions, int rank, int world, size_t region_data_bytes, int64_t slot_floats,
+                    int hidden, int cap, int experts_per_rank, int32_t* perm, int32_t* expert_off, int32_t* inv,
+                    int32_t* back_rows, void* stream) {
+  if (!perm || !expert_off || !inv || !back_rows) return hyq::api_fail(HYQ_E_INVALID, "moe_ep_plan: null output");
+  if (hidden < 1 || cap < 1 || experts_per_rank < 1 || experts_per_rank > hidden ||
+      (int64_t)world * experts_per_rank > hyq::kPlanMax || slot_floats % hidden)
+    return hyq::api_fail(HYQ_E_SHAPE, "moe_ep_plan: hidden %d, cap %d, %d experts per rank (at most %d with the ranks)",
+                         hidden, cap, experts_per_rank, hyq::kPlanMax);
+  hyq::XchgArgs x;
+  int rc = hyq::xchg_setup(regions, rank, world, region_data_bytes, slot_floats, (int64_t)(cap + 1) * hidden,
+                           "moe_ep_plan", x);
+  if (rc) return rc;
+  hyq::PlanArgs a{};
+  a.data = reinterpret_cast<const float*>(regions[rank] + HYQ_PEER_DATA_OFFSET);
+  a.world = world;
+  a.el = experts_per_rank;
+  a.cap = cap;
+  a.hidden = hidden;
+  a.slot = slot_floats;
+  a.perm = perm;
+  a.off = expert_off;
+  a.inv = inv;
+  a.back = back_rows;
+  hyq::moe_ep_plan_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(a);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "moe_ep_plan: %s", cudaGetErrorString(e));
+}
+
+int hyq_moe_ep_return(const uint64_t* regions, int rank, int world, size_t region_data_bytes, int64_t slot_floats,
+                      const float* y, int hidden, const int32_t* inv, const int32_t* back_rows, int cap,
+                      void* stream) {
+  if (!y || !inv || !back_rows) return hyq::api_fail(HYQ_E_INVALID, "moe_ep_return: null argument");
+  if (hidden < 1 || cap < 1) return hyq::api_fail(HYQ_E_SHAPE, "moe_ep_return: hidden %d, cap %d", hidden, cap);
+  hyq::XchgArgs a;
+  int rc = hyq::xchg_setup(regions, rank, world, region_data_bytes, slot_floats, (int64_t)cap * hidden,
+                           "moe_ep_return", a);
+  if (rc) return rc;
+  a.mode = 2;
+  a.send = y;
+  a.src_rows = world * cap;
+  a.gather = inv;
+  a.valid = back_rows;
+  a.rows = cap;
+  a.row_floats = hidden;
+  return hyq::xchg_launch(a, stream, "moe_ep_return");
+}
+
+int hyq_moe_ep_home(const uint64_t* regions, int rank, int world, size_t region_data_bytes, int64_t slot_floats,
+                    int hidden, const int32_t* off, int experts_per_rank, int cap, float* out, void* stream) {
+  if (!off || !out) return hyq::api_fail(HYQ_E_INVALID, "moe_ep_home: null argument");
+  if (hidden < 1 || cap < 1 || experts_per_rank < 1)
+    return hyq::api_fail(HYQ_E_SHAPE, "moe_ep_home: hidden %d, cap %d, %d experts per rank", hidden, cap,
+                         experts_per_rank);
+  hyq::XchgArgs x;
+  int rc = hyq::xchg_setup(regions, rank, world, region_data_bytes, slot_floats, (int64_t)cap * hidden,
+                           "moe_ep_home", x);
+  if (rc) return rc;
+  hyq::HomeArgs a{};
+  a.data = reinterpret_cast<const float*>(regions[rank] + HYQ_PEER_DATA_OFFSET);
+  a.off = off;
+  a.world = world;
+  a.el = experts_per_rank;
+  a.cap = cap;
+  a.hidden = hidden;
+  a.slot = slot_floats;
+  a.out = out;
+  hyq::moe_ep_home_kernel<<<dim3((unsigned)(cap < 64 ? cap : 64), (unsigned)world), 512, 0, (cudaStream_t)stream>>>(a);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HYQ_OK : hyq::api_fail(HYQ_E_CUDA, "moe_ep_home: %s", cudaGetErrorString(e));
 }
 
 }  // extern "C"

@@ -271,23 +271,16 @@ class MoeLayer:
         cap = T * c.used
         dev = x.device
         off = b["off"]
+        if self.xchg is not None:
+            self._experts_ep_peer(x, b, st)
+            return
         per_expert = off[1:] - off[:-1]                        # [E] rows per expert, this rank's tokens
         send_idx, send_valid = ep_send_index(off, world, El, cap)
         rows = b["row_token"].long()[send_idx.reshape(-1)]
         send = ep_pack(x, rows, per_expert, world, El, cap)    # [world * (cap + 1), hidden]
-        if self.xchg is not None:
-            # peer memory: only each block's valid rows and its count row
-            # cross NVLink, into the destination's region (slot = this rank)
-            X = self.xchg
-            stride = X.slot // c.hidden
-            if stride < cap + 1 or stride * c.hidden != X.slot:
-                raise ValueError("expert parallelism: the exchange's slots are too small for this token count")
-            X.exchange(send, cap + 1, send_valid.sum(1).to(torch.int32), last_row=True)
-            recv = X.recv(stride, c.hidden)
-        else:
-            stride = cap + 1
-            recv = torch.empty(world * stride, c.hidden, device=dev)
-            dist.all_to_all_single(recv, send, group=group)
+        stride = cap + 1
+        recv = torch.empty(world * stride, c.hidden, device=dev)
+        dist.all_to_all_single(recv, send, group=group)
         counts = ep_unpack_counts(recv, world, El, cap, stride)
         perm, valid, loff = ep_recv_perm(counts, cap)
         perm_d, off_d = ep_packed_rows(perm, cap, stride).to(torch.int32), loff.to(torch.int32)
@@ -301,19 +294,52 @@ class MoeLayer:
         # back into received order (padding rows go to a spare row), then home
         yr = torch.empty(Rr + 1, c.hidden, device=dev)
         yr.index_copy_(0, torch.where(valid, perm, torch.full_like(perm, Rr)), y)
-        if self.xchg is not None:
-            # each source gets back as many rows as it sent here
-            self.xchg.exchange(yr[:Rr], cap, counts.sum(1).to(torch.int32))
-            back = self.xchg.recv(stride, c.hidden).view(world, stride, c.hidden)[:, :cap].reshape(Rr, c.hidden)
-        else:
-            back = torch.empty(Rr, c.hidden, device=dev)
-            dist.all_to_all_single(back, yr[:Rr], group=group)
+        back = torch.empty(Rr, c.hidden, device=dev)
+        dist.all_to_all_single(back, yr[:Rr], group=group)
         R = T * c.used
         dest = torch.where(send_valid, send_idx, torch.full_like(send_idx, R)).reshape(-1)
         b["y"].index_copy_(0, dest, back)
 
+    def _experts_ep_peer(self, x, b, st):
+        """_experts_ep over NVLink peer memory with the index work inside the
+        library: dispatch (grouped rows gathered straight from x, counts
+        in-band), plan (expert-major gather index and its inverse from the
+        received counts), the expert products reading the region, return
+        (outputs gathered by the inverse), home (into b["y"])."""
+        rank, world, _ = self.ep
+        c, El, X = self.cfg, self.local_experts, self.xchg
+        T = x.shape[0]
+        cap = T * c.used
+        dev = x.device
+        if X.slot < (cap + 1) * c.hidden or X.slot % c.hidden:
+            raise ValueError("expert parallelism: the exchange's slots are too small for this token count")
+        Rr = world * cap
+        key = ("ep", T)
+        e = self._bufs.get(key)
+        if e is None:
+            i32 = dict(dtype=torch.int32, device=dev)
+            e = {"perm": torch.empty(Rr, **i32), "off": torch.empty(El + 1, **i32), "inv": torch.zeros(Rr, **i32),
+                 "back": torch.empty(world, **i32), "h": torch.empty(Rr, c.mid, device=dev),
+                 "y": torch.empty(Rr, c.hidden, device=dev)}
+            self._bufs[key] = e
+        regions, nbytes, slot = X._regions, X.data_bytes, X.slot
+        check(lib.hyq_moe_ep_dispatch(regions, rank, world, nbytes, slot, _p(x), T, c.hidden, _p(b["off"]),
+                                      _p(b["row_token"]), El, cap, st))
+        check(lib.hyq_moe_ep_plan(regions, rank, world, nbytes, slot, c.hidden, cap, El, _p(e["perm"]),
+                                  _p(e["off"]), _p(e["inv"]), _p(e["back"]), st))
+        recv = X.recv(slot // c.hidden, c.hidden)
+        check(lib.hyq_matmul_experts_gate_up_silu(self.gate.handle, self.up.handle, _p(recv), _p(e["perm"]), Rr,
+                                                  _p(e["off"]), world * T, _p(e["h"]), st))
+        check(lib.hyq_matmul_experts(self.down.handle, _p(e["h"]), None, Rr, _p(e["off"]), world * T, _p(e["y"]),
+                                     st))
+        check(lib.hyq_moe_ep_return(regions, rank, world, nbytes, slot, _p(e["y"]), c.hidden, _p(e["inv"]),
+                                    _p(e["back"]), cap, st))
+        check(lib.hyq_moe_ep_home(regions, rank, world, nbytes, slot, c.hidden, _p(b["off"]), El, cap, _p(b["y"]),
+                                  st))
+
     def launches(self, tokens):
         """Kernel launches of the library in one forward (for the bench's
         count): router, route, group, 2 x (conversion + expert GEMM), shared
-        FFN, combine; with the peer-memory exchange its 2 x 2 launches."""
-        return 3 + 4 + (2 if tokens == 1 else 4) + 1 + (4 if self.xchg is not None else 0)
+        FFN, combine; with the peer-memory exchange its dispatch and
+        return (two launches each), plan and home."""
+        return 3 + 4 + (2 if tokens == 1 else 4) + 1 + (6 if self.xchg is not None else 0)

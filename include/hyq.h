@@ -586,6 +586,37 @@ int hyq_peer_allreduce(const uint64_t* regions, int rank, int world, int64_t n, 
 int hyq_peer_exchange(const uint64_t* regions, int rank, int world, size_t region_data_bytes, const float* send,
                       int rows, int row_floats, const int32_t* valid, int last_row, int64_t slot_floats,
                       void* stream);
+/* Expert parallelism of the MoE layer over such regions (no counterpart in
+ * the reference: Moe::forward, model.rs:688-767, runs one process), the
+ * index work of the exchange done inside it.  Slots hold (cap + 1) rows of
+ * `hidden` floats, cap = tokens x experts used per token (the most rows a
+ * rank can send anywhere); every rank passes the same tokens and cap.
+ * hyq_moe_ep_dispatch: this rank's grouped rows for rank q's experts (off /
+ *   row_token from hyq_moe_group, experts_per_rank = E / world; rows
+ *   row_token[off[q El] + i] of x) go into q's region, slot = rank, with a
+ *   count row (row cap: the int32 row counts of q's experts);
+ * hyq_moe_ep_plan: from the count rows in this rank's region, the
+ *   expert-major gather index perm [world cap] (rows of the region data, as
+ *   hyq_matmul_experts* take it), expert_off [El + 1], the inverse inv
+ *   [world cap] and back_rows [world] (rows received from each source);
+ * hyq_moe_ep_return: the expert outputs y [world cap, hidden] (expert-major)
+ *   go back, rows inv[s cap + i] for i < back_rows[s] into source s's
+ *   region at slot = rank;
+ * hyq_moe_ep_home: the returned rows into out (the grouped-row outputs,
+ *   row off[q El] + i from slot q).
+ * Dispatch and return are exchanges (two launches each, bounded waits, as
+ * hyq_peer_exchange); plan and home are local. */
+int hyq_moe_ep_dispatch(const uint64_t* regions, int rank, int world, size_t region_data_bytes, int64_t slot_floats,
+                        const float* x, int tokens, int hidden, const int32_t* off, const int32_t* row_token,
+                        int experts_per_rank, int cap, void* stream);
+int hyq_moe_ep_plan(const uint64_t* regions, int rank, int world, size_t region_data_bytes, int64_t slot_floats,
+                    int hidden, int cap, int experts_per_rank, int32_t* perm, int32_t* expert_off, int32_t* inv,
+                    int32_t* back_rows, void* stream);
+int hyq_moe_ep_return(const uint64_t* regions, int rank, int world, size_t region_data_bytes, int64_t slot_floats,
+                      const float* y, int hidden, const int32_t* inv, const int32_t* back_rows, int cap,
+                      void* stream);
+int hyq_moe_ep_home(const uint64_t* regions, int rank, int world, size_t region_data_bytes, int64_t slot_floats,
+                    int hidden, const int32_t* off, int experts_per_rank, int cap, float* out, void* stream);
 /* How long hyq_peer_allreduce waits for the other ranks' flags before it
  * gives up with HYQ_DEV_TIMEOUT_PEER: 1 .. 600000 ms, 5000 by default;
  * process-wide, read when a call is issued. */

@@ -56,6 +56,21 @@ def _rank_main(rank, world, port, q, peer=False):
             got = ep.forward(x, T)
             ok &= torch.equal(got, ref)
         torch.cuda.synchronize(dev)
+    if peer:
+        # the plain exchange: block q of rank r is r * 1000 + q * 10 + row, the
+        # first (q + 2) rows of it sent, and the block's last row with last_row
+        H, rows = 64, 6
+        X = PeerExchange(rows * H, device=dev)
+        xchgs.append(X)
+        send = torch.stack([torch.full((rows, H), float(rank * 1000 + q * 10)) + torch.arange(rows)[:, None]
+                            for q in range(world)]).reshape(world * rows, H).to(dev)
+        valid = torch.tensor([q + 2 for q in range(world)], dtype=torch.int32, device=dev)
+        for _ in range(2):
+            X.exchange(send, rows, valid, last_row=True)
+            recv = X.recv(rows, H).view(world, rows, H).cpu()
+            for s in range(world):
+                for i in list(range(rank + 2)) + [rows - 1]:
+                    ok &= bool((recv[s, i] == float(s * 1000 + rank * 10 + i)).all())
     ok &= quant.device_status(dev) == 0
     for xchg in xchgs:
         xchg.close()
