@@ -1,5 +1,6 @@
 """GPU check of expert parallelism for the MoE layer (MoeLayer with ep=...)
-on two GPUs: each rank holds half of the experts and its own tokens; token
+on two GPUs (and four where the box has them): each rank holds its share of
+the experts and its own tokens; token
 rows travel to the expert's rank and back by NCCL all-to-all or, with a
 PeerExchange, by pushes into the other rank's peer-memory region.  Every
 expert output row is computed as on one GPU, so each rank's layer output
@@ -79,14 +80,14 @@ def _rank_main(rank, world, port, q, peer=False):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("peer", [False, True])
-def test_moe_expert_parallel_two_gpus(peer):
+@pytest.mark.parametrize("world,peer", [(2, False), (2, True), (4, True)])
+def test_moe_expert_parallel_two_gpus(world, peer):
     import torch
     import torch.multiprocessing as mp
 
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    world, port = 2, _free_port()
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    port = _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     procs = [ctx.Process(target=_rank_main, args=(r, world, port, q, peer)) for r in range(world)]
@@ -96,4 +97,4 @@ def test_moe_expert_parallel_two_gpus(peer):
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    assert res == {0: True, 1: True}
+    assert res == {r: True for r in range(world)}
