@@ -60,7 +60,7 @@ typedef enum hyq_profile {
 #define HYQ_DEV_TIMEOUT_EMPTY 2u /* a producer gave up waiting for a free stage */
 #define HYQ_DEV_TIMEOUT_DRAIN 4u /* exit path gave up waiting for copies in flight */
 #define HYQ_DEV_BAD_ARGS 8u      /* a kernel saw arguments the host should have rejected */
-#define HYQ_DEV_TIMEOUT_PEER 16u /* hyq_peer_allreduce gave up waiting for another rank */
+#define HYQ_DEV_TIMEOUT_PEER 16u /* a peer all-reduce or exchange gave up waiting for another rank */
 #define HYQ_DEV_TIMEOUT_GRID 32u /* hyq_dense_step_enqueue's kernel gave up at a grid-wide barrier */
 
 typedef struct hyq_weight hyq_weight;
